@@ -1,0 +1,198 @@
+/*
+ * libqwenb200 -- B200 (sm_100a) implementation of the speculative-decode hot
+ * path of the hybrid Qwen C engine (Julien-Bui/Qwen3.8-27B-in-C).
+ *
+ * Drop-in boundary.  The entry points below keep the names, argument meaning
+ * and return conventions of the reference headers, so a caller written
+ * against include/model.h and include/kernels.h (e.g. the spec loop of
+ * src/main.c:158-225) recompiles against this header unchanged:
+ *
+ *   model_init / model_free            include/model.h:117-118
+ *   model_forward                      include/model.h:125
+ *   model_forward_batch                include/model.h:130-131
+ *   model_rollback_to                  include/model.h:136
+ *   mtp_forward / mtp_forward_batch    include/model.h:139-145
+ *   model_sample_greedy                include/model.h:148
+ *   gemv_rows / gemv / gemv_rows_batch / gemv_batch
+ *                                      include/kernels.h:11-26
+ *   gemv_multi / gemv_multi_batch      include/kernels.h:28-34
+ *   rmsnorm / l2norm / silu_inplace / sigmoid_inplace / softplus_inplace /
+ *   softmax_inplace                    include/kernels.h:36-44
+ *   pool_create / pool_destroy / pool_run   include/threadpool.h:9-15
+ *
+ * All pointers in these calls are HOST pointers, as in the reference; the
+ * library owns the CUDA device memory (weights, KV caches, recurrent states
+ * and their rollback slots) and mirrors the fields a caller reads or writes
+ * (logits, logits_b, h_save, mtp_h, x, pos) in host memory.  The pool
+ * argument is accepted and ignored: all work runs on one CUDA stream per
+ * model.  Functions that return void in the reference record failures in
+ * qb_last_error(); nothing falls back to a CPU computation.
+ *
+ * The qb_* entry points at the end run whole loops on the device (prefill,
+ * greedy decode, greedy MTP speculation with on-device argmax, acceptance
+ * and rollback) with no host round trip per token.
+ */
+#ifndef QWEN_B200_H
+#define QWEN_B200_H
+
+#include <stdbool.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- types shared with the reference headers (same layout) ---- */
+
+/* include/gguf.h:40-64 */
+typedef enum {
+    GGML_F32 = 0, GGML_F16 = 1, GGML_Q4_0 = 2, GGML_Q4_1 = 3, GGML_Q5_0 = 6, GGML_Q5_1 = 7,
+    GGML_Q8_0 = 8, GGML_Q2_K = 10, GGML_Q3_K = 11, GGML_Q4_K = 12, GGML_Q5_K = 13, GGML_Q6_K = 14,
+    GGML_Q8_K = 15, GGML_IQ2_XXS = 16, GGML_IQ2_XS = 17, GGML_IQ3_XXS = 18, GGML_IQ1_S = 19,
+    GGML_IQ4_NL = 20, GGML_IQ3_S = 21, GGML_IQ2_S = 22, GGML_IQ4_XS = 23, GGML_IQ1_M = 24,
+    GGML_BF16 = 25
+} ggml_type_t;
+
+/* include/gguf.h:66-73 */
+typedef struct {
+    char name[64];
+    uint32_t n_dims;
+    uint64_t ne[4];        /* ne[0] = innermost (input) dimension */
+    ggml_type_t type;
+    uint64_t offset;
+    const void *data;      /* host pointer to the GGUF row-major blocks */
+} gguf_tensor_info_t;
+
+/* include/gguf.h:75-97 */
+typedef struct {
+    uint32_t n_embd, n_head, n_head_kv, head_dim, n_layer, n_ff, vocab_size, context_len;
+    float rope_theta;
+    uint32_t rope_dim_count;
+    uint32_t rope_sections[4];
+    float rms_norm_eps;
+    bool tie_word_embeddings;
+    uint32_t full_attn_interval, ssm_state_size, ssm_conv_kernel, ssm_inner_size, ssm_group_count;
+    uint32_t nextn_layers;
+} qwen_config_t;
+
+/* include/model.h:10-31 */
+typedef struct {
+    uint32_t n_embd, n_ff, n_layer, n_attn_layer, n_recr_layer;
+    uint32_t n_head, n_kv_head, head_dim;
+    uint32_t rope_sections[4];
+    uint32_t n_v_heads, n_k_heads, head_k_dim, head_v_dim, d_inner, conv_dim, d_conv, d_state;
+} qwen_dims_t;
+
+/* The model handle.  The named fields mean what they mean in the reference
+ * qwen_model_t (include/model.h:60-111); they are host mirrors of device
+ * state, refreshed by the calls that produce them:
+ *   logits    [vocab]            model_forward, mtp_forward(want_logits=1)
+ *   logits_b  [PREFILL_MAX_B][vocab]  model_forward_batch, mtp_forward_batch(want)
+ *   h_save    [PREFILL_MAX_B][n_embd] model_forward_batch (pre-norm hidden)
+ *   x         [n_embd]           model_forward (pre-norm hidden of the token)
+ *   mtp_h     [n_embd]           read by mtp_forward (caller may write it,
+ *                                src/main.c:220), written back after it
+ *   pos                          next position, as in the reference */
+typedef struct qwen_model {
+    qwen_config_t cfg;
+    qwen_dims_t dims;
+    float *mtp_h;
+    float *x;
+    float *logits;
+    float *logits_b;
+    float *h_save;
+    uint32_t n_ctx;
+    uint32_t pos;
+    void *eng;             /* device engine (opaque) */
+} qwen_model_t;
+
+typedef struct pool pool_t;
+typedef void (*pool_fn_t)(void *arg, int tid, int ntotal);
+
+#define SPEC_MAX_B 4       /* verify width: k = 3 drafts (the reference ships 3) */
+#define PREFILL_MAX_B 8
+#define GEMV_MAX_B 8
+
+/* ---- include/threadpool.h:9-15 (kept for source compatibility) ---- */
+pool_t *pool_create(int n_threads, int pin);
+void pool_destroy(pool_t *p);
+void pool_run(pool_t *p, pool_fn_t fn, void *arg);
+
+/* ---- include/model.h:117-148 ---- */
+int model_init(qwen_model_t *m, const char *path, uint32_t n_ctx);
+void model_free(qwen_model_t *m);
+void model_forward(qwen_model_t *m, pool_t *pool, uint32_t token, uint32_t pos);
+void model_forward_batch(qwen_model_t *m, pool_t *pool, const uint32_t *tokens, uint32_t pos,
+                         uint32_t B, int ckpt);
+int model_snapshot_states(qwen_model_t *m);
+void model_rollback_states(qwen_model_t *m);
+void model_rollback_to(qwen_model_t *m, uint32_t b);
+int mtp_forward(qwen_model_t *m, pool_t *pool, uint32_t token, uint32_t pos, int want_logits);
+int mtp_forward_batch(qwen_model_t *m, pool_t *pool, const uint32_t *tokens, uint32_t pos,
+                      uint32_t B, int want_logits);
+uint32_t model_sample_greedy(const float *logits, uint32_t vocab_size);
+
+/* ---- include/kernels.h:11-44 (host pointers; weights uploaded on first use
+ *      and cached on the current device, keyed by W->data) ---- */
+void gemv_rows(const gguf_tensor_info_t *W, const float *x, float *out, uint64_t r0, uint64_t r1);
+void gemv(pool_t *pool, const gguf_tensor_info_t *W, const float *x, float *out);
+void gemv_rows_batch(const gguf_tensor_info_t *W, const float *x, uint64_t ldx, int n, float *out,
+                     uint64_t ldo, uint64_t r0, uint64_t r1);
+void gemv_batch(pool_t *pool, const gguf_tensor_info_t *W, const float *x, uint64_t ldx, int n,
+                float *out, uint64_t ldo);
+void gemv_multi(pool_t *pool, const gguf_tensor_info_t *const *Ws, const float *x, float *const *outs,
+                int n_mat);
+void gemv_multi_batch(pool_t *pool, const gguf_tensor_info_t *const *Ws, const float *x, uint64_t ldx,
+                      int n, float *const *outs, const uint64_t *ldos, int n_mat);
+void rmsnorm(float *out, const float *x, const float *weight, uint64_t n, float eps);
+void l2norm(float *out, const float *x, uint64_t n, float eps);
+void silu_inplace(float *x, uint64_t n);
+void sigmoid_inplace(float *x, uint64_t n);
+void softplus_inplace(float *x, uint64_t n);
+void softmax_inplace(float *x, uint64_t n);
+
+/* ---- device-resident loops (no counterpart function in the reference: they
+ *      run the loops of src/main.c on the device) ---- */
+
+/* Last error of this thread: 0 = none.  qb_last_error_str() describes it. */
+int qb_last_error(void);
+const char *qb_last_error_str(void);
+void qb_clear_error(void);
+
+/* src/main.c:132-152: batched prefill in chunks of PREFILL_MAX_B, plus the
+ * MTP cache fill when spec != 0; afterwards m->logits holds the logits of
+ * the last prompt token.  Returns 0 or -1. */
+int qb_prefill(qwen_model_t *m, const uint32_t *tokens, uint32_t n, int spec);
+
+/* src/main.c:158-225: greedy MTP speculation with n_spec drafts.  Drafts,
+ * verify, argmax, acceptance, rollback and the MTP anchor all run on the
+ * device; the host only waits between batches of cycles.  When n_forced > 0
+ * the accept length of cycle c is forced[c % n_forced] (clamped to n_spec)
+ * instead of the first-mismatch rule.  Writes up to n_predict tokens to
+ * out_tokens and the accept length of each cycle to out_j (may be NULL,
+ * else room for max_cycles entries).  Returns the number of tokens, or -1. */
+int qb_spec_generate(qwen_model_t *m, uint32_t n_predict, uint32_t n_spec, const uint32_t *forced,
+                     uint32_t n_forced, uint32_t *out_tokens, uint32_t *out_j, uint32_t max_cycles,
+                     uint32_t *n_cycles);
+
+/* src/main.c:232-248 at temperature 0: token 0 = argmax(m->logits), then
+ * n_predict-1 single-token forwards, each fed its own device argmax.
+ * Returns the number of tokens, or -1. */
+int qb_greedy_generate(qwen_model_t *m, uint32_t n_predict, uint32_t *out_tokens);
+
+/* Device argmax of the last model_forward_batch row b (no host scan). */
+uint32_t qb_last_argmax(qwen_model_t *m, uint32_t b);
+
+/* Timing helper for benchmarks: CUDA-event time of the last qb_* loop, ms. */
+float qb_last_loop_ms(qwen_model_t *m);
+
+/* Copy the recurrent state of backbone layer il (0 conv, 1 ssm) or the KV
+ * cache (2 k, 3 v; il == n_layer selects the MTP block) to host memory, for
+ * state comparisons against the reference.  Returns the float count. */
+int64_t qb_read_state(qwen_model_t *m, uint32_t il, int which, float *dst, int64_t max_floats);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QWEN_B200_H */

@@ -1,0 +1,89 @@
+// Shared device helpers and launch-parameter structs for the sm_100a kernels.
+#pragma once
+#include <cstdint>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#define QB_TILE 16          // rows per tensor-core tile (m16n8k16 M dimension)
+#define QB_MAX_TOK 8        // verify / prefill width handled by one GEMV launch
+#define QB_MAX_SEG 4        // matrices fused into one GEMV launch (shared input)
+
+// ggml type ids, identical to the GGUF numbering (reference include/gguf.h:40-64)
+enum QbType : int { QB_F32 = 0, QB_Q8_0 = 8, QB_Q4_K = 12, QB_Q5_K = 13, QB_Q6_K = 14, QB_IQ4_XS = 23 };
+
+// Bytes of one repacked (16-row tile x 256-column super-block) unit.  Q8_0 uses
+// a (16-row tile x 32-column block) unit.  Every layout holds exactly the bytes
+// of the 16 source rows: the repack only reorders them.
+__host__ __device__ constexpr int qb_unit_bytes(int type) {
+    return type == QB_IQ4_XS ? 16 * 136
+         : type == QB_Q6_K   ? 16 * 210
+         : type == QB_Q4_K   ? 16 * 144
+         : type == QB_Q5_K   ? 16 * 176
+         : type == QB_Q8_0   ? 16 * 34
+         : 0;
+}
+__host__ __device__ constexpr int qb_unit_cols(int type) { return type == QB_Q8_0 ? 32 : 256; }
+
+struct QSeg {
+    const uint8_t* w;     // repacked weights of this matrix
+    float* out;           // out[t * ldo + row]
+    long long ldo;
+    int tile0;            // first grid tile of this segment
+    int rows;
+};
+
+struct QmvParams {
+    QSeg seg[QB_MAX_SEG];
+    int nseg;
+    int K;                // input length (columns)
+    int N;                // number of input vectors (tokens), 1..8
+    const uint2* xfrag;   // activations, hi/lo fp16 split, in mma B-fragment order
+    const float* xscale;  // [QB_MAX_TOK][K/256] power-of-two scale per 256-column block
+    const float* xsum;    // [QB_MAX_TOK][K/32] plain column sums (Q4_K / Q5_K only)
+    int accumulate;       // 0: out = y ; 1: out += y (residual add)
+    int row_lo, row_hi;   // only rows in [row_lo, row_hi) are stored (gemv_rows API)
+};
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
+__device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+// D = A(16x16, f16, row) * B(16x8, f16, col) + C, fp32 accumulate.
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                          uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint4 ldg_nc_128(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint2 ldg_nc_64(const void* p) {
+    uint2 v;
+    asm volatile("ld.global.nc.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ float h2f_bits(uint32_t h16) {
+    return __half2float(__ushort_as_half((unsigned short)(h16 & 0xFFFFu)));
+}
+
+// exact small-integer -> float for 0 <= v < 2^22 without I2F: (2^23 + v) - 2^23
+__device__ __forceinline__ float small_u2f(uint32_t v) {
+    return __int_as_float(0x4B000000u | v) - 8388608.0f;
+}

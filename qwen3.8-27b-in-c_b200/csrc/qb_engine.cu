@@ -1,0 +1,1346 @@
+// Device engine + C ABI of libqwenb200.
+//
+// Forward structure follows the reference engine:
+//   model_forward_batch  src/model.c:976-1002   (embed -> 64 layers -> h_save -> norm -> head)
+//   gdn_layer_batch      src/model.c:845-974
+//   attention_layer_batch src/model.c:760-843
+//   mtp_forward(_batch)  src/model.c:1038-1103
+//   model_rollback_to    src/model.c:1015-1031
+//   spec loop            src/main.c:158-225
+// Recurrent states live in 4 device slots per layer; a verify writes the
+// state after token b into slot b, and "rollback to b" selects slot b as the
+// live state (no copy).  Dynamic values (tokens, positions, live slot, draft
+// candidates, accept length) live in a device control block, so whole
+// speculative cycles are captured once as CUDA graphs and replayed.
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <cmath>
+#include <string>
+#include <vector>
+#include <mutex>
+#include <algorithm>
+#include <unordered_map>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include "qb_common.cuh"
+#include "qb_kernels.h"
+#include "qwen_b200.h"
+
+// ------------------------------- errors ---------------------------------------
+static thread_local int g_err = 0;
+static thread_local char g_err_str[256] = "";
+
+static void set_err(int code, const char* fmt, ...) {
+    if (g_err) return;   // keep the first error
+    g_err = code;
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err_str, sizeof g_err_str, fmt, ap);
+    va_end(ap);
+    fprintf(stderr, "libqwenb200: %s\n", g_err_str);
+}
+
+#define CK(call)                                                                             \
+    do {                                                                                     \
+        cudaError_t e_ = (call);                                                             \
+        if (e_ != cudaSuccess) {                                                             \
+            set_err((int)e_, "%s:%d %s: %s", __FILE__, __LINE__, #call, cudaGetErrorString(e_)); \
+            return -1;                                                                       \
+        }                                                                                    \
+    } while (0)
+
+extern "C" int qb_last_error(void) { return g_err; }
+extern "C" const char* qb_last_error_str(void) { return g_err_str; }
+extern "C" void qb_clear_error(void) {
+    g_err = 0;
+    g_err_str[0] = 0;
+}
+
+// ----------------------------- GGUF reader ------------------------------------
+// Minimal reader of the GGUF v2/v3 container: header, metadata (the
+// "<arch>.*" keys of the hybrid model), tensor table, aligned data section.
+namespace {
+
+struct GTensor {
+    std::string name;
+    uint32_t n_dims = 0;
+    uint64_t ne[4] = {1, 1, 1, 1};
+    int type = 0;
+    uint64_t offset = 0;
+    const uint8_t* data = nullptr;
+};
+
+struct Gguf {
+    int fd = -1;
+    size_t size = 0;
+    const uint8_t* map = nullptr;
+    std::string arch;
+    qwen_config_t cfg{};
+    std::vector<GTensor> tensors;
+    const GTensor* find(const char* n) const {
+        for (auto& t : tensors)
+            if (t.name == n) return &t;
+        return nullptr;
+    }
+    ~Gguf() {
+        if (map) munmap((void*)map, size);
+        if (fd >= 0) close(fd);
+    }
+};
+
+struct Cursor {
+    const uint8_t* p;
+    const uint8_t* end;
+    bool ok = true;
+    template <class T> T get() {
+        T v{};
+        if ((size_t)(end - p) < sizeof(T)) { ok = false; return v; }
+        memcpy(&v, p, sizeof(T));
+        p += sizeof(T);
+        return v;
+    }
+    std::string str() {
+        const uint64_t n = get<uint64_t>();
+        if (!ok || n > (uint64_t)(end - p)) { ok = false; return {}; }
+        std::string s((const char*)p, (size_t)n);
+        p += n;
+        return s;
+    }
+    void skip(uint32_t type) {
+        static const int fixed[] = {1, 1, 2, 2, 4, 4, 4, 1, 0, 0, 8, 8, 8};
+        if (type == 8) { (void)str(); return; }
+        if (type == 9) {
+            const uint32_t et = get<uint32_t>();
+            const uint64_t cnt = get<uint64_t>();
+            if (et > 12) { ok = false; return; }
+            for (uint64_t i = 0; i < cnt && ok; ++i) skip(et);
+            return;
+        }
+        if (type > 12) { ok = false; return; }
+        if ((size_t)(end - p) < (size_t)fixed[type]) { ok = false; return; }
+        p += fixed[type];
+    }
+};
+
+int gguf_load(Gguf& g, const char* path) {
+    g.fd = open(path, O_RDONLY);
+    if (g.fd < 0) { set_err(-1, "cannot open %s", path); return -1; }
+    struct stat st;
+    if (fstat(g.fd, &st) != 0 || st.st_size < 24) { set_err(-1, "bad file %s", path); return -1; }
+    g.size = (size_t)st.st_size;
+    void* m = mmap(nullptr, g.size, PROT_READ, MAP_SHARED, g.fd, 0);
+    if (m == MAP_FAILED) { set_err(-1, "mmap failed for %s", path); return -1; }
+    g.map = (const uint8_t*)m;
+    Cursor c{g.map, g.map + g.size};
+    const uint32_t magic = c.get<uint32_t>(), version = c.get<uint32_t>();
+    const uint64_t n_t = c.get<uint64_t>(), n_kv = c.get<uint64_t>();
+    if (magic != 0x46554747u || version < 2 || version > 3 || n_t == 0 || n_t > 100000) {
+        set_err(-1, "%s: not a GGUF v2/v3 file", path);
+        return -1;
+    }
+    uint32_t alignment = 32;
+    // pass 1: architecture + alignment; pass 2: "<arch>.*"
+    const uint8_t* kv0 = c.p;
+    for (int pass = 1; pass <= 2 && c.ok; ++pass) {
+        c.p = kv0;
+        for (uint64_t i = 0; i < n_kv && c.ok; ++i) {
+            const std::string key = c.str();
+            const uint32_t t = c.get<uint32_t>();
+            if (pass == 1) {
+                if (key == "general.architecture" && t == 8) { g.arch = c.str(); continue; }
+                if (key == "general.alignment" && t == 4) { const uint32_t a = c.get<uint32_t>(); if (a) alignment = a; continue; }
+                c.skip(t);
+                continue;
+            }
+            const std::string pre = g.arch + ".";
+            if (key.compare(0, pre.size(), pre) != 0) { c.skip(t); continue; }
+            const std::string k = key.substr(pre.size());
+            qwen_config_t& f = g.cfg;
+            auto u32 = [&](uint32_t& dst) { if (t == 4) dst = c.get<uint32_t>(); else c.skip(t); };
+            auto f32 = [&](float& dst) { if (t == 6) dst = c.get<float>(); else c.skip(t); };
+            if (k == "embedding_length") u32(f.n_embd);
+            else if (k == "attention.head_count") u32(f.n_head);
+            else if (k == "attention.head_count_kv") u32(f.n_head_kv);
+            else if (k == "attention.key_length") u32(f.head_dim);
+            else if (k == "block_count") u32(f.n_layer);
+            else if (k == "feed_forward_length") u32(f.n_ff);
+            else if (k == "vocab_size") u32(f.vocab_size);
+            else if (k == "context_length") u32(f.context_len);
+            else if (k == "rope.freq_base") f32(f.rope_theta);
+            else if (k == "rope.dimension_count") u32(f.rope_dim_count);
+            else if (k == "attention.layer_norm_rms_epsilon") f32(f.rms_norm_eps);
+            else if (k == "full_attention_interval") u32(f.full_attn_interval);
+            else if (k == "ssm.state_size") u32(f.ssm_state_size);
+            else if (k == "ssm.conv_kernel") u32(f.ssm_conv_kernel);
+            else if (k == "ssm.inner_size") u32(f.ssm_inner_size);
+            else if (k == "ssm.group_count") u32(f.ssm_group_count);
+            else if (k == "nextn_predict_layers") u32(f.nextn_layers);
+            else if (k == "tie_word_embeddings" && t == 7) f.tie_word_embeddings = c.get<uint8_t>() != 0;
+            else if (k == "rope.dimension_sections" && t == 9) {
+                const uint32_t et = c.get<uint32_t>();
+                const uint64_t cnt = c.get<uint64_t>();
+                for (uint64_t j = 0; j < cnt && c.ok; ++j) {
+                    if (et == 4 || et == 5) { const uint32_t v = c.get<uint32_t>(); if (j < 4) f.rope_sections[j] = v; }
+                    else c.skip(et);
+                }
+            } else c.skip(t);
+        }
+        if (pass == 1 && g.arch.empty()) { set_err(-1, "%s: no general.architecture", path); return -1; }
+    }
+    g.tensors.resize(n_t);
+    for (uint64_t i = 0; i < n_t && c.ok; ++i) {
+        GTensor& t = g.tensors[i];
+        t.name = c.str();
+        t.n_dims = c.get<uint32_t>();
+        if (t.n_dims > 4) { c.ok = false; break; }
+        for (uint32_t d = 0; d < t.n_dims; ++d) t.ne[d] = c.get<uint64_t>();
+        t.type = (int)c.get<uint32_t>();
+        t.offset = c.get<uint64_t>();
+    }
+    if (!c.ok) { set_err(-1, "%s: truncated GGUF header", path); return -1; }
+    const uint64_t cur = (uint64_t)(c.p - g.map);
+    const uint64_t base = (cur + alignment - 1) / alignment * alignment;
+    for (auto& t : g.tensors) {
+        t.data = g.map + base + t.offset;
+        if (base + t.offset >= g.size) { set_err(-1, "%s: tensor %s outside file", path, t.name.c_str()); return -1; }
+    }
+    if (g.cfg.vocab_size == 0) {
+        const GTensor* e = g.find("token_embd.weight");
+        if (e && e->n_dims == 2) g.cfg.vocab_size = (uint32_t)e->ne[1];
+    }
+    return 0;
+}
+
+size_t gguf_row_bytes(int type, uint64_t ne0) {
+    switch (type) {
+    case QB_F32: return ne0 * 4;
+    case QB_Q8_0: return ne0 / 32 * 34;
+    case QB_IQ4_XS: return ne0 / 256 * 136;
+    case QB_Q6_K: return ne0 / 256 * 210;
+    case QB_Q4_K: return ne0 / 256 * 144;
+    case QB_Q5_K: return ne0 / 256 * 176;
+    default: return 0;
+    }
+}
+
+// ------------------------------ engine ----------------------------------------
+
+constexpr int kNSlot = 4;
+
+struct DevMat {
+    int type = -1;
+    int rows = 0, K = 0;
+    void* w = nullptr;   // repacked (quant) or plain row-major (F32)
+};
+
+struct LayerW {
+    bool rec = false;
+    int ridx = -1, aidx = -1;
+    const float *attn_norm = nullptr, *post_norm = nullptr;
+    DevMat ffn_gate, ffn_up, ffn_down;
+    DevMat wqkv, wgate, wbeta, walpha, ssm_out;
+    const float *conv_w = nullptr, *dt_bias = nullptr, *ssm_a = nullptr, *ssm_norm = nullptr;
+    DevMat q, k, v, o;
+    const float *q_norm = nullptr, *k_norm = nullptr;
+};
+
+}  // namespace
+
+struct QbCtrl {
+    uint32_t fwd_pos;
+    uint32_t fwd_tok[QB_MAX_TOK];
+    uint32_t cur_slot;
+    uint32_t mtp_pos;
+    uint32_t mtp_tok[QB_MAX_TOK];
+    uint32_t argmax[QB_MAX_TOK];
+    uint32_t mtp_argmax[QB_MAX_TOK];
+    // speculative loop
+    uint32_t P, k, cand[QB_MAX_TOK], j, cycle, n_out, next_cand0, n_forced, cap_out, cap_j;
+    uint32_t greedy_n;
+};
+
+namespace {
+
+struct Engine {
+    int dev = 0;
+    cudaStream_t st = nullptr;
+    Gguf g;
+    qwen_config_t cfg{};
+    qwen_dims_t d{};
+    int V = 0, E = 0, F = 0, n_ctx = 0, rope_half = 0;
+    float eps = 1e-6f;
+    std::vector<LayerW> L;
+    LayerW mtp;
+    DevMat eh_proj, output;
+    const float *out_norm = nullptr, *enorm = nullptr, *hnorm = nullptr, *shnorm = nullptr;
+    int embd_type = 0;
+    void* tok_embd = nullptr;   // raw GGUF rows
+    std::vector<void*> allocs;
+
+    // state
+    float *conv_slots = nullptr, *ssm_slots = nullptr;
+    size_t conv_slot_stride = 0, ssm_slot_stride = 0, conv_layer = 0, ssm_layer = 0;
+    float *kv_k = nullptr, *kv_v = nullptr, *mtp_k = nullptr, *mtp_v = nullptr;
+    size_t kv_layer = 0;
+    float *rope_cos = nullptr, *rope_sin = nullptr;
+
+    // activations (QB_MAX_TOK rows each)
+    float *bx, *h_save, *qkv, *qkvc, *z, *beta, *alpha, *o, *y, *qbuf, *kvbuf, *attn_o, *gate, *up, *act;
+    float *logits, *mtp_x, *mtp_h, *mtp_logits, *emb;
+    uint2* xfrag = nullptr;
+    float *xscale = nullptr, *xsum = nullptr;
+    unsigned long long* keys = nullptr;   // [2][QB_MAX_TOK]: backbone, mtp
+    QbCtrl* ctrl = nullptr;
+    uint32_t* d_forced = nullptr;
+    uint32_t* d_out_tok = nullptr;
+    uint32_t* d_out_j = nullptr;
+    uint32_t cap_forced = 0, cap_out = 0, cap_j = 0;
+    int ld_qkv = 0;
+
+    // graphs
+    cudaGraphExec_t g_cycle = nullptr;
+    int g_cycle_k = -1;
+    cudaGraphExec_t g_greedy = nullptr;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    float last_ms = 0.f;
+    bool any_q45 = false;
+
+    ~Engine();
+    void* dalloc(size_t bytes) {
+        void* p = nullptr;
+        if (cudaMalloc(&p, bytes) != cudaSuccess) return nullptr;
+        allocs.push_back(p);
+        return p;
+    }
+};
+
+Engine::~Engine() {
+    cudaSetDevice(dev);
+    if (g_cycle) cudaGraphExecDestroy(g_cycle);
+    if (g_greedy) cudaGraphExecDestroy(g_greedy);
+    if (ev0) cudaEventDestroy(ev0);
+    if (ev1) cudaEventDestroy(ev1);
+    for (void* p : allocs) cudaFree(p);
+    if (st) cudaStreamDestroy(st);
+}
+
+int upload_mat(Engine& e, const GTensor* t, DevMat& m, void* tmp, size_t tmp_bytes) {
+    if (!t) { set_err(-1, "missing tensor"); return -1; }
+    m.type = t->type;
+    m.K = (int)t->ne[0];
+    m.rows = (int)t->ne[1];
+    const size_t src_bytes = gguf_row_bytes(t->type, t->ne[0]) * t->ne[1];
+    if (!src_bytes) { set_err(-1, "tensor %s: unsupported type %d", t->name.c_str(), t->type); return -1; }
+    if (t->type == QB_F32) {
+        m.w = e.dalloc(src_bytes);
+        if (!m.w) { set_err(-2, "cudaMalloc %zu", src_bytes); return -1; }
+        CK(cudaMemcpy(m.w, t->data, src_bytes, cudaMemcpyHostToDevice));
+        return 0;
+    }
+    const size_t rb = qb_repacked_bytes(t->type, m.rows, m.K);
+    if (!rb || src_bytes > tmp_bytes) { set_err(-1, "tensor %s: cannot repack", t->name.c_str()); return -1; }
+    m.w = e.dalloc(rb);
+    if (!m.w) { set_err(-2, "cudaMalloc %zu", rb); return -1; }
+    CK(cudaMemcpy(tmp, t->data, src_bytes, cudaMemcpyHostToDevice));
+    CK(qb_repack(t->type, tmp, m.rows, m.K, m.w, e.st));
+    CK(cudaStreamSynchronize(e.st));
+    if (t->type == QB_Q4_K || t->type == QB_Q5_K) e.any_q45 = true;
+    return 0;
+}
+
+const float* upload_f32(Engine& e, const GTensor* t) {
+    if (!t || t->type != QB_F32) return nullptr;
+    const size_t n = t->ne[0] * t->ne[1];
+    void* p = e.dalloc(n * 4);
+    if (!p) return nullptr;
+    if (cudaMemcpy(p, t->data, n * 4, cudaMemcpyHostToDevice) != cudaSuccess) return nullptr;
+    return (const float*)p;
+}
+
+int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
+    CK(cudaGetDevice(&e.dev));
+    CK(cudaStreamCreateWithFlags(&e.st, cudaStreamNonBlocking));
+    CK(qb_quant_init_constants());
+    if (gguf_load(e.g, path)) return -1;
+    e.cfg = e.g.cfg;
+    qwen_config_t& c = e.cfg;
+    qwen_dims_t& d = e.d;
+    d.n_embd = c.n_embd;
+    d.n_ff = c.n_ff;
+    d.n_head = c.n_head;
+    d.n_kv_head = c.n_head_kv;
+    d.head_dim = c.head_dim;
+    d.n_k_heads = c.ssm_group_count;
+    d.head_k_dim = d.head_v_dim = d.d_state = c.ssm_state_size;
+    d.d_inner = c.ssm_inner_size;
+    d.d_conv = c.ssm_conv_kernel;
+    memcpy(d.rope_sections, c.rope_sections, sizeof d.rope_sections);
+    const GTensor* a0 = e.g.find("blk.0.ssm_a");
+    if (!a0) { set_err(-1, "missing blk.0.ssm_a"); return -1; }
+    d.n_v_heads = (uint32_t)a0->ne[0];
+    d.conv_dim = 2 * d.n_k_heads * d.head_k_dim + d.d_inner;
+    d.n_layer = c.n_layer > c.nextn_layers ? c.n_layer - c.nextn_layers : c.n_layer;
+    if (d.d_inner != d.n_v_heads * d.head_v_dim || d.head_k_dim != 128 || d.head_dim != 256 ||
+        d.d_conv != 4 || c.rope_dim_count % 64 != 0 || c.nextn_layers < 1) {
+        set_err(-1, "unsupported model shape (head_k_dim %u head_dim %u d_conv %u rope %u)", d.head_k_dim,
+                d.head_dim, d.d_conv, c.rope_dim_count);
+        return -1;
+    }
+    e.E = (int)d.n_embd;
+    e.F = (int)d.n_ff;
+    e.V = (int)c.vocab_size;
+    e.eps = c.rms_norm_eps;
+    e.n_ctx = (int)n_ctx;
+    e.rope_half = (int)c.rope_dim_count / 2;
+
+    // temp buffer for repacking = largest quantised tensor
+    size_t tmp_bytes = 0;
+    for (auto& t : e.g.tensors)
+        if (t.type != QB_F32) tmp_bytes = std::max(tmp_bytes, gguf_row_bytes(t.type, t.ne[0]) * t.ne[1]);
+    void* tmp = nullptr;
+    CK(cudaMalloc(&tmp, tmp_bytes));
+    struct TmpFree { void* p; ~TmpFree() { cudaFree(p); } } tmp_guard{tmp};
+
+    char nm[96];
+    auto T = [&](const char* fmt, int il) -> const GTensor* {
+        snprintf(nm, sizeof nm, fmt, il);
+        const GTensor* t = e.g.find(nm);
+        if (!t) set_err(-1, "missing tensor %s", nm);
+        return t;
+    };
+    const GTensor* te = e.g.find("token_embd.weight");
+    if (!te || te->ne[0] != (uint64_t)e.E) { set_err(-1, "token_embd missing or wrong shape"); return -1; }
+    e.embd_type = te->type;
+    {
+        const size_t b = gguf_row_bytes(te->type, te->ne[0]) * te->ne[1];
+        e.tok_embd = e.dalloc(b);
+        if (!e.tok_embd) { set_err(-2, "cudaMalloc token_embd"); return -1; }
+        CK(cudaMemcpy(e.tok_embd, te->data, b, cudaMemcpyHostToDevice));
+    }
+    const GTensor* to = e.g.find("output.weight");
+    if (!to) to = te;
+    if (upload_mat(e, to, e.output, tmp, tmp_bytes)) return -1;
+    if (!(e.out_norm = upload_f32(e, e.g.find("output_norm.weight")))) { set_err(-1, "output_norm"); return -1; }
+
+    e.L.resize(d.n_layer);
+    int nr = 0, na = 0;
+    for (uint32_t il = 0; il < d.n_layer; ++il) {
+        LayerW& l = e.L[il];
+        l.rec = ((il + 1) % c.full_attn_interval) != 0;
+        if (!(l.attn_norm = upload_f32(e, T("blk.%d.attn_norm.weight", il)))) return -1;
+        if (!(l.post_norm = upload_f32(e, T("blk.%d.post_attention_norm.weight", il)))) return -1;
+        if (upload_mat(e, T("blk.%d.ffn_gate.weight", il), l.ffn_gate, tmp, tmp_bytes) ||
+            upload_mat(e, T("blk.%d.ffn_up.weight", il), l.ffn_up, tmp, tmp_bytes) ||
+            upload_mat(e, T("blk.%d.ffn_down.weight", il), l.ffn_down, tmp, tmp_bytes))
+            return -1;
+        if (l.rec) {
+            l.ridx = nr++;
+            if (upload_mat(e, T("blk.%d.attn_qkv.weight", il), l.wqkv, tmp, tmp_bytes) ||
+                upload_mat(e, T("blk.%d.attn_gate.weight", il), l.wgate, tmp, tmp_bytes) ||
+                upload_mat(e, T("blk.%d.ssm_beta.weight", il), l.wbeta, tmp, tmp_bytes) ||
+                upload_mat(e, T("blk.%d.ssm_alpha.weight", il), l.walpha, tmp, tmp_bytes) ||
+                upload_mat(e, T("blk.%d.ssm_out.weight", il), l.ssm_out, tmp, tmp_bytes))
+                return -1;
+            if (!(l.conv_w = upload_f32(e, T("blk.%d.ssm_conv1d.weight", il))) ||
+                !(l.dt_bias = upload_f32(e, T("blk.%d.ssm_dt.bias", il))) ||
+                !(l.ssm_a = upload_f32(e, T("blk.%d.ssm_a", il))) ||
+                !(l.ssm_norm = upload_f32(e, T("blk.%d.ssm_norm.weight", il))))
+                return -1;
+        } else {
+            l.aidx = na++;
+            if (upload_mat(e, T("blk.%d.attn_q.weight", il), l.q, tmp, tmp_bytes) ||
+                upload_mat(e, T("blk.%d.attn_k.weight", il), l.k, tmp, tmp_bytes) ||
+                upload_mat(e, T("blk.%d.attn_v.weight", il), l.v, tmp, tmp_bytes) ||
+                upload_mat(e, T("blk.%d.attn_output.weight", il), l.o, tmp, tmp_bytes))
+                return -1;
+            if (!(l.q_norm = upload_f32(e, T("blk.%d.attn_q_norm.weight", il))) ||
+                !(l.k_norm = upload_f32(e, T("blk.%d.attn_k_norm.weight", il))))
+                return -1;
+        }
+    }
+    d.n_recr_layer = nr;
+    d.n_attn_layer = na;
+    {   // MTP block blk.<n_layer>
+        const int im = (int)d.n_layer;
+        LayerW& l = e.mtp;
+        if (!(l.attn_norm = upload_f32(e, T("blk.%d.attn_norm.weight", im)))) return -1;
+        if (!(l.post_norm = upload_f32(e, T("blk.%d.post_attention_norm.weight", im)))) return -1;
+        if (upload_mat(e, T("blk.%d.attn_q.weight", im), l.q, tmp, tmp_bytes) ||
+            upload_mat(e, T("blk.%d.attn_k.weight", im), l.k, tmp, tmp_bytes) ||
+            upload_mat(e, T("blk.%d.attn_v.weight", im), l.v, tmp, tmp_bytes) ||
+            upload_mat(e, T("blk.%d.attn_output.weight", im), l.o, tmp, tmp_bytes) ||
+            upload_mat(e, T("blk.%d.ffn_gate.weight", im), l.ffn_gate, tmp, tmp_bytes) ||
+            upload_mat(e, T("blk.%d.ffn_up.weight", im), l.ffn_up, tmp, tmp_bytes) ||
+            upload_mat(e, T("blk.%d.ffn_down.weight", im), l.ffn_down, tmp, tmp_bytes) ||
+            upload_mat(e, T("blk.%d.nextn.eh_proj.weight", im), e.eh_proj, tmp, tmp_bytes))
+            return -1;
+        if (!(l.q_norm = upload_f32(e, T("blk.%d.attn_q_norm.weight", im))) ||
+            !(l.k_norm = upload_f32(e, T("blk.%d.attn_k_norm.weight", im))) ||
+            !(e.enorm = upload_f32(e, T("blk.%d.nextn.enorm.weight", im))) ||
+            !(e.hnorm = upload_f32(e, T("blk.%d.nextn.hnorm.weight", im))) ||
+            !(e.shnorm = upload_f32(e, T("blk.%d.nextn.shared_head_norm.weight", im))))
+            return -1;
+        if (e.eh_proj.K != 2 * e.E || e.eh_proj.rows != e.E) { set_err(-1, "eh_proj shape"); return -1; }
+    }
+
+    // ---- states ----
+    e.conv_layer = (size_t)d.conv_dim * 4;
+    e.ssm_layer = (size_t)d.n_v_heads * d.head_v_dim * d.head_k_dim;
+    e.conv_slot_stride = e.conv_layer * nr;
+    e.ssm_slot_stride = e.ssm_layer * nr;
+    e.conv_slots = (float*)e.dalloc(std::max<size_t>(1, e.conv_slot_stride * kNSlot) * 4);
+    e.ssm_slots = (float*)e.dalloc(std::max<size_t>(1, e.ssm_slot_stride * kNSlot) * 4);
+    e.kv_layer = (size_t)n_ctx * d.n_kv_head * d.head_dim;
+    e.kv_k = (float*)e.dalloc(std::max<size_t>(1, e.kv_layer * na) * 4);
+    e.kv_v = (float*)e.dalloc(std::max<size_t>(1, e.kv_layer * na) * 4);
+    e.mtp_k = (float*)e.dalloc(e.kv_layer * 4);
+    e.mtp_v = (float*)e.dalloc(e.kv_layer * 4);
+    if (!e.conv_slots || !e.ssm_slots || !e.kv_k || !e.kv_v || !e.mtp_k || !e.mtp_v) {
+        set_err(-2, "state allocation failed");
+        return -1;
+    }
+    CK(cudaMemset(e.conv_slots, 0, std::max<size_t>(1, e.conv_slot_stride * kNSlot) * 4));
+    CK(cudaMemset(e.ssm_slots, 0, std::max<size_t>(1, e.ssm_slot_stride * kNSlot) * 4));
+    CK(cudaMemset(e.kv_k, 0, std::max<size_t>(1, e.kv_layer * na) * 4));
+    CK(cudaMemset(e.kv_v, 0, std::max<size_t>(1, e.kv_layer * na) * 4));
+    CK(cudaMemset(e.mtp_k, 0, e.kv_layer * 4));
+    CK(cudaMemset(e.mtp_v, 0, e.kv_layer * 4));
+
+    // RoPE tables on the host with the reference's libm calls (src/model.c:186-201)
+    {
+        const int half = e.rope_half;
+        std::vector<float> cs((size_t)n_ctx * half), sn((size_t)n_ctx * half);
+        for (int p = 0; p < (int)n_ctx; ++p)
+            for (int i = 0; i < half; ++i) {
+                const float angle = (float)p * powf(c.rope_theta, -2.0f * (float)i / (float)c.rope_dim_count);
+                cs[(size_t)p * half + i] = cosf(angle);
+                sn[(size_t)p * half + i] = sinf(angle);
+            }
+        e.rope_cos = (float*)e.dalloc(cs.size() * 4);
+        e.rope_sin = (float*)e.dalloc(sn.size() * 4);
+        if (!e.rope_cos || !e.rope_sin) { set_err(-2, "rope alloc"); return -1; }
+        CK(cudaMemcpy(e.rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(e.rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+    }
+
+    // ---- activations ----
+    const int T8 = QB_MAX_TOK;
+    e.ld_qkv = std::max<int>({(int)d.conv_dim, 2 * (int)d.n_head * (int)d.head_dim, e.F, 2 * e.E});
+    auto A = [&](size_t n) { return (float*)e.dalloc(n * 4); };
+    e.bx = A((size_t)T8 * e.E);
+    e.h_save = A((size_t)T8 * e.E);
+    e.qkv = A((size_t)T8 * e.ld_qkv);
+    e.qkvc = A((size_t)T8 * e.ld_qkv);
+    e.z = A((size_t)T8 * d.d_inner);
+    e.beta = A((size_t)T8 * 256);
+    e.alpha = A((size_t)T8 * 256);
+    e.o = A((size_t)T8 * d.d_inner);
+    e.y = A((size_t)T8 * d.d_inner);
+    e.qbuf = A((size_t)T8 * 2 * d.n_head * d.head_dim);
+    e.kvbuf = A((size_t)T8 * 2 * d.n_kv_head * d.head_dim);
+    e.attn_o = A((size_t)T8 * d.n_head * d.head_dim);
+    e.gate = A((size_t)T8 * e.F);
+    e.up = A((size_t)T8 * e.F);
+    e.act = A((size_t)T8 * e.F);
+    e.logits = A((size_t)T8 * e.V);
+    e.mtp_x = A((size_t)T8 * e.E);
+    e.mtp_h = A((size_t)e.E);
+    e.mtp_logits = A((size_t)T8 * e.V);
+    e.emb = A((size_t)T8 * e.E);
+    const int Kmax = std::max<int>({2 * e.E, e.F, (int)d.d_inner, (int)(d.n_head * d.head_dim)});
+    const size_t xf_bytes = (size_t)Kmax / 32 * 2 * 2 * 32 * 8;   // NT = 2
+    e.xfrag = (uint2*)e.dalloc(xf_bytes);
+    e.xscale = A((size_t)T8 * (Kmax / 256));
+    e.xsum = A((size_t)T8 * (Kmax / 32));
+    e.keys = (unsigned long long*)e.dalloc(2 * T8 * sizeof(unsigned long long));
+    e.ctrl = (QbCtrl*)e.dalloc(sizeof(QbCtrl));
+    if (!e.bx || !e.logits || !e.xfrag || !e.ctrl || !e.emb || !e.keys) { set_err(-2, "activation alloc"); return -1; }
+    CK(cudaMemset(e.xfrag, 0, xf_bytes));
+    CK(cudaMemset(e.xscale, 0, (size_t)T8 * (Kmax / 256) * 4));
+    CK(cudaMemset(e.xsum, 0, (size_t)T8 * (Kmax / 32) * 4));
+    CK(cudaMemset(e.ctrl, 0, sizeof(QbCtrl)));
+    CK(cudaMemset(e.mtp_h, 0, (size_t)e.E * 4));
+    CK(cudaEventCreate(&e.ev0));
+    CK(cudaEventCreate(&e.ev1));
+    CK(cudaDeviceSynchronize());
+    return 0;
+}
+
+// ----------------------------- launch helpers ---------------------------------
+
+int gemv_group(Engine& e, const DevMat* const* mats, float* const* outs, const long long* ldos, int nm, int K,
+               int N, int accumulate) {
+    // fuse matrices of the same type; different types run as separate launches
+    int i = 0;
+    while (i < nm) {
+        QbQSeg segs[QB_MAX_SEG];
+        int ns = 0;
+        const int type = mats[i]->type;
+        while (i < nm && ns < QB_MAX_SEG && mats[i]->type == type) {
+            segs[ns].w = mats[i]->w;
+            segs[ns].out = outs[i];
+            segs[ns].ldo = ldos[i];
+            segs[ns].rows = mats[i]->rows;
+            ++ns;
+            ++i;
+        }
+        if (type == QB_F32) {
+            for (int s = 0; s < ns; ++s) CK(cudaErrorNotSupported);
+        } else {
+            CK(qb_qmv(type, segs, ns, K, N, e.xfrag, e.xscale, e.xsum, accumulate, 0, 1 << 30, e.st));
+        }
+    }
+    return 0;
+}
+
+int xprep1(Engine& e, const float* x, long long ldx, const float* norm_w, int len, int N) {
+    QbXIn in{x, ldx, norm_w, len};
+    CK(qb_xprep(&in, 1, N, e.eps, e.xfrag, e.xscale, e.xsum, e.any_q45 ? 1 : 0, e.st));
+    return 0;
+}
+
+// SwiGLU FFN on residual x (src/model.c:819-842)
+int ffn_block(Engine& e, const LayerW& l, float* x, int B) {
+    if (xprep1(e, x, e.E, l.post_norm, e.E, B)) return -1;
+    const DevMat* m2[2] = {&l.ffn_gate, &l.ffn_up};
+    float* o2[2] = {e.gate, e.up};
+    const long long ld2[2] = {e.F, e.F};
+    if (gemv_group(e, m2, o2, ld2, 2, e.E, B, 0)) return -1;
+    CK(qb_silu_mul(e.gate, e.up, e.F, e.F, B, e.act, e.st));
+    if (xprep1(e, e.act, e.F, nullptr, e.F, B)) return -1;
+    const DevMat* m1[1] = {&l.ffn_down};
+    float* o1[1] = {x};
+    const long long ld1[1] = {e.E};
+    return gemv_group(e, m1, o1, ld1, 1, e.F, B, 1);
+}
+
+// gated attention block on residual x, positions *pos .. *pos+B-1
+int attn_block(Engine& e, const LayerW& l, float* x, int B, const uint32_t* pos, float* kc, float* vc) {
+    const qwen_dims_t& d = e.d;
+    const int qw = 2 * d.n_head * d.head_dim, kvw = d.n_kv_head * d.head_dim;
+    if (xprep1(e, x, e.E, l.attn_norm, e.E, B)) return -1;
+    const DevMat* m3[3] = {&l.q, &l.k, &l.v};
+    float* o3[3] = {e.qbuf, e.kvbuf, e.kvbuf + kvw};
+    const long long ld3[3] = {qw, 2 * kvw, 2 * kvw};
+    if (gemv_group(e, m3, o3, ld3, 3, e.E, B, 0)) return -1;
+    CK(qb_attn_prep(e.qbuf, qw, e.kvbuf, 2 * kvw, l.q_norm, l.k_norm, d.n_head, d.n_kv_head, d.head_dim,
+                    e.rope_half, e.rope_cos, e.rope_sin, pos, B, e.eps, kc, vc, e.st));
+    CK(qb_attn_decode(e.qbuf, qw, kc, vc, d.n_head, d.n_kv_head, d.head_dim, pos, B, e.n_ctx, e.attn_o,
+                      d.n_head * d.head_dim, e.st));
+    const int ow = d.n_head * d.head_dim;
+    if (xprep1(e, e.attn_o, ow, nullptr, ow, B)) return -1;
+    const DevMat* m1[1] = {&l.o};
+    float* o1[1] = {x};
+    const long long ld1[1] = {e.E};
+    if (gemv_group(e, m1, o1, ld1, 1, ow, B, 1)) return -1;
+    return ffn_block(e, l, x, B);
+}
+
+int gdn_block(Engine& e, const LayerW& l, int B, int ckpt) {
+    const qwen_dims_t& d = e.d;
+    if (xprep1(e, e.bx, e.E, l.attn_norm, e.E, B)) return -1;
+    const DevMat* m4[4] = {&l.wqkv, &l.wgate, &l.wbeta, &l.walpha};
+    float* o4[4] = {e.qkv, e.z, e.beta, e.alpha};
+    const long long ld4[4] = {e.ld_qkv, d.d_inner, 256, 256};
+    if (gemv_group(e, m4, o4, ld4, 4, e.E, B, 0)) return -1;
+    float* conv = e.conv_slots + (size_t)l.ridx * e.conv_layer;
+    float* ssm = e.ssm_slots + (size_t)l.ridx * e.ssm_layer;
+    CK(qb_gdn_conv(e.qkv, e.ld_qkv, d.conv_dim, B, l.conv_w, conv, e.conv_slot_stride, &e.ctrl->cur_slot, ckpt,
+                   e.qkvc, e.ld_qkv, e.st));
+    CK(qb_gdn_recur(e.qkvc, e.ld_qkv, e.beta, e.alpha, 256, l.dt_bias, l.ssm_a, d.n_k_heads, d.n_v_heads,
+                    d.head_k_dim, B, e.eps, ssm, e.ssm_slot_stride, &e.ctrl->cur_slot, ckpt, e.o, d.d_inner,
+                    e.st));
+    CK(qb_gdn_out(e.o, e.z, d.d_inner, l.ssm_norm, d.n_v_heads, d.head_v_dim, B, e.eps, e.y, e.st));
+    if (xprep1(e, e.y, d.d_inner, nullptr, d.d_inner, B)) return -1;
+    const DevMat* m1[1] = {&l.ssm_out};
+    float* o1[1] = {e.bx};
+    const long long ld1[1] = {e.E};
+    if (gemv_group(e, m1, o1, ld1, 1, d.d_inner, B, 1)) return -1;
+    return ffn_block(e, l, e.bx, B);
+}
+
+__global__ void set_u32_kernel(uint32_t* p, uint32_t v) { *p = v; }
+
+// model_forward_batch on the device: tokens ctrl->fwd_tok[0..B), positions
+// ctrl->fwd_pos + b.  Logits -> e.logits[b], argmax -> ctrl->argmax[b].
+int fwd_backbone(Engine& e, int B, int ckpt) {
+    CK(qb_embed(e.embd_type, e.tok_embd, e.E, e.ctrl->fwd_tok, B, e.bx, e.E, e.st));
+    for (const LayerW& l : e.L) {
+        if (l.rec) {
+            if (gdn_block(e, l, B, ckpt)) return -1;
+        } else {
+            float* kc = e.kv_k + (size_t)l.aidx * e.kv_layer;
+            float* vc = e.kv_v + (size_t)l.aidx * e.kv_layer;
+            if (attn_block(e, l, e.bx, B, &e.ctrl->fwd_pos, kc, vc)) return -1;
+        }
+    }
+    CK(cudaMemcpyAsync(e.h_save, e.bx, (size_t)B * e.E * 4, cudaMemcpyDeviceToDevice, e.st));
+    if (xprep1(e, e.bx, e.E, e.out_norm, e.E, B)) return -1;
+    const DevMat* m1[1] = {&e.output};
+    float* o1[1] = {e.logits};
+    const long long ld1[1] = {e.V};
+    if (gemv_group(e, m1, o1, ld1, 1, e.E, B, 0)) return -1;
+    CK(qb_argmax_reset(e.keys, B, e.st));
+    CK(qb_argmax(e.logits, e.V, e.V, B, e.keys, e.st));
+    CK(qb_argmax_to_u32(e.keys, B, e.ctrl->argmax, e.st));
+    if (ckpt) set_u32_kernel<<<1, 1, 0, e.st>>>(&e.ctrl->cur_slot, (uint32_t)std::min(B - 1, kNSlot - 1));
+    CK(cudaGetLastError());
+    return 0;
+}
+
+// mtp_forward(_batch) on the device: tokens ctrl->mtp_tok[0..B), positions
+// ctrl->mtp_pos + b, hidden input = hsrc rows (mtp_h for the single-token
+// chain, h_save for the batch fill).  mtp_h <- output of the last token.
+int fwd_mtp(Engine& e, int B, const float* hsrc, int want_logits) {
+    CK(qb_embed(e.embd_type, e.tok_embd, e.E, e.ctrl->mtp_tok, B, e.emb, e.E, e.st));
+    QbXIn in[2] = {{e.emb, e.E, e.enorm, e.E}, {hsrc, e.E, e.hnorm, e.E}};
+    CK(qb_xprep(in, 2, B, e.eps, e.xfrag, e.xscale, e.xsum, e.any_q45 ? 1 : 0, e.st));
+    const DevMat* m1[1] = {&e.eh_proj};
+    float* o1[1] = {e.mtp_x};
+    const long long ld1[1] = {e.E};
+    if (gemv_group(e, m1, o1, ld1, 1, 2 * e.E, B, 0)) return -1;
+    if (attn_block(e, e.mtp, e.mtp_x, B, &e.ctrl->mtp_pos, e.mtp_k, e.mtp_v)) return -1;
+    CK(cudaMemcpyAsync(e.mtp_h, e.mtp_x + (size_t)(B - 1) * e.E, (size_t)e.E * 4, cudaMemcpyDeviceToDevice, e.st));
+    if (want_logits) {
+        if (xprep1(e, e.mtp_x, e.E, e.shnorm, e.E, B)) return -1;
+        const DevMat* mo[1] = {&e.output};
+        float* oo[1] = {e.mtp_logits};
+        const long long ldo[1] = {e.V};
+        if (gemv_group(e, mo, oo, ldo, 1, e.E, B, 0)) return -1;
+        CK(qb_argmax_reset(e.keys + QB_MAX_TOK, B, e.st));
+        CK(qb_argmax(e.mtp_logits, e.V, e.V, B, e.keys + QB_MAX_TOK, e.st));
+        CK(qb_argmax_to_u32(e.keys + QB_MAX_TOK, B, e.ctrl->mtp_argmax, e.st));
+    }
+    return 0;
+}
+
+// ------------------------- speculative cycle kernels ----------------------------
+
+// cycle start: cand[0] = next_cand0; first draft input = (cand[0], P+1)
+__global__ void spec_start_kernel(QbCtrl* c) {
+    c->cand[0] = c->next_cand0;
+    c->mtp_tok[0] = c->cand[0];
+    c->mtp_pos = c->P + 1;
+}
+// after draft s: cand[s] = argmax; next draft input = (cand[s], P+s+1)
+__global__ void spec_draft_kernel(QbCtrl* c, int s) {
+    c->cand[s] = c->mtp_argmax[0];
+    c->mtp_tok[0] = c->cand[s];
+    c->mtp_pos = c->P + s + 1;
+}
+__global__ void spec_verify_setup_kernel(QbCtrl* c, int k) {
+    for (int i = 0; i <= k; ++i) c->fwd_tok[i] = c->cand[i];
+    c->fwd_pos = c->P + 1;
+}
+// acceptance (src/main.c:191-223): j = first i < k with argmax(logits_b[i])
+// != cand[i+1], or the forced length; emit cand[0..j]; live slot = j; MTP
+// anchor on (cand[j], h_save[j]) at P+j+1; next cand0 = argmax(logits_b[j]).
+__global__ void spec_accept_kernel(QbCtrl* c, int k, const uint32_t* forced, uint32_t* out_tok,
+                                   uint32_t* out_j, const float* h_save, float* mtp_h, int E) {
+    __shared__ uint32_t sj;
+    if (threadIdx.x == 0) {
+        uint32_t j = (uint32_t)k;
+        for (int i = 0; i < k; ++i)
+            if (c->argmax[i] != c->cand[i + 1]) { j = (uint32_t)i; break; }
+        if (c->n_forced) {
+            j = forced[c->cycle % c->n_forced];
+            if (j > (uint32_t)k) j = (uint32_t)k;
+        }
+        for (uint32_t i = 0; i <= j; ++i)
+            if (c->n_out + i < c->cap_out) out_tok[c->n_out + i] = c->cand[i];
+        if (c->cycle < c->cap_j) out_j[c->cycle] = j;
+        c->n_out += j + 1;
+        c->cycle += 1;
+        c->j = j;
+        c->cur_slot = j;                 // rollback = select the slot after token j
+        const uint32_t P_new = c->P + j + 1;
+        c->mtp_tok[0] = c->cand[j];
+        c->mtp_pos = P_new;              // anchor position P + j + 1
+        c->next_cand0 = c->argmax[j];
+        c->P = P_new;
+        sj = j;
+    }
+    __syncthreads();
+    const float* src = h_save + (size_t)sj * E;
+    for (int i = threadIdx.x; i < E; i += blockDim.x) mtp_h[i] = src[i];
+}
+
+// greedy decode step: next token = argmax of the previous forward
+__global__ void greedy_step_kernel(QbCtrl* c, uint32_t* out_tok) {
+    const uint32_t t = c->argmax[0];
+    if (c->greedy_n < c->cap_out) out_tok[c->greedy_n] = t;
+    c->greedy_n += 1;
+    c->fwd_tok[0] = t;
+    c->fwd_pos += 1;
+}
+
+int record_cycle(Engine& e, int k) {
+    spec_start_kernel<<<1, 1, 0, e.st>>>(e.ctrl);
+    for (int s = 1; s <= k; ++s) {
+        if (fwd_mtp(e, 1, e.mtp_h, 1)) return -1;
+        spec_draft_kernel<<<1, 1, 0, e.st>>>(e.ctrl, s);
+    }
+    spec_verify_setup_kernel<<<1, 1, 0, e.st>>>(e.ctrl, k);
+    if (fwd_backbone(e, k + 1, 1)) return -1;
+    spec_accept_kernel<<<1, 256, 0, e.st>>>(e.ctrl, k, e.d_forced, e.d_out_tok, e.d_out_j, e.h_save, e.mtp_h, e.E);
+    if (fwd_mtp(e, 1, e.mtp_h, 0)) return -1;
+    CK(cudaGetLastError());
+    return 0;
+}
+
+int capture(Engine& e, cudaGraphExec_t* out, int (*rec)(Engine&, int), int arg) {
+    cudaGraph_t graph = nullptr;
+    CK(cudaStreamBeginCapture(e.st, cudaStreamCaptureModeThreadLocal));
+    const int r = rec(e, arg);
+    cudaError_t ce = cudaStreamEndCapture(e.st, &graph);
+    if (r || ce != cudaSuccess) {
+        if (graph) cudaGraphDestroy(graph);
+        if (!r) CK(ce);
+        return -1;
+    }
+    cudaError_t ie = cudaGraphInstantiate(out, graph, 0);
+    cudaGraphDestroy(graph);
+    CK(ie);
+    return 0;
+}
+
+int record_greedy(Engine& e, int) {
+    if (fwd_backbone(e, 1, 0)) return -1;
+    greedy_step_kernel<<<1, 1, 0, e.st>>>(e.ctrl, e.d_out_tok);
+    CK(cudaGetLastError());
+    return 0;
+}
+
+int ensure_out_buffers(Engine& e, uint32_t n_out, uint32_t n_j, uint32_t n_forced) {
+    if (n_out > e.cap_out || n_j > e.cap_j || n_forced > e.cap_forced) {
+        // buffers captured in graphs: re-capture after reallocation
+        if (e.g_cycle) { cudaGraphExecDestroy(e.g_cycle); e.g_cycle = nullptr; }
+        if (e.g_greedy) { cudaGraphExecDestroy(e.g_greedy); e.g_greedy = nullptr; }
+        const uint32_t co = std::max(n_out, std::max(e.cap_out, 4096u));
+        const uint32_t cj = std::max(n_j, std::max(e.cap_j, 4096u));
+        const uint32_t cf = std::max(n_forced, std::max(e.cap_forced, 1024u));
+        uint32_t *a = nullptr, *b = nullptr, *f = nullptr;
+        CK(cudaMalloc(&a, (size_t)co * 4));
+        CK(cudaMalloc(&b, (size_t)cj * 4));
+        CK(cudaMalloc(&f, (size_t)cf * 4));
+        if (e.d_out_tok) cudaFree(e.d_out_tok);
+        if (e.d_out_j) cudaFree(e.d_out_j);
+        if (e.d_forced) cudaFree(e.d_forced);
+        e.d_out_tok = a;
+        e.d_out_j = b;
+        e.d_forced = f;
+        e.cap_out = co;
+        e.cap_j = cj;
+        e.cap_forced = cf;
+    }
+    return 0;
+}
+
+Engine* E_(qwen_model_t* m) { return m ? (Engine*)m->eng : nullptr; }
+
+int sync_host_mirrors_after_batch(qwen_model_t* m, Engine& e, int B) {
+    CK(cudaMemcpyAsync(m->logits_b, e.logits, (size_t)B * e.V * 4, cudaMemcpyDeviceToHost, e.st));
+    CK(cudaMemcpyAsync(m->h_save, e.h_save, (size_t)B * e.E * 4, cudaMemcpyDeviceToHost, e.st));
+    CK(cudaStreamSynchronize(e.st));
+    return 0;
+}
+
+}  // namespace
+
+// ================================ C API: model ===================================
+
+struct pool { int n; };
+
+extern "C" pool_t* pool_create(int n_threads, int) {
+    pool_t* p = (pool_t*)calloc(1, sizeof(pool_t));
+    if (p) p->n = n_threads < 1 ? 1 : n_threads;
+    return p;
+}
+extern "C" void pool_destroy(pool_t* p) { free(p); }
+extern "C" void pool_run(pool_t*, pool_fn_t fn, void* arg) { fn(arg, 0, 1); }
+
+extern "C" int model_init(qwen_model_t* m, const char* path, uint32_t n_ctx) {
+    if (!m || !path) return -1;
+    memset(m, 0, sizeof *m);
+    Engine* e = new Engine();
+    if (engine_init(*e, path, n_ctx)) {
+        delete e;
+        return -1;
+    }
+    m->eng = e;
+    m->cfg = e->cfg;
+    m->dims = e->d;
+    m->n_ctx = n_ctx;
+    m->pos = 0;
+    const size_t VB = (size_t)PREFILL_MAX_B * e->V, EB = (size_t)PREFILL_MAX_B * e->E;
+    if (cudaMallocHost(&m->logits_b, VB * 4) != cudaSuccess || cudaMallocHost(&m->logits, (size_t)e->V * 4) != cudaSuccess ||
+        cudaMallocHost(&m->h_save, EB * 4) != cudaSuccess || cudaMallocHost(&m->mtp_h, (size_t)e->E * 4) != cudaSuccess ||
+        cudaMallocHost(&m->x, (size_t)e->E * 4) != cudaSuccess) {
+        set_err(-2, "pinned host mirrors");
+        model_free(m);
+        return -1;
+    }
+    memset(m->mtp_h, 0, (size_t)e->E * 4);
+    return 0;
+}
+
+extern "C" void model_free(qwen_model_t* m) {
+    if (!m) return;
+    delete E_(m);
+    if (m->logits_b) cudaFreeHost(m->logits_b);
+    if (m->logits) cudaFreeHost(m->logits);
+    if (m->h_save) cudaFreeHost(m->h_save);
+    if (m->mtp_h) cudaFreeHost(m->mtp_h);
+    if (m->x) cudaFreeHost(m->x);
+    memset(m, 0, sizeof *m);
+}
+
+static int do_forward_batch(qwen_model_t* m, const uint32_t* tokens, uint32_t pos, uint32_t B, int ckpt) {
+    Engine* e = E_(m);
+    if (!e || B < 1 || B > QB_MAX_TOK || pos + B > (uint32_t)e->n_ctx) {
+        set_err(-1, "model_forward_batch: bad arguments (B=%u pos=%u)", B, pos);
+        return -1;
+    }
+    CK(cudaSetDevice(e->dev));
+    CK(cudaMemcpyAsync(e->ctrl->fwd_tok, tokens, B * 4, cudaMemcpyHostToDevice, e->st));
+    CK(cudaMemcpyAsync(&e->ctrl->fwd_pos, &pos, 4, cudaMemcpyHostToDevice, e->st));
+    if (fwd_backbone(*e, (int)B, ckpt)) return -1;
+    if (sync_host_mirrors_after_batch(m, *e, (int)B)) return -1;
+    m->pos = pos + B;
+    return 0;
+}
+
+extern "C" void model_forward(qwen_model_t* m, pool_t*, uint32_t token, uint32_t pos) {
+    if (do_forward_batch(m, &token, pos, 1, 0)) return;
+    Engine* e = E_(m);
+    memcpy(m->logits, m->logits_b, (size_t)e->V * 4);
+    memcpy(m->x, m->h_save, (size_t)e->E * 4);
+}
+
+extern "C" void model_forward_batch(qwen_model_t* m, pool_t*, const uint32_t* tokens, uint32_t pos, uint32_t B,
+                                    int ckpt) {
+    do_forward_batch(m, tokens, pos, B, ckpt);
+}
+
+extern "C" int model_snapshot_states(qwen_model_t*) { return 0; }
+extern "C" void model_rollback_states(qwen_model_t*) {}
+
+extern "C" void model_rollback_to(qwen_model_t* m, uint32_t b) {
+    Engine* e = E_(m);
+    if (!e || b >= (uint32_t)kNSlot) { set_err(-1, "model_rollback_to: bad slot %u", b); return; }
+    cudaSetDevice(e->dev);
+    set_u32_kernel<<<1, 1, 0, e->st>>>(&e->ctrl->cur_slot, b);
+    cudaError_t ce = cudaStreamSynchronize(e->st);
+    if (ce != cudaSuccess) set_err((int)ce, "model_rollback_to: %s", cudaGetErrorString(ce));
+}
+
+static int do_mtp(qwen_model_t* m, const uint32_t* tokens, uint32_t pos, uint32_t B, int want_logits, bool batch) {
+    Engine* e = E_(m);
+    if (!e || B < 1 || B > QB_MAX_TOK || pos + B > (uint32_t)e->n_ctx) {
+        set_err(-1, "mtp_forward: bad arguments");
+        return -1;
+    }
+    CK(cudaSetDevice(e->dev));
+    CK(cudaMemcpyAsync(e->ctrl->mtp_tok, tokens, B * 4, cudaMemcpyHostToDevice, e->st));
+    CK(cudaMemcpyAsync(&e->ctrl->mtp_pos, &pos, 4, cudaMemcpyHostToDevice, e->st));
+    const float* hsrc = e->mtp_h;
+    if (batch) {
+        // h_save rows as the hidden input (src/model.c:1077-1084): the caller's host
+        // mirror is the source of truth, as for every other mirror
+        CK(cudaMemcpyAsync(e->h_save, m->h_save, (size_t)B * e->E * 4, cudaMemcpyHostToDevice, e->st));
+        hsrc = e->h_save;
+    } else {
+        CK(cudaMemcpyAsync(e->mtp_h, m->mtp_h, (size_t)e->E * 4, cudaMemcpyHostToDevice, e->st));
+    }
+    if (fwd_mtp(*e, (int)B, hsrc, want_logits)) return -1;
+    CK(cudaMemcpyAsync(m->mtp_h, e->mtp_h, (size_t)e->E * 4, cudaMemcpyDeviceToHost, e->st));
+    if (want_logits) {
+        if (batch)
+            CK(cudaMemcpyAsync(m->logits_b, e->mtp_logits, (size_t)B * e->V * 4, cudaMemcpyDeviceToHost, e->st));
+        else
+            CK(cudaMemcpyAsync(m->logits, e->mtp_logits, (size_t)e->V * 4, cudaMemcpyDeviceToHost, e->st));
+    }
+    CK(cudaStreamSynchronize(e->st));
+    return 0;
+}
+
+extern "C" int mtp_forward(qwen_model_t* m, pool_t*, uint32_t token, uint32_t pos, int want_logits) {
+    do_mtp(m, &token, pos, 1, want_logits, false);
+    return 0;   // the reference always returns 0 (src/model.c:1062)
+}
+
+extern "C" int mtp_forward_batch(qwen_model_t* m, pool_t*, const uint32_t* tokens, uint32_t pos, uint32_t B,
+                                 int want_logits) {
+    do_mtp(m, tokens, pos, B, want_logits, true);
+    return 0;
+}
+
+extern "C" uint32_t qb_last_argmax(qwen_model_t* m, uint32_t b) {
+    Engine* e = E_(m);
+    if (!e || b >= QB_MAX_TOK) return 0;
+    uint32_t v = 0;
+    cudaSetDevice(e->dev);
+    cudaMemcpy(&v, &e->ctrl->argmax[b], 4, cudaMemcpyDeviceToHost);
+    return v;
+}
+
+extern "C" float qb_last_loop_ms(qwen_model_t* m) {
+    Engine* e = E_(m);
+    return e ? e->last_ms : 0.f;
+}
+
+extern "C" int qb_prefill(qwen_model_t* m, const uint32_t* tokens, uint32_t n, int spec) {
+    Engine* e = E_(m);
+    if (!e || n == 0 || n > (uint32_t)e->n_ctx) { set_err(-1, "qb_prefill: bad arguments"); return -1; }
+    CK(cudaSetDevice(e->dev));
+    uint32_t pos = 0, lastB = 0;
+    while (pos < n) {
+        const uint32_t B = std::min<uint32_t>(n - pos, PREFILL_MAX_B);
+        CK(cudaMemcpyAsync(e->ctrl->fwd_tok, tokens + pos, B * 4, cudaMemcpyHostToDevice, e->st));
+        CK(cudaMemcpyAsync(&e->ctrl->fwd_pos, &pos, 4, cudaMemcpyHostToDevice, e->st));
+        if (fwd_backbone(*e, (int)B, 0)) return -1;
+        if (spec) {
+            CK(cudaMemcpyAsync(e->ctrl->mtp_tok, tokens + pos, B * 4, cudaMemcpyHostToDevice, e->st));
+            CK(cudaMemcpyAsync(&e->ctrl->mtp_pos, &pos, 4, cudaMemcpyHostToDevice, e->st));
+            if (fwd_mtp(*e, (int)B, e->h_save, 0)) return -1;
+        }
+        CK(cudaStreamSynchronize(e->st));   // host token/pos sources must outlive the copies
+        pos += B;
+        lastB = B;
+    }
+    // next cand0 = argmax of the last prompt token's logits
+    CK(cudaMemcpyAsync(&e->ctrl->next_cand0, &e->ctrl->argmax[lastB - 1], 4, cudaMemcpyDeviceToDevice, e->st));
+    CK(cudaMemcpyAsync(m->logits, e->logits + (size_t)(lastB - 1) * e->V, (size_t)e->V * 4, cudaMemcpyDeviceToHost,
+                       e->st));
+    CK(cudaMemcpyAsync(m->h_save, e->h_save, (size_t)lastB * e->E * 4, cudaMemcpyDeviceToHost, e->st));
+    CK(cudaMemcpyAsync(m->mtp_h, e->mtp_h, (size_t)e->E * 4, cudaMemcpyDeviceToHost, e->st));
+    CK(cudaStreamSynchronize(e->st));
+    m->pos = n;
+    return 0;
+}
+
+extern "C" int qb_spec_generate(qwen_model_t* m, uint32_t n_predict, uint32_t n_spec, const uint32_t* forced,
+                                uint32_t n_forced, uint32_t* out_tokens, uint32_t* out_j, uint32_t max_cycles,
+                                uint32_t* n_cycles) {
+    Engine* e = E_(m);
+    if (!e || !out_tokens || m->pos == 0) { set_err(-1, "qb_spec_generate: bad arguments / no prefill"); return -1; }
+    CK(cudaSetDevice(e->dev));
+    const int k = (int)std::min<uint32_t>(n_spec, SPEC_MAX_B - 1);
+    if (k < 1) { set_err(-1, "qb_spec_generate: n_spec must be >= 1"); return -1; }
+    if (ensure_out_buffers(*e, n_predict + (uint32_t)k + 1, max_cycles, n_forced)) return -1;
+    if (!e->g_cycle || e->g_cycle_k != k) {
+        if (e->g_cycle) { cudaGraphExecDestroy(e->g_cycle); e->g_cycle = nullptr; }
+        if (capture(*e, &e->g_cycle, record_cycle, k)) return -1;
+        e->g_cycle_k = k;
+    }
+    // loop state: P = pos - 1, counters reset, host mirror mtp_h is authoritative
+    QbCtrl hc;
+    CK(cudaMemcpy(&hc, e->ctrl, sizeof hc, cudaMemcpyDeviceToHost));
+    hc.P = m->pos - 1;
+    hc.k = (uint32_t)k;
+    hc.cycle = 0;
+    hc.n_out = 0;
+    hc.n_forced = n_forced;
+    hc.cap_out = e->cap_out;
+    hc.cap_j = max_cycles < e->cap_j ? max_cycles : e->cap_j;
+    CK(cudaMemcpy(e->ctrl, &hc, sizeof hc, cudaMemcpyHostToDevice));
+    if (n_forced) CK(cudaMemcpy(e->d_forced, forced, n_forced * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(e->mtp_h, m->mtp_h, (size_t)e->E * 4, cudaMemcpyHostToDevice));
+
+    uint32_t n_out = 0, cycles = 0;
+    CK(cudaEventRecord(e->ev0, e->st));
+    while (n_out < n_predict && cycles < max_cycles) {
+        // never overshoot: each cycle emits at most k+1 tokens
+        const uint32_t rem = n_predict - n_out;
+        uint32_t batch = std::max<uint32_t>(1, rem / (uint32_t)(k + 1));
+        batch = std::min(batch, max_cycles - cycles);
+        const uint32_t P_now = m->pos - 1 + 0;   // updated below from the device
+        (void)P_now;
+        // context bound: every cycle advances P by at most k+1; verify writes P+1..P+k+1
+        for (uint32_t i = 0; i < batch; ++i) CK(cudaGraphLaunch(e->g_cycle, e->st));
+        cycles += batch;
+        uint32_t dev_counts[2];
+        CK(cudaMemcpyAsync(dev_counts, &e->ctrl->cycle, 8, cudaMemcpyDeviceToHost, e->st));   // cycle, n_out
+        CK(cudaStreamSynchronize(e->st));
+        n_out = dev_counts[1];
+        uint32_t P;
+        CK(cudaMemcpy(&P, &e->ctrl->P, 4, cudaMemcpyDeviceToHost));
+        if (P + (uint32_t)k + 3 > (uint32_t)e->n_ctx) break;   // next cycle would pass n_ctx
+    }
+    CK(cudaEventRecord(e->ev1, e->st));
+    CK(cudaEventSynchronize(e->ev1));
+    cudaEventElapsedTime(&e->last_ms, e->ev0, e->ev1);
+    const uint32_t n_copy = std::min(n_out, n_predict);
+    CK(cudaMemcpy(out_tokens, e->d_out_tok, (size_t)n_copy * 4, cudaMemcpyDeviceToHost));
+    if (out_j) CK(cudaMemcpy(out_j, e->d_out_j, (size_t)std::min(cycles, max_cycles) * 4, cudaMemcpyDeviceToHost));
+    if (n_cycles) *n_cycles = cycles;
+    // host mirrors: position, next logits (logits_b[j]), MTP hidden
+    CK(cudaMemcpy(&hc, e->ctrl, sizeof hc, cudaMemcpyDeviceToHost));
+    m->pos = hc.P + 1;
+    CK(cudaMemcpy(m->logits, e->logits + (size_t)hc.j * e->V, (size_t)e->V * 4, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(m->mtp_h, e->mtp_h, (size_t)e->E * 4, cudaMemcpyDeviceToHost));
+    return (int)n_copy;
+}
+
+extern "C" int qb_greedy_generate(qwen_model_t* m, uint32_t n_predict, uint32_t* out_tokens) {
+    Engine* e = E_(m);
+    if (!e || !out_tokens || m->pos == 0) { set_err(-1, "qb_greedy_generate: bad arguments"); return -1; }
+    if (n_predict == 0) return 0;
+    CK(cudaSetDevice(e->dev));
+    if (ensure_out_buffers(*e, n_predict + 1, 1, 1)) return -1;
+    if (!e->g_greedy && capture(*e, &e->g_greedy, record_greedy, 0)) return -1;
+    // token 0 = argmax(m->logits): the device argmax of the last forward
+    QbCtrl hc;
+    CK(cudaMemcpy(&hc, e->ctrl, sizeof hc, cudaMemcpyDeviceToHost));
+    hc.fwd_tok[0] = hc.next_cand0;
+    hc.fwd_pos = m->pos;
+    hc.greedy_n = 1;
+    hc.cap_out = e->cap_out;
+    CK(cudaMemcpy(e->ctrl, &hc, sizeof hc, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(e->d_out_tok, &hc.next_cand0, 4, cudaMemcpyHostToDevice));
+    uint32_t steps = n_predict - 1;
+    if (m->pos + steps > (uint32_t)e->n_ctx) steps = (uint32_t)e->n_ctx - m->pos;
+    CK(cudaEventRecord(e->ev0, e->st));
+    for (uint32_t i = 0; i < steps; ++i) CK(cudaGraphLaunch(e->g_greedy, e->st));
+    CK(cudaEventRecord(e->ev1, e->st));
+    CK(cudaEventSynchronize(e->ev1));
+    cudaEventElapsedTime(&e->last_ms, e->ev0, e->ev1);
+    const uint32_t n = steps + 1;
+    CK(cudaMemcpy(out_tokens, e->d_out_tok, (size_t)n * 4, cudaMemcpyDeviceToHost));
+    m->pos += steps;
+    CK(cudaMemcpy(m->logits, e->logits, (size_t)e->V * 4, cudaMemcpyDeviceToHost));
+    // keep next_cand0 = argmax of the last forward for a following call
+    CK(cudaMemcpy(&e->ctrl->next_cand0, &e->ctrl->argmax[0], 4, cudaMemcpyDeviceToDevice));
+    return (int)n;
+}
+
+extern "C" int64_t qb_read_state(qwen_model_t* m, uint32_t il, int which, float* dst, int64_t max_floats) {
+    Engine* e = E_(m);
+    if (!e) return -1;
+    cudaSetDevice(e->dev);
+    const float* src = nullptr;
+    size_t n = 0;
+    uint32_t cur = 0;
+    cudaMemcpy(&cur, &e->ctrl->cur_slot, 4, cudaMemcpyDeviceToHost);
+    if (il == e->d.n_layer) {
+        if (which == 2) { src = e->mtp_k; n = e->kv_layer; }
+        if (which == 3) { src = e->mtp_v; n = e->kv_layer; }
+    } else if (il < e->d.n_layer) {
+        const LayerW& l = e->L[il];
+        if (l.rec && which == 0) { src = e->conv_slots + cur * e->conv_slot_stride + l.ridx * e->conv_layer; n = e->conv_layer; }
+        if (l.rec && which == 1) { src = e->ssm_slots + cur * e->ssm_slot_stride + l.ridx * e->ssm_layer; n = e->ssm_layer; }
+        if (!l.rec && which == 2) { src = e->kv_k + l.aidx * e->kv_layer; n = e->kv_layer; }
+        if (!l.rec && which == 3) { src = e->kv_v + l.aidx * e->kv_layer; n = e->kv_layer; }
+    }
+    if (!src) return -1;
+    if ((int64_t)n > max_floats) n = (size_t)max_floats;
+    if (cudaMemcpy(dst, src, n * 4, cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    return (int64_t)n;
+}
+
+// ============================ C API: kernels.h ====================================
+// Host-pointer GEMV and element-wise ops.  Weights are uploaded + repacked on
+// first use and cached per device, keyed by (device, W->data, type, shape).
+
+namespace {
+struct WKey {
+    int dev;
+    const void* p;
+    int type;
+    uint64_t ne0, ne1;
+    bool operator==(const WKey& o) const { return dev == o.dev && p == o.p && type == o.type && ne0 == o.ne0 && ne1 == o.ne1; }
+};
+struct WKeyHash {
+    size_t operator()(const WKey& k) const {
+        return std::hash<const void*>()(k.p) ^ (std::hash<uint64_t>()(k.ne0 * 131 + k.ne1) << 1) ^ (size_t)k.type ^ ((size_t)k.dev << 7);
+    }
+};
+struct Scratch {
+    cudaStream_t st = nullptr;
+    float *x = nullptr, *out = nullptr;
+    size_t x_cap = 0, out_cap = 0;
+    uint2* xfrag = nullptr;
+    float *xscale = nullptr, *xsum = nullptr;
+    size_t k_cap = 0;
+    unsigned long long* keys = nullptr;
+    uint32_t* am = nullptr;
+};
+std::mutex g_mu;
+std::unordered_map<WKey, DevMat, WKeyHash> g_wcache;
+std::unordered_map<int, Scratch> g_scratch;
+
+int scratch_get(Scratch*& s, size_t x_floats, size_t out_floats, int K) {
+    int dev = 0;
+    CK(cudaGetDevice(&dev));
+    s = &g_scratch[dev];
+    if (!s->st) CK(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
+    if (x_floats > s->x_cap) {
+        if (s->x) cudaFree(s->x);
+        s->x_cap = std::max<size_t>(x_floats, 1 << 16);
+        CK(cudaMalloc(&s->x, s->x_cap * 4));
+    }
+    if (out_floats > s->out_cap) {
+        if (s->out) cudaFree(s->out);
+        s->out_cap = std::max<size_t>(out_floats, 1 << 16);
+        CK(cudaMalloc(&s->out, s->out_cap * 4));
+    }
+    if ((size_t)K > s->k_cap) {
+        if (s->xfrag) cudaFree(s->xfrag);
+        if (s->xscale) cudaFree(s->xscale);
+        if (s->xsum) cudaFree(s->xsum);
+        s->k_cap = std::max<size_t>((size_t)K, 4096);
+        const size_t kc = (s->k_cap + 255) / 256 * 256;
+        CK(cudaMalloc(&s->xfrag, kc / 32 * 2 * 2 * 32 * 8));
+        CK(cudaMemset(s->xfrag, 0, kc / 32 * 2 * 2 * 32 * 8));
+        CK(cudaMalloc(&s->xscale, QB_MAX_TOK * (kc / 256) * 4));
+        CK(cudaMalloc(&s->xsum, QB_MAX_TOK * (kc / 32) * 4));
+    }
+    if (!s->keys) {
+        CK(cudaMalloc(&s->keys, QB_MAX_TOK * sizeof(unsigned long long)));
+        CK(cudaMalloc(&s->am, QB_MAX_TOK * 4));
+    }
+    return 0;
+}
+
+int wcache_get(const gguf_tensor_info_t* W, const DevMat*& out) {
+    int dev = 0;
+    CK(cudaGetDevice(&dev));
+    const WKey key{dev, W->data, (int)W->type, W->ne[0], W->ne[1]};
+    auto it = g_wcache.find(key);
+    if (it != g_wcache.end()) { out = &it->second; return 0; }
+    DevMat m;
+    m.type = (int)W->type;
+    m.K = (int)W->ne[0];
+    m.rows = (int)W->ne[1];
+    const size_t src_bytes = gguf_row_bytes(m.type, W->ne[0]) * W->ne[1];
+    if (!src_bytes || (m.type != QB_F32 && m.K % 256)) { set_err(-1, "gemv: unsupported tensor type %d / ne0 %llu", m.type, (unsigned long long)W->ne[0]); return -1; }
+    if (m.type == QB_F32) {
+        CK(cudaMalloc(&m.w, src_bytes));
+        CK(cudaMemcpy(m.w, W->data, src_bytes, cudaMemcpyHostToDevice));
+    } else {
+        void* tmp = nullptr;
+        CK(cudaMalloc(&tmp, src_bytes));
+        CK(cudaMemcpy(tmp, W->data, src_bytes, cudaMemcpyHostToDevice));
+        CK(cudaMalloc(&m.w, qb_repacked_bytes(m.type, m.rows, m.K)));
+        CK(qb_repack(m.type, tmp, m.rows, m.K, m.w, 0));
+        CK(cudaDeviceSynchronize());
+        cudaFree(tmp);
+    }
+    out = &(g_wcache[key] = m);
+    return 0;
+}
+
+// out[t][r] for rows [r0, r1), t < n, from host x/out
+int gemv_host(const gguf_tensor_info_t* W, const float* x, uint64_t ldx, int n, float* out, uint64_t ldo, uint64_t r0,
+              uint64_t r1) {
+    if (!W || !x || !out || n < 1) { set_err(-1, "gemv: bad arguments"); return -1; }
+    std::lock_guard<std::mutex> lk(g_mu);
+    const DevMat* M = nullptr;
+    if (wcache_get(W, M)) return -1;
+    const int K = M->K;
+    if (r1 > (uint64_t)M->rows) r1 = M->rows;
+    if (r0 >= r1) return 0;
+    Scratch* s = nullptr;
+    for (int t0 = 0; t0 < n; t0 += QB_MAX_TOK) {
+        const int nn = std::min(QB_MAX_TOK, n - t0);
+        if (scratch_get(s, (size_t)nn * K, (size_t)nn * M->rows, K)) return -1;
+        CK(cudaMemcpy2DAsync(s->x, (size_t)K * 4, x + (size_t)t0 * ldx, ldx * 4, (size_t)K * 4, nn, cudaMemcpyHostToDevice, s->st));
+        const int t_lo = (int)(r0 / QB_TILE);
+        if (M->type == QB_F32) {
+            CK(qb_qmv_f32((const float*)M->w, M->rows, K, s->x, K, nn, s->out, M->rows, 0, (int)r0, (int)r1, s->st));
+        } else {
+            QbXIn in{s->x, K, nullptr, K};
+            CK(qb_xprep(&in, 1, nn, 1e-6f, s->xfrag, s->xscale, s->xsum, (M->type == QB_Q4_K || M->type == QB_Q5_K) ? 1 : 0, s->st));
+            QbQSeg seg;
+            seg.w = (const uint8_t*)M->w + (size_t)t_lo * (K / qb_unit_cols(M->type)) * qb_unit_bytes(M->type);
+            seg.out = s->out + (size_t)t_lo * QB_TILE;
+            seg.ldo = M->rows;
+            seg.rows = (int)(r1 - (uint64_t)t_lo * QB_TILE);
+            CK(qb_qmv(M->type, &seg, 1, K, nn, s->xfrag, s->xscale, s->xsum, 0, (int)(r0 - (uint64_t)t_lo * QB_TILE),
+                      (int)(r1 - (uint64_t)t_lo * QB_TILE), s->st));
+        }
+        CK(cudaMemcpy2DAsync(out + (size_t)t0 * ldo + r0, ldo * 4, s->out + r0, (size_t)M->rows * 4, (size_t)(r1 - r0) * 4, nn,
+                             cudaMemcpyDeviceToHost, s->st));
+        CK(cudaStreamSynchronize(s->st));
+    }
+    return 0;
+}
+
+int op_host(int which, float* out, const float* x, const float* w, uint64_t n, float eps) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    Scratch* s = nullptr;
+    if (scratch_get(s, n, n, 0)) return -1;
+    CK(cudaMemcpyAsync(s->x, x, n * 4, cudaMemcpyHostToDevice, s->st));
+    float* wd = nullptr;
+    if (w) {
+        CK(cudaMemcpyAsync(s->out, w, n * 4, cudaMemcpyHostToDevice, s->st));
+        wd = s->out;
+    }
+    switch (which) {
+    case 0: CK(qb_op_rmsnorm(s->x, s->x, wd, (long long)n, eps, s->st)); break;
+    case 1: CK(qb_op_l2norm(s->x, s->x, (long long)n, eps, s->st)); break;
+    case 2: CK(qb_op_act(0, s->x, (long long)n, s->st)); break;
+    case 3: CK(qb_op_act(1, s->x, (long long)n, s->st)); break;
+    case 4: CK(qb_op_act(2, s->x, (long long)n, s->st)); break;
+    case 5: CK(qb_op_softmax(s->x, (long long)n, s->st)); break;
+    }
+    CK(cudaMemcpyAsync(out, s->x, n * 4, cudaMemcpyDeviceToHost, s->st));
+    CK(cudaStreamSynchronize(s->st));
+    return 0;
+}
+}  // namespace
+
+extern "C" void gemv_rows(const gguf_tensor_info_t* W, const float* x, float* out, uint64_t r0, uint64_t r1) {
+    gemv_host(W, x, W ? W->ne[0] : 0, 1, out, W ? W->ne[1] : 0, r0, r1);
+}
+extern "C" void gemv(pool_t*, const gguf_tensor_info_t* W, const float* x, float* out) {
+    gemv_host(W, x, W ? W->ne[0] : 0, 1, out, W ? W->ne[1] : 0, 0, W ? W->ne[1] : 0);
+}
+extern "C" void gemv_rows_batch(const gguf_tensor_info_t* W, const float* x, uint64_t ldx, int n, float* out, uint64_t ldo,
+                                uint64_t r0, uint64_t r1) {
+    gemv_host(W, x, ldx, n, out, ldo, r0, r1);
+}
+extern "C" void gemv_batch(pool_t*, const gguf_tensor_info_t* W, const float* x, uint64_t ldx, int n, float* out,
+                           uint64_t ldo) {
+    gemv_host(W, x, ldx, n, out, ldo, 0, W ? W->ne[1] : 0);
+}
+extern "C" void gemv_multi(pool_t*, const gguf_tensor_info_t* const* Ws, const float* x, float* const* outs, int n_mat) {
+    for (int i = 0; i < n_mat; ++i) gemv_host(Ws[i], x, Ws[i]->ne[0], 1, outs[i], Ws[i]->ne[1], 0, Ws[i]->ne[1]);
+}
+extern "C" void gemv_multi_batch(pool_t*, const gguf_tensor_info_t* const* Ws, const float* x, uint64_t ldx, int n,
+                                 float* const* outs, const uint64_t* ldos, int n_mat) {
+    for (int i = 0; i < n_mat; ++i) gemv_host(Ws[i], x, ldx, n, outs[i], ldos[i], 0, Ws[i]->ne[1]);
+}
+extern "C" void rmsnorm(float* out, const float* x, const float* weight, uint64_t n, float eps) {
+    op_host(0, out, x, weight, n, eps);
+}
+extern "C" void l2norm(float* out, const float* x, uint64_t n, float eps) { op_host(1, out, x, nullptr, n, eps); }
+extern "C" void silu_inplace(float* x, uint64_t n) { op_host(2, x, x, nullptr, n, 0.f); }
+extern "C" void sigmoid_inplace(float* x, uint64_t n) { op_host(3, x, x, nullptr, n, 0.f); }
+extern "C" void softplus_inplace(float* x, uint64_t n) { op_host(4, x, x, nullptr, n, 0.f); }
+extern "C" void softmax_inplace(float* x, uint64_t n) {
+    if (n) op_host(5, x, x, nullptr, n, 0.f);
+}
+
+extern "C" uint32_t model_sample_greedy(const float* logits, uint32_t vocab_size) {
+    if (!logits || vocab_size == 0) return 0;
+    std::lock_guard<std::mutex> lk(g_mu);
+    Scratch* s = nullptr;
+    if (scratch_get(s, vocab_size, 0, 0)) return 0;
+    uint32_t r = 0;
+    if (cudaMemcpyAsync(s->x, logits, (size_t)vocab_size * 4, cudaMemcpyHostToDevice, s->st) != cudaSuccess ||
+        qb_argmax_reset(s->keys, 1, s->st) != cudaSuccess ||
+        qb_argmax(s->x, vocab_size, (int)vocab_size, 1, s->keys, s->st) != cudaSuccess ||
+        qb_argmax_to_u32(s->keys, 1, s->am, s->st) != cudaSuccess ||
+        cudaMemcpyAsync(&r, s->am, 4, cudaMemcpyDeviceToHost, s->st) != cudaSuccess ||
+        cudaStreamSynchronize(s->st) != cudaSuccess) {
+        set_err(-1, "model_sample_greedy: CUDA failure");
+        return 0;
+    }
+    return r;
+}

@@ -1,0 +1,65 @@
+// Host-side launchers of the sm_100a kernels (internal interface of libqwenb200).
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+struct QbXIn {               // one segment of a GEMV input vector set
+    const float* x;          // token t at x + t * ldx
+    long long ldx;
+    const float* norm_w;     // RMSNorm weight applied first (nullptr: none)
+    int len;                 // columns, multiple of 256
+};
+
+struct QbQSeg {              // one matrix of a fused GEMV launch
+    const void* w;           // repacked weights (qb_repack)
+    float* out;
+    long long ldo;
+    int rows;
+};
+
+// ---- quantised GEMV (qb_quant.cu) ----
+cudaError_t qb_quant_init_constants();
+size_t qb_repacked_bytes(int type, int rows, int K);
+cudaError_t qb_repack(int type, const void* src_dev, int rows, int K, void* dst_dev, cudaStream_t st);
+cudaError_t qb_xprep(const QbXIn* in, int nseg, int N, float eps, uint2* xfrag, float* xscale, float* xsum,
+                     int want_xsum, cudaStream_t st);
+cudaError_t qb_qmv(int type, const QbQSeg* segs, int nseg, int K, int N, const uint2* xfrag,
+                   const float* xscale, const float* xsum, int accumulate, int row_lo, int row_hi,
+                   cudaStream_t st);
+cudaError_t qb_qmv_f32(const float* W, int rows, int K, const float* x, long long ldx, int N, float* out,
+                       long long ldo, int accumulate, int row_lo, int row_hi, cudaStream_t st);
+
+// ---- layer kernels (qb_layers.cu) ----
+struct QbCtrl;   // device control block (qb_engine.h)
+
+cudaError_t qb_embed(int type, const void* tok_embd, int n_embd, const uint32_t* tokens, int B, float* out,
+                     long long ldo, cudaStream_t st);
+cudaError_t qb_gdn_conv(const float* qkv, long long ld_qkv, int conv_dim, int B, const float* conv_w,
+                        float* state_slots, size_t slot_stride, const uint32_t* cur_slot, int ckpt,
+                        float* out, long long ld_out, cudaStream_t st);
+cudaError_t qb_gdn_recur(const float* qkvc, long long ld_qkvc, const float* beta, const float* alpha,
+                         long long ld_ba, const float* dt_bias, const float* ssm_a, int n_k, int n_v,
+                         int dk, int B, float eps, float* state_slots, size_t slot_stride,
+                         const uint32_t* cur_slot, int ckpt, float* out, long long ld_out, cudaStream_t st);
+cudaError_t qb_gdn_out(const float* o, const float* z, long long ld, const float* norm_w, int n_v, int dv,
+                       int B, float eps, float* y, cudaStream_t st);
+cudaError_t qb_attn_prep(float* q, long long ldq, const float* kv, long long ldkv, const float* q_norm,
+                         const float* k_norm, int n_head, int n_kv, int hd, int rope_half,
+                         const float* rope_cos, const float* rope_sin, const uint32_t* pos, int B, float eps,
+                         float* k_cache, float* v_cache, cudaStream_t st);
+cudaError_t qb_attn_decode(const float* q, long long ldq, const float* k_cache, const float* v_cache,
+                           int n_head, int n_kv, int hd, const uint32_t* pos, int B, int n_ctx, float* out,
+                           long long ldo, cudaStream_t st);
+cudaError_t qb_silu_mul(const float* gate, const float* up, long long ld, int n, int B, float* out,
+                        cudaStream_t st);
+cudaError_t qb_argmax_reset(unsigned long long* keys, int B, cudaStream_t st);
+cudaError_t qb_argmax(const float* x, long long ldx, int n, int B, unsigned long long* keys,
+                      cudaStream_t st);
+cudaError_t qb_argmax_to_u32(const unsigned long long* keys, int B, uint32_t* out, cudaStream_t st);
+
+// element-wise ops behind the kernels.h host-pointer API
+cudaError_t qb_op_rmsnorm(float* out, const float* x, const float* w, long long n, float eps,
+                          cudaStream_t st);
+cudaError_t qb_op_l2norm(float* out, const float* x, long long n, float eps, cudaStream_t st);
+cudaError_t qb_op_act(int which, float* x, long long n, cudaStream_t st);   // 0 silu 1 sigmoid 2 softplus
+cudaError_t qb_op_softmax(float* x, long long n, cudaStream_t st);

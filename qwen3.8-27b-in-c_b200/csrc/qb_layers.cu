@@ -1,0 +1,646 @@
+// Per-layer kernels of the hybrid decoder (everything except the weight GEMVs).
+//
+// Reference (all under src/): embedding dequant quant.c:86-182 / model.c:981-983,
+// Gated DeltaNet model.c:494-595 (recurrence) and 845-941 (conv1d, norms,
+// gating), gated attention model.c:318-406 (RoPE, heads) and 760-811 (Q/K
+// norm, KV append), SwiGLU model.c:830-836, greedy argmax model.c:746-756.
+//
+// Element-wise arithmetic follows the reference order where that is cheap:
+// the AVX2 polynomial exp (kernels.c:807-822) is restated exactly, products
+// that the reference rounds separately (ISO C, no FP contraction) use the
+// _rn intrinsics, and the Gated DeltaNet row dots reproduce the 8-lane
+// accumulation + horizontal-sum tree of the AVX2 code.  Scalar libm calls
+// (expf / log1pf in the gates and the softmax tail) are evaluated in double
+// and rounded once.
+#include "qb_common.cuh"
+#include "qb_kernels.h"
+
+namespace {
+
+constexpr int kNSlot = 4;   // recurrent-state slots (rollback targets)
+
+// AVX2 exp of the reference (src/kernels.c:807-822), lane-for-lane.
+__device__ __forceinline__ float exp_poly(float x) {
+    const float xc = fmaxf(fminf(x, 88.0f), -88.0f);
+    const float k = rintf(__fmul_rn(xc, 1.4426950408889634f));
+    const float r = fmaf(-k, 0.6931471805599453f, xc);
+    float p = 0.000198412698f;
+    p = fmaf(p, r, 0.00139304842f);
+    p = fmaf(p, r, 0.00833333333f);
+    p = fmaf(p, r, 0.04166666666f);
+    p = fmaf(p, r, 0.16666666666f);
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    const int ik = (int)k;
+    const float pow2 = __int_as_float((int)((unsigned)(ik + 127) << 23));
+    return __fmul_rn(p, pow2);
+}
+
+// silu / sigmoid of the vector body (src/kernels.c:825-871); the reference
+// only takes its scalar tail for n % 8 != 0, which no layer width hits.
+__device__ __forceinline__ float silu_ref(float v) {
+    const float e = exp_poly(__fsub_rn(0.0f, v));
+    const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
+    return __fmul_rn(v, sig);
+}
+__device__ __forceinline__ float sigmoid_ref(float v) {
+    const float e = exp_poly(__fsub_rn(0.0f, v));
+    return __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
+}
+__device__ __forceinline__ float expf_cr(float x) { return (float)exp((double)x); }
+__device__ __forceinline__ float log1pf_cr(float x) { return (float)log1p((double)x); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// horizontal sum of 8 lanes in the AVX2 hsum256 order ((0+4)+(1+5))+((2+6)+(3+7))
+__device__ __forceinline__ float hsum8(float v) {
+    v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));
+    v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
+    v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
+    return v;
+}
+
+// ----------------------------- embedding ------------------------------------
+__device__ __forceinline__ float f16bits(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+__device__ __forceinline__ uint16_t ld16(const uint8_t* p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+
+__device__ float dequant_elem(int type, const uint8_t* row, int e) {
+    switch (type) {
+    case QB_F32: return reinterpret_cast<const float*>(row)[e];
+    case QB_Q8_0: {
+        const uint8_t* b = row + (e >> 5) * 34;
+        return __fmul_rn(f16bits(ld16(b)), (float)(int8_t)b[2 + (e & 31)]);
+    }
+    case QB_IQ4_XS: {
+        const uint8_t* b = row + (e >> 8) * 136;
+        const int ib = (e & 255) >> 5, j = e & 31;
+        const int ls = ((b[4 + ib / 2] >> (4 * (ib % 2))) & 0xF) | (((ld16(b + 2) >> (2 * ib)) & 3) << 4);
+        const float dl = __fmul_rn(f16bits(ld16(b)), (float)(ls - 32));
+        const uint8_t q = b[8 + ib * 16 + (j & 15)];
+        const int nib = j < 16 ? (q & 0xF) : (q >> 4);
+        const int8_t kv[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+        return __fmul_rn(dl, (float)kv[nib]);
+    }
+    case QB_Q6_K: {
+        const uint8_t* b = row + (e >> 8) * 210;
+        const int i = e & 255, n = i >> 7, r = i & 127, m = r >> 5, l = r & 31;
+        const int lo = (b[64 * n + 32 * (m & 1) + l] >> (4 * (m >> 1))) & 0xF;
+        const int hi = (b[128 + 32 * n + l] >> (2 * m)) & 3;
+        const int q = (lo | (hi << 4)) - 32;
+        const int sc = (int8_t)b[192 + 8 * n + (l >> 4) + 2 * m];
+        return __fmul_rn(__fmul_rn(f16bits(ld16(b + 208)), (float)sc), (float)q);
+    }
+    case QB_Q4_K:
+    case QB_Q5_K: {
+        const bool q5 = type == QB_Q5_K;
+        const uint8_t* b = row + (e >> 8) * (q5 ? 176 : 144);
+        const int i = e & 255, j = i >> 6, half = (i >> 5) & 1, l = i & 31;
+        const int is = 2 * j + half;
+        const uint8_t* s = b + 4;
+        int sc, m;
+        if (is < 4) { sc = s[is] & 63; m = s[is + 4] & 63; }
+        else { sc = (s[is + 4] & 0xF) | ((s[is - 4] >> 6) << 4); m = (s[is + 4] >> 4) | ((s[is] >> 6) << 4); }
+        const float d1 = __fmul_rn(f16bits(ld16(b)), (float)sc);
+        const float m1 = __fmul_rn(f16bits(ld16(b + 2)), (float)m);
+        const uint8_t* qs = b + (q5 ? 48 : 16) + 32 * j;
+        int q = half ? (qs[l] >> 4) : (qs[l] & 0xF);
+        if (q5) q += (b[16 + l] >> is) & 1 ? 16 : 0;
+        return __fsub_rn(__fmul_rn(d1, (float)q), m1);
+    }
+    default: return 0.f;
+    }
+}
+
+__host__ __device__ inline size_t row_bytes_of(int type, int n) {
+    switch (type) {
+    case QB_F32: return (size_t)n * 4;
+    case QB_Q8_0: return (size_t)(n / 32) * 34;
+    case QB_IQ4_XS: return (size_t)(n / 256) * 136;
+    case QB_Q6_K: return (size_t)(n / 256) * 210;
+    case QB_Q4_K: return (size_t)(n / 256) * 144;
+    case QB_Q5_K: return (size_t)(n / 256) * 176;
+    default: return 0;
+    }
+}
+
+__global__ void embed_kernel(int type, const uint8_t* __restrict__ E, int n, const uint32_t* __restrict__ tok,
+                             float* __restrict__ out, long long ldo) {
+    const int b = blockIdx.y;
+    const uint8_t* row = E + (size_t)tok[b] * row_bytes_of(type, n);
+    for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < n; e += gridDim.x * blockDim.x)
+        out[(size_t)b * ldo + e] = dequant_elem(type, row, e);
+}
+
+// ------------------------------ GDN conv ------------------------------------
+// conv1d k=4 over the B tokens, state [c][4] newest last (src/model.c:891-903),
+// checkpoints per token (904-907), then SiLU (909).
+__global__ void gdn_conv_kernel(const float* __restrict__ qkv, long long ld_qkv, int conv_dim, int B,
+                                const float* __restrict__ w, float* __restrict__ slots, size_t slot_stride,
+                                const uint32_t* __restrict__ cur_slot, int ckpt, float* __restrict__ out,
+                                long long ld_out) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= conv_dim) return;
+    const int cur = (int)*cur_slot;
+    const float4 s0 = *reinterpret_cast<const float4*>(slots + (size_t)cur * slot_stride + (size_t)c * 4);
+    const float4 wv = *reinterpret_cast<const float4*>(w + (size_t)c * 4);
+    float s[4] = {s0.x, s0.y, s0.z, s0.w};
+    for (int b = 0; b < B; ++b) {
+        s[0] = s[1];
+        s[1] = s[2];
+        s[2] = s[3];
+        s[3] = qkv[(size_t)b * ld_qkv + c];
+        float y = __fmul_rn(s[0], wv.x);
+        y = __fadd_rn(y, __fmul_rn(s[1], wv.y));
+        y = __fadd_rn(y, __fmul_rn(s[2], wv.z));
+        y = __fadd_rn(y, __fmul_rn(s[3], wv.w));
+        int slot = -1;
+        if (ckpt) {
+            if (b < kNSlot - 1 || b == B - 1) slot = b < kNSlot - 1 ? b : kNSlot - 1;
+        } else if (b == B - 1) {
+            slot = cur;
+        }
+        if (slot >= 0)
+            *reinterpret_cast<float4*>(slots + (size_t)slot * slot_stride + (size_t)c * 4) =
+                make_float4(s[0], s[1], s[2], s[3]);
+        out[(size_t)b * ld_out + c] = silu_ref(y);
+    }
+}
+
+// --------------------------- GDN recurrence ---------------------------------
+// Grid (n_v, dk/16); block 128 = 4 warps x 4 rows x 8 lanes.  Lane l8 of a row
+// owns columns l8 + 8m (m = 0..15): the AVX2 accumulator lane l8 of
+// gdn_ssm_head (src/model.c:502-523).  q and k are L2-normalised here
+// (src/model.c:911-916, kernels.c:780-805) in the same 8-lane order.
+constexpr int kDK = 128;
+
+__global__ void __launch_bounds__(128) gdn_recur_kernel(
+    const float* __restrict__ qkvc, long long ld_qkvc, const float* __restrict__ beta,
+    const float* __restrict__ alpha, long long ld_ba, const float* __restrict__ dt_bias,
+    const float* __restrict__ ssm_a, int n_k, int n_v, int B, float eps, float* __restrict__ slots,
+    size_t slot_stride, const uint32_t* __restrict__ cur_slot, int ckpt, float* __restrict__ out,
+    long long ld_out) {
+    __shared__ float qn[QB_MAX_TOK][kDK], kn[QB_MAX_TOK][kDK];
+    __shared__ float kq_s[QB_MAX_TOK], beta_s[QB_MAX_TOK], decay_s[QB_MAX_TOK];
+    const int h = blockIdx.x, kh = h % n_k;
+    const int tid = threadIdx.x, lane = tid & 31, l8 = lane & 7;
+    const int grp = tid >> 3;   // 16 groups of 8 lanes
+
+    // L2 norms: group (b, which) for b < B, which in {q, k}.  Every lane of a
+    // warp runs the shuffles; inactive groups work on zeros and store nothing.
+    for (int base = 0; base < 2 * B; base += 16) {
+        const int gi = base + grp;
+        const bool act = gi < 2 * B;
+        const int b = act ? gi >> 1 : 0, which = gi & 1;
+        const float* src = qkvc + (size_t)b * ld_qkvc + (size_t)which * n_k * kDK + (size_t)kh * kDK;
+        float acc = 0.f;
+#pragma unroll
+        for (int m = 0; m < 16; ++m) {
+            const float v = act ? src[l8 + 8 * m] : 0.f;
+            acc = fmaf(v, v, acc);
+        }
+        const float ss = hsum8(acc);
+        const float nrm = sqrtf(ss);
+        const float scale = __fdiv_rn(1.0f, nrm > eps ? nrm : eps);
+        if (act) {
+            float* dst = which ? kn[b] : qn[b];
+#pragma unroll
+            for (int m = 0; m < 16; ++m) dst[l8 + 8 * m] = __fmul_rn(src[l8 + 8 * m], scale);
+        }
+    }
+    __syncthreads();
+    for (int base = 0; base < B; base += 16) {
+        const int b = base + grp;
+        const bool act = b < B;
+        float acc = 0.f;
+#pragma unroll
+        for (int m = 0; m < 16; ++m)
+            acc = act ? fmaf(kn[b][l8 + 8 * m], qn[b][l8 + 8 * m], acc) : 0.f;
+        const float kq = hsum8(acc);
+        if (act && l8 == 0) {
+            kq_s[b] = kq;
+            beta_s[b] = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf_cr(-beta[(size_t)b * ld_ba + h])));
+            const float a_raw = __fadd_rn(alpha[(size_t)b * ld_ba + h], dt_bias[h]);
+            const float a_sp = a_raw > 30.0f ? a_raw : log1pf_cr(expf_cr(a_raw));
+            decay_s[b] = expf_cr(__fmul_rn(ssm_a[h], a_sp));
+        }
+    }
+    __syncthreads();
+
+    const int row = blockIdx.y * 16 + (tid >> 3);
+    const int cur = (int)*cur_slot;
+    const size_t head_off = (size_t)h * kDK * kDK + (size_t)row * kDK;
+    float S[16];
+    {
+        const float* src = slots + (size_t)cur * slot_stride + head_off;
+#pragma unroll
+        for (int m = 0; m < 16; ++m) S[m] = src[l8 + 8 * m];
+    }
+    const float q_scale = __fdiv_rn(1.0f, sqrtf((float)kDK));
+    for (int b = 0; b < B; ++b) {
+        float ak = 0.f, aq = 0.f;
+#pragma unroll
+        for (int m = 0; m < 16; ++m) {
+            ak = fmaf(S[m], kn[b][l8 + 8 * m], ak);
+            aq = fmaf(S[m], qn[b][l8 + 8 * m], aq);
+        }
+        const float sk = hsum8(ak), sq = hsum8(aq);
+        const float decay = decay_s[b];
+        const float v = qkvc[(size_t)b * ld_qkvc + (size_t)2 * n_k * kDK + (size_t)h * kDK + row];
+        const float delta = __fmul_rn(decay, sk);
+        const float dj = __fmul_rn(__fsub_rn(v, delta), beta_s[b]);
+        const float o = __fmul_rn(__fadd_rn(__fmul_rn(decay, sq), __fmul_rn(dj, kq_s[b])), q_scale);
+#pragma unroll
+        for (int m = 0; m < 16; ++m) S[m] = fmaf(dj, kn[b][l8 + 8 * m], __fmul_rn(decay, S[m]));
+        if (l8 == 0) out[(size_t)b * ld_out + (size_t)h * kDK + row] = o;
+        int slot = -1;
+        if (ckpt) {
+            if (b < kNSlot - 1 || b == B - 1) slot = b < kNSlot - 1 ? b : kNSlot - 1;
+        } else if (b == B - 1) {
+            slot = cur;
+        }
+        if (slot >= 0) {
+            float* dst = slots + (size_t)slot * slot_stride + head_off;
+#pragma unroll
+            for (int m = 0; m < 16; ++m) dst[l8 + 8 * m] = S[m];
+        }
+    }
+}
+
+// per (token, v-head): RMSNorm(o_h, ssm_norm) * SiLU(z_h)  (src/model.c:927-941)
+__global__ void gdn_out_kernel(const float* __restrict__ o, const float* __restrict__ z, long long ld,
+                               const float* __restrict__ w, int dv, float eps, float* __restrict__ y) {
+    const int b = blockIdx.y, h = blockIdx.x;
+    const int lane = threadIdx.x;   // 32 lanes, dv = 128: 4 values each, 8-lane chains in lanes 0..7
+    const float* oh = o + (size_t)b * ld + (size_t)h * dv;
+    const float* zh = z + (size_t)b * ld + (size_t)h * dv;
+    // 8-lane accumulation of the AVX2 rmsnorm; lanes 8..31 repeat lanes 0..7
+    float acc = 0.f;
+    for (int m = 0; m < dv / 8; ++m) {
+        const float v = oh[(lane & 7) + 8 * m];
+        acc = fmaf(v, v, acc);
+    }
+    const float ssum = hsum8(acc);
+    const float mean = __fdiv_rn(ssum, (float)dv);
+    const float scale = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean, eps)));
+    for (int i = lane; i < dv; i += 32) {
+        const float nv = __fmul_rn(__fmul_rn(oh[i], scale), w[i]);
+        y[(size_t)b * ld + (size_t)h * dv + i] = __fmul_rn(nv, silu_ref(zh[i]));
+    }
+}
+
+// ----------------------------- attention ------------------------------------
+// One warp per (token, head or kv-head).  Lane owns elements lane + 32j.
+// q: RMSNorm(q_norm) then RoPE in place; k: RMSNorm(k_norm), append to the
+// cache at pos+b, RoPE in the cache; v: append (src/model.c:784-806).
+__global__ void attn_prep_kernel(float* __restrict__ q, long long ldq, const float* __restrict__ kv,
+                                 long long ldkv, const float* __restrict__ qw, const float* __restrict__ kw,
+                                 int n_head, int n_kv, int hd, int half, const float* __restrict__ rc,
+                                 const float* __restrict__ rs, const uint32_t* __restrict__ pos0, float eps,
+                                 float* __restrict__ kc, float* __restrict__ vc) {
+    const int b = blockIdx.y;
+    const int unit = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    const int nj = hd / 32;   // 8 for hd = 256
+    const uint32_t pos = *pos0 + b;
+    const int kvrow = n_kv * hd;
+    if (unit >= n_head + 2 * n_kv) return;
+    float v[8];
+    if (unit >= n_head + n_kv) {   // V: copy to cache
+        const int kh = unit - n_head - n_kv;
+        const float* src = kv + (size_t)b * ldkv + kvrow + (size_t)kh * hd;
+        float* dst = vc + (size_t)pos * kvrow + (size_t)kh * hd;
+        for (int j = 0; j < nj; ++j) dst[lane + 32 * j] = src[lane + 32 * j];
+        return;
+    }
+    const bool is_q = unit < n_head;
+    const int hh = is_q ? unit : unit - n_head;
+    const float* src = is_q ? q + (size_t)b * ldq + (size_t)hh * 2 * hd : kv + (size_t)b * ldkv + (size_t)hh * hd;
+    const float* w = is_q ? qw : kw;
+    float ss = 0.f;
+    for (int j = 0; j < nj; ++j) {
+        v[j] = src[lane + 32 * j];
+        ss = fmaf(v[j], v[j], ss);
+    }
+    ss = warp_sum(ss);
+    const float scale = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)hd), eps)));
+    for (int j = 0; j < nj; ++j) v[j] = __fmul_rn(__fmul_rn(v[j], scale), w[lane + 32 * j]);
+    // RoPE pairs (i, i + half) for i < half (NeoX, partial): half = 32 -> (lane, lane + 32)
+    const float* cs = rc + (size_t)pos * half;
+    const float* sn = rs + (size_t)pos * half;
+    for (int i0 = 0; i0 < half; i0 += 32) {
+        const int i = i0 + lane;
+        if (i < half) {
+            // element i lives in slot i/32, element i+half in slot (i+half)/32 (both on this lane
+            // when half is a multiple of 32)
+            const int ja = i >> 5, jb = (i + half) >> 5;
+            const float v0 = v[ja], v1 = v[jb];
+            v[ja] = __fsub_rn(__fmul_rn(v0, cs[i]), __fmul_rn(v1, sn[i]));
+            v[jb] = __fadd_rn(__fmul_rn(v0, sn[i]), __fmul_rn(v1, cs[i]));
+        }
+    }
+    float* dst = is_q ? q + (size_t)b * ldq + (size_t)hh * 2 * hd : kc + (size_t)pos * kvrow + (size_t)hh * hd;
+    for (int j = 0; j < nj; ++j) dst[lane + 32 * j] = v[j];
+}
+
+// One CTA (256 threads = hd) per (head, token).  Scores over t <= pos+b,
+// softmax (max-subtracted; polynomial exp on the 8-aligned body and
+// correctly-rounded expf on the tail, sum in double as src/kernels.c:901-939),
+// then out[i] = sum_t p_t v_t[i] accumulated in t order, times sigmoid(gate).
+__global__ void __launch_bounds__(256) attn_decode_kernel(const float* __restrict__ q, long long ldq,
+                                                          const float* __restrict__ kc,
+                                                          const float* __restrict__ vc, int n_head, int n_kv,
+                                                          int hd, const uint32_t* __restrict__ pos0,
+                                                          float* __restrict__ out, long long ldo) {
+    extern __shared__ float sc[];   // [n_ctx] scores
+    __shared__ float qs[256];
+    __shared__ double red_d[8];
+    __shared__ float red_f[8];
+    const int h = blockIdx.x, b = blockIdx.y;
+    const int kh = h / (n_head / n_kv);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int pl = (int)*pos0 + b;
+    const int n = pl + 1;
+    const int kvrow = n_kv * hd;
+    const float* qh = q + (size_t)b * ldq + (size_t)h * 2 * hd;
+    qs[tid] = qh[tid];
+    __syncthreads();
+    const float scale_attn = __fdiv_rn(1.0f, sqrtf((float)hd));
+    // scores: warp per position, lane owns 8 elements
+    for (int t = warp; t < n; t += 8) {
+        const float* kt = kc + (size_t)t * kvrow + (size_t)kh * hd;
+        float a = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) a = fmaf(qs[lane + 32 * j], kt[lane + 32 * j], a);
+        a = warp_sum(a);
+        if (lane == 0) sc[t] = __fmul_rn(a, scale_attn);
+    }
+    __syncthreads();
+    float mx = -INFINITY;
+    for (int t = tid; t < n; t += 256) mx = fmaxf(mx, sc[t]);
+    mx = warp_max(mx);
+    if (lane == 0) red_f[warp] = mx;
+    __syncthreads();
+    mx = red_f[0];
+    for (int i = 1; i < 8; ++i) mx = fmaxf(mx, red_f[i]);
+    const int body = n & ~7;
+    double s = 0.0;
+    for (int t = tid; t < n; t += 256) {
+        const float d = __fsub_rn(sc[t], mx);
+        const float e = t < body ? exp_poly(d) : expf_cr(d);
+        sc[t] = e;
+        s += (double)e;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    __syncthreads();
+    if (lane == 0) red_d[warp] = s;
+    __syncthreads();
+    double tot = 0.0;
+    for (int i = 0; i < 8; ++i) tot += red_d[i];
+    const float inv = (float)(1.0 / tot);
+    for (int t = tid; t < n; t += 256) sc[t] = __fmul_rn(sc[t], inv);
+    __syncthreads();
+    float acc = 0.f;
+    const float* vcol = vc + (size_t)kh * hd + tid;
+    for (int t = 0; t < n; ++t) acc = fmaf(sc[t], vcol[(size_t)t * kvrow], acc);
+    const float g = sigmoid_ref(qh[hd + tid]);
+    out[(size_t)b * ldo + (size_t)h * hd + tid] = __fmul_rn(acc, g);
+}
+
+// SwiGLU: silu(gate) * up (src/model.c:830-836)
+__global__ void silu_mul_kernel(const float* __restrict__ gate, const float* __restrict__ up, long long ld,
+                                int n, float* __restrict__ out) {
+    const int b = blockIdx.y;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const size_t o = (size_t)b * ld + i;
+        out[o] = __fmul_rn(silu_ref(gate[o]), up[o]);
+    }
+}
+
+// ------------------------------- argmax --------------------------------------
+// key = ordered(value) << 32 | ~index: the max key is the largest value with
+// the lowest index among equals (first maximum wins, src/model.c:746-756).
+__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t i) {
+    uint32_t u = __float_as_uint(v);
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)u << 32) | (0xFFFFFFFFu - i);
+}
+
+__global__ void argmax_reset_kernel(unsigned long long* keys, int B) {
+    if (threadIdx.x < B) keys[threadIdx.x] = 0ull;
+}
+
+__global__ void argmax_kernel(const float* __restrict__ x, long long ldx, int n,
+                              unsigned long long* __restrict__ keys) {
+    const int b = blockIdx.y;
+    const float* xr = x + (size_t)b * ldx;
+    unsigned long long best = 0ull;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const unsigned long long k = argmax_key(xr[i], (uint32_t)i);
+        best = k > best ? k : best;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+        best = other > best ? other : best;
+    }
+    if ((threadIdx.x & 31) == 0) atomicMax(keys + b, best);
+}
+
+__global__ void argmax_to_u32_kernel(const unsigned long long* keys, int B, uint32_t* out) {
+    if (threadIdx.x < B) out[threadIdx.x] = 0xFFFFFFFFu - (uint32_t)(keys[threadIdx.x] & 0xFFFFFFFFull);
+}
+
+// --------------------- kernels.h element-wise ops -----------------------------
+__global__ void op_rmsnorm_kernel(float* out, const float* x, const float* w, long long n, float eps) {
+    __shared__ float sh[32];
+    float ss = 0.f;
+    for (long long i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += sh[i];
+    const float scale = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(tot, (float)n), eps)));
+    __syncthreads();
+    for (long long i = threadIdx.x; i < n; i += blockDim.x)
+        out[i] = w ? __fmul_rn(__fmul_rn(x[i], scale), w[i]) : __fmul_rn(x[i], scale);
+}
+
+__global__ void op_l2norm_kernel(float* out, const float* x, long long n, float eps) {
+    __shared__ float sh[32];
+    float ss = 0.f;
+    for (long long i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += sh[i];
+    const float nrm = sqrtf(tot);
+    const float scale = __fdiv_rn(1.0f, nrm > eps ? nrm : eps);
+    __syncthreads();
+    for (long long i = threadIdx.x; i < n; i += blockDim.x) out[i] = __fmul_rn(x[i], scale);
+}
+
+// silu / sigmoid: vector body via the polynomial exp, scalar tail (n % 8) via
+// expf with the reference's clamps (src/kernels.c:825-871); softplus is scalar
+// in the reference (874-885).
+__global__ void op_act_kernel(int which, float* x, long long n) {
+    const long long body = n & ~7ll;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const float v = x[i];
+        float r;
+        if (which == 0) {
+            if (i < body) r = silu_ref(v);
+            else r = v < -20.0f ? __fmul_rn(v, expf_cr(v)) : v > 20.0f ? v : __fdiv_rn(v, __fadd_rn(1.0f, expf_cr(-v)));
+        } else if (which == 1) {
+            if (i < body) r = sigmoid_ref(v);
+            else r = v < -20.0f ? 0.0f : v > 20.0f ? 1.0f : __fdiv_rn(1.0f, __fadd_rn(1.0f, expf_cr(-v)));
+        } else {
+            r = v > 30.0f ? v : v < -30.0f ? expf_cr(v) : log1pf_cr(expf_cr(v));
+        }
+        x[i] = r;
+    }
+}
+
+__global__ void op_softmax_kernel(float* x, long long n) {
+    __shared__ float shf[32];
+    __shared__ double shd[32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    float mx = -INFINITY;
+    for (long long i = threadIdx.x; i < n; i += blockDim.x) mx = fmaxf(mx, x[i]);
+    mx = warp_max(mx);
+    if (lane == 0) shf[warp] = mx;
+    __syncthreads();
+    mx = shf[0];
+    for (int i = 1; i < nw; ++i) mx = fmaxf(mx, shf[i]);
+    const long long body = n & ~7ll;
+    double s = 0.0;
+    for (long long i = threadIdx.x; i < n; i += blockDim.x) {
+        const float d = __fsub_rn(x[i], mx);
+        const float e = i < body ? exp_poly(d) : expf_cr(d);
+        x[i] = e;
+        s += (double)e;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) shd[warp] = s;
+    __syncthreads();
+    double tot = 0.0;
+    for (int i = 0; i < nw; ++i) tot += shd[i];
+    const float inv = (float)(1.0 / tot);
+    for (long long i = threadIdx.x; i < n; i += blockDim.x) x[i] = __fmul_rn(x[i], inv);
+}
+
+}  // namespace
+
+// ================================ launchers ====================================
+
+cudaError_t qb_embed(int type, const void* tok_embd, int n_embd, const uint32_t* tokens, int B, float* out,
+                     long long ldo, cudaStream_t st) {
+    embed_kernel<<<dim3((n_embd + 255) / 256, B), 256, 0, st>>>(type, (const uint8_t*)tok_embd, n_embd, tokens,
+                                                                out, ldo);
+    return cudaGetLastError();
+}
+
+cudaError_t qb_gdn_conv(const float* qkv, long long ld_qkv, int conv_dim, int B, const float* conv_w,
+                        float* state_slots, size_t slot_stride, const uint32_t* cur_slot, int ckpt,
+                        float* out, long long ld_out, cudaStream_t st) {
+    gdn_conv_kernel<<<(conv_dim + 127) / 128, 128, 0, st>>>(qkv, ld_qkv, conv_dim, B, conv_w, state_slots,
+                                                            slot_stride, cur_slot, ckpt, out, ld_out);
+    return cudaGetLastError();
+}
+
+cudaError_t qb_gdn_recur(const float* qkvc, long long ld_qkvc, const float* beta, const float* alpha,
+                         long long ld_ba, const float* dt_bias, const float* ssm_a, int n_k, int n_v,
+                         int dk, int B, float eps, float* state_slots, size_t slot_stride,
+                         const uint32_t* cur_slot, int ckpt, float* out, long long ld_out, cudaStream_t st) {
+    if (dk != kDK || B > QB_MAX_TOK) return cudaErrorInvalidValue;
+    gdn_recur_kernel<<<dim3(n_v, kDK / 16), 128, 0, st>>>(qkvc, ld_qkvc, beta, alpha, ld_ba, dt_bias, ssm_a,
+                                                          n_k, n_v, B, eps, state_slots, slot_stride, cur_slot,
+                                                          ckpt, out, ld_out);
+    return cudaGetLastError();
+}
+
+cudaError_t qb_gdn_out(const float* o, const float* z, long long ld, const float* norm_w, int n_v, int dv,
+                       int B, float eps, float* y, cudaStream_t st) {
+    gdn_out_kernel<<<dim3(n_v, B), 32, 0, st>>>(o, z, ld, norm_w, dv, eps, y);
+    return cudaGetLastError();
+}
+
+cudaError_t qb_attn_prep(float* q, long long ldq, const float* kv, long long ldkv, const float* q_norm,
+                         const float* k_norm, int n_head, int n_kv, int hd, int rope_half,
+                         const float* rope_cos, const float* rope_sin, const uint32_t* pos, int B, float eps,
+                         float* k_cache, float* v_cache, cudaStream_t st) {
+    if (hd != 256 || rope_half % 32 != 0 || rope_half * 2 > hd) return cudaErrorInvalidValue;
+    const int units = n_head + 2 * n_kv;
+    attn_prep_kernel<<<dim3((units + 3) / 4, B), 128, 0, st>>>(q, ldq, kv, ldkv, q_norm, k_norm, n_head, n_kv,
+                                                               hd, rope_half, rope_cos, rope_sin, pos, eps,
+                                                               k_cache, v_cache);
+    return cudaGetLastError();
+}
+
+cudaError_t qb_attn_decode(const float* q, long long ldq, const float* k_cache, const float* v_cache,
+                           int n_head, int n_kv, int hd, const uint32_t* pos, int B, int n_ctx, float* out,
+                           long long ldo, cudaStream_t st) {
+    if (hd != 256) return cudaErrorInvalidValue;
+    const size_t smem = (size_t)n_ctx * sizeof(float);
+    static int configured_for = 0;
+    if ((int)smem > configured_for && smem > 48 * 1024) {
+        cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        configured_for = (int)smem;
+    }
+    attn_decode_kernel<<<dim3(n_head, B), 256, smem, st>>>(q, ldq, k_cache, v_cache, n_head, n_kv, hd, pos,
+                                                           out, ldo);
+    return cudaGetLastError();
+}
+
+cudaError_t qb_silu_mul(const float* gate, const float* up, long long ld, int n, int B, float* out,
+                        cudaStream_t st) {
+    silu_mul_kernel<<<dim3((n + 255) / 256, B), 256, 0, st>>>(gate, up, ld, n, out);
+    return cudaGetLastError();
+}
+
+cudaError_t qb_argmax_reset(unsigned long long* keys, int B, cudaStream_t st) {
+    argmax_reset_kernel<<<1, 32, 0, st>>>(keys, B);
+    return cudaGetLastError();
+}
+
+cudaError_t qb_argmax(const float* x, long long ldx, int n, int B, unsigned long long* keys, cudaStream_t st) {
+    const int blocks = (n + 1023) / 1024 < 148 ? (n + 1023) / 1024 : 148;
+    argmax_kernel<<<dim3(blocks, B), 256, 0, st>>>(x, ldx, n, keys);
+    return cudaGetLastError();
+}
+
+cudaError_t qb_argmax_to_u32(const unsigned long long* keys, int B, uint32_t* out, cudaStream_t st) {
+    argmax_to_u32_kernel<<<1, 32, 0, st>>>(keys, B, out);
+    return cudaGetLastError();
+}
+
+cudaError_t qb_op_rmsnorm(float* out, const float* x, const float* w, long long n, float eps, cudaStream_t st) {
+    op_rmsnorm_kernel<<<1, 1024, 0, st>>>(out, x, w, n, eps);
+    return cudaGetLastError();
+}
+cudaError_t qb_op_l2norm(float* out, const float* x, long long n, float eps, cudaStream_t st) {
+    op_l2norm_kernel<<<1, 1024, 0, st>>>(out, x, n, eps);
+    return cudaGetLastError();
+}
+cudaError_t qb_op_act(int which, float* x, long long n, cudaStream_t st) {
+    const long long blocks = (n + 255) / 256;
+    op_act_kernel<<<(unsigned)(blocks < 4096 ? (blocks ? blocks : 1) : 4096), 256, 0, st>>>(which, x, n);
+    return cudaGetLastError();
+}
+cudaError_t qb_op_softmax(float* x, long long n, cudaStream_t st) {
+    op_softmax_kernel<<<1, 1024, 0, st>>>(x, n);
+    return cudaGetLastError();
+}

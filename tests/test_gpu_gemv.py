@@ -1,0 +1,117 @@
+"""GPU gemv_batch / gemv_rows_batch (include/qwen_b200.h -> include/kernels.h
+API) against the compiled reference on the same seeded blocks.
+
+Tolerance: the kernels multiply exact weight codes on the tensor cores with
+activations split into fp16 hi+lo (~22 bits), accumulating in fp32, so
+results carry fp32-level error; the bar is relative L2 <= 1e-5 per row set
+(north_star allows 1e-2)."""
+import numpy as np
+import pytest
+
+from conftest import oracle, qb
+
+pytestmark = [pytest.mark.gpu, pytest.mark.skipif(not oracle.available(), reason="oracle/_ref not built")]
+
+FORMATS = [qb.GGML_IQ4_XS, qb.GGML_Q6_K, qb.GGML_Q8_0, qb.GGML_Q4_K, qb.GGML_Q5_K]
+RTOL = 1e-5
+
+
+def rel(a, b):
+    return float(np.linalg.norm(np.float64(a) - np.float64(b)) / max(np.linalg.norm(np.float64(b)), 1e-30))
+
+
+@pytest.mark.parametrize("gtype", FORMATS)
+@pytest.mark.parametrize("n", [1, 2, 3, 4, 5, 8])
+def test_gemv_batch_formats(gtype, n):
+    K, rows = 2048, 333        # rows not a multiple of the 16-row tile
+    raw = qb.synth_matrix(gtype, rows, K, seed=100 + gtype, d_sigma=0.01)
+    x = qb.synth_normal(n * K, seed=n).reshape(n, K)
+    t = qb.tensor(raw, gtype, K, rows)
+    got = qb.gemv_batch(t, x)
+    ref = oracle.ref_gemv_batch(raw, gtype, K, rows, x)
+    for i in range(n):
+        assert rel(got[i], ref[i]) < RTOL, (i, rel(got[i], ref[i]))
+
+
+@pytest.mark.parametrize("gtype", [qb.GGML_IQ4_XS, qb.GGML_Q6_K])
+def test_gemv_rows_subrange(gtype):
+    K, rows = 1024, 200
+    raw = qb.synth_matrix(gtype, rows, K, seed=3, d_sigma=0.01)
+    x = qb.synth_normal(3 * K, seed=9).reshape(3, K)
+    t = qb.tensor(raw, gtype, K, rows)
+    got = qb.gemv_rows_batch(t, x, 37, 151)
+    ref = oracle.ref_gemv_batch(raw, gtype, K, rows, x)
+    assert np.all(got[:, :37] == 0) and np.all(got[:, 151:] == 0)
+    assert rel(got[:, 37:151], ref[:, 37:151]) < RTOL
+
+
+def test_gemv_wide_dynamic_range():
+    """Activations spanning 1e-6 .. 1e4 exercise the per-256-block power-of-two scale."""
+    K, rows = 4096, 64
+    raw = qb.synth_matrix(qb.GGML_IQ4_XS, rows, K, seed=1, d_sigma=0.01)
+    rng = np.random.default_rng(0)
+    x = (rng.standard_normal((4, K)) * 10.0 ** rng.uniform(-6, 4, (4, K))).astype(np.float32)
+    got = qb.gemv_batch(qb.tensor(raw, qb.GGML_IQ4_XS, K, rows), x)
+    ref = oracle.port_gemv(raw, qb.GGML_IQ4_XS, K, x)
+    assert rel(got, ref) < RTOL
+
+
+def test_gemv_f32():
+    K, rows = 300, 17
+    W = qb.synth_normal(rows * K, seed=4)
+    x = qb.synth_normal(2 * K, seed=5).reshape(2, K)
+    raw = W.view(np.uint8)
+    got = qb.gemv_batch(qb.tensor(raw, qb.GGML_F32, K, rows), x)
+    ref = oracle.ref_gemv_batch(raw, qb.GGML_F32, K, rows, x)
+    assert rel(got, ref) < 1e-6
+
+
+def test_gemv_batch_equals_single_token():
+    """Same invariant as the reference's test_batch.c:44-57, on the GPU path:
+    every row of a batch equals the single-token result bit for bit."""
+    K, rows = 2048, 96
+    raw = qb.synth_matrix(qb.GGML_IQ4_XS, rows, K, seed=21, d_sigma=0.01)
+    t = qb.tensor(raw, qb.GGML_IQ4_XS, K, rows)
+    x = qb.synth_normal(4 * K, seed=22).reshape(4, K)
+    batch = qb.gemv_batch(t, x)
+    for i in range(4):
+        single = qb.gemv_batch(t, x[i:i + 1])
+        np.testing.assert_array_equal(batch[i], single[0])
+
+
+@pytest.mark.parametrize("n", [1, 2, 4])
+def test_micro_config_c1(n):
+    """W 17408x5120 IQ4_XS, d = |N|*0.02, x ~ N(0,1)."""
+    K, rows = 5120, 17408
+    raw = qb.synth_matrix(qb.GGML_IQ4_XS, rows, K, seed=0, d_sigma=0.02)
+    x = qb.synth_normal(n * K, seed=100 + n).reshape(n, K)
+    got = qb.gemv_batch(qb.tensor(raw, qb.GGML_IQ4_XS, K, rows), x)
+    ref = oracle.ref_gemv_batch(raw, qb.GGML_IQ4_XS, K, rows, x)
+    for i in range(n):
+        assert rel(got[i], ref[i]) < RTOL
+
+
+def test_sample_greedy_first_max_wins():
+    x = np.zeros(248320, np.float32)
+    x[[7, 100, 200000]] = 3.0
+    assert qb.sample_greedy(x) == 7
+    x[5] = -1.0
+    x[248319] = 3.5
+    assert qb.sample_greedy(x) == 248319
+    rng = np.random.default_rng(1)
+    y = rng.standard_normal(248320).astype(np.float32)
+    assert qb.sample_greedy(y) == oracle.port_argmax(y)
+
+
+@pytest.mark.parametrize("name", ["silu", "sigmoid", "softplus", "softmax", "rmsnorm", "l2norm"])
+@pytest.mark.parametrize("n", [8, 13, 5120])
+def test_ops_against_reference(name, n):
+    rng = np.random.default_rng(n)
+    x = (rng.standard_normal(n) * 4).astype(np.float32)
+    w = (1 + 0.02 * rng.standard_normal(n)).astype(np.float32)
+    got = qb.op(name, x, w if name == "rmsnorm" else None)
+    ref = oracle.ref_op(name, x, w if name == "rmsnorm" else None)
+    if name in ("silu", "sigmoid") and n % 8 == 0:
+        np.testing.assert_array_equal(got, ref)   # polynomial exp restated exactly
+    else:
+        np.testing.assert_allclose(got, ref, rtol=2e-6, atol=1e-7)
