@@ -192,6 +192,13 @@ float qb_last_loop_ms(qwen_model_t *m);
  * state comparisons against the reference.  Returns the float count. */
 int64_t qb_read_state(qwen_model_t *m, uint32_t il, int which, float *dst, int64_t max_floats);
 
+/* Copy internal activation buffer `id` ([PREFILL_MAX_B][width] rows of the
+ * last forward: 0 residual, 1 raw mixer projection, 2 conv output, 3 z,
+ * 4 beta, 5 alpha, 6 GDN output, 7 gated-norm output, 8 q, 9 k|v, 10
+ * attention output, 11 ffn gate, 12 ffn up, 13 SwiGLU, 14 MTP embedding, 15
+ * MTP residual, 16 h_save) to host.  Returns the float count, -1 on error. */
+int64_t qb_read_buffer(qwen_model_t *m, int id, float *dst, int64_t max_floats);
+
 #ifdef __cplusplus
 }
 #endif

@@ -339,14 +339,16 @@ int upload_mat(Engine& e, const GTensor* t, DevMat& m, void* tmp, size_t tmp_byt
     if (t->type == QB_F32) {
         m.w = e.dalloc(src_bytes);
         if (!m.w) { set_err(-2, "cudaMalloc %zu", src_bytes); return -1; }
-        CK(cudaMemcpy(m.w, t->data, src_bytes, cudaMemcpyHostToDevice));
+        CK(cudaMemcpyAsync(m.w, t->data, src_bytes, cudaMemcpyHostToDevice, e.st));
+        CK(cudaStreamSynchronize(e.st));
         return 0;
     }
     const size_t rb = qb_repacked_bytes(t->type, m.rows, m.K);
     if (!rb || src_bytes > tmp_bytes) { set_err(-1, "tensor %s: cannot repack", t->name.c_str()); return -1; }
     m.w = e.dalloc(rb);
     if (!m.w) { set_err(-2, "cudaMalloc %zu", rb); return -1; }
-    CK(cudaMemcpy(tmp, t->data, src_bytes, cudaMemcpyHostToDevice));
+    // stream-ordered: the repack must not start before the host->device copy lands
+    CK(cudaMemcpyAsync(tmp, t->data, src_bytes, cudaMemcpyHostToDevice, e.st));
     CK(qb_repack(t->type, tmp, m.rows, m.K, m.w, e.st));
     CK(cudaStreamSynchronize(e.st));
     if (t->type == QB_Q4_K || t->type == QB_Q5_K) e.any_q45 = true;
@@ -358,7 +360,8 @@ const float* upload_f32(Engine& e, const GTensor* t) {
     const size_t n = t->ne[0] * t->ne[1];
     void* p = e.dalloc(n * 4);
     if (!p) return nullptr;
-    if (cudaMemcpy(p, t->data, n * 4, cudaMemcpyHostToDevice) != cudaSuccess) return nullptr;
+    if (cudaMemcpyAsync(p, t->data, n * 4, cudaMemcpyHostToDevice, e.st) != cudaSuccess) return nullptr;
+    if (cudaStreamSynchronize(e.st) != cudaSuccess) return nullptr;
     return (const float*)p;
 }
 
@@ -420,7 +423,8 @@ int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
         const size_t b = gguf_row_bytes(te->type, te->ne[0]) * te->ne[1];
         e.tok_embd = e.dalloc(b);
         if (!e.tok_embd) { set_err(-2, "cudaMalloc token_embd"); return -1; }
-        CK(cudaMemcpy(e.tok_embd, te->data, b, cudaMemcpyHostToDevice));
+        CK(cudaMemcpyAsync(e.tok_embd, te->data, b, cudaMemcpyHostToDevice, e.st));
+        CK(cudaStreamSynchronize(e.st));
     }
     const GTensor* to = e.g.find("output.weight");
     if (!to) to = te;
@@ -524,8 +528,9 @@ int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
         e.rope_cos = (float*)e.dalloc(cs.size() * 4);
         e.rope_sin = (float*)e.dalloc(sn.size() * 4);
         if (!e.rope_cos || !e.rope_sin) { set_err(-2, "rope alloc"); return -1; }
-        CK(cudaMemcpy(e.rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
-        CK(cudaMemcpy(e.rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+        CK(cudaMemcpyAsync(e.rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice, e.st));
+        CK(cudaMemcpyAsync(e.rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice, e.st));
+        CK(cudaStreamSynchronize(e.st));
     }
 
     // ---- activations ----
@@ -985,7 +990,8 @@ extern "C" uint32_t qb_last_argmax(qwen_model_t* m, uint32_t b) {
     if (!e || b >= QB_MAX_TOK) return 0;
     uint32_t v = 0;
     cudaSetDevice(e->dev);
-    cudaMemcpy(&v, &e->ctrl->argmax[b], 4, cudaMemcpyDeviceToHost);
+    cudaMemcpyAsync(&v, &e->ctrl->argmax[b], 4, cudaMemcpyDeviceToHost, e->st);
+    cudaStreamSynchronize(e->st);
     return v;
 }
 
@@ -1040,7 +1046,8 @@ extern "C" int qb_spec_generate(qwen_model_t* m, uint32_t n_predict, uint32_t n_
     }
     // loop state: P = pos - 1, counters reset, host mirror mtp_h is authoritative
     QbCtrl hc;
-    CK(cudaMemcpy(&hc, e->ctrl, sizeof hc, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpyAsync(&hc, e->ctrl, sizeof hc, cudaMemcpyDeviceToHost, e->st));
+    CK(cudaStreamSynchronize(e->st));
     hc.P = m->pos - 1;
     hc.k = (uint32_t)k;
     hc.cycle = 0;
@@ -1048,9 +1055,9 @@ extern "C" int qb_spec_generate(qwen_model_t* m, uint32_t n_predict, uint32_t n_
     hc.n_forced = n_forced;
     hc.cap_out = e->cap_out;
     hc.cap_j = max_cycles < e->cap_j ? max_cycles : e->cap_j;
-    CK(cudaMemcpy(e->ctrl, &hc, sizeof hc, cudaMemcpyHostToDevice));
-    if (n_forced) CK(cudaMemcpy(e->d_forced, forced, n_forced * 4, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(e->mtp_h, m->mtp_h, (size_t)e->E * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpyAsync(e->ctrl, &hc, sizeof hc, cudaMemcpyHostToDevice, e->st));
+    if (n_forced) CK(cudaMemcpyAsync(e->d_forced, forced, n_forced * 4, cudaMemcpyHostToDevice, e->st));
+    CK(cudaMemcpyAsync(e->mtp_h, m->mtp_h, (size_t)e->E * 4, cudaMemcpyHostToDevice, e->st));
 
     uint32_t n_out = 0, cycles = 0;
     CK(cudaEventRecord(e->ev0, e->st));
@@ -1069,21 +1076,25 @@ extern "C" int qb_spec_generate(qwen_model_t* m, uint32_t n_predict, uint32_t n_
         CK(cudaStreamSynchronize(e->st));
         n_out = dev_counts[1];
         uint32_t P;
-        CK(cudaMemcpy(&P, &e->ctrl->P, 4, cudaMemcpyDeviceToHost));
+        CK(cudaMemcpyAsync(&P, &e->ctrl->P, 4, cudaMemcpyDeviceToHost, e->st));
+        CK(cudaStreamSynchronize(e->st));
         if (P + (uint32_t)k + 3 > (uint32_t)e->n_ctx) break;   // next cycle would pass n_ctx
     }
     CK(cudaEventRecord(e->ev1, e->st));
     CK(cudaEventSynchronize(e->ev1));
     cudaEventElapsedTime(&e->last_ms, e->ev0, e->ev1);
     const uint32_t n_copy = std::min(n_out, n_predict);
-    CK(cudaMemcpy(out_tokens, e->d_out_tok, (size_t)n_copy * 4, cudaMemcpyDeviceToHost));
-    if (out_j) CK(cudaMemcpy(out_j, e->d_out_j, (size_t)std::min(cycles, max_cycles) * 4, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpyAsync(out_tokens, e->d_out_tok, (size_t)n_copy * 4, cudaMemcpyDeviceToHost, e->st));
+    if (out_j)
+        CK(cudaMemcpyAsync(out_j, e->d_out_j, (size_t)std::min(cycles, max_cycles) * 4, cudaMemcpyDeviceToHost, e->st));
     if (n_cycles) *n_cycles = cycles;
     // host mirrors: position, next logits (logits_b[j]), MTP hidden
-    CK(cudaMemcpy(&hc, e->ctrl, sizeof hc, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpyAsync(&hc, e->ctrl, sizeof hc, cudaMemcpyDeviceToHost, e->st));
+    CK(cudaStreamSynchronize(e->st));
     m->pos = hc.P + 1;
-    CK(cudaMemcpy(m->logits, e->logits + (size_t)hc.j * e->V, (size_t)e->V * 4, cudaMemcpyDeviceToHost));
-    CK(cudaMemcpy(m->mtp_h, e->mtp_h, (size_t)e->E * 4, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpyAsync(m->logits, e->logits + (size_t)hc.j * e->V, (size_t)e->V * 4, cudaMemcpyDeviceToHost, e->st));
+    CK(cudaMemcpyAsync(m->mtp_h, e->mtp_h, (size_t)e->E * 4, cudaMemcpyDeviceToHost, e->st));
+    CK(cudaStreamSynchronize(e->st));
     return (int)n_copy;
 }
 
@@ -1096,13 +1107,14 @@ extern "C" int qb_greedy_generate(qwen_model_t* m, uint32_t n_predict, uint32_t*
     if (!e->g_greedy && capture(*e, &e->g_greedy, record_greedy, 0)) return -1;
     // token 0 = argmax(m->logits): the device argmax of the last forward
     QbCtrl hc;
-    CK(cudaMemcpy(&hc, e->ctrl, sizeof hc, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpyAsync(&hc, e->ctrl, sizeof hc, cudaMemcpyDeviceToHost, e->st));
+    CK(cudaStreamSynchronize(e->st));
     hc.fwd_tok[0] = hc.next_cand0;
     hc.fwd_pos = m->pos;
     hc.greedy_n = 1;
     hc.cap_out = e->cap_out;
-    CK(cudaMemcpy(e->ctrl, &hc, sizeof hc, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(e->d_out_tok, &hc.next_cand0, 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpyAsync(e->ctrl, &hc, sizeof hc, cudaMemcpyHostToDevice, e->st));
+    CK(cudaMemcpyAsync(e->d_out_tok, &hc.next_cand0, 4, cudaMemcpyHostToDevice, e->st));
     uint32_t steps = n_predict - 1;
     if (m->pos + steps > (uint32_t)e->n_ctx) steps = (uint32_t)e->n_ctx - m->pos;
     CK(cudaEventRecord(e->ev0, e->st));
@@ -1111,11 +1123,12 @@ extern "C" int qb_greedy_generate(qwen_model_t* m, uint32_t n_predict, uint32_t*
     CK(cudaEventSynchronize(e->ev1));
     cudaEventElapsedTime(&e->last_ms, e->ev0, e->ev1);
     const uint32_t n = steps + 1;
-    CK(cudaMemcpy(out_tokens, e->d_out_tok, (size_t)n * 4, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpyAsync(out_tokens, e->d_out_tok, (size_t)n * 4, cudaMemcpyDeviceToHost, e->st));
     m->pos += steps;
-    CK(cudaMemcpy(m->logits, e->logits, (size_t)e->V * 4, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpyAsync(m->logits, e->logits, (size_t)e->V * 4, cudaMemcpyDeviceToHost, e->st));
     // keep next_cand0 = argmax of the last forward for a following call
-    CK(cudaMemcpy(&e->ctrl->next_cand0, &e->ctrl->argmax[0], 4, cudaMemcpyDeviceToDevice));
+    CK(cudaMemcpyAsync(&e->ctrl->next_cand0, &e->ctrl->argmax[0], 4, cudaMemcpyDeviceToDevice, e->st));
+    CK(cudaStreamSynchronize(e->st));
     return (int)n;
 }
 
@@ -1126,7 +1139,8 @@ extern "C" int64_t qb_read_state(qwen_model_t* m, uint32_t il, int which, float*
     const float* src = nullptr;
     size_t n = 0;
     uint32_t cur = 0;
-    cudaMemcpy(&cur, &e->ctrl->cur_slot, 4, cudaMemcpyDeviceToHost);
+    cudaMemcpyAsync(&cur, &e->ctrl->cur_slot, 4, cudaMemcpyDeviceToHost, e->st);
+    cudaStreamSynchronize(e->st);
     if (il == e->d.n_layer) {
         if (which == 2) { src = e->mtp_k; n = e->kv_layer; }
         if (which == 3) { src = e->mtp_v; n = e->kv_layer; }
@@ -1139,7 +1153,43 @@ extern "C" int64_t qb_read_state(qwen_model_t* m, uint32_t il, int which, float*
     }
     if (!src) return -1;
     if ((int64_t)n > max_floats) n = (size_t)max_floats;
-    if (cudaMemcpy(dst, src, n * 4, cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    if (cudaMemcpyAsync(dst, src, n * 4, cudaMemcpyDeviceToHost, e->st) != cudaSuccess) return -1;
+    if (cudaStreamSynchronize(e->st) != cudaSuccess) return -1;
+    return (int64_t)n;
+}
+
+// Copy an internal activation buffer to host (debugging / layer-level parity).
+extern "C" int64_t qb_read_buffer(qwen_model_t* m, int id, float* dst, int64_t max_floats) {
+    Engine* e = E_(m);
+    if (!e) return -1;
+    cudaSetDevice(e->dev);
+    const qwen_dims_t& d = e->d;
+    const float* src = nullptr;
+    size_t n = 0;
+    const size_t T8 = QB_MAX_TOK;
+    switch (id) {
+    case 0: src = e->bx; n = T8 * e->E; break;
+    case 1: src = e->qkv; n = T8 * e->ld_qkv; break;
+    case 2: src = e->qkvc; n = T8 * e->ld_qkv; break;
+    case 3: src = e->z; n = T8 * d.d_inner; break;
+    case 4: src = e->beta; n = T8 * 256; break;
+    case 5: src = e->alpha; n = T8 * 256; break;
+    case 6: src = e->o; n = T8 * d.d_inner; break;
+    case 7: src = e->y; n = T8 * d.d_inner; break;
+    case 8: src = e->qbuf; n = T8 * 2 * d.n_head * d.head_dim; break;
+    case 9: src = e->kvbuf; n = T8 * 2 * d.n_kv_head * d.head_dim; break;
+    case 10: src = e->attn_o; n = T8 * d.n_head * d.head_dim; break;
+    case 11: src = e->gate; n = T8 * e->F; break;
+    case 12: src = e->up; n = T8 * e->F; break;
+    case 13: src = e->act; n = T8 * e->F; break;
+    case 14: src = e->emb; n = T8 * e->E; break;
+    case 15: src = e->mtp_x; n = T8 * e->E; break;
+    case 16: src = e->h_save; n = T8 * e->E; break;
+    default: return -1;
+    }
+    if ((int64_t)n > max_floats) n = (size_t)max_floats;
+    if (cudaMemcpyAsync(dst, src, n * 4, cudaMemcpyDeviceToHost, e->st) != cudaSuccess) return -1;
+    if (cudaStreamSynchronize(e->st) != cudaSuccess) return -1;
     return (int64_t)n;
 }
 
@@ -1169,6 +1219,7 @@ struct Scratch {
     size_t k_cap = 0;
     unsigned long long* keys = nullptr;
     uint32_t* am = nullptr;
+    bool consts = false;
 };
 std::mutex g_mu;
 std::unordered_map<WKey, DevMat, WKeyHash> g_wcache;
@@ -1179,6 +1230,10 @@ int scratch_get(Scratch*& s, size_t x_floats, size_t out_floats, int K) {
     CK(cudaGetDevice(&dev));
     s = &g_scratch[dev];
     if (!s->st) CK(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
+    if (!s->consts) {
+        CK(qb_quant_init_constants());   // IQ4 table in this device's constant bank
+        s->consts = true;
+    }
     if (x_floats > s->x_cap) {
         if (s->x) cudaFree(s->x);
         s->x_cap = std::max<size_t>(x_floats, 1 << 16);
@@ -1222,6 +1277,7 @@ int wcache_get(const gguf_tensor_info_t* W, const DevMat*& out) {
     if (m.type == QB_F32) {
         CK(cudaMalloc(&m.w, src_bytes));
         CK(cudaMemcpy(m.w, W->data, src_bytes, cudaMemcpyHostToDevice));
+        CK(cudaDeviceSynchronize());   // the DMA from pageable memory may still be in flight
     } else {
         void* tmp = nullptr;
         CK(cudaMalloc(&tmp, src_bytes));

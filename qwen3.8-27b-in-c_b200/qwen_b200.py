@@ -28,7 +28,7 @@ EXPORTED = [
     "gemv_rows", "gemv", "gemv_rows_batch", "gemv_batch", "gemv_multi", "gemv_multi_batch",
     "rmsnorm", "l2norm", "silu_inplace", "sigmoid_inplace", "softplus_inplace", "softmax_inplace",
     "qb_last_error", "qb_last_error_str", "qb_clear_error", "qb_prefill", "qb_spec_generate",
-    "qb_greedy_generate", "qb_last_argmax", "qb_last_loop_ms", "qb_read_state",
+    "qb_greedy_generate", "qb_last_argmax", "qb_last_loop_ms", "qb_read_state", "qb_read_buffer",
 ]
 
 
@@ -117,6 +117,8 @@ def lib():
         L.qb_last_loop_ms.restype = f32
         L.qb_read_state.argtypes = [P(QwenModel), u32, i32, P(f32), C.c_int64]
         L.qb_read_state.restype = C.c_int64
+        L.qb_read_buffer.argtypes = [P(QwenModel), i32, P(f32), C.c_int64]
+        L.qb_read_buffer.restype = C.c_int64
         _lib = L
     return _lib
 
@@ -292,6 +294,13 @@ class Model:
 
     def last_loop_ms(self):
         return lib().qb_last_loop_ms(C.byref(self.m))
+
+    def read_buffer(self, bid, n):
+        buf = np.zeros(n, np.float32)
+        got = lib().qb_read_buffer(C.byref(self.m), bid, _fp(buf), n)
+        if got < 0:
+            raise RuntimeError("qb_read_buffer failed")
+        return buf[:got]
 
     def read_state(self, il, which, n):
         buf = np.zeros(n, np.float32)
