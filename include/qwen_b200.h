@@ -192,6 +192,17 @@ float qb_last_loop_ms(qwen_model_t *m);
  * state comparisons against the reference.  Returns the float count. */
 int64_t qb_read_state(qwen_model_t *m, uint32_t il, int which, float *dst, int64_t max_floats);
 
+/* Start a new sequence on the same weights: recurrent states and mtp_h to
+ * zero, rollback slot 0, pos = 0.  Returns 0 or -1. */
+int qb_reset(qwen_model_t *m);
+
+/* Device time (ms, CUDA events on the model's stream, mean of `iters`) of one
+ * component: what = 0 verify forward of `arg` tokens with checkpoints, 1 the
+ * fused FFN gate+up GEMV at N = arg rotated over all layers, 2 one MTP draft
+ * with logits, 3 the output-head GEMV at N = arg.  *bytes receives the
+ * algorithmic bytes of one run.  Overwrites KV / recurrent state.  -1 on error. */
+float qb_bench(qwen_model_t *m, int what, uint32_t arg, uint32_t iters, double *bytes);
+
 /* Copy internal activation buffer `id` ([PREFILL_MAX_B][width] rows of the
  * last forward: 0 residual, 1 raw mixer projection, 2 conv output, 3 z,
  * 4 beta, 5 alpha, 6 GDN output, 7 gated-norm output, 8 q, 9 k|v, 10

@@ -1158,6 +1158,101 @@ extern "C" int64_t qb_read_state(qwen_model_t* m, uint32_t il, int which, float*
     return (int64_t)n;
 }
 
+// New sequence: recurrent states and MTP hidden to zero, live slot 0, pos 0.
+// KV entries need no clearing: positions >= pos are never read.
+extern "C" int qb_reset(qwen_model_t* m) {
+    Engine* e = E_(m);
+    if (!e) return -1;
+    CK(cudaSetDevice(e->dev));
+    CK(cudaMemsetAsync(e->conv_slots, 0, std::max<size_t>(1, e->conv_slot_stride * kNSlot) * 4, e->st));
+    CK(cudaMemsetAsync(e->ssm_slots, 0, std::max<size_t>(1, e->ssm_slot_stride * kNSlot) * 4, e->st));
+    CK(cudaMemsetAsync(e->mtp_h, 0, (size_t)e->E * 4, e->st));
+    set_u32_kernel<<<1, 1, 0, e->st>>>(&e->ctrl->cur_slot, 0u);
+    CK(cudaGetLastError());
+    CK(cudaStreamSynchronize(e->st));
+    memset(m->mtp_h, 0, (size_t)e->E * 4);
+    m->pos = 0;
+    return 0;
+}
+
+namespace {
+size_t mat_bytes(const DevMat& w) { return gguf_row_bytes(w.type, (uint64_t)w.K) * (size_t)w.rows; }
+
+int record_verify(Engine& e, int B) { return fwd_backbone(e, B, 1); }
+int record_draft(Engine& e, int) { return fwd_mtp(e, 1, e.mtp_h, 1); }
+}  // namespace
+
+// Device timing of one component, averaged over `iters` runs, CUDA events on
+// the engine stream.  what: 0 verify forward of `arg` tokens (64 layers +
+// head, graph replay), 1 fused FFN gate+up GEMV with N = arg rotating over
+// all layers, 2 one MTP draft with logits, 3 output-head GEMV with N = arg.
+// *bytes = algorithmic bytes of one run (GGUF weight bytes + activations and
+// states read/written once).  Mutates KV / recurrent state: call last.
+extern "C" float qb_bench(qwen_model_t* m, int what, uint32_t arg, uint32_t iters, double* bytes) {
+    Engine* e = E_(m);
+    if (!e || iters == 0) return -1.f;
+    if (cudaSetDevice(e->dev) != cudaSuccess) return -1.f;
+    const qwen_dims_t& d = e->d;
+    double b = 0;
+    float ms = 0.f;
+    cudaGraphExec_t ge = nullptr;
+    if (what == 0 || what == 2) {
+        if (what == 0 && (arg < 1 || arg > SPEC_MAX_B)) return -1.f;
+        if (capture(*e, &ge, what == 0 ? record_verify : record_draft, (int)arg)) return -1.f;
+        cudaGraphLaunch(ge, e->st);   // warm
+        cudaEventRecord(e->ev0, e->st);
+        for (uint32_t i = 0; i < iters; ++i) cudaGraphLaunch(ge, e->st);
+        cudaEventRecord(e->ev1, e->st);
+        cudaEventSynchronize(e->ev1);
+        cudaEventElapsedTime(&ms, e->ev0, e->ev1);
+        cudaGraphExecDestroy(ge);
+        if (what == 0) {
+            for (const LayerW& l : e->L) {
+                b += mat_bytes(l.ffn_gate) + mat_bytes(l.ffn_up) + mat_bytes(l.ffn_down);
+                if (l.rec) b += mat_bytes(l.wqkv) + mat_bytes(l.wgate) + mat_bytes(l.wbeta) + mat_bytes(l.walpha) + mat_bytes(l.ssm_out);
+                else b += mat_bytes(l.q) + mat_bytes(l.k) + mat_bytes(l.v) + mat_bytes(l.o);
+            }
+            b += mat_bytes(e->output);
+            b += 2.0 * e->ssm_slot_stride * 4 + 2.0 * e->conv_slot_stride * 4;   // states read + written once
+            uint32_t pos = 0;
+            cudaMemcpyAsync(&pos, &e->ctrl->fwd_pos, 4, cudaMemcpyDeviceToHost, e->st);
+            cudaStreamSynchronize(e->st);
+            b += (double)d.n_attn_layer * (pos + arg) * 2.0 * d.n_kv_head * d.head_dim * 4;   // KV read once
+        } else {
+            const LayerW& l = e->mtp;
+            b = mat_bytes(e->eh_proj) + mat_bytes(l.q) + mat_bytes(l.k) + mat_bytes(l.v) + mat_bytes(l.o) +
+                mat_bytes(l.ffn_gate) + mat_bytes(l.ffn_up) + mat_bytes(l.ffn_down) + mat_bytes(e->output);
+        }
+    } else if (what == 1 || what == 3) {
+        if (arg < 1 || arg > QB_MAX_TOK) return -1.f;
+        const int nl = what == 1 ? (int)e->L.size() : 1;
+        cudaEventRecord(e->ev0, e->st);
+        for (uint32_t i = 0; i < iters; ++i)
+            for (int li = 0; li < nl; ++li) {
+                if (what == 1) {
+                    const LayerW& l = e->L[li];
+                    QbQSeg segs[2] = {{l.ffn_gate.w, e->gate, e->F, l.ffn_gate.rows}, {l.ffn_up.w, e->up, e->F, l.ffn_up.rows}};
+                    qb_qmv(l.ffn_gate.type, segs, 2, e->E, (int)arg, e->xfrag, e->xscale, e->xsum, 0, 0, 1 << 30, e->st);
+                } else {
+                    QbQSeg seg = {e->output.w, e->logits, e->V, e->output.rows};
+                    qb_qmv(e->output.type, &seg, 1, e->E, (int)arg, e->xfrag, e->xscale, e->xsum, 0, 0, 1 << 30, e->st);
+                }
+            }
+        cudaEventRecord(e->ev1, e->st);
+        cudaEventSynchronize(e->ev1);
+        cudaEventElapsedTime(&ms, e->ev0, e->ev1);
+        iters *= (uint32_t)nl;
+        const LayerW& l0 = e->L[0];
+        b = what == 1 ? (double)(mat_bytes(l0.ffn_gate) + mat_bytes(l0.ffn_up)) : (double)mat_bytes(e->output);
+        b += (double)arg * e->E * 4 + (double)arg * (what == 1 ? 2.0 * e->F : e->V) * 4;
+    } else {
+        return -1.f;
+    }
+    if (cudaGetLastError() != cudaSuccess) return -1.f;
+    if (bytes) *bytes = b;
+    return ms / (float)iters;
+}
+
 // Copy an internal activation buffer to host (debugging / layer-level parity).
 extern "C" int64_t qb_read_buffer(qwen_model_t* m, int id, float* dst, int64_t max_floats) {
     Engine* e = E_(m);

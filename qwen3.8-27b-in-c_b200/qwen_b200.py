@@ -29,6 +29,7 @@ EXPORTED = [
     "rmsnorm", "l2norm", "silu_inplace", "sigmoid_inplace", "softplus_inplace", "softmax_inplace",
     "qb_last_error", "qb_last_error_str", "qb_clear_error", "qb_prefill", "qb_spec_generate",
     "qb_greedy_generate", "qb_last_argmax", "qb_last_loop_ms", "qb_read_state", "qb_read_buffer",
+    "qb_reset", "qb_bench",
 ]
 
 
@@ -119,6 +120,10 @@ def lib():
         L.qb_read_state.restype = C.c_int64
         L.qb_read_buffer.argtypes = [P(QwenModel), i32, P(f32), C.c_int64]
         L.qb_read_buffer.restype = C.c_int64
+        L.qb_reset.argtypes = [P(QwenModel)]
+        L.qb_reset.restype = i32
+        L.qb_bench.argtypes = [P(QwenModel), i32, u32, u32, P(C.c_double)]
+        L.qb_bench.restype = f32
         _lib = L
     return _lib
 
@@ -291,6 +296,20 @@ class Model:
             check()
             raise RuntimeError("qb_greedy_generate failed")
         return out[:n].copy()
+
+    def reset(self):
+        if lib().qb_reset(C.byref(self.m)) != 0:
+            check()
+            raise RuntimeError("qb_reset failed")
+
+    def bench(self, what, arg, iters):
+        """(ms per run, algorithmic bytes per run) from qb_bench."""
+        b = C.c_double()
+        ms = lib().qb_bench(C.byref(self.m), what, arg, iters, C.byref(b))
+        if ms < 0:
+            check()
+            raise RuntimeError("qb_bench failed")
+        return float(ms), float(b.value)
 
     def last_loop_ms(self):
         return lib().qb_last_loop_ms(C.byref(self.m))
