@@ -47,6 +47,14 @@ PROMPT_LEN = 128
 SEED = 0
 
 
+def log(msg):
+    try:
+        rss = int(open("/proc/self/statm").read().split()[1]) * os.sysconf("SC_PAGE_SIZE") / 1e9
+    except Exception:
+        rss = -1
+    print(f"[bench {time.strftime('%H:%M:%S')}] {msg} (rss {rss:.1f} GB)", file=sys.stderr, flush=True)
+
+
 def peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -132,7 +140,9 @@ def cpu_reference_run(path, n_threads, warmup, steps, time_budget=None):
         return None, "oracle/_ref not built"
     n_ctx = PROMPT_LEN + 4 * (warmup + steps) + 64
     m = orc.RefModel(path, n_ctx, n_threads)
+    log("reference model_init")
     m.prefill(prompt_tokens(0), 1)
+    log("reference prefill")
     forced = forced_schedule()
     if warmup:
         m.spec_generate(10 ** 6, 3, forced=forced, max_cycles=warmup)
@@ -185,7 +195,9 @@ def run_ours(args, rank, world, local_rank):
 
     # ---- device-timed value: K speculative cycles ----
     model.prefill(prompt_tokens(rank), 1)
+    log("prefill done")
     model.spec_generate(10 ** 6, 3, forced=forced, max_cycles=args.warmup)
+    log("warmup done")
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
@@ -196,6 +208,7 @@ def run_ours(args, rank, world, local_rank):
     if dist:
         dist.barrier()
     n_tok = len(toks)
+    log(f"timed: {args.steps} cycles {n_tok} tokens {ms:.1f} ms")
     t = torch.tensor([ms, float(n_tok)], dtype=torch.float64, device="cuda")
     if dist:
         mx = t.clone()
@@ -222,13 +235,16 @@ def run_ours(args, rank, world, local_rank):
         h2d = prompt.nbytes + forced.nbytes + 4 * model.E + 64
         d2h = out.nbytes + jj.nbytes + 4 * (model.V + model.E) * 2
     e2e = max(e2e_runs[1:]) if len(e2e_runs) > 1 else e2e_runs[0]
+    log(f"e2e {e2e_runs}")
 
     # ---- components (device events on the model's stream) ----
     hbm, peak_kind = peaks()
+    kernels_per_cycle, _ = model.bench(4, 0, 1)
     ms_gemv, b_gemv = model.bench(1, 4, 3)        # FFN gate+up, N=4, over all 64 layers
     ms_head, b_head = model.bench(3, 4, 20)
     ms_draft, b_draft = model.bench(2, 1, 10)
     ms_ver, b_ver = model.bench(0, 4, 10)        # verify step (64 layers + head, B=4)
+    log(f"components gemv {ms_gemv:.4f} head {ms_head:.4f} draft {ms_draft:.3f} verify {ms_ver:.3f} ms")
     gemv_gbs = b_gemv / (ms_gemv / 1e3) / 1e9
     ver_gbs = b_ver / (ms_ver / 1e3) / 1e9
 
@@ -236,7 +252,8 @@ def run_ours(args, rank, world, local_rank):
     if rank == 0:
         cpu_v, cpu_sample = (None, None)
         if world == 1 and not args.no_cpu:
-            cpu_v, cpu_sample = cpu_reference_run(path, os.cpu_count(), 1, 10 ** 6, time_budget=args.cpu_seconds)
+            log("cpu reference sample")
+            cpu_v, cpu_sample = cpu_reference_run(path, os.cpu_count(), 1, 400, time_budget=args.cpu_seconds)
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
@@ -247,7 +264,7 @@ def run_ours(args, rank, world, local_rank):
                        "mean_accept": float(np.mean(js)) if len(js) else None,
                        "l2": "weights 15 GB per cycle >> 126 MB L2 (no flush needed)",
                        "parallelism": f"replicas x{world}"},
-            "gpu_launches": None,
+            "gpu_launches": int(kernels_per_cycle) * args.steps,
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "step": "one request: reset + prefill 128 + decode 512 tokens"},
             "roofline": {"bound": "hbm", "kernel": "qmv IQ4_XS (FFN gate+up fused, N=4)", "achieved": gemv_gbs,

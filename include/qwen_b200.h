@@ -199,8 +199,10 @@ int qb_reset(qwen_model_t *m);
 /* Device time (ms, CUDA events on the model's stream, mean of `iters`) of one
  * component: what = 0 verify forward of `arg` tokens with checkpoints, 1 the
  * fused FFN gate+up GEMV at N = arg rotated over all layers, 2 one MTP draft
- * with logits, 3 the output-head GEMV at N = arg.  *bytes receives the
- * algorithmic bytes of one run.  Overwrites KV / recurrent state.  -1 on error. */
+ * with logits, 3 the output-head GEMV at N = arg; what = 4 returns instead
+ * the number of kernels one speculative cycle launches (after a
+ * qb_spec_generate call).  *bytes receives the algorithmic bytes of one
+ * run.  Overwrites KV / recurrent state.  -1 on error. */
 float qb_bench(qwen_model_t *m, int what, uint32_t arg, uint32_t iters, double *bytes);
 
 /* Copy internal activation buffer `id` ([PREFILL_MAX_B][width] rows of the

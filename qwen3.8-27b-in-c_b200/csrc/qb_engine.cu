@@ -305,6 +305,7 @@ struct Engine {
     // graphs
     cudaGraphExec_t g_cycle = nullptr;
     int g_cycle_k = -1;
+    size_t cycle_kernels = 0;
     cudaGraphExec_t g_greedy = nullptr;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     float last_ms = 0.f;
@@ -798,6 +799,8 @@ int record_cycle(Engine& e, int k) {
     return 0;
 }
 
+size_t g_last_graph_kernels = 0;
+
 int capture(Engine& e, cudaGraphExec_t* out, int (*rec)(Engine&, int), int arg) {
     cudaGraph_t graph = nullptr;
     CK(cudaStreamBeginCapture(e.st, cudaStreamCaptureModeThreadLocal));
@@ -808,6 +811,16 @@ int capture(Engine& e, cudaGraphExec_t* out, int (*rec)(Engine&, int), int arg) 
         if (!r) CK(ce);
         return -1;
     }
+    size_t n_nodes = 0, n_kern = 0;
+    if (cudaGraphGetNodes(graph, nullptr, &n_nodes) == cudaSuccess && n_nodes) {
+        std::vector<cudaGraphNode_t> nodes(n_nodes);
+        cudaGraphGetNodes(graph, nodes.data(), &n_nodes);
+        for (auto nd : nodes) {
+            cudaGraphNodeType t;
+            if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++n_kern;
+        }
+    }
+    g_last_graph_kernels = n_kern;
     cudaError_t ie = cudaGraphInstantiate(out, graph, 0);
     cudaGraphDestroy(graph);
     CK(ie);
@@ -1043,6 +1056,7 @@ extern "C" int qb_spec_generate(qwen_model_t* m, uint32_t n_predict, uint32_t n_
         if (e->g_cycle) { cudaGraphExecDestroy(e->g_cycle); e->g_cycle = nullptr; }
         if (capture(*e, &e->g_cycle, record_cycle, k)) return -1;
         e->g_cycle_k = k;
+        e->cycle_kernels = g_last_graph_kernels;
     }
     // loop state: P = pos - 1, counters reset, host mirror mtp_h is authoritative
     QbCtrl hc;
@@ -1245,6 +1259,10 @@ extern "C" float qb_bench(qwen_model_t* m, int what, uint32_t arg, uint32_t iter
         const LayerW& l0 = e->L[0];
         b = what == 1 ? (double)(mat_bytes(l0.ffn_gate) + mat_bytes(l0.ffn_up)) : (double)mat_bytes(e->output);
         b += (double)arg * e->E * 4 + (double)arg * (what == 1 ? 2.0 * e->F : e->V) * 4;
+    } else if (what == 4) {
+        // kernels launched per speculative cycle (nodes of the captured cycle graph)
+        if (bytes) *bytes = 0;
+        return (float)e->cycle_kernels;
     } else {
         return -1.f;
     }
