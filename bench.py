@@ -285,6 +285,31 @@ def run_ours(args, rank, world, local_rank):
         print(json.dumps(line))
 
 
+def run_components(args):
+    """Component timings only (used for ncu captures on a small model): shape
+    wide4 = the benchmark widths with 4 layers (~3 GB on the device)."""
+    import torch
+    torch.cuda.set_device(0)
+    shape = {"full": qb.FULL, "wide4": qb.WIDE4}[args.shape]
+    d = "/dev/shm" if os.path.isdir("/dev/shm") else "/tmp"
+    path = os.path.join(d, f"qb_bench_{args.shape}_seed{SEED}.gguf")
+    if not os.path.exists(path):
+        qb.write_synth_gguf(path + ".tmp", shape, seed=SEED)
+        os.replace(path + ".tmp", path)
+    model = qb.Model(path, 1024)
+    model.prefill(prompt_tokens(0), 1)
+    out = {}
+    for name, what, arg, iters in [("ffn_gate_up_n4", 1, 4, args.iters), ("ffn_gate_up_n1", 1, 1, args.iters),
+                                   ("head_n4", 3, 4, args.iters), ("head_n1", 3, 1, args.iters),
+                                   ("draft", 2, 1, args.iters), ("verify_b4", 0, 4, args.iters)]:
+        if args.only and name not in args.only.split(","):
+            continue
+        ms, b = model.bench(what, arg, iters)
+        out[name] = {"ms": ms, "bytes": b, "GB/s": b / ms / 1e6}
+    model.close()
+    print(json.dumps(out))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -293,7 +318,14 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--mode", default="bench", choices=["bench", "components"])
+    ap.add_argument("--shape", default="wide4", choices=["wide4", "full"])
+    ap.add_argument("--iters", type=int, default=3)
+    ap.add_argument("--only", default="")
     args = ap.parse_args()
+    if args.mode == "components":
+        run_components(args)
+        return
     args.warmup = max(args.warmup, 3)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -48,13 +48,13 @@ def _stale(target, deps):
     return any(os.path.getmtime(d) > t for d in deps)
 
 
-def build_engine(verbose=False, force=False, extra_flags=()):
+def build_engine(verbose=False, force=False, extra_flags=(), out=None, objdir=None):
     nvcc = _nvcc()
-    out = os.path.join(PKG, "libqwenb200.so")
+    out = out or os.path.join(PKG, "libqwenb200.so")
     headers = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".h", ".cuh"))]
     headers.append(os.path.join(INCLUDE, "qwen_b200.h"))
     objs = []
-    objdir = os.path.join(PKG, "_build")
+    objdir = objdir or os.path.join(PKG, "_build")
     os.makedirs(objdir, exist_ok=True)
     for src in CU_SOURCES:
         s = os.path.join(CSRC, src)

@@ -295,6 +295,7 @@ struct Engine {
     uint2* xfrag = nullptr;
     float *xscale = nullptr, *xsum = nullptr;
     unsigned long long* keys = nullptr;   // [2][QB_MAX_TOK]: backbone, mtp
+    QbQmvWork work{};
     QbCtrl* ctrl = nullptr;
     uint32_t* d_forced = nullptr;
     uint32_t* d_out_tok = nullptr;
@@ -327,6 +328,7 @@ Engine::~Engine() {
     if (ev0) cudaEventDestroy(ev0);
     if (ev1) cudaEventDestroy(ev1);
     for (void* p : allocs) cudaFree(p);
+    qb_qmv_work_free(work);
     if (st) cudaStreamDestroy(st);
 }
 
@@ -571,6 +573,10 @@ int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
     CK(cudaMemset(e.xsum, 0, (size_t)T8 * (Kmax / 32) * 4));
     CK(cudaMemset(e.ctrl, 0, sizeof(QbCtrl)));
     CK(cudaMemset(e.mtp_h, 0, (size_t)e.E * 4));
+    {   // GEMV scratch: arrival counters for the largest launch (head or fused FFN / mixer)
+        const int max_pairs = (e.V + 31) / 32 + (2 * e.F + e.ld_qkv) / 32 + 64;
+        CK(qb_qmv_work_alloc(e.work, max_pairs));
+    }
     CK(cudaEventCreate(&e.ev0));
     CK(cudaEventCreate(&e.ev1));
     CK(cudaDeviceSynchronize());
@@ -598,7 +604,7 @@ int gemv_group(Engine& e, const DevMat* const* mats, float* const* outs, const l
         if (type == QB_F32) {
             for (int s = 0; s < ns; ++s) CK(cudaErrorNotSupported);
         } else {
-            CK(qb_qmv(type, segs, ns, K, N, e.xfrag, e.xscale, e.xsum, accumulate, 0, 1 << 30, e.st));
+            CK(qb_qmv(type, segs, ns, K, N, e.xfrag, e.xscale, e.xsum, accumulate, 0, 1 << 30, e.work, e.st));
         }
     }
     return 0;
@@ -1239,22 +1245,35 @@ extern "C" float qb_bench(qwen_model_t* m, int what, uint32_t arg, uint32_t iter
         }
     } else if (what == 1 || what == 3) {
         if (arg < 1 || arg > QB_MAX_TOK) return -1.f;
+        // one graph of the launches (all layers for what 1), replayed: no host launch gaps
         const int nl = what == 1 ? (int)e->L.size() : 1;
-        cudaEventRecord(e->ev0, e->st);
-        for (uint32_t i = 0; i < iters; ++i)
-            for (int li = 0; li < nl; ++li) {
-                if (what == 1) {
-                    const LayerW& l = e->L[li];
-                    QbQSeg segs[2] = {{l.ffn_gate.w, e->gate, e->F, l.ffn_gate.rows}, {l.ffn_up.w, e->up, e->F, l.ffn_up.rows}};
-                    qb_qmv(l.ffn_gate.type, segs, 2, e->E, (int)arg, e->xfrag, e->xscale, e->xsum, 0, 0, 1 << 30, e->st);
-                } else {
-                    QbQSeg seg = {e->output.w, e->logits, e->V, e->output.rows};
-                    qb_qmv(e->output.type, &seg, 1, e->E, (int)arg, e->xfrag, e->xscale, e->xsum, 0, 0, 1 << 30, e->st);
+        struct Rec {
+            static int go(Engine& en, int packed) {
+                const int wh = packed & 0xFF, a = (packed >> 8) & 0xFF, nlay = packed >> 16;
+                for (int li = 0; li < nlay; ++li) {
+                    if (wh == 1) {
+                        const LayerW& l = en.L[li];
+                        QbQSeg segs[2] = {{l.ffn_gate.w, en.gate, en.F, l.ffn_gate.rows},
+                                          {l.ffn_up.w, en.up, en.F, l.ffn_up.rows}};
+                        CK(qb_qmv(l.ffn_gate.type, segs, 2, en.E, a, en.xfrag, en.xscale, en.xsum, 0, 0, 1 << 30,
+                                  en.work, en.st));
+                    } else {
+                        QbQSeg seg = {en.output.w, en.logits, en.V, en.output.rows};
+                        CK(qb_qmv(en.output.type, &seg, 1, en.E, a, en.xfrag, en.xscale, en.xsum, 0, 0, 1 << 30,
+                                  en.work, en.st));
+                    }
                 }
+                return 0;
             }
+        };
+        if (capture(*e, &ge, Rec::go, what | ((int)arg << 8) | (nl << 16))) return -1.f;
+        cudaGraphLaunch(ge, e->st);
+        cudaEventRecord(e->ev0, e->st);
+        for (uint32_t i = 0; i < iters; ++i) cudaGraphLaunch(ge, e->st);
         cudaEventRecord(e->ev1, e->st);
         cudaEventSynchronize(e->ev1);
         cudaEventElapsedTime(&ms, e->ev0, e->ev1);
+        cudaGraphExecDestroy(ge);
         iters *= (uint32_t)nl;
         const LayerW& l0 = e->L[0];
         b = what == 1 ? (double)(mat_bytes(l0.ffn_gate) + mat_bytes(l0.ffn_up)) : (double)mat_bytes(e->output);
@@ -1333,6 +1352,7 @@ struct Scratch {
     unsigned long long* keys = nullptr;
     uint32_t* am = nullptr;
     bool consts = false;
+    QbQmvWork work{};
 };
 std::mutex g_mu;
 std::unordered_map<WKey, DevMat, WKeyHash> g_wcache;
@@ -1371,6 +1391,15 @@ int scratch_get(Scratch*& s, size_t x_floats, size_t out_floats, int K) {
     if (!s->keys) {
         CK(cudaMalloc(&s->keys, QB_MAX_TOK * sizeof(unsigned long long)));
         CK(cudaMalloc(&s->am, QB_MAX_TOK * 4));
+    }
+    return 0;
+}
+
+int scratch_work(Scratch* s, int rows) {
+    const int pairs = (rows + 31) / 32 + 1;
+    if (pairs > s->work.max_pairs) {
+        qb_qmv_work_free(s->work);
+        CK(qb_qmv_work_alloc(s->work, std::max(pairs, 8192)));
     }
     return 0;
 }
@@ -1419,10 +1448,11 @@ int gemv_host(const gguf_tensor_info_t* W, const float* x, uint64_t ldx, int n, 
         const int nn = std::min(QB_MAX_TOK, n - t0);
         if (scratch_get(s, (size_t)nn * K, (size_t)nn * M->rows, K)) return -1;
         CK(cudaMemcpy2DAsync(s->x, (size_t)K * 4, x + (size_t)t0 * ldx, ldx * 4, (size_t)K * 4, nn, cudaMemcpyHostToDevice, s->st));
-        const int t_lo = (int)(r0 / QB_TILE);
+        const int t_lo = (int)(r0 / (2 * QB_TILE)) * 2;   // start on a tile pair
         if (M->type == QB_F32) {
             CK(qb_qmv_f32((const float*)M->w, M->rows, K, s->x, K, nn, s->out, M->rows, 0, (int)r0, (int)r1, s->st));
         } else {
+            if (scratch_work(s, M->rows)) return -1;
             QbXIn in{s->x, K, nullptr, K};
             CK(qb_xprep(&in, 1, nn, 1e-6f, s->xfrag, s->xscale, s->xsum, (M->type == QB_Q4_K || M->type == QB_Q5_K) ? 1 : 0, s->st));
             QbQSeg seg;
@@ -1431,7 +1461,7 @@ int gemv_host(const gguf_tensor_info_t* W, const float* x, uint64_t ldx, int n, 
             seg.ldo = M->rows;
             seg.rows = (int)(r1 - (uint64_t)t_lo * QB_TILE);
             CK(qb_qmv(M->type, &seg, 1, K, nn, s->xfrag, s->xscale, s->xsum, 0, (int)(r0 - (uint64_t)t_lo * QB_TILE),
-                      (int)(r1 - (uint64_t)t_lo * QB_TILE), s->st));
+                      (int)(r1 - (uint64_t)t_lo * QB_TILE), s->work, s->st));
         }
         CK(cudaMemcpy2DAsync(out + (size_t)t0 * ldo + r0, ldo * 4, s->out + r0, (size_t)M->rows * 4, (size_t)(r1 - r0) * 4, nn,
                              cudaMemcpyDeviceToHost, s->st));

@@ -17,6 +17,17 @@ struct QbQSeg {              // one matrix of a fused GEMV launch
     int rows;
 };
 
+// Scratch of one GEMV stream: split tile-pair partials, per-pair arrival
+// counters (zero between launches), error flag (non-zero after a bounded
+// wait gave up).
+struct QbQmvWork {
+    float* partial;          // [max_warps][2][32][8]
+    unsigned* counters;      // [max_pairs], zero-initialised
+    unsigned* err;           // [1]
+    int max_warps;
+    int max_pairs;
+};
+
 // ---- quantised GEMV (qb_quant.cu) ----
 cudaError_t qb_quant_init_constants();
 size_t qb_repacked_bytes(int type, int rows, int K);
@@ -25,7 +36,9 @@ cudaError_t qb_xprep(const QbXIn* in, int nseg, int N, float eps, uint2* xfrag, 
                      int want_xsum, cudaStream_t st);
 cudaError_t qb_qmv(int type, const QbQSeg* segs, int nseg, int K, int N, const uint2* xfrag,
                    const float* xscale, const float* xsum, int accumulate, int row_lo, int row_hi,
-                   cudaStream_t st);
+                   const QbQmvWork& work, cudaStream_t st);
+cudaError_t qb_qmv_work_alloc(QbQmvWork& w, int max_pairs);
+void qb_qmv_work_free(QbQmvWork& w);
 cudaError_t qb_qmv_f32(const float* W, int rows, int K, const float* x, long long ldx, int N, float* out,
                        long long ldo, int accumulate, int row_lo, int row_hi, cudaStream_t st);
 

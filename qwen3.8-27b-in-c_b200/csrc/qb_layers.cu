@@ -135,6 +135,8 @@ __host__ __device__ inline size_t row_bytes_of(int type, int n) {
 
 __global__ void embed_kernel(int type, const uint8_t* __restrict__ E, int n, const uint32_t* __restrict__ tok,
                              float* __restrict__ out, long long ldo) {
+    pdl_wait();
+    pdl_trigger();
     const int b = blockIdx.y;
     const uint8_t* row = E + (size_t)tok[b] * row_bytes_of(type, n);
     for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < n; e += gridDim.x * blockDim.x)
@@ -148,6 +150,8 @@ __global__ void gdn_conv_kernel(const float* __restrict__ qkv, long long ld_qkv,
                                 const float* __restrict__ w, float* __restrict__ slots, size_t slot_stride,
                                 const uint32_t* __restrict__ cur_slot, int ckpt, float* __restrict__ out,
                                 long long ld_out) {
+    pdl_wait();
+    pdl_trigger();
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= conv_dim) return;
     const int cur = (int)*cur_slot;
@@ -189,6 +193,8 @@ __global__ void __launch_bounds__(128) gdn_recur_kernel(
     const float* __restrict__ ssm_a, int n_k, int n_v, int B, float eps, float* __restrict__ slots,
     size_t slot_stride, const uint32_t* __restrict__ cur_slot, int ckpt, float* __restrict__ out,
     long long ld_out) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float qn[QB_MAX_TOK][kDK], kn[QB_MAX_TOK][kDK];
     __shared__ float kq_s[QB_MAX_TOK], beta_s[QB_MAX_TOK], decay_s[QB_MAX_TOK];
     const int h = blockIdx.x, kh = h % n_k;
@@ -279,6 +285,8 @@ __global__ void __launch_bounds__(128) gdn_recur_kernel(
 // per (token, v-head): RMSNorm(o_h, ssm_norm) * SiLU(z_h)  (src/model.c:927-941)
 __global__ void gdn_out_kernel(const float* __restrict__ o, const float* __restrict__ z, long long ld,
                                const float* __restrict__ w, int dv, float eps, float* __restrict__ y) {
+    pdl_wait();
+    pdl_trigger();
     const int b = blockIdx.y, h = blockIdx.x;
     const int lane = threadIdx.x;   // 32 lanes, dv = 128: 4 values each, 8-lane chains in lanes 0..7
     const float* oh = o + (size_t)b * ld + (size_t)h * dv;
@@ -307,6 +315,8 @@ __global__ void attn_prep_kernel(float* __restrict__ q, long long ldq, const flo
                                  int n_head, int n_kv, int hd, int half, const float* __restrict__ rc,
                                  const float* __restrict__ rs, const uint32_t* __restrict__ pos0, float eps,
                                  float* __restrict__ kc, float* __restrict__ vc) {
+    pdl_wait();
+    pdl_trigger();
     const int b = blockIdx.y;
     const int unit = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
@@ -352,17 +362,22 @@ __global__ void attn_prep_kernel(float* __restrict__ q, long long ldq, const flo
     for (int j = 0; j < nj; ++j) dst[lane + 32 * j] = v[j];
 }
 
-// One CTA (256 threads = hd) per (head, token).  Scores over t <= pos+b,
-// softmax (max-subtracted; polynomial exp on the 8-aligned body and
+// One CTA (8 warps) per (head, token).  Scores over t <= pos+b (warp per
+// position), softmax (max-subtracted; polynomial exp on the 8-aligned body and
 // correctly-rounded expf on the tail, sum in double as src/kernels.c:901-939),
-// then out[i] = sum_t p_t v_t[i] accumulated in t order, times sigmoid(gate).
+// then out = sum_t p_t v_t with the positions split over the 8 warps (lane
+// owns 8 of the 256 dims), partial sums reduced in warp order, times
+// sigmoid(gate) (src/model.c:353-406).
 __global__ void __launch_bounds__(256) attn_decode_kernel(const float* __restrict__ q, long long ldq,
                                                           const float* __restrict__ kc,
                                                           const float* __restrict__ vc, int n_head, int n_kv,
                                                           int hd, const uint32_t* __restrict__ pos0,
                                                           float* __restrict__ out, long long ldo) {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ float sc[];   // [n_ctx] scores
     __shared__ float qs[256];
+    __shared__ float part[8][256];
     __shared__ double red_d[8];
     __shared__ float red_f[8];
     const int h = blockIdx.x, b = blockIdx.y;
@@ -375,7 +390,6 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const float* __restric
     qs[tid] = qh[tid];
     __syncthreads();
     const float scale_attn = __fdiv_rn(1.0f, sqrtf((float)hd));
-    // scores: warp per position, lane owns 8 elements
     for (int t = warp; t < n; t += 8) {
         const float* kt = kc + (size_t)t * kvrow + (size_t)kh * hd;
         float a = 0.f;
@@ -408,18 +422,33 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const float* __restric
     double tot = 0.0;
     for (int i = 0; i < 8; ++i) tot += red_d[i];
     const float inv = (float)(1.0 / tot);
-    for (int t = tid; t < n; t += 256) sc[t] = __fmul_rn(sc[t], inv);
+    // weighted V sum: warp w takes positions [w*n/8, (w+1)*n/8)
+    const int t0 = (int)((long long)n * warp / 8), t1 = (int)((long long)n * (warp + 1) / 8);
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+    const float* vbase = vc + (size_t)kh * hd + lane;
+    for (int t = t0; t < t1; ++t) {
+        const float p = __fmul_rn(sc[t], inv);
+        const float* vt = vbase + (size_t)t * kvrow;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = fmaf(p, vt[32 * j], acc[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) part[warp][lane + 32 * j] = acc[j];
     __syncthreads();
-    float acc = 0.f;
-    const float* vcol = vc + (size_t)kh * hd + tid;
-    for (int t = 0; t < n; ++t) acc = fmaf(sc[t], vcol[(size_t)t * kvrow], acc);
+    float o = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) o += part[w][tid];
     const float g = sigmoid_ref(qh[hd + tid]);
-    out[(size_t)b * ldo + (size_t)h * hd + tid] = __fmul_rn(acc, g);
+    out[(size_t)b * ldo + (size_t)h * hd + tid] = __fmul_rn(o, g);
 }
 
 // SwiGLU: silu(gate) * up (src/model.c:830-836)
 __global__ void silu_mul_kernel(const float* __restrict__ gate, const float* __restrict__ up, long long ld,
                                 int n, float* __restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     const int b = blockIdx.y;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
         const size_t o = (size_t)b * ld + i;
@@ -437,11 +466,15 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t i) {
 }
 
 __global__ void argmax_reset_kernel(unsigned long long* keys, int B) {
+    pdl_wait();
+    pdl_trigger();
     if (threadIdx.x < B) keys[threadIdx.x] = 0ull;
 }
 
 __global__ void argmax_kernel(const float* __restrict__ x, long long ldx, int n,
                               unsigned long long* __restrict__ keys) {
+    pdl_wait();
+    pdl_trigger();
     const int b = blockIdx.y;
     const float* xr = x + (size_t)b * ldx;
     unsigned long long best = 0ull;
@@ -458,11 +491,15 @@ __global__ void argmax_kernel(const float* __restrict__ x, long long ldx, int n,
 }
 
 __global__ void argmax_to_u32_kernel(const unsigned long long* keys, int B, uint32_t* out) {
+    pdl_wait();
+    pdl_trigger();
     if (threadIdx.x < B) out[threadIdx.x] = 0xFFFFFFFFu - (uint32_t)(keys[threadIdx.x] & 0xFFFFFFFFull);
 }
 
 // --------------------- kernels.h element-wise ops -----------------------------
 __global__ void op_rmsnorm_kernel(float* out, const float* x, const float* w, long long n, float eps) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float sh[32];
     float ss = 0.f;
     for (long long i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
@@ -478,6 +515,8 @@ __global__ void op_rmsnorm_kernel(float* out, const float* x, const float* w, lo
 }
 
 __global__ void op_l2norm_kernel(float* out, const float* x, long long n, float eps) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float sh[32];
     float ss = 0.f;
     for (long long i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
@@ -496,6 +535,8 @@ __global__ void op_l2norm_kernel(float* out, const float* x, long long n, float 
 // expf with the reference's clamps (src/kernels.c:825-871); softplus is scalar
 // in the reference (874-885).
 __global__ void op_act_kernel(int which, float* x, long long n) {
+    pdl_wait();
+    pdl_trigger();
     const long long body = n & ~7ll;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
         const float v = x[i];
@@ -514,6 +555,8 @@ __global__ void op_act_kernel(int which, float* x, long long n) {
 }
 
 __global__ void op_softmax_kernel(float* x, long long n) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float shf[32];
     __shared__ double shd[32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -548,7 +591,7 @@ __global__ void op_softmax_kernel(float* x, long long n) {
 
 cudaError_t qb_embed(int type, const void* tok_embd, int n_embd, const uint32_t* tokens, int B, float* out,
                      long long ldo, cudaStream_t st) {
-    embed_kernel<<<dim3((n_embd + 255) / 256, B), 256, 0, st>>>(type, (const uint8_t*)tok_embd, n_embd, tokens,
+    qb_launch(embed_kernel, dim3((n_embd + 255) / 256, B), dim3(256), 0, st, type, (const uint8_t*)tok_embd, n_embd, tokens,
                                                                 out, ldo);
     return cudaGetLastError();
 }
@@ -556,7 +599,7 @@ cudaError_t qb_embed(int type, const void* tok_embd, int n_embd, const uint32_t*
 cudaError_t qb_gdn_conv(const float* qkv, long long ld_qkv, int conv_dim, int B, const float* conv_w,
                         float* state_slots, size_t slot_stride, const uint32_t* cur_slot, int ckpt,
                         float* out, long long ld_out, cudaStream_t st) {
-    gdn_conv_kernel<<<(conv_dim + 127) / 128, 128, 0, st>>>(qkv, ld_qkv, conv_dim, B, conv_w, state_slots,
+    qb_launch(gdn_conv_kernel, dim3((conv_dim + 127) / 128), dim3(128), 0, st, qkv, ld_qkv, conv_dim, B, conv_w, state_slots,
                                                             slot_stride, cur_slot, ckpt, out, ld_out);
     return cudaGetLastError();
 }
@@ -566,7 +609,7 @@ cudaError_t qb_gdn_recur(const float* qkvc, long long ld_qkvc, const float* beta
                          int dk, int B, float eps, float* state_slots, size_t slot_stride,
                          const uint32_t* cur_slot, int ckpt, float* out, long long ld_out, cudaStream_t st) {
     if (dk != kDK || B > QB_MAX_TOK) return cudaErrorInvalidValue;
-    gdn_recur_kernel<<<dim3(n_v, kDK / 16), 128, 0, st>>>(qkvc, ld_qkvc, beta, alpha, ld_ba, dt_bias, ssm_a,
+    qb_launch(gdn_recur_kernel, dim3(n_v, kDK / 16), dim3(128), 0, st, qkvc, ld_qkvc, beta, alpha, ld_ba, dt_bias, ssm_a,
                                                           n_k, n_v, B, eps, state_slots, slot_stride, cur_slot,
                                                           ckpt, out, ld_out);
     return cudaGetLastError();
@@ -574,7 +617,7 @@ cudaError_t qb_gdn_recur(const float* qkvc, long long ld_qkvc, const float* beta
 
 cudaError_t qb_gdn_out(const float* o, const float* z, long long ld, const float* norm_w, int n_v, int dv,
                        int B, float eps, float* y, cudaStream_t st) {
-    gdn_out_kernel<<<dim3(n_v, B), 32, 0, st>>>(o, z, ld, norm_w, dv, eps, y);
+    qb_launch(gdn_out_kernel, dim3(n_v, B), dim3(32), 0, st, o, z, ld, norm_w, dv, eps, y);
     return cudaGetLastError();
 }
 
@@ -584,7 +627,7 @@ cudaError_t qb_attn_prep(float* q, long long ldq, const float* kv, long long ldk
                          float* k_cache, float* v_cache, cudaStream_t st) {
     if (hd != 256 || rope_half % 32 != 0 || rope_half * 2 > hd) return cudaErrorInvalidValue;
     const int units = n_head + 2 * n_kv;
-    attn_prep_kernel<<<dim3((units + 3) / 4, B), 128, 0, st>>>(q, ldq, kv, ldkv, q_norm, k_norm, n_head, n_kv,
+    qb_launch(attn_prep_kernel, dim3((units + 3) / 4, B), dim3(128), 0, st, q, ldq, kv, ldkv, q_norm, k_norm, n_head, n_kv,
                                                                hd, rope_half, rope_cos, rope_sin, pos, eps,
                                                                k_cache, v_cache);
     return cudaGetLastError();
@@ -600,47 +643,47 @@ cudaError_t qb_attn_decode(const float* q, long long ldq, const float* k_cache, 
         cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         configured_for = (int)smem;
     }
-    attn_decode_kernel<<<dim3(n_head, B), 256, smem, st>>>(q, ldq, k_cache, v_cache, n_head, n_kv, hd, pos,
+    qb_launch(attn_decode_kernel, dim3(n_head, B), dim3(256), smem, st, q, ldq, k_cache, v_cache, n_head, n_kv, hd, pos,
                                                            out, ldo);
     return cudaGetLastError();
 }
 
 cudaError_t qb_silu_mul(const float* gate, const float* up, long long ld, int n, int B, float* out,
                         cudaStream_t st) {
-    silu_mul_kernel<<<dim3((n + 255) / 256, B), 256, 0, st>>>(gate, up, ld, n, out);
+    qb_launch(silu_mul_kernel, dim3((n + 255) / 256, B), dim3(256), 0, st, gate, up, ld, n, out);
     return cudaGetLastError();
 }
 
 cudaError_t qb_argmax_reset(unsigned long long* keys, int B, cudaStream_t st) {
-    argmax_reset_kernel<<<1, 32, 0, st>>>(keys, B);
+    qb_launch(argmax_reset_kernel, dim3(1), dim3(32), 0, st, keys, B);
     return cudaGetLastError();
 }
 
 cudaError_t qb_argmax(const float* x, long long ldx, int n, int B, unsigned long long* keys, cudaStream_t st) {
     const int blocks = (n + 1023) / 1024 < 148 ? (n + 1023) / 1024 : 148;
-    argmax_kernel<<<dim3(blocks, B), 256, 0, st>>>(x, ldx, n, keys);
+    qb_launch(argmax_kernel, dim3(blocks, B), dim3(256), 0, st, x, ldx, n, keys);
     return cudaGetLastError();
 }
 
 cudaError_t qb_argmax_to_u32(const unsigned long long* keys, int B, uint32_t* out, cudaStream_t st) {
-    argmax_to_u32_kernel<<<1, 32, 0, st>>>(keys, B, out);
+    qb_launch(argmax_to_u32_kernel, dim3(1), dim3(32), 0, st, keys, B, out);
     return cudaGetLastError();
 }
 
 cudaError_t qb_op_rmsnorm(float* out, const float* x, const float* w, long long n, float eps, cudaStream_t st) {
-    op_rmsnorm_kernel<<<1, 1024, 0, st>>>(out, x, w, n, eps);
+    qb_launch(op_rmsnorm_kernel, dim3(1), dim3(1024), 0, st, out, x, w, n, eps);
     return cudaGetLastError();
 }
 cudaError_t qb_op_l2norm(float* out, const float* x, long long n, float eps, cudaStream_t st) {
-    op_l2norm_kernel<<<1, 1024, 0, st>>>(out, x, n, eps);
+    qb_launch(op_l2norm_kernel, dim3(1), dim3(1024), 0, st, out, x, n, eps);
     return cudaGetLastError();
 }
 cudaError_t qb_op_act(int which, float* x, long long n, cudaStream_t st) {
     const long long blocks = (n + 255) / 256;
-    op_act_kernel<<<(unsigned)(blocks < 4096 ? (blocks ? blocks : 1) : 4096), 256, 0, st>>>(which, x, n);
+    qb_launch(op_act_kernel, dim3((unsigned)(blocks < 4096 ? (blocks ? blocks : 1) : 4096)), dim3(256), 0, st, which, x, n);
     return cudaGetLastError();
 }
 cudaError_t qb_op_softmax(float* x, long long n, cudaStream_t st) {
-    op_softmax_kernel<<<1, 1024, 0, st>>>(x, n);
+    qb_launch(op_softmax_kernel, dim3(1), dim3(1024), 0, st, x, n);
     return cudaGetLastError();
 }

@@ -6,17 +6,27 @@
 // and their dequantisation are those of include/quant.h:14-62 and
 // src/quant.c:86-182.
 //
-// Design.  The weights are repacked once at load time from GGUF super-blocks
+// Data path.  Weights are repacked once at load time from GGUF super-blocks
 // into 16-row tiles whose bytes land directly in mma.sync m16n8k16 A-fragment
-// order (same byte count, only reordered).  Inside the kernel each 4-bit /
-// 6-bit / 8-bit code is expanded to an *exact* fp16 integer (IQ4 lookup table
-// via byte permutes, K-quant codes via the 1024+q exponent trick), so the
-// tensor core multiplies exact weight codes with the activations.  The
-// activations are split into fp16 hi + lo halves (after a power-of-two scale
-// per 256-column block), which keeps ~22 significant bits: the products are
-// exact in the fp32 accumulator and the result carries fp32-level error.  The
-// per-32 (IQ4_XS, Q4_K, Q5_K, Q8_0) or per-16 (Q6_K) block scales are
-// applied to the fp32 partial sums after each sub-block's MMAs.
+// order (the byte count of every format is unchanged).  Inside the kernel
+// each 4/6/8-bit code is expanded to an *exact* fp16 integer (IQ4 lookup
+// table via byte permutes, K-quant codes via the 1024+q exponent trick), so
+// the tensor core multiplies exact weight codes with the activations.  The
+// activations are split into fp16 hi + lo halves after a power-of-two scale
+// per 256-column block (~22 significant bits): the products are exact in
+// the fp32 accumulator and results carry fp32-level error.  Per-32 / per-16
+// block scales are applied to the fp32 partial sums of each sub-block.
+//
+// Pipeline.  Two persistent CTAs of 8 warps per SM.  Every warp streams its
+// own (pair of tiles x 256 columns) stages of contiguous repacked bytes into
+// a private shared-memory ring with cp.async.bulk and mbarrier completion,
+// refilling a slot as soon as it has decoded it (~100 KB in flight per SM),
+// and decodes / runs the MMAs from shared memory.  The flattened (tile pair, block) stage
+// space of all fused matrices is split evenly over every consumer warp of
+// the grid (stream-K); a tile pair split across warps is finished by the last
+// contributing warp, which sums the partials in warp order (deterministic).
+// Programmatic dependent launch lets the producer prefetch weights while the
+// previous kernel on the stream finishes.
 //
 // mma k-index <-> element mapping, shared by every format and by the
 // activation fragments: within the 16-element step s of a 32-element
@@ -32,16 +42,26 @@ constexpr uint32_t H1152x2 = 0x64806480u;   // half2(1152, 1152) = 1024 + 128
 constexpr uint32_t H1024x2 = 0x64006400u;   // half2(1024, 1024)
 constexpr uint32_t H1056x2 = 0x64206420u;   // half2(1056, 1056) = 1024 + 32
 constexpr uint32_t C64 = 0x64646464u;
+constexpr int kConsumers = 8;                // warps per CTA (each streams its own weights)
+constexpr int kThreads = kConsumers * 32;
+#ifndef QB_QMV_CTAS
+#define QB_QMV_CTAS 2
+#endif
+constexpr int kCtasPerSm = QB_QMV_CTAS;
+#ifndef QB_QMV_SMEM_KB
+#define QB_QMV_SMEM_KB (224 / QB_QMV_CTAS)
+#endif
+constexpr int kSmemBudget = QB_QMV_SMEM_KB * 1024;   // per CTA
+constexpr int kRingOff = 512;                // full barriers (8 warps x 8 slots x 8 B), then the rings
 
 // IQ4_NL table biased by +128 (reference src/quant.c:30-32: kvalues_iq4nl).
-// u[v] = kvalues[v] + 128, packed four bytes per word, little endian.
 __constant__ uint32_t c_iq4_lut[4];
 
-// Expand 8 IQ4 nibbles (word = 4 qs bytes) into the four fp16x2 operands
-// of the two k16 steps: out[0] = step0 reg(k 2c,2c+1), out[1] = step0 reg
-// (k 2c+8,2c+9), out[2] / out[3] = step1.  Values are exact kvalues.
-__device__ __forceinline__ void iq4_expand(uint32_t w, uint32_t T0, uint32_t T1, uint32_t T2,
-                                           uint32_t T3, uint32_t (&o)[4]) {
+// Expand 8 IQ4 nibbles (word = qs bytes 4c..4c+3 of a sub-block: byte j holds
+// element j (low nibble) and j+16 (high)) into the four fp16x2 operands:
+// o[0] elems (4c, 4c+1) step 0, o[1] (4c+2, 4c+3) step 0, o[2]/o[3] step 1.
+__device__ __forceinline__ void iq4_expand(uint32_t w, uint32_t T0, uint32_t T1, uint32_t T2, uint32_t T3,
+                                           uint32_t (&o)[4]) {
     const uint32_t lo3 = w & 0x77777777u;
     const uint32_t sel = ((w >> 1) & 0x44444444u) | 0x32103210u;
     const uint32_t lo3h = lo3 >> 16;
@@ -49,31 +69,38 @@ __device__ __forceinline__ void iq4_expand(uint32_t w, uint32_t T0, uint32_t T1,
     const uint32_t r_lo = prmt(a, b, sel);                 // [b0lo b0hi b1lo b1hi]
     const uint32_t ah = prmt(T0, T1, lo3h), bh = prmt(T2, T3, lo3h);
     const uint32_t r_hi = prmt(ah, bh, sel >> 16);         // [b2lo b2hi b3lo b3hi]
-    o[0] = hsub2_u32(prmt(r_lo, C64, 0x5240u), H1152x2);   // elems 4c, 4c+1   (lo nibbles)
-    o[1] = hsub2_u32(prmt(r_hi, C64, 0x5240u), H1152x2);   // elems 4c+2, 4c+3
-    o[2] = hsub2_u32(prmt(r_lo, C64, 0x5341u), H1152x2);   // elems 16+4c, +1  (hi nibbles)
+    o[0] = hsub2_u32(prmt(r_lo, C64, 0x5240u), H1152x2);
+    o[1] = hsub2_u32(prmt(r_hi, C64, 0x5240u), H1152x2);
+    o[2] = hsub2_u32(prmt(r_lo, C64, 0x5341u), H1152x2);
     o[3] = hsub2_u32(prmt(r_hi, C64, 0x5341u), H1152x2);
 }
 
-// 4 unsigned bytes (each < 256 after bias) -> two half2 (b0,b1), (b2,b3) = 1024 + byte
+// 4 unsigned bytes -> two half2 (1024 + b0, 1024 + b1), (1024 + b2, 1024 + b3)
 __device__ __forceinline__ void bytes_to_h2(uint32_t u, uint32_t& h01, uint32_t& h23) {
     h01 = prmt(u, C64, 0x5140u);
     h23 = prmt(u, C64, 0x7362u);
 }
 
 template <int NT>
-__device__ __forceinline__ void mma_step(float (&cs)[NT][4], const uint32_t (&a)[4],
-                                         const uint2* __restrict__ xf, int lane) {
+__device__ __forceinline__ void zero(float (&a)[NT][4]) {
 #pragma unroll
-    for (int ct = 0; ct < NT; ++ct) {
-        const uint2 b = __ldg(xf + ct * 32 + lane);
-        mma_16816(cs[ct], a, b.x, b.y);
-    }
+    for (int c = 0; c < NT; ++c) a[c][0] = a[c][1] = a[c][2] = a[c][3] = 0.f;
 }
 
 template <int NT>
-__device__ __forceinline__ void scale_acc(float (&ab)[NT][4], const float (&cs)[NT][4], float dg,
-                                          float dg8) {
+__device__ __forceinline__ void load_b(uint2 (&b)[NT], const uint2* __restrict__ xf, int lane) {
+#pragma unroll
+    for (int ct = 0; ct < NT; ++ct) b[ct] = __ldg(xf + ct * 32 + lane);
+}
+
+template <int NT>
+__device__ __forceinline__ void mma_nt(float (&cs)[NT][4], const uint32_t (&a)[4], const uint2 (&b)[NT]) {
+#pragma unroll
+    for (int ct = 0; ct < NT; ++ct) mma_16816(cs[ct], a, b[ct].x, b[ct].y);
+}
+
+template <int NT>
+__device__ __forceinline__ void scale_acc(float (&ab)[NT][4], const float (&cs)[NT][4], float dg, float dg8) {
 #pragma unroll
     for (int ct = 0; ct < NT; ++ct) {
         ab[ct][0] = fmaf(dg, cs[ct][0], ab[ct][0]);
@@ -83,94 +110,140 @@ __device__ __forceinline__ void scale_acc(float (&ab)[NT][4], const float (&cs)[
     }
 }
 
-// token index of accumulator column (ct, 2c+i)
 template <int NT>
 __device__ __forceinline__ int col_token(int ct, int col) {
     return NT == 1 ? (col & 3) : col;
 }
 
-// ---------------------------------------------------------------------------
-// Per-format processing of one 256-column super-block for one 16-row tile.
-// ab accumulates sum over sub-blocks of (block scale * tensor-core partial);
-// xsum-based corrections (Q4_K/Q5_K mins) are returned in ab as well.
+// ------------------------- per-format stage processors ------------------------
+// A stage is (tile pair, one 256-column block); u points at the pair's bytes in
+// shared memory (tile 2p, then tile 2p+1).  ab[t] accumulates, for tile t,
+// sum over sub-blocks of (block scale * tensor-core partial); mt[t] collects
+// terms that are not scaled by the activation scale (Q4_K / Q5_K mins).
+
+// IQ4_XS tile-block: qs 2048 B (4 chunks x 32 lanes x 16 B) + 16 rows x 8 B
+// scales stored as [A(4) d(2) Bh(2)]: A byte i = ls_i | (ls_{4+i} & 3) << 6,
+// Bh nibble j = ls_{4+j} >> 2 (a byte-aligned rearrangement of the block's
+// scales_l / scales_h; same 8 bytes).
+constexpr int kIq4Tile = 16 * 136;
+
+__device__ __forceinline__ void iq4_scales(const uint8_t* u, int row, uint32_t& L0, uint32_t& L1, float& d) {
+    const uint2 v = lds64(u + 2048 + row * 8);
+    L0 = v.x & 0x3F3F3F3Fu;
+    const uint32_t x = prmt(v.y, 0u, 0x3322u);
+    const uint32_t nib = (x & 0x000F000Fu) | ((x >> 4) & 0x0F000F00u);
+    L1 = ((v.x >> 6) & 0x03030303u) | (nib << 2);
+    d = h2f_bits(v.y);
+}
+__device__ __forceinline__ float iq4_dl(uint32_t L0, uint32_t L1, float d, int sb) {
+    const uint32_t L = sb < 4 ? L0 : L1;
+    const float f = __int_as_float(prmt(L, 0x4B000000u, 0x7440u + (sb & 3)));   // 2^23 + ls
+    return (f - 8388640.0f) * d;                                                // (ls - 32) * d
+}
 
 template <int NT>
-__device__ __forceinline__ void blk_iq4xs(const uint8_t* __restrict__ unit, const uint2* __restrict__ xf,
-                                          int lane, float (&ab)[NT][4]) {
+__device__ __forceinline__ void stage_iq4xs(const uint8_t* u, const uint2* __restrict__ xf, int lane,
+                                            float (&ab)[2][NT][4], float (&)[2][NT][4]) {
     const int g = lane >> 2;
-    const uint4 q0 = ldg_nc_128(unit + 0 * 512 + lane * 16);
-    const uint4 q1 = ldg_nc_128(unit + 1 * 512 + lane * 16);
-    const uint4 q2 = ldg_nc_128(unit + 2 * 512 + lane * 16);
-    const uint4 q3 = ldg_nc_128(unit + 3 * 512 + lane * 16);
-    const uint2 sg = ldg_nc_64(unit + 2048 + g * 8);
-    const uint2 sg8 = ldg_nc_64(unit + 2048 + (g + 8) * 8);
-    const float dg = h2f_bits(sg.x), dg8 = h2f_bits(sg8.x);
-    const uint32_t shg = sg.x >> 16, shg8 = sg8.x >> 16;
+    uint32_t L[2][2][2];
+    float d[2][2];
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int r = 0; r < 2; ++r) iq4_scales(u + t * kIq4Tile, g + 8 * r, L[t][r][0], L[t][r][1], d[t][r]);
     const uint32_t T0 = c_iq4_lut[0], T1 = c_iq4_lut[1], T2 = c_iq4_lut[2], T3 = c_iq4_lut[3];
-    const uint4 qq[4] = {q0, q1, q2, q3};
+    // activation fragments of the chunk's 4 k16 steps, issued together ahead of the decode
+    uint2 bn[4][NT];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) load_b<NT>(bn[i], xf + i * NT * 32, lane);
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
+        uint2 bc[4][NT];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int ct = 0; ct < NT; ++ct) bc[i][ct] = bn[i][ct];
+        if (p < 3) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) load_b<NT>(bn[i], xf + ((p + 1) * 4 + i) * NT * 32, lane);
+        }
+        const uint4 q0 = lds128(u + p * 512 + lane * 16);
+        const uint4 q1 = lds128(u + kIq4Tile + p * 512 + lane * 16);
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
             const int sb = 2 * p + h;
-            const uint32_t wg = h ? qq[p].z : qq[p].x;
-            const uint32_t wg8 = h ? qq[p].w : qq[p].y;
-            uint32_t eg[4], eg8[4];
-            iq4_expand(wg, T0, T1, T2, T3, eg);
-            iq4_expand(wg8, T0, T1, T2, T3, eg8);
-            float cs[NT][4];
+            uint32_t e[2][2][4];
+            iq4_expand(h ? q0.z : q0.x, T0, T1, T2, T3, e[0][0]);
+            iq4_expand(h ? q0.w : q0.y, T0, T1, T2, T3, e[0][1]);
+            iq4_expand(h ? q1.z : q1.x, T0, T1, T2, T3, e[1][0]);
+            iq4_expand(h ? q1.w : q1.y, T0, T1, T2, T3, e[1][1]);
+            float cs[2][NT][4];
+            zero<NT>(cs[0]);
+            zero<NT>(cs[1]);
 #pragma unroll
-            for (int ct = 0; ct < NT; ++ct) cs[ct][0] = cs[ct][1] = cs[ct][2] = cs[ct][3] = 0.f;
-            {
-                const uint32_t a[4] = {eg[0], eg8[0], eg[1], eg8[1]};
-                mma_step<NT>(cs, a, xf + (sb * 2 + 0) * NT * 32, lane);
+            for (int s = 0; s < 2; ++s) {
+#pragma unroll
+                for (int t = 0; t < 2; ++t) {
+                    const uint32_t a[4] = {e[t][0][2 * s], e[t][1][2 * s], e[t][0][2 * s + 1], e[t][1][2 * s + 1]};
+                    mma_nt<NT>(cs[t], a, bc[2 * h + s]);
+                }
             }
-            {
-                const uint32_t a[4] = {eg[2], eg8[2], eg[3], eg8[3]};
-                mma_step<NT>(cs, a, xf + (sb * 2 + 1) * NT * 32, lane);
-            }
-            // ls = 6-bit sub-block scale (src/kernels.c:84-90)
-            const uint32_t lsg = ((sg.y >> (4 * sb)) & 0xFu) | (((shg >> (2 * sb)) & 3u) << 4);
-            const uint32_t lsg8 = ((sg8.y >> (4 * sb)) & 0xFu) | (((shg8 >> (2 * sb)) & 3u) << 4);
-            const float dlg = dg * (small_u2f(lsg) - 32.f);
-            const float dlg8 = dg8 * (small_u2f(lsg8) - 32.f);
-            scale_acc<NT>(ab, cs, dlg, dlg8);
+#pragma unroll
+            for (int t = 0; t < 2; ++t)
+                scale_acc<NT>(ab[t], cs[t], iq4_dl(L[t][0][0], L[t][0][1], d[t][0], sb),
+                              iq4_dl(L[t][1][0], L[t][1][1], d[t][1], sb));
         }
     }
 }
 
+// Q8_0: tile-block = 8 units of 544 B (32 columns: 16 rows x 32 qs in lane
+// order [row g s0][row g8 s0][row g s1][row g8 s1], then 16 x fp16 d).
+constexpr int kQ8Tile = 8 * 544;
 template <int NT>
-__device__ __forceinline__ void blk_q8_0(const uint8_t* __restrict__ unit0, const uint2* __restrict__ xf,
-                                         int lane, float (&ab)[NT][4]) {
+__device__ __forceinline__ void stage_q8_0(const uint8_t* u, const uint2* __restrict__ xf, int lane,
+                                           float (&ab)[2][NT][4], float (&)[2][NT][4]) {
     const int g = lane >> 2;
 #pragma unroll 2
     for (int sb = 0; sb < 8; ++sb) {
-        const uint8_t* unit = unit0 + sb * 544;
-        const uint4 q = ldg_nc_128(unit + lane * 16);
-        const uint32_t dd = __ldg(reinterpret_cast<const unsigned short*>(unit + 512) + g) |
-                            ((uint32_t)__ldg(reinterpret_cast<const unsigned short*>(unit + 512) + g + 8) << 16);
-        const float dg = h2f_bits(dd), dg8 = h2f_bits(dd >> 16);
-        float cs[NT][4];
+        float cs[2][NT][4];
+        zero<NT>(cs[0]);
+        zero<NT>(cs[1]);
+        uint32_t a[2][2][4];
+        float dd[2][2];
 #pragma unroll
-        for (int ct = 0; ct < NT; ++ct) cs[ct][0] = cs[ct][1] = cs[ct][2] = cs[ct][3] = 0.f;
-        // words: [row g s0][row g8 s0][row g s1][row g8 s1]
-        const uint32_t w[4] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u,
-                               q.w ^ 0x80808080u};
+        for (int t = 0; t < 2; ++t) {
+            const uint8_t* un = u + t * kQ8Tile + sb * 544;
+            const uint4 q = lds128(un + lane * 16);
+            const uint32_t w[4] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u, q.w ^ 0x80808080u};
+#pragma unroll
+            for (int s = 0; s < 2; ++s) {
+                bytes_to_h2(w[2 * s], a[t][s][0], a[t][s][2]);
+                bytes_to_h2(w[2 * s + 1], a[t][s][1], a[t][s][3]);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) a[t][s][i] = hsub2_u32(a[t][s][i], H1152x2);
+            }
+            const uint32_t dw = lds32(un + 512 + (g & ~1) * 2);                   // rows g&~1, g|1
+            const uint32_t dw8 = lds32(un + 512 + ((g + 8) & ~1) * 2);
+            dd[t][0] = h2f_bits(g & 1 ? dw >> 16 : dw);
+            dd[t][1] = h2f_bits(g & 1 ? dw8 >> 16 : dw8);
+        }
 #pragma unroll
         for (int s = 0; s < 2; ++s) {
-            uint32_t a[4];
-            bytes_to_h2(w[2 * s], a[0], a[2]);
-            bytes_to_h2(w[2 * s + 1], a[1], a[3]);
+            uint2 b[NT];
+            load_b<NT>(b, xf + (sb * 2 + s) * NT * 32, lane);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) a[i] = hsub2_u32(a[i], H1152x2);
-            mma_step<NT>(cs, a, xf + ((sb) * 2 + s) * NT * 32, lane);
+            for (int t = 0; t < 2; ++t) mma_nt<NT>(cs[t], a[t][s], b);
         }
-        scale_acc<NT>(ab, cs, dg, dg8);
+#pragma unroll
+        for (int t = 0; t < 2; ++t) scale_acc<NT>(ab[t], cs[t], dd[t][0], dd[t][1]);
     }
 }
 
-// Q4_K / Q5_K: w = d*sc*q - dmin*m  ->  d*sc*sum(q x) - dmin*m*sum(x)
-// (src/kernels.c:414-510; get_scale_min_k4 include/quant.h:21-29)
+// Q4_K / Q5_K: w = d*sc*q - dmin*m -> d*sc*sum(q x) - dmin*m*sum(x)
+// (src/kernels.c:414-510; get_scale_min_k4 include/quant.h:21-29).
+// Tile-block: qs 2048 B (chunk j: [row g s0][row g s1][row g8 s0][row g8 s1]
+// of bytes 32j + 16s + 4c..), [qh 512 B (Q5_K): [row g s0][row g s1][row g8 s0]
+// [row g8 s1] of qh bytes 16s + 4c..], then 16 rows x [d dmin scales(12)].
 __device__ __forceinline__ void k4_scale_min(const uint8_t* s12, int j, float& sc, float& m) {
     uint32_t d, mm;
     if (j < 4) {
@@ -185,223 +258,347 @@ __device__ __forceinline__ void k4_scale_min(const uint8_t* s12, int j, float& s
 }
 
 template <int NT, bool Q5>
-__device__ __forceinline__ void blk_qk(const uint8_t* __restrict__ unit, const uint2* __restrict__ xf,
-                                       const float* __restrict__ xsum_blk, int xsum_stride, int lane,
-                                       float (&ab)[NT][4], float (&mt)[NT][4]) {
+__device__ __forceinline__ void stage_qk(const uint8_t* u, const uint2* __restrict__ xf, const float* __restrict__ xsum_blk,
+                                         int xsum_stride, int lane, float (&ab)[2][NT][4], float (&mt)[2][NT][4]) {
     const int g = lane >> 2, c = lane & 3;
-    constexpr int QS = 2048, QH = 2048, SC = Q5 ? 2560 : 2048;
-    const uint8_t* hdr_g = unit + SC + g * 16;
-    const uint8_t* hdr_g8 = unit + SC + (g + 8) * 16;
-    const uint4 hg = ldg_nc_128(hdr_g);
-    const uint4 hg8 = ldg_nc_128(hdr_g8);
-    const float dg = h2f_bits(hg.x), dmg = h2f_bits(hg.x >> 16);
-    const float dg8 = h2f_bits(hg8.x), dmg8 = h2f_bits(hg8.x >> 16);
-    uint8_t s12g[12], s12g8[12];
-    {
-        const uint32_t a[3] = {hg.y, hg.z, hg.w}, b[3] = {hg8.y, hg8.z, hg8.w};
+    constexpr int TB = Q5 ? 16 * 176 : 16 * 144;
+    constexpr int SC = Q5 ? 2560 : 2048;
+#pragma unroll 1
+    for (int t = 0; t < 2; ++t) {
+        const uint8_t* ut = u + t * TB;
+        const uint4 hg = lds128(ut + SC + g * 16);
+        const uint4 hg8 = lds128(ut + SC + (g + 8) * 16);
+        const float dg = h2f_bits(hg.x), dmg = h2f_bits(hg.x >> 16);
+        const float dg8 = h2f_bits(hg8.x), dmg8 = h2f_bits(hg8.x >> 16);
+        uint8_t s12g[12], s12g8[12];
+        {
+            const uint32_t a[3] = {hg.y, hg.z, hg.w}, b[3] = {hg8.y, hg8.z, hg8.w};
 #pragma unroll
-        for (int i = 0; i < 12; ++i) {
-            s12g[i] = (uint8_t)(a[i >> 2] >> (8 * (i & 3)));
-            s12g8[i] = (uint8_t)(b[i >> 2] >> (8 * (i & 3)));
-        }
-    }
-    uint4 qh = make_uint4(0, 0, 0, 0);
-    if (Q5) qh = ldg_nc_128(unit + QH + lane * 16);   // [row g s0][row g s1][row g8 s0][row g8 s1]
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        // words [row g s0][row g s1][row g8 s0][row g8 s1] of bytes 32j + 16s + 4c..
-        const uint4 q = ldg_nc_128(unit + QS * 0 + j * 512 + lane * 16);
-#pragma unroll
-        for (int hi = 0; hi < 2; ++hi) {
-            const int sb = 2 * j + hi;
-            float cs[NT][4];
-#pragma unroll
-            for (int ct = 0; ct < NT; ++ct) cs[ct][0] = cs[ct][1] = cs[ct][2] = cs[ct][3] = 0.f;
-#pragma unroll
-            for (int s = 0; s < 2; ++s) {
-                uint32_t ug = ((s ? q.y : q.x) >> (4 * hi)) & 0x0F0F0F0Fu;
-                uint32_t ug8 = ((s ? q.w : q.z) >> (4 * hi)) & 0x0F0F0F0Fu;
-                if (Q5) {
-                    ug |= (((s ? qh.y : qh.x) >> sb) & 0x01010101u) << 4;
-                    ug8 |= (((s ? qh.w : qh.z) >> sb) & 0x01010101u) << 4;
-                }
-                uint32_t a[4];
-                bytes_to_h2(ug, a[0], a[2]);
-                bytes_to_h2(ug8, a[1], a[3]);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) a[i] = hsub2_u32(a[i], H1024x2);
-                mma_step<NT>(cs, a, xf + (sb * 2 + s) * NT * 32, lane);
+            for (int i = 0; i < 12; ++i) {
+                s12g[i] = (uint8_t)(a[i >> 2] >> (8 * (i & 3)));
+                s12g8[i] = (uint8_t)(b[i >> 2] >> (8 * (i & 3)));
             }
-            float scg, mg, scg8, mg8;
-            k4_scale_min(s12g, sb, scg, mg);
-            k4_scale_min(s12g8, sb, scg8, mg8);
-            scale_acc<NT>(ab, cs, dg * scg, dg8 * scg8);
-            // - dmin*m * sum(x): x sums are unscaled, so this term goes to mt, which
-            // is added to the result without the block's activation scale.
+        }
+        uint4 qh = make_uint4(0, 0, 0, 0);
+        if (Q5) qh = lds128(ut + 2048 + lane * 16);
 #pragma unroll
-            for (int ct = 0; ct < NT; ++ct) {
+        for (int j = 0; j < 4; ++j) {
+            const uint4 q = lds128(ut + j * 512 + lane * 16);
 #pragma unroll
-                for (int i = 0; i < 2; ++i) {
-                    const int col = 2 * c + i;
-                    const bool is_lo = NT == 1 ? (col >= 4) : (ct == 1);
-                    if (!is_lo) {
-                        const int tok = col_token<NT>(ct, col);
-                        const float xs = xsum_blk[tok * xsum_stride + sb];
-                        mt[ct][i] -= dmg * mg * xs;
-                        mt[ct][2 + i] -= dmg8 * mg8 * xs;
+            for (int hi = 0; hi < 2; ++hi) {
+                const int sb = 2 * j + hi;
+                float cs[NT][4];
+                zero<NT>(cs);
+#pragma unroll
+                for (int s = 0; s < 2; ++s) {
+                    uint32_t ug = ((s ? q.y : q.x) >> (4 * hi)) & 0x0F0F0F0Fu;
+                    uint32_t ug8 = ((s ? q.w : q.z) >> (4 * hi)) & 0x0F0F0F0Fu;
+                    if (Q5) {
+                        ug |= (((s ? qh.y : qh.x) >> sb) & 0x01010101u) << 4;
+                        ug8 |= (((s ? qh.w : qh.z) >> sb) & 0x01010101u) << 4;
                     }
+                    uint32_t a[4];
+                    bytes_to_h2(ug, a[0], a[2]);
+                    bytes_to_h2(ug8, a[1], a[3]);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) a[i] = hsub2_u32(a[i], H1024x2);
+                    uint2 b[NT];
+                    load_b<NT>(b, xf + (sb * 2 + s) * NT * 32, lane);
+                    mma_nt<NT>(cs, a, b);
+                }
+                float scg, mg, scg8, mg8;
+                k4_scale_min(s12g, sb, scg, mg);
+                k4_scale_min(s12g8, sb, scg8, mg8);
+                scale_acc<NT>(ab[t], cs, dg * scg, dg8 * scg8);
+#pragma unroll
+                for (int ct = 0; ct < NT; ++ct)
+#pragma unroll
+                    for (int i = 0; i < 2; ++i) {
+                        const int col = 2 * c + i;
+                        const bool is_lo = NT == 1 ? (col >= 4) : (ct == 1);
+                        if (!is_lo) {
+                            const float xs = xsum_blk[col_token<NT>(ct, col) * xsum_stride + sb];
+                            mt[t][ct][i] -= dmg * mg * xs;
+                            mt[t][ct][2 + i] -= dmg8 * mg8 * xs;
+                        }
+                    }
+            }
+        }
+    }
+}
+
+// Q6_K tile-block: lo plane 2048 B (chunk qc: word i = group 4qc+i, nibbles
+// 0..3 = row g elements 4c..4c+3, 4..7 = row g8), hi plane 1024 B (word per
+// group pair: byte j bits 4-5/6-7 = even/odd member of the first group, 0-1/
+// 2-3 of the second), scales 16 rows x 16 int8, d 16 x fp16.
+constexpr int kQ6Tile = 16 * 210;
+template <int NT>
+__device__ __forceinline__ void stage_q6k(const uint8_t* u, const uint2* __restrict__ xf, int lane,
+                                          float (&ab)[2][NT][4], float (&)[2][NT][4]) {
+    const int g = lane >> 2;
+#pragma unroll 1
+    for (int t = 0; t < 2; ++t) {
+        const uint8_t* ut = u + t * kQ6Tile;
+        const uint4 sc_g = lds128(ut + 3072 + g * 16);
+        const uint4 sc_g8 = lds128(ut + 3072 + (g + 8) * 16);
+        const uint32_t dw = lds32(ut + 3328 + (g & ~1) * 2);
+        const uint32_t dw8 = lds32(ut + 3328 + ((g + 8) & ~1) * 2);
+        const float dg = h2f_bits(g & 1 ? dw >> 16 : dw), dg8 = h2f_bits(g & 1 ? dw8 >> 16 : dw8);
+        const uint32_t scw_g[4] = {sc_g.x, sc_g.y, sc_g.z, sc_g.w};
+        const uint32_t scw_g8[4] = {sc_g8.x, sc_g8.y, sc_g8.z, sc_g8.w};
+#pragma unroll
+        for (int ch = 0; ch < 2; ++ch) {
+            const uint4 hq = lds128(ut + 2048 + ch * 512 + lane * 16);
+            const uint32_t hw[4] = {hq.x, hq.y, hq.z, hq.w};
+#pragma unroll
+            for (int qc = 0; qc < 2; ++qc) {
+                const uint4 lq = lds128(ut + (ch * 2 + qc) * 512 + lane * 16);
+                const uint32_t lw[4] = {lq.x, lq.y, lq.z, lq.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int G = (ch * 2 + qc) * 4 + i;
+                    const uint32_t h = hw[(G >> 1) & 3];
+                    const bool Bg = G & 1;
+                    const uint32_t he = Bg ? ((h << 4) & 0x30303030u) : (h & 0x30303030u);
+                    const uint32_t ho = Bg ? ((h << 2) & 0x30303030u) : ((h >> 2) & 0x30303030u);
+                    const uint32_t ev = (lw[i] & 0x0F0F0F0Fu) | he;
+                    const uint32_t od = ((lw[i] >> 4) & 0x0F0F0F0Fu) | ho;
+                    const uint32_t p01 = prmt(ev, od, 0x5140u);
+                    const uint32_t p23 = prmt(ev, od, 0x7362u);
+                    uint32_t a[4];
+                    a[0] = hsub2_u32(prmt(p01, C64, 0x5140u), H1056x2);
+                    a[2] = hsub2_u32(prmt(p01, C64, 0x7362u), H1056x2);
+                    a[1] = hsub2_u32(prmt(p23, C64, 0x5140u), H1056x2);
+                    a[3] = hsub2_u32(prmt(p23, C64, 0x7362u), H1056x2);
+                    float cs[NT][4];
+                    zero<NT>(cs);
+                    uint2 b[NT];
+                    load_b<NT>(b, xf + G * NT * 32, lane);
+                    mma_nt<NT>(cs, a, b);
+                    const int scg = (int)(int8_t)(scw_g[G >> 2] >> (8 * (G & 3)));
+                    const int scg8 = (int)(int8_t)(scw_g8[G >> 2] >> (8 * (G & 3)));
+                    scale_acc<NT>(ab[t], cs, dg * (small_u2f((uint32_t)(scg + 128)) - 128.f),
+                                  dg8 * (small_u2f((uint32_t)(scg8 + 128)) - 128.f));
                 }
             }
         }
     }
+}
+
+__host__ __device__ constexpr int tile_block_bytes(int type) {
+    return type == QB_IQ4_XS ? kIq4Tile
+         : type == QB_Q8_0   ? kQ8Tile
+         : type == QB_Q6_K   ? kQ6Tile
+         : type == QB_Q4_K   ? 16 * 144
+         : type == QB_Q5_K   ? 16 * 176
+         : 0;
+}
+
+// ------------------------------- the kernel ------------------------------------
+
+struct QmvK {
+    QSeg seg[QB_MAX_SEG];
+    int pair0[QB_MAX_SEG + 1];   // first tile pair of each segment; pair0[nseg] = total pairs
+    int nseg;
+    int K, nb, N;
+    int S;                       // total stages = pairs * nb (fits 32 bits for every launch)
+    int Wt;                      // consumer warps in the grid
+    int stages_per_warp_ring;    // ring depth
+    const uint2* xfrag;
+    const float* xscale;
+    const float* xsum;
+    int accumulate;
+    int row_lo, row_hi;
+    float* partial;              // [Wt][2][32][8]
+    unsigned* counters;          // [pairs]
+    unsigned* err;
+};
+
+// stage ranges: warp w owns [S*w/Wt, S*(w+1)/Wt); the grid guarantees Wt <= S,
+// so every warp owns at least one stage.  S * Wt < 2^31 for every launch.
+__device__ __forceinline__ int warp_s0(int S, int Wt, int w) { return (int)((unsigned)(S * w) / (unsigned)Wt); }
+__device__ __forceinline__ int stage_owner(int S, int Wt, int s) {
+    return (int)((unsigned)((s + 1) * Wt - 1) / (unsigned)S);
 }
 
 template <int NT>
-__device__ __forceinline__ void blk_q6k(const uint8_t* __restrict__ unit, const uint2* __restrict__ xf,
-                                        int lane, float (&ab)[NT][4]) {
-    const int g = lane >> 2;
-    // lo plane 2048 B: 4 chunks x 32 lanes x 16 B (one word per 16-element group)
-    // hi plane 1024 B: 2 chunks x 32 lanes x 16 B (one word per pair of groups)
-    // scales 256 B: [row][16] int8 ; d 32 B: [row] fp16
-    const uint4 sc_g = ldg_nc_128(unit + 3072 + g * 16);
-    const uint4 sc_g8 = ldg_nc_128(unit + 3072 + (g + 8) * 16);
-    const uint32_t dd = __ldg(reinterpret_cast<const unsigned short*>(unit + 3328) + g) |
-                        ((uint32_t)__ldg(reinterpret_cast<const unsigned short*>(unit + 3328) + g + 8) << 16);
-    const float dg = h2f_bits(dd), dg8 = h2f_bits(dd >> 16);
-    const uint32_t scw_g[4] = {sc_g.x, sc_g.y, sc_g.z, sc_g.w};
-    const uint32_t scw_g8[4] = {sc_g8.x, sc_g8.y, sc_g8.z, sc_g8.w};
-#pragma unroll
-    for (int ch = 0; ch < 2; ++ch) {
-        const uint4 hq = ldg_nc_128(unit + 2048 + ch * 512 + lane * 16);
-        const uint32_t hw[4] = {hq.x, hq.y, hq.z, hq.w};
-#pragma unroll
-        for (int qc = 0; qc < 2; ++qc) {
-            const uint4 lq = ldg_nc_128(unit + (ch * 2 + qc) * 512 + lane * 16);
-            const uint32_t lw[4] = {lq.x, lq.y, lq.z, lq.w};
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int G = (ch * 2 + qc) * 4 + i;       // 16-element group
-                const uint32_t h = hw[G >> 1 & 3];           // word of groups (2m, 2m+1)
-                const bool B = G & 1;
-                const uint32_t he = B ? ((h << 4) & 0x30303030u) : (h & 0x30303030u);
-                const uint32_t ho = B ? ((h << 2) & 0x30303030u) : ((h >> 2) & 0x30303030u);
-                const uint32_t ev = (lw[i] & 0x0F0F0F0Fu) | he;          // [e0(g) e2(g) e0(g8) e2(g8)]
-                const uint32_t od = ((lw[i] >> 4) & 0x0F0F0F0Fu) | ho;   // [e1(g) e3(g) e1(g8) e3(g8)]
-                const uint32_t p01 = prmt(ev, od, 0x5140u);  // [e0g o0g e1g o1g] -> rows g: (e0,o0),(e1,o1)
-                const uint32_t p23 = prmt(ev, od, 0x7362u);  // row g8
-                uint32_t a[4];
-                a[0] = hsub2_u32(prmt(p01, C64, 0x5140u), H1056x2);  // row g  elems 4c,4c+1
-                a[2] = hsub2_u32(prmt(p01, C64, 0x7362u), H1056x2);  // row g  elems 4c+2,4c+3
-                a[1] = hsub2_u32(prmt(p23, C64, 0x5140u), H1056x2);  // row g8
-                a[3] = hsub2_u32(prmt(p23, C64, 0x7362u), H1056x2);
-                float cs[NT][4];
-#pragma unroll
-                for (int ct = 0; ct < NT; ++ct) cs[ct][0] = cs[ct][1] = cs[ct][2] = cs[ct][3] = 0.f;
-                // group G = sub-block G/2, step G&1
-                mma_step<NT>(cs, a, xf + G * NT * 32, lane);
-                const int scg = (int)(int8_t)(scw_g[G >> 2] >> (8 * (G & 3)));
-                const int scg8 = (int)(int8_t)(scw_g8[G >> 2] >> (8 * (G & 3)));
-                const float fg = dg * (small_u2f((uint32_t)(scg + 128)) - 128.f);
-                const float fg8 = dg8 * (small_u2f((uint32_t)(scg8 + 128)) - 128.f);
-                scale_acc<NT>(ab, cs, fg, fg8);
-            }
-        }
-    }
-}
-
-template <int FMT, int NT>
-__global__ void __launch_bounds__(256) qmv_kernel(QmvParams p) {
-    const int tile = blockIdx.x;
+__device__ __forceinline__ void finish_pair(const QmvK& p, int pair, int gw, int s0, int s1, float (&acc)[2][NT][4],
+                                            int lane) {
     int si = 0;
 #pragma unroll
     for (int s = 1; s < QB_MAX_SEG; ++s)
-        if (s < p.nseg && tile >= p.seg[s].tile0) si = s;
-    const QSeg S = p.seg[si];
-    const int lt = tile - S.tile0;
-    const int nb = p.K >> 8;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+        if (s < p.nseg && pair >= p.pair0[s]) si = s;
+    const QSeg& S = p.seg[si];
+    const int lp = pair - p.pair0[si];
     const int g = lane >> 2, c = lane & 3;
-    const int b0 = nb * warp / nw, b1 = nb * (warp + 1) / nw;
-    constexpr int UB = FMT == QB_Q8_0 ? 8 * qb_unit_bytes(QB_Q8_0) : qb_unit_bytes(FMT);
-    const uint8_t* base = S.w + (size_t)lt * nb * UB;
-
-    float acc[NT][4];
+    // combine hi/lo columns: o[t][i], i = (row g tok t0, row g tok t1, row g8 tok t0, row g8 tok t1)
+    float o[2][4];
 #pragma unroll
-    for (int ct = 0; ct < NT; ++ct) acc[ct][0] = acc[ct][1] = acc[ct][2] = acc[ct][3] = 0.f;
-
-    for (int b = b0; b < b1; ++b) {
-        float ab[NT][4], mt[NT][4];
+    for (int t = 0; t < 2; ++t)
 #pragma unroll
-        for (int ct = 0; ct < NT; ++ct) {
-            ab[ct][0] = ab[ct][1] = ab[ct][2] = ab[ct][3] = 0.f;
-            mt[ct][0] = mt[ct][1] = mt[ct][2] = mt[ct][3] = 0.f;
-        }
-        const uint8_t* unit = base + (size_t)b * UB;
-        const uint2* xf = p.xfrag + (size_t)b * 16 * NT * 32;   // 8 sub-blocks x 2 steps
-        if (FMT == QB_IQ4_XS) blk_iq4xs<NT>(unit, xf, lane, ab);
-        else if (FMT == QB_Q8_0) blk_q8_0<NT>(unit, xf, lane, ab);
-        else if (FMT == QB_Q4_K) blk_qk<NT, false>(unit, xf, p.xsum + b * 8, p.K >> 5, lane, ab, mt);
-        else if (FMT == QB_Q5_K) blk_qk<NT, true>(unit, xf, p.xsum + b * 8, p.K >> 5, lane, ab, mt);
-        else if (FMT == QB_Q6_K) blk_q6k<NT>(unit, xf, lane, ab);
-#pragma unroll
-        for (int ct = 0; ct < NT; ++ct) {
-#pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                const int tok = col_token<NT>(ct, 2 * c + i);
-                const float xs = __ldg(p.xscale + tok * nb + b);
-                acc[ct][i] = fmaf(xs, ab[ct][i], acc[ct][i]) + mt[ct][i];
-                acc[ct][2 + i] = fmaf(xs, ab[ct][2 + i], acc[ct][2 + i]) + mt[ct][2 + i];
-            }
-        }
-    }
-
-    // deterministic cross-warp reduction (warp order 0..nw-1)
-    __shared__ float red[8][NT][4][32];
-#pragma unroll
-    for (int ct = 0; ct < NT; ++ct)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) red[warp][ct][i][lane] = acc[ct][i];
-    __syncthreads();
-    if (warp != 0) return;
-    float v[NT][4];
-#pragma unroll
-    for (int ct = 0; ct < NT; ++ct)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            float s = 0.f;
-            for (int w = 0; w < nw; ++w) s += red[w][ct][i][lane];
-            v[ct][i] = s;
-        }
-    // combine hi + lo columns
-    float o[4];   // rows g (i=0,1) and g+8 (i=2,3); tokens t0 = tok(2c), t1 = tok(2c+1)
-    int t0, t1;
-    bool active;
-    if (NT == 1) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) o[i] = v[0][i] + __shfl_xor_sync(0xffffffffu, v[0][i], 2);
-        active = c < 2;
-        t0 = 2 * c;
-        t1 = 2 * c + 1;
-    } else {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) o[i] = v[0][i] + v[NT - 1][i];
-        active = true;
-        t0 = 2 * c;
-        t1 = 2 * c + 1;
-    }
-    if (!active) return;
-    const int r0 = lt * QB_TILE + g, r1 = r0 + 8;
-    const int rlo = p.row_lo, rhi = p.row_hi;
-    auto store = [&](int t, int r, float val) {
-        if (t < p.N && r < S.rows && r >= rlo && r < rhi) {
-            float* dst = S.out + (size_t)t * S.ldo + r;
-            *dst = p.accumulate ? (*dst + val) : val;
+        for (int i = 0; i < 4; ++i)
+            o[t][i] = NT == 1 ? acc[t][0][i] + __shfl_xor_sync(0xffffffffu, acc[t][0][i], 2)
+                              : acc[t][0][i] + acc[t][NT - 1][i];
+    const bool active = NT == 1 ? (c < 2) : true;
+    const int t0 = 2 * c, t1 = 2 * c + 1;
+    const int P0 = pair * p.nb, P1 = P0 + p.nb;
+    auto store = [&](int t, int i, float v) {
+        const int rr = lp * 32 + t * 16 + g + ((i & 2) ? 8 : 0);
+        const int tok = (i & 1) ? t1 : t0;
+        if (tok < p.N && rr < S.rows && rr >= p.row_lo && rr < p.row_hi) {
+            float* dst = S.out + (size_t)tok * S.ldo + rr;
+            *dst = p.accumulate ? (*dst + v) : v;
         }
     };
-    store(t0, r0, o[0]);
-    store(t1, r0, o[1]);
-    store(t0, r1, o[2]);
-    store(t1, r1, o[3]);
+    if (s0 <= P0 && s1 >= P1) {
+        if (active)
+#pragma unroll
+            for (int t = 0; t < 2; ++t)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) store(t, i, o[t][i]);
+        return;
+    }
+    // split pair: piece 0 if this warp started inside the pair (its first pair), else 1 (its last)
+    const int piece = s0 >= P0 ? 0 : 1;
+    float* slot = p.partial + ((size_t)gw * 2 + piece) * 256;
+    auto pidx = [&](int t, int i) { return (t * 16 + g + ((i & 2) ? 8 : 0)) * 8 + ((i & 1) ? t1 : t0); };
+    if (active)
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) slot[pidx(t, i)] = o[t][i];
+    __threadfence();
+    __syncwarp();
+    const int w_first = stage_owner(p.S, p.Wt, P0), w_last = stage_owner(p.S, p.Wt, P1 - 1);
+    const int contributors = w_last - w_first + 1;
+    unsigned old = 0;
+    if (lane == 0) old = atomicAdd(p.counters + pair, 1u);
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if ((int)old != contributors - 1) return;
+    __threadfence();
+    // the first contributor started before the pair unless it starts exactly at P0
+    const int first_piece = warp_s0(p.S, p.Wt, w_first) == P0 ? 0 : 1;
+    float sum[2][4] = {};
+    for (int w = w_first; w <= w_last; ++w) {
+        const int pc = w == w_first ? first_piece : 0;
+        const volatile float* sl = p.partial + ((size_t)w * 2 + pc) * 256;
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) sum[t][i] += sl[pidx(t, i)];
+    }
+    if (active)
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) store(t, i, sum[t][i]);
+    if (lane == 0) p.counters[pair] = 0u;   // ready for the next launch
+}
+
+template <int FMT, int NT>
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_kernel(QmvK p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr int TB = tile_block_bytes(FMT);
+    constexpr uint32_t STAGE = 2 * TB;
+    const int R = p.stages_per_warp_ring;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem) + warp * 8;
+    uint8_t* ring = smem + kRingOff + (size_t)warp * R * STAGE;
+    if (lane == 0) {
+        for (int i = 0; i < R; ++i) mbar_init(full + i, 1);
+        mbar_fence_init();
+    }
+    __syncwarp();
+    pdl_trigger();
+
+    const int gw = blockIdx.x * kConsumers + warp;
+    if (gw >= p.Wt) return;
+    const int s0 = warp_s0(p.S, p.Wt, gw), s1 = warp_s0(p.S, p.Wt, gw + 1);
+    const int n = s1 - s0;
+    // producer cursor (lane 0): tile pair / block / segment of the next stage to fetch
+    int ip = s0 / p.nb, ib = s0 - ip * p.nb, iseg = 0;
+    while (iseg + 1 < p.nseg && ip >= p.pair0[iseg + 1]) ++iseg;
+    auto issue = [&](int slot) {
+        const uint8_t* src = p.seg[iseg].w + ((size_t)(ip - p.pair0[iseg]) * 2 * p.nb + ib) * TB;
+        uint8_t* dst = ring + (size_t)slot * STAGE;
+        mbar_expect_tx(full + slot, STAGE);
+        bulk_g2s(dst, src, TB, full + slot);
+        bulk_g2s(dst + TB, src + (size_t)p.nb * TB, TB, full + slot);
+        if (++ib == p.nb) {
+            ib = 0;
+            ++ip;
+            while (iseg + 1 < p.nseg && ip >= p.pair0[iseg + 1]) ++iseg;
+        }
+    };
+    // weights do not depend on the previous kernel: start streaming before the wait
+    if (lane == 0)
+        for (int r = 0; r < R && r < n; ++r) issue(r);
+    pdl_wait();   // activations written by the previous kernel are complete from here on
+
+    float acc[2][NT][4];
+    zero<NT>(acc[0]);
+    zero<NT>(acc[1]);
+    const int c = lane & 3;
+    int cp = s0 / p.nb, cb = s0 - cp * p.nb;
+    int cur_pair = cp;
+    int slot = 0;
+    uint32_t phase = 0;
+    for (int r = 0; r < n; ++r) {
+        if (cp != cur_pair) {
+            finish_pair<NT>(p, cur_pair, gw, s0, s1, acc, lane);
+            zero<NT>(acc[0]);
+            zero<NT>(acc[1]);
+            cur_pair = cp;
+        }
+        if (!mbar_wait(full + slot, phase)) {
+            // give up: record it, let the copies this warp issued land, return
+            if (lane == 0) {
+                atomicExch(p.err, 2u);
+                int sl = slot;
+                uint32_t ph = phase;
+                for (int q = r; q < n && q < r + R; ++q) {
+                    mbar_wait(full + sl, ph, 1u << 20);
+                    if (++sl == R) { sl = 0; ph ^= 1u; }
+                }
+            }
+            return;
+        }
+        const int b = cb;
+        const uint8_t* u = ring + (size_t)slot * STAGE;
+        const uint2* xf = p.xfrag + (size_t)b * 16 * NT * 32;
+        float ab[2][NT][4], mt[2][NT][4];
+        zero<NT>(ab[0]);
+        zero<NT>(ab[1]);
+        zero<NT>(mt[0]);
+        zero<NT>(mt[1]);
+        if (FMT == QB_IQ4_XS) stage_iq4xs<NT>(u, xf, lane, ab, mt);
+        else if (FMT == QB_Q8_0) stage_q8_0<NT>(u, xf, lane, ab, mt);
+        else if (FMT == QB_Q6_K) stage_q6k<NT>(u, xf, lane, ab, mt);
+        else if (FMT == QB_Q4_K) stage_qk<NT, false>(u, xf, p.xsum + b * 8, p.K >> 5, lane, ab, mt);
+        else if (FMT == QB_Q5_K) stage_qk<NT, true>(u, xf, p.xsum + b * 8, p.K >> 5, lane, ab, mt);
+        __syncwarp();   // every lane is done with the slot
+        if (lane == 0 && r + R < n) issue(slot);
+        if (++slot == R) {
+            slot = 0;
+            phase ^= 1u;
+        }
+#pragma unroll
+        for (int ct = 0; ct < NT; ++ct)
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const float xs = __ldg(p.xscale + col_token<NT>(ct, 2 * c + i) * p.nb + b);
+#pragma unroll
+                for (int t = 0; t < 2; ++t) {
+                    acc[t][ct][i] = fmaf(xs, ab[t][ct][i], acc[t][ct][i]) + mt[t][ct][i];
+                    acc[t][ct][2 + i] = fmaf(xs, ab[t][ct][2 + i], acc[t][ct][2 + i]) + mt[t][ct][2 + i];
+                }
+            }
+        if (++cb == p.nb) {
+            cb = 0;
+            ++cp;
+        }
+    }
+    if (cur_pair >= 0) finish_pair<NT>(p, cur_pair, gw, s0, s1, acc, lane);
 }
 
 // ------------------------------- F32 ---------------------------------------
@@ -409,6 +606,8 @@ __global__ void __launch_bounds__(256) qmv_kernel(QmvParams p) {
 __global__ void qmv_f32_kernel(const float* __restrict__ W, int rows, int K, const float* __restrict__ x,
                                long long ldx, int N, float* __restrict__ out, long long ldo, int accumulate,
                                int row_lo, int row_hi) {
+    pdl_wait();
+    pdl_trigger();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     const int r = row_lo + warp;
     if (r >= row_hi || r >= rows) return;
@@ -426,7 +625,8 @@ __global__ void qmv_f32_kernel(const float* __restrict__ W, int rows, int K, con
 }
 
 // ------------------------------- repack ------------------------------------
-// One warp per (tile, unit).  src rows are GGUF rows of row_bytes bytes.
+// One warp per (tile, unit).  src rows are GGUF rows of row_bytes bytes; rows
+// beyond `rows` (padding to a whole tile pair) are written as zeros.
 
 __device__ __forceinline__ uint32_t ld_u32_unaligned(const uint8_t* p) {
     return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
@@ -452,7 +652,6 @@ __global__ void repack_kernel(int type, const uint8_t* __restrict__ src, size_t 
     uint32_t* d32 = reinterpret_cast<uint32_t*>(d);
 
     if (type == QB_IQ4_XS) {
-        // qs at byte 8 of the 136-byte block; sub-block sb = bytes 8+16sb..
         for (int p = 0; p < 4; ++p) {
             d32[(p * 512 + lane * 16) / 4 + 0] = w32(pg, 8 + 16 * (2 * p) + 4 * c);
             d32[(p * 512 + lane * 16) / 4 + 1] = w32(pg8, 8 + 16 * (2 * p) + 4 * c);
@@ -460,12 +659,22 @@ __global__ void repack_kernel(int type, const uint8_t* __restrict__ src, size_t 
             d32[(p * 512 + lane * 16) / 4 + 3] = w32(pg8, 8 + 16 * (2 * p + 1) + 4 * c);
         }
         if (lane < 16) {
+            // ls_ib = scales_l nibble ib | scales_h bits 2ib..2ib+1 << 4 (src/kernels.c:84-90)
             const uint8_t* rp = rowp(lane);
-            d32[(2048 + lane * 8) / 4 + 0] = w32(rp, 0);
-            d32[(2048 + lane * 8) / 4 + 1] = w32(rp, 4);
+            uint32_t A = 0, Bh = 0, dd = 0;
+            if (rp) {
+                const uint32_t sh = rp[2] | (rp[3] << 8);
+                const uint32_t sl = w32(rp, 4);
+                uint32_t ls[8];
+                for (int ib = 0; ib < 8; ++ib) ls[ib] = ((sl >> (4 * ib)) & 0xF) | (((sh >> (2 * ib)) & 3) << 4);
+                for (int i = 0; i < 4; ++i) A |= (ls[i] | ((ls[4 + i] & 3) << 6)) << (8 * i);
+                for (int j = 0; j < 4; ++j) Bh |= (ls[4 + j] >> 2) << (4 * j);
+                dd = rp[0] | (rp[1] << 8);
+            }
+            d32[(2048 + lane * 8) / 4 + 0] = A;
+            d32[(2048 + lane * 8) / 4 + 1] = dd | (Bh << 16);
         }
     } else if (type == QB_Q8_0) {
-        // block: d (2) + qs[32]; step s: elements 16s + 4c .. 16s + 4c + 3
         d32[lane * 4 + 0] = w32(pg, 2 + 4 * c);
         d32[lane * 4 + 1] = w32(pg8, 2 + 4 * c);
         d32[lane * 4 + 2] = w32(pg, 2 + 16 + 4 * c);
@@ -475,7 +684,6 @@ __global__ void repack_kernel(int type, const uint8_t* __restrict__ src, size_t 
             reinterpret_cast<uint16_t*>(d + 512)[lane] = rp ? (uint16_t)(rp[0] | (rp[1] << 8)) : 0;
         }
     } else if (type == QB_Q4_K || type == QB_Q5_K) {
-        // block: d(2) dmin(2) scales(12) [qh(32) for Q5_K] qs(128)
         const int qs_off = type == QB_Q5_K ? 48 : 16;
         for (int j = 0; j < 4; ++j) {
             d32[(j * 512 + lane * 16) / 4 + 0] = w32(pg, qs_off + 32 * j + 4 * c);
@@ -496,7 +704,7 @@ __global__ void repack_kernel(int type, const uint8_t* __restrict__ src, size_t 
             for (int i = 0; i < 4; ++i) d32[(hdr + lane * 16) / 4 + i] = w32(rp, 4 * i);
         }
     } else if (type == QB_Q6_K) {
-        // block: ql[128] qh[64] scales[16] d(2).  Element e of group G (16G + l'):
+        // ql[128] qh[64] scales[16] d(2).  Element e of group G (16G + l'):
         // n = G/8, m = (G%8)/2, is = G%2, l = 16is + l'
         // q = (ql[64n + 32(m&1) + l] >> 4(m>>1)) & 15 | ((qh[32n + l] >> 2m) & 3) << 4
         auto q6 = [&](const uint8_t* rp, int e) -> uint32_t {
@@ -507,8 +715,6 @@ __global__ void repack_kernel(int type, const uint8_t* __restrict__ src, size_t 
             const uint32_t hi = (rp[128 + 32 * n + l] >> (2 * m)) & 3u;
             return lo | (hi << 4);
         };
-        // lo plane: chunk qc (groups 4qc..4qc+3), word i = group G = 4qc+i:
-        //   nibbles 0..3 = row g elements 4c..4c+3, nibbles 4..7 = row g8
         for (int qc = 0; qc < 4; ++qc)
             for (int i = 0; i < 4; ++i) {
                 const int G = 4 * qc + i;
@@ -519,14 +725,11 @@ __global__ void repack_kernel(int type, const uint8_t* __restrict__ src, size_t 
                 }
                 d32[(qc * 512 + lane * 16) / 4 + i] = wv;
             }
-        // hi plane: word for group pair (2m', 2m'+1), stored at chunk m'/4, slot m'%4.
-        // byte j: bits 4-5 = A even_j, 6-7 = A odd_j, 0-1 = B even_j, 2-3 = B odd_j, where
-        // even = (row g e0, row g e2, row g8 e0, row g8 e2), odd = (e1, e3 likewise).
         for (int mp = 0; mp < 8; ++mp) {
             uint32_t wv = 0;
             for (int j = 0; j < 4; ++j) {
                 const uint8_t* rp = j < 2 ? pg : pg8;
-                const int ee = (j & 1) ? 2 : 0;      // element offset of the even member
+                const int ee = (j & 1) ? 2 : 0;
                 for (int half = 0; half < 2; ++half) {
                     const int G = 2 * mp + half;
                     const uint32_t ev = q6(rp, 16 * G + 4 * c + ee) >> 4;
@@ -547,16 +750,16 @@ __global__ void repack_kernel(int type, const uint8_t* __restrict__ src, size_t 
 
 // ------------------------- activation fragments ------------------------------
 // x [N][ldx] fp32 -> xfrag (hi/lo fp16, B-fragment order), xscale, xsum.
-// Optional RMSNorm folded in: y = (x * inv_rms) * w  (src/kernels.c:741-777),
-// with inv_rms computed per token by the same CTA.  Two segments allow the
-// MTP concat [RMSNorm(e, enorm) || RMSNorm(h, hnorm)] (src/model.c:1044-1047).
-// One CTA per (token, slice of 256-column blocks).
+// Optional RMSNorm folded in: y = (x * inv_rms) * w  (src/kernels.c:741-777);
+// every CTA computes its token's inv_rms itself (the row is a few KB), so the
+// grid spreads over all 256-column blocks.  Two segments allow the MTP concat
+// [RMSNorm(e, enorm) || RMSNorm(h, hnorm)] (src/model.c:1044-1047).
 
 struct XSeg {
-    const float* x;       // segment input, token t at x + t*ldx
+    const float* x;
     long long ldx;
-    const float* w;       // RMSNorm weight (nullptr: no norm)
-    int len;              // columns in this segment (multiple of 256)
+    const float* w;
+    int len;
 };
 
 __device__ __forceinline__ float block_sum(float v, float* sh) {
@@ -574,86 +777,93 @@ __device__ __forceinline__ float block_sum(float v, float* sh) {
 __global__ void __launch_bounds__(256) xprep_kernel(XSeg s0, XSeg s1, int nseg, int N, int NT, float eps,
                                                     uint2* __restrict__ xfrag, float* __restrict__ xscale,
                                                     float* __restrict__ xsum, int want_xsum) {
+    pdl_wait();
+    pdl_trigger();
     const int t = blockIdx.y;
     const int K = s0.len + (nseg > 1 ? s1.len : 0);
     const int nb = K >> 8;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
     __shared__ float sh[32];
     float inv[2] = {1.f, 1.f};
+    const int b_first = blockIdx.x * nw;
     for (int si = 0; si < nseg; ++si) {
         const XSeg& S = si ? s1 : s0;
         if (!S.w) continue;
         const float* x = S.x + (size_t)t * S.ldx;
         float ss = 0.f;
-        for (int i = threadIdx.x; i < S.len; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
+        for (int i = threadIdx.x * 4; i < S.len; i += blockDim.x * 4) {
+            const float4 v = *reinterpret_cast<const float4*>(x + i);
+            ss = fmaf(v.x, v.x, ss);
+            ss = fmaf(v.y, v.y, ss);
+            ss = fmaf(v.z, v.z, ss);
+            ss = fmaf(v.w, v.w, ss);
+        }
         ss = block_sum(ss, sh);
         inv[si] = 1.0f / sqrtf(ss / (float)S.len + eps);
     }
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    const int ct_hi = 0;
-    for (int b = blockIdx.x * nw + warp; b < nb; b += gridDim.x * nw) {
-        const int col0 = b * 256;
-        const int si = (nseg > 1 && col0 >= s0.len) ? 1 : 0;
-        const XSeg& S = si ? s1 : s0;
-        const int lc0 = col0 - (si ? s0.len : 0);
-        const float* x = S.x + (size_t)t * S.ldx + lc0;
-        float v[8];
-        // lane owns elements 4*lane .. 4*lane+3 and 128 + 4*lane .. +3
+    const int b = b_first + warp;
+    if (b >= nb) return;
+    const int col0 = b * 256;
+    const int si = (nseg > 1 && col0 >= s0.len) ? 1 : 0;
+    const XSeg& S = si ? s1 : s0;
+    const int lc0 = col0 - (si ? s0.len : 0);
+    const float* x = S.x + (size_t)t * S.ldx + lc0;
+    float v[8];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const float4 xv = *reinterpret_cast<const float4*>(x + h * 128 + 4 * lane);
-            v[4 * h + 0] = xv.x; v[4 * h + 1] = xv.y; v[4 * h + 2] = xv.z; v[4 * h + 3] = xv.w;
-            if (S.w) {
-                const float4 wv = *reinterpret_cast<const float4*>(S.w + lc0 + h * 128 + 4 * lane);
-                v[4 * h + 0] = (v[4 * h + 0] * inv[si]) * wv.x;
-                v[4 * h + 1] = (v[4 * h + 1] * inv[si]) * wv.y;
-                v[4 * h + 2] = (v[4 * h + 2] * inv[si]) * wv.z;
-                v[4 * h + 3] = (v[4 * h + 3] * inv[si]) * wv.w;
-            }
+    for (int h = 0; h < 2; ++h) {
+        const float4 xv = *reinterpret_cast<const float4*>(x + h * 128 + 4 * lane);
+        v[4 * h + 0] = xv.x; v[4 * h + 1] = xv.y; v[4 * h + 2] = xv.z; v[4 * h + 3] = xv.w;
+        if (S.w) {
+            const float4 wv = *reinterpret_cast<const float4*>(S.w + lc0 + h * 128 + 4 * lane);
+            v[4 * h + 0] = (v[4 * h + 0] * inv[si]) * wv.x;
+            v[4 * h + 1] = (v[4 * h + 1] * inv[si]) * wv.y;
+            v[4 * h + 2] = (v[4 * h + 2] * inv[si]) * wv.z;
+            v[4 * h + 3] = (v[4 * h + 3] * inv[si]) * wv.w;
         }
-        float am = 0.f;
+    }
+    float am = 0.f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(v[i]));
+    for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(v[i]));
 #pragma unroll
-        for (int o = 16; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-        int e = 0;
-        if (am > 0.f && isfinite(am)) {
-            int ex;
-            frexpf(am, &ex);          // am in [2^(ex-1), 2^ex)
-            e = 15 - ex;              // am * 2^e in [2^14, 2^15)
-            e = max(-100, min(100, e));
+    for (int o = 16; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    int e = 0;
+    if (am > 0.f && isfinite(am)) {
+        int ex;
+        frexpf(am, &ex);
+        e = max(-100, min(100, 15 - ex));   // am * 2^e in [2^14, 2^15)
+    }
+    if (lane == 0) xscale[t * nb + b] = ldexpf(1.f, -e);
+    const float sc = ldexpf(1.f, e);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int el = h * 128 + 4 * lane;
+        const int sb = b * 8 + (el >> 5), st = (el >> 4) & 1, cq = (el >> 2) & 3;
+        __half hv[4], lv[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float xs = v[4 * h + k] * sc;
+            hv[k] = __float2half_rn(xs);
+            lv[k] = __float2half_rn(xs - __half2float(hv[k]));
         }
-        if (lane == 0) xscale[t * nb + b] = ldexpf(1.f, -e);
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            // elements col0 + h*128 + 4*lane + k  -> sub-block, step, quad thread
-            const int el = h * 128 + 4 * lane;          // within the 256-block
-            const int sb = b * 8 + (el >> 5), st = (el >> 4) & 1, cq = (el >> 2) & 3;
-            __half hv[4], lv[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const float xs = ldexpf(v[4 * h + k], e);
-                hv[k] = __float2half_rn(xs);
-                lv[k] = __float2half_rn(xs - __half2float(hv[k]));
-            }
-            uint2 hi, lo;
-            hi.x = (uint32_t)__half_as_ushort(hv[0]) | ((uint32_t)__half_as_ushort(hv[1]) << 16);
-            hi.y = (uint32_t)__half_as_ushort(hv[2]) | ((uint32_t)__half_as_ushort(hv[3]) << 16);
-            lo.x = (uint32_t)__half_as_ushort(lv[0]) | ((uint32_t)__half_as_ushort(lv[1]) << 16);
-            lo.y = (uint32_t)__half_as_ushort(lv[2]) | ((uint32_t)__half_as_ushort(lv[3]) << 16);
-            int col_hi, col_lo, cth, ctl;
-            if (NT == 1) { col_hi = t; col_lo = t + 4; cth = ctl = 0; }
-            else { col_hi = t; col_lo = t; cth = ct_hi; ctl = 1; }
-            const size_t base = (size_t)(sb * 2 + st) * NT;
-            xfrag[(base + cth) * 32 + col_hi * 4 + cq] = hi;
-            xfrag[(base + ctl) * 32 + col_lo * 4 + cq] = lo;
-            if (want_xsum) {
-                // sum of the 32 unscaled elements of sub-block sb: 8 lanes hold it
-                float ps = v[4 * h] + v[4 * h + 1] + v[4 * h + 2] + v[4 * h + 3];
-                ps += __shfl_xor_sync(0xffffffffu, ps, 1);
-                ps += __shfl_xor_sync(0xffffffffu, ps, 2);
-                ps += __shfl_xor_sync(0xffffffffu, ps, 4);
-                if ((lane & 7) == 0) xsum[t * (K >> 5) + sb] = ps;
-            }
+        uint2 hi, lo;
+        hi.x = (uint32_t)__half_as_ushort(hv[0]) | ((uint32_t)__half_as_ushort(hv[1]) << 16);
+        hi.y = (uint32_t)__half_as_ushort(hv[2]) | ((uint32_t)__half_as_ushort(hv[3]) << 16);
+        lo.x = (uint32_t)__half_as_ushort(lv[0]) | ((uint32_t)__half_as_ushort(lv[1]) << 16);
+        lo.y = (uint32_t)__half_as_ushort(lv[2]) | ((uint32_t)__half_as_ushort(lv[3]) << 16);
+        const size_t base = (size_t)(sb * 2 + st) * NT;
+        if (NT == 1) {
+            xfrag[base * 32 + t * 4 + cq] = hi;
+            xfrag[base * 32 + (t + 4) * 4 + cq] = lo;
+        } else {
+            xfrag[base * 32 + t * 4 + cq] = hi;
+            xfrag[(base + 1) * 32 + t * 4 + cq] = lo;
+        }
+        if (want_xsum) {
+            float ps = v[4 * h] + v[4 * h + 1] + v[4 * h + 2] + v[4 * h + 3];
+            ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+            ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+            ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+            if ((lane & 7) == 0) xsum[t * (K >> 5) + sb] = ps;
         }
     }
 }
@@ -675,11 +885,13 @@ cudaError_t qb_quant_init_constants() {
     return cudaMemcpyToSymbol(c_iq4_lut, w, sizeof w);
 }
 
+// repacked matrices are padded to whole 32-row tile pairs
+static size_t padded_tiles(int rows) { return (size_t)((rows + 31) / 32) * 2; }
+
 size_t qb_repacked_bytes(int type, int rows, int K) {
     const int ub = qb_unit_bytes(type), uc = qb_unit_cols(type);
     if (!ub || K % 256) return 0;
-    const size_t tiles = (size_t)(rows + QB_TILE - 1) / QB_TILE;
-    return tiles * (size_t)(K / uc) * ub;
+    return padded_tiles(rows) * (size_t)(K / uc) * ub;
 }
 
 cudaError_t qb_repack(int type, const void* src_dev, int rows, int K, void* dst_dev, cudaStream_t st) {
@@ -687,8 +899,7 @@ cudaError_t qb_repack(int type, const void* src_dev, int rows, int K, void* dst_
     if (!ub || K % 256) return cudaErrorInvalidValue;
     const int upr = K / uc;
     const size_t row_bytes = (size_t)upr * (type == QB_Q8_0 ? 34 : ub / 16);
-    const long long tiles = (rows + QB_TILE - 1) / QB_TILE;
-    const long long units = tiles * upr;
+    const long long units = (long long)padded_tiles(rows) * upr;
     const int threads = 256;
     const long long blocks = (units * 32 + threads - 1) / threads;
     repack_kernel<<<(unsigned)blocks, threads, 0, st>>>(type, (const uint8_t*)src_dev, row_bytes, rows, upr,
@@ -710,46 +921,76 @@ cudaError_t qb_xprep(const QbXIn* in, int nseg, int N, float eps, uint2* xfrag, 
     }
     const int NT = N <= 4 ? 1 : 2;
     const int nb = K / 256;
-    const int any_norm = (s[0].w != nullptr) || (nseg > 1 && s[1].w != nullptr);
-    // with a norm the per-token reduction needs the whole token in one CTA
-    const int gx = any_norm ? 1 : (nb + 7) / 8;
-    xprep_kernel<<<dim3(gx, N), 256, 0, st>>>(s[0], s[1], nseg, N, NT, eps, xfrag, xscale, xsum, want_xsum);
-    return cudaGetLastError();
+    return qb_launch(xprep_kernel, dim3((nb + 7) / 8, N), dim3(256), 0, st, s[0], s[1], nseg, N, NT, eps, xfrag,
+                     xscale, xsum, want_xsum);
 }
+
+static int g_num_sms = 0;
 
 cudaError_t qb_qmv(int type, const QbQSeg* segs, int nseg, int K, int N, const uint2* xfrag,
                    const float* xscale, const float* xsum, int accumulate, int row_lo, int row_hi,
-                   cudaStream_t st) {
+                   const QbQmvWork& work, cudaStream_t st) {
     if (nseg < 1 || nseg > QB_MAX_SEG || N < 1 || N > QB_MAX_TOK || K % 256) return cudaErrorInvalidValue;
-    QmvParams p = {};
-    int tiles = 0;
+    if (!g_num_sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+    }
+    QmvK p = {};
+    int pairs = 0;
     for (int i = 0; i < nseg; ++i) {
         p.seg[i].w = (const uint8_t*)segs[i].w;
         p.seg[i].out = segs[i].out;
         p.seg[i].ldo = segs[i].ldo;
         p.seg[i].rows = segs[i].rows;
-        p.seg[i].tile0 = tiles;
-        tiles += (segs[i].rows + QB_TILE - 1) / QB_TILE;
+        p.pair0[i] = pairs;
+        pairs += (segs[i].rows + 31) / 32;
     }
+    p.pair0[nseg] = pairs;
+    if (pairs > work.max_pairs) return cudaErrorInvalidValue;
     p.nseg = nseg;
     p.K = K;
+    p.nb = K / 256;
     p.N = N;
+    const long long S64 = (long long)pairs * p.nb;
+    if (S64 * (long long)work.max_warps >= (1ll << 31)) return cudaErrorInvalidValue;
+    p.S = (int)S64;
+    const int tb = tile_block_bytes(type);
+    if (!tb) return cudaErrorInvalidValue;
+    const int stage = 2 * tb;
+    int R = (kSmemBudget - kRingOff) / (kConsumers * stage);
+    if (R > 8) R = 8;
+    if (R < 2) R = 2;
+    p.stages_per_warp_ring = R;
+    const size_t smem = kRingOff + (size_t)kConsumers * R * stage;
+    // every warp owns >= 1 stage (Wt <= S); aim for >= 4 stages per warp
+    int grid = g_num_sms * kCtasPerSm;
+    const int warps_needed = (p.S + 3) / 4;
+    if (grid * kConsumers > warps_needed) grid = (warps_needed + kConsumers - 1) / kConsumers;
+    if (grid < 1) grid = 1;
+    while (grid > 1 && grid * kConsumers > p.S) --grid;
+    p.Wt = grid * kConsumers < p.S ? grid * kConsumers : p.S;   // warps beyond Wt exit at once
+    if (p.Wt > work.max_warps) return cudaErrorInvalidValue;
     p.xfrag = xfrag;
     p.xscale = xscale;
     p.xsum = xsum;
     p.accumulate = accumulate;
     p.row_lo = row_lo;
     p.row_hi = row_hi;
-    // K split across warps of the CTA: more warps when there are few tiles
-    const int nb = K / 256;
-    int warps = tiles >= 1024 ? 4 : 8;
-    if (warps > nb) warps = nb;
-    const dim3 grid(tiles), block(32 * warps);
+    p.partial = work.partial;
+    p.counters = work.counters;
+    p.err = work.err;
     const bool nt2 = N > 4;
-#define QB_LAUNCH(F)                                                             \
-    do {                                                                         \
-        if (nt2) qmv_kernel<F, 2><<<grid, block, 0, st>>>(p);                    \
-        else qmv_kernel<F, 1><<<grid, block, 0, st>>>(p);                        \
+    cudaError_t e = cudaSuccess;
+#define QB_LAUNCH(F)                                                                                   \
+    do {                                                                                               \
+        auto kern = nt2 ? qmv_kernel<F, 2> : qmv_kernel<F, 1>;                                         \
+        static bool attr_set[2] = {false, false};                                                      \
+        if (!attr_set[nt2]) {                                                                          \
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);       \
+            attr_set[nt2] = true;                                                                      \
+        }                                                                                              \
+        e = qb_launch(kern, dim3(grid), dim3(kThreads), smem, st, p);                                  \
     } while (0)
     switch (type) {
     case QB_IQ4_XS: QB_LAUNCH(QB_IQ4_XS); break;
@@ -760,7 +1001,29 @@ cudaError_t qb_qmv(int type, const QbQSeg* segs, int nseg, int K, int N, const u
     default: return cudaErrorInvalidValue;
     }
 #undef QB_LAUNCH
-    return cudaGetLastError();
+    return e;
+}
+
+cudaError_t qb_qmv_work_alloc(QbQmvWork& w, int max_pairs) {
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    w.max_warps = sms * kCtasPerSm * kConsumers;
+    w.max_pairs = max_pairs;
+    cudaError_t e;
+    if ((e = cudaMalloc(&w.partial, (size_t)w.max_warps * 2 * 256 * sizeof(float))) != cudaSuccess) return e;
+    if ((e = cudaMalloc(&w.counters, (size_t)max_pairs * sizeof(unsigned))) != cudaSuccess) return e;
+    if ((e = cudaMalloc(&w.err, sizeof(unsigned))) != cudaSuccess) return e;
+    if ((e = cudaMemset(w.counters, 0, (size_t)max_pairs * sizeof(unsigned))) != cudaSuccess) return e;
+    if ((e = cudaMemset(w.err, 0, sizeof(unsigned))) != cudaSuccess) return e;
+    return cudaDeviceSynchronize();
+}
+
+void qb_qmv_work_free(QbQmvWork& w) {
+    if (w.partial) cudaFree(w.partial);
+    if (w.counters) cudaFree(w.counters);
+    if (w.err) cudaFree(w.err);
+    w = QbQmvWork{};
 }
 
 cudaError_t qb_qmv_f32(const float* W, int rows, int K, const float* x, long long ldx, int N, float* out,
@@ -769,6 +1032,6 @@ cudaError_t qb_qmv_f32(const float* W, int rows, int K, const float* x, long lon
     if (n <= 0) return cudaSuccess;
     const int threads = 256;
     const int blocks = (n * 32 + threads - 1) / threads;
-    qmv_f32_kernel<<<blocks, threads, 0, st>>>(W, rows, K, x, ldx, N, out, ldo, accumulate, row_lo, row_hi);
-    return cudaGetLastError();
+    return qb_launch(qmv_f32_kernel, dim3(blocks), dim3(threads), 0, st, W, rows, K, x, ldx, N, out, ldo, accumulate,
+                     row_lo, row_hi);
 }

@@ -12,7 +12,7 @@ import os
 import numpy as np
 
 _PKG = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_PKG, "libqwenb200.so")
+LIB_PATH = os.environ.get("QB_LIB", os.path.join(_PKG, "libqwenb200.so"))
 SYNTH_PATH = os.path.join(_PKG, "libqbsynth.so")
 
 GGML_F32, GGML_Q8_0, GGML_Q4_K, GGML_Q5_K, GGML_Q6_K, GGML_IQ4_XS = 0, 8, 12, 13, 14, 23
