@@ -212,6 +212,29 @@ float qb_bench(qwen_model_t *m, int what, uint32_t arg, uint32_t iters, double *
  * MTP residual, 16 h_save) to host.  Returns the float count, -1 on error. */
 int64_t qb_read_buffer(qwen_model_t *m, int id, float *dst, int64_t max_floats);
 
+/* ---- allocation-free entry point (no counterpart in the reference) ----
+ *
+ * For callers that cannot allocate device memory at call time: a runtime that
+ * owns all GPU memory through its own arena, or code on a latency-critical
+ * path where cudaMalloc would synchronise the device or fail under memory
+ * pressure.  Greedy argmax of `rows` fp32 logit rows that are already on the
+ * device (row r at logits + r * ld, n entries, first maximum wins as in
+ * model_sample_greedy / src/model.c:746-756); the index of row r goes to the
+ * device array out[r].  Work is enqueued on `stream` (a cudaStream_t; NULL is
+ * the legacy default stream) and the call returns without waiting.
+ *
+ * The scratch is a fixed static device array of QB_ARGMAX_NOALLOC_MAX_ROWS
+ * 64-bit keys (256 bytes); rows above that limit are rejected with an error.
+ * The function allocates nothing.  The first call on each device does a
+ * one-time set-up (a symbol-address lookup that may load the module): make
+ * it with that device current and before any stream capture.  All calls on a
+ * device share the one array, so calls that overlap on the GPU (e.g. on two
+ * streams without ordering between them) race.  Returns 0, or -1 with
+ * qb_last_error() set. */
+#define QB_ARGMAX_NOALLOC_MAX_ROWS 32
+int qb_argmax_rows_noalloc(const float *logits, int64_t ld, uint32_t n, uint32_t rows, uint32_t *out,
+                           void *stream);
+
 #ifdef __cplusplus
 }
 #endif

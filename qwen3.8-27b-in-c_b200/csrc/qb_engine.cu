@@ -1543,3 +1543,56 @@ extern "C" uint32_t model_sample_greedy(const float* logits, uint32_t vocab_size
     }
     return r;
 }
+
+// ---------------------- allocation-free greedy argmax -------------------------
+// For callers that must not allocate device memory at call time: code that
+// owns every byte of the GPU through its own arena or pool, or runs where a
+// cudaMalloc would synchronise the device or may fail under memory pressure.
+// Same kernels as model_sample_greedy, but the per-row (value, index) keys
+// live in this fixed file-scope array instead of library-allocated scratch.
+static __device__ __align__(256) unsigned long long g_noalloc_keys[QB_ARGMAX_NOALLOC_MAX_ROWS];
+
+namespace {
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+unsigned long long* g_noalloc_keys_ptr[kNoAllocMaxDevices] = {};   // per device, set on first use
+}   // namespace
+
+extern "C" int qb_argmax_rows_noalloc(const float* logits, int64_t ld, uint32_t n, uint32_t rows,
+                                      uint32_t* out, void* stream) {
+    if (!logits || !out || n == 0 || rows == 0) {
+        set_err(-1, "qb_argmax_rows_noalloc: null pointer or empty size (n %u, rows %u)", n, rows);
+        return -1;
+    }
+    if (rows > QB_ARGMAX_NOALLOC_MAX_ROWS) {
+        set_err(-1, "qb_argmax_rows_noalloc: rows %u exceeds the static scratch maximum of %d", rows,
+                QB_ARGMAX_NOALLOC_MAX_ROWS);
+        return -1;
+    }
+    if (n > 0x7FFFFFFFu || ld < (int64_t)n) {
+        set_err(-1, "qb_argmax_rows_noalloc: n %u must be < 2^31 and ld %lld >= n", n, (long long)ld);
+        return -1;
+    }
+    int dev = 0;
+    CK(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kNoAllocMaxDevices) {
+        set_err(-1, "qb_argmax_rows_noalloc: device ordinal %d >= %d", dev, kNoAllocMaxDevices);
+        return -1;
+    }
+    unsigned long long* keys = nullptr;
+    {
+        // set-up, once per device with that device current
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        if (!g_noalloc_keys_ptr[dev]) {
+            void* p = nullptr;
+            CK(cudaGetSymbolAddress(&p, g_noalloc_keys));
+            g_noalloc_keys_ptr[dev] = static_cast<unsigned long long*>(p);
+        }
+        keys = g_noalloc_keys_ptr[dev];
+    }
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    CK(qb_argmax_reset(keys, (int)rows, st));   // the keys of the previous call are stale
+    CK(qb_argmax(logits, ld, (int)n, (int)rows, keys, st));
+    CK(qb_argmax_to_u32(keys, (int)rows, out, st));
+    return 0;
+}

@@ -29,7 +29,7 @@ EXPORTED = [
     "rmsnorm", "l2norm", "silu_inplace", "sigmoid_inplace", "softplus_inplace", "softmax_inplace",
     "qb_last_error", "qb_last_error_str", "qb_clear_error", "qb_prefill", "qb_spec_generate",
     "qb_greedy_generate", "qb_last_argmax", "qb_last_loop_ms", "qb_read_state", "qb_read_buffer",
-    "qb_reset", "qb_bench",
+    "qb_reset", "qb_bench", "qb_argmax_rows_noalloc",
 ]
 
 
@@ -124,6 +124,8 @@ def lib():
         L.qb_reset.restype = i32
         L.qb_bench.argtypes = [P(QwenModel), i32, u32, u32, P(C.c_double)]
         L.qb_bench.restype = f32
+        L.qb_argmax_rows_noalloc.argtypes = [vp, C.c_int64, u32, u32, vp, vp]
+        L.qb_argmax_rows_noalloc.restype = i32
         _lib = L
     return _lib
 
@@ -180,6 +182,14 @@ def sample_greedy(logits):
     r = lib().model_sample_greedy(_fp(logits), logits.size)
     check()
     return r
+
+
+def argmax_rows_noalloc(logits_ptr, ld, n, rows, out_ptr, stream_ptr=None):
+    """qb_argmax_rows_noalloc on device pointers (ints); enqueued on the stream."""
+    rc = lib().qb_argmax_rows_noalloc(logits_ptr, ld, n, rows, out_ptr, stream_ptr)
+    if rc:
+        check()
+    return rc
 
 
 def op(name, x, w=None, eps=1e-6):
