@@ -292,8 +292,7 @@ struct Engine {
     // activations (QB_MAX_TOK rows each)
     float *bx, *h_save, *qkv, *qkvc, *z, *beta, *alpha, *o, *y, *qbuf, *kvbuf, *attn_o, *gate, *up, *act;
     float *logits, *mtp_x, *mtp_h, *mtp_logits, *emb;
-    uint2* xfrag = nullptr;
-    float *xscale = nullptr, *xsum = nullptr;
+    QbXBuf xb{};                          // prepared GEMV activations
     unsigned long long* keys = nullptr;   // [2][QB_MAX_TOK]: backbone, mtp
     QbQmvWork work{};
     QbCtrl* ctrl = nullptr;
@@ -371,7 +370,6 @@ const float* upload_f32(Engine& e, const GTensor* t) {
 int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
     CK(cudaGetDevice(&e.dev));
     CK(cudaStreamCreateWithFlags(&e.st, cudaStreamNonBlocking));
-    CK(qb_quant_init_constants());
     if (gguf_load(e.g, path)) return -1;
     e.cfg = e.g.cfg;
     qwen_config_t& c = e.cfg;
@@ -561,16 +559,22 @@ int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
     e.mtp_logits = A((size_t)T8 * e.V);
     e.emb = A((size_t)T8 * e.E);
     const int Kmax = std::max<int>({2 * e.E, e.F, (int)d.d_inner, (int)(d.n_head * d.head_dim)});
-    const size_t xf_bytes = (size_t)Kmax / 32 * 2 * 2 * 32 * 8;   // NT = 2
-    e.xfrag = (uint2*)e.dalloc(xf_bytes);
-    e.xscale = A((size_t)T8 * (Kmax / 256));
-    e.xsum = A((size_t)T8 * (Kmax / 32));
+    e.xb.xfrag = (uint2*)e.dalloc(qb_xfrag_bytes(Kmax));
+    e.xb.xscale = A((size_t)T8 * (Kmax / 256));
+    e.xb.xsum = A((size_t)T8 * (Kmax / 32));
+    e.xb.xq = (uint2*)e.dalloc(qb_xq_bytes(Kmax));
+    e.xb.xqscale = A((size_t)T8 * (Kmax / 256));
     e.keys = (unsigned long long*)e.dalloc(2 * T8 * sizeof(unsigned long long));
     e.ctrl = (QbCtrl*)e.dalloc(sizeof(QbCtrl));
-    if (!e.bx || !e.logits || !e.xfrag || !e.ctrl || !e.emb || !e.keys) { set_err(-2, "activation alloc"); return -1; }
-    CK(cudaMemset(e.xfrag, 0, xf_bytes));
-    CK(cudaMemset(e.xscale, 0, (size_t)T8 * (Kmax / 256) * 4));
-    CK(cudaMemset(e.xsum, 0, (size_t)T8 * (Kmax / 32) * 4));
+    if (!e.bx || !e.logits || !e.xb.xfrag || !e.xb.xq || !e.ctrl || !e.emb || !e.keys) {
+        set_err(-2, "activation alloc");
+        return -1;
+    }
+    CK(cudaMemset(e.xb.xfrag, 0, qb_xfrag_bytes(Kmax)));
+    CK(cudaMemset(e.xb.xscale, 0, (size_t)T8 * (Kmax / 256) * 4));
+    CK(cudaMemset(e.xb.xsum, 0, (size_t)T8 * (Kmax / 32) * 4));
+    CK(cudaMemset(e.xb.xq, 0, qb_xq_bytes(Kmax)));
+    CK(cudaMemset(e.xb.xqscale, 0, (size_t)T8 * (Kmax / 256) * 4));
     CK(cudaMemset(e.ctrl, 0, sizeof(QbCtrl)));
     CK(cudaMemset(e.mtp_h, 0, (size_t)e.E * 4));
     {   // GEMV scratch: arrival counters for the largest launch (head or fused FFN / mixer)
@@ -604,27 +608,34 @@ int gemv_group(Engine& e, const DevMat* const* mats, float* const* outs, const l
         if (type == QB_F32) {
             for (int s = 0; s < ns; ++s) CK(cudaErrorNotSupported);
         } else {
-            CK(qb_qmv(type, segs, ns, K, N, e.xfrag, e.xscale, e.xsum, accumulate, 0, 1 << 30, e.work, e.st));
+            CK(qb_qmv(type, segs, ns, K, N, e.xb, accumulate, 0, 1 << 30, e.work, e.st));
         }
     }
     return 0;
 }
 
-int xprep1(Engine& e, const float* x, long long ldx, const float* norm_w, int len, int N) {
+// the qb_xprep outputs that the matrices consuming an input read
+int xp_needs(std::initializer_list<const DevMat*> ms) {
+    int w = 0;
+    for (const DevMat* m : ms) w |= qb_xprep_needs(m->type);
+    return w;
+}
+
+int xprep1(Engine& e, const float* x, long long ldx, const float* norm_w, int len, int N, int what) {
     QbXIn in{x, ldx, norm_w, len};
-    CK(qb_xprep(&in, 1, N, e.eps, e.xfrag, e.xscale, e.xsum, e.any_q45 ? 1 : 0, e.st));
+    CK(qb_xprep(&in, 1, N, e.eps, e.xb, what, e.st));
     return 0;
 }
 
 // SwiGLU FFN on residual x (src/model.c:819-842)
 int ffn_block(Engine& e, const LayerW& l, float* x, int B) {
-    if (xprep1(e, x, e.E, l.post_norm, e.E, B)) return -1;
+    if (xprep1(e, x, e.E, l.post_norm, e.E, B, xp_needs({&l.ffn_gate, &l.ffn_up}))) return -1;
     const DevMat* m2[2] = {&l.ffn_gate, &l.ffn_up};
     float* o2[2] = {e.gate, e.up};
     const long long ld2[2] = {e.F, e.F};
     if (gemv_group(e, m2, o2, ld2, 2, e.E, B, 0)) return -1;
     CK(qb_silu_mul(e.gate, e.up, e.F, e.F, B, e.act, e.st));
-    if (xprep1(e, e.act, e.F, nullptr, e.F, B)) return -1;
+    if (xprep1(e, e.act, e.F, nullptr, e.F, B, xp_needs({&l.ffn_down}))) return -1;
     const DevMat* m1[1] = {&l.ffn_down};
     float* o1[1] = {x};
     const long long ld1[1] = {e.E};
@@ -635,7 +646,7 @@ int ffn_block(Engine& e, const LayerW& l, float* x, int B) {
 int attn_block(Engine& e, const LayerW& l, float* x, int B, const uint32_t* pos, float* kc, float* vc) {
     const qwen_dims_t& d = e.d;
     const int qw = 2 * d.n_head * d.head_dim, kvw = d.n_kv_head * d.head_dim;
-    if (xprep1(e, x, e.E, l.attn_norm, e.E, B)) return -1;
+    if (xprep1(e, x, e.E, l.attn_norm, e.E, B, xp_needs({&l.q, &l.k, &l.v}))) return -1;
     const DevMat* m3[3] = {&l.q, &l.k, &l.v};
     float* o3[3] = {e.qbuf, e.kvbuf, e.kvbuf + kvw};
     const long long ld3[3] = {qw, 2 * kvw, 2 * kvw};
@@ -645,7 +656,7 @@ int attn_block(Engine& e, const LayerW& l, float* x, int B, const uint32_t* pos,
     CK(qb_attn_decode(e.qbuf, qw, kc, vc, d.n_head, d.n_kv_head, d.head_dim, pos, B, e.n_ctx, e.attn_o,
                       d.n_head * d.head_dim, e.st));
     const int ow = d.n_head * d.head_dim;
-    if (xprep1(e, e.attn_o, ow, nullptr, ow, B)) return -1;
+    if (xprep1(e, e.attn_o, ow, nullptr, ow, B, xp_needs({&l.o}))) return -1;
     const DevMat* m1[1] = {&l.o};
     float* o1[1] = {x};
     const long long ld1[1] = {e.E};
@@ -655,7 +666,7 @@ int attn_block(Engine& e, const LayerW& l, float* x, int B, const uint32_t* pos,
 
 int gdn_block(Engine& e, const LayerW& l, int B, int ckpt) {
     const qwen_dims_t& d = e.d;
-    if (xprep1(e, e.bx, e.E, l.attn_norm, e.E, B)) return -1;
+    if (xprep1(e, e.bx, e.E, l.attn_norm, e.E, B, xp_needs({&l.wqkv, &l.wgate, &l.wbeta, &l.walpha}))) return -1;
     const DevMat* m4[4] = {&l.wqkv, &l.wgate, &l.wbeta, &l.walpha};
     float* o4[4] = {e.qkv, e.z, e.beta, e.alpha};
     const long long ld4[4] = {e.ld_qkv, d.d_inner, 256, 256};
@@ -668,7 +679,7 @@ int gdn_block(Engine& e, const LayerW& l, int B, int ckpt) {
                     d.head_k_dim, B, e.eps, ssm, e.ssm_slot_stride, &e.ctrl->cur_slot, ckpt, e.o, d.d_inner,
                     e.st));
     CK(qb_gdn_out(e.o, e.z, d.d_inner, l.ssm_norm, d.n_v_heads, d.head_v_dim, B, e.eps, e.y, e.st));
-    if (xprep1(e, e.y, d.d_inner, nullptr, d.d_inner, B)) return -1;
+    if (xprep1(e, e.y, d.d_inner, nullptr, d.d_inner, B, xp_needs({&l.ssm_out}))) return -1;
     const DevMat* m1[1] = {&l.ssm_out};
     float* o1[1] = {e.bx};
     const long long ld1[1] = {e.E};
@@ -692,7 +703,7 @@ int fwd_backbone(Engine& e, int B, int ckpt) {
         }
     }
     CK(cudaMemcpyAsync(e.h_save, e.bx, (size_t)B * e.E * 4, cudaMemcpyDeviceToDevice, e.st));
-    if (xprep1(e, e.bx, e.E, e.out_norm, e.E, B)) return -1;
+    if (xprep1(e, e.bx, e.E, e.out_norm, e.E, B, xp_needs({&e.output}))) return -1;
     const DevMat* m1[1] = {&e.output};
     float* o1[1] = {e.logits};
     const long long ld1[1] = {e.V};
@@ -711,7 +722,7 @@ int fwd_backbone(Engine& e, int B, int ckpt) {
 int fwd_mtp(Engine& e, int B, const float* hsrc, int want_logits) {
     CK(qb_embed(e.embd_type, e.tok_embd, e.E, e.ctrl->mtp_tok, B, e.emb, e.E, e.st));
     QbXIn in[2] = {{e.emb, e.E, e.enorm, e.E}, {hsrc, e.E, e.hnorm, e.E}};
-    CK(qb_xprep(in, 2, B, e.eps, e.xfrag, e.xscale, e.xsum, e.any_q45 ? 1 : 0, e.st));
+    CK(qb_xprep(in, 2, B, e.eps, e.xb, xp_needs({&e.eh_proj}), e.st));
     const DevMat* m1[1] = {&e.eh_proj};
     float* o1[1] = {e.mtp_x};
     const long long ld1[1] = {e.E};
@@ -719,7 +730,7 @@ int fwd_mtp(Engine& e, int B, const float* hsrc, int want_logits) {
     if (attn_block(e, e.mtp, e.mtp_x, B, &e.ctrl->mtp_pos, e.mtp_k, e.mtp_v)) return -1;
     CK(cudaMemcpyAsync(e.mtp_h, e.mtp_x + (size_t)(B - 1) * e.E, (size_t)e.E * 4, cudaMemcpyDeviceToDevice, e.st));
     if (want_logits) {
-        if (xprep1(e, e.mtp_x, e.E, e.shnorm, e.E, B)) return -1;
+        if (xprep1(e, e.mtp_x, e.E, e.shnorm, e.E, B, xp_needs({&e.output}))) return -1;
         const DevMat* mo[1] = {&e.output};
         float* oo[1] = {e.mtp_logits};
         const long long ldo[1] = {e.V};
@@ -1255,12 +1266,10 @@ extern "C" float qb_bench(qwen_model_t* m, int what, uint32_t arg, uint32_t iter
                         const LayerW& l = en.L[li];
                         QbQSeg segs[2] = {{l.ffn_gate.w, en.gate, en.F, l.ffn_gate.rows},
                                           {l.ffn_up.w, en.up, en.F, l.ffn_up.rows}};
-                        CK(qb_qmv(l.ffn_gate.type, segs, 2, en.E, a, en.xfrag, en.xscale, en.xsum, 0, 0, 1 << 30,
-                                  en.work, en.st));
+                        CK(qb_qmv(l.ffn_gate.type, segs, 2, en.E, a, en.xb, 0, 0, 1 << 30, en.work, en.st));
                     } else {
                         QbQSeg seg = {en.output.w, en.logits, en.V, en.output.rows};
-                        CK(qb_qmv(en.output.type, &seg, 1, en.E, a, en.xfrag, en.xscale, en.xsum, 0, 0, 1 << 30,
-                                  en.work, en.st));
+                        CK(qb_qmv(en.output.type, &seg, 1, en.E, a, en.xb, 0, 0, 1 << 30, en.work, en.st));
                     }
                 }
                 return 0;
@@ -1346,12 +1355,10 @@ struct Scratch {
     cudaStream_t st = nullptr;
     float *x = nullptr, *out = nullptr;
     size_t x_cap = 0, out_cap = 0;
-    uint2* xfrag = nullptr;
-    float *xscale = nullptr, *xsum = nullptr;
+    QbXBuf xb{};
     size_t k_cap = 0;
     unsigned long long* keys = nullptr;
     uint32_t* am = nullptr;
-    bool consts = false;
     QbQmvWork work{};
 };
 std::mutex g_mu;
@@ -1363,10 +1370,6 @@ int scratch_get(Scratch*& s, size_t x_floats, size_t out_floats, int K) {
     CK(cudaGetDevice(&dev));
     s = &g_scratch[dev];
     if (!s->st) CK(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
-    if (!s->consts) {
-        CK(qb_quant_init_constants());   // IQ4 table in this device's constant bank
-        s->consts = true;
-    }
     if (x_floats > s->x_cap) {
         if (s->x) cudaFree(s->x);
         s->x_cap = std::max<size_t>(x_floats, 1 << 16);
@@ -1378,15 +1381,20 @@ int scratch_get(Scratch*& s, size_t x_floats, size_t out_floats, int K) {
         CK(cudaMalloc(&s->out, s->out_cap * 4));
     }
     if ((size_t)K > s->k_cap) {
-        if (s->xfrag) cudaFree(s->xfrag);
-        if (s->xscale) cudaFree(s->xscale);
-        if (s->xsum) cudaFree(s->xsum);
+        if (s->xb.xfrag) cudaFree(s->xb.xfrag);
+        if (s->xb.xscale) cudaFree(s->xb.xscale);
+        if (s->xb.xsum) cudaFree(s->xb.xsum);
+        if (s->xb.xq) cudaFree(s->xb.xq);
+        if (s->xb.xqscale) cudaFree(s->xb.xqscale);
         s->k_cap = std::max<size_t>((size_t)K, 4096);
-        const size_t kc = (s->k_cap + 255) / 256 * 256;
-        CK(cudaMalloc(&s->xfrag, kc / 32 * 2 * 2 * 32 * 8));
-        CK(cudaMemset(s->xfrag, 0, kc / 32 * 2 * 2 * 32 * 8));
-        CK(cudaMalloc(&s->xscale, QB_MAX_TOK * (kc / 256) * 4));
-        CK(cudaMalloc(&s->xsum, QB_MAX_TOK * (kc / 32) * 4));
+        const int kc = (int)((s->k_cap + 255) / 256 * 256);
+        CK(cudaMalloc(&s->xb.xfrag, qb_xfrag_bytes(kc)));
+        CK(cudaMemset(s->xb.xfrag, 0, qb_xfrag_bytes(kc)));
+        CK(cudaMalloc(&s->xb.xq, qb_xq_bytes(kc)));
+        CK(cudaMemset(s->xb.xq, 0, qb_xq_bytes(kc)));
+        CK(cudaMalloc(&s->xb.xscale, QB_MAX_TOK * (kc / 256) * 4));
+        CK(cudaMalloc(&s->xb.xqscale, QB_MAX_TOK * (kc / 256) * 4));
+        CK(cudaMalloc(&s->xb.xsum, QB_MAX_TOK * (kc / 32) * 4));
     }
     if (!s->keys) {
         CK(cudaMalloc(&s->keys, QB_MAX_TOK * sizeof(unsigned long long)));
@@ -1454,13 +1462,13 @@ int gemv_host(const gguf_tensor_info_t* W, const float* x, uint64_t ldx, int n, 
         } else {
             if (scratch_work(s, M->rows)) return -1;
             QbXIn in{s->x, K, nullptr, K};
-            CK(qb_xprep(&in, 1, nn, 1e-6f, s->xfrag, s->xscale, s->xsum, (M->type == QB_Q4_K || M->type == QB_Q5_K) ? 1 : 0, s->st));
+            CK(qb_xprep(&in, 1, nn, 1e-6f, s->xb, qb_xprep_needs(M->type), s->st));
             QbQSeg seg;
             seg.w = (const uint8_t*)M->w + (size_t)t_lo * (K / qb_unit_cols(M->type)) * qb_unit_bytes(M->type);
             seg.out = s->out + (size_t)t_lo * QB_TILE;
             seg.ldo = M->rows;
             seg.rows = (int)(r1 - (uint64_t)t_lo * QB_TILE);
-            CK(qb_qmv(M->type, &seg, 1, K, nn, s->xfrag, s->xscale, s->xsum, 0, (int)(r0 - (uint64_t)t_lo * QB_TILE),
+            CK(qb_qmv(M->type, &seg, 1, K, nn, s->xb, 0, (int)(r0 - (uint64_t)t_lo * QB_TILE),
                       (int)(r1 - (uint64_t)t_lo * QB_TILE), s->work, s->st));
         }
         CK(cudaMemcpy2DAsync(out + (size_t)t0 * ldo + r0, ldo * 4, s->out + r0, (size_t)M->rows * 4, (size_t)(r1 - r0) * 4, nn,

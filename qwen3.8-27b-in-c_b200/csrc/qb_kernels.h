@@ -28,15 +28,27 @@ struct QbQmvWork {
     int max_pairs;
 };
 
+// Prepared activations of one GEMV input (written by qb_xprep, read by qb_qmv).
+struct QbXBuf {
+    uint2* xfrag;            // fp16 hi/lo mma B fragments (all formats but IQ4_XS), qb_xbuf_bytes
+    float* xscale;           // [QB_MAX_TOK][K/256] power-of-two scale of xfrag
+    float* xsum;             // [QB_MAX_TOK][K/32] plain column sums (Q4_K / Q5_K)
+    uint2* xq;               // int8 digit mma B fragments (IQ4_XS), qb_xbuf_bytes
+    float* xqscale;          // [QB_MAX_TOK][K/256] power-of-two scale of xq
+};
+enum { QB_XP_F16 = 1, QB_XP_SUM = 2, QB_XP_I8 = 4 };   // qb_xprep outputs
+
 // ---- quantised GEMV (qb_quant.cu) ----
-cudaError_t qb_quant_init_constants();
 size_t qb_repacked_bytes(int type, int rows, int K);
 cudaError_t qb_repack(int type, const void* src_dev, int rows, int K, void* dst_dev, cudaStream_t st);
-cudaError_t qb_xprep(const QbXIn* in, int nseg, int N, float eps, uint2* xfrag, float* xscale, float* xsum,
-                     int want_xsum, cudaStream_t st);
-cudaError_t qb_qmv(int type, const QbQSeg* segs, int nseg, int K, int N, const uint2* xfrag,
-                   const float* xscale, const float* xsum, int accumulate, int row_lo, int row_hi,
-                   const QbQmvWork& work, cudaStream_t st);
+// bytes of xfrag / xq for inputs of up to K columns
+size_t qb_xfrag_bytes(int K);
+size_t qb_xq_bytes(int K);
+// which qb_xprep outputs a matrix of this type reads
+int qb_xprep_needs(int type);
+cudaError_t qb_xprep(const QbXIn* in, int nseg, int N, float eps, const QbXBuf& xb, int what, cudaStream_t st);
+cudaError_t qb_qmv(int type, const QbQSeg* segs, int nseg, int K, int N, const QbXBuf& xb, int accumulate,
+                   int row_lo, int row_hi, const QbQmvWork& work, cudaStream_t st);
 cudaError_t qb_qmv_work_alloc(QbQmvWork& w, int max_pairs);
 void qb_qmv_work_free(QbQmvWork& w);
 cudaError_t qb_qmv_f32(const float* W, int rows, int K, const float* x, long long ldx, int N, float* out,

@@ -7,15 +7,20 @@
 // src/quant.c:86-182.
 //
 // Data path.  Weights are repacked once at load time from GGUF super-blocks
-// into 16-row tiles whose bytes land directly in mma.sync m16n8k16 A-fragment
-// order (the byte count of every format is unchanged).  Inside the kernel
-// each 4/6/8-bit code is expanded to an *exact* fp16 integer (IQ4 lookup
-// table via byte permutes, K-quant codes via the 1024+q exponent trick), so
-// the tensor core multiplies exact weight codes with the activations.  The
-// activations are split into fp16 hi + lo halves after a power-of-two scale
-// per 256-column block (~22 significant bits): the products are exact in
-// the fp32 accumulator and results carry fp32-level error.  Per-32 / per-16
-// block scales are applied to the fp32 partial sums of each sub-block.
+// into 16-row tiles whose bytes land directly in mma.sync A-fragment order
+// (the byte count of every format is unchanged).  Two tensor-core paths:
+//  * IQ4_XS (93 % of the model's bytes): int8 mma m16n8k32.  Each code is
+//    looked up as its int8 table value by byte permutes; the activations are
+//    three balanced int8 digits per element after a power-of-two scale per
+//    256-column block (~23 significant bits), so every sub-block dot product
+//    is an exact int32, and the 6-bit sub-block scales are applied in int32 by
+//    summation by parts along the mma accumulator chain.
+//  * Q4_K / Q5_K / Q6_K / Q8_0: fp16 mma m16n8k16.  Each code becomes an
+//    *exact* fp16 integer (the 1024+q exponent trick); the activations are
+//    split into fp16 hi + lo halves after a power-of-two scale per block (~22
+//    significant bits), the products are exact in the fp32 accumulator, and
+//    per-32 / per-16 block scales are applied to each sub-block's fp32 sums.
+// Either way results carry fp32-level error.
 //
 // Pipeline.  Two persistent CTAs of 8 warps per SM.  Every warp streams its
 // own (pair of tiles x 256 columns) stages of contiguous repacked bytes into
@@ -53,27 +58,6 @@ constexpr int kCtasPerSm = QB_QMV_CTAS;
 #endif
 constexpr int kSmemBudget = QB_QMV_SMEM_KB * 1024;   // per CTA
 constexpr int kRingOff = 512;                // full barriers (8 warps x 8 slots x 8 B), then the rings
-
-// IQ4_NL table biased by +128 (reference src/quant.c:30-32: kvalues_iq4nl).
-__constant__ uint32_t c_iq4_lut[4];
-
-// Expand 8 IQ4 nibbles (word = qs bytes 4c..4c+3 of a sub-block: byte j holds
-// element j (low nibble) and j+16 (high)) into the four fp16x2 operands:
-// o[0] elems (4c, 4c+1) step 0, o[1] (4c+2, 4c+3) step 0, o[2]/o[3] step 1.
-__device__ __forceinline__ void iq4_expand(uint32_t w, uint32_t T0, uint32_t T1, uint32_t T2, uint32_t T3,
-                                           uint32_t (&o)[4]) {
-    const uint32_t lo3 = w & 0x77777777u;
-    const uint32_t sel = ((w >> 1) & 0x44444444u) | 0x32103210u;
-    const uint32_t lo3h = lo3 >> 16;
-    const uint32_t a = prmt(T0, T1, lo3), b = prmt(T2, T3, lo3);
-    const uint32_t r_lo = prmt(a, b, sel);                 // [b0lo b0hi b1lo b1hi]
-    const uint32_t ah = prmt(T0, T1, lo3h), bh = prmt(T2, T3, lo3h);
-    const uint32_t r_hi = prmt(ah, bh, sel >> 16);         // [b2lo b2hi b3lo b3hi]
-    o[0] = hsub2_u32(prmt(r_lo, C64, 0x5240u), H1152x2);
-    o[1] = hsub2_u32(prmt(r_hi, C64, 0x5240u), H1152x2);
-    o[2] = hsub2_u32(prmt(r_lo, C64, 0x5341u), H1152x2);
-    o[3] = hsub2_u32(prmt(r_hi, C64, 0x5341u), H1152x2);
-}
 
 // 4 unsigned bytes -> two half2 (1024 + b0, 1024 + b1), (1024 + b2, 1024 + b3)
 __device__ __forceinline__ void bytes_to_h2(uint32_t u, uint32_t& h01, uint32_t& h23) {
@@ -141,59 +125,117 @@ __device__ __forceinline__ float iq4_dl(uint32_t L0, uint32_t L1, float d, int s
     return (f - 8388640.0f) * d;                                                // (ls - 32) * d
 }
 
-template <int NT>
-__device__ __forceinline__ void stage_iq4xs(const uint8_t* u, const uint2* __restrict__ xf, int lane,
-                                            float (&ab)[2][NT][4], float (&)[2][NT][4]) {
+// ---- IQ4_XS on the int8 tensor-core path (mma m16n8k32 s8 -> s32) ----
+// Codes become the int8 values of kvalues_iq4nl (src/quant.c:30-32) by two
+// 8-byte permute lookups and a select; the activations arrive as three
+// balanced int8 digits per token (X = 65536 d0 + 256 d1 + d2, xprep), so
+// every sub-block dot product is exact in int32.  The same repacked tile
+// layout as above serves both paths: the word of (row, sub-block) holds qs
+// bytes 4c..4c+3, i.e. elements 4c..4c+3 (low nibbles) and 16+4c..16+4c+3
+// (high nibbles), which is exactly the k-range of mma registers a0/a2 of
+// thread c; the k order inside a register is (4c, 4c+16, 4c+1, 4c+17) and
+// (4c+2, 4c+18, 4c+3, 4c+19), matched by the digit fragments.
+//
+// Columns of the n8 tiles: tile 0 = (token c: d0, d1), tile 1 = (token c: d2,
+// token c+4: d2), tile 2 = (token c+4: d0, d1); NTI = 2 serves N <= 4.
+//
+// Sub-block scales by summation by parts: the mma chains its accumulator, so
+// after sub-block j it holds R_j = sum_{i<=j} C_i, and
+// sum_j s_j C_j = sum_{j<7} (s_j - s_{j+1}) R_j + s_7 R_7 with s_j = ls_j - 32.
+constexpr uint32_t kIq4I8T0 = 0xBFAD9881u;   // -127 -104  -83  -65
+constexpr uint32_t kIq4I8T1 = 0xF6EADDCFu;   //  -49  -35  -22  -10
+constexpr uint32_t kIq4I8T2 = 0x26190D01u;   //    1   13   25   38
+constexpr uint32_t kIq4I8T3 = 0x71594535u;   //   53   69   89  113
+
+__device__ __forceinline__ void iq4_i8(uint32_t w, uint32_t& lo, uint32_t& hi) {
+    const uint32_t idx = w & 0x77777777u;                         // table index, code bit 3 cleared
+    const uint32_t sel = ((w >> 1) & 0x44444444u) | 0x32103210u;  // code bit 3 picks the upper table
+    const uint32_t idxh = idx >> 16, selh = sel >> 16;
+    lo = prmt(prmt(kIq4I8T0, kIq4I8T1, idx), prmt(kIq4I8T2, kIq4I8T3, idx), sel);
+    hi = prmt(prmt(kIq4I8T0, kIq4I8T1, idxh), prmt(kIq4I8T2, kIq4I8T3, idxh), selh);
+}
+
+// byte i of w, sign-extended
+__device__ __forceinline__ int sbyte(uint32_t w, int i) {
+    return (int)prmt(w, 0u, (uint32_t)(i | ((8 | i) << 4) | ((8 | i) << 8) | ((8 | i) << 12)));
+}
+
+// B fragments of sub-block sb of a block
+template <int NTI>
+__device__ __forceinline__ void load_bq(uint2 (&b)[NTI], const uint2* __restrict__ xq, int sb, int lane) {
+#pragma unroll
+    for (int nt = 0; nt < NTI; ++nt) b[nt] = __ldg(xq + (sb * NTI + nt) * 32 + lane);
+}
+
+// v[t][r][k]: d * (sum over the super-block) for tile t, row g + 8r, token c + 4k.
+// bb holds the B fragments of sub-blocks 0 and 1 on entry; loads run two
+// sub-blocks ahead, so on return bb holds sub-blocks 0 and 1 of xq_next.
+template <int NTI>
+__device__ __forceinline__ void stage_iq4_i8(const uint8_t* u, const uint2* __restrict__ xq,
+                                             const uint2* __restrict__ xq_next, int lane, uint2 (&bb)[2][NTI],
+                                             float (&v)[2][2][2]) {
     const int g = lane >> 2;
-    uint32_t L[2][2][2];
+    uint32_t dl[2][2][2];   // signed bytes: ls_j - ls_{j+1} (j < 7), ls_7 - 32
     float d[2][2];
 #pragma unroll
     for (int t = 0; t < 2; ++t)
 #pragma unroll
-        for (int r = 0; r < 2; ++r) iq4_scales(u + t * kIq4Tile, g + 8 * r, L[t][r][0], L[t][r][1], d[t][r]);
-    const uint32_t T0 = c_iq4_lut[0], T1 = c_iq4_lut[1], T2 = c_iq4_lut[2], T3 = c_iq4_lut[3];
-    // activation fragments of the chunk's 4 k16 steps, issued together ahead of the decode
-    uint2 bn[4][NT];
+        for (int r = 0; r < 2; ++r) {
+            uint32_t L0, L1;
+            iq4_scales(u + t * kIq4Tile, g + 8 * r, L0, L1, d[t][r]);
+            const uint32_t n0 = prmt(L0, L1, 0x4321u), n1 = prmt(L1, 0x20202020u, 0x4321u);
+            dl[t][r][0] = (L0 + 0x80808080u - n0) ^ 0x80808080u;   // bytes stay in [65, 191]: no borrows
+            dl[t][r][1] = (L1 + 0x80808080u - n1) ^ 0x80808080u;
+        }
+    int R[2][NTI][4], acc[2][NTI][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) load_b<NT>(bn[i], xf + i * NT * 32, lane);
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int nt = 0; nt < NTI; ++nt)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) R[t][nt][i] = acc[t][nt][i] = 0;
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
-        uint2 bc[4][NT];
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-            for (int ct = 0; ct < NT; ++ct) bc[i][ct] = bn[i][ct];
-        if (p < 3) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) load_b<NT>(bn[i], xf + ((p + 1) * 4 + i) * NT * 32, lane);
-        }
         const uint4 q0 = lds128(u + p * 512 + lane * 16);
         const uint4 q1 = lds128(u + kIq4Tile + p * 512 + lane * 16);
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
             const int sb = 2 * p + h;
-            uint32_t e[2][2][4];
-            iq4_expand(h ? q0.z : q0.x, T0, T1, T2, T3, e[0][0]);
-            iq4_expand(h ? q0.w : q0.y, T0, T1, T2, T3, e[0][1]);
-            iq4_expand(h ? q1.z : q1.x, T0, T1, T2, T3, e[1][0]);
-            iq4_expand(h ? q1.w : q1.y, T0, T1, T2, T3, e[1][1]);
-            float cs[2][NT][4];
-            zero<NT>(cs[0]);
-            zero<NT>(cs[1]);
+            uint2 bq[NTI];
 #pragma unroll
-            for (int s = 0; s < 2; ++s) {
+            for (int nt = 0; nt < NTI; ++nt) bq[nt] = bb[h][nt];
+            if (sb < 6) load_bq<NTI>(bb[h], xq, sb + 2, lane);
+            else load_bq<NTI>(bb[h], xq_next, sb - 6, lane);
 #pragma unroll
-                for (int t = 0; t < 2; ++t) {
-                    const uint32_t a[4] = {e[t][0][2 * s], e[t][1][2 * s], e[t][0][2 * s + 1], e[t][1][2 * s + 1]};
-                    mma_nt<NT>(cs[t], a, bc[2 * h + s]);
-                }
+            for (int t = 0; t < 2; ++t) {
+                const uint4& q = t ? q1 : q0;
+                uint32_t a[4];
+                iq4_i8(h ? q.z : q.x, a[0], a[2]);   // row g
+                iq4_i8(h ? q.w : q.y, a[1], a[3]);   // row g + 8
+#pragma unroll
+                for (int nt = 0; nt < NTI; ++nt) mma_16832_s8(R[t][nt], a, bq[nt].x, bq[nt].y);
+                const int s_g = sbyte(dl[t][0][sb >> 2], sb & 3), s_g8 = sbyte(dl[t][1][sb >> 2], sb & 3);
+#pragma unroll
+                for (int nt = 0; nt < NTI; ++nt)
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        if (NTI == 2 && nt == 1 && (i & 1)) continue;   // unused column
+                        acc[t][nt][i] += ((i & 2) ? s_g8 : s_g) * R[t][nt][i];
+                    }
             }
-#pragma unroll
-            for (int t = 0; t < 2; ++t)
-                scale_acc<NT>(ab[t], cs[t], iq4_dl(L[t][0][0], L[t][0][1], d[t][0], sb),
-                              iq4_dl(L[t][1][0], L[t][1][1], d[t][1], sb));
         }
     }
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            v[t][r][0] = fmaf((float)acc[t][0][2 * r], 65536.f, fmaf((float)acc[t][0][2 * r + 1], 256.f,
+                                                                     (float)acc[t][1][2 * r])) * d[t][r];
+            v[t][r][1] = NTI == 3 ? fmaf((float)acc[t][NTI - 1][2 * r], 65536.f,
+                                         fmaf((float)acc[t][NTI - 1][2 * r + 1], 256.f,
+                                              (float)acc[t][1][2 * r + 1])) * d[t][r]
+                                  : 0.f;
+        }
 }
 
 // Q8_0: tile-block = 8 units of 544 B (32 columns: 16 rows x 32 qs in lane
@@ -407,6 +449,8 @@ struct QmvK {
     const uint2* xfrag;
     const float* xscale;
     const float* xsum;
+    const uint2* xq;             // int8 digit fragments (IQ4_XS int8 path)
+    const float* xqscale;
     int accumulate;
     int row_lo, row_hi;
     float* partial;              // [Wt][2][32][8]
@@ -421,9 +465,10 @@ __device__ __forceinline__ int stage_owner(int S, int Wt, int s) {
     return (int)((unsigned)((s + 1) * Wt - 1) / (unsigned)S);
 }
 
-template <int NT>
-__device__ __forceinline__ void finish_pair(const QmvK& p, int pair, int gw, int s0, int s1, float (&acc)[2][NT][4],
-                                            int lane) {
+// o[t][i], i = (row g tok 2c, row g tok 2c+1, row g8 tok 2c, row g8 tok 2c+1) of
+// tile t; lanes with active == false hold nothing to store.
+__device__ __forceinline__ void finish_pair(const QmvK& p, int pair, int gw, int s0, int s1, const float (&o)[2][4],
+                                            bool active, int lane) {
     int si = 0;
 #pragma unroll
     for (int s = 1; s < QB_MAX_SEG; ++s)
@@ -431,15 +476,6 @@ __device__ __forceinline__ void finish_pair(const QmvK& p, int pair, int gw, int
     const QSeg& S = p.seg[si];
     const int lp = pair - p.pair0[si];
     const int g = lane >> 2, c = lane & 3;
-    // combine hi/lo columns: o[t][i], i = (row g tok t0, row g tok t1, row g8 tok t0, row g8 tok t1)
-    float o[2][4];
-#pragma unroll
-    for (int t = 0; t < 2; ++t)
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-            o[t][i] = NT == 1 ? acc[t][0][i] + __shfl_xor_sync(0xffffffffu, acc[t][0][i], 2)
-                              : acc[t][0][i] + acc[t][NT - 1][i];
-    const bool active = NT == 1 ? (c < 2) : true;
     const int t0 = 2 * c, t1 = 2 * c + 1;
     const int P0 = pair * p.nb, P1 = P0 + p.nb;
     auto store = [&](int t, int i, float v) {
@@ -495,7 +531,44 @@ __device__ __forceinline__ void finish_pair(const QmvK& p, int pair, int gw, int
     if (lane == 0) p.counters[pair] = 0u;   // ready for the next launch
 }
 
-template <int FMT, int NT>
+// fp16 path: combine the hi/lo columns of the mma accumulators
+template <int NT>
+__device__ __forceinline__ void pair_out_f16(const float (&acc)[2][NT][4], float (&o)[2][4], bool& active, int lane) {
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            o[t][i] = NT == 1 ? acc[t][0][i] + __shfl_xor_sync(0xffffffffu, acc[t][0][i], 2)
+                              : acc[t][0][i] + acc[t][NT - 1][i];
+    active = NT == 1 ? ((lane & 3) < 2) : true;
+}
+
+// int8 path: lane (g, c) holds tok[t][r][k] = (tile t, row g + 8r, token c + 4k);
+// regroup to tokens (2c, 2c+1) per lane
+template <int NT>
+__device__ __forceinline__ void pair_out_i8(const float (&tok)[2][2][2], float (&o)[2][4], bool& active, int lane) {
+    const int c = lane & 3, base = lane & ~3;
+    const int src0 = base + ((2 * c) & 3), src1 = base + ((2 * c + 1) & 3);
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const float a0 = __shfl_sync(0xffffffffu, tok[t][r][0], src0);
+            const float a1 = __shfl_sync(0xffffffffu, tok[t][r][0], src1);
+            if (NT == 1) {
+                o[t][2 * r] = a0;
+                o[t][2 * r + 1] = a1;
+            } else {
+                const float b0 = __shfl_sync(0xffffffffu, tok[t][r][1], src0);
+                const float b1 = __shfl_sync(0xffffffffu, tok[t][r][1], src1);
+                o[t][2 * r] = (c >> 1) ? b0 : a0;
+                o[t][2 * r + 1] = (c >> 1) ? b1 : a1;
+            }
+        }
+    active = NT == 1 ? (c < 2) : true;
+}
+
+template <int FMT, int NT, bool I8>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_kernel(QmvK p) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int TB = tile_block_bytes(FMT);
@@ -515,19 +588,32 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_kernel(QmvK p) {
     if (gw >= p.Wt) return;
     const int s0 = warp_s0(p.S, p.Wt, gw), s1 = warp_s0(p.S, p.Wt, gw + 1);
     const int n = s1 - s0;
-    // producer cursor (lane 0): tile pair / block / segment of the next stage to fetch
-    int ip = s0 / p.nb, ib = s0 - ip * p.nb, iseg = 0;
-    while (iseg + 1 < p.nseg && ip >= p.pair0[iseg + 1]) ++iseg;
+    // producer cursor (lane 0): source of the next stage, its block, pairs left in the segment
+    int ib, iseg = 0, seg_pairs_left;
+    const uint8_t* src;
+    {
+        const int ip = s0 / p.nb;
+        ib = s0 - ip * p.nb;
+        while (iseg + 1 < p.nseg && ip >= p.pair0[iseg + 1]) ++iseg;
+        src = p.seg[iseg].w + ((size_t)(ip - p.pair0[iseg]) * 2 * p.nb + ib) * TB;
+        seg_pairs_left = p.pair0[iseg + 1] - ip;
+    }
+    const size_t tile_bytes = (size_t)p.nb * TB;   // the units of one tile
+    const uint32_t ring_s = smem_u32(ring), full_s = smem_u32(full);
     auto issue = [&](int slot) {
-        const uint8_t* src = p.seg[iseg].w + ((size_t)(ip - p.pair0[iseg]) * 2 * p.nb + ib) * TB;
-        uint8_t* dst = ring + (size_t)slot * STAGE;
-        mbar_expect_tx(full + slot, STAGE);
-        bulk_g2s(dst, src, TB, full + slot);
-        bulk_g2s(dst + TB, src + (size_t)p.nb * TB, TB, full + slot);
+        const uint32_t dst = ring_s + (uint32_t)slot * STAGE, bar = full_s + (uint32_t)slot * 8u;
+        mbar_expect_tx_s(bar, STAGE);
+        bulk_g2s_s(dst, src, TB, bar);
+        bulk_g2s_s(dst + TB, src + tile_bytes, TB, bar);
+        src += TB;
         if (++ib == p.nb) {
             ib = 0;
-            ++ip;
-            while (iseg + 1 < p.nseg && ip >= p.pair0[iseg + 1]) ++iseg;
+            src += tile_bytes;   // past the pair's second tile
+            if (--seg_pairs_left == 0 && iseg + 1 < p.nseg) {
+                ++iseg;
+                src = p.seg[iseg].w;
+                seg_pairs_left = p.pair0[iseg + 1] - p.pair0[iseg];
+            }
         }
     };
     // weights do not depend on the previous kernel: start streaming before the wait
@@ -535,19 +621,38 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_kernel(QmvK p) {
         for (int r = 0; r < R && r < n; ++r) issue(r);
     pdl_wait();   // activations written by the previous kernel are complete from here on
 
-    float acc[2][NT][4];
-    zero<NT>(acc[0]);
-    zero<NT>(acc[1]);
+    float acc[2][NT][4];   // fp16 path: mma accumulator layout
+    float tk[2][2][2];     // int8 path: (tile, row g + 8r, token c + 4k)
+    auto reset = [&]() {
+        zero<NT>(acc[0]);
+        zero<NT>(acc[1]);
+#pragma unroll
+        for (int t = 0; t < 2; ++t) tk[t][0][0] = tk[t][0][1] = tk[t][1][0] = tk[t][1][1] = 0.f;
+    };
+    auto finish = [&](int pair) {
+        float o[2][4];
+        bool active;
+        if (I8) pair_out_i8<NT>(tk, o, active, lane);
+        else pair_out_f16<NT>(acc, o, active, lane);
+        finish_pair(p, pair, gw, s0, s1, o, active, lane);
+    };
+    reset();
     const int c = lane & 3;
     int cp = s0 / p.nb, cb = s0 - cp * p.nb;
+    // int8 path: B fragments of sub-blocks 0, 1 of the next stage (prefetched one stage ahead)
+    uint2 bpre[2][NT == 1 ? 2 : 3];
+    if constexpr (I8) {
+        constexpr int NTI = NT == 1 ? 2 : 3;
+        load_bq<NTI>(bpre[0], p.xq + (size_t)cb * 8 * NTI * 32, 0, lane);
+        load_bq<NTI>(bpre[1], p.xq + (size_t)cb * 8 * NTI * 32, 1, lane);
+    }
     int cur_pair = cp;
     int slot = 0;
     uint32_t phase = 0;
     for (int r = 0; r < n; ++r) {
         if (cp != cur_pair) {
-            finish_pair<NT>(p, cur_pair, gw, s0, s1, acc, lane);
-            zero<NT>(acc[0]);
-            zero<NT>(acc[1]);
+            finish(cur_pair);
+            reset();
             cur_pair = cp;
         }
         if (!mbar_wait(full + slot, phase)) {
@@ -565,40 +670,66 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_kernel(QmvK p) {
         }
         const int b = cb;
         const uint8_t* u = ring + (size_t)slot * STAGE;
-        const uint2* xf = p.xfrag + (size_t)b * 16 * NT * 32;
-        float ab[2][NT][4], mt[2][NT][4];
-        zero<NT>(ab[0]);
-        zero<NT>(ab[1]);
-        zero<NT>(mt[0]);
-        zero<NT>(mt[1]);
-        if (FMT == QB_IQ4_XS) stage_iq4xs<NT>(u, xf, lane, ab, mt);
-        else if (FMT == QB_Q8_0) stage_q8_0<NT>(u, xf, lane, ab, mt);
-        else if (FMT == QB_Q6_K) stage_q6k<NT>(u, xf, lane, ab, mt);
-        else if (FMT == QB_Q4_K) stage_qk<NT, false>(u, xf, p.xsum + b * 8, p.K >> 5, lane, ab, mt);
-        else if (FMT == QB_Q5_K) stage_qk<NT, true>(u, xf, p.xsum + b * 8, p.K >> 5, lane, ab, mt);
-        __syncwarp();   // every lane is done with the slot
-        if (lane == 0 && r + R < n) issue(slot);
-        if (++slot == R) {
-            slot = 0;
-            phase ^= 1u;
-        }
+        if constexpr (I8) {
+            constexpr int NTI = NT == 1 ? 2 : 3;
+            float xs[NT];
 #pragma unroll
-        for (int ct = 0; ct < NT; ++ct)
+            for (int k = 0; k < NT; ++k) {
+                const int tok = c + 4 * k;
+                xs[k] = tok < p.N ? __ldg(p.xqscale + tok * p.nb + b) : 0.f;
+            }
+            const int b_next = b + 1 == p.nb ? 0 : b + 1;
+            float v[2][2][2];
+            stage_iq4_i8<NTI>(u, p.xq + (size_t)b * 8 * NTI * 32, p.xq + (size_t)b_next * 8 * NTI * 32, lane,
+                              bpre, v);
+            __syncwarp();   // every lane is done with the slot
+            if (lane == 0 && r + R < n) issue(slot);
+            if (++slot == R) {
+                slot = 0;
+                phase ^= 1u;
+            }
 #pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                const float xs = __ldg(p.xscale + col_token<NT>(ct, 2 * c + i) * p.nb + b);
+            for (int k = 0; k < NT; ++k)
 #pragma unroll
                 for (int t = 0; t < 2; ++t) {
-                    acc[t][ct][i] = fmaf(xs, ab[t][ct][i], acc[t][ct][i]) + mt[t][ct][i];
-                    acc[t][ct][2 + i] = fmaf(xs, ab[t][ct][2 + i], acc[t][ct][2 + i]) + mt[t][ct][2 + i];
+                    tk[t][0][k] = fmaf(xs[k], v[t][0][k], tk[t][0][k]);
+                    tk[t][1][k] = fmaf(xs[k], v[t][1][k], tk[t][1][k]);
                 }
+        } else {
+            const uint2* xf = p.xfrag + (size_t)b * 16 * NT * 32;
+            float ab[2][NT][4], mt[2][NT][4];
+            zero<NT>(ab[0]);
+            zero<NT>(ab[1]);
+            zero<NT>(mt[0]);
+            zero<NT>(mt[1]);
+            if (FMT == QB_Q8_0) stage_q8_0<NT>(u, xf, lane, ab, mt);
+            else if (FMT == QB_Q6_K) stage_q6k<NT>(u, xf, lane, ab, mt);
+            else if (FMT == QB_Q4_K) stage_qk<NT, false>(u, xf, p.xsum + b * 8, p.K >> 5, lane, ab, mt);
+            else if (FMT == QB_Q5_K) stage_qk<NT, true>(u, xf, p.xsum + b * 8, p.K >> 5, lane, ab, mt);
+            __syncwarp();   // every lane is done with the slot
+            if (lane == 0 && r + R < n) issue(slot);
+            if (++slot == R) {
+                slot = 0;
+                phase ^= 1u;
             }
+#pragma unroll
+            for (int ct = 0; ct < NT; ++ct)
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    const float xs = __ldg(p.xscale + col_token<NT>(ct, 2 * c + i) * p.nb + b);
+#pragma unroll
+                    for (int t = 0; t < 2; ++t) {
+                        acc[t][ct][i] = fmaf(xs, ab[t][ct][i], acc[t][ct][i]) + mt[t][ct][i];
+                        acc[t][ct][2 + i] = fmaf(xs, ab[t][ct][2 + i], acc[t][ct][2 + i]) + mt[t][ct][2 + i];
+                    }
+                }
+        }
         if (++cb == p.nb) {
             cb = 0;
             ++cp;
         }
     }
-    if (cur_pair >= 0) finish_pair<NT>(p, cur_pair, gw, s0, s1, acc, lane);
+    if (cur_pair >= 0) finish(cur_pair);
 }
 
 // ------------------------------- F32 ---------------------------------------
@@ -774,9 +905,8 @@ __device__ __forceinline__ float block_sum(float v, float* sh) {
     return s;
 }
 
-__global__ void __launch_bounds__(256) xprep_kernel(XSeg s0, XSeg s1, int nseg, int N, int NT, float eps,
-                                                    uint2* __restrict__ xfrag, float* __restrict__ xscale,
-                                                    float* __restrict__ xsum, int want_xsum) {
+__global__ void __launch_bounds__(256) xprep_kernel(XSeg s0, XSeg s1, int nseg, int N, float eps, QbXBuf xb,
+                                                    int what) {
     pdl_wait();
     pdl_trigger();
     const int t = blockIdx.y;
@@ -826,44 +956,97 @@ __global__ void __launch_bounds__(256) xprep_kernel(XSeg s0, XSeg s1, int nseg, 
     for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(v[i]));
 #pragma unroll
     for (int o = 16; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-    int e = 0;
-    if (am > 0.f && isfinite(am)) {
-        int ex;
-        frexpf(am, &ex);
-        e = max(-100, min(100, 15 - ex));   // am * 2^e in [2^14, 2^15)
+    int ex = 0;
+    const bool nz = am > 0.f && isfinite(am);
+    if (nz) frexpf(am, &ex);   // am < 2^ex
+    if (what & QB_XP_F16) {
+        const int NT = N <= 4 ? 1 : 2;
+        const int e = nz ? max(-100, min(100, 15 - ex)) : 0;   // am * 2^e in [2^14, 2^15)
+        if (lane == 0) xb.xscale[t * nb + b] = ldexpf(1.f, -e);
+        const float sc = ldexpf(1.f, e);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int el = h * 128 + 4 * lane;
+            const int sb = b * 8 + (el >> 5), st = (el >> 4) & 1, cq = (el >> 2) & 3;
+            __half hv[4], lv[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float xs = v[4 * h + k] * sc;
+                hv[k] = __float2half_rn(xs);
+                lv[k] = __float2half_rn(xs - __half2float(hv[k]));
+            }
+            uint2 hi, lo;
+            hi.x = (uint32_t)__half_as_ushort(hv[0]) | ((uint32_t)__half_as_ushort(hv[1]) << 16);
+            hi.y = (uint32_t)__half_as_ushort(hv[2]) | ((uint32_t)__half_as_ushort(hv[3]) << 16);
+            lo.x = (uint32_t)__half_as_ushort(lv[0]) | ((uint32_t)__half_as_ushort(lv[1]) << 16);
+            lo.y = (uint32_t)__half_as_ushort(lv[2]) | ((uint32_t)__half_as_ushort(lv[3]) << 16);
+            const size_t base = (size_t)(sb * 2 + st) * NT;
+            if (NT == 1) {
+                xb.xfrag[base * 32 + t * 4 + cq] = hi;
+                xb.xfrag[base * 32 + (t + 4) * 4 + cq] = lo;
+            } else {
+                xb.xfrag[base * 32 + t * 4 + cq] = hi;
+                xb.xfrag[(base + 1) * 32 + t * 4 + cq] = lo;
+            }
+        }
     }
-    if (lane == 0) xscale[t * nb + b] = ldexpf(1.f, -e);
-    const float sc = ldexpf(1.f, e);
+    if (what & QB_XP_SUM) {
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        const int el = h * 128 + 4 * lane;
-        const int sb = b * 8 + (el >> 5), st = (el >> 4) & 1, cq = (el >> 2) & 3;
-        __half hv[4], lv[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const float xs = v[4 * h + k] * sc;
-            hv[k] = __float2half_rn(xs);
-            lv[k] = __float2half_rn(xs - __half2float(hv[k]));
-        }
-        uint2 hi, lo;
-        hi.x = (uint32_t)__half_as_ushort(hv[0]) | ((uint32_t)__half_as_ushort(hv[1]) << 16);
-        hi.y = (uint32_t)__half_as_ushort(hv[2]) | ((uint32_t)__half_as_ushort(hv[3]) << 16);
-        lo.x = (uint32_t)__half_as_ushort(lv[0]) | ((uint32_t)__half_as_ushort(lv[1]) << 16);
-        lo.y = (uint32_t)__half_as_ushort(lv[2]) | ((uint32_t)__half_as_ushort(lv[3]) << 16);
-        const size_t base = (size_t)(sb * 2 + st) * NT;
-        if (NT == 1) {
-            xfrag[base * 32 + t * 4 + cq] = hi;
-            xfrag[base * 32 + (t + 4) * 4 + cq] = lo;
-        } else {
-            xfrag[base * 32 + t * 4 + cq] = hi;
-            xfrag[(base + 1) * 32 + t * 4 + cq] = lo;
-        }
-        if (want_xsum) {
+        for (int h = 0; h < 2; ++h) {
+            const int sb = b * 8 + ((h * 128 + 4 * lane) >> 5);
             float ps = v[4 * h] + v[4 * h + 1] + v[4 * h + 2] + v[4 * h + 3];
             ps += __shfl_xor_sync(0xffffffffu, ps, 1);
             ps += __shfl_xor_sync(0xffffffffu, ps, 2);
             ps += __shfl_xor_sync(0xffffffffu, ps, 4);
-            if ((lane & 7) == 0) xsum[t * (K >> 5) + sb] = ps;
+            if ((lane & 7) == 0) xb.xsum[t * (K >> 5) + sb] = ps;
+        }
+    }
+    if (what & QB_XP_I8) {
+        // X = rint(x * 2^e) with |X| <= 2^22, as balanced int8 digits X = 65536 d0 + 256 d1 + d2
+        // (|d0| <= 64).  Lane 8j + c (c < 4) holds elements 4c..4c+3 of sub-block j and
+        // lane 8j + c + 4 elements 16+4c..16+4c+3: together one mma B register pair.
+        const int NTI = N <= 4 ? 2 : 3;
+        const int e = nz ? max(-120, min(120, 22 - ex)) : 0;
+        if (lane == 0) xb.xqscale[t * nb + b] = ldexpf(1.f, -e);
+        const float sc = ldexpf(1.f, e);
+        const int c = lane & 3;
+        const bool first = (lane & 4) == 0;
+        // destination (n8 tile, column) of each digit of token t
+        int dnt[3], dcol[3];
+        if (t < 4) {
+            dnt[0] = 0; dcol[0] = 2 * t;
+            dnt[1] = 0; dcol[1] = 2 * t + 1;
+            dnt[2] = 1; dcol[2] = 2 * t;
+        } else {
+            dnt[0] = 2; dcol[0] = 2 * (t - 4);
+            dnt[1] = 2; dcol[1] = 2 * (t - 4) + 1;
+            dnt[2] = 1; dcol[2] = 2 * (t - 4) + 1;
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            uint32_t dg[3] = {0u, 0u, 0u};   // per digit: 4 bytes, element order 0..3 of this lane
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int X = __float2int_rn(v[4 * h + k] * sc);
+                const int d2 = (int)(int8_t)(X & 0xFF);
+                const int X1 = (X - d2) >> 8;
+                const int d1 = (int)(int8_t)(X1 & 0xFF);
+                const int d0 = (X1 - d1) >> 8;
+                dg[0] |= ((uint32_t)d0 & 0xFFu) << (8 * k);
+                dg[1] |= ((uint32_t)d1 & 0xFFu) << (8 * k);
+                dg[2] |= ((uint32_t)d2 & 0xFFu) << (8 * k);
+            }
+            const int kb = b * 8 + h * 4 + (lane >> 3);   // global sub-block (k32) index
+#pragma unroll
+            for (int dgi = 0; dgi < 3; ++dgi) {
+                const uint32_t other = __shfl_xor_sync(0xffffffffu, dg[dgi], 4);
+                if (first) {
+                    uint2 bv;
+                    bv.x = prmt(dg[dgi], other, 0x5140u);   // (4c, 4c+16, 4c+1, 4c+17)
+                    bv.y = prmt(dg[dgi], other, 0x7362u);   // (4c+2, 4c+18, 4c+3, 4c+19)
+                    xb.xq[((size_t)kb * NTI + dnt[dgi]) * 32 + dcol[dgi] * 4 + c] = bv;
+                }
+            }
         }
     }
 }
@@ -871,19 +1054,6 @@ __global__ void __launch_bounds__(256) xprep_kernel(XSeg s0, XSeg s1, int nseg, 
 }  // namespace
 
 // ============================ host launchers ==================================
-
-static const uint8_t kIq4Lut[16] = {
-    // kvalues_iq4nl + 128
-    1, 24, 45, 63, 79, 93, 106, 118, 129, 141, 153, 166, 181, 197, 217, 241,
-};
-
-cudaError_t qb_quant_init_constants() {
-    uint32_t w[4];
-    for (int i = 0; i < 4; ++i)
-        w[i] = kIq4Lut[4 * i] | (kIq4Lut[4 * i + 1] << 8) | (kIq4Lut[4 * i + 2] << 16) |
-               ((uint32_t)kIq4Lut[4 * i + 3] << 24);
-    return cudaMemcpyToSymbol(c_iq4_lut, w, sizeof w);
-}
 
 // repacked matrices are padded to whole 32-row tile pairs
 static size_t padded_tiles(int rows) { return (size_t)((rows + 31) / 32) * 2; }
@@ -907,10 +1077,24 @@ cudaError_t qb_repack(int type, const void* src_dev, int rows, int K, void* dst_
     return cudaGetLastError();
 }
 
-cudaError_t qb_xprep(const QbXIn* in, int nseg, int N, float eps, uint2* xfrag, float* xscale, float* xsum,
-                     int want_xsum, cudaStream_t st) {
+size_t qb_xfrag_bytes(int K) { return (size_t)(K + 255) / 256 * 256 / 16 * 2 * 32 * sizeof(uint2); }
+size_t qb_xq_bytes(int K) { return (size_t)(K + 255) / 256 * 256 / 32 * 3 * 32 * sizeof(uint2); }
+
+int qb_xprep_needs(int type) {
+    switch (type) {
+    case QB_IQ4_XS: return QB_XP_I8;
+    case QB_Q4_K:
+    case QB_Q5_K: return QB_XP_F16 | QB_XP_SUM;
+    case QB_Q6_K:
+    case QB_Q8_0: return QB_XP_F16;
+    default: return 0;
+    }
+}
+
+cudaError_t qb_xprep(const QbXIn* in, int nseg, int N, float eps, const QbXBuf& xb, int what, cudaStream_t st) {
     XSeg s[2] = {};
     int K = 0;
+    if (nseg < 1 || nseg > 2 || N < 1 || N > QB_MAX_TOK) return cudaErrorInvalidValue;
     for (int i = 0; i < nseg; ++i) {
         s[i].x = in[i].x;
         s[i].ldx = in[i].ldx;
@@ -919,17 +1103,17 @@ cudaError_t qb_xprep(const QbXIn* in, int nseg, int N, float eps, uint2* xfrag, 
         if (in[i].len % 256) return cudaErrorInvalidValue;
         K += in[i].len;
     }
-    const int NT = N <= 4 ? 1 : 2;
+    if (((what & QB_XP_F16) && (!xb.xfrag || !xb.xscale)) || ((what & QB_XP_SUM) && !xb.xsum) ||
+        ((what & QB_XP_I8) && (!xb.xq || !xb.xqscale)))
+        return cudaErrorInvalidValue;
     const int nb = K / 256;
-    return qb_launch(xprep_kernel, dim3((nb + 7) / 8, N), dim3(256), 0, st, s[0], s[1], nseg, N, NT, eps, xfrag,
-                     xscale, xsum, want_xsum);
+    return qb_launch(xprep_kernel, dim3((nb + 7) / 8, N), dim3(256), 0, st, s[0], s[1], nseg, N, eps, xb, what);
 }
 
 static int g_num_sms = 0;
 
-cudaError_t qb_qmv(int type, const QbQSeg* segs, int nseg, int K, int N, const uint2* xfrag,
-                   const float* xscale, const float* xsum, int accumulate, int row_lo, int row_hi,
-                   const QbQmvWork& work, cudaStream_t st) {
+cudaError_t qb_qmv(int type, const QbQSeg* segs, int nseg, int K, int N, const QbXBuf& xb, int accumulate,
+                   int row_lo, int row_hi, const QbQmvWork& work, cudaStream_t st) {
     if (nseg < 1 || nseg > QB_MAX_SEG || N < 1 || N > QB_MAX_TOK || K % 256) return cudaErrorInvalidValue;
     if (!g_num_sms) {
         int dev = 0;
@@ -971,9 +1155,15 @@ cudaError_t qb_qmv(int type, const QbQSeg* segs, int nseg, int K, int N, const u
     while (grid > 1 && grid * kConsumers > p.S) --grid;
     p.Wt = grid * kConsumers < p.S ? grid * kConsumers : p.S;   // warps beyond Wt exit at once
     if (p.Wt > work.max_warps) return cudaErrorInvalidValue;
-    p.xfrag = xfrag;
-    p.xscale = xscale;
-    p.xsum = xsum;
+    p.xfrag = xb.xfrag;
+    p.xscale = xb.xscale;
+    p.xsum = xb.xsum;
+    p.xq = xb.xq;
+    p.xqscale = xb.xqscale;
+    const int need = qb_xprep_needs(type);
+    if (((need & QB_XP_F16) && (!p.xfrag || !p.xscale)) || ((need & QB_XP_SUM) && !p.xsum) ||
+        ((need & QB_XP_I8) && (!p.xq || !p.xqscale)))
+        return cudaErrorInvalidValue;
     p.accumulate = accumulate;
     p.row_lo = row_lo;
     p.row_hi = row_hi;
@@ -982,9 +1172,9 @@ cudaError_t qb_qmv(int type, const QbQSeg* segs, int nseg, int K, int N, const u
     p.err = work.err;
     const bool nt2 = N > 4;
     cudaError_t e = cudaSuccess;
-#define QB_LAUNCH(F)                                                                                   \
+#define QB_LAUNCH(F, I8)                                                                               \
     do {                                                                                               \
-        auto kern = nt2 ? qmv_kernel<F, 2> : qmv_kernel<F, 1>;                                         \
+        auto kern = nt2 ? qmv_kernel<F, 2, I8> : qmv_kernel<F, 1, I8>;                                 \
         static bool attr_set[2] = {false, false};                                                      \
         if (!attr_set[nt2]) {                                                                          \
             cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);       \
@@ -993,11 +1183,11 @@ cudaError_t qb_qmv(int type, const QbQSeg* segs, int nseg, int K, int N, const u
         e = qb_launch(kern, dim3(grid), dim3(kThreads), smem, st, p);                                  \
     } while (0)
     switch (type) {
-    case QB_IQ4_XS: QB_LAUNCH(QB_IQ4_XS); break;
-    case QB_Q8_0: QB_LAUNCH(QB_Q8_0); break;
-    case QB_Q4_K: QB_LAUNCH(QB_Q4_K); break;
-    case QB_Q5_K: QB_LAUNCH(QB_Q5_K); break;
-    case QB_Q6_K: QB_LAUNCH(QB_Q6_K); break;
+    case QB_IQ4_XS: QB_LAUNCH(QB_IQ4_XS, true); break;
+    case QB_Q8_0: QB_LAUNCH(QB_Q8_0, false); break;
+    case QB_Q4_K: QB_LAUNCH(QB_Q4_K, false); break;
+    case QB_Q5_K: QB_LAUNCH(QB_Q5_K, false); break;
+    case QB_Q6_K: QB_LAUNCH(QB_Q6_K, false); break;
     default: return cudaErrorInvalidValue;
     }
 #undef QB_LAUNCH
