@@ -293,6 +293,8 @@ struct Engine {
     float *bx, *h_save, *qkv, *qkvc, *z, *beta, *alpha, *o, *y, *qbuf, *kvbuf, *attn_o, *gate, *up, *act;
     float *logits, *mtp_x, *mtp_h, *mtp_logits, *emb;
     QbXBuf xb{};                          // prepared GEMV activations
+    float* attn_po = nullptr;             // attention chunk partials (qb_attn_decode)
+    float2* attn_pml = nullptr;
     unsigned long long* keys = nullptr;   // [2][QB_MAX_TOK]: backbone, mtp
     QbQmvWork work{};
     QbCtrl* ctrl = nullptr;
@@ -564,6 +566,12 @@ int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
     e.xb.xsum = A((size_t)T8 * (Kmax / 32));
     e.xb.xq = (uint2*)e.dalloc(qb_xq_bytes(Kmax));
     e.xb.xqscale = A((size_t)T8 * (Kmax / 256));
+    {
+        const size_t q_rows = (size_t)d.n_head * T8 * qb_attn_max_chunks((int)e.n_ctx);
+        e.attn_po = A(q_rows * d.head_dim);
+        e.attn_pml = (float2*)e.dalloc(q_rows * sizeof(float2));
+        if (!e.attn_po || !e.attn_pml) { set_err(-2, "attention scratch alloc"); return -1; }
+    }
     e.keys = (unsigned long long*)e.dalloc(2 * T8 * sizeof(unsigned long long));
     e.ctrl = (QbCtrl*)e.dalloc(sizeof(QbCtrl));
     if (!e.bx || !e.logits || !e.xb.xfrag || !e.xb.xq || !e.ctrl || !e.emb || !e.keys) {
@@ -654,7 +662,7 @@ int attn_block(Engine& e, const LayerW& l, float* x, int B, const uint32_t* pos,
     CK(qb_attn_prep(e.qbuf, qw, e.kvbuf, 2 * kvw, l.q_norm, l.k_norm, d.n_head, d.n_kv_head, d.head_dim,
                     e.rope_half, e.rope_cos, e.rope_sin, pos, B, e.eps, kc, vc, e.st));
     CK(qb_attn_decode(e.qbuf, qw, kc, vc, d.n_head, d.n_kv_head, d.head_dim, pos, B, e.n_ctx, e.attn_o,
-                      d.n_head * d.head_dim, e.st));
+                      d.n_head * d.head_dim, e.attn_po, e.attn_pml, e.st));
     const int ow = d.n_head * d.head_dim;
     if (xprep1(e, e.attn_o, ow, nullptr, ow, B, xp_needs({&l.o}))) return -1;
     const DevMat* m1[1] = {&l.o};

@@ -72,9 +72,12 @@ cudaError_t qb_attn_prep(float* q, long long ldq, const float* kv, long long ldk
                          const float* k_norm, int n_head, int n_kv, int hd, int rope_half,
                          const float* rope_cos, const float* rope_sin, const uint32_t* pos, int B, float eps,
                          float* k_cache, float* v_cache, cudaStream_t st);
+// attention scratch: part_o [n_head][QB_MAX_TOK][qb_attn_max_chunks(n_ctx)][256] floats,
+// part_ml [n_head][QB_MAX_TOK][qb_attn_max_chunks(n_ctx)] float2
+int qb_attn_max_chunks(int n_ctx);
 cudaError_t qb_attn_decode(const float* q, long long ldq, const float* k_cache, const float* v_cache,
                            int n_head, int n_kv, int hd, const uint32_t* pos, int B, int n_ctx, float* out,
-                           long long ldo, cudaStream_t st);
+                           long long ldo, float* part_o, float2* part_ml, cudaStream_t st);
 cudaError_t qb_silu_mul(const float* gate, const float* up, long long ld, int n, int B, float* out,
                         cudaStream_t st);
 cudaError_t qb_argmax_reset(unsigned long long* keys, int B, cudaStream_t st);

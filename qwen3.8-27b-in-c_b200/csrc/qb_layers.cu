@@ -362,89 +362,174 @@ __global__ void attn_prep_kernel(float* __restrict__ q, long long ldq, const flo
     for (int j = 0; j < nj; ++j) dst[lane + 32 * j] = v[j];
 }
 
-// One CTA (8 warps) per (head, token).  Scores over t <= pos+b (warp per
-// position), softmax (max-subtracted; polynomial exp on the 8-aligned body and
-// correctly-rounded expf on the tail, sum in double as src/kernels.c:901-939),
-// then out = sum_t p_t v_t with the positions split over the 8 warps (lane
-// owns 8 of the 256 dims), partial sums reduced in warp order, times
-// sigmoid(gate) (src/model.c:353-406).
-__global__ void __launch_bounds__(256) attn_decode_kernel(const float* __restrict__ q, long long ldq,
-                                                          const float* __restrict__ kc,
-                                                          const float* __restrict__ vc, int n_head, int n_kv,
-                                                          int hd, const uint32_t* __restrict__ pos0,
-                                                          float* __restrict__ out, long long ldo) {
-    pdl_wait();
-    pdl_trigger();
-    extern __shared__ float sc[];   // [n_ctx] scores
-    __shared__ float qs[256];
-    __shared__ float part[8][256];
-    __shared__ double red_d[8];
-    __shared__ float red_f[8];
-    const int h = blockIdx.x, b = blockIdx.y;
-    const int kh = h / (n_head / n_kv);
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int pl = (int)*pos0 + b;
-    const int n = pl + 1;
-    const int kvrow = n_kv * hd;
-    const float* qh = q + (size_t)b * ldq + (size_t)h * 2 * hd;
-    qs[tid] = qh[tid];
-    __syncthreads();
-    const float scale_attn = __fdiv_rn(1.0f, sqrtf((float)hd));
-    for (int t = warp; t < n; t += 8) {
-        const float* kt = kc + (size_t)t * kvrow + (size_t)kh * hd;
-        float a = 0.f;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) a = fmaf(qs[lane + 32 * j], kt[lane + 32 * j], a);
-        a = warp_sum(a);
-        if (lane == 0) sc[t] = __fmul_rn(a, scale_attn);
-    }
-    __syncthreads();
-    float mx = -INFINITY;
-    for (int t = tid; t < n; t += 256) mx = fmaxf(mx, sc[t]);
-    mx = warp_max(mx);
-    if (lane == 0) red_f[warp] = mx;
-    __syncthreads();
-    mx = red_f[0];
-    for (int i = 1; i < 8; ++i) mx = fmaxf(mx, red_f[i]);
-    const int body = n & ~7;
-    double s = 0.0;
-    for (int t = tid; t < n; t += 256) {
-        const float d = __fsub_rn(sc[t], mx);
-        const float e = t < body ? exp_poly(d) : expf_cr(d);
-        sc[t] = e;
-        s += (double)e;
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    __syncthreads();
-    if (lane == 0) red_d[warp] = s;
-    __syncthreads();
-    double tot = 0.0;
-    for (int i = 0; i < 8; ++i) tot += red_d[i];
-    const float inv = (float)(1.0 / tot);
-    // weighted V sum: warp w takes positions [w*n/8, (w+1)*n/8)
-    const int t0 = (int)((long long)n * warp / 8), t1 = (int)((long long)n * (warp + 1) / 8);
-    float acc[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-    const float* vbase = vc + (size_t)kh * hd + lane;
-    for (int t = t0; t < t1; ++t) {
-        const float p = __fmul_rn(sc[t], inv);
-        const float* vt = vbase + (size_t)t * kvrow;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[j] = fmaf(p, vt[32 * j], acc[j]);
-    }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) part[warp][lane + 32 * j] = acc[j];
-    __syncthreads();
-    float o = 0.f;
-#pragma unroll
-    for (int w = 0; w < 8; ++w) o += part[w][tid];
-    const float g = sigmoid_ref(qh[hd + tid]);
-    out[(size_t)b * ldo + (size_t)h * hd + tid] = __fmul_rn(o, g);
+// Gated GQA attention over the KV cache (src/model.c:353-406, softmax as
+// src/kernels.c:901-939), split over position chunks (flash decoding).  The
+// G = n_head / n_kv query heads that share a KV head and the B verify tokens
+// form NQ = G * B queries; query qi = g * B + b is head kh * G + g of token b
+// and attends positions t <= pos + b.
+//
+// attn_part_kernel: one CTA per (KV head, chunk of kAttnC positions) reads the
+// chunk's keys once into shared memory and computes all NQ x kAttnC scores,
+// then per query the chunk max m, p_t = exp(s_t - m), l = sum p_t and the
+// partial o = sum_t p_t v_t (values read once per CTA).  attn_combine_kernel:
+// one CTA per (head, token) merges the chunks: M = max m_c,
+// out = sum_c e^(m_c - M) o_c / sum_c e^(m_c - M) l_c, times sigmoid(gate).
+// The exponentials are the reference's polynomial; the per-chunk rescaling
+// makes the result differ from the single-pass reference by rounding only.
+constexpr int kAttnC = 32;       // positions per chunk (key and query rows padded by 4 floats in smem)
+constexpr int kAttnHD = 256;     // head dimension
+constexpr int kAttnMaxQPT = 6;   // queries per thread in the score phase (NQ <= 48)
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
 }
 
-// SwiGLU: silu(gate) * up (src/model.c:830-836)
+// QPT = ceil(NQ / 8) queries per thread in the score phase, 2 * QPT in the value phase
+template <int QPT>
+__global__ void __launch_bounds__(256) attn_part_kernel(const float* __restrict__ q, long long ldq,
+                                                        const float* __restrict__ kc, const float* __restrict__ vc,
+                                                        int n_head, int n_kv, const uint32_t* __restrict__ pos0p,
+                                                        int B, float* __restrict__ part_o,
+                                                        float2* __restrict__ part_ml, int max_chunks) {
+    pdl_wait();
+    pdl_trigger();
+    constexpr int HD = kAttnHD, C = kAttnC, KS = HD + 4;   // padded rows: conflict-free 16-byte loads
+    const int kh = blockIdx.x, c = blockIdx.y;
+    const int pos0 = (int)*pos0p;
+    const int t0 = c * C;
+    if (t0 >= pos0 + B) return;
+    const int G = n_head / n_kv, NQ = G * B;
+    const int nt = min(C, pos0 + B - t0);   // positions of this chunk that exist
+    extern __shared__ __align__(16) float sm[];
+    float* Ks = sm;              // [C][KS]
+    float* Vs = Ks + C * KS;     // [C][HD]
+    float* Qs = Vs + C * HD;     // [NQ][KS]
+    float* Ss = Qs + NQ * KS;    // [NQ][C] scores, then p
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int kvrow = n_kv * HD;
+    // all copies in flight at once, one wait
+    for (int i = tid; i < C * (HD / 4); i += 256) {
+        const int t = i / (HD / 4), d4 = i % (HD / 4);
+        if (t < nt) {
+            const size_t src = (size_t)(t0 + t) * kvrow + (size_t)kh * HD + 4 * d4;
+            cp_async16(Ks + t * KS + 4 * d4, kc + src);
+            cp_async16(Vs + t * HD + 4 * d4, vc + src);
+        } else {
+            *reinterpret_cast<float4*>(Ks + t * KS + 4 * d4) = make_float4(0.f, 0.f, 0.f, 0.f);
+            *reinterpret_cast<float4*>(Vs + t * HD + 4 * d4) = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+    for (int i = tid; i < NQ * (HD / 4); i += 256) {
+        const int qi = i / (HD / 4), d4 = i % (HD / 4);
+        const int g = qi / B, b = qi - g * B;
+        cp_async16(Qs + qi * KS + 4 * d4, q + (size_t)b * ldq + (size_t)(kh * G + g) * 2 * HD + 4 * d4);
+    }
+    cp_async_wait_all();
+    __syncthreads();
+    const float scale = __fdiv_rn(1.0f, sqrtf((float)HD));
+    {   // scores: warp w -> positions 4w .. 4w+3; lane -> position 4w + (lane & 3), queries (lane >> 2) + 8j
+        const int t = 4 * warp + (lane & 3), qg = lane >> 2;
+        float a[QPT];
+#pragma unroll
+        for (int j = 0; j < QPT; ++j) a[j] = 0.f;
+        const float* kr = Ks + t * KS;
+        const float* qr = Qs + qg * KS;
+#pragma unroll 4
+        for (int d4 = 0; d4 < HD / 4; ++d4) {
+            const float4 k4 = *reinterpret_cast<const float4*>(kr + 4 * d4);
+#pragma unroll
+            for (int j = 0; j < QPT; ++j) {
+                const float4 q4 = *reinterpret_cast<const float4*>(qr + 8 * j * KS + 4 * d4);
+                a[j] = fmaf(q4.x, k4.x, a[j]);
+                a[j] = fmaf(q4.y, k4.y, a[j]);
+                a[j] = fmaf(q4.z, k4.z, a[j]);
+                a[j] = fmaf(q4.w, k4.w, a[j]);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < QPT; ++j) {
+            const int qi = qg + 8 * j;
+            if (qi < NQ) Ss[qi * C + t] = __fmul_rn(a[j], scale);
+        }
+    }
+    __syncthreads();
+    // chunk softmax: warp per query, lane -> position
+    for (int qi = warp; qi < NQ; qi += 8) {
+        const int b = qi % B;
+        const int lim = pos0 + b - t0;   // last valid local position
+        const float s0 = lane <= lim ? Ss[qi * C + lane] : -INFINITY;
+        const float m = warp_max(s0);
+        const float p0 = (m != -INFINITY && lane <= lim) ? exp_poly(__fsub_rn(s0, m)) : 0.f;
+        Ss[qi * C + lane] = p0;
+        const float l = warp_sum(p0);
+        if (lane == 0) {
+            const int g = qi / B;
+            part_ml[((size_t)(kh * G + g) * QB_MAX_TOK + b) * max_chunks + c] = make_float2(m, l);
+        }
+    }
+    __syncthreads();
+    {   // o = sum_t p_t v_t: thread -> 4 dims (tid & 63) x queries (tid >> 6) + 4j
+        constexpr int QV = 2 * QPT;
+        const int d4 = tid & 63, qg = tid >> 6;
+        float4 o[QV];
+#pragma unroll
+        for (int j = 0; j < QV; ++j) o[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        const float* pr = Ss + qg * C;
+#pragma unroll 2
+        for (int t = 0; t < nt; ++t) {
+            const float4 v4 = *reinterpret_cast<const float4*>(Vs + t * HD + 4 * d4);
+#pragma unroll
+            for (int j = 0; j < QV; ++j) {
+                const float pt = pr[4 * j * C + t];
+                o[j].x = fmaf(pt, v4.x, o[j].x);
+                o[j].y = fmaf(pt, v4.y, o[j].y);
+                o[j].z = fmaf(pt, v4.z, o[j].z);
+                o[j].w = fmaf(pt, v4.w, o[j].w);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < QV; ++j) {
+            const int qi = qg + 4 * j;
+            if (qi < NQ) {
+                const int g = qi / B, b = qi - g * B;
+                float* dst = part_o + (((size_t)(kh * G + g) * QB_MAX_TOK + b) * max_chunks + c) * HD + 4 * d4;
+                *reinterpret_cast<float4*>(dst) = o[j];
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restrict__ q, long long ldq,
+                                                           const uint32_t* __restrict__ pos0p,
+                                                           const float* __restrict__ part_o,
+                                                           const float2* __restrict__ part_ml, int max_chunks,
+                                                           float* __restrict__ out, long long ldo) {
+    pdl_wait();
+    pdl_trigger();
+    constexpr int HD = kAttnHD;
+    const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+    const int nch = ((int)*pos0p + b) / kAttnC + 1;   // chunks holding positions 0 .. pos + b
+    const size_t qrow = (size_t)h * QB_MAX_TOK + b;
+    const float2* ml = part_ml + qrow * max_chunks;
+    float M = -INFINITY;
+    for (int cc = 0; cc < nch; ++cc) M = fmaxf(M, ml[cc].x);
+    double L = 0.0;
+    float o = 0.f;
+    const float* po = part_o + qrow * max_chunks * HD + d;
+    for (int cc = 0; cc < nch; ++cc) {
+        const float2 v = ml[cc];
+        const float w = exp_poly(__fsub_rn(v.x, M));
+        L += (double)w * (double)v.y;
+        o = fmaf(w, po[(size_t)cc * HD], o);
+    }
+    const float* qh = q + (size_t)b * ldq + (size_t)h * 2 * HD;
+    const float g = sigmoid_ref(qh[HD + d]);
+    out[(size_t)b * ldo + (size_t)h * HD + d] = __fmul_rn(__fmul_rn(o, (float)(1.0 / L)), g);
+}
+
 __global__ void silu_mul_kernel(const float* __restrict__ gate, const float* __restrict__ up, long long ld,
                                 int n, float* __restrict__ out) {
     pdl_wait();
@@ -633,18 +718,40 @@ cudaError_t qb_attn_prep(float* q, long long ldq, const float* kv, long long ldk
     return cudaGetLastError();
 }
 
+int qb_attn_max_chunks(int n_ctx) { return (n_ctx + kAttnC - 1) / kAttnC; }
+
 cudaError_t qb_attn_decode(const float* q, long long ldq, const float* k_cache, const float* v_cache,
                            int n_head, int n_kv, int hd, const uint32_t* pos, int B, int n_ctx, float* out,
-                           long long ldo, cudaStream_t st) {
-    if (hd != 256) return cudaErrorInvalidValue;
-    const size_t smem = (size_t)n_ctx * sizeof(float);
-    static int configured_for = 0;
-    if ((int)smem > configured_for && smem > 48 * 1024) {
-        cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        configured_for = (int)smem;
+                           long long ldo, float* part_o, float2* part_ml, cudaStream_t st) {
+    if (hd != kAttnHD || n_kv < 1 || n_head % n_kv || B < 1 || B > QB_MAX_TOK) return cudaErrorInvalidValue;
+    const int G = n_head / n_kv, NQ = G * B;
+    if ((NQ + 7) / 8 > kAttnMaxQPT) return cudaErrorInvalidValue;
+    const int max_chunks = qb_attn_max_chunks(n_ctx);
+    const int qpt = (NQ + 7) / 8;
+    // query and score rows up to 8 * qpt are read (rows past NQ hold junk that is never stored)
+    const size_t smem = ((size_t)kAttnC * (kAttnHD + 4) + (size_t)kAttnC * kAttnHD + (size_t)8 * qpt * (kAttnHD + 4) +
+                         (size_t)8 * qpt * kAttnC) * sizeof(float);
+    cudaError_t e = cudaSuccess;
+#define QB_ATTN_CASE(Q)                                                                                         \
+    case Q: {                                                                                                   \
+        static size_t configured_for = 0;                                                                       \
+        if (smem > configured_for) {                                                                            \
+            if ((e = cudaFuncSetAttribute(attn_part_kernel<Q>, cudaFuncAttributeMaxDynamicSharedMemorySize,    \
+                                          (int)smem)) != cudaSuccess)                                           \
+                return e;                                                                                       \
+            configured_for = smem;                                                                              \
+        }                                                                                                       \
+        qb_launch(attn_part_kernel<Q>, dim3(n_kv, max_chunks), dim3(256), smem, st, q, ldq, k_cache, v_cache,  \
+                  n_head, n_kv, pos, B, part_o, part_ml, max_chunks);                                           \
+        break;                                                                                                  \
     }
-    qb_launch(attn_decode_kernel, dim3(n_head, B), dim3(256), smem, st, q, ldq, k_cache, v_cache, n_head, n_kv, hd, pos,
-                                                           out, ldo);
+    switch (qpt) {
+        QB_ATTN_CASE(1) QB_ATTN_CASE(2) QB_ATTN_CASE(3) QB_ATTN_CASE(4) QB_ATTN_CASE(5) QB_ATTN_CASE(6)
+    default: return cudaErrorInvalidValue;
+    }
+#undef QB_ATTN_CASE
+    qb_launch(attn_combine_kernel, dim3(n_head, B), dim3(kAttnHD), 0, st, q, ldq, pos, (const float*)part_o,
+              (const float2*)part_ml, max_chunks, out, ldo);
     return cudaGetLastError();
 }
 

@@ -119,11 +119,6 @@ __device__ __forceinline__ void iq4_scales(const uint8_t* u, int row, uint32_t& 
     L1 = ((v.x >> 6) & 0x03030303u) | (nib << 2);
     d = h2f_bits(v.y);
 }
-__device__ __forceinline__ float iq4_dl(uint32_t L0, uint32_t L1, float d, int sb) {
-    const uint32_t L = sb < 4 ? L0 : L1;
-    const float f = __int_as_float(prmt(L, 0x4B000000u, 0x7440u + (sb & 3)));   // 2^23 + ls
-    return (f - 8388640.0f) * d;                                                // (ls - 32) * d
-}
 
 // ---- IQ4_XS on the int8 tensor-core path (mma m16n8k32 s8 -> s32) ----
 // Codes become the int8 values of kvalues_iq4nl (src/quant.c:30-32) by two
