@@ -64,6 +64,19 @@ def peaks():
         return 6650.0, "fallback"
 
 
+def profiled_traffic():
+    """DRAM bytes (read + write) of one FFN gate+up launch, from the committed ncu
+    summary of that launch (same shape in the 4-layer capture and the full model)."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "qmv_iq4xs_ffn_gate_up_n4_wide4.md")) as f:
+            for line in f:
+                if line.strip().startswith("dram_bytes_per_launch:"):
+                    return float(line.split(":")[1])
+    except OSError:
+        pass
+    return None
+
+
 def gguf_path(rank, world):
     d = "/dev/shm" if os.path.isdir("/dev/shm") else "/tmp"
     path = os.path.join(d, f"qb_bench_full_seed{SEED}.gguf")
@@ -268,7 +281,8 @@ def run_ours(args, rank, world, local_rank):
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "step": "one request: reset + prefill 128 + decode 512 tokens"},
             "roofline": {"bound": "hbm", "kernel": "qmv IQ4_XS (FFN gate+up fused, N=4)", "achieved": gemv_gbs,
-                         "peak": hbm, "unit": "GB/s", "frac": gemv_gbs / hbm, "traffic": None,
+                         "peak": hbm, "unit": "GB/s", "frac": gemv_gbs / hbm, "traffic": profiled_traffic(),
+                         "algorithmic_bytes": b_gemv,
                          "peak_kind": peak_kind},
             "verify_step": {"ms": ms_ver, "bytes": b_ver, "GB/s": ver_gbs, "frac": ver_gbs / hbm},
             "draft_ms": ms_draft, "head_ms": ms_head,

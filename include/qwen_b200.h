@@ -43,7 +43,10 @@
 extern "C" {
 #endif
 
-/* ---- types shared with the reference headers (same layout) ---- */
+/* ---- types shared with the reference headers (same layout) ----
+ * When the reference gguf.h was included first (a relinked reference caller),
+ * its identical definitions are used instead. */
+#ifndef GGUF_H
 
 /* include/gguf.h:40-64 */
 typedef enum {
@@ -75,6 +78,8 @@ typedef struct {
     uint32_t full_attn_interval, ssm_state_size, ssm_conv_kernel, ssm_inner_size, ssm_group_count;
     uint32_t nextn_layers;
 } qwen_config_t;
+
+#endif /* GGUF_H */
 
 /* include/model.h:10-31 */
 typedef struct {
@@ -151,6 +156,13 @@ void silu_inplace(float *x, uint64_t n);
 void sigmoid_inplace(float *x, uint64_t n);
 void softplus_inplace(float *x, uint64_t n);
 void softmax_inplace(float *x, uint64_t n);
+
+/* include/model.h:151-152: per-section timers of the CPU engine's
+ * model_forward.  Exported so reference callers (src/main.c:256-263) link; the
+ * device engine leaves them at zero and qwen_prof_calls at 0, so the CLI skips
+ * its profile line.  Device timings come from qb_last_loop_ms / qb_bench. */
+extern double qwen_prof_embed, qwen_prof_gdn, qwen_prof_attn, qwen_prof_head;
+extern uint64_t qwen_prof_calls;
 
 /* ---- device-resident loops (no counterpart function in the reference: they
  *      run the loops of src/main.c on the device) ---- */

@@ -54,6 +54,11 @@ static void set_err(int code, const char* fmt, ...) {
         }                                                                                    \
     } while (0)
 
+extern "C" {
+double qwen_prof_embed = 0.0, qwen_prof_gdn = 0.0, qwen_prof_attn = 0.0, qwen_prof_head = 0.0;
+uint64_t qwen_prof_calls = 0;
+}
+
 extern "C" int qb_last_error(void) { return g_err; }
 extern "C" const char* qb_last_error_str(void) { return g_err_str; }
 extern "C" void qb_clear_error(void) {
