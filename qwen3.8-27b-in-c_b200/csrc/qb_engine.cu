@@ -241,6 +241,7 @@ struct DevMat {
     int type = -1;
     int rows = 0, K = 0;
     void* w = nullptr;   // repacked (quant) or plain row-major (F32)
+    uint64_t fingerprint = 0;   // host-API weight cache only
 };
 
 struct LayerW {
@@ -647,8 +648,7 @@ int ffn_block(Engine& e, const LayerW& l, float* x, int B) {
     float* o2[2] = {e.gate, e.up};
     const long long ld2[2] = {e.F, e.F};
     if (gemv_group(e, m2, o2, ld2, 2, e.E, B, 0)) return -1;
-    CK(qb_silu_mul(e.gate, e.up, e.F, e.F, B, e.act, e.st));
-    if (xprep1(e, e.act, e.F, nullptr, e.F, B, xp_needs({&l.ffn_down}))) return -1;
+    CK(qb_silu_mul_xprep(e.gate, e.up, e.F, e.F, B, e.act, e.xb, xp_needs({&l.ffn_down}), e.st));
     const DevMat* m1[1] = {&l.ffn_down};
     float* o1[1] = {x};
     const long long ld1[1] = {e.E};
@@ -667,9 +667,8 @@ int attn_block(Engine& e, const LayerW& l, float* x, int B, const uint32_t* pos,
     CK(qb_attn_prep(e.qbuf, qw, e.kvbuf, 2 * kvw, l.q_norm, l.k_norm, d.n_head, d.n_kv_head, d.head_dim,
                     e.rope_half, e.rope_cos, e.rope_sin, pos, B, e.eps, kc, vc, e.st));
     CK(qb_attn_decode(e.qbuf, qw, kc, vc, d.n_head, d.n_kv_head, d.head_dim, pos, B, e.n_ctx, e.attn_o,
-                      d.n_head * d.head_dim, e.attn_po, e.attn_pml, e.st));
+                      d.n_head * d.head_dim, e.attn_po, e.attn_pml, e.xb, xp_needs({&l.o}), e.st));
     const int ow = d.n_head * d.head_dim;
-    if (xprep1(e, e.attn_o, ow, nullptr, ow, B, xp_needs({&l.o}))) return -1;
     const DevMat* m1[1] = {&l.o};
     float* o1[1] = {x};
     const long long ld1[1] = {e.E};
@@ -691,8 +690,13 @@ int gdn_block(Engine& e, const LayerW& l, int B, int ckpt) {
     CK(qb_gdn_recur(e.qkvc, e.ld_qkv, e.beta, e.alpha, 256, l.dt_bias, l.ssm_a, d.n_k_heads, d.n_v_heads,
                     d.head_k_dim, B, e.eps, ssm, e.ssm_slot_stride, &e.ctrl->cur_slot, ckpt, e.o, d.d_inner,
                     e.st));
-    CK(qb_gdn_out(e.o, e.z, d.d_inner, l.ssm_norm, d.n_v_heads, d.head_v_dim, B, e.eps, e.y, e.st));
-    if (xprep1(e, e.y, d.d_inner, nullptr, d.d_inner, B, xp_needs({&l.ssm_out}))) return -1;
+    if (d.head_v_dim == 128 && d.n_v_heads % 2 == 0) {
+        CK(qb_gdn_out_xprep(e.o, e.z, d.d_inner, l.ssm_norm, d.n_v_heads, d.head_v_dim, B, e.eps, e.y, e.xb,
+                            xp_needs({&l.ssm_out}), e.st));
+    } else {
+        CK(qb_gdn_out(e.o, e.z, d.d_inner, l.ssm_norm, d.n_v_heads, d.head_v_dim, B, e.eps, e.y, e.st));
+        if (xprep1(e, e.y, d.d_inner, nullptr, d.d_inner, B, xp_needs({&l.ssm_out}))) return -1;
+    }
     const DevMat* m1[1] = {&l.ssm_out};
     float* o1[1] = {e.bx};
     const long long ld1[1] = {e.E};
@@ -1425,17 +1429,38 @@ int scratch_work(Scratch* s, int rows) {
     return 0;
 }
 
+// FNV-1a over 64 evenly spaced 16-byte windows plus both ends of the weight
+// bytes.  The device copy is keyed by (pointer, type, shape) as the reference
+// hands out stable mmap pointers; the fingerprint catches a caller that
+// reuses an address for different weights (freed and reallocated buffers).
+uint64_t weight_fingerprint(const uint8_t* p, size_t n) {
+    uint64_t h = 1469598103934665603ull;
+    auto mix = [&](size_t off, size_t len) {
+        for (size_t i = 0; i < len && off + i < n; ++i) h = (h ^ p[off + i]) * 1099511628211ull;
+    };
+    mix(0, 64);
+    for (int k = 0; k < 64; ++k) mix(n / 64 * (size_t)k, 16);
+    if (n > 64) mix(n - 64, 64);
+    return h;
+}
+
 int wcache_get(const gguf_tensor_info_t* W, const DevMat*& out) {
     int dev = 0;
     CK(cudaGetDevice(&dev));
     const WKey key{dev, W->data, (int)W->type, W->ne[0], W->ne[1]};
+    const size_t src_bytes = gguf_row_bytes((int)W->type, W->ne[0]) * W->ne[1];
+    const uint64_t fp = src_bytes ? weight_fingerprint((const uint8_t*)W->data, src_bytes) : 0;
     auto it = g_wcache.find(key);
-    if (it != g_wcache.end()) { out = &it->second; return 0; }
+    if (it != g_wcache.end()) {
+        if (it->second.fingerprint == fp) { out = &it->second; return 0; }
+        cudaFree(it->second.w);   // same address, different weights: replace the device copy
+        g_wcache.erase(it);
+    }
     DevMat m;
     m.type = (int)W->type;
     m.K = (int)W->ne[0];
     m.rows = (int)W->ne[1];
-    const size_t src_bytes = gguf_row_bytes(m.type, W->ne[0]) * W->ne[1];
+    m.fingerprint = fp;
     if (!src_bytes || (m.type != QB_F32 && m.K % 256)) { set_err(-1, "gemv: unsupported tensor type %d / ne0 %llu", m.type, (unsigned long long)W->ne[0]); return -1; }
     if (m.type == QB_F32) {
         CK(cudaMalloc(&m.w, src_bytes));

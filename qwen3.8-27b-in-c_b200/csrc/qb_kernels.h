@@ -77,7 +77,13 @@ cudaError_t qb_attn_prep(float* q, long long ldq, const float* kv, long long ldk
 int qb_attn_max_chunks(int n_ctx);
 cudaError_t qb_attn_decode(const float* q, long long ldq, const float* k_cache, const float* v_cache,
                            int n_head, int n_kv, int hd, const uint32_t* pos, int B, int n_ctx, float* out,
-                           long long ldo, float* part_o, float2* part_ml, cudaStream_t st);
+                           long long ldo, float* part_o, float2* part_ml, const QbXBuf& xb, int what,
+                           cudaStream_t st);   // also emits the o-projection GEMV input (what: QB_XP_*)
+// SwiGLU / gated RMSNorm fused with the GEMV activation prep of their output
+cudaError_t qb_silu_mul_xprep(const float* gate, const float* up, long long ld, int n, int B, float* out,
+                              const QbXBuf& xb, int what, cudaStream_t st);
+cudaError_t qb_gdn_out_xprep(const float* o, const float* z, long long ld, const float* norm_w, int n_v, int dv,
+                             int B, float eps, float* y, const QbXBuf& xb, int what, cudaStream_t st);
 cudaError_t qb_silu_mul(const float* gate, const float* up, long long ld, int n, int B, float* out,
                         cudaStream_t st);
 cudaError_t qb_argmax_reset(unsigned long long* keys, int B, cudaStream_t st);

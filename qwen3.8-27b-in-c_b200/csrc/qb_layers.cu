@@ -14,6 +14,7 @@
 // and rounded once.
 #include "qb_common.cuh"
 #include "qb_kernels.h"
+#include "qb_xprep.cuh"
 
 namespace {
 
@@ -306,6 +307,50 @@ __global__ void gdn_out_kernel(const float* __restrict__ o, const float* __restr
     }
 }
 
+// The same, fused with the GEMV activation prep of its output (the ssm_out
+// input): one warp per pair of 128-wide v-heads = one 256-column block.  The
+// norm sums keep gdn_out_kernel's 8-lane chains: lanes 0-7 head 2p, lanes
+// 8-15 head 2p+1.
+__global__ void __launch_bounds__(128) gdn_out_xprep_kernel(const float* __restrict__ o, const float* __restrict__ z,
+                                                            long long ld, const float* __restrict__ w, int n_v,
+                                                            float eps, float* __restrict__ y, int N, QbXBuf xb,
+                                                            int what) {
+    pdl_wait();
+    pdl_trigger();
+    constexpr int DV = 128;
+    const int t = blockIdx.y, lane = threadIdx.x & 31;
+    const int pb = blockIdx.x * 4 + (threadIdx.x >> 5);   // head pair = block index of the ssm_out input
+    const int nb = n_v / 2;
+    if (pb >= nb) return;
+    const float* ob = o + (size_t)t * ld + (size_t)pb * 2 * DV;
+    const float* zb = z + (size_t)t * ld + (size_t)pb * 2 * DV;
+    const int hsel = (lane >> 3) & 1;   // 8-lane group -> head of the pair
+    float acc = 0.f;
+    for (int m = 0; m < DV / 8; ++m) {
+        const float v = ob[hsel * DV + (lane & 7) + 8 * m];
+        acc = fmaf(v, v, acc);
+    }
+    const float ssum = hsum8(acc);
+    const float mean = __fdiv_rn(ssum, (float)DV);
+    const float sc = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean, eps)));
+    const float scale[2] = {__shfl_sync(0xffffffffu, sc, 0), __shfl_sync(0xffffffffu, sc, 8)};
+    float v[8];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int d0 = 4 * lane;
+        const float4 o4 = *reinterpret_cast<const float4*>(ob + h * DV + d0);
+        const float4 z4 = *reinterpret_cast<const float4*>(zb + h * DV + d0);
+        const float4 w4 = *reinterpret_cast<const float4*>(w + d0);
+        const float ov[4] = {o4.x, o4.y, o4.z, o4.w}, zv[4] = {z4.x, z4.y, z4.z, z4.w}, wv[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            v[4 * h + k] = __fmul_rn(__fmul_rn(__fmul_rn(ov[k], scale[h]), wv[k]), silu_ref(zv[k]));
+        *reinterpret_cast<float4*>(y + (size_t)t * ld + (size_t)pb * 2 * DV + h * DV + d0) =
+            make_float4(v[4 * h], v[4 * h + 1], v[4 * h + 2], v[4 * h + 3]);
+    }
+    xprep_emit(v, t, pb, N, nb, nb * 256, xb, what, lane);
+}
+
 // ----------------------------- attention ------------------------------------
 // One warp per (token, head or kv-head).  Lane owns elements lane + 32j.
 // q: RMSNorm(q_norm) then RoPE in place; k: RMSNorm(k_norm), append to the
@@ -502,32 +547,52 @@ __global__ void __launch_bounds__(256) attn_part_kernel(const float* __restrict_
     }
 }
 
-__global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restrict__ q, long long ldq,
+__global__ void __launch_bounds__(128) attn_combine_kernel(const float* __restrict__ q, long long ldq,
                                                            const uint32_t* __restrict__ pos0p,
                                                            const float* __restrict__ part_o,
                                                            const float2* __restrict__ part_ml, int max_chunks,
-                                                           float* __restrict__ out, long long ldo) {
+                                                           int n_head, int N, float* __restrict__ out,
+                                                           long long ldo, QbXBuf xb, int what) {
     pdl_wait();
     pdl_trigger();
     constexpr int HD = kAttnHD;
-    const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+    const int b = blockIdx.y, lane = threadIdx.x & 31;
+    const int h = blockIdx.x * 4 + (threadIdx.x >> 5);
+    if (h >= n_head) return;
     const int nch = ((int)*pos0p + b) / kAttnC + 1;   // chunks holding positions 0 .. pos + b
     const size_t qrow = (size_t)h * QB_MAX_TOK + b;
     const float2* ml = part_ml + qrow * max_chunks;
     float M = -INFINITY;
     for (int cc = 0; cc < nch; ++cc) M = fmaxf(M, ml[cc].x);
     double L = 0.0;
-    float o = 0.f;
-    const float* po = part_o + qrow * max_chunks * HD + d;
+    float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};   // dims 4*lane.., 128 + 4*lane..
+    const float* po = part_o + qrow * max_chunks * HD + 4 * lane;
     for (int cc = 0; cc < nch; ++cc) {
-        const float2 v = ml[cc];
-        const float w = exp_poly(__fsub_rn(v.x, M));
-        L += (double)w * (double)v.y;
-        o = fmaf(w, po[(size_t)cc * HD], o);
+        const float2 mv = ml[cc];
+        const float w = exp_poly(__fsub_rn(mv.x, M));
+        L += (double)w * (double)mv.y;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            const float4 p4 = *reinterpret_cast<const float4*>(po + (size_t)cc * HD + hh * 128);
+            o[4 * hh + 0] = fmaf(w, p4.x, o[4 * hh + 0]);
+            o[4 * hh + 1] = fmaf(w, p4.y, o[4 * hh + 1]);
+            o[4 * hh + 2] = fmaf(w, p4.z, o[4 * hh + 2]);
+            o[4 * hh + 3] = fmaf(w, p4.w, o[4 * hh + 3]);
+        }
     }
-    const float* qh = q + (size_t)b * ldq + (size_t)h * 2 * HD;
-    const float g = sigmoid_ref(qh[HD + d]);
-    out[(size_t)b * ldo + (size_t)h * HD + d] = __fmul_rn(__fmul_rn(o, (float)(1.0 / L)), g);
+    const float inv = (float)(1.0 / L);
+    const float* gh = q + (size_t)b * ldq + (size_t)h * 2 * HD + HD;
+    float v[8];
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+        const float4 g4 = *reinterpret_cast<const float4*>(gh + hh * 128 + 4 * lane);
+        const float gv[4] = {g4.x, g4.y, g4.z, g4.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) v[4 * hh + k] = __fmul_rn(__fmul_rn(o[4 * hh + k], inv), sigmoid_ref(gv[k]));
+        *reinterpret_cast<float4*>(out + (size_t)b * ldo + (size_t)h * HD + hh * 128 + 4 * lane) =
+            make_float4(v[4 * hh], v[4 * hh + 1], v[4 * hh + 2], v[4 * hh + 3]);
+    }
+    xprep_emit(v, b, h, N, n_head, n_head * HD, xb, what, lane);
 }
 
 __global__ void silu_mul_kernel(const float* __restrict__ gate, const float* __restrict__ up, long long ld,
@@ -539,6 +604,33 @@ __global__ void silu_mul_kernel(const float* __restrict__ gate, const float* __r
         const size_t o = (size_t)b * ld + i;
         out[o] = __fmul_rn(silu_ref(gate[o]), up[o]);
     }
+}
+
+// SwiGLU fused with the GEMV activation prep of its output (the ffn_down
+// input): one warp per 256-column block of one token.
+__global__ void __launch_bounds__(128) silu_mul_xprep_kernel(const float* __restrict__ gate,
+                                                             const float* __restrict__ up, long long ld, int n,
+                                                             int N, float* __restrict__ out, QbXBuf xb, int what) {
+    pdl_wait();
+    pdl_trigger();
+    const int t = blockIdx.y, lane = threadIdx.x & 31;
+    const int b = blockIdx.x * 4 + (threadIdx.x >> 5);
+    const int nb = n >> 8;
+    if (b >= nb) return;
+    const size_t base = (size_t)t * ld + (size_t)b * 256;
+    float v[8];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const size_t o = base + h * 128 + 4 * lane;
+        const float4 g4 = *reinterpret_cast<const float4*>(gate + o);
+        const float4 u4 = *reinterpret_cast<const float4*>(up + o);
+        v[4 * h + 0] = __fmul_rn(silu_ref(g4.x), u4.x);
+        v[4 * h + 1] = __fmul_rn(silu_ref(g4.y), u4.y);
+        v[4 * h + 2] = __fmul_rn(silu_ref(g4.z), u4.z);
+        v[4 * h + 3] = __fmul_rn(silu_ref(g4.w), u4.w);
+        *reinterpret_cast<float4*>(out + o) = make_float4(v[4 * h], v[4 * h + 1], v[4 * h + 2], v[4 * h + 3]);
+    }
+    xprep_emit(v, t, b, N, nb, n, xb, what, lane);
 }
 
 // ------------------------------- argmax --------------------------------------
@@ -722,7 +814,8 @@ int qb_attn_max_chunks(int n_ctx) { return (n_ctx + kAttnC - 1) / kAttnC; }
 
 cudaError_t qb_attn_decode(const float* q, long long ldq, const float* k_cache, const float* v_cache,
                            int n_head, int n_kv, int hd, const uint32_t* pos, int B, int n_ctx, float* out,
-                           long long ldo, float* part_o, float2* part_ml, cudaStream_t st) {
+                           long long ldo, float* part_o, float2* part_ml, const QbXBuf& xb, int what,
+                           cudaStream_t st) {
     if (hd != kAttnHD || n_kv < 1 || n_head % n_kv || B < 1 || B > QB_MAX_TOK) return cudaErrorInvalidValue;
     const int G = n_head / n_kv, NQ = G * B;
     if ((NQ + 7) / 8 > kAttnMaxQPT) return cudaErrorInvalidValue;
@@ -750,14 +843,29 @@ cudaError_t qb_attn_decode(const float* q, long long ldq, const float* k_cache, 
     default: return cudaErrorInvalidValue;
     }
 #undef QB_ATTN_CASE
-    qb_launch(attn_combine_kernel, dim3(n_head, B), dim3(kAttnHD), 0, st, q, ldq, pos, (const float*)part_o,
-              (const float2*)part_ml, max_chunks, out, ldo);
+    qb_launch(attn_combine_kernel, dim3((n_head + 3) / 4, B), dim3(128), 0, st, q, ldq, pos, (const float*)part_o,
+              (const float2*)part_ml, max_chunks, n_head, B, out, ldo, xb, what);
     return cudaGetLastError();
 }
 
 cudaError_t qb_silu_mul(const float* gate, const float* up, long long ld, int n, int B, float* out,
                         cudaStream_t st) {
     qb_launch(silu_mul_kernel, dim3((n + 255) / 256, B), dim3(256), 0, st, gate, up, ld, n, out);
+    return cudaGetLastError();
+}
+
+cudaError_t qb_silu_mul_xprep(const float* gate, const float* up, long long ld, int n, int B, float* out,
+                              const QbXBuf& xb, int what, cudaStream_t st) {
+    if (n % 256 || B < 1 || B > QB_MAX_TOK) return cudaErrorInvalidValue;
+    qb_launch(silu_mul_xprep_kernel, dim3((n / 256 + 3) / 4, B), dim3(128), 0, st, gate, up, ld, n, B, out, xb, what);
+    return cudaGetLastError();
+}
+
+cudaError_t qb_gdn_out_xprep(const float* o, const float* z, long long ld, const float* norm_w, int n_v, int dv,
+                             int B, float eps, float* y, const QbXBuf& xb, int what, cudaStream_t st) {
+    if (dv != 128 || n_v % 2 || B < 1 || B > QB_MAX_TOK) return cudaErrorInvalidValue;
+    qb_launch(gdn_out_xprep_kernel, dim3((n_v / 2 + 3) / 4, B), dim3(128), 0, st, o, z, ld, norm_w, n_v, eps, y, B, xb,
+              what);
     return cudaGetLastError();
 }
 

@@ -91,6 +91,22 @@ def test_micro_config_c1(n):
         assert rel(got[i], ref[i]) < RTOL
 
 
+def test_weight_cache_follows_new_contents_at_same_address():
+    """The host API caches device copies by weight pointer (the reference hands
+    out stable mmap pointers); new bytes at the same address must be picked up."""
+    K, rows = 1024, 512
+    raw = qb.synth_matrix(qb.GGML_IQ4_XS, rows, K, seed=5, d_sigma=0.02)
+    x = qb.synth_normal(2 * K, seed=6).reshape(2, K)
+    t = qb.tensor(raw, qb.GGML_IQ4_XS, K, rows)
+    first = qb.gemv_batch(t, x)
+    raw[:] = qb.synth_matrix(qb.GGML_IQ4_XS, rows, K, seed=7, d_sigma=0.02)   # same buffer, new weights
+    second = qb.gemv_batch(t, x)
+    ref = oracle.ref_gemv_batch(raw, qb.GGML_IQ4_XS, K, rows, x)
+    for i in range(2):
+        assert rel(second[i], ref[i]) < RTOL
+    assert rel(first[0], second[0]) > 0.1
+
+
 def test_sample_greedy_first_max_wins():
     x = np.zeros(248320, np.float32)
     x[[7, 100, 200000]] = 3.0
