@@ -158,6 +158,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
     }
     return false;
 }
+// bounded wait that lets the hardware suspend the thread up to hint_ns per try
+// instead of spinning; returns false when the bound was hit
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns,
+                                                uint32_t max_iter = (1u << 16)) {
+    const uint32_t a = smem_u32(bar);
+    for (uint32_t it = 0; it < max_iter; ++it) {
+        uint32_t ok;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(ok)
+            : "r"(a), "r"(parity), "r"(hint_ns)
+            : "memory");
+        if (ok) return true;
+    }
+    return false;
+}
 // the same two operations on shared-memory addresses already in the shared window
 __device__ __forceinline__ void mbar_expect_tx_s(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");

@@ -240,7 +240,8 @@ constexpr int kNSlot = 4;
 struct DevMat {
     int type = -1;
     int rows = 0, K = 0;
-    void* w = nullptr;   // repacked (quant) or plain row-major (F32)
+    void* w = nullptr;      // repacked into 16-row mma.sync tiles (quant) or plain row-major (F32)
+    void* w_tc = nullptr;   // IQ4_XS also in 128-row tcgen05 tiles (qb_qmv_tc, N <= 4)
     uint64_t fingerprint = 0;   // host-API weight cache only
 };
 
@@ -299,6 +300,7 @@ struct Engine {
     float *bx, *h_save, *qkv, *qkvc, *z, *beta, *alpha, *o, *y, *qbuf, *kvbuf, *attn_o, *gate, *up, *act;
     float *logits, *mtp_x, *mtp_h, *mtp_logits, *emb;
     QbXBuf xb{};                          // prepared GEMV activations
+    bool use_tc = false;                  // IQ4_XS at N <= 4 on tcgen05 (QB_TC=1); default: int8 mma.sync
     float* attn_po = nullptr;             // attention chunk partials (qb_attn_decode)
     float2* attn_pml = nullptr;
     unsigned long long* keys = nullptr;   // [2][QB_MAX_TOK]: backbone, mtp
@@ -360,6 +362,12 @@ int upload_mat(Engine& e, const GTensor* t, DevMat& m, void* tmp, size_t tmp_byt
     // stream-ordered: the repack must not start before the host->device copy lands
     CK(cudaMemcpyAsync(tmp, t->data, src_bytes, cudaMemcpyHostToDevice, e.st));
     CK(qb_repack(t->type, tmp, m.rows, m.K, m.w, e.st));
+    if (t->type == QB_IQ4_XS) {
+        const size_t rt = qb_repacked_bytes_tc(m.rows, m.K);
+        m.w_tc = e.dalloc(rt);
+        if (!m.w_tc) { set_err(-2, "cudaMalloc %zu", rt); return -1; }
+        CK(qb_repack_tc(tmp, m.rows, m.K, m.w_tc, e.st));
+    }
     CK(cudaStreamSynchronize(e.st));
     if (t->type == QB_Q4_K || t->type == QB_Q5_K) e.any_q45 = true;
     return 0;
@@ -572,6 +580,13 @@ int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
     e.xb.xsum = A((size_t)T8 * (Kmax / 32));
     e.xb.xq = (uint2*)e.dalloc(qb_xq_bytes(Kmax));
     e.xb.xqscale = A((size_t)T8 * (Kmax / 256));
+    e.xb.xtc = (uint8_t*)e.dalloc(qb_xtc_bytes(Kmax));
+    if (!e.xb.xtc) { set_err(-2, "activation alloc"); return -1; }
+    CK(cudaMemset(e.xb.xtc, 0, qb_xtc_bytes(Kmax)));
+    {
+        const char* tc = getenv("QB_TC");
+        e.use_tc = tc && tc[0] == '1';
+    }
     {
         const size_t q_rows = (size_t)d.n_head * T8 * qb_attn_max_chunks((int)e.n_ctx);
         e.attn_po = A(q_rows * d.head_dim);
@@ -621,6 +636,9 @@ int gemv_group(Engine& e, const DevMat* const* mats, float* const* outs, const l
         }
         if (type == QB_F32) {
             for (int s = 0; s < ns; ++s) CK(cudaErrorNotSupported);
+        } else if (type == QB_IQ4_XS && N <= 4 && e.use_tc) {
+            for (int s = 0; s < ns; ++s) segs[s].w = mats[i - ns + s]->w_tc;
+            CK(qb_qmv_tc(segs, ns, K, N, e.xb, accumulate, 0, 1 << 30, e.work, e.st));
         } else {
             CK(qb_qmv(type, segs, ns, K, N, e.xb, accumulate, 0, 1 << 30, e.work, e.st));
         }
@@ -628,10 +646,10 @@ int gemv_group(Engine& e, const DevMat* const* mats, float* const* outs, const l
     return 0;
 }
 
-// the qb_xprep outputs that the matrices consuming an input read
-int xp_needs(std::initializer_list<const DevMat*> ms) {
+// the qb_xprep outputs that the matrices consuming an input of N tokens read
+int xp_needs(const Engine& e, std::initializer_list<const DevMat*> ms, int N) {
     int w = 0;
-    for (const DevMat* m : ms) w |= qb_xprep_needs(m->type);
+    for (const DevMat* m : ms) w |= qb_xprep_needs(m->type, N, e.use_tc ? 1 : 0);
     return w;
 }
 
@@ -643,12 +661,12 @@ int xprep1(Engine& e, const float* x, long long ldx, const float* norm_w, int le
 
 // SwiGLU FFN on residual x (src/model.c:819-842)
 int ffn_block(Engine& e, const LayerW& l, float* x, int B) {
-    if (xprep1(e, x, e.E, l.post_norm, e.E, B, xp_needs({&l.ffn_gate, &l.ffn_up}))) return -1;
+    if (xprep1(e, x, e.E, l.post_norm, e.E, B, xp_needs(e, {&l.ffn_gate, &l.ffn_up}, B))) return -1;
     const DevMat* m2[2] = {&l.ffn_gate, &l.ffn_up};
     float* o2[2] = {e.gate, e.up};
     const long long ld2[2] = {e.F, e.F};
     if (gemv_group(e, m2, o2, ld2, 2, e.E, B, 0)) return -1;
-    CK(qb_silu_mul_xprep(e.gate, e.up, e.F, e.F, B, e.act, e.xb, xp_needs({&l.ffn_down}), e.st));
+    CK(qb_silu_mul_xprep(e.gate, e.up, e.F, e.F, B, e.act, e.xb, xp_needs(e, {&l.ffn_down}, B), e.st));
     const DevMat* m1[1] = {&l.ffn_down};
     float* o1[1] = {x};
     const long long ld1[1] = {e.E};
@@ -659,7 +677,7 @@ int ffn_block(Engine& e, const LayerW& l, float* x, int B) {
 int attn_block(Engine& e, const LayerW& l, float* x, int B, const uint32_t* pos, float* kc, float* vc) {
     const qwen_dims_t& d = e.d;
     const int qw = 2 * d.n_head * d.head_dim, kvw = d.n_kv_head * d.head_dim;
-    if (xprep1(e, x, e.E, l.attn_norm, e.E, B, xp_needs({&l.q, &l.k, &l.v}))) return -1;
+    if (xprep1(e, x, e.E, l.attn_norm, e.E, B, xp_needs(e, {&l.q, &l.k, &l.v}, B))) return -1;
     const DevMat* m3[3] = {&l.q, &l.k, &l.v};
     float* o3[3] = {e.qbuf, e.kvbuf, e.kvbuf + kvw};
     const long long ld3[3] = {qw, 2 * kvw, 2 * kvw};
@@ -667,7 +685,7 @@ int attn_block(Engine& e, const LayerW& l, float* x, int B, const uint32_t* pos,
     CK(qb_attn_prep(e.qbuf, qw, e.kvbuf, 2 * kvw, l.q_norm, l.k_norm, d.n_head, d.n_kv_head, d.head_dim,
                     e.rope_half, e.rope_cos, e.rope_sin, pos, B, e.eps, kc, vc, e.st));
     CK(qb_attn_decode(e.qbuf, qw, kc, vc, d.n_head, d.n_kv_head, d.head_dim, pos, B, e.n_ctx, e.attn_o,
-                      d.n_head * d.head_dim, e.attn_po, e.attn_pml, e.xb, xp_needs({&l.o}), e.st));
+                      d.n_head * d.head_dim, e.attn_po, e.attn_pml, e.xb, xp_needs(e, {&l.o}, B), e.st));
     const int ow = d.n_head * d.head_dim;
     const DevMat* m1[1] = {&l.o};
     float* o1[1] = {x};
@@ -678,7 +696,7 @@ int attn_block(Engine& e, const LayerW& l, float* x, int B, const uint32_t* pos,
 
 int gdn_block(Engine& e, const LayerW& l, int B, int ckpt) {
     const qwen_dims_t& d = e.d;
-    if (xprep1(e, e.bx, e.E, l.attn_norm, e.E, B, xp_needs({&l.wqkv, &l.wgate, &l.wbeta, &l.walpha}))) return -1;
+    if (xprep1(e, e.bx, e.E, l.attn_norm, e.E, B, xp_needs(e, {&l.wqkv, &l.wgate, &l.wbeta, &l.walpha}, B))) return -1;
     const DevMat* m4[4] = {&l.wqkv, &l.wgate, &l.wbeta, &l.walpha};
     float* o4[4] = {e.qkv, e.z, e.beta, e.alpha};
     const long long ld4[4] = {e.ld_qkv, d.d_inner, 256, 256};
@@ -692,10 +710,10 @@ int gdn_block(Engine& e, const LayerW& l, int B, int ckpt) {
                     e.st));
     if (d.head_v_dim == 128 && d.n_v_heads % 2 == 0) {
         CK(qb_gdn_out_xprep(e.o, e.z, d.d_inner, l.ssm_norm, d.n_v_heads, d.head_v_dim, B, e.eps, e.y, e.xb,
-                            xp_needs({&l.ssm_out}), e.st));
+                            xp_needs(e, {&l.ssm_out}, B), e.st));
     } else {
         CK(qb_gdn_out(e.o, e.z, d.d_inner, l.ssm_norm, d.n_v_heads, d.head_v_dim, B, e.eps, e.y, e.st));
-        if (xprep1(e, e.y, d.d_inner, nullptr, d.d_inner, B, xp_needs({&l.ssm_out}))) return -1;
+        if (xprep1(e, e.y, d.d_inner, nullptr, d.d_inner, B, xp_needs(e, {&l.ssm_out}, B))) return -1;
     }
     const DevMat* m1[1] = {&l.ssm_out};
     float* o1[1] = {e.bx};
@@ -720,7 +738,7 @@ int fwd_backbone(Engine& e, int B, int ckpt) {
         }
     }
     CK(cudaMemcpyAsync(e.h_save, e.bx, (size_t)B * e.E * 4, cudaMemcpyDeviceToDevice, e.st));
-    if (xprep1(e, e.bx, e.E, e.out_norm, e.E, B, xp_needs({&e.output}))) return -1;
+    if (xprep1(e, e.bx, e.E, e.out_norm, e.E, B, xp_needs(e, {&e.output}, B))) return -1;
     const DevMat* m1[1] = {&e.output};
     float* o1[1] = {e.logits};
     const long long ld1[1] = {e.V};
@@ -739,7 +757,7 @@ int fwd_backbone(Engine& e, int B, int ckpt) {
 int fwd_mtp(Engine& e, int B, const float* hsrc, int want_logits) {
     CK(qb_embed(e.embd_type, e.tok_embd, e.E, e.ctrl->mtp_tok, B, e.emb, e.E, e.st));
     QbXIn in[2] = {{e.emb, e.E, e.enorm, e.E}, {hsrc, e.E, e.hnorm, e.E}};
-    CK(qb_xprep(in, 2, B, e.eps, e.xb, xp_needs({&e.eh_proj}), e.st));
+    CK(qb_xprep(in, 2, B, e.eps, e.xb, xp_needs(e, {&e.eh_proj}, B), e.st));
     const DevMat* m1[1] = {&e.eh_proj};
     float* o1[1] = {e.mtp_x};
     const long long ld1[1] = {e.E};
@@ -747,7 +765,7 @@ int fwd_mtp(Engine& e, int B, const float* hsrc, int want_logits) {
     if (attn_block(e, e.mtp, e.mtp_x, B, &e.ctrl->mtp_pos, e.mtp_k, e.mtp_v)) return -1;
     CK(cudaMemcpyAsync(e.mtp_h, e.mtp_x + (size_t)(B - 1) * e.E, (size_t)e.E * 4, cudaMemcpyDeviceToDevice, e.st));
     if (want_logits) {
-        if (xprep1(e, e.mtp_x, e.E, e.shnorm, e.E, B, xp_needs({&e.output}))) return -1;
+        if (xprep1(e, e.mtp_x, e.E, e.shnorm, e.E, B, xp_needs(e, {&e.output}, B))) return -1;
         const DevMat* mo[1] = {&e.output};
         float* oo[1] = {e.mtp_logits};
         const long long ldo[1] = {e.V};
@@ -1281,12 +1299,15 @@ extern "C" float qb_bench(qwen_model_t* m, int what, uint32_t arg, uint32_t iter
                 for (int li = 0; li < nlay; ++li) {
                     if (wh == 1) {
                         const LayerW& l = en.L[li];
-                        QbQSeg segs[2] = {{l.ffn_gate.w, en.gate, en.F, l.ffn_gate.rows},
-                                          {l.ffn_up.w, en.up, en.F, l.ffn_up.rows}};
-                        CK(qb_qmv(l.ffn_gate.type, segs, 2, en.E, a, en.xb, 0, 0, 1 << 30, en.work, en.st));
+                        const DevMat* m2[2] = {&l.ffn_gate, &l.ffn_up};
+                        float* o2[2] = {en.gate, en.up};
+                        const long long ld2[2] = {en.F, en.F};
+                        if (gemv_group(en, m2, o2, ld2, 2, en.E, a, 0)) return -1;
                     } else {
-                        QbQSeg seg = {en.output.w, en.logits, en.V, en.output.rows};
-                        CK(qb_qmv(en.output.type, &seg, 1, en.E, a, en.xb, 0, 0, 1 << 30, en.work, en.st));
+                        const DevMat* m1[1] = {&en.output};
+                        float* o1[1] = {en.logits};
+                        const long long ld1[1] = {en.V};
+                        if (gemv_group(en, m1, o1, ld1, 1, en.E, a, 0)) return -1;
                     }
                 }
                 return 0;
@@ -1379,6 +1400,7 @@ struct Scratch {
     QbQmvWork work{};
 };
 std::mutex g_mu;
+bool g_host_tc = false;   // host GEMV API: IQ4_XS at n <= 4 on tcgen05 (QB_TC=1); default: int8 mma.sync
 std::unordered_map<WKey, DevMat, WKeyHash> g_wcache;
 std::unordered_map<int, Scratch> g_scratch;
 
@@ -1386,7 +1408,11 @@ int scratch_get(Scratch*& s, size_t x_floats, size_t out_floats, int K) {
     int dev = 0;
     CK(cudaGetDevice(&dev));
     s = &g_scratch[dev];
-    if (!s->st) CK(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
+    if (!s->st) {
+        CK(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
+        const char* tc = getenv("QB_TC");
+        g_host_tc = tc && tc[0] == '1';
+    }
     if (x_floats > s->x_cap) {
         if (s->x) cudaFree(s->x);
         s->x_cap = std::max<size_t>(x_floats, 1 << 16);
@@ -1403,6 +1429,7 @@ int scratch_get(Scratch*& s, size_t x_floats, size_t out_floats, int K) {
         if (s->xb.xsum) cudaFree(s->xb.xsum);
         if (s->xb.xq) cudaFree(s->xb.xq);
         if (s->xb.xqscale) cudaFree(s->xb.xqscale);
+        if (s->xb.xtc) cudaFree(s->xb.xtc);
         s->k_cap = std::max<size_t>((size_t)K, 4096);
         const int kc = (int)((s->k_cap + 255) / 256 * 256);
         CK(cudaMalloc(&s->xb.xfrag, qb_xfrag_bytes(kc)));
@@ -1411,6 +1438,8 @@ int scratch_get(Scratch*& s, size_t x_floats, size_t out_floats, int K) {
         CK(cudaMemset(s->xb.xq, 0, qb_xq_bytes(kc)));
         CK(cudaMalloc(&s->xb.xscale, QB_MAX_TOK * (kc / 256) * 4));
         CK(cudaMalloc(&s->xb.xqscale, QB_MAX_TOK * (kc / 256) * 4));
+        CK(cudaMalloc(&s->xb.xtc, qb_xtc_bytes(kc)));
+        CK(cudaMemset(s->xb.xtc, 0, qb_xtc_bytes(kc)));
         CK(cudaMalloc(&s->xb.xsum, QB_MAX_TOK * (kc / 32) * 4));
     }
     if (!s->keys) {
@@ -1454,6 +1483,7 @@ int wcache_get(const gguf_tensor_info_t* W, const DevMat*& out) {
     if (it != g_wcache.end()) {
         if (it->second.fingerprint == fp) { out = &it->second; return 0; }
         cudaFree(it->second.w);   // same address, different weights: replace the device copy
+        if (it->second.w_tc) cudaFree(it->second.w_tc);
         g_wcache.erase(it);
     }
     DevMat m;
@@ -1472,6 +1502,10 @@ int wcache_get(const gguf_tensor_info_t* W, const DevMat*& out) {
         CK(cudaMemcpy(tmp, W->data, src_bytes, cudaMemcpyHostToDevice));
         CK(cudaMalloc(&m.w, qb_repacked_bytes(m.type, m.rows, m.K)));
         CK(qb_repack(m.type, tmp, m.rows, m.K, m.w, 0));
+        if (m.type == QB_IQ4_XS) {
+            CK(cudaMalloc(&m.w_tc, qb_repacked_bytes_tc(m.rows, m.K)));
+            CK(qb_repack_tc(tmp, m.rows, m.K, m.w_tc, 0));
+        }
         CK(cudaDeviceSynchronize());
         cudaFree(tmp);
     }
@@ -1500,7 +1534,18 @@ int gemv_host(const gguf_tensor_info_t* W, const float* x, uint64_t ldx, int n, 
         } else {
             if (scratch_work(s, M->rows)) return -1;
             QbXIn in{s->x, K, nullptr, K};
-            CK(qb_xprep(&in, 1, nn, 1e-6f, s->xb, qb_xprep_needs(M->type), s->st));
+            const bool tc = M->w_tc && nn <= 4 && g_host_tc;
+            CK(qb_xprep(&in, 1, nn, 1e-6f, s->xb, qb_xprep_needs(M->type, nn, tc ? 1 : 0), s->st));
+            if (tc) {
+                const int T0 = (int)(r0 / 128);   // start on a 128-row tile
+                QbQSeg seg;
+                seg.w = (const uint8_t*)M->w_tc + (size_t)T0 * (K / 256) * qb_repacked_bytes_tc(128, 256);
+                seg.out = s->out + (size_t)T0 * 128;
+                seg.ldo = M->rows;
+                seg.rows = (int)(r1 - (uint64_t)T0 * 128);
+                CK(qb_qmv_tc(&seg, 1, K, nn, s->xb, 0, (int)(r0 - (uint64_t)T0 * 128), (int)(r1 - (uint64_t)T0 * 128),
+                             s->work, s->st));
+            } else {
             QbQSeg seg;
             seg.w = (const uint8_t*)M->w + (size_t)t_lo * (K / qb_unit_cols(M->type)) * qb_unit_bytes(M->type);
             seg.out = s->out + (size_t)t_lo * QB_TILE;
@@ -1508,6 +1553,7 @@ int gemv_host(const gguf_tensor_info_t* W, const float* x, uint64_t ldx, int n, 
             seg.rows = (int)(r1 - (uint64_t)t_lo * QB_TILE);
             CK(qb_qmv(M->type, &seg, 1, K, nn, s->xb, 0, (int)(r0 - (uint64_t)t_lo * QB_TILE),
                       (int)(r1 - (uint64_t)t_lo * QB_TILE), s->work, s->st));
+            }
         }
         CK(cudaMemcpy2DAsync(out + (size_t)t0 * ldo + r0, ldo * 4, s->out + r0, (size_t)M->rows * 4, (size_t)(r1 - r0) * 4, nn,
                              cudaMemcpyDeviceToHost, s->st));

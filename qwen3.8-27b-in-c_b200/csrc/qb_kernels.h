@@ -22,10 +22,16 @@ struct QbQSeg {              // one matrix of a fused GEMV launch
 // wait gave up).
 struct QbQmvWork {
     float* partial;          // [max_warps][2][32][8]
+    float* gpartial;         // [max_warps][2][32][8] (per CTA, or per warp without CTA grouping)
     unsigned* counters;      // [max_pairs], zero-initialised
     unsigned* err;           // [1]
     int max_warps;
     int max_pairs;
+    // tcgen05 IQ4_XS path (qb_qmv_tc)
+    float* tc_partial;       // [max_tc_ctas][2][128][4]
+    unsigned* tc_counters;   // [max_tc_rows], zero-initialised
+    int max_tc_ctas;
+    long long max_tc_rows;   // rows of all fused matrices, rounded up to 128-row tiles
 };
 
 // Prepared activations of one GEMV input (written by qb_xprep, read by qb_qmv).
@@ -34,9 +40,10 @@ struct QbXBuf {
     float* xscale;           // [QB_MAX_TOK][K/256] power-of-two scale of xfrag
     float* xsum;             // [QB_MAX_TOK][K/32] plain column sums (Q4_K / Q5_K)
     uint2* xq;               // int8 digit mma B fragments (IQ4_XS), qb_xbuf_bytes
-    float* xqscale;          // [QB_MAX_TOK][K/256] power-of-two scale of xq
+    float* xqscale;          // [QB_MAX_TOK][K/256] power-of-two scale of xq and xtc
+    uint8_t* xtc;            // int8 digits as tcgen05 B tiles, 4 KB per 256 columns (N <= 4)
 };
-enum { QB_XP_F16 = 1, QB_XP_SUM = 2, QB_XP_I8 = 4 };   // qb_xprep outputs
+enum { QB_XP_F16 = 1, QB_XP_SUM = 2, QB_XP_I8 = 4, QB_XP_TC = 8 };   // qb_xprep outputs
 
 // ---- quantised GEMV (qb_quant.cu) ----
 size_t qb_repacked_bytes(int type, int rows, int K);
@@ -44,12 +51,23 @@ cudaError_t qb_repack(int type, const void* src_dev, int rows, int K, void* dst_
 // bytes of xfrag / xq for inputs of up to K columns
 size_t qb_xfrag_bytes(int K);
 size_t qb_xq_bytes(int K);
-// which qb_xprep outputs a matrix of this type reads
-int qb_xprep_needs(int type);
+size_t qb_xtc_bytes(int K);
+// which qb_xprep outputs a matrix of this type reads at N input vectors
+// (IQ4_XS: the tcgen05 tiles when N <= 4 and tc != 0, else the mma.sync fragments)
+int qb_xprep_needs(int type, int N = QB_MAX_TOK, int tc = 0);
 cudaError_t qb_xprep(const QbXIn* in, int nseg, int N, float eps, const QbXBuf& xb, int what, cudaStream_t st);
 cudaError_t qb_qmv(int type, const QbQSeg* segs, int nseg, int K, int N, const QbXBuf& xb, int accumulate,
                    int row_lo, int row_hi, const QbQmvWork& work, cudaStream_t st);
 cudaError_t qb_qmv_work_alloc(QbQmvWork& w, int max_pairs);
+
+// ---- IQ4_XS GEMV on tcgen05 (qb_qmv_tc.cu), N <= 4 ----
+size_t qb_repacked_bytes_tc(int rows, int K);
+cudaError_t qb_repack_tc(const void* src_dev, int rows, int K, void* dst_dev, cudaStream_t st);
+int qb_qmv_tc_max_ctas();
+size_t qb_qmv_tc_partial_floats(int max_ctas);
+// segs[i].w are qb_repack_tc layouts
+cudaError_t qb_qmv_tc(const QbQSeg* segs, int nseg, int K, int N, const QbXBuf& xb, int accumulate, int row_lo,
+                      int row_hi, const QbQmvWork& work, cudaStream_t st);
 void qb_qmv_work_free(QbQmvWork& w);
 cudaError_t qb_qmv_f32(const float* W, int rows, int K, const float* x, long long ldx, int N, float* out,
                        long long ldo, int accumulate, int row_lo, int row_hi, cudaStream_t st);

@@ -1,0 +1,399 @@
+// IQ4_XS GEMV on the sm_100a tcgen05 tensor cores, for N <= 4 input vectors
+// (the verify width k+1 = 4 and the single-token drafts).
+//
+// Reference: dot_iq4_xs_b / gemv_rows_batch, src/kernels.c:373-412, 570-599;
+// block format include/quant.h:56-62, values src/quant.c:30-32, 175-176.
+//
+// Data path per (128-row tile, 256-column block) stage:
+//   * a producer warp bulk-copies the stage's 17408 weight bytes and the
+//     block's 4 KB of activation digits into a shared-memory ring;
+//   * four decode warps, one thread per weight row, turn the row's 256 codes
+//     into int8 values (byte-permute table lookup) and store them to tensor
+//     memory: lane = row, 4 values per 32-bit column, 8 columns per 32-column
+//     sub-block;
+//   * one thread issues eight tcgen05.mma.kind::i8 (M 128, N 16, K 32), one
+//     per sub-block, each into its own 16 accumulator columns: A from tensor
+//     memory, B = the digits (token t, digit d at row 3t + d) from shared
+//     memory, exact int32 sums;
+//   * one stage later the decode threads read their row's accumulators back
+//     (tcgen05.ld), apply the 6-bit sub-block scales in int32, combine the
+//     digits (X = 65536 d0 + 256 d1 + d2) and the fp16 block scale in fp32.
+// The decode of stage r overlaps the MMAs of stage r-1.  Stages of all fused
+// matrices are split evenly over the CTAs (stream-K); a tile split across
+// CTAs is finished per row by the last contributing CTA, which sums the
+// partials in CTA order (deterministic).  Every wait is bounded; on a
+// time-out the kernel records an error, drains its copies and MMAs, frees
+// its tensor memory and returns.
+#include "qb_common.cuh"
+#include "qb_kernels.h"
+#include "qb_iq4.cuh"
+#include "qb_tc.cuh"
+
+namespace {
+
+constexpr int kRows = 128;                  // rows per tile = tensor-memory lanes
+constexpr int kUnit = kRows * 136;          // repacked bytes of one (tile, block)
+constexpr int kQsBytes = kRows * 128;       // [8 sub-blocks][128 rows][16 B]
+constexpr int kBBytes = 4096;               // activation digits of one block
+constexpr int kStage = kUnit + kBBytes;     // 21504
+constexpr int kRing = 4;
+constexpr int kDecodeWarps = 4;
+constexpr int kDecodeThreads = kDecodeWarps * 32;
+constexpr int kThreads = kDecodeThreads + 32;   // + producer warp
+constexpr int kCtasPerSm = 2;               // 2 x 256 tensor-memory columns = all 512
+constexpr uint32_t kCols = 256;             // A: 2 x 64 columns, D: 8 sub-blocks x 16 columns
+constexpr uint32_t kDCol = 128;
+constexpr int kHdr = 256;
+constexpr uint32_t kIdesc = idesc_i8(128, 16);
+#ifndef QB_TC_SLEEP_NS
+#define QB_TC_SLEEP_NS 2000
+#endif
+constexpr uint32_t kSleepNs = QB_TC_SLEEP_NS;   // suspend hint of the mbarrier waits (bounded: 2^16 tries)
+
+struct TcK {
+    const uint8_t* w[QB_MAX_SEG];   // tile-repacked weights of each fused matrix
+    float* out[QB_MAX_SEG];
+    long long ldo[QB_MAX_SEG];
+    int rows[QB_MAX_SEG];
+    int tile0[QB_MAX_SEG + 1];      // first tile of each matrix; tile0[nseg] = tiles
+    int nseg, nb, N, S, G;          // S = tiles * nb stages over G CTAs
+    const uint8_t* xb;              // activation digits, kBBytes per block
+    const float* xqscale;           // [QB_MAX_TOK][nb]
+    int accumulate, row_lo, row_hi;
+    float* partial;                 // [G][2][kRows][4]
+    unsigned* counters;             // [tiles][kRows], zero between launches
+    unsigned* err;
+};
+
+__device__ __forceinline__ int cta_s0(int S, int G, int c) { return (int)((long long)S * c / G); }
+__device__ __forceinline__ int stage_cta(int S, int G, int s) { return (int)(((long long)(s + 1) * G - 1) / S); }
+
+__device__ __forceinline__ int seg_of_tile(const TcK& p, int T) {
+    int sg = 0;
+#pragma unroll
+    for (int i = 1; i < QB_MAX_SEG; ++i)
+        if (i < p.nseg && T >= p.tile0[i]) sg = i;
+    return sg;
+}
+
+// row m of tile T is complete in this CTA's tot[]: store it, or combine the
+// split tile's per-CTA partials (last arriving CTA, CTA order)
+__device__ void finish_row(const TcK& p, int T, int cta, int s0, int s1, int m, const float (&tot)[4]) {
+    const int sg = seg_of_tile(p, T);
+    const int row = (T - p.tile0[sg]) * kRows + m;
+    auto store = [&](const float (&v)[4]) {
+        if (row >= p.rows[sg] || row < p.row_lo || row >= p.row_hi) return;
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+            if (t < p.N) {
+                float* dst = p.out[sg] + (size_t)t * p.ldo[sg] + row;
+                *dst = p.accumulate ? (*dst + v[t]) : v[t];
+            }
+    };
+    const int P0 = T * p.nb, P1 = P0 + p.nb;
+    if (s0 <= P0 && s1 >= P1) {
+        store(tot);
+        return;
+    }
+    const int piece = s0 > P0 ? 0 : 1;   // 0: the tile is this CTA's first (it started inside it)
+    *reinterpret_cast<float4*>(p.partial + (((size_t)cta * 2 + piece) * kRows + m) * 4) =
+        make_float4(tot[0], tot[1], tot[2], tot[3]);
+    __threadfence();
+    const int c_first = stage_cta(p.S, p.G, P0), c_last = stage_cta(p.S, p.G, P1 - 1);
+    unsigned* ctr = p.counters + (size_t)T * kRows + m;
+    const unsigned old = atomicAdd(ctr, 1u);
+    if ((int)old != c_last - c_first) return;
+    __threadfence();
+    float sum[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int c = c_first; c <= c_last; ++c) {
+        const int pc = cta_s0(p.S, p.G, c) > P0 ? 0 : 1;
+        const volatile float* v = p.partial + (((size_t)c * 2 + pc) * kRows + m) * 4;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) sum[t] += v[t];
+    }
+    store(sum);
+    *ctr = 0u;   // ready for the next launch
+}
+
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_tc_kernel(TcK p) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + kRing;
+    uint64_t* mma_done = empty + kRing;
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mma_done + 1);
+    volatile int* dec_abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
+    uint8_t* ring = smem + kHdr;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int cta = blockIdx.x;
+    const int s0 = cta_s0(p.S, p.G, cta), s1 = cta_s0(p.S, p.G, cta + 1);
+    const int n = s1 - s0;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kRing; ++i) {
+            mbar_init(full + i, 1);
+            mbar_init(empty + i, 1);
+        }
+        mbar_init(mma_done, 1);
+        *dec_abort = 0;
+        mbar_fence_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(tmem_holder, kCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_holder;
+    pdl_trigger();
+
+    if (warp == kDecodeWarps) {
+        // ------------------------------ producer ------------------------------
+        if (lane == 0 && n > 0) {
+            auto weights_of = [&](int s) -> const uint8_t* {
+                const int T = s / p.nb, b = s - T * p.nb;
+                const int sg = seg_of_tile(p, T);
+                return p.w[sg] + ((size_t)(T - p.tile0[sg]) * p.nb + b) * kUnit;
+            };
+            const int pre = n < kRing ? n : kRing;
+            // weights do not depend on the previous kernel: start streaming them before the wait
+            for (int r = 0; r < pre; ++r) {
+                mbar_expect_tx(full + r, kStage);
+                bulk_g2s(ring + r * kStage, weights_of(s0 + r), kUnit, full + r);
+            }
+            pdl_wait();   // the activation digits are written by the previous kernel
+            for (int r = 0; r < pre; ++r)
+                bulk_g2s(ring + r * kStage + kUnit, p.xb + (size_t)((s0 + r) % p.nb) * kBBytes, kBBytes, full + r);
+            int issued = pre;
+            for (int r = kRing; r < n; ++r) {
+                const int slot = r % kRing;
+                if (!mbar_wait_sleep(empty + slot, (uint32_t)((r / kRing) - 1) & 1u, kSleepNs)) {
+                    atomicExch(p.err, 3u);
+                    break;
+                }
+                const int s = s0 + r;
+                mbar_expect_tx(full + slot, kStage);
+                bulk_g2s(ring + slot * kStage, weights_of(s), kUnit, full + slot);
+                bulk_g2s(ring + slot * kStage + kUnit, p.xb + (size_t)(s % p.nb) * kBBytes, kBBytes, full + slot);
+                issued = r + 1;
+            }
+            // let every copy this CTA issued land before it may exit
+            for (int r = issued - kRing > 0 ? issued - kRing : 0; r < issued; ++r)
+                mbar_wait(full + r % kRing, (uint32_t)(r / kRing) & 1u, 1u << 20);
+        }
+    } else if (n > 0) {
+        // --------------------------- decode / epilogue ---------------------------
+        pdl_wait();   // the activation scales are written by the previous kernel
+        const int m = threadIdx.x;
+        const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+        float tot[4] = {0.f, 0.f, 0.f, 0.f};
+        int sc_prev[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        float d_prev = 0.f;
+        int last_mma = -1;
+        for (int r = 0; r <= n; ++r) {
+            int sc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            float d = 0.f;
+            // decode stage r into tensor-memory buffer r & 1 (the MMAs of stage r-2,
+            // which read it, completed before the epilogue of stage r-2)
+            if (r < n) {
+                const int slot = r % kRing;
+                if (!mbar_wait_sleep(full + slot, (uint32_t)(r / kRing) & 1u, kSleepNs)) {
+                    *dec_abort = 1;
+                } else {
+                    const uint8_t* u = ring + slot * kStage;
+                    uint32_t L0, L1;
+                    iq4_scale_bytes(lds64(u + kQsBytes + m * 8), L0, L1, d);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        sc[i] = ubyte(L0, i) - 32;
+                        sc[4 + i] = ubyte(L1, i) - 32;
+                    }
+                    const uint32_t abuf = tmem + lane_base + (uint32_t)((r & 1) * 64);
+#pragma unroll
+                    for (int sb = 0; sb < 8; ++sb) {
+                        const uint4 q = lds128(u + sb * (kRows * 16) + m * 16);
+                        uint32_t a[8];
+                        iq4_i8(q.x, a[0], a[1]);
+                        iq4_i8(q.y, a[2], a[3]);
+                        iq4_i8(q.z, a[4], a[5]);
+                        iq4_i8(q.w, a[6], a[7]);
+                        tmem_st8(abuf + (uint32_t)(sb * 8), a);
+                    }
+                    tmem_wait_st();
+                }
+            }
+            // epilogue of stage r-1
+            if (r >= 1 && !*dec_abort) {
+                const int rp = r - 1;
+                if (!mbar_wait_sleep(mma_done, (uint32_t)rp & 1u, kSleepNs)) {
+                    *dec_abort = 1;
+                } else {
+                    tc_fence_after();
+                    const uint32_t dbase = tmem + lane_base + kDCol;
+                    int acc[12];
+#pragma unroll
+                    for (int j = 0; j < 12; ++j) acc[j] = 0;
+#pragma unroll
+                    for (int sb = 0; sb < 8; sb += 2) {
+                        uint32_t v0[16], v1[16];
+                        tmem_ld16(dbase + (uint32_t)(sb * 16), v0);
+                        tmem_ld16(dbase + (uint32_t)((sb + 1) * 16), v1);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int j = 0; j < 12; ++j)
+                            acc[j] += sc_prev[sb] * (int)v0[j] + sc_prev[sb + 1] * (int)v1[j];
+                    }
+                    const int b_prev = (s0 + rp) % p.nb;
+#pragma unroll
+                    for (int t = 0; t < 4; ++t) {
+                        const float v = fmaf((float)acc[3 * t], 65536.f,
+                                             fmaf((float)acc[3 * t + 1], 256.f, (float)acc[3 * t + 2])) * d_prev;
+                        const float xs = t < p.N ? __ldg(p.xqscale + t * p.nb + b_prev) : 0.f;
+                        tot[t] = fmaf(xs, v, tot[t]);
+                    }
+                    if (threadIdx.x == 0) mbar_arrive(empty + rp % kRing);   // weights decoded, digits consumed
+                    const int s = s0 + rp;
+                    if ((s + 1) % p.nb == 0 || rp == n - 1) {
+                        finish_row(p, s / p.nb, cta, s0, s1, m, tot);
+#pragma unroll
+                        for (int t = 0; t < 4; ++t) tot[t] = 0.f;
+                    }
+                }
+            }
+            // every row of stage r is in tensor memory, every read of the accumulators is done
+            tc_fence_before();
+            named_bar_sync(1, kDecodeThreads);
+            if (*dec_abort) break;
+            if (r < n && threadIdx.x == 0) {
+                tc_fence_after();
+                const uint32_t a0 = tmem + (uint32_t)((r & 1) * 64);
+                const uint32_t bsm = smem_u32(ring + (r % kRing) * kStage + kUnit);
+#pragma unroll
+                for (int sb = 0; sb < 8; ++sb)
+                    tc_mma_i8(tmem + kDCol + (uint32_t)(sb * 16), a0 + (uint32_t)(sb * 8),
+                              smem_desc_kmajor(bsm + (uint32_t)(sb * 512), 128u, 256u), kIdesc, 0u);
+                tc_commit(mma_done);
+                last_mma = r;
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) sc_prev[i] = sc[i];
+            d_prev = d;
+        }
+        if (*dec_abort) {
+            if (threadIdx.x == 0) {
+                atomicExch(p.err, 4u);
+                if (last_mma >= 0) mbar_wait(mma_done, (uint32_t)last_mma & 1u, 1u << 20);
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 0) tmem_dealloc(tmem, kCols);
+}
+
+// ------------------------------- repack ---------------------------------------
+// GGUF block_iq4_xs rows -> per (128-row tile, 256-column block): qs as
+// [8 sub-blocks][128 rows][16 B], then [128 rows][8 B] scales in the
+// [A(4) d(2) Bh(2)] form of qb_iq4.cuh.  Rows past `rows` are zeros.
+__global__ void repack_tc_kernel(const uint8_t* __restrict__ src, int rows, int nb, int tiles,
+                                 uint8_t* __restrict__ dst) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;   // (tile, block, row)
+    if (i >= (long long)tiles * nb * kRows) return;
+    const int m = (int)(i % kRows);
+    const long long tb = i / kRows;
+    const int b = (int)(tb % nb), T = (int)(tb / nb);
+    const int r = T * kRows + m;
+    uint8_t* u = dst + (size_t)tb * kUnit;
+    if (r >= rows) {
+        for (int sb = 0; sb < 8; ++sb)
+            for (int j = 0; j < 16; ++j) u[sb * (kRows * 16) + m * 16 + j] = 0;
+        for (int j = 0; j < 8; ++j) u[kQsBytes + m * 8 + j] = 0;
+        return;
+    }
+    const uint8_t* blk = src + ((size_t)r * nb + b) * 136;
+    for (int sb = 0; sb < 8; ++sb)
+        for (int j = 0; j < 16; ++j) u[sb * (kRows * 16) + m * 16 + j] = blk[8 + 16 * sb + j];
+    const uint32_t sh = blk[2] | (blk[3] << 8);
+    const uint32_t sl = blk[4] | (blk[5] << 8) | (blk[6] << 16) | ((uint32_t)blk[7] << 24);
+    uint32_t ls[8];
+    for (int ib = 0; ib < 8; ++ib) ls[ib] = ((sl >> (4 * ib)) & 0xF) | (((sh >> (2 * ib)) & 3) << 4);
+    uint32_t A = 0, Bh = 0;
+    for (int k = 0; k < 4; ++k) A |= (ls[k] | ((ls[4 + k] & 3) << 6)) << (8 * k);
+    for (int k = 0; k < 4; ++k) Bh |= (ls[4 + k] >> 2) << (4 * k);
+    const uint32_t dd = blk[0] | (blk[1] << 8);
+    uint8_t* s = u + kQsBytes + m * 8;
+    for (int k = 0; k < 4; ++k) s[k] = (uint8_t)(A >> (8 * k));
+    s[4] = (uint8_t)dd;
+    s[5] = (uint8_t)(dd >> 8);
+    s[6] = (uint8_t)Bh;
+    s[7] = (uint8_t)(Bh >> 8);
+}
+
+}  // namespace
+
+size_t qb_repacked_bytes_tc(int rows, int K) {
+    if (K % 256) return 0;
+    return (size_t)((rows + kRows - 1) / kRows) * (K / 256) * kUnit;
+}
+
+cudaError_t qb_repack_tc(const void* src_dev, int rows, int K, void* dst_dev, cudaStream_t st) {
+    if (K % 256 || rows < 1) return cudaErrorInvalidValue;
+    const int nb = K / 256, tiles = (rows + kRows - 1) / kRows;
+    const long long n = (long long)tiles * nb * kRows;
+    repack_tc_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>((const uint8_t*)src_dev, rows, nb, tiles,
+                                                                    (uint8_t*)dst_dev);
+    return cudaGetLastError();
+}
+
+int qb_qmv_tc_max_ctas() {
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return sms * kCtasPerSm;
+}
+
+size_t qb_qmv_tc_partial_floats(int max_ctas) { return (size_t)max_ctas * 2 * kRows * 4; }
+
+cudaError_t qb_qmv_tc(const QbQSeg* segs, int nseg, int K, int N, const QbXBuf& xb, int accumulate, int row_lo,
+                      int row_hi, const QbQmvWork& work, cudaStream_t st) {
+    if (nseg < 1 || nseg > QB_MAX_SEG || N < 1 || N > 4 || K % 256 || !xb.xtc || !xb.xqscale)
+        return cudaErrorInvalidValue;
+    TcK p = {};
+    int tiles = 0;
+    for (int i = 0; i < nseg; ++i) {
+        p.w[i] = (const uint8_t*)segs[i].w;
+        p.out[i] = segs[i].out;
+        p.ldo[i] = segs[i].ldo;
+        p.rows[i] = segs[i].rows;
+        p.tile0[i] = tiles;
+        tiles += (segs[i].rows + kRows - 1) / kRows;
+    }
+    p.tile0[nseg] = tiles;
+    if ((long long)tiles * kRows > work.max_tc_rows) return cudaErrorInvalidValue;
+    p.nseg = nseg;
+    p.nb = K / 256;
+    p.N = N;
+    const long long S = (long long)tiles * p.nb;
+    if (S >= (1ll << 30)) return cudaErrorInvalidValue;
+    p.S = (int)S;
+    int G = qb_qmv_tc_max_ctas();
+    if (G > work.max_tc_ctas) G = work.max_tc_ctas;
+    if (G > p.S) G = p.S;
+    p.G = G;
+    p.xb = xb.xtc;
+    p.xqscale = xb.xqscale;
+    p.accumulate = accumulate;
+    p.row_lo = row_lo;
+    p.row_hi = row_hi;
+    p.partial = work.tc_partial;
+    p.counters = work.tc_counters;
+    p.err = work.err;
+    const size_t smem = kHdr + (size_t)kRing * kStage;
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(qmv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
+    return qb_launch(qmv_tc_kernel, dim3(G), dim3(kThreads), smem, st, p);
+}

@@ -41,6 +41,7 @@
 #include "qb_common.cuh"
 #include "qb_kernels.h"
 #include "qb_xprep.cuh"
+#include "qb_iq4.cuh"
 
 namespace {
 
@@ -62,6 +63,7 @@ constexpr int kSmemBudget = QB_QMV_SMEM_KB * 1024;   // per CTA
 #define QB_QMV_MIN_STAGES 4
 #endif
 constexpr int kMinStagesPerWarp = QB_QMV_MIN_STAGES;
+constexpr int kLocalPairs = 64;             // pairs one CTA's stage range may touch (else no level 1)
 constexpr int kRingOff = 512;                // full barriers (8 warps x 8 slots x 8 B), then the rings
 
 // 4 unsigned bytes -> two half2 (1024 + b0, 1024 + b1), (1024 + b2, 1024 + b3)
@@ -111,18 +113,11 @@ __device__ __forceinline__ int col_token(int ct, int col) {
 // terms that are not scaled by the activation scale (Q4_K / Q5_K mins).
 
 // IQ4_XS tile-block: qs 2048 B (4 chunks x 32 lanes x 16 B) + 16 rows x 8 B
-// scales stored as [A(4) d(2) Bh(2)]: A byte i = ls_i | (ls_{4+i} & 3) << 6,
-// Bh nibble j = ls_{4+j} >> 2 (a byte-aligned rearrangement of the block's
-// scales_l / scales_h; same 8 bytes).
+// of scales (layout in qb_iq4.cuh).
 constexpr int kIq4Tile = 16 * 136;
 
 __device__ __forceinline__ void iq4_scales(const uint8_t* u, int row, uint32_t& L0, uint32_t& L1, float& d) {
-    const uint2 v = lds64(u + 2048 + row * 8);
-    L0 = v.x & 0x3F3F3F3Fu;
-    const uint32_t x = prmt(v.y, 0u, 0x3322u);
-    const uint32_t nib = (x & 0x000F000Fu) | ((x >> 4) & 0x0F000F00u);
-    L1 = ((v.x >> 6) & 0x03030303u) | (nib << 2);
-    d = h2f_bits(v.y);
+    iq4_scale_bytes(lds64(u + 2048 + row * 8), L0, L1, d);
 }
 
 // ---- IQ4_XS on the int8 tensor-core path (mma m16n8k32 s8 -> s32) ----
@@ -142,24 +137,6 @@ __device__ __forceinline__ void iq4_scales(const uint8_t* u, int row, uint32_t& 
 // Sub-block scales by summation by parts: the mma chains its accumulator, so
 // after sub-block j it holds R_j = sum_{i<=j} C_i, and
 // sum_j s_j C_j = sum_{j<7} (s_j - s_{j+1}) R_j + s_7 R_7 with s_j = ls_j - 32.
-constexpr uint32_t kIq4I8T0 = 0xBFAD9881u;   // -127 -104  -83  -65
-constexpr uint32_t kIq4I8T1 = 0xF6EADDCFu;   //  -49  -35  -22  -10
-constexpr uint32_t kIq4I8T2 = 0x26190D01u;   //    1   13   25   38
-constexpr uint32_t kIq4I8T3 = 0x71594535u;   //   53   69   89  113
-
-__device__ __forceinline__ void iq4_i8(uint32_t w, uint32_t& lo, uint32_t& hi) {
-    const uint32_t idx = w & 0x77777777u;                         // table index, code bit 3 cleared
-    const uint32_t sel = ((w >> 1) & 0x44444444u) | 0x32103210u;  // code bit 3 picks the upper table
-    const uint32_t idxh = idx >> 16, selh = sel >> 16;
-    lo = prmt(prmt(kIq4I8T0, kIq4I8T1, idx), prmt(kIq4I8T2, kIq4I8T3, idx), sel);
-    hi = prmt(prmt(kIq4I8T0, kIq4I8T1, idxh), prmt(kIq4I8T2, kIq4I8T3, idxh), selh);
-}
-
-// byte i of w, sign-extended
-__device__ __forceinline__ int sbyte(uint32_t w, int i) {
-    return (int)prmt(w, 0u, (uint32_t)(i | ((8 | i) << 4) | ((8 | i) << 8) | ((8 | i) << 12)));
-}
-
 // B fragments of sub-block sb of a block
 template <int NTI>
 __device__ __forceinline__ void load_bq(uint2 (&b)[NTI], const uint2* __restrict__ xq, int sb, int lane) {
@@ -453,8 +430,10 @@ struct QmvK {
     const float* xqscale;
     int accumulate;
     int row_lo, row_hi;
-    float* partial;              // [Wt][2][32][8]
+    float* partial;              // [Wt][2][32][8] warp partials of split pairs
+    float* gpartial;             // [Wt / group + 1][2][32][8] group partials
     unsigned* counters;          // [pairs]
+    int group;                   // warps combined in shared memory before the device-wide combine
     unsigned* err;
 };
 
@@ -468,7 +447,7 @@ __device__ __forceinline__ int stage_owner(int S, int Wt, int s) {
 // o[t][i], i = (row g tok 2c, row g tok 2c+1, row g8 tok 2c, row g8 tok 2c+1) of
 // tile t; lanes with active == false hold nothing to store.
 __device__ __forceinline__ void finish_pair(const QmvK& p, int pair, int gw, int s0, int s1, const float (&o)[2][4],
-                                            bool active, int lane) {
+                                            bool active, int lane, unsigned* lcnt, int grp_pair0) {
     int si = 0;
 #pragma unroll
     for (int s = 1; s < QB_MAX_SEG; ++s)
@@ -494,30 +473,73 @@ __device__ __forceinline__ void finish_pair(const QmvK& p, int pair, int gw, int
                 for (int i = 0; i < 4; ++i) store(t, i, o[t][i]);
         return;
     }
-    // split pair: piece 0 if this warp started inside the pair (its first pair), else 1 (its last)
-    const int piece = s0 >= P0 ? 0 : 1;
-    float* slot = p.partial + ((size_t)gw * 2 + piece) * 256;
+    // Split pair.  A contributor's piece is 0 if it started inside the pair
+    // (the pair is its first), 1 if it started before (the pair is its last).
     auto pidx = [&](int t, int i) { return (t * 16 + g + ((i & 2) ? 8 : 0)) * 8 + ((i & 1) ? t1 : t0); };
+    auto piece_of = [&](int first_warp) { return warp_s0(p.S, p.Wt, first_warp) >= P0 ? 0 : 1; };
+    const int G = p.group;   // warps combined through shared memory first (8 = a CTA, 1 = none)
+    const int w_first = stage_owner(p.S, p.Wt, P0), w_last = stage_owner(p.S, p.Wt, P1 - 1);
+    const int grp = gw / G;
+    const int lw_first = max(w_first, grp * G), lw_last = min(w_last, grp * G + G - 1);
+    float v[2][4];
+    if (lw_first == lw_last) {
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[t][i] = o[t][i];
+    } else {
+        // level 1: the group's warps, block-scope ordering, last arrival sums in warp order
+        float* slot = p.partial + ((size_t)gw * 2 + piece_of(gw)) * 256;
+        if (active)
+#pragma unroll
+            for (int t = 0; t < 2; ++t)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) slot[pidx(t, i)] = o[t][i];
+        __threadfence_block();
+        __syncwarp();
+        unsigned old = 0;
+        if (lane == 0) old = atomicAdd(lcnt + (pair - grp_pair0), 1u);
+        old = __shfl_sync(0xffffffffu, old, 0);
+        if ((int)old != lw_last - lw_first) return;
+        __threadfence_block();
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[t][i] = 0.f;
+        for (int w = lw_first; w <= lw_last; ++w) {
+            const volatile float* sl = p.partial + ((size_t)w * 2 + piece_of(w)) * 256;
+#pragma unroll
+            for (int t = 0; t < 2; ++t)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) v[t][i] += sl[pidx(t, i)];
+        }
+    }
+    const int g_first = w_first / G, g_last = w_last / G;
+    if (g_first == g_last) {
+        if (active)
+#pragma unroll
+            for (int t = 0; t < 2; ++t)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) store(t, i, v[t][i]);
+        return;
+    }
+    // level 2: the groups, device-scope ordering, last arrival sums in group order
+    float* gslot = p.gpartial + ((size_t)grp * 2 + piece_of(grp * G)) * 256;
     if (active)
 #pragma unroll
         for (int t = 0; t < 2; ++t)
 #pragma unroll
-            for (int i = 0; i < 4; ++i) slot[pidx(t, i)] = o[t][i];
+            for (int i = 0; i < 4; ++i) gslot[pidx(t, i)] = v[t][i];
     __threadfence();
     __syncwarp();
-    const int w_first = stage_owner(p.S, p.Wt, P0), w_last = stage_owner(p.S, p.Wt, P1 - 1);
-    const int contributors = w_last - w_first + 1;
     unsigned old = 0;
     if (lane == 0) old = atomicAdd(p.counters + pair, 1u);
     old = __shfl_sync(0xffffffffu, old, 0);
-    if ((int)old != contributors - 1) return;
+    if ((int)old != g_last - g_first) return;
     __threadfence();
-    // the first contributor started before the pair unless it starts exactly at P0
-    const int first_piece = warp_s0(p.S, p.Wt, w_first) == P0 ? 0 : 1;
     float sum[2][4] = {};
-    for (int w = w_first; w <= w_last; ++w) {
-        const int pc = w == w_first ? first_piece : 0;
-        const volatile float* sl = p.partial + ((size_t)w * 2 + pc) * 256;
+    for (int gg = g_first; gg <= g_last; ++gg) {
+        const volatile float* sl = p.gpartial + ((size_t)gg * 2 + piece_of(gg * G)) * 256;
 #pragma unroll
         for (int t = 0; t < 2; ++t)
 #pragma unroll
@@ -584,8 +606,13 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_kernel(QmvK p) {
     __syncwarp();
     pdl_trigger();
 
+    // per-CTA arrival counters of the pairs its warps share (level 1 of the split-pair combine)
+    __shared__ unsigned s_lcnt[kLocalPairs];
+    for (int i = threadIdx.x; i < kLocalPairs; i += kThreads) s_lcnt[i] = 0u;
+    __syncthreads();
     const int gw = blockIdx.x * kConsumers + warp;
     if (gw >= p.Wt) return;
+    const int grp_pair0 = warp_s0(p.S, p.Wt, (gw / p.group) * p.group) / p.nb;
     const int s0 = warp_s0(p.S, p.Wt, gw), s1 = warp_s0(p.S, p.Wt, gw + 1);
     const int n = s1 - s0;
     // producer cursor (lane 0): source of the next stage, its block, pairs left in the segment
@@ -634,7 +661,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_kernel(QmvK p) {
         bool active;
         if (I8) pair_out_i8<NT>(tk, o, active, lane);
         else pair_out_f16<NT>(acc, o, active, lane);
-        finish_pair(p, pair, gw, s0, s1, o, active, lane);
+        finish_pair(p, pair, gw, s0, s1, o, active, lane, s_lcnt, grp_pair0);
     };
     reset();
     const int c = lane & 3;
@@ -983,9 +1010,11 @@ cudaError_t qb_repack(int type, const void* src_dev, int rows, int K, void* dst_
 size_t qb_xfrag_bytes(int K) { return (size_t)(K + 255) / 256 * 256 / 16 * 2 * 32 * sizeof(uint2); }
 size_t qb_xq_bytes(int K) { return (size_t)(K + 255) / 256 * 256 / 32 * 3 * 32 * sizeof(uint2); }
 
-int qb_xprep_needs(int type) {
+size_t qb_xtc_bytes(int K) { return (size_t)(K + 255) / 256 * 4096; }
+
+int qb_xprep_needs(int type, int N, int tc) {
     switch (type) {
-    case QB_IQ4_XS: return QB_XP_I8;
+    case QB_IQ4_XS: return (tc && N <= 4) ? QB_XP_TC : QB_XP_I8;
     case QB_Q4_K:
     case QB_Q5_K: return QB_XP_F16 | QB_XP_SUM;
     case QB_Q6_K:
@@ -1007,7 +1036,7 @@ cudaError_t qb_xprep(const QbXIn* in, int nseg, int N, float eps, const QbXBuf& 
         K += in[i].len;
     }
     if (((what & QB_XP_F16) && (!xb.xfrag || !xb.xscale)) || ((what & QB_XP_SUM) && !xb.xsum) ||
-        ((what & QB_XP_I8) && (!xb.xq || !xb.xqscale)))
+        ((what & QB_XP_I8) && (!xb.xq || !xb.xqscale)) || ((what & QB_XP_TC) && (!xb.xtc || !xb.xqscale || N > 4)))
         return cudaErrorInvalidValue;
     const int nb = K / 256;
     return qb_launch(xprep_kernel, dim3((nb + 7) / 8, N), dim3(256), 0, st, s[0], s[1], nseg, N, eps, xb, what);
@@ -1063,7 +1092,7 @@ cudaError_t qb_qmv(int type, const QbQSeg* segs, int nseg, int K, int N, const Q
     p.xsum = xb.xsum;
     p.xq = xb.xq;
     p.xqscale = xb.xqscale;
-    const int need = qb_xprep_needs(type);
+    const int need = qb_xprep_needs(type, N, 0);
     if (((need & QB_XP_F16) && (!p.xfrag || !p.xscale)) || ((need & QB_XP_SUM) && !p.xsum) ||
         ((need & QB_XP_I8) && (!p.xq || !p.xqscale)))
         return cudaErrorInvalidValue;
@@ -1071,7 +1100,12 @@ cudaError_t qb_qmv(int type, const QbQSeg* segs, int nseg, int K, int N, const Q
     p.row_lo = row_lo;
     p.row_hi = row_hi;
     p.partial = work.partial;
+    p.gpartial = work.gpartial;
     p.counters = work.counters;
+    {   // CTA-level combine when a CTA's stage range touches at most kLocalPairs pairs
+        const long long per_cta = ((long long)p.S * kConsumers + p.Wt - 1) / p.Wt;   // stages of 8 warps
+        p.group = per_cta / p.nb + 2 <= kLocalPairs ? kConsumers : 1;
+    }
     p.err = work.err;
     const bool nt2 = N > 4;
     cudaError_t e = cudaSuccess;
@@ -1105,15 +1139,25 @@ cudaError_t qb_qmv_work_alloc(QbQmvWork& w, int max_pairs) {
     w.max_pairs = max_pairs;
     cudaError_t e;
     if ((e = cudaMalloc(&w.partial, (size_t)w.max_warps * 2 * 256 * sizeof(float))) != cudaSuccess) return e;
+    if ((e = cudaMalloc(&w.gpartial, (size_t)w.max_warps * 2 * 256 * sizeof(float))) != cudaSuccess) return e;
     if ((e = cudaMalloc(&w.counters, (size_t)max_pairs * sizeof(unsigned))) != cudaSuccess) return e;
     if ((e = cudaMalloc(&w.err, sizeof(unsigned))) != cudaSuccess) return e;
     if ((e = cudaMemset(w.counters, 0, (size_t)max_pairs * sizeof(unsigned))) != cudaSuccess) return e;
+    w.max_tc_ctas = qb_qmv_tc_max_ctas();
+    w.max_tc_rows = (long long)max_pairs * 32 + 128 * QB_MAX_SEG;   // every fused matrix rounds up to a tile
+    if ((e = cudaMalloc(&w.tc_partial, qb_qmv_tc_partial_floats(w.max_tc_ctas) * sizeof(float))) != cudaSuccess)
+        return e;
+    if ((e = cudaMalloc(&w.tc_counters, (size_t)w.max_tc_rows * sizeof(unsigned))) != cudaSuccess) return e;
+    if ((e = cudaMemset(w.tc_counters, 0, (size_t)w.max_tc_rows * sizeof(unsigned))) != cudaSuccess) return e;
     if ((e = cudaMemset(w.err, 0, sizeof(unsigned))) != cudaSuccess) return e;
     return cudaDeviceSynchronize();
 }
 
 void qb_qmv_work_free(QbQmvWork& w) {
     if (w.partial) cudaFree(w.partial);
+    if (w.gpartial) cudaFree(w.gpartial);
+    if (w.tc_partial) cudaFree(w.tc_partial);
+    if (w.tc_counters) cudaFree(w.tc_counters);
     if (w.counters) cudaFree(w.counters);
     if (w.err) cudaFree(w.err);
     w = QbQmvWork{};

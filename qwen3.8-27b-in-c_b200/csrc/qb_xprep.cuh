@@ -60,7 +60,7 @@ __device__ __forceinline__ void xprep_emit(const float (&v)[8], int t, int b, in
             if ((lane & 7) == 0) xb.xsum[t * (K >> 5) + sb] = ps;
         }
     }
-    if (what & QB_XP_I8) {
+    if (what & (QB_XP_I8 | QB_XP_TC)) {
         // X = rint(x * 2^e) with |X| <= 2^22, as balanced int8 digits X = 65536 d0 + 256 d1 + d2
         // (|d0| <= 64).  Lane 8j + c (c < 4) holds elements 4c..4c+3 of sub-block j and
         // lane 8j + c + 4 elements 16+4c..16+4c+3: together one mma B register pair.
@@ -103,7 +103,15 @@ __device__ __forceinline__ void xprep_emit(const float (&v)[8], int t, int b, in
                     uint2 bv;
                     bv.x = prmt(dg[dgi], other, 0x5140u);   // (4c, 4c+16, 4c+1, 4c+17)
                     bv.y = prmt(dg[dgi], other, 0x7362u);   // (4c+2, 4c+18, 4c+3, 4c+19)
-                    xb.xq[((size_t)kb * NTI + dnt[dgi]) * 32 + dcol[dgi] * 4 + c] = bv;
+                    if (what & QB_XP_I8) xb.xq[((size_t)kb * NTI + dnt[dgi]) * 32 + dcol[dgi] * 4 + c] = bv;
+                    if ((what & QB_XP_TC) && t < 4) {
+                        // tcgen05 B tile of the sub-block: row n = 3t + digit, 32 k bytes in the
+                        // order above; K-major core matrices of 8 rows x 16 B, K chunks 128 B apart,
+                        // 8-row groups 256 B apart
+                        const int nrow = 3 * t + dgi;
+                        *reinterpret_cast<uint2*>(xb.xtc + (size_t)kb * 512 + (c >> 1) * 128 + (nrow >> 3) * 256 +
+                                                  (nrow & 7) * 16 + (c & 1) * 8) = bv;
+                    }
                 }
             }
         }
