@@ -302,6 +302,7 @@ struct Engine {
     QbXBuf xb{};                          // prepared GEMV activations
     bool use_tc = false;                  // IQ4_XS at N <= 4 on tcgen05 (QB_TC=1); default: int8 mma.sync
     float* attn_po = nullptr;             // attention chunk partials (qb_attn_decode)
+    float2* gates = nullptr;              // DeltaNet (beta, decay) per (token, v-head)
     float2* attn_pml = nullptr;
     unsigned long long* keys = nullptr;   // [2][QB_MAX_TOK]: backbone, mtp
     QbQmvWork work{};
@@ -593,6 +594,7 @@ int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
         e.attn_pml = (float2*)e.dalloc(q_rows * sizeof(float2));
         if (!e.attn_po || !e.attn_pml) { set_err(-2, "attention scratch alloc"); return -1; }
     }
+    e.gates = (float2*)e.dalloc((size_t)T8 * 256 * sizeof(float2));
     e.keys = (unsigned long long*)e.dalloc(2 * T8 * sizeof(unsigned long long));
     e.ctrl = (QbCtrl*)e.dalloc(sizeof(QbCtrl));
     if (!e.bx || !e.logits || !e.xb.xfrag || !e.xb.xq || !e.ctrl || !e.emb || !e.keys) {
@@ -704,10 +706,9 @@ int gdn_block(Engine& e, const LayerW& l, int B, int ckpt) {
     float* conv = e.conv_slots + (size_t)l.ridx * e.conv_layer;
     float* ssm = e.ssm_slots + (size_t)l.ridx * e.ssm_layer;
     CK(qb_gdn_conv(e.qkv, e.ld_qkv, d.conv_dim, B, l.conv_w, conv, e.conv_slot_stride, &e.ctrl->cur_slot, ckpt,
-                   e.qkvc, e.ld_qkv, e.st));
-    CK(qb_gdn_recur(e.qkvc, e.ld_qkv, e.beta, e.alpha, 256, l.dt_bias, l.ssm_a, d.n_k_heads, d.n_v_heads,
-                    d.head_k_dim, B, e.eps, ssm, e.ssm_slot_stride, &e.ctrl->cur_slot, ckpt, e.o, d.d_inner,
-                    e.st));
+                   e.qkvc, e.ld_qkv, e.beta, e.alpha, 256, l.dt_bias, l.ssm_a, d.n_v_heads, e.gates, e.st));
+    CK(qb_gdn_recur(e.qkvc, e.ld_qkv, e.gates, d.n_k_heads, d.n_v_heads, d.head_k_dim, B, e.eps, ssm,
+                    e.ssm_slot_stride, &e.ctrl->cur_slot, ckpt, e.o, d.d_inner, e.st));
     if (d.head_v_dim == 128 && d.n_v_heads % 2 == 0) {
         CK(qb_gdn_out_xprep(e.o, e.z, d.d_inner, l.ssm_norm, d.n_v_heads, d.head_v_dim, B, e.eps, e.y, e.xb,
                             xp_needs(e, {&l.ssm_out}, B), e.st));

@@ -77,13 +77,14 @@ struct QbCtrl;   // device control block (qb_engine.h)
 
 cudaError_t qb_embed(int type, const void* tok_embd, int n_embd, const uint32_t* tokens, int B, float* out,
                      long long ldo, cudaStream_t st);
+// conv1d + SiLU of all channels, plus the recurrence gates (beta, decay) per (token, v-head)
 cudaError_t qb_gdn_conv(const float* qkv, long long ld_qkv, int conv_dim, int B, const float* conv_w,
                         float* state_slots, size_t slot_stride, const uint32_t* cur_slot, int ckpt,
-                        float* out, long long ld_out, cudaStream_t st);
-cudaError_t qb_gdn_recur(const float* qkvc, long long ld_qkvc, const float* beta, const float* alpha,
-                         long long ld_ba, const float* dt_bias, const float* ssm_a, int n_k, int n_v,
-                         int dk, int B, float eps, float* state_slots, size_t slot_stride,
-                         const uint32_t* cur_slot, int ckpt, float* out, long long ld_out, cudaStream_t st);
+                        float* out, long long ld_out, const float* beta, const float* alpha, long long ld_ba,
+                        const float* dt_bias, const float* ssm_a, int n_v, float2* gates, cudaStream_t st);
+cudaError_t qb_gdn_recur(const float* qkvc, long long ld_qkvc, const float2* gates, int n_k, int n_v, int dk, int B,
+                         float eps, float* state_slots, size_t slot_stride, const uint32_t* cur_slot, int ckpt,
+                         float* out, long long ld_out, cudaStream_t st);
 cudaError_t qb_gdn_out(const float* o, const float* z, long long ld, const float* norm_w, int n_v, int dv,
                        int B, float eps, float* y, cudaStream_t st);
 cudaError_t qb_attn_prep(float* q, long long ldq, const float* kv, long long ldkv, const float* q_norm,

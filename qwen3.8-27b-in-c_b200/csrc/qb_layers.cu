@@ -150,10 +150,21 @@ __global__ void embed_kernel(int type, const uint8_t* __restrict__ E, int n, con
 __global__ void gdn_conv_kernel(const float* __restrict__ qkv, long long ld_qkv, int conv_dim, int B,
                                 const float* __restrict__ w, float* __restrict__ slots, size_t slot_stride,
                                 const uint32_t* __restrict__ cur_slot, int ckpt, float* __restrict__ out,
-                                long long ld_out) {
+                                long long ld_out, const float* __restrict__ beta, const float* __restrict__ alpha,
+                                long long ld_ba, const float* __restrict__ dt_bias, const float* __restrict__ ssm_a,
+                                int n_v, float2* __restrict__ gates) {
     pdl_wait();
     pdl_trigger();
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c < n_v * B) {
+        // per (token, v-head) gates of the recurrence (src/model.c:494-500):
+        // beta = 1/(1+e^-b), decay = e^(A * softplus(a + dt_bias)), softplus = x > 30 ? x : log1p(e^x)
+        const int b = c / n_v, h = c - b * n_v;
+        const float bs = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf_cr(-beta[(size_t)b * ld_ba + h])));
+        const float a_raw = __fadd_rn(alpha[(size_t)b * ld_ba + h], dt_bias[h]);
+        const float a_sp = a_raw > 30.0f ? a_raw : log1pf_cr(expf_cr(a_raw));
+        gates[c] = make_float2(bs, expf_cr(__fmul_rn(ssm_a[h], a_sp)));
+    }
     if (c >= conv_dim) return;
     const int cur = (int)*cur_slot;
     const float4 s0 = *reinterpret_cast<const float4*>(slots + (size_t)cur * slot_stride + (size_t)c * 4);
@@ -189,9 +200,8 @@ __global__ void gdn_conv_kernel(const float* __restrict__ qkv, long long ld_qkv,
 constexpr int kDK = 128;
 
 __global__ void __launch_bounds__(128) gdn_recur_kernel(
-    const float* __restrict__ qkvc, long long ld_qkvc, const float* __restrict__ beta,
-    const float* __restrict__ alpha, long long ld_ba, const float* __restrict__ dt_bias,
-    const float* __restrict__ ssm_a, int n_k, int n_v, int B, float eps, float* __restrict__ slots,
+    const float* __restrict__ qkvc, long long ld_qkvc, const float2* __restrict__ gates, int n_k, int n_v, int B,
+    float eps, float* __restrict__ slots,
     size_t slot_stride, const uint32_t* __restrict__ cur_slot, int ckpt, float* __restrict__ out,
     long long ld_out) {
     pdl_wait();
@@ -235,10 +245,9 @@ __global__ void __launch_bounds__(128) gdn_recur_kernel(
         const float kq = hsum8(acc);
         if (act && l8 == 0) {
             kq_s[b] = kq;
-            beta_s[b] = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf_cr(-beta[(size_t)b * ld_ba + h])));
-            const float a_raw = __fadd_rn(alpha[(size_t)b * ld_ba + h], dt_bias[h]);
-            const float a_sp = a_raw > 30.0f ? a_raw : log1pf_cr(expf_cr(a_raw));
-            decay_s[b] = expf_cr(__fmul_rn(ssm_a[h], a_sp));
+            const float2 gt = gates[(size_t)b * n_v + h];   // gdn_conv_kernel
+            beta_s[b] = gt.x;
+            decay_s[b] = gt.y;
         }
     }
     __syncthreads();
@@ -775,20 +784,20 @@ cudaError_t qb_embed(int type, const void* tok_embd, int n_embd, const uint32_t*
 
 cudaError_t qb_gdn_conv(const float* qkv, long long ld_qkv, int conv_dim, int B, const float* conv_w,
                         float* state_slots, size_t slot_stride, const uint32_t* cur_slot, int ckpt,
-                        float* out, long long ld_out, cudaStream_t st) {
-    qb_launch(gdn_conv_kernel, dim3((conv_dim + 127) / 128), dim3(128), 0, st, qkv, ld_qkv, conv_dim, B, conv_w, state_slots,
-                                                            slot_stride, cur_slot, ckpt, out, ld_out);
+                        float* out, long long ld_out, const float* beta, const float* alpha, long long ld_ba,
+                        const float* dt_bias, const float* ssm_a, int n_v, float2* gates, cudaStream_t st) {
+    const int threads = conv_dim > n_v * B ? conv_dim : n_v * B;
+    qb_launch(gdn_conv_kernel, dim3((threads + 127) / 128), dim3(128), 0, st, qkv, ld_qkv, conv_dim, B, conv_w,
+              state_slots, slot_stride, cur_slot, ckpt, out, ld_out, beta, alpha, ld_ba, dt_bias, ssm_a, n_v, gates);
     return cudaGetLastError();
 }
 
-cudaError_t qb_gdn_recur(const float* qkvc, long long ld_qkvc, const float* beta, const float* alpha,
-                         long long ld_ba, const float* dt_bias, const float* ssm_a, int n_k, int n_v,
-                         int dk, int B, float eps, float* state_slots, size_t slot_stride,
-                         const uint32_t* cur_slot, int ckpt, float* out, long long ld_out, cudaStream_t st) {
+cudaError_t qb_gdn_recur(const float* qkvc, long long ld_qkvc, const float2* gates, int n_k, int n_v, int dk, int B,
+                         float eps, float* state_slots, size_t slot_stride, const uint32_t* cur_slot, int ckpt,
+                         float* out, long long ld_out, cudaStream_t st) {
     if (dk != kDK || B > QB_MAX_TOK) return cudaErrorInvalidValue;
-    qb_launch(gdn_recur_kernel, dim3(n_v, kDK / 16), dim3(128), 0, st, qkvc, ld_qkvc, beta, alpha, ld_ba, dt_bias, ssm_a,
-                                                          n_k, n_v, B, eps, state_slots, slot_stride, cur_slot,
-                                                          ckpt, out, ld_out);
+    qb_launch(gdn_recur_kernel, dim3(n_v, kDK / 16), dim3(128), 0, st, qkvc, ld_qkvc, gates, n_k, n_v, B, eps,
+              state_slots, slot_stride, cur_slot, ckpt, out, ld_out);
     return cudaGetLastError();
 }
 

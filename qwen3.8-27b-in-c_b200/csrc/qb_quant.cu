@@ -941,42 +941,46 @@ __global__ void __launch_bounds__(256) xprep_kernel(XSeg s0, XSeg s1, int nseg, 
     const int nb = K >> 8;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
     __shared__ float sh[32];
-    float inv[2] = {1.f, 1.f};
-    const int b_first = blockIdx.x * nw;
-    for (int si = 0; si < nseg; ++si) {
-        const XSeg& S = si ? s1 : s0;
-        if (!S.w) continue;
-        const float* x = S.x + (size_t)t * S.ldx;
-        float ss = 0.f;
-        for (int i = threadIdx.x * 4; i < S.len; i += blockDim.x * 4) {
-            const float4 v = *reinterpret_cast<const float4*>(x + i);
-            ss = fmaf(v.x, v.x, ss);
-            ss = fmaf(v.y, v.y, ss);
-            ss = fmaf(v.z, v.z, ss);
-            ss = fmaf(v.w, v.w, ss);
-        }
-        ss = block_sum(ss, sh);
-        inv[si] = 1.0f / sqrtf(ss / (float)S.len + eps);
-    }
-    const int b = b_first + warp;
-    if (b >= nb) return;
+    // this warp's block: its loads go out before the row reductions (one round trip, not two)
+    const int b = blockIdx.x * nw + warp;
+    const bool has_block = b < nb;
     const int col0 = b * 256;
     const int si = (nseg > 1 && col0 >= s0.len) ? 1 : 0;
     const XSeg& S = si ? s1 : s0;
     const int lc0 = col0 - (si ? s0.len : 0);
-    const float* x = S.x + (size_t)t * S.ldx + lc0;
-    float v[8];
+    float v[8], wv[8];
+    if (has_block) {
+        const float* x = S.x + (size_t)t * S.ldx + lc0;
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        const float4 xv = *reinterpret_cast<const float4*>(x + h * 128 + 4 * lane);
-        v[4 * h + 0] = xv.x; v[4 * h + 1] = xv.y; v[4 * h + 2] = xv.z; v[4 * h + 3] = xv.w;
-        if (S.w) {
-            const float4 wv = *reinterpret_cast<const float4*>(S.w + lc0 + h * 128 + 4 * lane);
-            v[4 * h + 0] = (v[4 * h + 0] * inv[si]) * wv.x;
-            v[4 * h + 1] = (v[4 * h + 1] * inv[si]) * wv.y;
-            v[4 * h + 2] = (v[4 * h + 2] * inv[si]) * wv.z;
-            v[4 * h + 3] = (v[4 * h + 3] * inv[si]) * wv.w;
+        for (int h = 0; h < 2; ++h) {
+            const float4 xv = *reinterpret_cast<const float4*>(x + h * 128 + 4 * lane);
+            v[4 * h + 0] = xv.x; v[4 * h + 1] = xv.y; v[4 * h + 2] = xv.z; v[4 * h + 3] = xv.w;
+            if (S.w) {
+                const float4 w4 = *reinterpret_cast<const float4*>(S.w + lc0 + h * 128 + 4 * lane);
+                wv[4 * h + 0] = w4.x; wv[4 * h + 1] = w4.y; wv[4 * h + 2] = w4.z; wv[4 * h + 3] = w4.w;
+            }
         }
+    }
+    float inv[2] = {1.f, 1.f};
+    for (int sj = 0; sj < nseg; ++sj) {
+        const XSeg& Q = sj ? s1 : s0;
+        if (!Q.w) continue;
+        const float* x = Q.x + (size_t)t * Q.ldx;
+        float ss = 0.f;
+        for (int i = threadIdx.x * 4; i < Q.len; i += blockDim.x * 4) {
+            const float4 q4 = *reinterpret_cast<const float4*>(x + i);
+            ss = fmaf(q4.x, q4.x, ss);
+            ss = fmaf(q4.y, q4.y, ss);
+            ss = fmaf(q4.z, q4.z, ss);
+            ss = fmaf(q4.w, q4.w, ss);
+        }
+        ss = block_sum(ss, sh);
+        inv[sj] = 1.0f / sqrtf(ss / (float)Q.len + eps);
+    }
+    if (!has_block) return;
+    if (S.w) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = (v[i] * inv[si]) * wv[i];
     }
     xprep_emit(v, t, b, N, nb, K, xb, what, lane);
 }
