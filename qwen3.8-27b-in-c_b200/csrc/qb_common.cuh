@@ -12,10 +12,12 @@
 enum QbType : int { QB_F32 = 0, QB_Q8_0 = 8, QB_Q4_K = 12, QB_Q5_K = 13, QB_Q6_K = 14, QB_IQ4_XS = 23 };
 
 // Bytes of one repacked (16-row tile x 256-column super-block) unit.  Q8_0 uses
-// a (16-row tile x 32-column block) unit.  Every layout holds exactly the bytes
-// of the 16 source rows: the repack only reorders them.
+// a (16-row tile x 32-column block) unit.  The K-quant and Q8_0 layouts hold
+// exactly the bytes of the 16 source rows (the repack only reorders them);
+// IQ4_XS keeps 2 more bytes per row (138 instead of 136): its 6-bit sub-block
+// scales are stored expanded, as the int8 differences the GEMV applies.
 __host__ __device__ constexpr int qb_unit_bytes(int type) {
-    return type == QB_IQ4_XS ? 16 * 136
+    return type == QB_IQ4_XS ? 16 * 138
          : type == QB_Q6_K   ? 16 * 210
          : type == QB_Q4_K   ? 16 * 144
          : type == QB_Q5_K   ? 16 * 176
@@ -131,6 +133,24 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 __device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
 __device__ __forceinline__ uint2 lds64(const uint8_t* p) { return *reinterpret_cast<const uint2*>(p); }
 __device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
+__device__ __forceinline__ uint32_t lds16(const uint8_t* p) { return *reinterpret_cast<const uint16_t*>(p); }
+__device__ __forceinline__ int lds_s8(const uint8_t* p) { return *reinterpret_cast<const int8_t*>(p); }
+
+// 4-byte global -> shared copy completed by cp_async_wait_all (this thread's copies)
+__device__ __forceinline__ void cp_async4(float* smem_dst, const float* gsrc) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"((uint32_t)__cvta_generic_to_shared(smem_dst)),
+                 "l"(gsrc)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+// device-scope atomic add with acquire-release semantics; returns the old value
+__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v) {
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
 }

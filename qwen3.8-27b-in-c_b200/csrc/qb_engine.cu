@@ -250,6 +250,7 @@ struct LayerW {
     int ridx = -1, aidx = -1;
     const float *attn_norm = nullptr, *post_norm = nullptr;
     DevMat ffn_gate, ffn_up, ffn_down;
+    DevMat gu;   // gate and up tiles interleaved (fused SwiGLU epilogue); gate / up keep only their shapes
     DevMat wqkv, wgate, wbeta, walpha, ssm_out;
     const float *conv_w = nullptr, *dt_bias = nullptr, *ssm_a = nullptr, *ssm_norm = nullptr;
     DevMat q, k, v, o;
@@ -299,7 +300,12 @@ struct Engine {
     // activations (QB_MAX_TOK rows each)
     float *bx, *h_save, *qkv, *qkvc, *z, *beta, *alpha, *o, *y, *qbuf, *kvbuf, *attn_o, *gate, *up, *act;
     float *logits, *mtp_x, *mtp_h, *mtp_logits, *emb;
-    QbXBuf xb{};                          // prepared GEMV activations
+    QbXBuf xb{};                          // prepared GEMV activations (what the next GEMV reads)
+    QbXBuf xb_alt{};                      // where a fused GEMV epilogue prepares the input after that
+    const float* xss = nullptr;           // xb holds x * norm_w: per-block sums of squares of x (QbInNorm)
+    bool xready = false;                  // xb already holds the next normed input (fused epilogue)
+    bool fuse = false;                    // fused GEMV epilogues (QB_FUSE=1; mma.sync path only)
+    float* ss = nullptr;                  // [QB_MAX_TOK][Kmax / 256]
     bool use_tc = false;                  // IQ4_XS at N <= 4 on tcgen05 (QB_TC=1); default: int8 mma.sync
     float* attn_po = nullptr;             // attention chunk partials (qb_attn_decode)
     float2* gates = nullptr;              // DeltaNet (beta, decay) per (token, v-head)
@@ -328,6 +334,14 @@ struct Engine {
         if (cudaMalloc(&p, bytes) != cudaSuccess) return nullptr;
         allocs.push_back(p);
         return p;
+    }
+    void dfree(void* p) {
+        for (size_t i = 0; i < allocs.size(); ++i)
+            if (allocs[i] == p) {
+                cudaFree(p);
+                allocs.erase(allocs.begin() + (long)i);
+                return;
+            }
     }
 };
 
@@ -363,7 +377,7 @@ int upload_mat(Engine& e, const GTensor* t, DevMat& m, void* tmp, size_t tmp_byt
     // stream-ordered: the repack must not start before the host->device copy lands
     CK(cudaMemcpyAsync(tmp, t->data, src_bytes, cudaMemcpyHostToDevice, e.st));
     CK(qb_repack(t->type, tmp, m.rows, m.K, m.w, e.st));
-    if (t->type == QB_IQ4_XS) {
+    if (t->type == QB_IQ4_XS && e.use_tc) {
         const size_t rt = qb_repacked_bytes_tc(m.rows, m.K);
         m.w_tc = e.dalloc(rt);
         if (!m.w_tc) { set_err(-2, "cudaMalloc %zu", rt); return -1; }
@@ -382,6 +396,25 @@ const float* upload_f32(Engine& e, const GTensor* t) {
     if (cudaMemcpyAsync(p, t->data, n * 4, cudaMemcpyHostToDevice, e.st) != cudaSuccess) return nullptr;
     if (cudaStreamSynchronize(e.st) != cudaSuccess) return nullptr;
     return (const float*)p;
+}
+
+// gate / up of one FFN as one tile-interleaved matrix for the fused SwiGLU
+// epilogue; the separate copies are released (their shapes stay for accounting)
+int build_gu(Engine& e, LayerW& l) {
+    const DevMat &g = l.ffn_gate, &u = l.ffn_up;
+    if (!e.fuse || g.type != u.type || g.type == QB_F32 || g.rows != u.rows || g.K != u.K || g.rows % 256) return 0;
+    l.gu.type = g.type;
+    l.gu.rows = 2 * g.rows;
+    l.gu.K = g.K;
+    const size_t rb = qb_repacked_bytes(g.type, l.gu.rows, g.K);
+    l.gu.w = e.dalloc(rb);
+    if (!l.gu.w) { set_err(-2, "cudaMalloc %zu", rb); return -1; }
+    CK(qb_interleave_tiles(g.type, g.w, u.w, g.rows, g.K, l.gu.w, e.st));
+    CK(cudaStreamSynchronize(e.st));
+    e.dfree(l.ffn_gate.w);
+    e.dfree(l.ffn_up.w);
+    l.ffn_gate.w = l.ffn_up.w = nullptr;
+    return 0;
 }
 
 int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
@@ -418,6 +451,12 @@ int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
     e.eps = c.rms_norm_eps;
     e.n_ctx = (int)n_ctx;
     e.rope_half = (int)c.rope_dim_count / 2;
+    {
+        const char* tc = getenv("QB_TC");
+        e.use_tc = tc && tc[0] == '1';
+        const char* fz = getenv("QB_FUSE");
+        e.fuse = !e.use_tc && fz && fz[0] == '1';
+    }
 
     // temp buffer for repacking = largest quantised tensor
     size_t tmp_bytes = 0;
@@ -458,7 +497,7 @@ int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
         if (!(l.post_norm = upload_f32(e, T("blk.%d.post_attention_norm.weight", il)))) return -1;
         if (upload_mat(e, T("blk.%d.ffn_gate.weight", il), l.ffn_gate, tmp, tmp_bytes) ||
             upload_mat(e, T("blk.%d.ffn_up.weight", il), l.ffn_up, tmp, tmp_bytes) ||
-            upload_mat(e, T("blk.%d.ffn_down.weight", il), l.ffn_down, tmp, tmp_bytes))
+            upload_mat(e, T("blk.%d.ffn_down.weight", il), l.ffn_down, tmp, tmp_bytes) || build_gu(e, l))
             return -1;
         if (l.rec) {
             l.ridx = nr++;
@@ -499,7 +538,7 @@ int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
             upload_mat(e, T("blk.%d.ffn_gate.weight", im), l.ffn_gate, tmp, tmp_bytes) ||
             upload_mat(e, T("blk.%d.ffn_up.weight", im), l.ffn_up, tmp, tmp_bytes) ||
             upload_mat(e, T("blk.%d.ffn_down.weight", im), l.ffn_down, tmp, tmp_bytes) ||
-            upload_mat(e, T("blk.%d.nextn.eh_proj.weight", im), e.eh_proj, tmp, tmp_bytes))
+            upload_mat(e, T("blk.%d.nextn.eh_proj.weight", im), e.eh_proj, tmp, tmp_bytes) || build_gu(e, l))
             return -1;
         if (!(l.q_norm = upload_f32(e, T("blk.%d.attn_q_norm.weight", im))) ||
             !(l.k_norm = upload_f32(e, T("blk.%d.attn_k_norm.weight", im))) ||
@@ -583,11 +622,21 @@ int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
     e.xb.xqscale = A((size_t)T8 * (Kmax / 256));
     e.xb.xtc = (uint8_t*)e.dalloc(qb_xtc_bytes(Kmax));
     if (!e.xb.xtc) { set_err(-2, "activation alloc"); return -1; }
-    CK(cudaMemset(e.xb.xtc, 0, qb_xtc_bytes(Kmax)));
-    {
-        const char* tc = getenv("QB_TC");
-        e.use_tc = tc && tc[0] == '1';
+    if (e.fuse) {
+        e.xb_alt.xfrag = (uint2*)e.dalloc(qb_xfrag_bytes(Kmax));
+        e.xb_alt.xscale = A((size_t)T8 * (Kmax / 256));
+        e.xb_alt.xsum = A((size_t)T8 * (Kmax / 32));
+        e.xb_alt.xq = (uint2*)e.dalloc(qb_xq_bytes(Kmax));
+        e.xb_alt.xqscale = A((size_t)T8 * (Kmax / 256));
+        e.ss = A((size_t)T8 * (Kmax / 256));
+        if (!e.xb_alt.xfrag || !e.xb_alt.xq || !e.ss) { set_err(-2, "activation alloc"); return -1; }
+        CK(cudaMemset(e.xb_alt.xfrag, 0, qb_xfrag_bytes(Kmax)));
+        CK(cudaMemset(e.xb_alt.xq, 0, qb_xq_bytes(Kmax)));
+        CK(cudaMemset(e.xb_alt.xscale, 0, (size_t)T8 * (Kmax / 256) * 4));
+        CK(cudaMemset(e.xb_alt.xqscale, 0, (size_t)T8 * (Kmax / 256) * 4));
+        CK(cudaMemset(e.xb_alt.xsum, 0, (size_t)T8 * (Kmax / 32) * 4));
     }
+    CK(cudaMemset(e.xb.xtc, 0, qb_xtc_bytes(Kmax)));
     {
         const size_t q_rows = (size_t)d.n_head * T8 * qb_attn_max_chunks((int)e.n_ctx);
         e.attn_po = A(q_rows * d.head_dim);
@@ -620,8 +669,12 @@ int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
 
 // ----------------------------- launch helpers ---------------------------------
 
+// y = W x for every matrix of mats (one input, e.xb).  With epi (one matrix)
+// the launch also prepares the next input into e.xb_alt, which then becomes e.xb.
 int gemv_group(Engine& e, const DevMat* const* mats, float* const* outs, const long long* ldos, int nm, int K,
-               int N, int accumulate) {
+               int N, int accumulate, const QbEpi* epi = nullptr) {
+    if (epi && nm != 1) { set_err(-1, "fused epilogue on a multi-matrix GEMV"); return -1; }
+    const QbInNorm in_norm{e.xss, e.eps};
     // fuse matrices of the same type; different types run as separate launches
     int i = 0;
     while (i < nm) {
@@ -639,13 +692,25 @@ int gemv_group(Engine& e, const DevMat* const* mats, float* const* outs, const l
         if (type == QB_F32) {
             for (int s = 0; s < ns; ++s) CK(cudaErrorNotSupported);
         } else if (type == QB_IQ4_XS && N <= 4 && e.use_tc) {
+            if (e.xss || epi) { set_err(-1, "fused epilogues need the mma.sync GEMV"); return -1; }
             for (int s = 0; s < ns; ++s) segs[s].w = mats[i - ns + s]->w_tc;
             CK(qb_qmv_tc(segs, ns, K, N, e.xb, accumulate, 0, 1 << 30, e.work, e.st));
         } else {
-            CK(qb_qmv(type, segs, ns, K, N, e.xb, accumulate, 0, 1 << 30, e.work, e.st));
+            CK(qb_qmv_ex(type, segs, ns, K, N, e.xb, accumulate, &in_norm, epi, e.work, e.st));
         }
     }
+    e.xready = epi != nullptr;
+    if (epi) {
+        std::swap(e.xb, e.xb_alt);
+        e.xss = epi->kind == QB_EPI_NORM ? epi->ss : nullptr;
+    }
     return 0;
+}
+
+// a kernel other than a GEMV epilogue is about to write e.xb
+void fresh_input(Engine& e) {
+    e.xss = nullptr;
+    e.xready = false;
 }
 
 // the qb_xprep outputs that the matrices consuming an input of N tokens read
@@ -656,49 +721,99 @@ int xp_needs(const Engine& e, std::initializer_list<const DevMat*> ms, int N) {
 }
 
 int xprep1(Engine& e, const float* x, long long ldx, const float* norm_w, int len, int N, int what) {
+    fresh_input(e);
     QbXIn in{x, ldx, norm_w, len};
     CK(qb_xprep(&in, 1, N, e.eps, e.xb, what, e.st));
     return 0;
 }
 
+// The RMSNorm the residual stream gets next and the fragments its readers
+// need: the residual GEMV before it prepares that input in its epilogue.
+struct NextIn {
+    const float* norm_w = nullptr;
+    int what = 0;
+};
+
+// RMSNorm(x) * norm_w as the next GEMV input, unless the last GEMV's epilogue made it
+int norm_input(Engine& e, const float* x, const float* norm_w, int B, int what) {
+    if (e.xready) {
+        e.xready = false;
+        return 0;
+    }
+    return xprep1(e, x, e.E, norm_w, e.E, B, what);
+}
+
+// the epilogue that prepares next from a residual GEMV's output, or none
+const QbEpi* residual_epi(Engine& e, const NextIn& next, QbEpi& buf) {
+    if (!e.fuse || !next.norm_w) return nullptr;
+    buf = QbEpi{QB_EPI_NORM, next.norm_w, e.ss, nullptr, 0, e.xb_alt, next.what};
+    return &buf;
+}
+
 // SwiGLU FFN on residual x (src/model.c:819-842)
-int ffn_block(Engine& e, const LayerW& l, float* x, int B) {
-    if (xprep1(e, x, e.E, l.post_norm, e.E, B, xp_needs(e, {&l.ffn_gate, &l.ffn_up}, B))) return -1;
-    const DevMat* m2[2] = {&l.ffn_gate, &l.ffn_up};
-    float* o2[2] = {e.gate, e.up};
-    const long long ld2[2] = {e.F, e.F};
-    if (gemv_group(e, m2, o2, ld2, 2, e.E, B, 0)) return -1;
-    CK(qb_silu_mul_xprep(e.gate, e.up, e.F, e.F, B, e.act, e.xb, xp_needs(e, {&l.ffn_down}, B), e.st));
+int ffn_block(Engine& e, const LayerW& l, float* x, int B, const NextIn& next) {
+    if (l.gu.w) {
+        if (norm_input(e, x, l.post_norm, B, xp_needs(e, {&l.gu}, B))) return -1;
+        // gate / up GEMV whose epilogue writes h = silu(gate) * up and its fragments
+        const QbEpi sw{QB_EPI_SWIGLU, nullptr, nullptr, e.act, e.F, e.xb_alt, xp_needs(e, {&l.ffn_down}, B)};
+        const DevMat* m2[1] = {&l.gu};
+        float* o2[1] = {e.act};
+        const long long ld2[1] = {e.F};
+        if (gemv_group(e, m2, o2, ld2, 1, e.E, B, 0, &sw)) return -1;
+    } else {
+        if (norm_input(e, x, l.post_norm, B, xp_needs(e, {&l.ffn_gate, &l.ffn_up}, B))) return -1;
+        const DevMat* m2[2] = {&l.ffn_gate, &l.ffn_up};
+        float* o2[2] = {e.gate, e.up};
+        const long long ld2[2] = {e.F, e.F};
+        if (gemv_group(e, m2, o2, ld2, 2, e.E, B, 0)) return -1;
+        fresh_input(e);
+        CK(qb_silu_mul_xprep(e.gate, e.up, e.F, e.F, B, e.act, e.xb, xp_needs(e, {&l.ffn_down}, B), e.st));
+    }
+    QbEpi eb;
     const DevMat* m1[1] = {&l.ffn_down};
     float* o1[1] = {x};
     const long long ld1[1] = {e.E};
-    return gemv_group(e, m1, o1, ld1, 1, e.F, B, 1);
+    return gemv_group(e, m1, o1, ld1, 1, e.F, B, 1, residual_epi(e, next, eb));
+}
+
+// the readers of a layer's normed input: DeltaNet in-projections or q / k / v
+NextIn layer_in(const Engine& e, const LayerW& l, int B) {
+    if (l.rec) return {l.attn_norm, xp_needs(e, {&l.wqkv, &l.wgate, &l.wbeta, &l.walpha}, B)};
+    return {l.attn_norm, xp_needs(e, {&l.q, &l.k, &l.v}, B)};
+}
+
+// the FFN's input: post-attention norm, read by gate / up
+NextIn ffn_in(const Engine& e, const LayerW& l, int B) {
+    return {l.post_norm, l.gu.w ? xp_needs(e, {&l.gu}, B) : xp_needs(e, {&l.ffn_gate, &l.ffn_up}, B)};
 }
 
 // gated attention block on residual x, positions *pos .. *pos+B-1
-int attn_block(Engine& e, const LayerW& l, float* x, int B, const uint32_t* pos, float* kc, float* vc) {
+int attn_block(Engine& e, const LayerW& l, float* x, int B, const uint32_t* pos, float* kc, float* vc,
+               const NextIn& next) {
     const qwen_dims_t& d = e.d;
     const int qw = 2 * d.n_head * d.head_dim, kvw = d.n_kv_head * d.head_dim;
-    if (xprep1(e, x, e.E, l.attn_norm, e.E, B, xp_needs(e, {&l.q, &l.k, &l.v}, B))) return -1;
+    if (norm_input(e, x, l.attn_norm, B, xp_needs(e, {&l.q, &l.k, &l.v}, B))) return -1;
     const DevMat* m3[3] = {&l.q, &l.k, &l.v};
     float* o3[3] = {e.qbuf, e.kvbuf, e.kvbuf + kvw};
     const long long ld3[3] = {qw, 2 * kvw, 2 * kvw};
     if (gemv_group(e, m3, o3, ld3, 3, e.E, B, 0)) return -1;
     CK(qb_attn_prep(e.qbuf, qw, e.kvbuf, 2 * kvw, l.q_norm, l.k_norm, d.n_head, d.n_kv_head, d.head_dim,
                     e.rope_half, e.rope_cos, e.rope_sin, pos, B, e.eps, kc, vc, e.st));
+    fresh_input(e);
     CK(qb_attn_decode(e.qbuf, qw, kc, vc, d.n_head, d.n_kv_head, d.head_dim, pos, B, e.n_ctx, e.attn_o,
                       d.n_head * d.head_dim, e.attn_po, e.attn_pml, e.xb, xp_needs(e, {&l.o}, B), e.st));
     const int ow = d.n_head * d.head_dim;
+    QbEpi eb;
     const DevMat* m1[1] = {&l.o};
     float* o1[1] = {x};
     const long long ld1[1] = {e.E};
-    if (gemv_group(e, m1, o1, ld1, 1, ow, B, 1)) return -1;
-    return ffn_block(e, l, x, B);
+    if (gemv_group(e, m1, o1, ld1, 1, ow, B, 1, residual_epi(e, ffn_in(e, l, B), eb))) return -1;
+    return ffn_block(e, l, x, B, next);
 }
 
-int gdn_block(Engine& e, const LayerW& l, int B, int ckpt) {
+int gdn_block(Engine& e, const LayerW& l, int B, int ckpt, const NextIn& next) {
     const qwen_dims_t& d = e.d;
-    if (xprep1(e, e.bx, e.E, l.attn_norm, e.E, B, xp_needs(e, {&l.wqkv, &l.wgate, &l.wbeta, &l.walpha}, B))) return -1;
+    if (norm_input(e, e.bx, l.attn_norm, B, xp_needs(e, {&l.wqkv, &l.wgate, &l.wbeta, &l.walpha}, B))) return -1;
     const DevMat* m4[4] = {&l.wqkv, &l.wgate, &l.wbeta, &l.walpha};
     float* o4[4] = {e.qkv, e.z, e.beta, e.alpha};
     const long long ld4[4] = {e.ld_qkv, d.d_inner, 256, 256};
@@ -709,6 +824,7 @@ int gdn_block(Engine& e, const LayerW& l, int B, int ckpt) {
                    e.qkvc, e.ld_qkv, e.beta, e.alpha, 256, l.dt_bias, l.ssm_a, d.n_v_heads, e.gates, e.st));
     CK(qb_gdn_recur(e.qkvc, e.ld_qkv, e.gates, d.n_k_heads, d.n_v_heads, d.head_k_dim, B, e.eps, ssm,
                     e.ssm_slot_stride, &e.ctrl->cur_slot, ckpt, e.o, d.d_inner, e.st));
+    fresh_input(e);
     if (d.head_v_dim == 128 && d.n_v_heads % 2 == 0) {
         CK(qb_gdn_out_xprep(e.o, e.z, d.d_inner, l.ssm_norm, d.n_v_heads, d.head_v_dim, B, e.eps, e.y, e.xb,
                             xp_needs(e, {&l.ssm_out}, B), e.st));
@@ -716,11 +832,12 @@ int gdn_block(Engine& e, const LayerW& l, int B, int ckpt) {
         CK(qb_gdn_out(e.o, e.z, d.d_inner, l.ssm_norm, d.n_v_heads, d.head_v_dim, B, e.eps, e.y, e.st));
         if (xprep1(e, e.y, d.d_inner, nullptr, d.d_inner, B, xp_needs(e, {&l.ssm_out}, B))) return -1;
     }
+    QbEpi eb;
     const DevMat* m1[1] = {&l.ssm_out};
     float* o1[1] = {e.bx};
     const long long ld1[1] = {e.E};
-    if (gemv_group(e, m1, o1, ld1, 1, d.d_inner, B, 1)) return -1;
-    return ffn_block(e, l, e.bx, B);
+    if (gemv_group(e, m1, o1, ld1, 1, d.d_inner, B, 1, residual_epi(e, ffn_in(e, l, B), eb))) return -1;
+    return ffn_block(e, l, e.bx, B, next);
 }
 
 __global__ void set_u32_kernel(uint32_t* p, uint32_t v) { *p = v; }
@@ -729,17 +846,21 @@ __global__ void set_u32_kernel(uint32_t* p, uint32_t v) { *p = v; }
 // ctrl->fwd_pos + b.  Logits -> e.logits[b], argmax -> ctrl->argmax[b].
 int fwd_backbone(Engine& e, int B, int ckpt) {
     CK(qb_embed(e.embd_type, e.tok_embd, e.E, e.ctrl->fwd_tok, B, e.bx, e.E, e.st));
-    for (const LayerW& l : e.L) {
+    fresh_input(e);
+    for (size_t il = 0; il < e.L.size(); ++il) {
+        const LayerW& l = e.L[il];
+        const NextIn next = il + 1 < e.L.size() ? layer_in(e, e.L[il + 1], B)
+                                                : NextIn{e.out_norm, xp_needs(e, {&e.output}, B)};
         if (l.rec) {
-            if (gdn_block(e, l, B, ckpt)) return -1;
+            if (gdn_block(e, l, B, ckpt, next)) return -1;
         } else {
             float* kc = e.kv_k + (size_t)l.aidx * e.kv_layer;
             float* vc = e.kv_v + (size_t)l.aidx * e.kv_layer;
-            if (attn_block(e, l, e.bx, B, &e.ctrl->fwd_pos, kc, vc)) return -1;
+            if (attn_block(e, l, e.bx, B, &e.ctrl->fwd_pos, kc, vc, next)) return -1;
         }
     }
     CK(cudaMemcpyAsync(e.h_save, e.bx, (size_t)B * e.E * 4, cudaMemcpyDeviceToDevice, e.st));
-    if (xprep1(e, e.bx, e.E, e.out_norm, e.E, B, xp_needs(e, {&e.output}, B))) return -1;
+    if (norm_input(e, e.bx, e.out_norm, B, xp_needs(e, {&e.output}, B))) return -1;
     const DevMat* m1[1] = {&e.output};
     float* o1[1] = {e.logits};
     const long long ld1[1] = {e.V};
@@ -758,15 +879,17 @@ int fwd_backbone(Engine& e, int B, int ckpt) {
 int fwd_mtp(Engine& e, int B, const float* hsrc, int want_logits) {
     CK(qb_embed(e.embd_type, e.tok_embd, e.E, e.ctrl->mtp_tok, B, e.emb, e.E, e.st));
     QbXIn in[2] = {{e.emb, e.E, e.enorm, e.E}, {hsrc, e.E, e.hnorm, e.E}};
+    fresh_input(e);
     CK(qb_xprep(in, 2, B, e.eps, e.xb, xp_needs(e, {&e.eh_proj}, B), e.st));
     const DevMat* m1[1] = {&e.eh_proj};
     float* o1[1] = {e.mtp_x};
     const long long ld1[1] = {e.E};
     if (gemv_group(e, m1, o1, ld1, 1, 2 * e.E, B, 0)) return -1;
-    if (attn_block(e, e.mtp, e.mtp_x, B, &e.ctrl->mtp_pos, e.mtp_k, e.mtp_v)) return -1;
+    const NextIn next = want_logits ? NextIn{e.shnorm, xp_needs(e, {&e.output}, B)} : NextIn{};
+    if (attn_block(e, e.mtp, e.mtp_x, B, &e.ctrl->mtp_pos, e.mtp_k, e.mtp_v, next)) return -1;
     CK(cudaMemcpyAsync(e.mtp_h, e.mtp_x + (size_t)(B - 1) * e.E, (size_t)e.E * 4, cudaMemcpyDeviceToDevice, e.st));
     if (want_logits) {
-        if (xprep1(e, e.mtp_x, e.E, e.shnorm, e.E, B, xp_needs(e, {&e.output}, B))) return -1;
+        if (norm_input(e, e.mtp_x, e.shnorm, B, xp_needs(e, {&e.output}, B))) return -1;
         const DevMat* mo[1] = {&e.output};
         float* oo[1] = {e.mtp_logits};
         const long long ldo[1] = {e.V};
@@ -1299,11 +1422,21 @@ extern "C" float qb_bench(qwen_model_t* m, int what, uint32_t arg, uint32_t iter
                 const int wh = packed & 0xFF, a = (packed >> 8) & 0xFF, nlay = packed >> 16;
                 for (int li = 0; li < nlay; ++li) {
                     if (wh == 1) {
+                        // the FFN gate / up launch as the forward runs it
                         const LayerW& l = en.L[li];
-                        const DevMat* m2[2] = {&l.ffn_gate, &l.ffn_up};
-                        float* o2[2] = {en.gate, en.up};
-                        const long long ld2[2] = {en.F, en.F};
-                        if (gemv_group(en, m2, o2, ld2, 2, en.E, a, 0)) return -1;
+                        if (l.gu.w) {
+                            const QbEpi sw{QB_EPI_SWIGLU, nullptr, nullptr, en.act, en.F, en.xb_alt,
+                                           xp_needs(en, {&l.ffn_down}, a)};
+                            const DevMat* m1[1] = {&l.gu};
+                            float* o1[1] = {en.act};
+                            const long long ld1[1] = {en.F};
+                            if (gemv_group(en, m1, o1, ld1, 1, en.E, a, 0, &sw)) return -1;
+                        } else {
+                            const DevMat* m2[2] = {&l.ffn_gate, &l.ffn_up};
+                            float* o2[2] = {en.gate, en.up};
+                            const long long ld2[2] = {en.F, en.F};
+                            if (gemv_group(en, m2, o2, ld2, 2, en.E, a, 0)) return -1;
+                        }
                     } else {
                         const DevMat* m1[1] = {&en.output};
                         float* o1[1] = {en.logits};
@@ -1401,7 +1534,14 @@ struct Scratch {
     QbQmvWork work{};
 };
 std::mutex g_mu;
-bool g_host_tc = false;   // host GEMV API: IQ4_XS at n <= 4 on tcgen05 (QB_TC=1); default: int8 mma.sync
+// host GEMV API: IQ4_XS at n <= 4 on tcgen05 (QB_TC=1); default: int8 mma.sync
+bool host_tc() {
+    static const bool on = [] {
+        const char* tc = getenv("QB_TC");
+        return tc && tc[0] == '1';
+    }();
+    return on;
+}
 std::unordered_map<WKey, DevMat, WKeyHash> g_wcache;
 std::unordered_map<int, Scratch> g_scratch;
 
@@ -1411,8 +1551,6 @@ int scratch_get(Scratch*& s, size_t x_floats, size_t out_floats, int K) {
     s = &g_scratch[dev];
     if (!s->st) {
         CK(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
-        const char* tc = getenv("QB_TC");
-        g_host_tc = tc && tc[0] == '1';
     }
     if (x_floats > s->x_cap) {
         if (s->x) cudaFree(s->x);
@@ -1503,7 +1641,7 @@ int wcache_get(const gguf_tensor_info_t* W, const DevMat*& out) {
         CK(cudaMemcpy(tmp, W->data, src_bytes, cudaMemcpyHostToDevice));
         CK(cudaMalloc(&m.w, qb_repacked_bytes(m.type, m.rows, m.K)));
         CK(qb_repack(m.type, tmp, m.rows, m.K, m.w, 0));
-        if (m.type == QB_IQ4_XS) {
+        if (m.type == QB_IQ4_XS && host_tc()) {
             CK(cudaMalloc(&m.w_tc, qb_repacked_bytes_tc(m.rows, m.K)));
             CK(qb_repack_tc(tmp, m.rows, m.K, m.w_tc, 0));
         }
@@ -1535,7 +1673,7 @@ int gemv_host(const gguf_tensor_info_t* W, const float* x, uint64_t ldx, int n, 
         } else {
             if (scratch_work(s, M->rows)) return -1;
             QbXIn in{s->x, K, nullptr, K};
-            const bool tc = M->w_tc && nn <= 4 && g_host_tc;
+            const bool tc = M->w_tc && nn <= 4 && host_tc();
             CK(qb_xprep(&in, 1, nn, 1e-6f, s->xb, qb_xprep_needs(M->type, nn, tc ? 1 : 0), s->st));
             if (tc) {
                 const int T0 = (int)(r0 / 128);   // start on a 128-row tile

@@ -24,6 +24,7 @@ struct QbQmvWork {
     float* partial;          // [max_warps][2][32][8]
     float* gpartial;         // [max_warps][2][32][8] (per CTA, or per warp without CTA grouping)
     unsigned* counters;      // [max_pairs], zero-initialised
+    unsigned* bcounters;     // [max_pairs] per 256-row output block (qb_qmv_ex epilogues), zero-initialised
     unsigned* err;           // [1]
     int max_warps;
     int max_pairs;
@@ -58,6 +59,40 @@ int qb_xprep_needs(int type, int N = QB_MAX_TOK, int tc = 0);
 cudaError_t qb_xprep(const QbXIn* in, int nseg, int N, float eps, const QbXBuf& xb, int what, cudaStream_t st);
 cudaError_t qb_qmv(int type, const QbQSeg* segs, int nseg, int K, int N, const QbXBuf& xb, int accumulate,
                    int row_lo, int row_hi, const QbQmvWork& work, cudaStream_t st);
+
+// Activation preparation of the next GEMV's input, fused into this GEMV: as
+// the last tile pair of a 256-row block of the output finishes, its warp
+// writes that block's fragments (one matrix per launch, rows a multiple of
+// 256, no row range).
+//  * NORM: the output is a residual stream x (usually accumulate = 1); the
+//    fragments hold x * norm_w, and ss[t * (rows / 256) + b] the block's sum
+//    of squares of x.  The consuming launch applies the RMSNorm scale to its
+//    outputs (QbInNorm): W (x / rms * w) = (W (x * w)) / rms.
+//  * SWIGLU: the matrix interleaves gate and up tiles (tile 2p = gate rows
+//    16p..16p+15, tile 2p+1 = the same up rows, qb_interleave_tiles); the
+//    output is h = silu(gate) * up at h[t * ldh + j], and the fragments are h's.
+enum { QB_EPI_NONE = 0, QB_EPI_NORM = 1, QB_EPI_SWIGLU = 2 };
+struct QbEpi {
+    int kind;
+    const float* norm_w;     // NORM
+    float* ss;               // NORM: [N][rows / 256]
+    float* h;                // SWIGLU: [N][ldh]
+    long long ldh;
+    QbXBuf xb;               // fragments of the next input (not the buffer this launch reads)
+    int what;                // QB_XP_* the next input's consumers read
+};
+// Deferred RMSNorm of this launch's input (prepared by a NORM epilogue):
+// out *= 1 / sqrt(sum_b ss[t * (K / 256) + b] / K + eps).
+struct QbInNorm {
+    const float* ss;
+    float eps;
+};
+cudaError_t qb_qmv_ex(int type, const QbQSeg* segs, int nseg, int K, int N, const QbXBuf& xb, int accumulate,
+                      const QbInNorm* in_norm, const QbEpi* epi, const QbQmvWork& work, cudaStream_t st);
+// Tile-interleaved copy of two repacked matrices of equal shape (rows % 16 == 0):
+// dst tile 2i = tile i of a, dst tile 2i + 1 = tile i of b.  dst holds
+// qb_repacked_bytes(type, 2 * rows, K) bytes.
+cudaError_t qb_interleave_tiles(int type, const void* a, const void* b, int rows, int K, void* dst, cudaStream_t st);
 cudaError_t qb_qmv_work_alloc(QbQmvWork& w, int max_pairs);
 
 // ---- IQ4_XS GEMV on tcgen05 (qb_qmv_tc.cu), N <= 4 ----

@@ -8,7 +8,8 @@
 //
 // Data path.  Weights are repacked once at load time from GGUF super-blocks
 // into 16-row tiles whose bytes land directly in mma.sync A-fragment order
-// (the byte count of every format is unchanged).  Two tensor-core paths:
+// (the byte count of every format is unchanged, except 2 B more per IQ4_XS
+// row and super-block for its expanded sub-block scales).  Two tensor-core paths:
 //  * IQ4_XS (93 % of the model's bytes): int8 mma m16n8k32.  Each code is
 //    looked up as its int8 table value by byte permutes; the activations are
 //    three balanced int8 digits per element after a power-of-two scale per
@@ -42,6 +43,7 @@
 #include "qb_kernels.h"
 #include "qb_xprep.cuh"
 #include "qb_iq4.cuh"
+#include "qb_refmath.cuh"
 
 namespace {
 
@@ -65,6 +67,7 @@ constexpr int kSmemBudget = QB_QMV_SMEM_KB * 1024;   // per CTA
 constexpr int kMinStagesPerWarp = QB_QMV_MIN_STAGES;
 constexpr int kLocalPairs = 64;             // pairs one CTA's stage range may touch (else no level 1)
 constexpr int kRingOff = 512;                // full barriers (8 warps x 8 slots x 8 B), then the rings
+constexpr int kSsMax = 160;                  // deferred-norm sums prefetched per warp (N * K / 256)
 
 // 4 unsigned bytes -> two half2 (1024 + b0, 1024 + b1), (1024 + b2, 1024 + b3)
 __device__ __forceinline__ void bytes_to_h2(uint32_t u, uint32_t& h01, uint32_t& h23) {
@@ -112,13 +115,13 @@ __device__ __forceinline__ int col_token(int ct, int col) {
 // sum over sub-blocks of (block scale * tensor-core partial); mt[t] collects
 // terms that are not scaled by the activation scale (Q4_K / Q5_K mins).
 
-// IQ4_XS tile-block: qs 2048 B (4 chunks x 32 lanes x 16 B) + 16 rows x 8 B
-// of scales (layout in qb_iq4.cuh).
-constexpr int kIq4Tile = 16 * 136;
-
-__device__ __forceinline__ void iq4_scales(const uint8_t* u, int row, uint32_t& L0, uint32_t& L1, float& d) {
-    iq4_scale_bytes(lds64(u + 2048 + row * 8), L0, L1, d);
-}
+// IQ4_XS tile-block: qs 2048 B (4 chunks x 32 lanes x 16 B), then 16 rows x 8
+// int8 sub-block scale differences (ls_j - ls_{j+1} for j < 7, ls_7 - 32: the
+// factors of the summation by parts below), then 16 rows x the fp16 d.
+constexpr int kIq4Dl = 2048;
+constexpr int kIq4D = 2048 + 16 * 8;
+constexpr int kIq4Tile = kIq4D + 16 * 2;
+static_assert(kIq4Tile == qb_unit_bytes(QB_IQ4_XS) && kIq4Tile % 16 == 0, "IQ4_XS tile-block layout");
 
 // ---- IQ4_XS on the int8 tensor-core path (mma m16n8k32 s8 -> s32) ----
 // Codes become the int8 values of kvalues_iq4nl (src/quant.c:30-32) by two
@@ -152,18 +155,11 @@ __device__ __forceinline__ void stage_iq4_i8(const uint8_t* u, const uint2* __re
                                              const uint2* __restrict__ xq_next, int lane, uint2 (&bb)[2][NTI],
                                              float (&v)[2][2][2]) {
     const int g = lane >> 2;
-    uint32_t dl[2][2][2];   // signed bytes: ls_j - ls_{j+1} (j < 7), ls_7 - 32
     float d[2][2];
 #pragma unroll
     for (int t = 0; t < 2; ++t)
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            uint32_t L0, L1;
-            iq4_scales(u + t * kIq4Tile, g + 8 * r, L0, L1, d[t][r]);
-            const uint32_t n0 = prmt(L0, L1, 0x4321u), n1 = prmt(L1, 0x20202020u, 0x4321u);
-            dl[t][r][0] = (L0 + 0x80808080u - n0) ^ 0x80808080u;   // bytes stay in [65, 191]: no borrows
-            dl[t][r][1] = (L1 + 0x80808080u - n1) ^ 0x80808080u;
-        }
+        for (int r = 0; r < 2; ++r) d[t][r] = h2f_bits(lds16(u + t * kIq4Tile + kIq4D + (g + 8 * r) * 2));
     int R[2][NTI][4], acc[2][NTI][4];
 #pragma unroll
     for (int t = 0; t < 2; ++t)
@@ -191,7 +187,8 @@ __device__ __forceinline__ void stage_iq4_i8(const uint8_t* u, const uint2* __re
                 iq4_i8(h ? q.w : q.y, a[1], a[3]);   // row g + 8
 #pragma unroll
                 for (int nt = 0; nt < NTI; ++nt) mma_16832_s8(R[t][nt], a, bq[nt].x, bq[nt].y);
-                const int s_g = sbyte(dl[t][0][sb >> 2], sb & 3), s_g8 = sbyte(dl[t][1][sb >> 2], sb & 3);
+                const uint8_t* dl = u + t * kIq4Tile + kIq4Dl + g * 8 + sb;
+                const int s_g = lds_s8(dl), s_g8 = lds_s8(dl + 64);
 #pragma unroll
                 for (int nt = 0; nt < NTI; ++nt)
 #pragma unroll
@@ -435,6 +432,19 @@ struct QmvK {
     unsigned* counters;          // [pairs]
     int group;                   // warps combined in shared memory before the device-wide combine
     unsigned* err;
+    // deferred RMSNorm of the input (QbInNorm), in_ss == nullptr: none
+    const float* in_ss;
+    float in_eps;
+    // fused preparation of the next input (QbEpi)
+    int epi;                     // QB_EPI_*
+    unsigned* bcnt;              // [output blocks] pair arrivals, zero between launches
+    const float* epi_w;
+    float* epi_ss;
+    float* epi_h;
+    long long epi_ldh;
+    int epi_K;                   // columns of the next input (= this launch's output rows, or half of them)
+    int epi_what;
+    QbXBuf epi_xb;
 };
 
 // stage ranges: warp w owns [S*w/Wt, S*(w+1)/Wt); the grid guarantees Wt <= S,
@@ -444,10 +454,96 @@ __device__ __forceinline__ int stage_owner(int S, int Wt, int s) {
     return (int)((unsigned)((s + 1) * Wt - 1) / (unsigned)S);
 }
 
-// o[t][i], i = (row g tok 2c, row g tok 2c+1, row g8 tok 2c, row g8 tok 2c+1) of
-// tile t; lanes with active == false hold nothing to store.
-__device__ __forceinline__ void finish_pair(const QmvK& p, int pair, int gw, int s0, int s1, const float (&o)[2][4],
-                                            bool active, int lane, unsigned* lcnt, int grp_pair0) {
+// Next-input preparation for the 256-row output block blk, by the warp that
+// finished its last tile pair: per token, 8 values per lane (elements
+// 4 lane .. 4 lane + 3 and 128 + 4 lane ..) of src (h, or the residual x
+// times the norm weight w), then the fragments.  Four tokens at a time, so
+// that their load / shuffle chains overlap (tokens N..3 of a group are
+// computed too and land in the unused token columns; every buffer holds
+// QB_MAX_TOK tokens).  Not inlined, and given plain values, so that the GEMV
+// main loop keeps its registers.
+__device__ __noinline__ void block_emit(const float* __restrict__ src, long long ld, const float* __restrict__ w,
+                                        float* __restrict__ ss_out, int blk, int N, int K, QbXBuf xb, int what,
+                                        int lane) {
+    const int nbo = K >> 8;
+    for (int t0 = 0; t0 < N; t0 += 4) {
+        float v[4][8];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float* x = src + (size_t)(t0 + k) * ld + (size_t)blk * 256;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const float4 a = __ldcg(reinterpret_cast<const float4*>(x + h * 128 + 4 * lane));
+                v[k][4 * h + 0] = a.x; v[k][4 * h + 1] = a.y; v[k][4 * h + 2] = a.z; v[k][4 * h + 3] = a.w;
+            }
+        }
+        if (w) {
+            float wv[8];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const float4 a = __ldg(reinterpret_cast<const float4*>(w + (size_t)blk * 256 + h * 128 + 4 * lane));
+                wv[4 * h + 0] = a.x; wv[4 * h + 1] = a.y; wv[4 * h + 2] = a.z; wv[4 * h + 3] = a.w;
+            }
+            float ss[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                ss[k] = 0.f;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) ss[k] = fmaf(v[k][i], v[k][i], ss[k]);
+            }
+#pragma unroll
+            for (int o = 16; o; o >>= 1)
+#pragma unroll
+                for (int k = 0; k < 4; ++k) ss[k] += __shfl_xor_sync(0xffffffffu, ss[k], o);
+            if (lane == 0)
+#pragma unroll
+                for (int k = 0; k < 4; ++k) ss_out[(t0 + k) * nbo + blk] = ss[k];
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[k][i] = __fmul_rn(v[k][i], wv[i]);
+        }
+        xprep_emit_g<4>(v, t0, blk, N, nbo, K, xb, what, lane);
+    }
+}
+
+// 1 / rms of tokens 2c and 2c + 1 (c = lane & 3) from the producer's per-block
+// sums of squares, in a fixed order: ss[t * nb + b], prefetched into s_ss at
+// kernel start when N * nb <= kSsMax.  Not inlined: it runs once per pair.
+__device__ __noinline__ void deferred_inv(const float* s_ss, const float* __restrict__ ss, int N, int nb, int K,
+                                          float eps, int lane, float& i0, float& i1) {
+    const bool pre = N * nb <= kSsMax;
+    if (pre) {
+        cp_async_wait_all();
+        __syncwarp();
+    }
+    float sum[QB_MAX_TOK];
+#pragma unroll
+    for (int t = 0; t < QB_MAX_TOK; ++t) {
+        sum[t] = 0.f;
+        if (t < N)
+            for (int b = lane; b < nb; b += 32) sum[t] += pre ? s_ss[t * nb + b] : __ldg(ss + (size_t)t * nb + b);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1)
+#pragma unroll
+        for (int t = 0; t < QB_MAX_TOK; ++t) sum[t] += __shfl_xor_sync(0xffffffffu, sum[t], o);
+    const int t0 = 2 * (lane & 3), t1 = t0 + 1;
+    i0 = i1 = 1.f;
+#pragma unroll
+    for (int t = 0; t < QB_MAX_TOK; ++t) {
+        const float iv = 1.0f / sqrtf(sum[t] / (float)K + eps);
+        if (t == t0) i0 = iv;
+        if (t == t1) i1 = iv;
+    }
+}
+
+// The final values of a tile pair, held by one warp (lanes with active ==
+// false hold nothing): the deferred input norm, the store (or SwiGLU of the
+// gate / up tiles), then the block-completion epilogue.
+template <bool EPI>
+__device__ __forceinline__ void pair_final(const QmvK& p, int pair, float (&v)[2][4], bool active, int lane,
+                                           const float* s_ss) {
     int si = 0;
 #pragma unroll
     for (int s = 1; s < QB_MAX_SEG; ++s)
@@ -456,21 +552,68 @@ __device__ __forceinline__ void finish_pair(const QmvK& p, int pair, int gw, int
     const int lp = pair - p.pair0[si];
     const int g = lane >> 2, c = lane & 3;
     const int t0 = 2 * c, t1 = 2 * c + 1;
-    const int P0 = pair * p.nb, P1 = P0 + p.nb;
-    auto store = [&](int t, int i, float v) {
-        const int rr = lp * 32 + t * 16 + g + ((i & 2) ? 8 : 0);
-        const int tok = (i & 1) ? t1 : t0;
-        if (tok < p.N && rr < S.rows && rr >= p.row_lo && rr < p.row_hi) {
-            float* dst = S.out + (size_t)tok * S.ldo + rr;
-            *dst = p.accumulate ? (*dst + v) : v;
-        }
-    };
-    if (s0 <= P0 && s1 >= P1) {
+    if (EPI && p.in_ss) {
+        float i0, i1;
+        deferred_inv(s_ss, p.in_ss, p.N, p.nb, p.K, p.in_eps, lane, i0, i1);
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[t][i] *= (i & 1) ? i1 : i0;
+    }
+    if (EPI && p.epi == QB_EPI_SWIGLU) {
         if (active)
 #pragma unroll
-            for (int t = 0; t < 2; ++t)
+            for (int i = 0; i < 4; ++i) {
+                const int j = lp * 16 + g + ((i & 2) ? 8 : 0);
+                const int tok = (i & 1) ? t1 : t0;
+                if (tok < p.N) p.epi_h[(size_t)tok * p.epi_ldh + j] = __fmul_rn(silu_ref(v[0][i]), v[1][i]);
+            }
+    } else if (active) {
 #pragma unroll
-                for (int i = 0; i < 4; ++i) store(t, i, o[t][i]);
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int rr = lp * 32 + t * 16 + g + ((i & 2) ? 8 : 0);
+                const int tok = (i & 1) ? t1 : t0;
+                if (tok < p.N && rr < S.rows && rr >= p.row_lo && rr < p.row_hi) {
+                    float* dst = S.out + (size_t)tok * S.ldo + rr;
+                    *dst = p.accumulate ? (*dst + v[t][i]) : v[t][i];
+                }
+            }
+    }
+    if (!EPI || p.epi == QB_EPI_NONE) return;
+    // block of 256 output rows complete: 8 pairs (16 for SwiGLU, whose pairs yield 16 rows of h)
+    const int ppb = p.epi == QB_EPI_SWIGLU ? 16 : 8;
+    const int blk = lp / ppb;
+    // the warp's stores, then one acquire-release arrival (cumulative over the warp's stores)
+    __syncwarp();
+    unsigned old = 0;
+    if (lane == 0) old = atom_add_acq_rel_gpu(p.bcnt + blk, 1u);
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if ((int)old != ppb - 1) return;
+    if (lane == 0) p.bcnt[blk] = 0u;   // ready for the next launch
+    __syncwarp();
+    if (p.epi == QB_EPI_SWIGLU)
+        block_emit(p.epi_h, p.epi_ldh, nullptr, nullptr, blk, p.N, p.epi_K, p.epi_xb, p.epi_what, lane);
+    else
+        block_emit(S.out, S.ldo, p.epi_w, p.epi_ss, blk, p.N, p.epi_K, p.epi_xb, p.epi_what, lane);
+}
+
+// o[t][i], i = (row g tok 2c, row g tok 2c+1, row g8 tok 2c, row g8 tok 2c+1) of
+// tile t; lanes with active == false hold nothing to store.
+template <bool EPI>
+__device__ __forceinline__ void finish_pair(const QmvK& p, int pair, int gw, int s0, int s1, const float (&o)[2][4],
+                                            bool active, int lane, unsigned* lcnt, int grp_pair0, const float* s_ss) {
+    const int g = lane >> 2, c = lane & 3;
+    const int t0 = 2 * c, t1 = 2 * c + 1;
+    const int P0 = pair * p.nb, P1 = P0 + p.nb;
+    float v[2][4];
+    if (s0 <= P0 && s1 >= P1) {
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[t][i] = o[t][i];
+        pair_final<EPI>(p, pair, v, active, lane, s_ss);
         return;
     }
     // Split pair.  A contributor's piece is 0 if it started inside the pair
@@ -481,7 +624,6 @@ __device__ __forceinline__ void finish_pair(const QmvK& p, int pair, int gw, int
     const int w_first = stage_owner(p.S, p.Wt, P0), w_last = stage_owner(p.S, p.Wt, P1 - 1);
     const int grp = gw / G;
     const int lw_first = max(w_first, grp * G), lw_last = min(w_last, grp * G + G - 1);
-    float v[2][4];
     if (lw_first == lw_last) {
 #pragma unroll
         for (int t = 0; t < 2; ++t)
@@ -516,11 +658,7 @@ __device__ __forceinline__ void finish_pair(const QmvK& p, int pair, int gw, int
     }
     const int g_first = w_first / G, g_last = w_last / G;
     if (g_first == g_last) {
-        if (active)
-#pragma unroll
-            for (int t = 0; t < 2; ++t)
-#pragma unroll
-                for (int i = 0; i < 4; ++i) store(t, i, v[t][i]);
+        pair_final<EPI>(p, pair, v, active, lane, s_ss);
         return;
     }
     // level 2: the groups, device-scope ordering, last arrival sums in group order
@@ -545,12 +683,8 @@ __device__ __forceinline__ void finish_pair(const QmvK& p, int pair, int gw, int
 #pragma unroll
             for (int i = 0; i < 4; ++i) sum[t][i] += sl[pidx(t, i)];
     }
-    if (active)
-#pragma unroll
-        for (int t = 0; t < 2; ++t)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) store(t, i, sum[t][i]);
     if (lane == 0) p.counters[pair] = 0u;   // ready for the next launch
+    pair_final<EPI>(p, pair, sum, active, lane, s_ss);
 }
 
 // fp16 path: combine the hi/lo columns of the mma accumulators
@@ -590,7 +724,9 @@ __device__ __forceinline__ void pair_out_i8(const float (&tok)[2][2][2], float (
     active = NT == 1 ? (c < 2) : true;
 }
 
-template <int FMT, int NT, bool I8>
+// EPI: the launch has a deferred input norm or a next-input epilogue (QbInNorm,
+// QbEpi); launches without either run the variant that has neither.
+template <int FMT, int NT, bool I8, bool EPI>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_kernel(QmvK p) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int TB = tile_block_bytes(FMT);
@@ -608,6 +744,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_kernel(QmvK p) {
 
     // per-CTA arrival counters of the pairs its warps share (level 1 of the split-pair combine)
     __shared__ unsigned s_lcnt[kLocalPairs];
+    __shared__ float s_ss[EPI ? kConsumers : 1][EPI ? kSsMax : 1];   // deferred-norm sums (QbInNorm), per warp
     for (int i = threadIdx.x; i < kLocalPairs; i += kThreads) s_lcnt[i] = 0u;
     __syncthreads();
     const int gw = blockIdx.x * kConsumers + warp;
@@ -647,6 +784,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_kernel(QmvK p) {
     if (lane == 0)
         for (int r = 0; r < R && r < n; ++r) issue(r);
     pdl_wait();   // activations written by the previous kernel are complete from here on
+    // the deferred norm's per-block sums: copied now, read at the first pair finish
+    if (EPI && p.in_ss && p.N * p.nb <= kSsMax)
+        for (int i = lane; i < p.N * p.nb; i += 32) cp_async4(&s_ss[warp][i], p.in_ss + i);
 
     float acc[2][NT][4];   // fp16 path: mma accumulator layout
     float tk[2][2][2];     // int8 path: (tile, row g + 8r, token c + 4k)
@@ -661,7 +801,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_kernel(QmvK p) {
         bool active;
         if (I8) pair_out_i8<NT>(tk, o, active, lane);
         else pair_out_f16<NT>(acc, o, active, lane);
-        finish_pair(p, pair, gw, s0, s1, o, active, lane, s_lcnt, grp_pair0);
+        finish_pair<EPI>(p, pair, gw, s0, s1, o, active, lane, s_lcnt, grp_pair0, s_ss[EPI ? warp : 0]);
     };
     reset();
     const int c = lane & 3;
@@ -799,7 +939,7 @@ __global__ void repack_kernel(int type, const uint8_t* __restrict__ src, size_t 
     const int g = lane >> 2, c = lane & 3;
     const int UB = qb_unit_bytes(type);
     uint8_t* d = dst + (size_t)gw * UB;
-    const int src_block = type == QB_Q8_0 ? 34 : UB / 16;
+    const int src_block = type == QB_Q8_0 ? 34 : type == QB_IQ4_XS ? 136 : UB / 16;
     auto rowp = [&](int rr) -> const uint8_t* {
         const int r = tile * QB_TILE + rr;
         return r < rows ? src + (size_t)r * row_bytes + (size_t)u * src_block : nullptr;
@@ -817,20 +957,25 @@ __global__ void repack_kernel(int type, const uint8_t* __restrict__ src, size_t 
             d32[(p * 512 + lane * 16) / 4 + 3] = w32(pg8, 8 + 16 * (2 * p + 1) + 4 * c);
         }
         if (lane < 16) {
-            // ls_ib = scales_l nibble ib | scales_h bits 2ib..2ib+1 << 4 (src/kernels.c:84-90)
+            // ls_ib = scales_l nibble ib | scales_h bits 2ib..2ib+1 << 4 (src/kernels.c:84-90),
+            // stored as the differences ls_j - ls_{j+1} (j < 7) and ls_7 - 32
             const uint8_t* rp = rowp(lane);
-            uint32_t A = 0, Bh = 0, dd = 0;
+            uint32_t D0 = 0, D1 = 0, dd = 0;
             if (rp) {
                 const uint32_t sh = rp[2] | (rp[3] << 8);
                 const uint32_t sl = w32(rp, 4);
-                uint32_t ls[8];
-                for (int ib = 0; ib < 8; ++ib) ls[ib] = ((sl >> (4 * ib)) & 0xF) | (((sh >> (2 * ib)) & 3) << 4);
-                for (int i = 0; i < 4; ++i) A |= (ls[i] | ((ls[4 + i] & 3) << 6)) << (8 * i);
-                for (int j = 0; j < 4; ++j) Bh |= (ls[4 + j] >> 2) << (4 * j);
+                int ls[9];
+                for (int ib = 0; ib < 8; ++ib) ls[ib] = (int)(((sl >> (4 * ib)) & 0xF) | (((sh >> (2 * ib)) & 3) << 4));
+                ls[8] = 32;
+                for (int j = 0; j < 4; ++j) {
+                    D0 |= ((uint32_t)(ls[j] - ls[j + 1]) & 0xFFu) << (8 * j);
+                    D1 |= ((uint32_t)(ls[4 + j] - ls[5 + j]) & 0xFFu) << (8 * j);
+                }
                 dd = rp[0] | (rp[1] << 8);
             }
-            d32[(2048 + lane * 8) / 4 + 0] = A;
-            d32[(2048 + lane * 8) / 4 + 1] = dd | (Bh << 16);
+            d32[(kIq4Dl + lane * 8) / 4 + 0] = D0;
+            d32[(kIq4Dl + lane * 8) / 4 + 1] = D1;
+            reinterpret_cast<uint16_t*>(d + kIq4D)[lane] = (uint16_t)dd;
         }
     } else if (type == QB_Q8_0) {
         d32[lane * 4 + 0] = w32(pg, 2 + 4 * c);
@@ -1002,7 +1147,7 @@ cudaError_t qb_repack(int type, const void* src_dev, int rows, int K, void* dst_
     const int ub = qb_unit_bytes(type), uc = qb_unit_cols(type);
     if (!ub || K % 256) return cudaErrorInvalidValue;
     const int upr = K / uc;
-    const size_t row_bytes = (size_t)upr * (type == QB_Q8_0 ? 34 : ub / 16);
+    const size_t row_bytes = (size_t)upr * (type == QB_Q8_0 ? 34 : type == QB_IQ4_XS ? 136 : ub / 16);
     const long long units = (long long)padded_tiles(rows) * upr;
     const int threads = 256;
     const long long blocks = (units * 32 + threads - 1) / threads;
@@ -1048,8 +1193,10 @@ cudaError_t qb_xprep(const QbXIn* in, int nseg, int N, float eps, const QbXBuf& 
 
 static int g_num_sms = 0;
 
-cudaError_t qb_qmv(int type, const QbQSeg* segs, int nseg, int K, int N, const QbXBuf& xb, int accumulate,
-                   int row_lo, int row_hi, const QbQmvWork& work, cudaStream_t st) {
+namespace {
+cudaError_t qmv_launch(int type, const QbQSeg* segs, int nseg, int K, int N, const QbXBuf& xb, int accumulate,
+                       int row_lo, int row_hi, const QbInNorm* in_norm, const QbEpi* epi, const QbQmvWork& work,
+                       cudaStream_t st) {
     if (nseg < 1 || nseg > QB_MAX_SEG || N < 1 || N > QB_MAX_TOK || K % 256) return cudaErrorInvalidValue;
     if (!g_num_sms) {
         int dev = 0;
@@ -1111,15 +1258,45 @@ cudaError_t qb_qmv(int type, const QbQSeg* segs, int nseg, int K, int N, const Q
         p.group = per_cta / p.nb + 2 <= kLocalPairs ? kConsumers : 1;
     }
     p.err = work.err;
+    if (in_norm && in_norm->ss) {
+        p.in_ss = in_norm->ss;
+        p.in_eps = in_norm->eps;
+    }
+    if (epi && epi->kind != QB_EPI_NONE) {
+        // one matrix, whole output, whole 256-row blocks; the fragments go to another buffer
+        const int rows = segs[0].rows;
+        const bool swiglu = epi->kind == QB_EPI_SWIGLU;
+        const int next_k = swiglu ? rows / 2 : rows;
+        if (nseg != 1 || row_lo > 0 || row_hi < rows || next_k % 256 || !work.bcounters ||
+            (epi->kind != QB_EPI_NORM && !swiglu) || (swiglu && (accumulate || !epi->h || epi->ldh < next_k)) ||
+            (!swiglu && (!epi->norm_w || !epi->ss)) || epi->xb.xq == xb.xq || epi->xb.xfrag == xb.xfrag ||
+            next_k / 256 > work.max_pairs)
+            return cudaErrorInvalidValue;
+        const int what = epi->what;
+        if (((what & QB_XP_F16) && (!epi->xb.xfrag || !epi->xb.xscale)) || ((what & QB_XP_SUM) && !epi->xb.xsum) ||
+            ((what & QB_XP_I8) && (!epi->xb.xq || !epi->xb.xqscale)) || (what & QB_XP_TC) || !what)
+            return cudaErrorInvalidValue;
+        p.epi = epi->kind;
+        p.bcnt = work.bcounters;
+        p.epi_w = epi->norm_w;
+        p.epi_ss = epi->ss;
+        p.epi_h = epi->h;
+        p.epi_ldh = epi->ldh;
+        p.epi_K = next_k;
+        p.epi_what = what;
+        p.epi_xb = epi->xb;
+    }
     const bool nt2 = N > 4;
+    const bool epi_k = p.in_ss != nullptr || p.epi != QB_EPI_NONE;
     cudaError_t e = cudaSuccess;
 #define QB_LAUNCH(F, I8)                                                                               \
     do {                                                                                               \
-        auto kern = nt2 ? qmv_kernel<F, 2, I8> : qmv_kernel<F, 1, I8>;                                 \
-        static bool attr_set[2] = {false, false};                                                      \
-        if (!attr_set[nt2]) {                                                                          \
+        auto kern = epi_k ? (nt2 ? qmv_kernel<F, 2, I8, true> : qmv_kernel<F, 1, I8, true>)           \
+                          : (nt2 ? qmv_kernel<F, 2, I8, false> : qmv_kernel<F, 1, I8, false>);         \
+        static bool attr_set[4] = {false, false, false, false};                                        \
+        if (!attr_set[nt2 + 2 * epi_k]) {                                                              \
             cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);       \
-            attr_set[nt2] = true;                                                                      \
+            attr_set[nt2 + 2 * epi_k] = true;                                                          \
         }                                                                                              \
         e = qb_launch(kern, dim3(grid), dim3(kThreads), smem, st, p);                                  \
     } while (0)
@@ -1134,6 +1311,27 @@ cudaError_t qb_qmv(int type, const QbQSeg* segs, int nseg, int K, int N, const Q
 #undef QB_LAUNCH
     return e;
 }
+}  // namespace
+
+cudaError_t qb_qmv(int type, const QbQSeg* segs, int nseg, int K, int N, const QbXBuf& xb, int accumulate,
+                   int row_lo, int row_hi, const QbQmvWork& work, cudaStream_t st) {
+    return qmv_launch(type, segs, nseg, K, N, xb, accumulate, row_lo, row_hi, nullptr, nullptr, work, st);
+}
+
+cudaError_t qb_qmv_ex(int type, const QbQSeg* segs, int nseg, int K, int N, const QbXBuf& xb, int accumulate,
+                      const QbInNorm* in_norm, const QbEpi* epi, const QbQmvWork& work, cudaStream_t st) {
+    return qmv_launch(type, segs, nseg, K, N, xb, accumulate, 0, 1 << 30, in_norm, epi, work, st);
+}
+
+cudaError_t qb_interleave_tiles(int type, const void* a, const void* b, int rows, int K, void* dst, cudaStream_t st) {
+    const int ub = qb_unit_bytes(type), uc = qb_unit_cols(type);
+    if (!ub || K % 256 || rows % 16 || rows <= 0) return cudaErrorInvalidValue;
+    const size_t tile = (size_t)(K / uc) * ub;   // the units of one 16-row tile
+    const size_t tiles = (size_t)rows / 16;
+    cudaError_t e = cudaMemcpy2DAsync(dst, 2 * tile, a, tile, tile, tiles, cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess) return e;
+    return cudaMemcpy2DAsync((uint8_t*)dst + tile, 2 * tile, b, tile, tile, tiles, cudaMemcpyDeviceToDevice, st);
+}
 
 cudaError_t qb_qmv_work_alloc(QbQmvWork& w, int max_pairs) {
     int dev = 0, sms = 0;
@@ -1145,6 +1343,8 @@ cudaError_t qb_qmv_work_alloc(QbQmvWork& w, int max_pairs) {
     if ((e = cudaMalloc(&w.partial, (size_t)w.max_warps * 2 * 256 * sizeof(float))) != cudaSuccess) return e;
     if ((e = cudaMalloc(&w.gpartial, (size_t)w.max_warps * 2 * 256 * sizeof(float))) != cudaSuccess) return e;
     if ((e = cudaMalloc(&w.counters, (size_t)max_pairs * sizeof(unsigned))) != cudaSuccess) return e;
+    if ((e = cudaMalloc(&w.bcounters, (size_t)max_pairs * sizeof(unsigned))) != cudaSuccess) return e;
+    if ((e = cudaMemset(w.bcounters, 0, (size_t)max_pairs * sizeof(unsigned))) != cudaSuccess) return e;
     if ((e = cudaMalloc(&w.err, sizeof(unsigned))) != cudaSuccess) return e;
     if ((e = cudaMemset(w.counters, 0, (size_t)max_pairs * sizeof(unsigned))) != cudaSuccess) return e;
     w.max_tc_ctas = qb_qmv_tc_max_ctas();
@@ -1163,6 +1363,7 @@ void qb_qmv_work_free(QbQmvWork& w) {
     if (w.tc_partial) cudaFree(w.tc_partial);
     if (w.tc_counters) cudaFree(w.tc_counters);
     if (w.counters) cudaFree(w.counters);
+    if (w.bcounters) cudaFree(w.bcounters);
     if (w.err) cudaFree(w.err);
     w = QbQmvWork{};
 }
