@@ -26,7 +26,7 @@
 // Pipeline.  Two persistent CTAs of 8 warps per SM.  Every warp streams its
 // own (pair of tiles x 256 columns) stages of contiguous repacked bytes into
 // a private shared-memory ring with cp.async.bulk and mbarrier completion,
-// refilling a slot as soon as it has decoded it (~100 KB in flight per SM),
+// refilling a slot as soon as it has decoded it (~140 KB in flight per SM),
 // and decodes / runs the MMAs from shared memory.  The flattened (tile pair, block) stage
 // space of all fused matrices is split evenly over every consumer warp of
 // the grid (stream-K); a tile pair split across warps is finished by the last
@@ -57,8 +57,11 @@ constexpr int kThreads = kConsumers * 32;
 #define QB_QMV_CTAS 2
 #endif
 constexpr int kCtasPerSm = QB_QMV_CTAS;
+// ring budget per CTA: 80 KB gives IQ4_XS a 2-stage ring per warp (141 KB in
+// flight per SM, well above what HBM latency needs) and leaves the rest of the
+// SM's shared memory to L1
 #ifndef QB_QMV_SMEM_KB
-#define QB_QMV_SMEM_KB (224 / QB_QMV_CTAS)
+#define QB_QMV_SMEM_KB 80
 #endif
 constexpr int kSmemBudget = QB_QMV_SMEM_KB * 1024;   // per CTA
 #ifndef QB_QMV_MIN_STAGES
@@ -577,7 +580,7 @@ __device__ __forceinline__ void pair_final(const QmvK& p, int pair, float (&v)[2
                 const int tok = (i & 1) ? t1 : t0;
                 if (tok < p.N && rr < S.rows && rr >= p.row_lo && rr < p.row_hi) {
                     float* dst = S.out + (size_t)tok * S.ldo + rr;
-                    *dst = p.accumulate ? (*dst + v[t][i]) : v[t][i];
+                    *dst = p.accumulate ? (__ldcg(dst) + v[t][i]) : v[t][i];
                 }
             }
     }
