@@ -224,6 +224,32 @@ float qb_bench(qwen_model_t *m, int what, uint32_t arg, uint32_t iters, double *
  * MTP residual, 16 h_save) to host.  Returns the float count, -1 on error. */
 int64_t qb_read_buffer(qwen_model_t *m, int id, float *dst, int64_t max_floats);
 
+/* ---- tensor parallelism (no counterpart function in the reference; it
+ *      splits the rows of every GEMV as src/kernels.c:608-613 splits them
+ *      over CPU threads, here over GPUs) ----
+ *
+ * One process per GPU.  Every rank loads the same GGUF with
+ * qb_model_init_tp(m, path, n_ctx, rank, world) (world <= 8; model_init is
+ * world = 1) and keeps rows [r0, r1) of every quantised matrix
+ * (qb_tp_rows; the output head splits over the vocabulary).  Everything else
+ * is replicated.  Each GEMV stores its rows into every rank's copy of the
+ * output over NVLink and ends with a bounded cross-rank barrier, so all
+ * ranks hold identical activations, logits and tokens.
+ *
+ * Set-up: qb_tp_handle() writes this rank's 64-byte IPC handle of its
+ * activation arena; the caller exchanges the handles of all ranks (any host
+ * channel) and passes them, rank-ordered `stride` bytes apart, to
+ * qb_tp_connect().  Then every rank calls the same sequence of model API
+ * functions with the same arguments.  Before model_free, synchronise the
+ * ranks on the host so that no rank still writes into a freed peer.
+ * Returns: init / connect 0 or -1; handle the byte count or -1. */
+int qb_model_init_tp(qwen_model_t *m, const char *gguf_path, uint32_t n_ctx, int rank, int world);
+int64_t qb_tp_handle(qwen_model_t *m, void *out, int64_t cap);
+int qb_tp_connect(qwen_model_t *m, const void *handles, int64_t stride);
+/* The row range [*r0, *r1) of a rows-row matrix held by rank of world:
+ * whole 32-row tile pairs, split as evenly as possible. */
+void qb_tp_rows(int rows, int rank, int world, int *r0, int *r1);
+
 /* ---- allocation-free entry point (no counterpart in the reference) ----
  *
  * For callers that cannot allocate device memory at call time: a runtime that

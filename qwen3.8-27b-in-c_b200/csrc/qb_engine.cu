@@ -240,6 +240,7 @@ constexpr int kNSlot = 4;
 struct DevMat {
     int type = -1;
     int rows = 0, K = 0;
+    int row0 = 0, rows_all = 0;   // tensor parallelism: this rank holds rows [row0, row0 + rows) of rows_all
     void* w = nullptr;      // repacked into 16-row mma.sync tiles (quant) or plain row-major (F32)
     void* w_tc = nullptr;   // IQ4_XS also in 128-row tcgen05 tiles (qb_qmv_tc, N <= 4)
     uint64_t fingerprint = 0;   // host-API weight cache only
@@ -306,6 +307,15 @@ struct Engine {
     bool xready = false;                  // xb already holds the next normed input (fused epilogue)
     bool fuse = false;                    // fused GEMV epilogues (QB_FUSE=1; mma.sync path only)
     float* ss = nullptr;                  // [QB_MAX_TOK][Kmax / 256]
+    // tensor parallelism (qb_model_init_tp / qb_tp_connect): this rank holds a row
+    // range of every quantised matrix; the GEMV outputs live in an arena that every
+    // peer maps, and each GEMV stores its rows into all copies
+    int tp_rank = 0, tp_world = 1;
+    bool tp_ready = false;                // peers connected
+    char* arena = nullptr;                // GEMV outputs + TP flags (cudaMalloc'd: IPC-shareable)
+    size_t arena_bytes = 0;
+    QbTp tp{};
+    void* peer_arena[QB_TP_MAX] = {};     // peers' arenas mapped here
     bool use_tc = false;                  // IQ4_XS at N <= 4 on tcgen05 (QB_TC=1); default: int8 mma.sync
     float* attn_po = nullptr;             // attention chunk partials (qb_attn_decode)
     float2* gates = nullptr;              // DeltaNet (beta, decay) per (token, v-head)
@@ -347,6 +357,11 @@ struct Engine {
 
 Engine::~Engine() {
     cudaSetDevice(dev);
+    for (void*& p : peer_arena)
+        if (p) {
+            cudaIpcCloseMemHandle(p);
+            p = nullptr;
+        }
     if (g_cycle) cudaGraphExecDestroy(g_cycle);
     if (g_greedy) cudaGraphExecDestroy(g_greedy);
     if (ev0) cudaEventDestroy(ev0);
@@ -356,13 +371,37 @@ Engine::~Engine() {
     if (st) cudaStreamDestroy(st);
 }
 
+}  // namespace
+
+// Rows of a matrix held by one rank: whole 32-row tile pairs, split evenly.
+extern "C" void qb_tp_rows(int rows, int rank, int world, int* r0, int* r1) {
+    const long long pairs = (rows + 31) / 32;
+    const int p0 = (int)(pairs * rank / world), p1 = (int)(pairs * (rank + 1) / world);
+    *r0 = std::min(rows, 32 * p0);
+    *r1 = std::min(rows, 32 * p1);
+}
+
+namespace {
+
 int upload_mat(Engine& e, const GTensor* t, DevMat& m, void* tmp, size_t tmp_bytes) {
     if (!t) { set_err(-1, "missing tensor"); return -1; }
     m.type = t->type;
     m.K = (int)t->ne[0];
-    m.rows = (int)t->ne[1];
-    const size_t src_bytes = gguf_row_bytes(t->type, t->ne[0]) * t->ne[1];
+    m.rows = m.rows_all = (int)t->ne[1];
+    m.row0 = 0;
+    size_t src_bytes = gguf_row_bytes(t->type, t->ne[0]) * t->ne[1];
     if (!src_bytes) { set_err(-1, "tensor %s: unsupported type %d", t->name.c_str(), t->type); return -1; }
+    const uint8_t* src = (const uint8_t*)t->data;
+    if (e.tp_world > 1 && t->type != QB_F32) {   // this rank's rows only
+        int r0 = 0, r1 = 0;
+        qb_tp_rows(m.rows_all, e.tp_rank, e.tp_world, &r0, &r1);
+        const size_t rb = gguf_row_bytes(t->type, t->ne[0]);
+        m.row0 = r0;
+        m.rows = r1 - r0;
+        src += (size_t)r0 * rb;
+        src_bytes = (size_t)m.rows * rb;
+        if (m.rows == 0) return 0;
+    }
     if (t->type == QB_F32) {
         m.w = e.dalloc(src_bytes);
         if (!m.w) { set_err(-2, "cudaMalloc %zu", src_bytes); return -1; }
@@ -375,7 +414,7 @@ int upload_mat(Engine& e, const GTensor* t, DevMat& m, void* tmp, size_t tmp_byt
     m.w = e.dalloc(rb);
     if (!m.w) { set_err(-2, "cudaMalloc %zu", rb); return -1; }
     // stream-ordered: the repack must not start before the host->device copy lands
-    CK(cudaMemcpyAsync(tmp, t->data, src_bytes, cudaMemcpyHostToDevice, e.st));
+    CK(cudaMemcpyAsync(tmp, src, src_bytes, cudaMemcpyHostToDevice, e.st));
     CK(qb_repack(t->type, tmp, m.rows, m.K, m.w, e.st));
     if (t->type == QB_IQ4_XS && e.use_tc) {
         const size_t rt = qb_repacked_bytes_tc(m.rows, m.K);
@@ -452,10 +491,11 @@ int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
     e.n_ctx = (int)n_ctx;
     e.rope_half = (int)c.rope_dim_count / 2;
     {
+        // tensor parallelism runs the mma.sync GEMV without fused epilogues
         const char* tc = getenv("QB_TC");
-        e.use_tc = tc && tc[0] == '1';
+        e.use_tc = e.tp_world == 1 && tc && tc[0] == '1';
         const char* fz = getenv("QB_FUSE");
-        e.fuse = !e.use_tc && fz && fz[0] == '1';
+        e.fuse = e.tp_world == 1 && !e.use_tc && fz && fz[0] == '1';
     }
 
     // temp buffer for repacking = largest quantised tensor
@@ -546,7 +586,7 @@ int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
             !(e.hnorm = upload_f32(e, T("blk.%d.nextn.hnorm.weight", im))) ||
             !(e.shnorm = upload_f32(e, T("blk.%d.nextn.shared_head_norm.weight", im))))
             return -1;
-        if (e.eh_proj.K != 2 * e.E || e.eh_proj.rows != e.E) { set_err(-1, "eh_proj shape"); return -1; }
+        if (e.eh_proj.K != 2 * e.E || e.eh_proj.rows_all != e.E) { set_err(-1, "eh_proj shape"); return -1; }
     }
 
     // ---- states ----
@@ -594,25 +634,35 @@ int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
     const int T8 = QB_MAX_TOK;
     e.ld_qkv = std::max<int>({(int)d.conv_dim, 2 * (int)d.n_head * (int)d.head_dim, e.F, 2 * e.E});
     auto A = [&](size_t n) { return (float*)e.dalloc(n * 4); };
-    e.bx = A((size_t)T8 * e.E);
+    {   // every buffer a GEMV writes, plus the TP flags, in one arena (peers map it)
+        const size_t sz[12] = {(size_t)T8 * e.E,      (size_t)T8 * e.ld_qkv,   (size_t)T8 * d.d_inner,
+                               (size_t)T8 * 256,      (size_t)T8 * 256,        (size_t)T8 * 2 * d.n_head * d.head_dim,
+                               (size_t)T8 * 2 * d.n_kv_head * d.head_dim,      (size_t)T8 * e.F,
+                               (size_t)T8 * e.F,      (size_t)T8 * e.V,        (size_t)T8 * e.E,
+                               (size_t)T8 * e.V};
+        float** dst[12] = {&e.bx, &e.qkv, &e.z, &e.beta, &e.alpha, &e.qbuf, &e.kvbuf, &e.gate, &e.up, &e.logits,
+                           &e.mtp_x, &e.mtp_logits};
+        size_t off[12], total = 0;
+        for (int i = 0; i < 12; ++i) {
+            off[i] = total;
+            total += (sz[i] * 4 + 255) / 256 * 256;
+        }
+        const size_t flags_off = total;
+        total += 256;
+        e.arena = (char*)e.dalloc(total);
+        if (!e.arena) { set_err(-2, "activation arena alloc"); return -1; }
+        e.arena_bytes = total;
+        CK(cudaMemset(e.arena, 0, total));
+        for (int i = 0; i < 12; ++i) *dst[i] = (float*)(e.arena + off[i]);
+        e.tp.flags = (unsigned*)(e.arena + flags_off);
+    }
     e.h_save = A((size_t)T8 * e.E);
-    e.qkv = A((size_t)T8 * e.ld_qkv);
     e.qkvc = A((size_t)T8 * e.ld_qkv);
-    e.z = A((size_t)T8 * d.d_inner);
-    e.beta = A((size_t)T8 * 256);
-    e.alpha = A((size_t)T8 * 256);
     e.o = A((size_t)T8 * d.d_inner);
     e.y = A((size_t)T8 * d.d_inner);
-    e.qbuf = A((size_t)T8 * 2 * d.n_head * d.head_dim);
-    e.kvbuf = A((size_t)T8 * 2 * d.n_kv_head * d.head_dim);
     e.attn_o = A((size_t)T8 * d.n_head * d.head_dim);
-    e.gate = A((size_t)T8 * e.F);
-    e.up = A((size_t)T8 * e.F);
     e.act = A((size_t)T8 * e.F);
-    e.logits = A((size_t)T8 * e.V);
-    e.mtp_x = A((size_t)T8 * e.E);
     e.mtp_h = A((size_t)e.E);
-    e.mtp_logits = A((size_t)T8 * e.V);
     e.emb = A((size_t)T8 * e.E);
     const int Kmax = std::max<int>({2 * e.E, e.F, (int)d.d_inner, (int)(d.n_head * d.head_dim)});
     e.xb.xfrag = (uint2*)e.dalloc(qb_xfrag_bytes(Kmax));
@@ -681,22 +731,31 @@ int gemv_group(Engine& e, const DevMat* const* mats, float* const* outs, const l
         QbQSeg segs[QB_MAX_SEG];
         int ns = 0;
         const int type = mats[i]->type;
-        while (i < nm && ns < QB_MAX_SEG && mats[i]->type == type) {
-            segs[ns].w = mats[i]->w;
-            segs[ns].out = outs[i];
-            segs[ns].ldo = ldos[i];
-            segs[ns].rows = mats[i]->rows;
-            ++ns;
+        int nt = 0;   // matrices of this launch (with or without rows on this rank)
+        while (i < nm && nt < QB_MAX_SEG && mats[i]->type == type) {
+            if (mats[i]->rows > 0) {   // tensor parallelism: this rank's rows land at their global index
+                segs[ns].w = mats[i]->w;
+                segs[ns].out = outs[i] + mats[i]->row0;
+                segs[ns].ldo = ldos[i];
+                segs[ns].rows = mats[i]->rows;
+                ++ns;
+            }
+            ++nt;
             ++i;
+        }
+        if (e.tp_world > 1) {
+            if (!e.tp_ready || type == QB_F32) { set_err(-1, "tensor-parallel GEMV before qb_tp_connect"); return -1; }
+            CK(qb_qmv_ex(type, segs, ns, K, N, e.xb, accumulate, nullptr, nullptr, &e.tp, e.work, e.st));
+            continue;
         }
         if (type == QB_F32) {
             for (int s = 0; s < ns; ++s) CK(cudaErrorNotSupported);
         } else if (type == QB_IQ4_XS && N <= 4 && e.use_tc) {
             if (e.xss || epi) { set_err(-1, "fused epilogues need the mma.sync GEMV"); return -1; }
-            for (int s = 0; s < ns; ++s) segs[s].w = mats[i - ns + s]->w_tc;
+            for (int s = 0; s < ns; ++s) segs[s].w = mats[i - nt + s]->w_tc;
             CK(qb_qmv_tc(segs, ns, K, N, e.xb, accumulate, 0, 1 << 30, e.work, e.st));
         } else {
-            CK(qb_qmv_ex(type, segs, ns, K, N, e.xb, accumulate, &in_norm, epi, e.work, e.st));
+            CK(qb_qmv_ex(type, segs, ns, K, N, e.xb, accumulate, &in_norm, epi, nullptr, e.work, e.st));
         }
     }
     e.xready = epi != nullptr;
@@ -1037,6 +1096,20 @@ int ensure_out_buffers(Engine& e, uint32_t n_out, uint32_t n_j, uint32_t n_force
 
 Engine* E_(qwen_model_t* m) { return m ? (Engine*)m->eng : nullptr; }
 
+// Wait for the stream; a kernel whose bounded wait gave up (a ring copy, a
+// tensor-parallel peer) left a code in work.err, reported here as an error.
+int dev_sync(Engine& e) {
+    CK(cudaStreamSynchronize(e.st));
+    unsigned code = 0;
+    CK(cudaMemcpy(&code, e.work.err, sizeof code, cudaMemcpyDeviceToHost));
+    if (code) {
+        cudaMemset(e.work.err, 0, sizeof code);
+        set_err(-3, "a device-side wait gave up (code %u: 2 weight copy, 4 tensor-parallel peer)", code);
+        return -1;
+    }
+    return 0;
+}
+
 int sync_host_mirrors_after_batch(qwen_model_t* m, Engine& e, int B) {
     CK(cudaMemcpyAsync(m->logits_b, e.logits, (size_t)B * e.V * 4, cudaMemcpyDeviceToHost, e.st));
     CK(cudaMemcpyAsync(m->h_save, e.h_save, (size_t)B * e.E * 4, cudaMemcpyDeviceToHost, e.st));
@@ -1059,9 +1132,17 @@ extern "C" void pool_destroy(pool_t* p) { free(p); }
 extern "C" void pool_run(pool_t*, pool_fn_t fn, void* arg) { fn(arg, 0, 1); }
 
 extern "C" int model_init(qwen_model_t* m, const char* path, uint32_t n_ctx) {
-    if (!m || !path) return -1;
+    return qb_model_init_tp(m, path, n_ctx, 0, 1);
+}
+
+extern "C" int qb_model_init_tp(qwen_model_t* m, const char* path, uint32_t n_ctx, int rank, int world) {
+    if (!m || !path || world < 1 || world > QB_TP_MAX || rank < 0 || rank >= world) return -1;
     memset(m, 0, sizeof *m);
     Engine* e = new Engine();
+    e->tp_rank = rank;
+    e->tp_world = world;
+    e->tp.rank = rank;
+    e->tp.world = world;
     if (engine_init(*e, path, n_ctx)) {
         delete e;
         return -1;
@@ -1080,6 +1161,44 @@ extern "C" int model_init(qwen_model_t* m, const char* path, uint32_t n_ctx) {
         return -1;
     }
     memset(m->mtp_h, 0, (size_t)e->E * 4);
+    return 0;
+}
+
+extern "C" int64_t qb_tp_handle(qwen_model_t* m, void* out, int64_t cap) {
+    Engine* e = E_(m);
+    if (!e || !out || cap < (int64_t)sizeof(cudaIpcMemHandle_t)) return -1;
+    cudaSetDevice(e->dev);
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, e->arena) != cudaSuccess) { set_err(-2, "cudaIpcGetMemHandle"); return -1; }
+    memcpy(out, &h, sizeof h);
+    return (int64_t)sizeof h;
+}
+
+extern "C" int qb_tp_connect(qwen_model_t* m, const void* handles, int64_t stride) {
+    Engine* e = E_(m);
+    if (!e || !handles || stride < (int64_t)sizeof(cudaIpcMemHandle_t) || e->tp_world < 2 || e->tp_ready) return -1;
+    cudaSetDevice(e->dev);
+    int q = 0;
+    for (int r = 0; r < e->tp_world; ++r) {
+        if (r == e->tp_rank) continue;
+        cudaIpcMemHandle_t h;
+        memcpy(&h, (const char*)handles + (size_t)r * stride, sizeof h);
+        void* p = nullptr;
+        if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            set_err(-2, "cudaIpcOpenMemHandle (rank %d)", r);
+            return -1;
+        }
+        e->peer_arena[r] = p;
+        e->tp.delta[q++] = (long long)((char*)p - e->arena);
+    }
+    e->tp.done = (unsigned*)e->dalloc(256);
+    if (!e->tp.done) { set_err(-2, "tp counters"); return -1; }
+    e->tp.seq = e->tp.done + 32;
+    if (cudaMemset(e->tp.done, 0, 256) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+        set_err(-2, "tp counters");
+        return -1;
+    }
+    e->tp_ready = true;
     return 0;
 }
 
@@ -1159,7 +1278,7 @@ static int do_mtp(qwen_model_t* m, const uint32_t* tokens, uint32_t pos, uint32_
         else
             CK(cudaMemcpyAsync(m->logits, e->mtp_logits, (size_t)e->V * 4, cudaMemcpyDeviceToHost, e->st));
     }
-    CK(cudaStreamSynchronize(e->st));
+    if (dev_sync(*e)) return -1;
     return 0;
 }
 
@@ -1204,7 +1323,7 @@ extern "C" int qb_prefill(qwen_model_t* m, const uint32_t* tokens, uint32_t n, i
             CK(cudaMemcpyAsync(&e->ctrl->mtp_pos, &pos, 4, cudaMemcpyHostToDevice, e->st));
             if (fwd_mtp(*e, (int)B, e->h_save, 0)) return -1;
         }
-        CK(cudaStreamSynchronize(e->st));   // host token/pos sources must outlive the copies
+        if (dev_sync(*e)) return -1;   // host token/pos sources must outlive the copies
         pos += B;
         lastB = B;
     }
@@ -1214,7 +1333,7 @@ extern "C" int qb_prefill(qwen_model_t* m, const uint32_t* tokens, uint32_t n, i
                        e->st));
     CK(cudaMemcpyAsync(m->h_save, e->h_save, (size_t)lastB * e->E * 4, cudaMemcpyDeviceToHost, e->st));
     CK(cudaMemcpyAsync(m->mtp_h, e->mtp_h, (size_t)e->E * 4, cudaMemcpyDeviceToHost, e->st));
-    CK(cudaStreamSynchronize(e->st));
+    if (dev_sync(*e)) return -1;
     m->pos = n;
     return 0;
 }
@@ -1237,7 +1356,7 @@ extern "C" int qb_spec_generate(qwen_model_t* m, uint32_t n_predict, uint32_t n_
     // loop state: P = pos - 1, counters reset, host mirror mtp_h is authoritative
     QbCtrl hc;
     CK(cudaMemcpyAsync(&hc, e->ctrl, sizeof hc, cudaMemcpyDeviceToHost, e->st));
-    CK(cudaStreamSynchronize(e->st));
+    if (dev_sync(*e)) return -1;
     hc.P = m->pos - 1;
     hc.k = (uint32_t)k;
     hc.cycle = 0;
@@ -1263,11 +1382,11 @@ extern "C" int qb_spec_generate(qwen_model_t* m, uint32_t n_predict, uint32_t n_
         cycles += batch;
         uint32_t dev_counts[2];
         CK(cudaMemcpyAsync(dev_counts, &e->ctrl->cycle, 8, cudaMemcpyDeviceToHost, e->st));   // cycle, n_out
-        CK(cudaStreamSynchronize(e->st));
+        if (dev_sync(*e)) return -1;
         n_out = dev_counts[1];
         uint32_t P;
         CK(cudaMemcpyAsync(&P, &e->ctrl->P, 4, cudaMemcpyDeviceToHost, e->st));
-        CK(cudaStreamSynchronize(e->st));
+        if (dev_sync(*e)) return -1;
         if (P + (uint32_t)k + 3 > (uint32_t)e->n_ctx) break;   // next cycle would pass n_ctx
     }
     CK(cudaEventRecord(e->ev1, e->st));
@@ -1280,11 +1399,11 @@ extern "C" int qb_spec_generate(qwen_model_t* m, uint32_t n_predict, uint32_t n_
     if (n_cycles) *n_cycles = cycles;
     // host mirrors: position, next logits (logits_b[j]), MTP hidden
     CK(cudaMemcpyAsync(&hc, e->ctrl, sizeof hc, cudaMemcpyDeviceToHost, e->st));
-    CK(cudaStreamSynchronize(e->st));
+    if (dev_sync(*e)) return -1;
     m->pos = hc.P + 1;
     CK(cudaMemcpyAsync(m->logits, e->logits + (size_t)hc.j * e->V, (size_t)e->V * 4, cudaMemcpyDeviceToHost, e->st));
     CK(cudaMemcpyAsync(m->mtp_h, e->mtp_h, (size_t)e->E * 4, cudaMemcpyDeviceToHost, e->st));
-    CK(cudaStreamSynchronize(e->st));
+    if (dev_sync(*e)) return -1;
     return (int)n_copy;
 }
 
@@ -1298,7 +1417,7 @@ extern "C" int qb_greedy_generate(qwen_model_t* m, uint32_t n_predict, uint32_t*
     // token 0 = argmax(m->logits): the device argmax of the last forward
     QbCtrl hc;
     CK(cudaMemcpyAsync(&hc, e->ctrl, sizeof hc, cudaMemcpyDeviceToHost, e->st));
-    CK(cudaStreamSynchronize(e->st));
+    if (dev_sync(*e)) return -1;
     hc.fwd_tok[0] = hc.next_cand0;
     hc.fwd_pos = m->pos;
     hc.greedy_n = 1;
@@ -1318,7 +1437,7 @@ extern "C" int qb_greedy_generate(qwen_model_t* m, uint32_t n_predict, uint32_t*
     CK(cudaMemcpyAsync(m->logits, e->logits, (size_t)e->V * 4, cudaMemcpyDeviceToHost, e->st));
     // keep next_cand0 = argmax of the last forward for a following call
     CK(cudaMemcpyAsync(&e->ctrl->next_cand0, &e->ctrl->argmax[0], 4, cudaMemcpyDeviceToDevice, e->st));
-    CK(cudaStreamSynchronize(e->st));
+    if (dev_sync(*e)) return -1;
     return (int)n;
 }
 
@@ -1359,14 +1478,14 @@ extern "C" int qb_reset(qwen_model_t* m) {
     CK(cudaMemsetAsync(e->mtp_h, 0, (size_t)e->E * 4, e->st));
     set_u32_kernel<<<1, 1, 0, e->st>>>(&e->ctrl->cur_slot, 0u);
     CK(cudaGetLastError());
-    CK(cudaStreamSynchronize(e->st));
+    if (dev_sync(*e)) return -1;
     memset(m->mtp_h, 0, (size_t)e->E * 4);
     m->pos = 0;
     return 0;
 }
 
 namespace {
-size_t mat_bytes(const DevMat& w) { return gguf_row_bytes(w.type, (uint64_t)w.K) * (size_t)w.rows; }
+size_t mat_bytes(const DevMat& w) { return gguf_row_bytes(w.type, (uint64_t)w.K) * (size_t)w.rows_all; }
 
 int record_verify(Engine& e, int B) { return fwd_backbone(e, B, 1); }
 int record_draft(Engine& e, int) { return fwd_mtp(e, 1, e.mtp_h, 1); }

@@ -87,8 +87,24 @@ struct QbInNorm {
     const float* ss;
     float eps;
 };
+// Tensor parallelism of one GEMV launch (row-sharded weights, one process per
+// GPU): the segments hold this rank's rows, every output value is stored both
+// locally and at the same address of each peer's buffer (dst + delta[i], over
+// NVLink), and the launch ends with a bounded cross-rank barrier, so that when
+// it completes every rank holds all rows.  The output buffers, and flags, lie
+// in an arena each peer has mapped.
+#define QB_TP_MAX 8
+struct QbTp {
+    int rank, world;
+    long long delta[QB_TP_MAX - 1];   // peer i (ranks in order, this one skipped): its address - ours
+    unsigned* flags;                  // [QB_TP_MAX] in the shared arena, zero-initialised
+    unsigned* done;                   // zero-initialised
+    unsigned* seq;                    // zero-initialised; counts this rank's TP launches
+};
+// nseg == 0 is allowed with tp (a rank without rows of this launch still takes part in the barrier)
 cudaError_t qb_qmv_ex(int type, const QbQSeg* segs, int nseg, int K, int N, const QbXBuf& xb, int accumulate,
-                      const QbInNorm* in_norm, const QbEpi* epi, const QbQmvWork& work, cudaStream_t st);
+                      const QbInNorm* in_norm, const QbEpi* epi, const QbTp* tp, const QbQmvWork& work,
+                      cudaStream_t st);
 // Tile-interleaved copy of two repacked matrices of equal shape (rows % 16 == 0):
 // dst tile 2i = tile i of a, dst tile 2i + 1 = tile i of b.  dst holds
 // qb_repacked_bytes(type, 2 * rows, K) bytes.

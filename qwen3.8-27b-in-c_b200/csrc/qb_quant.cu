@@ -415,6 +415,15 @@ __host__ __device__ constexpr int tile_block_bytes(int type) {
 
 // ------------------------------- the kernel ------------------------------------
 
+struct TpK {
+    int np, rank;                // peers, this rank
+    long long delta[QB_TP_MAX - 1];   // byte offset from a local arena address to the same address of peer i
+    unsigned* flags;             // [QB_TP_MAX] in the shared arena: the last sequence number seen from each rank
+    unsigned* done;              // warps of the grid that finished (zero between launches)
+    unsigned* seq;               // this rank's count of TP launches
+    unsigned* err;
+};
+
 struct QmvK {
     QSeg seg[QB_MAX_SEG];
     int pair0[QB_MAX_SEG + 1];   // first tile pair of each segment; pair0[nseg] = total pairs
@@ -435,6 +444,10 @@ struct QmvK {
     unsigned* counters;          // [pairs]
     int group;                   // warps combined in shared memory before the device-wide combine
     unsigned* err;
+    // tensor parallelism (QbTp): every stored output value also goes to the
+    // same address of each peer's buffer (dst + tp_delta[i]), then the grid's
+    // last warp exchanges a sequence number with the peers (cross-rank barrier)
+    TpK tp;
     // deferred RMSNorm of the input (QbInNorm), in_ss == nullptr: none
     const float* in_ss;
     float in_eps;
@@ -544,7 +557,7 @@ __device__ __noinline__ void deferred_inv(const float* s_ss, const float* __rest
 // The final values of a tile pair, held by one warp (lanes with active ==
 // false hold nothing): the deferred input norm, the store (or SwiGLU of the
 // gate / up tiles), then the block-completion epilogue.
-template <bool EPI>
+template <bool EPI, bool TP>
 __device__ __forceinline__ void pair_final(const QmvK& p, int pair, float (&v)[2][4], bool active, int lane,
                                            const float* s_ss) {
     int si = 0;
@@ -580,7 +593,11 @@ __device__ __forceinline__ void pair_final(const QmvK& p, int pair, float (&v)[2
                 const int tok = (i & 1) ? t1 : t0;
                 if (tok < p.N && rr < S.rows && rr >= p.row_lo && rr < p.row_hi) {
                     float* dst = S.out + (size_t)tok * S.ldo + rr;
-                    *dst = p.accumulate ? (__ldcg(dst) + v[t][i]) : v[t][i];
+                    const float y = p.accumulate ? (__ldcg(dst) + v[t][i]) : v[t][i];
+                    *dst = y;
+                    if (TP)
+                        for (int q = 0; q < p.tp.np; ++q)
+                            *reinterpret_cast<float*>(reinterpret_cast<char*>(dst) + p.tp.delta[q]) = y;
                 }
             }
     }
@@ -604,7 +621,7 @@ __device__ __forceinline__ void pair_final(const QmvK& p, int pair, float (&v)[2
 
 // o[t][i], i = (row g tok 2c, row g tok 2c+1, row g8 tok 2c, row g8 tok 2c+1) of
 // tile t; lanes with active == false hold nothing to store.
-template <bool EPI>
+template <bool EPI, bool TP>
 __device__ __forceinline__ void finish_pair(const QmvK& p, int pair, int gw, int s0, int s1, const float (&o)[2][4],
                                             bool active, int lane, unsigned* lcnt, int grp_pair0, const float* s_ss) {
     const int g = lane >> 2, c = lane & 3;
@@ -616,7 +633,7 @@ __device__ __forceinline__ void finish_pair(const QmvK& p, int pair, int gw, int
         for (int t = 0; t < 2; ++t)
 #pragma unroll
             for (int i = 0; i < 4; ++i) v[t][i] = o[t][i];
-        pair_final<EPI>(p, pair, v, active, lane, s_ss);
+        pair_final<EPI, TP>(p, pair, v, active, lane, s_ss);
         return;
     }
     // Split pair.  A contributor's piece is 0 if it started inside the pair
@@ -661,7 +678,7 @@ __device__ __forceinline__ void finish_pair(const QmvK& p, int pair, int gw, int
     }
     const int g_first = w_first / G, g_last = w_last / G;
     if (g_first == g_last) {
-        pair_final<EPI>(p, pair, v, active, lane, s_ss);
+        pair_final<EPI, TP>(p, pair, v, active, lane, s_ss);
         return;
     }
     // level 2: the groups, device-scope ordering, last arrival sums in group order
@@ -687,7 +704,7 @@ __device__ __forceinline__ void finish_pair(const QmvK& p, int pair, int gw, int
             for (int i = 0; i < 4; ++i) sum[t][i] += sl[pidx(t, i)];
     }
     if (lane == 0) p.counters[pair] = 0u;   // ready for the next launch
-    pair_final<EPI>(p, pair, sum, active, lane, s_ss);
+    pair_final<EPI, TP>(p, pair, sum, active, lane, s_ss);
 }
 
 // fp16 path: combine the hi/lo columns of the mma accumulators
@@ -727,9 +744,45 @@ __device__ __forceinline__ void pair_out_i8(const float (&tok)[2][2][2], float (
     active = NT == 1 ? (c < 2) : true;
 }
 
+// Tensor parallelism: a warp that is done (its peer stores included) arrives;
+// the grid's last warp publishes the launch's sequence number into its slot of
+// every peer's flag array and waits, bounded, until every peer has published
+// the same number into this rank's array.  The launch therefore ends only when
+// all ranks' outputs have landed here.  A warp that gave up a wait never
+// arrives, so the peers time out and record the error too.
+__device__ __noinline__ void tp_arrive(TpK t, int lane) {
+    __threadfence_system();   // this lane's stores, peer stores included
+    __syncwarp();
+    if (lane != 0) return;
+    const unsigned old = atomicAdd(t.done, 1u);
+    if (old != gridDim.x * kConsumers - 1) return;
+    *t.done = 0u;   // ready for the next launch
+    const unsigned seq = *t.seq + 1u;
+    *t.seq = seq;
+    for (int q = 0; q < t.np; ++q) {
+        unsigned* slot = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(t.flags + t.rank) + t.delta[q]);
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(slot), "r"(seq) : "memory");
+    }
+    for (int q = 0; q < t.np; ++q) {
+        const int peer = q < t.rank ? q : q + 1;
+        const unsigned* f = t.flags + peer;
+        for (uint32_t it = 0;; ++it) {
+            unsigned v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+            if ((int)(v - seq) >= 0) break;
+            if (it >= (1u << 24)) {
+                atomicExch(t.err, 4u);
+                return;
+            }
+            __nanosleep(64);
+        }
+    }
+}
+
 // EPI: the launch has a deferred input norm or a next-input epilogue (QbInNorm,
 // QbEpi); launches without either run the variant that has neither.
-template <int FMT, int NT, bool I8, bool EPI>
+// TP: tensor-parallel launch (peer stores and the cross-rank barrier, QbTp).
+template <int FMT, int NT, bool I8, bool EPI, bool TP>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_kernel(QmvK p) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int TB = tile_block_bytes(FMT);
@@ -751,7 +804,13 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_kernel(QmvK p) {
     for (int i = threadIdx.x; i < kLocalPairs; i += kThreads) s_lcnt[i] = 0u;
     __syncthreads();
     const int gw = blockIdx.x * kConsumers + warp;
-    if (gw >= p.Wt) return;
+    if (gw >= p.Wt) {
+        if (TP) {
+            pdl_wait();   // arrive only after the previous TP launch has finished its own count
+            tp_arrive(p.tp, lane);
+        }
+        return;
+    }
     const int grp_pair0 = warp_s0(p.S, p.Wt, (gw / p.group) * p.group) / p.nb;
     const int s0 = warp_s0(p.S, p.Wt, gw), s1 = warp_s0(p.S, p.Wt, gw + 1);
     const int n = s1 - s0;
@@ -804,7 +863,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_kernel(QmvK p) {
         bool active;
         if (I8) pair_out_i8<NT>(tk, o, active, lane);
         else pair_out_f16<NT>(acc, o, active, lane);
-        finish_pair<EPI>(p, pair, gw, s0, s1, o, active, lane, s_lcnt, grp_pair0, s_ss[EPI ? warp : 0]);
+        finish_pair<EPI, TP>(p, pair, gw, s0, s1, o, active, lane, s_lcnt, grp_pair0, s_ss[EPI ? warp : 0]);
     };
     reset();
     const int c = lane & 3;
@@ -900,6 +959,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_kernel(QmvK p) {
         }
     }
     if (cur_pair >= 0) finish(cur_pair);
+    if (TP) tp_arrive(p.tp, lane);
 }
 
 // ------------------------------- F32 ---------------------------------------
@@ -1198,9 +1258,13 @@ static int g_num_sms = 0;
 
 namespace {
 cudaError_t qmv_launch(int type, const QbQSeg* segs, int nseg, int K, int N, const QbXBuf& xb, int accumulate,
-                       int row_lo, int row_hi, const QbInNorm* in_norm, const QbEpi* epi, const QbQmvWork& work,
-                       cudaStream_t st) {
-    if (nseg < 1 || nseg > QB_MAX_SEG || N < 1 || N > QB_MAX_TOK || K % 256) return cudaErrorInvalidValue;
+                       int row_lo, int row_hi, const QbInNorm* in_norm, const QbEpi* epi, const QbTp* tp,
+                       const QbQmvWork& work, cudaStream_t st) {
+    const bool tp_k = tp && tp->world > 1;
+    if (nseg < (tp_k ? 0 : 1) || nseg > QB_MAX_SEG || N < 1 || N > QB_MAX_TOK || K % 256) return cudaErrorInvalidValue;
+    if (tp_k && (tp->world > QB_TP_MAX || tp->rank < 0 || tp->rank >= tp->world || !tp->flags || !tp->done || !tp->seq ||
+                 (epi && epi->kind != QB_EPI_NONE) || (in_norm && in_norm->ss)))
+        return cudaErrorInvalidValue;
     if (!g_num_sms) {
         int dev = 0;
         cudaGetDevice(&dev);
@@ -1239,7 +1303,7 @@ cudaError_t qmv_launch(int type, const QbQSeg* segs, int nseg, int K, int N, con
     if (grid * kConsumers > warps_needed) grid = (warps_needed + kConsumers - 1) / kConsumers;
     if (grid < 1) grid = 1;
     while (grid > 1 && grid * kConsumers > p.S) --grid;
-    p.Wt = grid * kConsumers < p.S ? grid * kConsumers : p.S;   // warps beyond Wt exit at once
+    p.Wt = grid * kConsumers < p.S ? grid * kConsumers : p.S;   // warps beyond Wt exit at once (S == 0: all)
     if (p.Wt > work.max_warps) return cudaErrorInvalidValue;
     p.xfrag = xb.xfrag;
     p.xscale = xb.xscale;
@@ -1256,9 +1320,20 @@ cudaError_t qmv_launch(int type, const QbQSeg* segs, int nseg, int K, int N, con
     p.partial = work.partial;
     p.gpartial = work.gpartial;
     p.counters = work.counters;
-    {   // CTA-level combine when a CTA's stage range touches at most kLocalPairs pairs
+    if (p.Wt > 0) {   // CTA-level combine when a CTA's stage range touches at most kLocalPairs pairs
         const long long per_cta = ((long long)p.S * kConsumers + p.Wt - 1) / p.Wt;   // stages of 8 warps
         p.group = per_cta / p.nb + 2 <= kLocalPairs ? kConsumers : 1;
+    } else {
+        p.group = 1;
+    }
+    if (tp_k) {
+        p.tp.np = tp->world - 1;
+        p.tp.rank = tp->rank;
+        for (int i = 0; i < tp->world - 1; ++i) p.tp.delta[i] = tp->delta[i];
+        p.tp.flags = tp->flags;
+        p.tp.done = tp->done;
+        p.tp.seq = tp->seq;
+        p.tp.err = work.err;
     }
     p.err = work.err;
     if (in_norm && in_norm->ss) {
@@ -1294,12 +1369,14 @@ cudaError_t qmv_launch(int type, const QbQSeg* segs, int nseg, int K, int N, con
     cudaError_t e = cudaSuccess;
 #define QB_LAUNCH(F, I8)                                                                               \
     do {                                                                                               \
-        auto kern = epi_k ? (nt2 ? qmv_kernel<F, 2, I8, true> : qmv_kernel<F, 1, I8, true>)           \
-                          : (nt2 ? qmv_kernel<F, 2, I8, false> : qmv_kernel<F, 1, I8, false>);         \
-        static bool attr_set[4] = {false, false, false, false};                                        \
-        if (!attr_set[nt2 + 2 * epi_k]) {                                                              \
+        auto kern = tp_k    ? (nt2 ? qmv_kernel<F, 2, I8, false, true> : qmv_kernel<F, 1, I8, false, true>)   \
+                    : epi_k ? (nt2 ? qmv_kernel<F, 2, I8, true, false> : qmv_kernel<F, 1, I8, true, false>)   \
+                            : (nt2 ? qmv_kernel<F, 2, I8, false, false> : qmv_kernel<F, 1, I8, false, false>); \
+        const int variant = nt2 + 2 * (epi_k ? 1 : tp_k ? 2 : 0);                                      \
+        static bool attr_set[6] = {false, false, false, false, false, false};                          \
+        if (!attr_set[variant]) {                                                                      \
             cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);       \
-            attr_set[nt2 + 2 * epi_k] = true;                                                          \
+            attr_set[variant] = true;                                                                  \
         }                                                                                              \
         e = qb_launch(kern, dim3(grid), dim3(kThreads), smem, st, p);                                  \
     } while (0)
@@ -1318,12 +1395,13 @@ cudaError_t qmv_launch(int type, const QbQSeg* segs, int nseg, int K, int N, con
 
 cudaError_t qb_qmv(int type, const QbQSeg* segs, int nseg, int K, int N, const QbXBuf& xb, int accumulate,
                    int row_lo, int row_hi, const QbQmvWork& work, cudaStream_t st) {
-    return qmv_launch(type, segs, nseg, K, N, xb, accumulate, row_lo, row_hi, nullptr, nullptr, work, st);
+    return qmv_launch(type, segs, nseg, K, N, xb, accumulate, row_lo, row_hi, nullptr, nullptr, nullptr, work, st);
 }
 
 cudaError_t qb_qmv_ex(int type, const QbQSeg* segs, int nseg, int K, int N, const QbXBuf& xb, int accumulate,
-                      const QbInNorm* in_norm, const QbEpi* epi, const QbQmvWork& work, cudaStream_t st) {
-    return qmv_launch(type, segs, nseg, K, N, xb, accumulate, 0, 1 << 30, in_norm, epi, work, st);
+                      const QbInNorm* in_norm, const QbEpi* epi, const QbTp* tp, const QbQmvWork& work,
+                      cudaStream_t st) {
+    return qmv_launch(type, segs, nseg, K, N, xb, accumulate, 0, 1 << 30, in_norm, epi, tp, work, st);
 }
 
 cudaError_t qb_interleave_tiles(int type, const void* a, const void* b, int rows, int K, void* dst, cudaStream_t st) {

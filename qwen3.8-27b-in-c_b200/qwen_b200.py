@@ -29,7 +29,8 @@ EXPORTED = [
     "rmsnorm", "l2norm", "silu_inplace", "sigmoid_inplace", "softplus_inplace", "softmax_inplace",
     "qb_last_error", "qb_last_error_str", "qb_clear_error", "qb_prefill", "qb_spec_generate",
     "qb_greedy_generate", "qb_last_argmax", "qb_last_loop_ms", "qb_read_state", "qb_read_buffer",
-    "qb_reset", "qb_bench", "qb_argmax_rows_noalloc",
+    "qb_reset", "qb_bench", "qb_model_init_tp", "qb_tp_handle", "qb_tp_connect", "qb_tp_rows",
+    "qb_argmax_rows_noalloc",
 ]
 
 
@@ -124,6 +125,14 @@ def lib():
         L.qb_reset.restype = i32
         L.qb_bench.argtypes = [P(QwenModel), i32, u32, u32, P(C.c_double)]
         L.qb_bench.restype = f32
+        L.qb_model_init_tp.argtypes = [P(QwenModel), C.c_char_p, u32, i32, i32]
+        L.qb_model_init_tp.restype = i32
+        L.qb_tp_handle.argtypes = [P(QwenModel), vp, C.c_int64]
+        L.qb_tp_handle.restype = C.c_int64
+        L.qb_tp_connect.argtypes = [P(QwenModel), vp, C.c_int64]
+        L.qb_tp_connect.restype = i32
+        L.qb_tp_rows.argtypes = [i32, i32, i32, P(i32), P(i32)]
+        L.qb_tp_rows.restype = None
         L.qb_argmax_rows_noalloc.argtypes = [vp, C.c_int64, u32, u32, vp, vp]
         L.qb_argmax_rows_noalloc.restype = i32
         _lib = L
@@ -210,18 +219,49 @@ def op(name, x, w=None, eps=1e-6):
     return x
 
 
-class Model:
-    """Owns a qwen_model_t (include/qwen_b200.h) on the current CUDA device."""
+def tp_rows(rows, rank, world):
+    """Row range [r0, r1) of a rows-row matrix held by rank of world (qb_tp_rows)."""
+    r0, r1 = C.c_int(0), C.c_int(0)
+    lib().qb_tp_rows(rows, rank, world, C.byref(r0), C.byref(r1))
+    return r0.value, r1.value
 
-    def __init__(self, path, n_ctx):
+
+class Model:
+    """Owns a qwen_model_t (include/qwen_b200.h) on the current CUDA device.
+
+    With world > 1 the model is this rank's share of a tensor-parallel group
+    (qb_model_init_tp): call tp_connect() with every rank's tp_handle() before
+    the first forward, then drive all ranks with the same calls."""
+
+    def __init__(self, path, n_ctx, rank=0, world=1):
         self.m = QwenModel()
-        r = lib().model_init(C.byref(self.m), os.fsencode(path), n_ctx)
+        if world == 1:
+            r = lib().model_init(C.byref(self.m), os.fsencode(path), n_ctx)
+        else:
+            r = lib().qb_model_init_tp(C.byref(self.m), os.fsencode(path), n_ctx, rank, world)
         if r != 0:
             msg = lib().qb_last_error_str().decode()
             lib().qb_clear_error()
             raise RuntimeError(f"model_init failed: {msg}")
         self.V = self.m.cfg.vocab_size
         self.E = self.m.dims.n_embd
+        self.rank, self.world = rank, world
+
+    def tp_handle(self):
+        """This rank's IPC handle of its activation arena (bytes)."""
+        buf = (C.c_char * 64)()
+        n = lib().qb_tp_handle(C.byref(self.m), buf, 64)
+        if n <= 0:
+            raise RuntimeError("qb_tp_handle failed: " + lib().qb_last_error_str().decode())
+        return bytes(buf[:n])
+
+    def tp_connect(self, handles):
+        """Map every peer's arena; handles = the tp_handle() of all ranks, rank-ordered."""
+        stride = max(len(h) for h in handles)
+        blob = b"".join(h.ljust(stride, b"\0") for h in handles)
+        buf = C.create_string_buffer(blob, len(blob))
+        if lib().qb_tp_connect(C.byref(self.m), buf, stride) != 0:
+            raise RuntimeError("qb_tp_connect failed: " + lib().qb_last_error_str().decode())
 
     def close(self):
         if self.m.eng:
