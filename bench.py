@@ -13,9 +13,13 @@ drafts, batched verify, acceptance, rollback, MTP anchor); the default
 W + K = 5 + 200 cycles emit ~512 tokens.  Weights are random (no checkpoint
 is available); the GGUF is written by the seeded generator before timing.
 
-Multi-GPU: one process per GPU (torchrun), each rank a full replica
-decoding its own sequence; value = tokens of all ranks / max rank time
-(weak scaling, no data-path collective).
+Multi-GPU: one process per GPU (torchrun).  --parallel replicas (the
+default): each rank a full model decoding its own sequence; value = tokens
+of all ranks / max rank time (weak scaling, no data-path collective).
+--parallel tp: the ranks decode ONE sequence together; each holds 1/N of
+the rows of every quantised matrix, every GEMV stores its rows into all
+ranks' outputs over NVLink and ends with a cross-rank barrier; value = that
+sequence's tokens / max rank time (strong scaling).
 """
 import argparse
 import json
@@ -199,15 +203,24 @@ def run_ours(args, rank, world, local_rank):
     dist = None
     if world > 1:
         import torch.distributed as dist
+    tp = world > 1 and args.parallel == "tp"
+    seq_rank = 0 if tp else rank   # tensor parallelism: one sequence for all ranks
     path = gguf_path(rank, world)
     n_ctx = max(1024, PROMPT_LEN + 4 * (args.warmup + args.steps) + 64)
     t0 = time.time()
-    model = qb.Model(path, n_ctx)
+    if tp:
+        model = qb.Model(path, n_ctx, rank, world)
+        handles = [None] * world
+        dist.all_gather_object(handles, model.tp_handle())
+        model.tp_connect(handles)
+        dist.barrier()
+    else:
+        model = qb.Model(path, n_ctx)
     print(f"[bench r{rank}] model_init {time.time() - t0:.1f}s", file=sys.stderr, flush=True)
     forced = forced_schedule()
 
     # ---- device-timed value: K speculative cycles ----
-    model.prefill(prompt_tokens(rank), 1)
+    model.prefill(prompt_tokens(seq_rank), 1)
     log("prefill done")
     model.spec_generate(10 ** 6, 3, forced=forced, max_cycles=args.warmup)
     log("warmup done")
@@ -228,6 +241,8 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(mx[:1], op=dist.ReduceOp.MAX)
         dist.all_reduce(t[1:], op=dist.ReduceOp.SUM)
         ms_max, tok_sum = float(mx[0]), float(t[1])
+        if tp:
+            tok_sum = float(n_tok)   # the ranks decoded the same tokens
     else:
         ms_max, tok_sum = ms, float(n_tok)
     value = tok_sum / (ms_max / 1e3)
@@ -237,7 +252,7 @@ def run_ours(args, rank, world, local_rank):
     e2e_runs = []
     h2d = d2h = 0
     for rep in range(2):
-        prompt = prompt_tokens(rank)
+        prompt = prompt_tokens(seq_rank)
         torch.cuda.synchronize()
         t1 = time.perf_counter()
         model.reset()
@@ -258,8 +273,9 @@ def run_ours(args, rank, world, local_rank):
     ms_draft, b_draft = model.bench(2, 1, 10)
     ms_ver, b_ver = model.bench(0, 4, 10)        # verify step (64 layers + head, B=4)
     log(f"components gemv {ms_gemv:.4f} head {ms_head:.4f} draft {ms_draft:.3f} verify {ms_ver:.3f} ms")
-    gemv_gbs = b_gemv / (ms_gemv / 1e3) / 1e9
-    ver_gbs = b_ver / (ms_ver / 1e3) / 1e9
+    shards = world if tp else 1   # each GPU streams 1/shards of the weights
+    gemv_gbs = b_gemv / shards / (ms_gemv / 1e3) / 1e9
+    ver_gbs = b_ver / shards / (ms_ver / 1e3) / 1e9
 
     line = None
     if rank == 0:
@@ -270,28 +286,33 @@ def run_ours(args, rank, world, local_rank):
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+            "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "fp32",
             "data": "synthetic (seeded random weights, random prompt)",
             "config": {"workload": "C3: 64-layer hybrid + MTP, k=3, verify width 4, forced accept U{0..3}",
                        "prompt": PROMPT_LEN, "tokens_timed": int(tok_sum), "cycles_timed": args.steps,
                        "mean_accept": float(np.mean(js)) if len(js) else None,
                        "l2": "weights 15 GB per cycle >> 126 MB L2 (no flush needed)",
-                       "parallelism": f"replicas x{world}"},
+                       "parallelism": f"tp x{world}" if tp else f"replicas x{world}"},
             "gpu_launches": int(kernels_per_cycle) * args.steps,
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "step": "one request: reset + prefill 128 + decode 512 tokens"},
             "roofline": {"bound": "hbm", "kernel": "qmv IQ4_XS (FFN gate+up fused, N=4)", "achieved": gemv_gbs,
-                         "peak": hbm, "unit": "GB/s", "frac": gemv_gbs / hbm, "traffic": profiled_traffic(),
-                         "algorithmic_bytes": b_gemv,
+                         "peak": hbm, "unit": "GB/s", "frac": gemv_gbs / hbm,
+                         "traffic": (profiled_traffic() / shards) if profiled_traffic() else None,
+                         "algorithmic_bytes": b_gemv / shards,
                          "peak_kind": peak_kind},
-            "verify_step": {"ms": ms_ver, "bytes": b_ver, "GB/s": ver_gbs, "frac": ver_gbs / hbm},
+            "verify_step": {"ms": ms_ver, "bytes": b_ver, "bytes_per_gpu": b_ver / shards, "GB/s": ver_gbs,
+                            "frac": ver_gbs / hbm},
             "draft_ms": ms_draft, "head_ms": ms_head,
-            "head_GB/s": b_head / (ms_head / 1e3) / 1e9,
+            "head_GB/s": b_head / shards / (ms_head / 1e3) / 1e9,
             "clocks": clk.summary(),
         }
         if cpu_v is not None:
             line["cpu_baseline"] = {"value": cpu_v, "unit": "tok/s", "cores": os.cpu_count(), "kind": "reference",
                                     "sample": cpu_sample}
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()   # tensor parallelism: no rank still writes into a peer's buffers
     model.close()
     if dist:
         dist.barrier()
@@ -336,6 +357,8 @@ def main():
     ap.add_argument("--shape", default="wide4", choices=["wide4", "full"])
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--only", default="")
+    ap.add_argument("--parallel", default="replicas", choices=["tp", "replicas"],
+                    help="N > 1: one sequence over all GPUs (tp) or one sequence per GPU (replicas)")
     args = ap.parse_args()
     if args.mode == "components":
         run_components(args)

@@ -744,18 +744,24 @@ __device__ __forceinline__ void pair_out_i8(const float (&tok)[2][2][2], float (
     active = NT == 1 ? (c < 2) : true;
 }
 
-// Tensor parallelism: a warp that is done (its peer stores included) arrives;
-// the grid's last warp publishes the launch's sequence number into its slot of
-// every peer's flag array and waits, bounded, until every peer has published
-// the same number into this rank's array.  The launch therefore ends only when
-// all ranks' outputs have landed here.  A warp that gave up a wait never
-// arrives, so the peers time out and record the error too.
-__device__ __noinline__ void tp_arrive(TpK t, int lane) {
-    __threadfence_system();   // this lane's stores, peer stores included
+// Tensor parallelism: a warp that is done (its peer stores included) arrives
+// on its CTA's shared counter (acquire-release, so the CTA's last warp has
+// observed every store of the CTA); that warp makes them visible system-wide
+// and arrives on the device counter; the grid's last CTA publishes the
+// launch's sequence number into its slot of every peer's flag array and
+// waits, bounded, until every peer has published the same number into this
+// rank's array.  The launch therefore ends only when all ranks' outputs have
+// landed here.  A warp that gave up a wait never arrives, so the peers time
+// out and record the error too.
+__device__ __noinline__ void tp_arrive(TpK t, uint32_t s_arrive, int lane) {
     __syncwarp();
     if (lane != 0) return;
-    const unsigned old = atomicAdd(t.done, 1u);
-    if (old != gridDim.x * kConsumers - 1) return;
+    unsigned old;
+    asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], 1;" : "=r"(old) : "r"(s_arrive) : "memory");
+    if (old != kConsumers - 1) return;
+    __threadfence_system();   // the CTA's stores, peer stores included
+    old = atom_add_acq_rel_gpu(t.done, 1u);
+    if (old != gridDim.x - 1) return;
     *t.done = 0u;   // ready for the next launch
     const unsigned seq = *t.seq + 1u;
     *t.seq = seq;
@@ -801,13 +807,15 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_kernel(QmvK p) {
     // per-CTA arrival counters of the pairs its warps share (level 1 of the split-pair combine)
     __shared__ unsigned s_lcnt[kLocalPairs];
     __shared__ float s_ss[EPI ? kConsumers : 1][EPI ? kSsMax : 1];   // deferred-norm sums (QbInNorm), per warp
+    __shared__ unsigned s_arrive;   // TP: warps of this CTA that are done
     for (int i = threadIdx.x; i < kLocalPairs; i += kThreads) s_lcnt[i] = 0u;
+    if (threadIdx.x == 0) s_arrive = 0u;
     __syncthreads();
     const int gw = blockIdx.x * kConsumers + warp;
     if (gw >= p.Wt) {
         if (TP) {
             pdl_wait();   // arrive only after the previous TP launch has finished its own count
-            tp_arrive(p.tp, lane);
+            tp_arrive(p.tp, smem_u32(&s_arrive), lane);
         }
         return;
     }
@@ -959,7 +967,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_kernel(QmvK p) {
         }
     }
     if (cur_pair >= 0) finish(cur_pair);
-    if (TP) tp_arrive(p.tp, lane);
+    if (TP) tp_arrive(p.tp, smem_u32(&s_arrive), lane);
 }
 
 // ------------------------------- F32 ---------------------------------------
