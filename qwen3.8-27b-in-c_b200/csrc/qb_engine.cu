@@ -240,7 +240,8 @@ constexpr int kNSlot = 4;
 struct DevMat {
     int type = -1;
     int rows = 0, K = 0;
-    int row0 = 0, rows_all = 0;   // tensor parallelism: this rank holds rows [row0, row0 + rows) of rows_all
+    int row0 = 0, rows_all = 0;   // tensor parallelism: output rows land at row0 + i; rows_all = the tensor's rows
+    size_t bytes_all = 0;         // GGUF bytes of the whole tensor (algorithmic traffic of the job)
     void* w = nullptr;      // repacked into 16-row mma.sync tiles (quant) or plain row-major (F32)
     void* w_tc = nullptr;   // IQ4_XS also in 128-row tcgen05 tiles (qb_qmv_tc, N <= 4)
     uint64_t fingerprint = 0;   // host-API weight cache only
@@ -316,6 +317,14 @@ struct Engine {
     size_t arena_bytes = 0;
     QbTp tp{};
     void* peer_arena[QB_TP_MAX] = {};     // peers' arenas mapped here
+    // head-parallel share of this rank (the whole model when tp_world == 1): DeltaNet
+    // k-heads [k0, k0 + nk_loc) with their v-heads (local v-head j * nk_loc + i is global
+    // j * n_k + k0 + i), attention q-heads [h0, h0 + nh_loc), kv-heads [kv0, kv0 + nkv_loc),
+    // FFN columns [f0, f0 + F_loc)
+    int nk_loc = 0, nv_loc = 0, nh_loc = 0, nkv_loc = 0, F_loc = 0;
+    int k0 = 0, h0 = 0, kv0 = 0, f0 = 0;
+    float* part = nullptr;                // [2][QB_MAX_TOK][E] partial sums of the residual GEMVs (arena)
+    const float* peer_part[QB_TP_MAX] = {};   // rank r's part buffer, mapped here
     bool use_tc = false;                  // IQ4_XS at N <= 4 on tcgen05 (QB_TC=1); default: int8 mma.sync
     float* attn_po = nullptr;             // attention chunk partials (qb_attn_decode)
     float2* gates = nullptr;              // DeltaNet (beta, decay) per (token, v-head)
@@ -383,32 +392,65 @@ extern "C" void qb_tp_rows(int rows, int rank, int world, int* r0, int* r1) {
 
 namespace {
 
-int upload_mat(Engine& e, const GTensor* t, DevMat& m, void* tmp, size_t tmp_bytes) {
+// A part of a GGUF matrix to upload: row ranges (start, count) in this order,
+// and column ranges of whole quantisation blocks; empty = all.
+struct Sel {
+    std::vector<std::pair<int, int>> rows, cols;
+};
+
+// Gathers the selected rows and column blocks of t into one host buffer in
+// GGUF row layout (rows ne0' = the selected columns).  False if a column range
+// does not fall on quantisation-block boundaries.
+bool gather_host(const GTensor* t, const Sel& sel, std::vector<uint8_t>& out, int& rows, int& cols) {
+    const int K = (int)t->ne[0], R = (int)t->ne[1];
+    const size_t rb = gguf_row_bytes(t->type, (uint64_t)K);
+    const int bc = t->type == QB_F32 ? 1 : t->type == QB_Q8_0 ? 32 : 256;   // columns per block
+    const size_t bb = rb / (size_t)(K / bc);                                 // bytes per block
+    std::vector<std::pair<int, int>> rr = sel.rows, cc = sel.cols;
+    if (rr.empty()) rr.push_back({0, R});
+    if (cc.empty()) cc.push_back({0, K});
+    rows = cols = 0;
+    for (auto& r : rr) rows += r.second;
+    for (auto& c : cc) {
+        if (c.first % bc || c.second % bc || c.first + c.second > K) return false;
+        cols += c.second;
+    }
+    const size_t orb = (size_t)cols / bc * bb;
+    out.resize((size_t)rows * orb);
+    uint8_t* o = out.data();
+    for (auto& r : rr)
+        for (int i = 0; i < r.second; ++i) {
+            const uint8_t* row = (const uint8_t*)t->data + (size_t)(r.first + i) * rb;
+            for (auto& c : cc) {
+                const size_t n = (size_t)c.second / bc * bb;
+                memcpy(o, row + (size_t)c.first / bc * bb, n);
+                o += n;
+            }
+        }
+    return true;
+}
+
+// Uploads the selected part of a quantised matrix, repacked for the GEMV.
+// row0 = the global index of its first output row (tensor-parallel gather).
+int upload_mat(Engine& e, const GTensor* t, DevMat& m, void* tmp, size_t tmp_bytes, const Sel& sel = Sel(),
+               int row0 = 0) {
     if (!t) { set_err(-1, "missing tensor"); return -1; }
     m.type = t->type;
-    m.K = (int)t->ne[0];
-    m.rows = m.rows_all = (int)t->ne[1];
-    m.row0 = 0;
-    size_t src_bytes = gguf_row_bytes(t->type, t->ne[0]) * t->ne[1];
-    if (!src_bytes) { set_err(-1, "tensor %s: unsupported type %d", t->name.c_str(), t->type); return -1; }
+    m.rows_all = (int)t->ne[1];
+    m.row0 = row0;
+    m.bytes_all = gguf_row_bytes(t->type, t->ne[0]) * t->ne[1];
+    if (!m.bytes_all || t->type == QB_F32) { set_err(-1, "tensor %s: unsupported type %d", t->name.c_str(), t->type); return -1; }
+    std::vector<uint8_t> host;
     const uint8_t* src = (const uint8_t*)t->data;
-    if (e.tp_world > 1 && t->type != QB_F32) {   // this rank's rows only
-        int r0 = 0, r1 = 0;
-        qb_tp_rows(m.rows_all, e.tp_rank, e.tp_world, &r0, &r1);
-        const size_t rb = gguf_row_bytes(t->type, t->ne[0]);
-        m.row0 = r0;
-        m.rows = r1 - r0;
-        src += (size_t)r0 * rb;
-        src_bytes = (size_t)m.rows * rb;
-        if (m.rows == 0) return 0;
+    size_t src_bytes = m.bytes_all;
+    m.K = (int)t->ne[0];
+    m.rows = (int)t->ne[1];
+    if (!sel.rows.empty() || !sel.cols.empty()) {
+        if (!gather_host(t, sel, host, m.rows, m.K)) { set_err(-1, "tensor %s: split off block bounds", t->name.c_str()); return -1; }
+        src = host.data();
+        src_bytes = host.size();
     }
-    if (t->type == QB_F32) {
-        m.w = e.dalloc(src_bytes);
-        if (!m.w) { set_err(-2, "cudaMalloc %zu", src_bytes); return -1; }
-        CK(cudaMemcpyAsync(m.w, t->data, src_bytes, cudaMemcpyHostToDevice, e.st));
-        CK(cudaStreamSynchronize(e.st));
-        return 0;
-    }
+    if (m.rows == 0) return 0;
     const size_t rb = qb_repacked_bytes(t->type, m.rows, m.K);
     if (!rb || src_bytes > tmp_bytes) { set_err(-1, "tensor %s: cannot repack", t->name.c_str()); return -1; }
     m.w = e.dalloc(rb);
@@ -422,17 +464,21 @@ int upload_mat(Engine& e, const GTensor* t, DevMat& m, void* tmp, size_t tmp_byt
         if (!m.w_tc) { set_err(-2, "cudaMalloc %zu", rt); return -1; }
         CK(qb_repack_tc(tmp, m.rows, m.K, m.w_tc, e.st));
     }
-    CK(cudaStreamSynchronize(e.st));
+    CK(cudaStreamSynchronize(e.st));   // the host buffer must outlive the copy
     if (t->type == QB_Q4_K || t->type == QB_Q5_K) e.any_q45 = true;
     return 0;
 }
 
-const float* upload_f32(Engine& e, const GTensor* t) {
+// Uploads the selected rows of an F32 tensor (a vector is one row of ne0 values,
+// selected by columns; a matrix [ne1][ne0] by rows).
+const float* upload_f32(Engine& e, const GTensor* t, const Sel& sel = Sel()) {
     if (!t || t->type != QB_F32) return nullptr;
-    const size_t n = t->ne[0] * t->ne[1];
-    void* p = e.dalloc(n * 4);
+    std::vector<uint8_t> host;
+    int rows = 0, cols = 0;
+    if (!gather_host(t, sel, host, rows, cols)) return nullptr;
+    void* p = e.dalloc(host.size());
     if (!p) return nullptr;
-    if (cudaMemcpyAsync(p, t->data, n * 4, cudaMemcpyHostToDevice, e.st) != cudaSuccess) return nullptr;
+    if (cudaMemcpyAsync(p, host.data(), host.size(), cudaMemcpyHostToDevice, e.st) != cudaSuccess) return nullptr;
     if (cudaStreamSynchronize(e.st) != cudaSuccess) return nullptr;
     return (const float*)p;
 }
@@ -523,9 +569,68 @@ int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
         CK(cudaMemcpyAsync(e.tok_embd, te->data, b, cudaMemcpyHostToDevice, e.st));
         CK(cudaStreamSynchronize(e.st));
     }
+    // ---- this rank's share (tensor parallelism) ----
+    const int g = e.tp_world, rk = e.tp_rank;
+    const int nk = (int)d.n_k_heads, nv = (int)d.n_v_heads, nh = (int)d.n_head, nkv = (int)d.n_kv_head;
+    const int dk = (int)d.head_k_dim, hd = (int)d.head_dim;
+    if (g > 1 && (nk % g || (nk / g) % 2 || nv % nk || nh % g || !(nkv % g == 0 || g % nkv == 0) || e.F % 256 ||
+                  (e.F / 256) < g)) {
+        set_err(-1, "tensor parallelism over %d ranks needs k-heads / ranks even and q-/kv-heads and FFN "
+                    "blocks divisible (k-heads %d, q-heads %d, kv-heads %d, FFN %d)", g, nk, nh, nkv, e.F);
+        return -1;
+    }
+    e.nk_loc = nk / g;
+    e.k0 = rk * e.nk_loc;
+    e.nv_loc = nv / g;
+    e.nh_loc = nh / g;
+    e.h0 = rk * e.nh_loc;
+    if (nkv % g == 0) {
+        e.nkv_loc = nkv / g;
+        e.kv0 = rk * e.nkv_loc;
+    } else {   // fewer kv-heads than ranks: each rank keeps the one its q-heads use
+        e.nkv_loc = 1;
+        e.kv0 = e.h0 / (nh / nkv);
+    }
+    if (g > 1) {   // whole 256-column blocks of the FFN
+        const int nb = e.F / 256, b0 = (int)((long long)nb * rk / g), b1 = (int)((long long)nb * (rk + 1) / g);
+        e.f0 = b0 * 256;
+        e.F_loc = (b1 - b0) * 256;
+    } else {
+        e.f0 = 0;
+        e.F_loc = e.F;
+    }
+    Sel s_qkv, s_z, s_ba, s_out, s_q, s_kv, s_o, s_up, s_down, s_head;
+    int head_row0 = 0;
+    if (g > 1) {
+        const int R3 = nv / nk;   // v-heads per k-head
+        s_qkv.rows.push_back({e.k0 * dk, e.nk_loc * dk});
+        s_qkv.rows.push_back({(nk + e.k0) * dk, e.nk_loc * dk});
+        for (int j = 0; j < R3; ++j) {
+            s_qkv.rows.push_back({2 * nk * dk + (j * nk + e.k0) * dk, e.nk_loc * dk});
+            s_z.rows.push_back({(j * nk + e.k0) * dk, e.nk_loc * dk});
+            s_ba.rows.push_back({j * nk + e.k0, e.nk_loc});
+            s_out.cols.push_back({(j * nk + e.k0) * dk, e.nk_loc * dk});
+        }
+        s_q.rows.push_back({e.h0 * 2 * hd, e.nh_loc * 2 * hd});
+        s_kv.rows.push_back({e.kv0 * hd, e.nkv_loc * hd});
+        s_o.cols.push_back({e.h0 * hd, e.nh_loc * hd});
+        s_up.rows.push_back({e.f0, e.F_loc});
+        s_down.cols.push_back({e.f0, e.F_loc});
+    }
+    Sel s_vec = s_ba;   // per-v-head vectors: the same heads, as columns of one row
+    s_vec.cols = s_ba.rows;
+    s_vec.rows.clear();
+    Sel s_conv = s_qkv;   // conv1d weights [conv channel][4]: the channels of the qkv rows
+
     const GTensor* to = e.g.find("output.weight");
     if (!to) to = te;
-    if (upload_mat(e, to, e.output, tmp, tmp_bytes)) return -1;
+    if (g > 1) {   // the head splits over the vocabulary, its rows gathered to every rank
+        int r0 = 0, r1 = 0;
+        qb_tp_rows((int)to->ne[1], rk, g, &r0, &r1);
+        s_head.rows.push_back({r0, r1 - r0});
+        head_row0 = r0;
+    }
+    if (upload_mat(e, to, e.output, tmp, tmp_bytes, s_head, head_row0)) return -1;
     if (!(e.out_norm = upload_f32(e, e.g.find("output_norm.weight")))) { set_err(-1, "output_norm"); return -1; }
 
     e.L.resize(d.n_layer);
@@ -535,29 +640,29 @@ int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
         l.rec = ((il + 1) % c.full_attn_interval) != 0;
         if (!(l.attn_norm = upload_f32(e, T("blk.%d.attn_norm.weight", il)))) return -1;
         if (!(l.post_norm = upload_f32(e, T("blk.%d.post_attention_norm.weight", il)))) return -1;
-        if (upload_mat(e, T("blk.%d.ffn_gate.weight", il), l.ffn_gate, tmp, tmp_bytes) ||
-            upload_mat(e, T("blk.%d.ffn_up.weight", il), l.ffn_up, tmp, tmp_bytes) ||
-            upload_mat(e, T("blk.%d.ffn_down.weight", il), l.ffn_down, tmp, tmp_bytes) || build_gu(e, l))
+        if (upload_mat(e, T("blk.%d.ffn_gate.weight", il), l.ffn_gate, tmp, tmp_bytes, s_up) ||
+            upload_mat(e, T("blk.%d.ffn_up.weight", il), l.ffn_up, tmp, tmp_bytes, s_up) ||
+            upload_mat(e, T("blk.%d.ffn_down.weight", il), l.ffn_down, tmp, tmp_bytes, s_down) || build_gu(e, l))
             return -1;
         if (l.rec) {
             l.ridx = nr++;
-            if (upload_mat(e, T("blk.%d.attn_qkv.weight", il), l.wqkv, tmp, tmp_bytes) ||
-                upload_mat(e, T("blk.%d.attn_gate.weight", il), l.wgate, tmp, tmp_bytes) ||
-                upload_mat(e, T("blk.%d.ssm_beta.weight", il), l.wbeta, tmp, tmp_bytes) ||
-                upload_mat(e, T("blk.%d.ssm_alpha.weight", il), l.walpha, tmp, tmp_bytes) ||
-                upload_mat(e, T("blk.%d.ssm_out.weight", il), l.ssm_out, tmp, tmp_bytes))
+            if (upload_mat(e, T("blk.%d.attn_qkv.weight", il), l.wqkv, tmp, tmp_bytes, s_qkv) ||
+                upload_mat(e, T("blk.%d.attn_gate.weight", il), l.wgate, tmp, tmp_bytes, s_z) ||
+                upload_mat(e, T("blk.%d.ssm_beta.weight", il), l.wbeta, tmp, tmp_bytes, s_ba) ||
+                upload_mat(e, T("blk.%d.ssm_alpha.weight", il), l.walpha, tmp, tmp_bytes, s_ba) ||
+                upload_mat(e, T("blk.%d.ssm_out.weight", il), l.ssm_out, tmp, tmp_bytes, s_out))
                 return -1;
-            if (!(l.conv_w = upload_f32(e, T("blk.%d.ssm_conv1d.weight", il))) ||
-                !(l.dt_bias = upload_f32(e, T("blk.%d.ssm_dt.bias", il))) ||
-                !(l.ssm_a = upload_f32(e, T("blk.%d.ssm_a", il))) ||
+            if (!(l.conv_w = upload_f32(e, T("blk.%d.ssm_conv1d.weight", il), s_conv)) ||
+                !(l.dt_bias = upload_f32(e, T("blk.%d.ssm_dt.bias", il), s_vec)) ||
+                !(l.ssm_a = upload_f32(e, T("blk.%d.ssm_a", il), s_vec)) ||
                 !(l.ssm_norm = upload_f32(e, T("blk.%d.ssm_norm.weight", il))))
                 return -1;
         } else {
             l.aidx = na++;
-            if (upload_mat(e, T("blk.%d.attn_q.weight", il), l.q, tmp, tmp_bytes) ||
-                upload_mat(e, T("blk.%d.attn_k.weight", il), l.k, tmp, tmp_bytes) ||
-                upload_mat(e, T("blk.%d.attn_v.weight", il), l.v, tmp, tmp_bytes) ||
-                upload_mat(e, T("blk.%d.attn_output.weight", il), l.o, tmp, tmp_bytes))
+            if (upload_mat(e, T("blk.%d.attn_q.weight", il), l.q, tmp, tmp_bytes, s_q) ||
+                upload_mat(e, T("blk.%d.attn_k.weight", il), l.k, tmp, tmp_bytes, s_kv) ||
+                upload_mat(e, T("blk.%d.attn_v.weight", il), l.v, tmp, tmp_bytes, s_kv) ||
+                upload_mat(e, T("blk.%d.attn_output.weight", il), l.o, tmp, tmp_bytes, s_o))
                 return -1;
             if (!(l.q_norm = upload_f32(e, T("blk.%d.attn_q_norm.weight", il))) ||
                 !(l.k_norm = upload_f32(e, T("blk.%d.attn_k_norm.weight", il))))
@@ -571,13 +676,13 @@ int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
         LayerW& l = e.mtp;
         if (!(l.attn_norm = upload_f32(e, T("blk.%d.attn_norm.weight", im)))) return -1;
         if (!(l.post_norm = upload_f32(e, T("blk.%d.post_attention_norm.weight", im)))) return -1;
-        if (upload_mat(e, T("blk.%d.attn_q.weight", im), l.q, tmp, tmp_bytes) ||
-            upload_mat(e, T("blk.%d.attn_k.weight", im), l.k, tmp, tmp_bytes) ||
-            upload_mat(e, T("blk.%d.attn_v.weight", im), l.v, tmp, tmp_bytes) ||
-            upload_mat(e, T("blk.%d.attn_output.weight", im), l.o, tmp, tmp_bytes) ||
-            upload_mat(e, T("blk.%d.ffn_gate.weight", im), l.ffn_gate, tmp, tmp_bytes) ||
-            upload_mat(e, T("blk.%d.ffn_up.weight", im), l.ffn_up, tmp, tmp_bytes) ||
-            upload_mat(e, T("blk.%d.ffn_down.weight", im), l.ffn_down, tmp, tmp_bytes) ||
+        if (upload_mat(e, T("blk.%d.attn_q.weight", im), l.q, tmp, tmp_bytes, s_q) ||
+            upload_mat(e, T("blk.%d.attn_k.weight", im), l.k, tmp, tmp_bytes, s_kv) ||
+            upload_mat(e, T("blk.%d.attn_v.weight", im), l.v, tmp, tmp_bytes, s_kv) ||
+            upload_mat(e, T("blk.%d.attn_output.weight", im), l.o, tmp, tmp_bytes, s_o) ||
+            upload_mat(e, T("blk.%d.ffn_gate.weight", im), l.ffn_gate, tmp, tmp_bytes, s_up) ||
+            upload_mat(e, T("blk.%d.ffn_up.weight", im), l.ffn_up, tmp, tmp_bytes, s_up) ||
+            upload_mat(e, T("blk.%d.ffn_down.weight", im), l.ffn_down, tmp, tmp_bytes, s_down) ||
             upload_mat(e, T("blk.%d.nextn.eh_proj.weight", im), e.eh_proj, tmp, tmp_bytes) || build_gu(e, l))
             return -1;
         if (!(l.q_norm = upload_f32(e, T("blk.%d.attn_q_norm.weight", im))) ||
@@ -590,13 +695,13 @@ int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
     }
 
     // ---- states ----
-    e.conv_layer = (size_t)d.conv_dim * 4;
-    e.ssm_layer = (size_t)d.n_v_heads * d.head_v_dim * d.head_k_dim;
+    e.conv_layer = (size_t)(2 * e.nk_loc * dk + e.nv_loc * (int)d.head_v_dim) * 4;
+    e.ssm_layer = (size_t)e.nv_loc * d.head_v_dim * d.head_k_dim;
     e.conv_slot_stride = e.conv_layer * nr;
     e.ssm_slot_stride = e.ssm_layer * nr;
     e.conv_slots = (float*)e.dalloc(std::max<size_t>(1, e.conv_slot_stride * kNSlot) * 4);
     e.ssm_slots = (float*)e.dalloc(std::max<size_t>(1, e.ssm_slot_stride * kNSlot) * 4);
-    e.kv_layer = (size_t)n_ctx * d.n_kv_head * d.head_dim;
+    e.kv_layer = (size_t)n_ctx * e.nkv_loc * d.head_dim;
     e.kv_k = (float*)e.dalloc(std::max<size_t>(1, e.kv_layer * na) * 4);
     e.kv_v = (float*)e.dalloc(std::max<size_t>(1, e.kv_layer * na) * 4);
     e.mtp_k = (float*)e.dalloc(e.kv_layer * 4);
@@ -649,12 +754,17 @@ int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
         }
         const size_t flags_off = total;
         total += 256;
+        const size_t part_off = total;   // tensor parallelism: 2 slots of partial sums
+        total += 2 * (size_t)T8 * e.E * 4;
         e.arena = (char*)e.dalloc(total);
         if (!e.arena) { set_err(-2, "activation arena alloc"); return -1; }
         e.arena_bytes = total;
         CK(cudaMemset(e.arena, 0, total));
         for (int i = 0; i < 12; ++i) *dst[i] = (float*)(e.arena + off[i]);
         e.tp.flags = (unsigned*)(e.arena + flags_off);
+        e.part = (float*)(e.arena + part_off);
+        e.tp.part = e.part;
+        e.tp.part_slot = (long long)T8 * e.E;
     }
     e.h_save = A((size_t)T8 * e.E);
     e.qkvc = A((size_t)T8 * e.ld_qkv);
@@ -719,10 +829,17 @@ int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
 
 // ----------------------------- launch helpers ---------------------------------
 
+// How a GEMV runs under tensor parallelism (tp_world > 1):
+enum TpMode {
+    TP_LOCAL = 0,     // this rank's output rows (heads / FFN columns) stay here: no exchange
+    TP_PARTIAL = 1,   // this rank's input columns: partial sums, then qb_tp_reduce into the output
+    TP_GATHER = 2,    // this rank's rows stored into every rank's output (the vocabulary head)
+};
+
 // y = W x for every matrix of mats (one input, e.xb).  With epi (one matrix)
 // the launch also prepares the next input into e.xb_alt, which then becomes e.xb.
 int gemv_group(Engine& e, const DevMat* const* mats, float* const* outs, const long long* ldos, int nm, int K,
-               int N, int accumulate, const QbEpi* epi = nullptr) {
+               int N, int accumulate, const QbEpi* epi = nullptr, int tp_mode = TP_LOCAL) {
     if (epi && nm != 1) { set_err(-1, "fused epilogue on a multi-matrix GEMV"); return -1; }
     const QbInNorm in_norm{e.xss, e.eps};
     // fuse matrices of the same type; different types run as separate launches
@@ -743,9 +860,11 @@ int gemv_group(Engine& e, const DevMat* const* mats, float* const* outs, const l
             ++nt;
             ++i;
         }
-        if (e.tp_world > 1) {
+        if (e.tp_world > 1 && tp_mode != TP_LOCAL) {
             if (!e.tp_ready || type == QB_F32) { set_err(-1, "tensor-parallel GEMV before qb_tp_connect"); return -1; }
-            CK(qb_qmv_ex(type, segs, ns, K, N, e.xb, accumulate, nullptr, nullptr, &e.tp, e.work, e.st));
+            QbTp tp = e.tp;
+            tp.gather = tp_mode == TP_GATHER;
+            CK(qb_qmv_ex(type, segs, ns, K, N, e.xb, tp.gather ? accumulate : 0, nullptr, nullptr, &tp, e.work, e.st));
             continue;
         }
         if (type == QB_F32) {
@@ -770,6 +889,19 @@ int gemv_group(Engine& e, const DevMat* const* mats, float* const* outs, const l
 void fresh_input(Engine& e) {
     e.xss = nullptr;
     e.xready = false;
+}
+
+// Residual GEMV x += W h (x [N][E]).  Under tensor parallelism W holds this
+// rank's input columns: partial sums, then every rank adds all ranks' partials
+// in rank order (the all-reduce, by NVLink loads of the peers' slots).
+int residual_gemv(Engine& e, const DevMat* m, float* x, int K, int N, const QbEpi* epi) {
+    const DevMat* m1[1] = {m};
+    float* o1[1] = {x};
+    const long long ld1[1] = {e.E};
+    if (e.tp_world == 1) return gemv_group(e, m1, o1, ld1, 1, K, N, 1, epi);
+    if (gemv_group(e, m1, o1, ld1, 1, K, N, 0, nullptr, TP_PARTIAL)) return -1;
+    CK(qb_tp_reduce(x, e.E, e.E, N, e.tp, e.peer_part, e.work.err, e.st));
+    return 0;
 }
 
 // the qb_xprep outputs that the matrices consuming an input of N tokens read
@@ -826,13 +958,10 @@ int ffn_block(Engine& e, const LayerW& l, float* x, int B, const NextIn& next) {
         const long long ld2[2] = {e.F, e.F};
         if (gemv_group(e, m2, o2, ld2, 2, e.E, B, 0)) return -1;
         fresh_input(e);
-        CK(qb_silu_mul_xprep(e.gate, e.up, e.F, e.F, B, e.act, e.xb, xp_needs(e, {&l.ffn_down}, B), e.st));
+        CK(qb_silu_mul_xprep(e.gate, e.up, e.F, e.F_loc, B, e.act, e.xb, xp_needs(e, {&l.ffn_down}, B), e.st));
     }
     QbEpi eb;
-    const DevMat* m1[1] = {&l.ffn_down};
-    float* o1[1] = {x};
-    const long long ld1[1] = {e.E};
-    return gemv_group(e, m1, o1, ld1, 1, e.F, B, 1, residual_epi(e, next, eb));
+    return residual_gemv(e, &l.ffn_down, x, e.F_loc, B, residual_epi(e, next, eb));
 }
 
 // the readers of a layer's normed input: DeltaNet in-projections or q / k / v
@@ -849,29 +978,29 @@ NextIn ffn_in(const Engine& e, const LayerW& l, int B) {
 // gated attention block on residual x, positions *pos .. *pos+B-1
 int attn_block(Engine& e, const LayerW& l, float* x, int B, const uint32_t* pos, float* kc, float* vc,
                const NextIn& next) {
+    // this rank's q-heads and kv-heads (all of them on one GPU)
     const qwen_dims_t& d = e.d;
-    const int qw = 2 * d.n_head * d.head_dim, kvw = d.n_kv_head * d.head_dim;
+    const int qw = 2 * d.n_head * d.head_dim, kvw = d.n_kv_head * d.head_dim, kvw_loc = e.nkv_loc * d.head_dim;
     if (norm_input(e, x, l.attn_norm, B, xp_needs(e, {&l.q, &l.k, &l.v}, B))) return -1;
     const DevMat* m3[3] = {&l.q, &l.k, &l.v};
-    float* o3[3] = {e.qbuf, e.kvbuf, e.kvbuf + kvw};
+    float* o3[3] = {e.qbuf, e.kvbuf, e.kvbuf + kvw_loc};
     const long long ld3[3] = {qw, 2 * kvw, 2 * kvw};
     if (gemv_group(e, m3, o3, ld3, 3, e.E, B, 0)) return -1;
-    CK(qb_attn_prep(e.qbuf, qw, e.kvbuf, 2 * kvw, l.q_norm, l.k_norm, d.n_head, d.n_kv_head, d.head_dim,
+    CK(qb_attn_prep(e.qbuf, qw, e.kvbuf, 2 * kvw, l.q_norm, l.k_norm, e.nh_loc, e.nkv_loc, d.head_dim,
                     e.rope_half, e.rope_cos, e.rope_sin, pos, B, e.eps, kc, vc, e.st));
     fresh_input(e);
-    CK(qb_attn_decode(e.qbuf, qw, kc, vc, d.n_head, d.n_kv_head, d.head_dim, pos, B, e.n_ctx, e.attn_o,
-                      d.n_head * d.head_dim, e.attn_po, e.attn_pml, e.xb, xp_needs(e, {&l.o}, B), e.st));
-    const int ow = d.n_head * d.head_dim;
+    CK(qb_attn_decode(e.qbuf, qw, kc, vc, e.nh_loc, e.nkv_loc, d.head_dim, pos, B, e.n_ctx, e.attn_o,
+                      e.nh_loc * d.head_dim, e.attn_po, e.attn_pml, e.xb, xp_needs(e, {&l.o}, B), e.st));
     QbEpi eb;
-    const DevMat* m1[1] = {&l.o};
-    float* o1[1] = {x};
-    const long long ld1[1] = {e.E};
-    if (gemv_group(e, m1, o1, ld1, 1, ow, B, 1, residual_epi(e, ffn_in(e, l, B), eb))) return -1;
+    if (residual_gemv(e, &l.o, x, e.nh_loc * d.head_dim, B, residual_epi(e, ffn_in(e, l, B), eb))) return -1;
     return ffn_block(e, l, x, B, next);
 }
 
 int gdn_block(Engine& e, const LayerW& l, int B, int ckpt, const NextIn& next) {
+    // this rank's k-heads, their v-heads and conv channels (all of them on one GPU)
     const qwen_dims_t& d = e.d;
+    const int conv_loc = 2 * e.nk_loc * (int)d.head_k_dim + e.nv_loc * (int)d.head_v_dim;
+    const int inner_loc = e.nv_loc * (int)d.head_v_dim;
     if (norm_input(e, e.bx, l.attn_norm, B, xp_needs(e, {&l.wqkv, &l.wgate, &l.wbeta, &l.walpha}, B))) return -1;
     const DevMat* m4[4] = {&l.wqkv, &l.wgate, &l.wbeta, &l.walpha};
     float* o4[4] = {e.qkv, e.z, e.beta, e.alpha};
@@ -879,23 +1008,20 @@ int gdn_block(Engine& e, const LayerW& l, int B, int ckpt, const NextIn& next) {
     if (gemv_group(e, m4, o4, ld4, 4, e.E, B, 0)) return -1;
     float* conv = e.conv_slots + (size_t)l.ridx * e.conv_layer;
     float* ssm = e.ssm_slots + (size_t)l.ridx * e.ssm_layer;
-    CK(qb_gdn_conv(e.qkv, e.ld_qkv, d.conv_dim, B, l.conv_w, conv, e.conv_slot_stride, &e.ctrl->cur_slot, ckpt,
-                   e.qkvc, e.ld_qkv, e.beta, e.alpha, 256, l.dt_bias, l.ssm_a, d.n_v_heads, e.gates, e.st));
-    CK(qb_gdn_recur(e.qkvc, e.ld_qkv, e.gates, d.n_k_heads, d.n_v_heads, d.head_k_dim, B, e.eps, ssm,
+    CK(qb_gdn_conv(e.qkv, e.ld_qkv, conv_loc, B, l.conv_w, conv, e.conv_slot_stride, &e.ctrl->cur_slot, ckpt,
+                   e.qkvc, e.ld_qkv, e.beta, e.alpha, 256, l.dt_bias, l.ssm_a, e.nv_loc, e.gates, e.st));
+    CK(qb_gdn_recur(e.qkvc, e.ld_qkv, e.gates, e.nk_loc, e.nv_loc, d.head_k_dim, B, e.eps, ssm,
                     e.ssm_slot_stride, &e.ctrl->cur_slot, ckpt, e.o, d.d_inner, e.st));
     fresh_input(e);
-    if (d.head_v_dim == 128 && d.n_v_heads % 2 == 0) {
-        CK(qb_gdn_out_xprep(e.o, e.z, d.d_inner, l.ssm_norm, d.n_v_heads, d.head_v_dim, B, e.eps, e.y, e.xb,
+    if (d.head_v_dim == 128 && e.nv_loc % 2 == 0) {
+        CK(qb_gdn_out_xprep(e.o, e.z, d.d_inner, l.ssm_norm, e.nv_loc, d.head_v_dim, B, e.eps, e.y, e.xb,
                             xp_needs(e, {&l.ssm_out}, B), e.st));
     } else {
-        CK(qb_gdn_out(e.o, e.z, d.d_inner, l.ssm_norm, d.n_v_heads, d.head_v_dim, B, e.eps, e.y, e.st));
-        if (xprep1(e, e.y, d.d_inner, nullptr, d.d_inner, B, xp_needs(e, {&l.ssm_out}, B))) return -1;
+        CK(qb_gdn_out(e.o, e.z, d.d_inner, l.ssm_norm, e.nv_loc, d.head_v_dim, B, e.eps, e.y, e.st));
+        if (xprep1(e, e.y, d.d_inner, nullptr, inner_loc, B, xp_needs(e, {&l.ssm_out}, B))) return -1;
     }
     QbEpi eb;
-    const DevMat* m1[1] = {&l.ssm_out};
-    float* o1[1] = {e.bx};
-    const long long ld1[1] = {e.E};
-    if (gemv_group(e, m1, o1, ld1, 1, d.d_inner, B, 1, residual_epi(e, ffn_in(e, l, B), eb))) return -1;
+    if (residual_gemv(e, &l.ssm_out, e.bx, inner_loc, B, residual_epi(e, ffn_in(e, l, B), eb))) return -1;
     return ffn_block(e, l, e.bx, B, next);
 }
 
@@ -923,7 +1049,7 @@ int fwd_backbone(Engine& e, int B, int ckpt) {
     const DevMat* m1[1] = {&e.output};
     float* o1[1] = {e.logits};
     const long long ld1[1] = {e.V};
-    if (gemv_group(e, m1, o1, ld1, 1, e.E, B, 0)) return -1;
+    if (gemv_group(e, m1, o1, ld1, 1, e.E, B, 0, nullptr, TP_GATHER)) return -1;
     CK(qb_argmax_reset(e.keys, B, e.st));
     CK(qb_argmax(e.logits, e.V, e.V, B, e.keys, e.st));
     CK(qb_argmax_to_u32(e.keys, B, e.ctrl->argmax, e.st));
@@ -952,7 +1078,7 @@ int fwd_mtp(Engine& e, int B, const float* hsrc, int want_logits) {
         const DevMat* mo[1] = {&e.output};
         float* oo[1] = {e.mtp_logits};
         const long long ldo[1] = {e.V};
-        if (gemv_group(e, mo, oo, ldo, 1, e.E, B, 0)) return -1;
+        if (gemv_group(e, mo, oo, ldo, 1, e.E, B, 0, nullptr, TP_GATHER)) return -1;
         CK(qb_argmax_reset(e.keys + QB_MAX_TOK, B, e.st));
         CK(qb_argmax(e.mtp_logits, e.V, e.V, B, e.keys + QB_MAX_TOK, e.st));
         CK(qb_argmax_to_u32(e.keys + QB_MAX_TOK, B, e.ctrl->mtp_argmax, e.st));
@@ -1190,7 +1316,9 @@ extern "C" int qb_tp_connect(qwen_model_t* m, const void* handles, int64_t strid
         }
         e->peer_arena[r] = p;
         e->tp.delta[q++] = (long long)((char*)p - e->arena);
+        e->peer_part[r] = (const float*)((char*)p + ((char*)e->part - e->arena));
     }
+    e->peer_part[e->tp_rank] = e->part;
     e->tp.done = (unsigned*)e->dalloc(256);
     if (!e->tp.done) { set_err(-2, "tp counters"); return -1; }
     e->tp.seq = e->tp.done + 32;
@@ -1485,7 +1613,7 @@ extern "C" int qb_reset(qwen_model_t* m) {
 }
 
 namespace {
-size_t mat_bytes(const DevMat& w) { return gguf_row_bytes(w.type, (uint64_t)w.K) * (size_t)w.rows_all; }
+size_t mat_bytes(const DevMat& w) { return w.bytes_all; }
 
 int record_verify(Engine& e, int B) { return fwd_backbone(e, B, 1); }
 int record_draft(Engine& e, int) { return fwd_mtp(e, 1, e.mtp_h, 1); }
@@ -1560,7 +1688,7 @@ extern "C" float qb_bench(qwen_model_t* m, int what, uint32_t arg, uint32_t iter
                         const DevMat* m1[1] = {&en.output};
                         float* o1[1] = {en.logits};
                         const long long ld1[1] = {en.V};
-                        if (gemv_group(en, m1, o1, ld1, 1, en.E, a, 0)) return -1;
+                        if (gemv_group(en, m1, o1, ld1, 1, en.E, a, 0, nullptr, TP_GATHER)) return -1;
                     }
                 }
                 return 0;

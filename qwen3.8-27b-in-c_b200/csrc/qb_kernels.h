@@ -87,12 +87,16 @@ struct QbInNorm {
     const float* ss;
     float eps;
 };
-// Tensor parallelism of one GEMV launch (row-sharded weights, one process per
-// GPU): the segments hold this rank's rows, every output value is stored both
-// locally and at the same address of each peer's buffer (dst + delta[i], over
-// NVLink), and the launch ends with a bounded cross-rank barrier, so that when
-// it completes every rank holds all rows.  The output buffers, and flags, lie
-// in an arena each peer has mapped.
+// Tensor parallelism of one GEMV launch (one process per GPU; the buffers
+// involved and the flags lie in an arena every peer has mapped).  Two modes:
+//  * gather: the segments hold this rank's rows; every output value is stored
+//    both locally and at the same address of each peer's buffer (dst +
+//    delta[i], over NVLink), and the launch ends with a bounded cross-rank
+//    barrier, so that when it completes every rank holds all rows;
+//  * partial (gather = 0): the matrix holds this rank's share of the input
+//    columns; the launch writes its partial sums (all rows, accumulate = 0) to
+//    part + (sequence parity) * part_slot and signals the peers without
+//    waiting; qb_tp_reduce then adds every rank's partials to the output.
 #define QB_TP_MAX 8
 struct QbTp {
     int rank, world;
@@ -100,7 +104,15 @@ struct QbTp {
     unsigned* flags;                  // [QB_TP_MAX] in the shared arena, zero-initialised
     unsigned* done;                   // zero-initialised
     unsigned* seq;                    // zero-initialised; counts this rank's TP launches
+    int gather;
+    float* part;                      // partial mode: 2 slots in the shared arena
+    long long part_slot;              // floats per slot
 };
+// x[t * ldx + e] += sum over ranks r (in rank order) of rank r's partial sums
+// of the last partial-mode launch (e < E, t < N), after a bounded wait for
+// every peer's signal.  parts[r] = rank r's part buffer mapped here.
+cudaError_t qb_tp_reduce(float* x, long long ldx, int E, int N, const QbTp& tp, const float* const* parts,
+                         unsigned* err, cudaStream_t st);
 // nseg == 0 is allowed with tp (a rank without rows of this launch still takes part in the barrier)
 cudaError_t qb_qmv_ex(int type, const QbQSeg* segs, int nseg, int K, int N, const QbXBuf& xb, int accumulate,
                       const QbInNorm* in_norm, const QbEpi* epi, const QbTp* tp, const QbQmvWork& work,

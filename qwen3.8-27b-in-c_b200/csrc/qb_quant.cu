@@ -417,6 +417,9 @@ __host__ __device__ constexpr int tile_block_bytes(int type) {
 
 struct TpK {
     int np, rank;                // peers, this rank
+    int gather;                  // 1: rows to every peer + wait; 0: partial sums into part, signal only
+    float* part;                 // partial mode: 2 slots of [.][ldo], the slot = this launch's sequence parity
+    long long part_slot;         // floats per slot
     long long delta[QB_TP_MAX - 1];   // byte offset from a local arena address to the same address of peer i
     unsigned* flags;             // [QB_TP_MAX] in the shared arena: the last sequence number seen from each rank
     unsigned* done;              // warps of the grid that finished (zero between launches)
@@ -593,9 +596,12 @@ __device__ __forceinline__ void pair_final(const QmvK& p, int pair, float (&v)[2
                 const int tok = (i & 1) ? t1 : t0;
                 if (tok < p.N && rr < S.rows && rr >= p.row_lo && rr < p.row_hi) {
                     float* dst = S.out + (size_t)tok * S.ldo + rr;
+                    if (TP && !p.tp.gather)   // partial sums of this rank, in the slot of this launch
+                        dst = p.tp.part + (size_t)(*(volatile const unsigned*)p.tp.seq & 1u) * p.tp.part_slot +
+                              (size_t)tok * S.ldo + rr;
                     const float y = p.accumulate ? (__ldcg(dst) + v[t][i]) : v[t][i];
                     *dst = y;
-                    if (TP)
+                    if (TP && p.tp.gather)
                         for (int q = 0; q < p.tp.np; ++q)
                             *reinterpret_cast<float*>(reinterpret_cast<char*>(dst) + p.tp.delta[q]) = y;
                 }
@@ -744,7 +750,7 @@ __device__ __forceinline__ void pair_out_i8(const float (&tok)[2][2][2], float (
     active = NT == 1 ? (c < 2) : true;
 }
 
-// Tensor parallelism: a warp that is done (its peer stores included) arrives
+// Tensor parallelism: a warp that is done (its stores, peer stores included) arrives
 // on its CTA's shared counter (acquire-release, so the CTA's last warp has
 // observed every store of the CTA); that warp makes them visible system-wide
 // and arrives on the device counter; the grid's last CTA publishes the
@@ -769,6 +775,7 @@ __device__ __noinline__ void tp_arrive(TpK t, uint32_t s_arrive, int lane) {
         unsigned* slot = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(t.flags + t.rank) + t.delta[q]);
         asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(slot), "r"(seq) : "memory");
     }
+    if (!t.gather) return;   // partial sums: the reduction waits for the peers
     for (int q = 0; q < t.np; ++q) {
         const int peer = q < t.rank ? q : q + 1;
         const unsigned* f = t.flags + peer;
@@ -968,6 +975,63 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_kernel(QmvK p) {
     }
     if (cur_pair >= 0) finish(cur_pair);
     if (TP) tp_arrive(p.tp, smem_u32(&s_arrive), lane);
+}
+
+// ----------------------- tensor-parallel reduction ------------------------
+struct TpR {
+    int world, rank;
+    const float* part[QB_TP_MAX];   // rank r's part buffer (2 slots), mapped here
+    long long slot;
+    const unsigned* flags;
+    const unsigned* seq;
+    unsigned* err;
+};
+
+// x += sum over ranks of the last partial-mode launch's partial sums, in rank
+// order (every rank adds the same numbers in the same order).  Each CTA's
+// thread 0 waits, bounded, until every peer has signalled this launch.
+__global__ void __launch_bounds__(256) tp_reduce_kernel(float* __restrict__ x, long long ldx, int E, int N, TpR r) {
+    pdl_wait();
+    pdl_trigger();
+    __shared__ unsigned s_seq;
+    __shared__ int s_ok;
+    if (threadIdx.x == 0) {
+        const unsigned sq = *(volatile const unsigned*)r.seq;
+        int ok = 1;
+        for (int q = 0; q < r.world && ok; ++q) {
+            if (q == r.rank) continue;
+            for (uint32_t it = 0;; ++it) {
+                unsigned v;
+                asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(r.flags + q) : "memory");
+                if ((int)(v - sq) >= 0) break;
+                if (it >= (1u << 24)) {
+                    atomicExch(r.err, 4u);
+                    ok = 0;
+                    break;
+                }
+                __nanosleep(64);
+            }
+        }
+        s_seq = sq;
+        s_ok = ok;
+    }
+    __syncthreads();
+    if (!s_ok) return;
+    const size_t off = (size_t)((s_seq - 1u) & 1u) * r.slot;   // the slot the partial launch wrote
+    const int n4 = E >> 2;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= N * n4) return;
+    const int t = i / n4, e = (i - t * n4) * 4;
+    const size_t pe = off + (size_t)t * E + e;
+    float4 acc = __ldcg(reinterpret_cast<const float4*>(r.part[0] + pe));
+    for (int q = 1; q < r.world; ++q) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(r.part[q] + pe));
+        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    float4* xp = reinterpret_cast<float4*>(x + (size_t)t * ldx + e);
+    float4 xv = *xp;
+    xv.x += acc.x; xv.y += acc.y; xv.z += acc.z; xv.w += acc.w;
+    *xp = xv;
 }
 
 // ------------------------------- F32 ---------------------------------------
@@ -1342,6 +1406,11 @@ cudaError_t qmv_launch(int type, const QbQSeg* segs, int nseg, int K, int N, con
         p.tp.done = tp->done;
         p.tp.seq = tp->seq;
         p.tp.err = work.err;
+        p.tp.gather = tp->gather;
+        p.tp.part = tp->part;
+        p.tp.part_slot = tp->part_slot;
+        if (!tp->gather && (!tp->part || accumulate || nseg > 1 || (nseg == 1 && segs[0].ldo * QB_MAX_TOK > tp->part_slot)))
+            return cudaErrorInvalidValue;
     }
     p.err = work.err;
     if (in_norm && in_norm->ss) {
@@ -1410,6 +1479,25 @@ cudaError_t qb_qmv_ex(int type, const QbQSeg* segs, int nseg, int K, int N, cons
                       const QbInNorm* in_norm, const QbEpi* epi, const QbTp* tp, const QbQmvWork& work,
                       cudaStream_t st) {
     return qmv_launch(type, segs, nseg, K, N, xb, accumulate, 0, 1 << 30, in_norm, epi, tp, work, st);
+}
+
+cudaError_t qb_tp_reduce(float* x, long long ldx, int E, int N, const QbTp& tp, const float* const* parts,
+                         unsigned* err, cudaStream_t st) {
+    if (tp.world < 2 || tp.world > QB_TP_MAX || E % 4 || ldx % 4 || N < 1 || N > QB_MAX_TOK || !tp.flags || !tp.seq)
+        return cudaErrorInvalidValue;
+    TpR r = {};
+    r.world = tp.world;
+    r.rank = tp.rank;
+    for (int q = 0; q < tp.world; ++q) {
+        if (!parts[q]) return cudaErrorInvalidValue;
+        r.part[q] = parts[q];
+    }
+    r.slot = tp.part_slot;
+    r.flags = tp.flags;
+    r.seq = tp.seq;
+    r.err = err;
+    const int n = N * (E / 4);
+    return qb_launch(tp_reduce_kernel, dim3((n + 255) / 256), dim3(256), 0, st, x, ldx, E, N, r);
 }
 
 cudaError_t qb_interleave_tiles(int type, const void* a, const void* b, int rows, int K, void* dst, cudaStream_t st) {

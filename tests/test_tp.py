@@ -1,9 +1,12 @@
-"""Tensor parallelism: the row split (CPU) and 2-rank runs against the golden
-token streams and a single-GPU run (GPU, needs 2 devices).
+"""Tensor parallelism: the vocabulary row split (CPU) and 2-rank runs against
+the compiled reference engine and a single-GPU run (GPU, needs 2 devices).
 
-Each rank holds the rows qb_tp_rows gives it of every quantised matrix; a
-GEMV stores its rows into every rank's copy of the output and ends with a
-cross-rank barrier, so all ranks must hold the same activations and tokens.
+Each rank keeps its share of the DeltaNet k-heads (with their v-heads),
+attention q-/kv-heads and FFN columns, so the mixers and the FFN run on
+local data; the out-projections and the down projection write partial sums
+that every rank adds up in rank order; the output head splits over the
+vocabulary, its rows stored into every rank's logits.  All ranks must hold
+the same logits and emit the same tokens as one GPU and as the reference.
 """
 import os
 import socket
@@ -64,40 +67,36 @@ def close(m):
     m.close()
     dist.barrier()
 
-for name, seed, profile in (("tiny_spec", 1, 0), ("tiny_mixed_spec", 2, 1)):
-    g = np.load(os.path.join({root!r}, "tests", "golden", name + ".npz"))
-    path = qb.write_synth_gguf(os.path.join({tmp!r}, f"{{name}}_{{rank}}.gguf"), qb.TINY, seed=seed, profile=profile)
-    m = group(path, 256)
-    m.prefill(g["prompt"], 1)
-    r = rel(m.logits()[:64], g["prefill_logits64"])
-    assert r < 1e-4, (name, r)
-    toks, js = m.spec_generate(int(g["n_predict"]), 3, forced=g["forced"])
-    assert np.array_equal(toks, g["tokens"]), (name, rank, toks[:16], g["tokens"][:16])
-    assert np.array_equal(js, g["accept"]), (name, rank, js, g["accept"])
-    close(m)
+from conftest import oracle
 
-# full layer widths: the same tokens and logits as one GPU
-path = qb.write_synth_gguf(os.path.join({tmp!r}, f"wide_{{rank}}.gguf"), qb.WIDE4, seed=4)
-p = np.random.default_rng(7).integers(0, qb.WIDE4["vocab"], 12).astype(np.uint32)
-forced = np.array([3, 0, 2, 1, 3, 3, 0, 1], np.uint32)
-ref = None
-if rank == 0:
-    s = qb.Model(path, 128)
+def single(path, shape, n_ctx, p, forced, n, reference):
+    # logits after the prompt, tokens, accept lengths, final logits on one GPU (or the reference)
+    s = oracle.RefModel(path, n_ctx, 8) if reference else qb.Model(path, n_ctx)
     s.prefill(p, 1)
     l0 = s.logits().copy()
-    st, sj = s.spec_generate(24, 3, forced=forced)
-    ref = (l0, st, sj, s.logits().copy())
+    st, sj = s.spec_generate(n, 3, forced=forced)
+    out = (l0, np.asarray(st), np.asarray(sj), s.logits().copy())
     s.close()
-obj = [ref]
-dist.broadcast_object_list(obj, 0)
-l0, st, sj, l1 = obj[0]
-m = group(path, 128)
-m.prefill(p, 1)
-assert rel(m.logits(), l0) < 1e-5, rel(m.logits(), l0)
-tt, tj = m.spec_generate(24, 3, forced=forced)
-assert np.array_equal(tt, st) and np.array_equal(tj, sj), (tt, st, tj, sj)
-assert rel(m.logits(), l1) < 1e-5, rel(m.logits(), l1)
-close(m)
+    return out
+
+for shape, name, seed, n_ctx, n, refs in ((qb.SMALL, "small", 3, 256, 40, (False, True)),
+                                          (qb.WIDE4, "wide4", 4, 128, 24, (False,))):
+    path = qb.write_synth_gguf(os.path.join({tmp!r}, f"{{name}}_{{rank}}.gguf"), shape, seed=seed)
+    p = np.random.default_rng(7).integers(0, shape["vocab"], 12).astype(np.uint32)
+    forced = np.array([3, 0, 2, 1, 3, 3, 0, 1], np.uint32)
+    obj = [[single(path, shape, n_ctx, p, forced, n, r) for r in refs] if rank == 0 else None]
+    dist.broadcast_object_list(obj, 0)
+    m = group(path, n_ctx)
+    m.prefill(p, 1)
+    l0 = m.logits().copy()
+    tt, tj = m.spec_generate(n, 3, forced=forced)
+    l1 = m.logits().copy()
+    close(m)
+    for r, (s0, st, sj, s1) in zip(refs, obj[0]):
+        who = (name, "reference" if r else "one GPU", rank)
+        assert rel(l0, s0) < 1e-4, (who, rel(l0, s0))
+        assert np.array_equal(tt, st) and np.array_equal(tj, sj), (who, tt, st, tj, sj)
+        assert rel(l1, s1) < 1e-4, (who, rel(l1, s1))
 dist.destroy_process_group()
 print("tp ok", rank)
 """
