@@ -323,8 +323,8 @@ struct Engine {
     // FFN columns [f0, f0 + F_loc)
     int nk_loc = 0, nv_loc = 0, nh_loc = 0, nkv_loc = 0, F_loc = 0;
     int k0 = 0, h0 = 0, kv0 = 0, f0 = 0;
-    float* part = nullptr;                // [2][QB_MAX_TOK][E] partial sums of the residual GEMVs (arena)
-    const float* peer_part[QB_TP_MAX] = {};   // rank r's part buffer, mapped here
+    uint2* part = nullptr;                // [2][QB_MAX_TOK][E] (value, tag) partial sums of the residual GEMVs (arena)
+    const void* peer_part[QB_TP_MAX] = {};    // rank r's part buffer, mapped here
     bool use_tc = false;                  // IQ4_XS at N <= 4 on tcgen05 (QB_TC=1); default: int8 mma.sync
     float* attn_po = nullptr;             // attention chunk partials (qb_attn_decode)
     float2* gates = nullptr;              // DeltaNet (beta, decay) per (token, v-head)
@@ -755,14 +755,14 @@ int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
         const size_t flags_off = total;
         total += 256;
         const size_t part_off = total;   // tensor parallelism: 2 slots of partial sums
-        total += 2 * (size_t)T8 * e.E * 4;
+        total += 2 * (size_t)T8 * e.E * 8;
         e.arena = (char*)e.dalloc(total);
         if (!e.arena) { set_err(-2, "activation arena alloc"); return -1; }
         e.arena_bytes = total;
         CK(cudaMemset(e.arena, 0, total));
         for (int i = 0; i < 12; ++i) *dst[i] = (float*)(e.arena + off[i]);
         e.tp.flags = (unsigned*)(e.arena + flags_off);
-        e.part = (float*)(e.arena + part_off);
+        e.part = (uint2*)(e.arena + part_off);
         e.tp.part = e.part;
         e.tp.part_slot = (long long)T8 * e.E;
     }
@@ -1316,7 +1316,7 @@ extern "C" int qb_tp_connect(qwen_model_t* m, const void* handles, int64_t strid
         }
         e->peer_arena[r] = p;
         e->tp.delta[q++] = (long long)((char*)p - e->arena);
-        e->peer_part[r] = (const float*)((char*)p + ((char*)e->part - e->arena));
+        e->peer_part[r] = (const void*)((char*)p + ((char*)e->part - e->arena));
     }
     e->peer_part[e->tp_rank] = e->part;
     e->tp.done = (unsigned*)e->dalloc(256);

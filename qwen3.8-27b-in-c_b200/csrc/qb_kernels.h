@@ -94,9 +94,11 @@ struct QbInNorm {
 //    delta[i], over NVLink), and the launch ends with a bounded cross-rank
 //    barrier, so that when it completes every rank holds all rows;
 //  * partial (gather = 0): the matrix holds this rank's share of the input
-//    columns; the launch writes its partial sums (all rows, accumulate = 0) to
-//    part + (sequence parity) * part_slot and signals the peers without
-//    waiting; qb_tp_reduce then adds every rank's partials to the output.
+//    columns; the launch writes its partial sums (all rows, accumulate = 0) as
+//    8-byte (value, tag) words to part + (sequence parity) * part_slot, the
+//    tag being its sequence number, so no fence or flag is needed;
+//    qb_tp_reduce then adds every rank's partials, as their tags arrive, to
+//    the output.
 #define QB_TP_MAX 8
 struct QbTp {
     int rank, world;
@@ -105,13 +107,13 @@ struct QbTp {
     unsigned* done;                   // zero-initialised
     unsigned* seq;                    // zero-initialised; counts this rank's TP launches
     int gather;
-    float* part;                      // partial mode: 2 slots in the shared arena
-    long long part_slot;              // floats per slot
+    void* part;                       // partial mode: 2 slots of (value, tag) words in the shared arena
+    long long part_slot;              // words per slot
 };
 // x[t * ldx + e] += sum over ranks r (in rank order) of rank r's partial sums
-// of the last partial-mode launch (e < E, t < N), after a bounded wait for
-// every peer's signal.  parts[r] = rank r's part buffer mapped here.
-cudaError_t qb_tp_reduce(float* x, long long ldx, int E, int N, const QbTp& tp, const float* const* parts,
+// of the last partial-mode launch (e < E, t < N), each read once its tag is
+// there (bounded wait).  parts[r] = rank r's part buffer mapped here.
+cudaError_t qb_tp_reduce(float* x, long long ldx, int E, int N, const QbTp& tp, const void* const* parts,
                          unsigned* err, cudaStream_t st);
 // nseg == 0 is allowed with tp (a rank without rows of this launch still takes part in the barrier)
 cudaError_t qb_qmv_ex(int type, const QbQSeg* segs, int nseg, int K, int N, const QbXBuf& xb, int accumulate,

@@ -417,9 +417,9 @@ __host__ __device__ constexpr int tile_block_bytes(int type) {
 
 struct TpK {
     int np, rank;                // peers, this rank
-    int gather;                  // 1: rows to every peer + wait; 0: partial sums into part, signal only
-    float* part;                 // partial mode: 2 slots of [.][ldo], the slot = this launch's sequence parity
-    long long part_slot;         // floats per slot
+    int gather;                  // 1: rows to every peer + wait; 0: tagged partial sums into part
+    uint2* part;                 // partial mode: 2 slots of [.][ldo] (value, tag), slot = sequence parity
+    long long part_slot;         // words per slot
     long long delta[QB_TP_MAX - 1];   // byte offset from a local arena address to the same address of peer i
     unsigned* flags;             // [QB_TP_MAX] in the shared arena: the last sequence number seen from each rank
     unsigned* done;              // warps of the grid that finished (zero between launches)
@@ -596,9 +596,14 @@ __device__ __forceinline__ void pair_final(const QmvK& p, int pair, float (&v)[2
                 const int tok = (i & 1) ? t1 : t0;
                 if (tok < p.N && rr < S.rows && rr >= p.row_lo && rr < p.row_hi) {
                     float* dst = S.out + (size_t)tok * S.ldo + rr;
-                    if (TP && !p.tp.gather)   // partial sums of this rank, in the slot of this launch
-                        dst = p.tp.part + (size_t)(*(volatile const unsigned*)p.tp.seq & 1u) * p.tp.part_slot +
-                              (size_t)tok * S.ldo + rr;
+                    if (TP && !p.tp.gather) {
+                        // partial sum of this rank as one 8-byte (value, tag) store, tag = this launch's
+                        // sequence number: a peer that sees the tag has the value (no fence, no flag)
+                        const unsigned sq = *(volatile const unsigned*)p.tp.seq;
+                        uint2* w = p.tp.part + (size_t)(sq & 1u) * p.tp.part_slot + (size_t)tok * S.ldo + rr;
+                        *w = make_uint2(__float_as_uint(v[t][i]), sq + 1u);
+                        continue;
+                    }
                     const float y = p.accumulate ? (__ldcg(dst) + v[t][i]) : v[t][i];
                     *dst = y;
                     if (TP && p.tp.gather)
@@ -765,17 +770,17 @@ __device__ __noinline__ void tp_arrive(TpK t, uint32_t s_arrive, int lane) {
     unsigned old;
     asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], 1;" : "=r"(old) : "r"(s_arrive) : "memory");
     if (old != kConsumers - 1) return;
-    __threadfence_system();   // the CTA's stores, peer stores included
+    if (t.gather) __threadfence_system();   // the CTA's stores, peer stores included
     old = atom_add_acq_rel_gpu(t.done, 1u);
     if (old != gridDim.x - 1) return;
     *t.done = 0u;   // ready for the next launch
     const unsigned seq = *t.seq + 1u;
     *t.seq = seq;
+    if (!t.gather) return;   // tagged partial sums: the reduction checks the tags
     for (int q = 0; q < t.np; ++q) {
         unsigned* slot = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(t.flags + t.rank) + t.delta[q]);
         asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(slot), "r"(seq) : "memory");
     }
-    if (!t.gather) return;   // partial sums: the reduction waits for the peers
     for (int q = 0; q < t.np; ++q) {
         const int peer = q < t.rank ? q : q + 1;
         const unsigned* f = t.flags + peer;
@@ -979,58 +984,53 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_kernel(QmvK p) {
 
 // ----------------------- tensor-parallel reduction ------------------------
 struct TpR {
-    int world, rank;
-    const float* part[QB_TP_MAX];   // rank r's part buffer (2 slots), mapped here
+    int world;
+    const uint2* part[QB_TP_MAX];   // rank r's part buffer (2 slots of (value, tag)), mapped here
     long long slot;
-    const unsigned* flags;
     const unsigned* seq;
     unsigned* err;
 };
 
 // x += sum over ranks of the last partial-mode launch's partial sums, in rank
-// order (every rank adds the same numbers in the same order).  Each CTA's
-// thread 0 waits, bounded, until every peer has signalled this launch.
+// order (every rank adds the same numbers in the same order).  A partial sum
+// counts once its tag equals this rank's sequence number, which that launch
+// advanced: an element not yet tagged is re-read (bounded).
 __global__ void __launch_bounds__(256) tp_reduce_kernel(float* __restrict__ x, long long ldx, int E, int N, TpR r) {
     pdl_wait();
     pdl_trigger();
-    __shared__ unsigned s_seq;
-    __shared__ int s_ok;
-    if (threadIdx.x == 0) {
-        const unsigned sq = *(volatile const unsigned*)r.seq;
-        int ok = 1;
-        for (int q = 0; q < r.world && ok; ++q) {
-            if (q == r.rank) continue;
-            for (uint32_t it = 0;; ++it) {
-                unsigned v;
-                asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(r.flags + q) : "memory");
-                if ((int)(v - sq) >= 0) break;
-                if (it >= (1u << 24)) {
-                    atomicExch(r.err, 4u);
-                    ok = 0;
-                    break;
-                }
-                __nanosleep(64);
-            }
-        }
-        s_seq = sq;
-        s_ok = ok;
-    }
-    __syncthreads();
-    if (!s_ok) return;
-    const size_t off = (size_t)((s_seq - 1u) & 1u) * r.slot;   // the slot the partial launch wrote
-    const int n4 = E >> 2;
+    const unsigned sq = *(volatile const unsigned*)r.seq;
+    const size_t off = (size_t)((sq - 1u) & 1u) * r.slot;   // the slot the partial launch wrote
+    const int n2 = E >> 1;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= N * n4) return;
-    const int t = i / n4, e = (i - t * n4) * 4;
+    if (i >= N * n2) return;
+    const int t = i / n2, e = (i - t * n2) * 2;
     const size_t pe = off + (size_t)t * E + e;
-    float4 acc = __ldcg(reinterpret_cast<const float4*>(r.part[0] + pe));
-    for (int q = 1; q < r.world; ++q) {
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(r.part[q] + pe));
-        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    float a0 = 0.f, a1 = 0.f;
+    for (int q = 0; q < r.world; ++q) {
+        const uint4* src = reinterpret_cast<const uint4*>(r.part[q] + pe);
+        uint4 v;
+        for (uint32_t it = 0;; ++it) {
+            asm volatile("ld.volatile.global.v4.u32 {%0,%1,%2,%3}, [%4];"
+                         : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(src) : "memory");
+            if (v.y == sq && v.w == sq) break;
+            if (it >= (1u << 22)) {
+                atomicExch(r.err, 4u);
+                return;
+            }
+            __nanosleep(32);
+        }
+        if (q == 0) {
+            a0 = __uint_as_float(v.x);
+            a1 = __uint_as_float(v.z);
+        } else {
+            a0 += __uint_as_float(v.x);
+            a1 += __uint_as_float(v.z);
+        }
     }
-    float4* xp = reinterpret_cast<float4*>(x + (size_t)t * ldx + e);
-    float4 xv = *xp;
-    xv.x += acc.x; xv.y += acc.y; xv.z += acc.z; xv.w += acc.w;
+    float2* xp = reinterpret_cast<float2*>(x + (size_t)t * ldx + e);
+    float2 xv = *xp;
+    xv.x += a0;
+    xv.y += a1;
     *xp = xv;
 }
 
@@ -1407,7 +1407,7 @@ cudaError_t qmv_launch(int type, const QbQSeg* segs, int nseg, int K, int N, con
         p.tp.seq = tp->seq;
         p.tp.err = work.err;
         p.tp.gather = tp->gather;
-        p.tp.part = tp->part;
+        p.tp.part = reinterpret_cast<uint2*>(tp->part);
         p.tp.part_slot = tp->part_slot;
         if (!tp->gather && (!tp->part || accumulate || nseg > 1 || (nseg == 1 && segs[0].ldo * QB_MAX_TOK > tp->part_slot)))
             return cudaErrorInvalidValue;
@@ -1481,22 +1481,20 @@ cudaError_t qb_qmv_ex(int type, const QbQSeg* segs, int nseg, int K, int N, cons
     return qmv_launch(type, segs, nseg, K, N, xb, accumulate, 0, 1 << 30, in_norm, epi, tp, work, st);
 }
 
-cudaError_t qb_tp_reduce(float* x, long long ldx, int E, int N, const QbTp& tp, const float* const* parts,
+cudaError_t qb_tp_reduce(float* x, long long ldx, int E, int N, const QbTp& tp, const void* const* parts,
                          unsigned* err, cudaStream_t st) {
-    if (tp.world < 2 || tp.world > QB_TP_MAX || E % 4 || ldx % 4 || N < 1 || N > QB_MAX_TOK || !tp.flags || !tp.seq)
+    if (tp.world < 2 || tp.world > QB_TP_MAX || E % 4 || ldx % 2 || N < 1 || N > QB_MAX_TOK || !tp.seq)
         return cudaErrorInvalidValue;
     TpR r = {};
     r.world = tp.world;
-    r.rank = tp.rank;
     for (int q = 0; q < tp.world; ++q) {
         if (!parts[q]) return cudaErrorInvalidValue;
-        r.part[q] = parts[q];
+        r.part[q] = reinterpret_cast<const uint2*>(parts[q]);
     }
     r.slot = tp.part_slot;
-    r.flags = tp.flags;
     r.seq = tp.seq;
     r.err = err;
-    const int n = N * (E / 4);
+    const int n = N * (E / 2);
     return qb_launch(tp_reduce_kernel, dim3((n + 255) / 256), dim3(256), 0, st, x, ldx, E, N, r);
 }
 
