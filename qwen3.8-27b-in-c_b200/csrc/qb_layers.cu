@@ -183,6 +183,21 @@ __global__ void __launch_bounds__(128) gdn_recur_kernel(
     const int h = blockIdx.x, kh = h % n_k;
     const int tid = threadIdx.x, lane = tid & 31, l8 = lane & 7;
     const int grp = tid >> 3;   // 16 groups of 8 lanes
+    // this group's state row and its tokens' v values: loads issued first, so that
+    // their latency overlaps the q / k norms below
+    const int row = blockIdx.y * 16 + grp;
+    const int cur = (int)*cur_slot;
+    const size_t head_off = (size_t)h * kDK * kDK + (size_t)row * kDK;
+    float S[16];
+    {
+        const float* src = slots + (size_t)cur * slot_stride + head_off;
+#pragma unroll
+        for (int m = 0; m < 16; ++m) S[m] = src[l8 + 8 * m];
+    }
+    float vrow[QB_MAX_TOK];
+#pragma unroll
+    for (int b = 0; b < QB_MAX_TOK; ++b)
+        vrow[b] = b < B ? qkvc[(size_t)b * ld_qkvc + (size_t)2 * n_k * kDK + (size_t)h * kDK + row] : 0.f;
 
     // L2 norms: group (b, which) for b < B, which in {q, k}.  Every lane of a
     // warp runs the shuffles; inactive groups work on zeros and store nothing.
@@ -224,17 +239,10 @@ __global__ void __launch_bounds__(128) gdn_recur_kernel(
     }
     __syncthreads();
 
-    const int row = blockIdx.y * 16 + (tid >> 3);
-    const int cur = (int)*cur_slot;
-    const size_t head_off = (size_t)h * kDK * kDK + (size_t)row * kDK;
-    float S[16];
-    {
-        const float* src = slots + (size_t)cur * slot_stride + head_off;
-#pragma unroll
-        for (int m = 0; m < 16; ++m) S[m] = src[l8 + 8 * m];
-    }
     const float q_scale = __fdiv_rn(1.0f, sqrtf((float)kDK));
-    for (int b = 0; b < B; ++b) {
+#pragma unroll
+    for (int b = 0; b < QB_MAX_TOK; ++b) {
+        if (b >= B) break;
         float ak = 0.f, aq = 0.f;
 #pragma unroll
         for (int m = 0; m < 16; ++m) {
@@ -243,7 +251,7 @@ __global__ void __launch_bounds__(128) gdn_recur_kernel(
         }
         const float sk = hsum8(ak), sq = hsum8(aq);
         const float decay = decay_s[b];
-        const float v = qkvc[(size_t)b * ld_qkvc + (size_t)2 * n_k * kDK + (size_t)h * kDK + row];
+        const float v = vrow[b];
         const float delta = __fmul_rn(decay, sk);
         const float dj = __fmul_rn(__fsub_rn(v, delta), beta_s[b]);
         const float o = __fmul_rn(__fadd_rn(__fmul_rn(decay, sq), __fmul_rn(dj, kq_s[b])), q_scale);
