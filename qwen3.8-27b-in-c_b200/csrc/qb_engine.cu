@@ -325,6 +325,7 @@ struct Engine {
     int k0 = 0, h0 = 0, kv0 = 0, f0 = 0;
     uint2* part = nullptr;                // [2][QB_MAX_TOK][E] (value, tag) partial sums of the residual GEMVs (arena)
     const void* peer_part[QB_TP_MAX] = {};    // rank r's part buffer, mapped here
+    QbArgX ax{};                          // argmax exchange of the heads inside the decode graphs
     bool use_tc = false;                  // IQ4_XS at N <= 4 on tcgen05 (QB_TC=1); default: int8 mma.sync
     float* attn_po = nullptr;             // attention chunk partials (qb_attn_decode)
     float2* gates = nullptr;              // DeltaNet (beta, decay) per (token, v-head)
@@ -752,8 +753,8 @@ int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
             off[i] = total;
             total += (sz[i] * 4 + 255) / 256 * 256;
         }
-        const size_t flags_off = total;
-        total += 256;
+        const size_t flags_off = total;   // TP barrier flags, then the argmax exchange words
+        total += 256 + 2 * QB_TP_MAX * QB_MAX_TOK * 16;
         const size_t part_off = total;   // tensor parallelism: 2 slots of partial sums
         total += 2 * (size_t)T8 * e.E * 8;
         e.arena = (char*)e.dalloc(total);
@@ -762,6 +763,7 @@ int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
         CK(cudaMemset(e.arena, 0, total));
         for (int i = 0; i < 12; ++i) *dst[i] = (float*)(e.arena + off[i]);
         e.tp.flags = (unsigned*)(e.arena + flags_off);
+        e.ax.xk = (unsigned long long*)(e.arena + flags_off + 256);
         e.part = (uint2*)(e.arena + part_off);
         e.tp.part = e.part;
         e.tp.part_slot = (long long)T8 * e.E;
@@ -867,6 +869,7 @@ int gemv_group(Engine& e, const DevMat* const* mats, float* const* outs, const l
             CK(qb_qmv_ex(type, segs, ns, K, N, e.xb, tp.gather ? accumulate : 0, nullptr, nullptr, &tp, e.work, e.st));
             continue;
         }
+        if (ns == 0) continue;   // tensor parallelism: no rows of this launch on this rank
         if (type == QB_F32) {
             for (int s = 0; s < ns; ++s) CK(cudaErrorNotSupported);
         } else if (type == QB_IQ4_XS && N <= 4 && e.use_tc) {
@@ -1027,9 +1030,33 @@ int gdn_block(Engine& e, const LayerW& l, int B, int ckpt, const NextIn& next) {
 
 __global__ void set_u32_kernel(uint32_t* p, uint32_t v) { *p = v; }
 
+// Output head on the prepared input e.xb: logits -> out[b], argmax -> am[b]
+// (the greedy pick of src/model.c:746-756 over the full row).  Under tensor
+// parallelism every rank computes its vocabulary rows; with local_rows they stay
+// on their rank and the ranks exchange their row maxima instead (the decode
+// graphs, which only need the index), otherwise each rank stores its rows into
+// every rank's logits.
+int head(Engine& e, float* out, int B, unsigned long long* keys, uint32_t* am, bool local_rows) {
+    const DevMat* m1[1] = {&e.output};
+    float* o1[1] = {out};
+    const long long ld1[1] = {e.V};
+    const bool xchg = e.tp_world > 1 && local_rows;
+    if (gemv_group(e, m1, o1, ld1, 1, e.E, B, 0, nullptr, xchg ? TP_LOCAL : TP_GATHER)) return -1;
+    CK(qb_argmax_reset(keys, B, e.st));
+    if (xchg) {
+        CK(qb_argmax(out + e.output.row0, e.V, e.output.rows, B, keys, e.st, e.output.row0));
+        CK(qb_tp_argmax(keys, B, am, e.ax, e.st));
+    } else {
+        CK(qb_argmax(out, e.V, e.V, B, keys, e.st));
+        CK(qb_argmax_to_u32(keys, B, am, e.st));
+    }
+    return 0;
+}
+
 // model_forward_batch on the device: tokens ctrl->fwd_tok[0..B), positions
-// ctrl->fwd_pos + b.  Logits -> e.logits[b], argmax -> ctrl->argmax[b].
-int fwd_backbone(Engine& e, int B, int ckpt) {
+// ctrl->fwd_pos + b.  Logits -> e.logits[b] (this rank's vocabulary rows only
+// with local_rows under tensor parallelism), argmax -> ctrl->argmax[b].
+int fwd_backbone(Engine& e, int B, int ckpt, bool local_rows = false) {
     CK(qb_embed(e.embd_type, e.tok_embd, e.E, e.ctrl->fwd_tok, B, e.bx, e.E, e.st));
     fresh_input(e);
     for (size_t il = 0; il < e.L.size(); ++il) {
@@ -1046,13 +1073,7 @@ int fwd_backbone(Engine& e, int B, int ckpt) {
     }
     CK(cudaMemcpyAsync(e.h_save, e.bx, (size_t)B * e.E * 4, cudaMemcpyDeviceToDevice, e.st));
     if (norm_input(e, e.bx, e.out_norm, B, xp_needs(e, {&e.output}, B))) return -1;
-    const DevMat* m1[1] = {&e.output};
-    float* o1[1] = {e.logits};
-    const long long ld1[1] = {e.V};
-    if (gemv_group(e, m1, o1, ld1, 1, e.E, B, 0, nullptr, TP_GATHER)) return -1;
-    CK(qb_argmax_reset(e.keys, B, e.st));
-    CK(qb_argmax(e.logits, e.V, e.V, B, e.keys, e.st));
-    CK(qb_argmax_to_u32(e.keys, B, e.ctrl->argmax, e.st));
+    if (head(e, e.logits, B, e.keys, e.ctrl->argmax, local_rows)) return -1;
     if (ckpt) set_u32_kernel<<<1, 1, 0, e.st>>>(&e.ctrl->cur_slot, (uint32_t)std::min(B - 1, kNSlot - 1));
     CK(cudaGetLastError());
     return 0;
@@ -1061,7 +1082,7 @@ int fwd_backbone(Engine& e, int B, int ckpt) {
 // mtp_forward(_batch) on the device: tokens ctrl->mtp_tok[0..B), positions
 // ctrl->mtp_pos + b, hidden input = hsrc rows (mtp_h for the single-token
 // chain, h_save for the batch fill).  mtp_h <- output of the last token.
-int fwd_mtp(Engine& e, int B, const float* hsrc, int want_logits) {
+int fwd_mtp(Engine& e, int B, const float* hsrc, int want_logits, bool local_rows = false) {
     CK(qb_embed(e.embd_type, e.tok_embd, e.E, e.ctrl->mtp_tok, B, e.emb, e.E, e.st));
     QbXIn in[2] = {{e.emb, e.E, e.enorm, e.E}, {hsrc, e.E, e.hnorm, e.E}};
     fresh_input(e);
@@ -1075,13 +1096,7 @@ int fwd_mtp(Engine& e, int B, const float* hsrc, int want_logits) {
     CK(cudaMemcpyAsync(e.mtp_h, e.mtp_x + (size_t)(B - 1) * e.E, (size_t)e.E * 4, cudaMemcpyDeviceToDevice, e.st));
     if (want_logits) {
         if (norm_input(e, e.mtp_x, e.shnorm, B, xp_needs(e, {&e.output}, B))) return -1;
-        const DevMat* mo[1] = {&e.output};
-        float* oo[1] = {e.mtp_logits};
-        const long long ldo[1] = {e.V};
-        if (gemv_group(e, mo, oo, ldo, 1, e.E, B, 0, nullptr, TP_GATHER)) return -1;
-        CK(qb_argmax_reset(e.keys + QB_MAX_TOK, B, e.st));
-        CK(qb_argmax(e.mtp_logits, e.V, e.V, B, e.keys + QB_MAX_TOK, e.st));
-        CK(qb_argmax_to_u32(e.keys + QB_MAX_TOK, B, e.ctrl->mtp_argmax, e.st));
+        if (head(e, e.mtp_logits, B, e.keys + QB_MAX_TOK, e.ctrl->mtp_argmax, local_rows)) return -1;
     }
     return 0;
 }
@@ -1149,11 +1164,11 @@ __global__ void greedy_step_kernel(QbCtrl* c, uint32_t* out_tok) {
 int record_cycle(Engine& e, int k) {
     spec_start_kernel<<<1, 1, 0, e.st>>>(e.ctrl);
     for (int s = 1; s <= k; ++s) {
-        if (fwd_mtp(e, 1, e.mtp_h, 1)) return -1;
+        if (fwd_mtp(e, 1, e.mtp_h, 1, true)) return -1;
         spec_draft_kernel<<<1, 1, 0, e.st>>>(e.ctrl, s);
     }
     spec_verify_setup_kernel<<<1, 1, 0, e.st>>>(e.ctrl, k);
-    if (fwd_backbone(e, k + 1, 1)) return -1;
+    if (fwd_backbone(e, k + 1, 1, true)) return -1;
     spec_accept_kernel<<<1, 256, 0, e.st>>>(e.ctrl, k, e.d_forced, e.d_out_tok, e.d_out_j, e.h_save, e.mtp_h, e.E);
     if (fwd_mtp(e, 1, e.mtp_h, 0)) return -1;
     CK(cudaGetLastError());
@@ -1189,9 +1204,31 @@ int capture(Engine& e, cudaGraphExec_t* out, int (*rec)(Engine&, int), int arg) 
 }
 
 int record_greedy(Engine& e, int) {
-    if (fwd_backbone(e, 1, 0)) return -1;
+    if (fwd_backbone(e, 1, 0, true)) return -1;
     greedy_step_kernel<<<1, 1, 0, e.st>>>(e.ctrl, e.d_out_tok);
     CK(cudaGetLastError());
+    return 0;
+}
+
+// Decode graphs under tensor parallelism leave in each row of e.logits only this
+// rank's vocabulary rows: fetch the others of row `row` from the peers' copies.
+// Every rank calls this at the same point.  The barrier before the loads orders
+// them after every peer's last head GEMV; the one after keeps each peer's
+// logits unchanged until all ranks have read them.
+int tp_fill_logits_row(Engine& e, int row) {
+    if (e.tp_world < 2) return 0;
+    QbTp bar = e.tp;
+    bar.gather = 1;
+    CK(qb_qmv_ex(e.output.type, nullptr, 0, e.E, 1, e.xb, 0, nullptr, nullptr, &bar, e.work, e.st));
+    float* dst = e.logits + (size_t)row * e.V;
+    const float* src[QB_TP_MAX] = {};
+    int r0[QB_TP_MAX] = {}, r1[QB_TP_MAX] = {};
+    for (int r = 0; r < e.tp_world; ++r) {
+        if (r != e.tp_rank) src[r] = (const float*)((char*)e.peer_arena[r] + ((char*)dst - e.arena));
+        qb_tp_rows(e.V, r, e.tp_world, &r0[r], &r1[r]);
+    }
+    CK(qb_tp_pull_rows(dst, src, r0, r1, e.tp_world, e.tp_rank, e.st));
+    CK(qb_qmv_ex(e.output.type, nullptr, 0, e.E, 1, e.xb, 0, nullptr, nullptr, &bar, e.work, e.st));
     return 0;
 }
 
@@ -1319,9 +1356,15 @@ extern "C" int qb_tp_connect(qwen_model_t* m, const void* handles, int64_t strid
         e->peer_part[r] = (const void*)((char*)p + ((char*)e->part - e->arena));
     }
     e->peer_part[e->tp_rank] = e->part;
+    e->ax.rank = e->tp_rank;
+    e->ax.world = e->tp_world;
+    for (int r = 0; r < e->tp_world; ++r)
+        e->ax.delta[r] = r == e->tp_rank ? 0 : (long long)((char*)e->peer_arena[r] - e->arena);
+    e->ax.err = e->work.err;
     e->tp.done = (unsigned*)e->dalloc(256);
     if (!e->tp.done) { set_err(-2, "tp counters"); return -1; }
     e->tp.seq = e->tp.done + 32;
+    e->ax.xseq = e->tp.done + 48;
     if (cudaMemset(e->tp.done, 0, 256) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
         set_err(-2, "tp counters");
         return -1;
@@ -1529,6 +1572,7 @@ extern "C" int qb_spec_generate(qwen_model_t* m, uint32_t n_predict, uint32_t n_
     CK(cudaMemcpyAsync(&hc, e->ctrl, sizeof hc, cudaMemcpyDeviceToHost, e->st));
     if (dev_sync(*e)) return -1;
     m->pos = hc.P + 1;
+    if (tp_fill_logits_row(*e, (int)hc.j)) return -1;
     CK(cudaMemcpyAsync(m->logits, e->logits + (size_t)hc.j * e->V, (size_t)e->V * 4, cudaMemcpyDeviceToHost, e->st));
     CK(cudaMemcpyAsync(m->mtp_h, e->mtp_h, (size_t)e->E * 4, cudaMemcpyDeviceToHost, e->st));
     if (dev_sync(*e)) return -1;
@@ -1562,6 +1606,7 @@ extern "C" int qb_greedy_generate(qwen_model_t* m, uint32_t n_predict, uint32_t*
     const uint32_t n = steps + 1;
     CK(cudaMemcpyAsync(out_tokens, e->d_out_tok, (size_t)n * 4, cudaMemcpyDeviceToHost, e->st));
     m->pos += steps;
+    if (steps && tp_fill_logits_row(*e, 0)) return -1;
     CK(cudaMemcpyAsync(m->logits, e->logits, (size_t)e->V * 4, cudaMemcpyDeviceToHost, e->st));
     // keep next_cand0 = argmax of the last forward for a following call
     CK(cudaMemcpyAsync(&e->ctrl->next_cand0, &e->ctrl->argmax[0], 4, cudaMemcpyDeviceToDevice, e->st));

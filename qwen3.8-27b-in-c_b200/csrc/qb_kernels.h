@@ -171,9 +171,26 @@ cudaError_t qb_gdn_out_xprep(const float* o, const float* z, long long ld, const
 cudaError_t qb_silu_mul(const float* gate, const float* up, long long ld, int n, int B, float* out,
                         cudaStream_t st);
 cudaError_t qb_argmax_reset(unsigned long long* keys, int B, cudaStream_t st);
+// keys[b] = max(keys[b], max over i < n of (x[b * ldx + i], index i0 + i)), first index on ties
 cudaError_t qb_argmax(const float* x, long long ldx, int n, int B, unsigned long long* keys,
-                      cudaStream_t st);
+                      cudaStream_t st, int i0 = 0);
 cudaError_t qb_argmax_to_u32(const unsigned long long* keys, int B, uint32_t* out, cudaStream_t st);
+
+// Tensor-parallel argmax over a vocabulary split by rows: every rank holds the
+// keys of its own rows (qb_argmax with i0 = its first row); qb_tp_argmax stores
+// them into every rank's exchange array, waits (bounded) for all ranks' keys of
+// the same exchange and writes the index of the largest to out[b] on every rank.
+struct QbArgX {
+    int rank, world;
+    unsigned long long* xk;         // this rank's array [2][QB_TP_MAX][QB_MAX_TOK][2] words (shared arena)
+    long long delta[QB_TP_MAX];     // rank r's array address - ours (0 for this rank)
+    unsigned* xseq;                 // zero-initialised; counts this rank's exchanges
+    unsigned* err;                  // set to 4 when a wait ran out
+};
+cudaError_t qb_tp_argmax(const unsigned long long* keys, int B, uint32_t* out, const QbArgX& x, cudaStream_t st);
+// dst[i] = src[r][i] for i in [r0[r], r1[r]) and every rank r != rank (NVLink loads)
+cudaError_t qb_tp_pull_rows(float* dst, const float* const* src, const int* r0, const int* r1, int world, int rank,
+                            cudaStream_t st);
 
 // element-wise ops behind the kernels.h host-pointer API
 cudaError_t qb_op_rmsnorm(float* out, const float* x, const float* w, long long n, float eps,

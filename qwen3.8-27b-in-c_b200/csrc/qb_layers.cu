@@ -636,14 +636,14 @@ __global__ void argmax_reset_kernel(unsigned long long* keys, int B) {
 }
 
 __global__ void argmax_kernel(const float* __restrict__ x, long long ldx, int n,
-                              unsigned long long* __restrict__ keys) {
+                              unsigned long long* __restrict__ keys, int i0) {
     pdl_wait();
     pdl_trigger();
     const int b = blockIdx.y;
     const float* xr = x + (size_t)b * ldx;
     unsigned long long best = 0ull;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-        const unsigned long long k = argmax_key(xr[i], (uint32_t)i);
+        const unsigned long long k = argmax_key(xr[i], (uint32_t)(i0 + i));
         best = k > best ? k : best;
     }
 #pragma unroll
@@ -658,6 +658,69 @@ __global__ void argmax_to_u32_kernel(const unsigned long long* keys, int B, uint
     pdl_wait();
     pdl_trigger();
     if (threadIdx.x < B) out[threadIdx.x] = 0xFFFFFFFFu - (uint32_t)(keys[threadIdx.x] & 0xFFFFFFFFull);
+}
+
+// Tensor-parallel argmax exchange, one thread per row b.  Exchange s (this
+// rank's count + 1) stores the row's key into slot s & 1 of every rank's array
+// as two 64-bit words (key half << 32 | s), each stored and loaded whole, so a
+// word counts once its low half is s.  A rank starts exchange s + 2, which
+// reuses the slot, only after every rank's words of exchange s + 1 arrived,
+// which each rank stores only after its exchange s is over.
+__global__ void tp_argmax_kernel(const unsigned long long* __restrict__ keys, int B, uint32_t* out, QbArgX x) {
+    pdl_wait();
+    pdl_trigger();
+    const int b = threadIdx.x;
+    const unsigned s = *(volatile const unsigned*)x.xseq + 1u;
+    __syncthreads();   // every thread has read the count before thread 0 advances it
+    if (b < B) {
+        const unsigned long long k = keys[b];
+        const unsigned long long w0 = (k & 0xFFFFFFFF00000000ull) | s, w1 = (k << 32) | s;
+        const size_t at = ((size_t)(s & 1u) * QB_TP_MAX + x.rank) * QB_MAX_TOK + b;
+        for (int r = 0; r < x.world; ++r) {
+            unsigned long long* d = reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(x.xk + 2 * at) +
+                                                                          x.delta[r]);
+            asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(d), "l"(w0), "l"(w1) : "memory");
+        }
+        unsigned long long best = 0ull;
+        bool ok = true;
+        for (int r = 0; r < x.world && ok; ++r) {
+            const unsigned long long* src = x.xk + 2 * (((size_t)(s & 1u) * QB_TP_MAX + r) * QB_MAX_TOK + b);
+            unsigned long long v0, v1;
+            for (uint32_t it = 0;; ++it) {
+                asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v0) : "l"(src) : "memory");
+                asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v1) : "l"(src + 1) : "memory");
+                if ((unsigned)v0 == s && (unsigned)v1 == s) break;
+                if (it >= (1u << 24)) {
+                    atomicExch(x.err, 4u);
+                    ok = false;
+                    break;
+                }
+                __nanosleep(64);
+            }
+            const unsigned long long kr = (v0 & 0xFFFFFFFF00000000ull) | (v1 >> 32);
+            best = kr > best ? kr : best;
+        }
+        if (ok) out[b] = 0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull);
+    }
+    __syncthreads();
+    if (b == 0) *(volatile unsigned*)x.xseq = s;
+}
+
+struct QbPull {
+    int world, rank;
+    const float* src[QB_TP_MAX];
+    int r0[QB_TP_MAX], r1[QB_TP_MAX];
+};
+// rows [r0[r], r1[r]) of every other rank's copy, by loads over NVLink
+__global__ void tp_pull_rows_kernel(float* __restrict__ dst, QbPull p) {
+    pdl_wait();
+    pdl_trigger();
+    for (int r = 0; r < p.world; ++r) {
+        if (r == p.rank) continue;
+        const float* src = p.src[r];
+        for (int i = p.r0[r] + blockIdx.x * blockDim.x + threadIdx.x; i < p.r1[r]; i += gridDim.x * blockDim.x)
+            dst[i] = src[i];
+    }
 }
 
 // --------------------- kernels.h element-wise ops -----------------------------
@@ -861,9 +924,35 @@ cudaError_t qb_argmax_reset(unsigned long long* keys, int B, cudaStream_t st) {
     return cudaGetLastError();
 }
 
-cudaError_t qb_argmax(const float* x, long long ldx, int n, int B, unsigned long long* keys, cudaStream_t st) {
+cudaError_t qb_argmax(const float* x, long long ldx, int n, int B, unsigned long long* keys, cudaStream_t st,
+                      int i0) {
     const int blocks = (n + 1023) / 1024 < 148 ? (n + 1023) / 1024 : 148;
-    qb_launch(argmax_kernel, dim3(blocks, B), dim3(256), 0, st, x, ldx, n, keys);
+    if (n < 1) return cudaSuccess;   // no rows here: the keys keep their reset value
+    qb_launch(argmax_kernel, dim3(blocks, B), dim3(256), 0, st, x, ldx, n, keys, i0);
+    return cudaGetLastError();
+}
+
+cudaError_t qb_tp_argmax(const unsigned long long* keys, int B, uint32_t* out, const QbArgX& x, cudaStream_t st) {
+    if (x.world < 2 || x.world > QB_TP_MAX || x.rank < 0 || x.rank >= x.world || B < 1 || B > QB_MAX_TOK ||
+        !x.xk || !x.xseq || !x.err || x.delta[x.rank] != 0)
+        return cudaErrorInvalidValue;
+    qb_launch(tp_argmax_kernel, dim3(1), dim3(32), 0, st, keys, B, out, x);
+    return cudaGetLastError();
+}
+
+cudaError_t qb_tp_pull_rows(float* dst, const float* const* src, const int* r0, const int* r1, int world, int rank,
+                            cudaStream_t st) {
+    if (world < 2 || world > QB_TP_MAX || rank < 0 || rank >= world) return cudaErrorInvalidValue;
+    QbPull p = {};
+    p.world = world;
+    p.rank = rank;
+    for (int r = 0; r < world; ++r) {
+        if (r != rank && (!src[r] || r0[r] > r1[r])) return cudaErrorInvalidValue;
+        p.src[r] = src[r];
+        p.r0[r] = r0[r];
+        p.r1[r] = r1[r];
+    }
+    qb_launch(tp_pull_rows_kernel, dim3(148), dim3(256), 0, st, dst, p);
     return cudaGetLastError();
 }
 

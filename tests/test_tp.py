@@ -5,8 +5,10 @@ Each rank keeps its share of the DeltaNet k-heads (with their v-heads),
 attention q-/kv-heads and FFN columns, so the mixers and the FFN run on
 local data; the out-projections and the down projection write partial sums
 that every rank adds up in rank order; the output head splits over the
-vocabulary, its rows stored into every rank's logits.  All ranks must hold
-the same logits and emit the same tokens as one GPU and as the reference.
+vocabulary: inside the decode loops each rank keeps its rows and the ranks
+exchange their row maxima, elsewhere (and for the logits a decode call leaves
+behind) every rank holds all rows.  All ranks must hold the same logits and
+emit the same tokens as one GPU and as the reference.
 """
 import os
 import socket
@@ -70,12 +72,15 @@ def close(m):
 from conftest import oracle
 
 def single(path, shape, n_ctx, p, forced, n, reference):
-    # logits after the prompt, tokens, accept lengths, final logits on one GPU (or the reference)
+    # logits after the prompt, tokens, accept lengths, logits after them, then
+    # greedy tokens and the logits after those, on one GPU (or the reference)
     s = oracle.RefModel(path, n_ctx, 8) if reference else qb.Model(path, n_ctx)
     s.prefill(p, 1)
     l0 = s.logits().copy()
     st, sj = s.spec_generate(n, 3, forced=forced)
-    out = (l0, np.asarray(st), np.asarray(sj), s.logits().copy())
+    l1 = s.logits().copy()
+    sg = np.asarray(s.greedy_generate(6))
+    out = (l0, np.asarray(st), np.asarray(sj), l1, sg, s.logits().copy())
     s.close()
     return out
 
@@ -91,12 +96,16 @@ for shape, name, seed, n_ctx, n, refs in ((qb.SMALL, "small", 3, 256, 40, (False
     l0 = m.logits().copy()
     tt, tj = m.spec_generate(n, 3, forced=forced)
     l1 = m.logits().copy()
+    tg = np.asarray(m.greedy_generate(6))
+    l2 = m.logits().copy()
     close(m)
-    for r, (s0, st, sj, s1) in zip(refs, obj[0]):
+    for r, (s0, st, sj, s1, sg, s2) in zip(refs, obj[0]):
         who = (name, "reference" if r else "one GPU", rank)
         assert rel(l0, s0) < 1e-4, (who, rel(l0, s0))
         assert np.array_equal(tt, st) and np.array_equal(tj, sj), (who, tt, st, tj, sj)
         assert rel(l1, s1) < 1e-4, (who, rel(l1, s1))
+        assert np.array_equal(tg, sg), (who, tg, sg)
+        assert rel(l2, s2) < 1e-4, (who, rel(l2, s2))
 dist.destroy_process_group()
 print("tp ok", rank)
 """
