@@ -39,6 +39,21 @@ __device__ __forceinline__ void iq4_i8(uint32_t w, uint32_t& lo, uint32_t& hi) {
     hi = prmt(prmt(kIq4I8T0, kIq4I8T1, idxh), prmt(kIq4I8T2, kIq4I8T3, idxh), selh);
 }
 
+// The same 8 codes as two int8 terms P + Q = the table value, with no select:
+// a byte-permute selector nibble with bit 3 set yields the selected byte's sign
+// replicated.  P looks up values 0..7 (all negative) with the code itself as
+// the selector: codes 8..15 give -1.  Q looks up values 8..15 plus 1 (all
+// positive) with code ^ 8: codes 0..7 give 0.  Two mma steps then sum P and Q.
+constexpr uint32_t kIq4QT2 = 0x271A0E02u;   //  2 14 26  39  (values 8..11, plus 1)
+constexpr uint32_t kIq4QT3 = 0x725A4636u;   // 54 70 90 114  (values 12..15, plus 1)
+__device__ __forceinline__ void iq4_pq(uint32_t w, uint32_t& plo, uint32_t& phi, uint32_t& qlo, uint32_t& qhi) {
+    const uint32_t x = w ^ 0x88888888u;
+    plo = prmt(kIq4I8T0, kIq4I8T1, w);
+    phi = prmt(kIq4I8T0, kIq4I8T1, w >> 16);
+    qlo = prmt(kIq4QT2, kIq4QT3, x);
+    qhi = prmt(kIq4QT2, kIq4QT3, x >> 16);
+}
+
 // byte i of w, sign-extended
 __device__ __forceinline__ int sbyte(uint32_t w, int i) {
     return (int)prmt(w, 0u, (uint32_t)(i | ((8 | i) << 4) | ((8 | i) << 8) | ((8 | i) << 12)));

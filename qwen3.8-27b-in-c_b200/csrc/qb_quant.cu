@@ -127,8 +127,8 @@ constexpr int kIq4Tile = kIq4D + 16 * 2;
 static_assert(kIq4Tile == qb_unit_bytes(QB_IQ4_XS) && kIq4Tile % 16 == 0, "IQ4_XS tile-block layout");
 
 // ---- IQ4_XS on the int8 tensor-core path (mma m16n8k32 s8 -> s32) ----
-// Codes become the int8 values of kvalues_iq4nl (src/quant.c:30-32) by two
-// 8-byte permute lookups and a select; the activations arrive as three
+// Codes become the int8 values of kvalues_iq4nl (src/quant.c:30-32) as the
+// sum of two byte-permute lookups (iq4_pq), each fed to its own mma; the activations arrive as three
 // balanced int8 digits per token (X = 65536 d0 + 256 d1 + d2, xprep), so
 // every sub-block dot product is exact in int32.  The same repacked tile
 // layout as above serves both paths: the word of (row, sub-block) holds qs
@@ -185,11 +185,14 @@ __device__ __forceinline__ void stage_iq4_i8(const uint8_t* u, const uint2* __re
 #pragma unroll
             for (int t = 0; t < 2; ++t) {
                 const uint4& q = t ? q1 : q0;
-                uint32_t a[4];
-                iq4_i8(h ? q.z : q.x, a[0], a[2]);   // row g
-                iq4_i8(h ? q.w : q.y, a[1], a[3]);   // row g + 8
+                uint32_t pa[4], qa[4];
+                iq4_pq(h ? q.z : q.x, pa[0], pa[2], qa[0], qa[2]);   // row g
+                iq4_pq(h ? q.w : q.y, pa[1], pa[3], qa[1], qa[3]);   // row g + 8
 #pragma unroll
-                for (int nt = 0; nt < NTI; ++nt) mma_16832_s8(R[t][nt], a, bq[nt].x, bq[nt].y);
+                for (int nt = 0; nt < NTI; ++nt) {
+                    mma_16832_s8(R[t][nt], pa, bq[nt].x, bq[nt].y);
+                    mma_16832_s8(R[t][nt], qa, bq[nt].x, bq[nt].y);
+                }
                 const uint8_t* dl = u + t * kIq4Tile + kIq4Dl + g * 8 + sb;
                 const int s_g = lds_s8(dl), s_g8 = lds_s8(dl + 64);
 #pragma unroll
