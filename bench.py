@@ -336,7 +336,10 @@ def run_components(args):
     out = {}
     for name, what, arg, iters in [("ffn_gate_up_n4", 1, 4, args.iters), ("ffn_gate_up_n1", 1, 1, args.iters),
                                    ("head_n4", 3, 4, args.iters), ("head_n1", 3, 1, args.iters),
-                                   ("draft", 2, 1, args.iters), ("verify_b4", 0, 4, args.iters)]:
+                                   ("draft", 2, 1, args.iters), ("verify_b4", 0, 4, args.iters),
+                                   # these run on stale activations (timing only): after the others
+                                   ("ffn_down_n4", 5, 4, args.iters), ("out_proj_n4", 6, 4, args.iters),
+                                   ("in_proj_n4", 7, 4, args.iters)]:
         if args.only and name not in args.only.split(","):
             continue
         ms, b = model.bench(what, arg, iters)

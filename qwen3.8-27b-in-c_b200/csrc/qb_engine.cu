@@ -1667,7 +1667,9 @@ int record_draft(Engine& e, int) { return fwd_mtp(e, 1, e.mtp_h, 1); }
 // Device timing of one component, averaged over `iters` runs, CUDA events on
 // the engine stream.  what: 0 verify forward of `arg` tokens (64 layers +
 // head, graph replay), 1 fused FFN gate+up GEMV with N = arg rotating over
-// all layers, 2 one MTP draft with logits, 3 output-head GEMV with N = arg.
+// all layers, 2 one MTP draft with logits, 3 output-head GEMV with N = arg,
+// 5 / 6 / 7 the FFN down / mixer out-projection / mixer in-projection GEMV
+// with N = arg rotating over all layers, as the forward launches them.
 // *bytes = algorithmic bytes of one run (GGUF weight bytes + activations and
 // states read/written once).  Mutates KV / recurrent state: call last.
 extern "C" float qb_bench(qwen_model_t* m, int what, uint32_t arg, uint32_t iters, double* bytes) {
@@ -1705,15 +1707,38 @@ extern "C" float qb_bench(qwen_model_t* m, int what, uint32_t arg, uint32_t iter
             b = mat_bytes(e->eh_proj) + mat_bytes(l.q) + mat_bytes(l.k) + mat_bytes(l.v) + mat_bytes(l.o) +
                 mat_bytes(l.ffn_gate) + mat_bytes(l.ffn_up) + mat_bytes(l.ffn_down) + mat_bytes(e->output);
         }
-    } else if (what == 1 || what == 3) {
+    } else if (what == 1 || what == 3 || (what >= 5 && what <= 7)) {
         if (arg < 1 || arg > QB_MAX_TOK) return -1.f;
-        // one graph of the launches (all layers for what 1), replayed: no host launch gaps
-        const int nl = what == 1 ? (int)e->L.size() : 1;
+        // one graph of the launches (all layers except for the head), replayed: no host launch gaps
+        const int nl = what != 3 ? (int)e->L.size() : 1;
         struct Rec {
             static int go(Engine& en, int packed) {
                 const int wh = packed & 0xFF, a = (packed >> 8) & 0xFF, nlay = packed >> 16;
                 for (int li = 0; li < nlay; ++li) {
-                    if (wh == 1) {
+                    const LayerW& ly = en.L[li];
+                    if (wh == 5) {
+                        fresh_input(en);
+                        if (residual_gemv(en, &ly.ffn_down, en.bx, en.F_loc, a, nullptr)) return -1;
+                    } else if (wh == 6) {
+                        fresh_input(en);
+                        const int K = ly.rec ? en.nv_loc * (int)en.d.head_v_dim : en.nh_loc * (int)en.d.head_dim;
+                        if (residual_gemv(en, ly.rec ? &ly.ssm_out : &ly.o, en.bx, K, a, nullptr)) return -1;
+                    } else if (wh == 7) {
+                        fresh_input(en);
+                        if (ly.rec) {
+                            const DevMat* m4[4] = {&ly.wqkv, &ly.wgate, &ly.wbeta, &ly.walpha};
+                            float* o4[4] = {en.qkv, en.z, en.beta, en.alpha};
+                            const long long ld4[4] = {en.ld_qkv, (long long)en.d.d_inner, 256, 256};
+                            if (gemv_group(en, m4, o4, ld4, 4, en.E, a, 0)) return -1;
+                        } else {
+                            const DevMat* m3[3] = {&ly.q, &ly.k, &ly.v};
+                            float* o3[3] = {en.qbuf, en.kvbuf, en.kvbuf + ly.k.rows_all};
+                            const long long ld3[3] = {2LL * en.d.n_head * en.d.head_dim,
+                                                      2LL * en.d.n_kv_head * en.d.head_dim,
+                                                      2LL * en.d.n_kv_head * en.d.head_dim};
+                            if (gemv_group(en, m3, o3, ld3, 3, en.E, a, 0)) return -1;
+                        }
+                    } else if (wh == 1) {
                         // the FFN gate / up launch as the forward runs it
                         const LayerW& l = en.L[li];
                         if (l.gu.w) {
@@ -1749,8 +1774,18 @@ extern "C" float qb_bench(qwen_model_t* m, int what, uint32_t arg, uint32_t iter
         cudaGraphExecDestroy(ge);
         iters *= (uint32_t)nl;
         const LayerW& l0 = e->L[0];
-        b = what == 1 ? (double)(mat_bytes(l0.ffn_gate) + mat_bytes(l0.ffn_up)) : (double)mat_bytes(e->output);
-        b += (double)arg * e->E * 4 + (double)arg * (what == 1 ? 2.0 * e->F : e->V) * 4;
+        if (what == 1 || what == 3) {
+            b = what == 1 ? (double)(mat_bytes(l0.ffn_gate) + mat_bytes(l0.ffn_up)) : (double)mat_bytes(e->output);
+            b += (double)arg * e->E * 4 + (double)arg * (what == 1 ? 2.0 * e->F : e->V) * 4;
+        } else {
+            for (const LayerW& l : e->L) {   // the average launch over the layers
+                if (what == 5) b += mat_bytes(l.ffn_down);
+                else if (what == 6) b += mat_bytes(l.rec ? l.ssm_out : l.o);
+                else if (l.rec) b += mat_bytes(l.wqkv) + mat_bytes(l.wgate) + mat_bytes(l.wbeta) + mat_bytes(l.walpha);
+                else b += mat_bytes(l.q) + mat_bytes(l.k) + mat_bytes(l.v);
+            }
+            b /= (double)nl;
+        }
     } else if (what == 4) {
         // kernels launched per speculative cycle (nodes of the captured cycle graph)
         if (bytes) *bytes = 0;

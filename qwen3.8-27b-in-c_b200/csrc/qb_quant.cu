@@ -817,7 +817,6 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_kernel(QmvK p) {
         mbar_fence_init();
     }
     __syncwarp();
-    pdl_trigger();
 
     // per-CTA arrival counters of the pairs its warps share (level 1 of the split-pair combine)
     __shared__ unsigned s_lcnt[kLocalPairs];
@@ -869,6 +868,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_kernel(QmvK p) {
     if (lane == 0)
         for (int r = 0; r < R && r < n; ++r) issue(r);
     pdl_wait();   // activations written by the previous kernel are complete from here on
+    // let the next launch start only now: triggered at entry, a chain of GEMVs had CTAs of
+    // the next two launches resident and idle in their wait, crowding this one onto fewer SMs
+    pdl_trigger();
     // the deferred norm's per-block sums: copied now, read at the first pair finish
     if (EPI && p.in_ss && p.N * p.nb <= kSsMax)
         for (int i = lane; i < p.N * p.nb; i += 32) cp_async4(&s_ss[warp][i], p.in_ss + i);
