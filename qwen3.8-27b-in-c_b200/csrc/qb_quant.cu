@@ -96,6 +96,13 @@ __device__ __forceinline__ void mma_nt(float (&cs)[NT][4], const uint32_t (&a)[4
     for (int ct = 0; ct < NT; ++ct) mma_16816(cs[ct], a, b[ct].x, b[ct].y);
 }
 
+// the same with a zero accumulator input
+template <int NT>
+__device__ __forceinline__ void mma_nt_z(float (&cs)[NT][4], const uint32_t (&a)[4], const uint2 (&b)[NT]) {
+#pragma unroll
+    for (int ct = 0; ct < NT; ++ct) mma_16816_z(cs[ct], a, b[ct].x, b[ct].y);
+}
+
 template <int NT>
 __device__ __forceinline__ void scale_acc(float (&ab)[NT][4], const float (&cs)[NT][4], float dg, float dg8) {
 #pragma unroll
@@ -352,7 +359,7 @@ __device__ __forceinline__ void stage_qk(const uint8_t* u, const uint2* __restri
 // Q6_K tile-block: lo plane 2048 B (chunk qc: word i = group 4qc+i, nibbles
 // 0..3 = row g elements 4c..4c+3, 4..7 = row g8), hi plane 1024 B (word per
 // group pair: byte j bits 4-5/6-7 = even/odd member of the first group, 0-1/
-// 2-3 of the second), scales 16 rows x 16 int8, d 16 x fp16.
+// 2-3 of the second), scales 16 rows x 16 bytes (int8 scale + 128), d 16 x fp16.
 constexpr int kQ6Tile = 16 * 210;
 template <int NT>
 __device__ __forceinline__ void stage_q6k(const uint8_t* u, const uint2* __restrict__ xf, int lane,
@@ -393,14 +400,14 @@ __device__ __forceinline__ void stage_q6k(const uint8_t* u, const uint2* __restr
                     a[1] = hsub2_u32(prmt(p23, C64, 0x5140u), H1056x2);
                     a[3] = hsub2_u32(prmt(p23, C64, 0x7362u), H1056x2);
                     float cs[NT][4];
-                    zero<NT>(cs);
                     uint2 b[NT];
                     load_b<NT>(b, xf + G * NT * 32, lane);
-                    mma_nt<NT>(cs, a, b);
-                    const int scg = (int)(int8_t)(scw_g[G >> 2] >> (8 * (G & 3)));
-                    const int scg8 = (int)(int8_t)(scw_g8[G >> 2] >> (8 * (G & 3)));
-                    scale_acc<NT>(ab[t], cs, dg * (small_u2f((uint32_t)(scg + 128)) - 128.f),
-                                  dg8 * (small_u2f((uint32_t)(scg8 + 128)) - 128.f));
+                    mma_nt_z<NT>(cs, a, b);
+                    // the scale byte u = sc + 128 as the float 2^23 + u, minus 2^23 + 128: sc, exactly
+                    const uint32_t sel = 0x7650u | (uint32_t)(G & 3);
+                    const float scg = __uint_as_float(prmt(scw_g[G >> 2], 0x4B000000u, sel)) - 8388736.0f;
+                    const float scg8 = __uint_as_float(prmt(scw_g8[G >> 2], 0x4B000000u, sel)) - 8388736.0f;
+                    scale_acc<NT>(ab[t], cs, dg * scg, dg8 * scg8);
                 }
             }
         }
@@ -1185,7 +1192,8 @@ __global__ void repack_kernel(int type, const uint8_t* __restrict__ src, size_t 
         }
         if (lane < 16) {
             const uint8_t* rp = rowp(lane);
-            for (int i = 0; i < 4; ++i) d32[(3072 + lane * 16) / 4 + i] = w32(rp, 192 + 4 * i);
+            // int8 scales stored as sc + 128 (unsigned): one byte permute makes the float 2^23 + sc + 128
+            for (int i = 0; i < 4; ++i) d32[(3072 + lane * 16) / 4 + i] = w32(rp, 192 + 4 * i) ^ 0x80808080u;
             reinterpret_cast<uint16_t*>(d + 3328)[lane] = rp ? (uint16_t)(rp[208] | (rp[209] << 8)) : 0;
         }
     }
