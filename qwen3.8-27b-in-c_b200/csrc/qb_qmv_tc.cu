@@ -98,12 +98,11 @@ __device__ void finish_row(const TcK& p, int T, int cta, int s0, int s1, int m, 
     const int piece = s0 > P0 ? 0 : 1;   // 0: the tile is this CTA's first (it started inside it)
     *reinterpret_cast<float4*>(p.partial + (((size_t)cta * 2 + piece) * kRows + m) * 4) =
         make_float4(tot[0], tot[1], tot[2], tot[3]);
-    __threadfence();
     const int c_first = stage_cta(p.S, p.G, P0), c_last = stage_cta(p.S, p.G, P1 - 1);
     unsigned* ctr = p.counters + (size_t)T * kRows + m;
-    const unsigned old = atomicAdd(ctr, 1u);
+    // release orders this thread's partial before the count, acquire the others' after it
+    const unsigned old = atom_add_acq_rel_gpu(ctr, 1u);
     if ((int)old != c_last - c_first) return;
-    __threadfence();
     float sum[4] = {0.f, 0.f, 0.f, 0.f};
     for (int c = c_first; c <= c_last; ++c) {
         const int pc = cta_s0(p.S, p.G, c) > P0 ? 0 : 1;

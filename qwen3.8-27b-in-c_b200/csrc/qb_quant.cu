@@ -709,13 +709,13 @@ __device__ __forceinline__ void finish_pair(const QmvK& p, int pair, int gw, int
         for (int t = 0; t < 2; ++t)
 #pragma unroll
             for (int i = 0; i < 4; ++i) gslot[pidx(t, i)] = v[t][i];
-    __threadfence();
+    // the warp barrier orders every lane's stores before lane 0's release (cumulative), and
+    // the last arrival's acquire before every lane's loads: no full fences on this path
     __syncwarp();
     unsigned old = 0;
-    if (lane == 0) old = atomicAdd(p.counters + pair, 1u);
+    if (lane == 0) old = atom_add_acq_rel_gpu(p.counters + pair, 1u);
     old = __shfl_sync(0xffffffffu, old, 0);
     if ((int)old != g_last - g_first) return;
-    __threadfence();
     float sum[2][4] = {};
     for (int gg = g_first; gg <= g_last; ++gg) {
         const volatile float* sl = p.gpartial + ((size_t)gg * 2 + piece_of(gg * G)) * 256;
