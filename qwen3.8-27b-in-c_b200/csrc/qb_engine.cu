@@ -1056,7 +1056,9 @@ int head(Engine& e, float* out, int B, unsigned long long* keys, uint32_t* am, b
 // model_forward_batch on the device: tokens ctrl->fwd_tok[0..B), positions
 // ctrl->fwd_pos + b.  Logits -> e.logits[b] (this rank's vocabulary rows only
 // with local_rows under tensor parallelism), argmax -> ctrl->argmax[b].
-int fwd_backbone(Engine& e, int B, int ckpt, bool local_rows = false) {
+// Without with_head (prefill chunks before the last) the output head and the
+// argmax are skipped: only the states, the KV cache and h_save advance.
+int fwd_backbone(Engine& e, int B, int ckpt, bool local_rows = false, bool with_head = true) {
     CK(qb_embed(e.embd_type, e.tok_embd, e.E, e.ctrl->fwd_tok, B, e.bx, e.E, e.st));
     fresh_input(e);
     for (size_t il = 0; il < e.L.size(); ++il) {
@@ -1072,8 +1074,10 @@ int fwd_backbone(Engine& e, int B, int ckpt, bool local_rows = false) {
         }
     }
     CK(cudaMemcpyAsync(e.h_save, e.bx, (size_t)B * e.E * 4, cudaMemcpyDeviceToDevice, e.st));
-    if (norm_input(e, e.bx, e.out_norm, B, xp_needs(e, {&e.output}, B))) return -1;
-    if (head(e, e.logits, B, e.keys, e.ctrl->argmax, local_rows)) return -1;
+    if (with_head) {
+        if (norm_input(e, e.bx, e.out_norm, B, xp_needs(e, {&e.output}, B))) return -1;
+        if (head(e, e.logits, B, e.keys, e.ctrl->argmax, local_rows)) return -1;
+    }
     if (ckpt) set_u32_kernel<<<1, 1, 0, e.st>>>(&e.ctrl->cur_slot, (uint32_t)std::min(B - 1, kNSlot - 1));
     CK(cudaGetLastError());
     return 0;
@@ -1488,7 +1492,7 @@ extern "C" int qb_prefill(qwen_model_t* m, const uint32_t* tokens, uint32_t n, i
         const uint32_t B = std::min<uint32_t>(n - pos, PREFILL_MAX_B);
         CK(cudaMemcpyAsync(e->ctrl->fwd_tok, tokens + pos, B * 4, cudaMemcpyHostToDevice, e->st));
         CK(cudaMemcpyAsync(&e->ctrl->fwd_pos, &pos, 4, cudaMemcpyHostToDevice, e->st));
-        if (fwd_backbone(*e, (int)B, 0)) return -1;
+        if (fwd_backbone(*e, (int)B, 0, false, pos + B >= n)) return -1;   // logits of the last chunk only
         if (spec) {
             CK(cudaMemcpyAsync(e->ctrl->mtp_tok, tokens + pos, B * 4, cudaMemcpyHostToDevice, e->st));
             CK(cudaMemcpyAsync(&e->ctrl->mtp_pos, &pos, 4, cudaMemcpyHostToDevice, e->st));
