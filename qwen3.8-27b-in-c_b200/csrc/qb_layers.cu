@@ -304,8 +304,10 @@ __global__ void __launch_bounds__(128) gdn_out_xprep_kernel(const float* __restr
                                                             long long ld, const float* __restrict__ w, int n_v,
                                                             float eps, float* __restrict__ y, int N, QbXBuf xb,
                                                             int what) {
-    pdl_wait();
+    // a GEMV follows: release it before waiting, so that its CTAs take their places and
+    // start streaming weights while this short kernel runs
     pdl_trigger();
+    pdl_wait();
     constexpr int DV = 128;
     const int t = blockIdx.y, lane = threadIdx.x & 31;
     const int pb = blockIdx.x * 4 + (threadIdx.x >> 5);   // head pair = block index of the ssm_out input
@@ -540,8 +542,10 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const float* __restri
                                                            const float2* __restrict__ part_ml, int max_chunks,
                                                            int n_head, int N, float* __restrict__ out,
                                                            long long ldo, QbXBuf xb, int what) {
-    pdl_wait();
+    // a GEMV follows: release it before waiting, so that its CTAs take their places and
+    // start streaming weights while this short kernel runs
     pdl_trigger();
+    pdl_wait();
     constexpr int HD = kAttnHD;
     const int b = blockIdx.y, lane = threadIdx.x & 31;
     const int h = blockIdx.x * 4 + (threadIdx.x >> 5);
@@ -598,8 +602,10 @@ __global__ void silu_mul_kernel(const float* __restrict__ gate, const float* __r
 __global__ void __launch_bounds__(128) silu_mul_xprep_kernel(const float* __restrict__ gate,
                                                              const float* __restrict__ up, long long ld, int n,
                                                              int N, float* __restrict__ out, QbXBuf xb, int what) {
-    pdl_wait();
+    // a GEMV follows: release it before waiting, so that its CTAs take their places and
+    // start streaming weights while this short kernel runs
     pdl_trigger();
+    pdl_wait();
     const int t = blockIdx.y, lane = threadIdx.x & 31;
     const int b = blockIdx.x * 4 + (threadIdx.x >> 5);
     const int nb = n >> 8;

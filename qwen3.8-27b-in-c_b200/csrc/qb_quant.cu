@@ -1227,8 +1227,10 @@ __device__ __forceinline__ float block_sum(float v, float* sh) {
 
 __global__ void __launch_bounds__(256) xprep_kernel(XSeg s0, XSeg s1, int nseg, int N, float eps, QbXBuf xb,
                                                     int what) {
-    pdl_wait();
+    // a GEMV follows: release it before waiting, so that its CTAs take their places and
+    // start streaming weights while this short kernel runs
     pdl_trigger();
+    pdl_wait();
     const int t = blockIdx.y;
     const int K = s0.len + (nseg > 1 ? s1.len : 0);
     const int nb = K >> 8;
@@ -1456,6 +1458,10 @@ cudaError_t qmv_launch(int type, const QbQSeg* segs, int nseg, int K, int N, con
     }
     const bool nt2 = N > 4;
     const bool epi_k = p.in_ss != nullptr || p.epi != QB_EPI_NONE;
+    // a grid of at most one CTA per SM asks for more than half of an SM's shared memory:
+    // CTAs placed early, while the previous kernels still hold SMs, then cannot pair up on
+    // the SMs that free first
+    const size_t smem_launch = grid <= g_num_sms && smem < (size_t)116 * 1024 ? (size_t)116 * 1024 : smem;
     cudaError_t e = cudaSuccess;
 #define QB_LAUNCH(F, I8)                                                                               \
     do {                                                                                               \
@@ -1468,7 +1474,7 @@ cudaError_t qmv_launch(int type, const QbQSeg* segs, int nseg, int K, int N, con
             cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);       \
             attr_set[variant] = true;                                                                  \
         }                                                                                              \
-        e = qb_launch(kern, dim3(grid), dim3(kThreads), smem, st, p);                                  \
+        e = qb_launch(kern, dim3(grid), dim3(kThreads), smem_launch, st, p);                           \
     } while (0)
     switch (type) {
     case QB_IQ4_XS: QB_LAUNCH(QB_IQ4_XS, true); break;
