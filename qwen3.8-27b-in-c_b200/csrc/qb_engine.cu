@@ -1028,7 +1028,23 @@ int gdn_block(Engine& e, const LayerW& l, int B, int ckpt, const NextIn& next) {
     return ffn_block(e, l, e.bx, B, next);
 }
 
-__global__ void set_u32_kernel(uint32_t* p, uint32_t v) { *p = v; }
+// Control-block and copy kernels of the decode graphs.  Launched like every other
+// kernel (qb_launch: programmatic dependent launch), so that they do not break the
+// chain of early launches the way plain launches and memcpy nodes do.
+__global__ void set_u32_kernel(uint32_t* p, uint32_t v) {
+    pdl_wait();
+    pdl_trigger();
+    *p = v;
+}
+__global__ void copy_f32_kernel(float* __restrict__ dst, const float* __restrict__ src, int n) {
+    pdl_wait();
+    pdl_trigger();
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) dst[i] = src[i];
+}
+cudaError_t copy_f32(float* dst, const float* src, int n, cudaStream_t st) {
+    const int blocks = std::min((n + 255) / 256, 64);
+    return qb_launch(copy_f32_kernel, dim3(blocks), dim3(256), 0, st, dst, src, n);
+}
 
 // Output head on the prepared input e.xb: logits -> out[b], argmax -> am[b]
 // (the greedy pick of src/model.c:746-756 over the full row).  Under tensor
@@ -1073,12 +1089,13 @@ int fwd_backbone(Engine& e, int B, int ckpt, bool local_rows = false, bool with_
             if (attn_block(e, l, e.bx, B, &e.ctrl->fwd_pos, kc, vc, next)) return -1;
         }
     }
-    CK(cudaMemcpyAsync(e.h_save, e.bx, (size_t)B * e.E * 4, cudaMemcpyDeviceToDevice, e.st));
+    CK(copy_f32(e.h_save, e.bx, B * e.E, e.st));
     if (with_head) {
         if (norm_input(e, e.bx, e.out_norm, B, xp_needs(e, {&e.output}, B))) return -1;
         if (head(e, e.logits, B, e.keys, e.ctrl->argmax, local_rows)) return -1;
     }
-    if (ckpt) set_u32_kernel<<<1, 1, 0, e.st>>>(&e.ctrl->cur_slot, (uint32_t)std::min(B - 1, kNSlot - 1));
+    if (ckpt) CK(qb_launch(set_u32_kernel, dim3(1), dim3(1), 0, e.st, &e.ctrl->cur_slot,
+                           (uint32_t)std::min(B - 1, kNSlot - 1)));
     CK(cudaGetLastError());
     return 0;
 }
@@ -1097,7 +1114,7 @@ int fwd_mtp(Engine& e, int B, const float* hsrc, int want_logits, bool local_row
     if (gemv_group(e, m1, o1, ld1, 1, 2 * e.E, B, 0)) return -1;
     const NextIn next = want_logits ? NextIn{e.shnorm, xp_needs(e, {&e.output}, B)} : NextIn{};
     if (attn_block(e, e.mtp, e.mtp_x, B, &e.ctrl->mtp_pos, e.mtp_k, e.mtp_v, next)) return -1;
-    CK(cudaMemcpyAsync(e.mtp_h, e.mtp_x + (size_t)(B - 1) * e.E, (size_t)e.E * 4, cudaMemcpyDeviceToDevice, e.st));
+    CK(copy_f32(e.mtp_h, e.mtp_x + (size_t)(B - 1) * e.E, e.E, e.st));
     if (want_logits) {
         if (norm_input(e, e.mtp_x, e.shnorm, B, xp_needs(e, {&e.output}, B))) return -1;
         if (head(e, e.mtp_logits, B, e.keys + QB_MAX_TOK, e.ctrl->mtp_argmax, local_rows)) return -1;
@@ -1109,17 +1126,23 @@ int fwd_mtp(Engine& e, int B, const float* hsrc, int want_logits, bool local_row
 
 // cycle start: cand[0] = next_cand0; first draft input = (cand[0], P+1)
 __global__ void spec_start_kernel(QbCtrl* c) {
+    pdl_wait();
+    pdl_trigger();
     c->cand[0] = c->next_cand0;
     c->mtp_tok[0] = c->cand[0];
     c->mtp_pos = c->P + 1;
 }
 // after draft s: cand[s] = argmax; next draft input = (cand[s], P+s+1)
 __global__ void spec_draft_kernel(QbCtrl* c, int s) {
+    pdl_wait();
+    pdl_trigger();
     c->cand[s] = c->mtp_argmax[0];
     c->mtp_tok[0] = c->cand[s];
     c->mtp_pos = c->P + s + 1;
 }
 __global__ void spec_verify_setup_kernel(QbCtrl* c, int k) {
+    pdl_wait();
+    pdl_trigger();
     for (int i = 0; i <= k; ++i) c->fwd_tok[i] = c->cand[i];
     c->fwd_pos = c->P + 1;
 }
@@ -1128,6 +1151,8 @@ __global__ void spec_verify_setup_kernel(QbCtrl* c, int k) {
 // anchor on (cand[j], h_save[j]) at P+j+1; next cand0 = argmax(logits_b[j]).
 __global__ void spec_accept_kernel(QbCtrl* c, int k, const uint32_t* forced, uint32_t* out_tok,
                                    uint32_t* out_j, const float* h_save, float* mtp_h, int E) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ uint32_t sj;
     if (threadIdx.x == 0) {
         uint32_t j = (uint32_t)k;
@@ -1158,6 +1183,8 @@ __global__ void spec_accept_kernel(QbCtrl* c, int k, const uint32_t* forced, uin
 
 // greedy decode step: next token = argmax of the previous forward
 __global__ void greedy_step_kernel(QbCtrl* c, uint32_t* out_tok) {
+    pdl_wait();
+    pdl_trigger();
     const uint32_t t = c->argmax[0];
     if (c->greedy_n < c->cap_out) out_tok[c->greedy_n] = t;
     c->greedy_n += 1;
@@ -1166,14 +1193,15 @@ __global__ void greedy_step_kernel(QbCtrl* c, uint32_t* out_tok) {
 }
 
 int record_cycle(Engine& e, int k) {
-    spec_start_kernel<<<1, 1, 0, e.st>>>(e.ctrl);
+    CK(qb_launch(spec_start_kernel, dim3(1), dim3(1), 0, e.st, e.ctrl));
     for (int s = 1; s <= k; ++s) {
         if (fwd_mtp(e, 1, e.mtp_h, 1, true)) return -1;
-        spec_draft_kernel<<<1, 1, 0, e.st>>>(e.ctrl, s);
+        CK(qb_launch(spec_draft_kernel, dim3(1), dim3(1), 0, e.st, e.ctrl, s));
     }
-    spec_verify_setup_kernel<<<1, 1, 0, e.st>>>(e.ctrl, k);
+    CK(qb_launch(spec_verify_setup_kernel, dim3(1), dim3(1), 0, e.st, e.ctrl, k));
     if (fwd_backbone(e, k + 1, 1, true)) return -1;
-    spec_accept_kernel<<<1, 256, 0, e.st>>>(e.ctrl, k, e.d_forced, e.d_out_tok, e.d_out_j, e.h_save, e.mtp_h, e.E);
+    CK(qb_launch(spec_accept_kernel, dim3(1), dim3(256), 0, e.st, e.ctrl, k, (const uint32_t*)e.d_forced, e.d_out_tok,
+                 e.d_out_j, (const float*)e.h_save, e.mtp_h, e.E));
     if (fwd_mtp(e, 1, e.mtp_h, 0)) return -1;
     CK(cudaGetLastError());
     return 0;
@@ -1209,7 +1237,7 @@ int capture(Engine& e, cudaGraphExec_t* out, int (*rec)(Engine&, int), int arg) 
 
 int record_greedy(Engine& e, int) {
     if (fwd_backbone(e, 1, 0, true)) return -1;
-    greedy_step_kernel<<<1, 1, 0, e.st>>>(e.ctrl, e.d_out_tok);
+    CK(qb_launch(greedy_step_kernel, dim3(1), dim3(1), 0, e.st, e.ctrl, e.d_out_tok));
     CK(cudaGetLastError());
     return 0;
 }
