@@ -1,6 +1,8 @@
-// IQ4_XS decode helpers shared by the mma.sync and the tcgen05 GEMV paths.
+// IQ4_XS decode helpers of the mma.sync GEMV (iq4_pq) and of the tcgen05 variant
+// (iq4_scale_bytes, iq4_i8).
 //
-// Scales: each row of a 256-column block keeps its 8 bytes of scales as
+// Scales in the tcgen05 tile (the mma.sync tile stores the sub-block scales as
+// int8 differences instead, qb_quant.cu): each row of a 256-column block keeps its 8 bytes of scales as
 // [A(4) d(2) Bh(2)]: A byte i = ls_i | (ls_{4+i} & 3) << 6, Bh nibble j =
 // ls_{4+j} >> 2, d = the fp16 super-block scale (a byte-aligned rearrangement
 // of block_iq4_xs scales_l / scales_h, include/quant.h:56-62; the 6-bit
