@@ -30,20 +30,7 @@ struct QSeg {
     const uint8_t* w;     // repacked weights of this matrix
     float* out;           // out[t * ldo + row]
     long long ldo;
-    int tile0;            // first grid tile of this segment
     int rows;
-};
-
-struct QmvParams {
-    QSeg seg[QB_MAX_SEG];
-    int nseg;
-    int K;                // input length (columns)
-    int N;                // number of input vectors (tokens), 1..8
-    const uint2* xfrag;   // activations, hi/lo fp16 split, in mma B-fragment order
-    const float* xscale;  // [QB_MAX_TOK][K/256] power-of-two scale per 256-column block
-    const float* xsum;    // [QB_MAX_TOK][K/32] plain column sums (Q4_K / Q5_K only)
-    int accumulate;       // 0: out = y ; 1: out += y (residual add)
-    int row_lo, row_hi;   // only rows in [row_lo, row_hi) are stored (gemv_rows API)
 };
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
@@ -84,19 +71,6 @@ __device__ __forceinline__ void mma_16832_s8(int (&d)[4], const uint32_t (&a)[4]
         "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
         : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ uint4 ldg_nc_128(const void* p) {
-    uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p));
-    return v;
-}
-__device__ __forceinline__ uint2 ldg_nc_64(const void* p) {
-    uint2 v;
-    asm volatile("ld.global.nc.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
-    return v;
 }
 
 __device__ __forceinline__ float h2f_bits(uint32_t h16) {
