@@ -17,9 +17,9 @@ Multi-GPU: one process per GPU (torchrun).  --parallel replicas (the
 default): each rank a full model decoding its own sequence; value = tokens
 of all ranks / max rank time (weak scaling, no data-path collective).
 --parallel tp: the ranks decode ONE sequence together; each holds 1/N of
-the rows of every quantised matrix, every GEMV stores its rows into all
-ranks' outputs over NVLink and ends with a cross-rank barrier; value = that
-sequence's tokens / max rank time (strong scaling).
+the DeltaNet / attention heads and FFN columns, the residual projections
+exchange partial sums over NVLink, the output head is split over the
+vocabulary; value = that sequence's tokens / max rank time (strong scaling).
 """
 import argparse
 import json
@@ -178,6 +178,25 @@ def cpu_reference_run(path, n_threads, warmup, steps, time_budget=None):
     return toks / dt, f"{cycles} cycles ({toks} tokens) after {warmup} warm-up cycles, prompt {PROMPT_LEN}"
 
 
+def aggregate(ms, n_tok, tp, dist=None, device="cpu"):
+    """Whole-job throughput from this rank's (device ms, tokens) and, under
+    torch.distributed, every other rank's: the slowest rank's time over the tokens
+    of all ranks (replicas), or of the one sequence they share (tensor
+    parallelism).  Returns (tok/s, max ms, tokens counted).  device: where the
+    collective's tensor lives (cuda for NCCL, cpu for gloo)."""
+    import torch
+    if dist is None:
+        return float(n_tok) / (ms / 1e3), float(ms), float(n_tok)
+    t = torch.tensor([ms, float(n_tok)], dtype=torch.float64, device=device)
+    mx = t.clone()
+    dist.all_reduce(mx[:1], op=dist.ReduceOp.MAX)
+    dist.all_reduce(t[1:], op=dist.ReduceOp.SUM)
+    ms_max, tok_sum = float(mx[0]), float(t[1])
+    if tp:
+        tok_sum = float(n_tok)   # the ranks decoded the same tokens
+    return tok_sum / (ms_max / 1e3), ms_max, tok_sum
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return
@@ -235,17 +254,7 @@ def run_ours(args, rank, world, local_rank):
         dist.barrier()
     n_tok = len(toks)
     log(f"timed: {args.steps} cycles {n_tok} tokens {ms:.1f} ms")
-    t = torch.tensor([ms, float(n_tok)], dtype=torch.float64, device="cuda")
-    if dist:
-        mx = t.clone()
-        dist.all_reduce(mx[:1], op=dist.ReduceOp.MAX)
-        dist.all_reduce(t[1:], op=dist.ReduceOp.SUM)
-        ms_max, tok_sum = float(mx[0]), float(t[1])
-        if tp:
-            tok_sum = float(n_tok)   # the ranks decoded the same tokens
-    else:
-        ms_max, tok_sum = ms, float(n_tok)
-    value = tok_sum / (ms_max / 1e3)
+    value, ms_max, tok_sum = aggregate(ms, n_tok, tp, dist, "cuda")
 
     # ---- end to end through the public C ABI: one request = reset + prefill(128)
     #      + decode 512 tokens, host buffers in and out, wall clock ----
