@@ -10,6 +10,7 @@ constants in the kernel headers (no GPU needed).
   exactly (qb_quant.cu `stage_q6k`).
 * Activations: X = 65536 d0 + 256 d1 + d2 with balanced int8 digits for every
   |X| <= 2^22, |d0| <= 64 (qb_xprep.cuh).
+* The IQ4_XS int32 sums, scaled by summation by parts, cannot overflow.
 """
 import os
 import re
@@ -81,3 +82,28 @@ def test_balanced_digits_reconstruct_the_integer():
         d0 = (X1 - d1) >> 8
         assert 65536 * d0 + 256 * d1 + d2 == X
         assert -128 <= d1 <= 127 and -128 <= d2 <= 127 and abs(d0) <= 64
+
+
+def test_iq4_int32_accumulators_cannot_overflow():
+    """Worst case of the IQ4_XS int8 path's int32 sums (qb_quant.cu stage_iq4_i8):
+    per 32-column sub-block and digit column C_j = sum of 32 products of a table
+    value (or a P / Q term) and a digit (|d0| <= 64, |d1|, |d2| <= 128); the mma
+    chain holds R_j = C_0 + .. + C_j (and, between the P and Q steps, R_{j-1}
+    plus the P products); the scales apply by summation by parts,
+    sum_j s_j C_j = sum_{j<7} (s_j - s_{j+1}) R_j + s_7 R_7, s_j = ls_j - 32 in
+    [-32, 31].  Every partial value must fit in int32."""
+    text = open(os.path.join(CSRC, "qb_iq4.cuh")).read()
+    t = [_const("kIq4I8T%d" % i, text) for i in range(4)]
+    q2, q3 = _const("kIq4QT2", text), _const("kIq4QT3", text)
+    vals = [_s8((w >> (8 * i)) & 0xFF) for w in t for i in range(4)]
+    pq = [_s8((w >> (8 * i)) & 0xFF) for w in t[:2] for i in range(4)] + [-1] + \
+         [_s8((w >> (8 * i)) & 0xFF) for w in (q2, q3) for i in range(4)]
+    wmax = max(max(abs(v) for v in vals), max(abs(v) for v in pq))
+    dmax = 128
+    c_max = 32 * wmax * dmax                 # one sub-block, one digit column
+    r_max = [(j + 1) * c_max for j in range(8)]
+    p_mid = [r_max[j - 1] + c_max if j else c_max for j in range(8)]   # after the P step of sub-block j
+    delta_max, s_max = 63, 32
+    acc_max = sum(delta_max * r_max[j] for j in range(7)) + s_max * r_max[7]
+    assert max(r_max + p_mid) < 2 ** 31
+    assert acc_max < 2 ** 31, acc_max
