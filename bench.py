@@ -13,13 +13,19 @@ drafts, batched verify, acceptance, rollback, MTP anchor); the default
 W + K = 5 + 200 cycles emit ~512 tokens.  Weights are random (no checkpoint
 is available); the GGUF is written by the seeded generator before timing.
 
-Multi-GPU: one process per GPU (torchrun).  --parallel replicas (the
-default): each rank a full model decoding its own sequence; value = tokens
-of all ranks / max rank time (weak scaling, no data-path collective).
---parallel tp: the ranks decode ONE sequence together; each holds 1/N of
-the DeltaNet / attention heads and FFN columns, the residual projections
-exchange partial sums over NVLink, the output head is split over the
-vocabulary; value = that sequence's tokens / max rank time (strong scaling).
+Multi-GPU: one process per GPU (torchrun).  --parallel tp (the default): the
+ranks decode ONE sequence together; each holds 1/N of the DeltaNet /
+attention heads and FFN columns, the residual projections exchange partial
+sums over NVLink, the output head is split over the vocabulary; value = that
+sequence's tokens / max rank time (strong scaling).  --parallel replicas: each
+rank a full model decoding its own sequence; value = tokens of all ranks /
+max rank time (weak scaling, no data-path collective).
+
+Parity: the line's "parity" object compares the stream just timed (from the
+first cycle after prefill) with the compiled reference's stream for the same
+workload, committed in tests/golden/full_spec.npz, and, at N = 1, with the
+reference run live on the host cores in the cpu_baseline leg; under tensor
+parallelism every rank's stream must also equal rank 0's.
 """
 import argparse
 import json
@@ -47,6 +53,7 @@ def _load(name, path):
 qb = _load("qwen_b200", os.path.join(ROOT, "qwen3.8-27b-in-c_b200", "qwen_b200.py"))
 
 METRIC = "decode tok/s (greedy, MTP k=3)"
+WORKLOAD = "C3: 64-layer hybrid + MTP, k=3, verify width 4, forced accept U{0..3}"
 PROMPT_LEN = 128
 SEED = 0
 
@@ -69,16 +76,37 @@ def peaks():
 
 
 def profiled_traffic():
-    """DRAM bytes (read + write) of one FFN gate+up launch, from the committed ncu
-    summary of that launch (same shape in the 4-layer capture and the full model)."""
+    """DRAM bytes (read + write) of one FFN gate+up launch from an ncu capture,
+    kept as data in profiles/roofline_traffic.json (same launch shape in the
+    4-layer capture and the full model)."""
     try:
-        with open(os.path.join(ROOT, "profiles", "qmv_iq4xs_ffn_gate_up_n4_wide4.md")) as f:
-            for line in f:
-                if line.strip().startswith("dram_bytes_per_launch:"):
-                    return float(line.split(":")[1])
+        with open(os.path.join(ROOT, "profiles", "roofline_traffic.json")) as f:
+            return float(json.load(f)["dram_bytes_per_launch"])
+    except (OSError, KeyError, ValueError):
+        return None
+
+
+def golden_full():
+    """The compiled reference's output on this exact workload (prompt, forced
+    schedule, FULL seed-0 model), committed as tests/golden/full_spec.npz."""
+    try:
+        return np.load(os.path.join(ROOT, "tests", "golden", "full_spec.npz"))
     except OSError:
-        pass
-    return None
+        return None
+
+
+def rel_l2(a, b):
+    a, b = np.float64(a), np.float64(b)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def stream_parity(toks, js, ref_toks, ref_js):
+    """Compare two speculative streams over their common prefix."""
+    n = min(len(toks), len(ref_toks))
+    nj = min(len(js), len(ref_js))
+    diff = next((i for i in range(n) if toks[i] != ref_toks[i]), None)
+    return {"tokens_equal": diff is None and n > 0, "n_tokens": int(n), "first_diff": diff,
+            "accept_equal": bool(nj > 0 and np.array_equal(js[:nj], ref_js[:nj])), "n_cycles": int(nj)}
 
 
 def gguf_path(rank, world):
@@ -151,18 +179,24 @@ class Clocks:
 
 def cpu_reference_run(path, n_threads, warmup, steps, time_budget=None):
     """The reference engine (oracle/_ref, compiled from its own sources) on the
-    host cores: prefill 128, then speculative cycles.  Returns (tok/s, info)."""
+    host cores: prefill 128, then speculative cycles.  Returns (tok/s, sample
+    description, stream) where stream holds the emitted tokens and accept lengths
+    from the first cycle on and the prefill logits, for the parity check."""
     orc = _load("qb_oracle", os.path.join(ROOT, "oracle", "ref.py"))
     if not orc.available():
-        return None, "oracle/_ref not built"
+        return None, "oracle/_ref not built", None
     n_ctx = PROMPT_LEN + 4 * (warmup + steps) + 64
     m = orc.RefModel(path, n_ctx, n_threads)
     log("reference model_init")
     m.prefill(prompt_tokens(0), 1)
+    prefill_logits = m.logits()
     log("reference prefill")
     forced = forced_schedule()
+    all_t, all_j = [], []
     if warmup:
-        m.spec_generate(10 ** 6, 3, forced=forced, max_cycles=warmup)
+        t, j = m.spec_generate(10 ** 6, 3, forced=forced, max_cycles=warmup)
+        all_t.append(t)
+        all_j.append(j)
     toks = 0
     cycles = 0
     t0 = time.perf_counter()
@@ -171,11 +205,14 @@ def cpu_reference_run(path, n_threads, warmup, steps, time_budget=None):
         t, j = m.spec_generate(10 ** 6, 3, forced=np.roll(forced, -(warmup + cycles)), max_cycles=1)
         toks += len(t)
         cycles += 1
+        all_t.append(t)
+        all_j.append(j)
         if time_budget and time.perf_counter() - t0 > time_budget:
             break
     dt = time.perf_counter() - t0
     m.close()
-    return toks / dt, f"{cycles} cycles ({toks} tokens) after {warmup} warm-up cycles, prompt {PROMPT_LEN}"
+    stream = {"tokens": np.concatenate(all_t), "accept": np.concatenate(all_j), "prefill_logits": prefill_logits}
+    return toks / dt, f"{cycles} cycles ({toks} tokens) after {warmup} warm-up cycles, prompt {PROMPT_LEN}", stream
 
 
 def aggregate(ms, n_tok, tp, dist=None, device="cpu"):
@@ -197,20 +234,28 @@ def aggregate(ms, n_tok, tp, dist=None, device="cpu"):
     return tok_sum / (ms_max / 1e3), ms_max, tok_sum
 
 
+def bench_config(args, world, tp):
+    """The `config` object both arms print (the same workload)."""
+    return {"workload": WORKLOAD, "prompt": PROMPT_LEN, "cycles_timed": args.steps,
+            "l2": "weights 15 GB per cycle >> 126 MB L2 (no flush needed)",
+            "parallelism": f"tp x{world}" if tp else f"replicas x{world}"}
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return
     path = gguf_path(0, 1)
     n_threads = os.cpu_count()
-    v, sample = cpu_reference_run(path, n_threads, args.warmup, args.steps)
+    v, sample, _ = cpu_reference_run(path, n_threads, args.warmup, args.steps)
     if v is None:
         print(json.dumps({"impl": "reference", "unavailable": sample}))
         return
-    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus,
+    cfg = bench_config(args, world, world > 1 and args.parallel == "tp")
+    line = {"impl": "reference", "platform": "host CPU, reference AVX2 engine", "metric": METRIC, "value": v,
+            "unit": "tok/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded random weights, random prompt)",
-            "config": {"workload": "C3: 64-layer hybrid + MTP, k=3, verify width 4, forced accept U{0..3}",
-                       "prompt": PROMPT_LEN, "platform": "host CPU, reference AVX2 engine"},
+            "config": cfg,
             "cpu_baseline": {"value": v, "unit": "tok/s", "cores": n_threads, "kind": "reference", "sample": sample},
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
@@ -240,8 +285,9 @@ def run_ours(args, rank, world, local_rank):
 
     # ---- device-timed value: K speculative cycles ----
     model.prefill(prompt_tokens(seq_rank), 1)
+    prefill_logits = model.logits()
     log("prefill done")
-    model.spec_generate(10 ** 6, 3, forced=forced, max_cycles=args.warmup)
+    warm_t, warm_j = model.spec_generate(10 ** 6, 3, forced=forced, max_cycles=args.warmup)
     log("warmup done")
     torch.cuda.synchronize()
     if dist:
@@ -255,6 +301,20 @@ def run_ours(args, rank, world, local_rank):
     n_tok = len(toks)
     log(f"timed: {args.steps} cycles {n_tok} tokens {ms:.1f} ms")
     value, ms_max, tok_sum = aggregate(ms, n_tok, tp, dist, "cuda")
+
+    # ---- parity of the stream just timed (from the first cycle after prefill) ----
+    stream_t, stream_j = np.concatenate([warm_t, toks]), np.concatenate([warm_j, js])
+    parity = {}
+    gold = golden_full()
+    if gold is not None and seq_rank == 0:
+        parity["golden"] = stream_parity(stream_t, stream_j, gold["tokens"], gold["accept"])
+        parity["golden"]["prefill_logits_rel_l2"] = rel_l2(prefill_logits[:: int(gold["sub_stride"])],
+                                                           gold["prefill_sub"])
+    if tp:   # every rank decoded the one sequence: all streams must be rank 0's
+        mine = (stream_t.tobytes(), stream_j.tobytes())
+        every = [None] * world
+        dist.all_gather_object(every, mine)
+        parity["ranks_agree"] = all(e == every[0] for e in every)
 
     # ---- end to end through the public C ABI: one request = reset + prefill(128)
     #      + decode 512 tokens, host buffers in and out, wall clock ----
@@ -291,17 +351,24 @@ def run_ours(args, rank, world, local_rank):
         cpu_v, cpu_sample = (None, None)
         if world == 1 and not args.no_cpu:
             log("cpu reference sample")
-            cpu_v, cpu_sample = cpu_reference_run(path, os.cpu_count(), 1, 400, time_budget=args.cpu_seconds)
+            cpu_v, cpu_sample, ref = cpu_reference_run(path, os.cpu_count(), 1, 400, time_budget=args.cpu_seconds)
+            if ref is not None:   # the reference's own stream on the same box, same inputs
+                parity["reference_live"] = stream_parity(stream_t, stream_j, ref["tokens"], ref["accept"])
+                parity["reference_live"]["prefill_logits_rel_l2"] = rel_l2(prefill_logits, ref["prefill_logits"])
+        checks = [v for v in parity.values() if isinstance(v, dict)]
+        parity["tokens_equal"] = bool(checks) and all(c["tokens_equal"] for c in checks) and \
+            parity.get("ranks_agree", True)
+        parity["accept_equal"] = bool(checks) and all(c["accept_equal"] for c in checks)
+        parity["logits_rel_l2"] = max((c["prefill_logits_rel_l2"] for c in checks), default=None)
+        parity["n_tokens"] = max((c["n_tokens"] for c in checks), default=0)
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
             "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "fp32",
             "data": "synthetic (seeded random weights, random prompt)",
-            "config": {"workload": "C3: 64-layer hybrid + MTP, k=3, verify width 4, forced accept U{0..3}",
-                       "prompt": PROMPT_LEN, "tokens_timed": int(tok_sum), "cycles_timed": args.steps,
-                       "mean_accept": float(np.mean(js)) if len(js) else None,
-                       "l2": "weights 15 GB per cycle >> 126 MB L2 (no flush needed)",
-                       "parallelism": f"tp x{world}" if tp else f"replicas x{world}"},
+            "config": bench_config(args, world, tp),
+            "run": {"tokens_timed": int(tok_sum), "mean_accept": float(np.mean(js)) if len(js) else None},
+            "parity": parity,
             "gpu_launches": int(kernels_per_cycle) * args.steps,
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "step": "one request: reset + prefill 128 + decode 512 tokens"},
@@ -369,8 +436,9 @@ def main():
     ap.add_argument("--shape", default="wide4", choices=["wide4", "full"])
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--only", default="")
-    ap.add_argument("--parallel", default="replicas", choices=["tp", "replicas"],
-                    help="N > 1: one sequence over all GPUs (tp) or one sequence per GPU (replicas)")
+    ap.add_argument("--parallel", default="tp", choices=["tp", "replicas"],
+                    help="N > 1: one sequence over all GPUs (tp, the default) or one sequence per GPU "
+                         "(replicas)")
     args = ap.parse_args()
     if args.mode == "components":
         run_components(args)

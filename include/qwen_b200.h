@@ -4,8 +4,8 @@
  *
  * Drop-in boundary.  The entry points below keep the names, argument meaning
  * and return conventions of the reference headers, so a caller written
- * against include/model.h and include/kernels.h (e.g. the spec loop of
- * src/main.c:158-225) recompiles against this header unchanged:
+ * against include/model.h and include/kernels.h recompiles against this
+ * header (through include/shim) with no source edit; src/main.c does:
  *
  *   model_init / model_free            include/model.h:117-118
  *   model_forward                      include/model.h:125
@@ -110,6 +110,15 @@ typedef struct qwen_model {
     uint32_t n_ctx;
     uint32_t pos;
     void *eng;             /* device engine (opaque) */
+#ifdef GGUF_H
+    /* Only when the reference gguf.h was included first (a relinked reference
+     * caller): the file's parsed GGUF context, opened on the host by the
+     * model_init wrapper below, for callers that read metadata from it
+     * (src/main.c:93 hands it to tokenizer_init).  The library never reads it;
+     * as the last member it leaves the offsets of every field the library
+     * touches unchanged. */
+    gguf_context_t gguf;
+#endif
 } qwen_model_t;
 
 typedef struct pool pool_t;
@@ -137,6 +146,27 @@ int mtp_forward(qwen_model_t *m, pool_t *pool, uint32_t token, uint32_t pos, int
 int mtp_forward_batch(qwen_model_t *m, pool_t *pool, const uint32_t *tokens, uint32_t pos,
                       uint32_t B, int want_logits);
 uint32_t model_sample_greedy(const float *logits, uint32_t vocab_size);
+
+#ifdef GGUF_H
+/* A reference caller that reaches into m->gguf (include/model.h:60-61) gets it
+ * through these wrappers: model_init also opens the GGUF on the host with the
+ * reference's own gguf_open (include/gguf.h:109), model_free closes it first.
+ * The device engine does not use that context; it parses the file itself. */
+static inline int qb_model_init_with_gguf(qwen_model_t *m, const char *path, uint32_t n_ctx) {
+    if (model_init(m, path, n_ctx) != 0) return -1;
+    if (gguf_open(&m->gguf, path) != 0) {
+        model_free(m);
+        return -1;
+    }
+    return 0;
+}
+static inline void qb_model_free_with_gguf(qwen_model_t *m) {
+    if (m->eng) gguf_close(&m->gguf);
+    model_free(m);
+}
+#define model_init qb_model_init_with_gguf
+#define model_free qb_model_free_with_gguf
+#endif
 
 /* ---- include/kernels.h:11-44 (host pointers; weights uploaded on first use
  *      and cached on the current device, keyed by W->data) ---- */
@@ -256,8 +286,11 @@ void qb_tp_rows(int rows, int rank, int world, int *r0, int *r1);
  * owns all GPU memory through its own arena, or code on a latency-critical
  * path where cudaMalloc would synchronise the device or fail under memory
  * pressure.  Greedy argmax of `rows` fp32 logit rows that are already on the
- * device (row r at logits + r * ld, n entries, first maximum wins as in
- * model_sample_greedy / src/model.c:746-756); the index of row r goes to the
+ * device (row r at logits + r * ld, n < 2^31 entries); the index of row r
+ * is the one model_sample_greedy (src/model.c:746-756) returns for that row,
+ * NaN and signed zeros included: the first maximum wins, -0 equals +0, a NaN
+ * is never the maximum unless it is entry 0 (then entry 0 is returned, as the
+ * reference's scan does).  The index of row r goes to the
  * device array out[r].  Work is enqueued on `stream` (a cudaStream_t; NULL is
  * the legacy default stream) and the call returns without waiting.
  *
@@ -265,7 +298,10 @@ void qb_tp_rows(int rows, int rank, int world, int *r0, int *r1);
  * 64-bit keys (256 bytes); rows above that limit are rejected with an error.
  * The function allocates nothing.  The first call on each device does a
  * one-time set-up (a symbol-address lookup that may load the module): make
- * it with that device current and before any stream capture.  All calls on a
+ * it with that device current and before any stream capture.  The address
+ * found then is kept for the life of the process: after cudaDeviceReset (or
+ * any teardown of the device's primary context) the module may load at
+ * another address, so do not call this function on that device again.  All calls on a
  * device share the one array, so calls that overlap on the GPU (e.g. on two
  * streams without ordering between them) race.  Returns 0, or -1 with
  * qb_last_error() set. */

@@ -363,5 +363,11 @@ def port_gdn_step(S, q, k, v, beta_raw, alpha_raw, dt_bias, ssm_a):
 
 
 def port_argmax(x):
-    """First maximum wins (src/model.c:746-756)."""
-    return int(np.argmax(np.asarray(x)))
+    """The scan of src/model.c:746-756: max seeded with x[0], replaced only when
+    x[i] > max.  So the first maximum wins, -0 equals +0, a NaN never wins,
+    and a NaN at x[0] makes every comparison false (result 0)."""
+    x = np.asarray(x, np.float32)
+    if np.isnan(x[0]):
+        return 0
+    m = np.nanmax(x)
+    return int(np.flatnonzero(x == m)[0])

@@ -76,10 +76,18 @@ def build_synth(verbose=False, force=False):
     return out
 
 
+def reference_dir():
+    """Where the reference checkout lies: $QB_REFERENCE_DIR, else a directory
+    named "reference" beside this repository.  None when neither has the
+    reference sources (the parity checker is then not built here)."""
+    ref = os.environ.get("QB_REFERENCE_DIR") or os.path.join(os.path.dirname(ROOT), "reference")
+    return ref if os.path.isfile(os.path.join(ref, "src", "model.c")) else None
+
+
 def build_oracle(verbose=False):
     """The checker: compiled only where the reference sources exist."""
-    ref = os.environ.get("QB_REFERENCE_DIR", "/root/reference")
-    if not os.path.isdir(os.path.join(ref, "src")):
+    ref = reference_dir()
+    if ref is None:
         return None
     _run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), f"REF={ref}"], verbose)
     return os.path.join(ROOT, "oracle", "_ref", "libqwenref.so")

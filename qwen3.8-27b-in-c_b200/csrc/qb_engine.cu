@@ -132,6 +132,32 @@ struct Cursor {
     }
 };
 
+// (elements per block, bytes per block) of the formats the engine decodes;
+// {0, 0} for any other ggml type id (include/quant.h:14-68, gguf.h:40-64)
+struct BlockFmt { uint64_t elems, bytes; };
+BlockFmt block_fmt(int type) {
+    switch (type) {
+    case QB_F32: return {1, 4};
+    case QB_Q8_0: return {32, 34};
+    case QB_IQ4_XS: return {256, 136};
+    case QB_Q6_K: return {256, 210};
+    case QB_Q4_K: return {256, 144};
+    case QB_Q5_K: return {256, 176};
+    default: return {0, 0};
+    }
+}
+
+// Bytes of a whole tensor, ~0 for a type this engine does not decode (its
+// extent is then unknown here; the model checks reject such a tensor where
+// the model needs it) or for a size that does not fit 64 bits.
+uint64_t gguf_tensor_bytes(int type, const uint64_t* ne, uint32_t n_dims) {
+    const BlockFmt f = block_fmt(type);
+    if (!f.elems || ne[0] % f.elems) return ~0ull;
+    unsigned __int128 b = (unsigned __int128)(ne[0] / f.elems) * f.bytes;
+    for (uint32_t d = 1; d < n_dims; ++d) b *= ne[d];
+    return b > (unsigned __int128)(~0ull - 1) ? ~0ull : (uint64_t)b;
+}
+
 int gguf_load(Gguf& g, const char* path) {
     g.fd = open(path, O_RDONLY);
     if (g.fd < 0) { set_err(-1, "cannot open %s", path); return -1; }
@@ -211,8 +237,14 @@ int gguf_load(Gguf& g, const char* path) {
     const uint64_t cur = (uint64_t)(c.p - g.map);
     const uint64_t base = (cur + alignment - 1) / alignment * alignment;
     for (auto& t : g.tensors) {
+        // the whole tensor must lie inside the file (a truncated file fails
+        // here instead of faulting in a later copy)
+        const uint64_t bytes = gguf_tensor_bytes(t.type, t.ne, t.n_dims);
+        if (base > g.size || t.offset > g.size - base || (bytes != ~0ull && bytes > g.size - base - t.offset)) {
+            set_err(-1, "%s: tensor %s extends past the end of the file", path, t.name.c_str());
+            return -1;
+        }
         t.data = g.map + base + t.offset;
-        if (base + t.offset >= g.size) { set_err(-1, "%s: tensor %s outside file", path, t.name.c_str()); return -1; }
     }
     if (g.cfg.vocab_size == 0) {
         const GTensor* e = g.find("token_embd.weight");
@@ -222,15 +254,107 @@ int gguf_load(Gguf& g, const char* path) {
 }
 
 size_t gguf_row_bytes(int type, uint64_t ne0) {
-    switch (type) {
-    case QB_F32: return ne0 * 4;
-    case QB_Q8_0: return ne0 / 32 * 34;
-    case QB_IQ4_XS: return ne0 / 256 * 136;
-    case QB_Q6_K: return ne0 / 256 * 210;
-    case QB_Q4_K: return ne0 / 256 * 144;
-    case QB_Q5_K: return ne0 / 256 * 176;
-    default: return 0;
+    const BlockFmt f = block_fmt(type);
+    return f.elems ? ne0 / f.elems * f.bytes : 0;
+}
+
+// The structural checks of the reference's model_init (src/model.c:31-53 and
+// 55-150: every tensor present, with the dimensions the config implies) plus
+// the MTP block blk.<n_layer> (src/model.c:245-279) and the formats this engine
+// decodes.  Runs before any device work, so a malformed file makes model_init
+// return -1 with a message, as the reference's does.
+int validate_model(const Gguf& g) {
+    const qwen_config_t& c = g.cfg;
+    char nm[96];
+    auto find = [&](const char* fmt, int il) -> const GTensor* {
+        snprintf(nm, sizeof nm, fmt, il);
+        const GTensor* t = g.find(nm);
+        if (!t) set_err(-1, "model_init: missing tensor %s", nm);
+        return t;
+    };
+    auto shape = [&](const GTensor* t, uint64_t ne0, uint64_t ne1, bool matrix) -> bool {
+        if (!t) return false;
+        const bool ok = matrix ? (t->n_dims == 2 && t->ne[0] == ne0 && t->ne[1] == ne1)
+                               : (t->n_dims == 1 && t->ne[0] == ne0);
+        if (!ok) {
+            set_err(-1, "model_init: %s dimension mismatch (%llu x %llu, want %llu x %llu)", t->name.c_str(),
+                    (unsigned long long)t->ne[0], (unsigned long long)(t->n_dims > 1 ? t->ne[1] : 1),
+                    (unsigned long long)ne0, (unsigned long long)(matrix ? ne1 : 1));
+            return false;
+        }
+        // vectors and the conv1d taps are F32; every other matrix is one of
+        // the quantised formats the GEMV decodes
+        const BlockFmt f = block_fmt(t->type);
+        const bool want_f32 = !matrix || t->name.find("ssm_conv1d") != std::string::npos;
+        if (!f.elems || t->ne[0] % f.elems || want_f32 != (t->type == QB_F32)) {
+            set_err(-1, "model_init: %s has unsupported type %d for its shape", t->name.c_str(), t->type);
+            return false;
+        }
+        return true;
+    };
+    if (!c.full_attn_interval || !c.ssm_state_size || !c.n_embd || !c.vocab_size) {
+        set_err(-1, "model_init: incomplete model metadata");
+        return -1;
     }
+    const GTensor* a0 = find("blk.%d.ssm_a", 0);
+    if (!a0 || a0->n_dims != 1) { if (a0) set_err(-1, "model_init: blk.0.ssm_a dimension mismatch"); return -1; }
+    const uint64_t E = c.n_embd, F = c.n_ff, nv = a0->ne[0], dk = c.ssm_state_size, dv = c.ssm_state_size;
+    const uint64_t d_inner = c.ssm_inner_size, conv_dim = 2ull * c.ssm_group_count * dk + d_inner;
+    const uint64_t hd = c.head_dim, nh = c.n_head, nkv = c.n_head_kv;
+    const uint32_t n_layer = c.n_layer > c.nextn_layers ? c.n_layer - c.nextn_layers : c.n_layer;
+    if (d_inner != nv * dv || nv > 256 || dv > 256 || dk > 256) {
+        set_err(-1, "model_init: inconsistent DeltaNet sizes (inner %llu, v-heads %llu, state %llu)",
+                (unsigned long long)d_inner, (unsigned long long)nv, (unsigned long long)dk);
+        return -1;
+    }
+    const GTensor* te = g.find("token_embd.weight");
+    if (!te) { set_err(-1, "model_init: missing tensor token_embd.weight"); return -1; }
+    if (!shape(te, E, c.vocab_size, true)) return -1;
+    const GTensor* on = g.find("output_norm.weight");
+    if (!on) { set_err(-1, "model_init: missing tensor output_norm.weight"); return -1; }
+    if (!shape(on, E, 0, false)) return -1;
+    const GTensor* out = g.find("output.weight");
+    if (out && !shape(out, E, c.vocab_size, true)) return -1;
+    auto attn = [&](int il) -> bool {
+        return shape(find("blk.%d.attn_q.weight", il), E, 2 * nh * hd, true) &&
+               shape(find("blk.%d.attn_k.weight", il), E, nkv * hd, true) &&
+               shape(find("blk.%d.attn_v.weight", il), E, nkv * hd, true) &&
+               shape(find("blk.%d.attn_output.weight", il), nh * hd, E, true) &&
+               shape(find("blk.%d.attn_q_norm.weight", il), hd, 0, false) &&
+               shape(find("blk.%d.attn_k_norm.weight", il), hd, 0, false);
+    };
+    auto common = [&](int il) -> bool {
+        return shape(find("blk.%d.attn_norm.weight", il), E, 0, false) &&
+               shape(find("blk.%d.post_attention_norm.weight", il), E, 0, false) &&
+               shape(find("blk.%d.ffn_gate.weight", il), E, F, true) &&
+               shape(find("blk.%d.ffn_up.weight", il), E, F, true) &&
+               shape(find("blk.%d.ffn_down.weight", il), F, E, true);
+    };
+    for (uint32_t il = 0; il < n_layer; ++il) {
+        if (!common((int)il)) return -1;
+        const bool rec = ((il + 1) % c.full_attn_interval) != 0;
+        if (rec) {
+            if (!(shape(find("blk.%d.attn_qkv.weight", il), E, conv_dim, true) &&
+                  shape(find("blk.%d.attn_gate.weight", il), E, d_inner, true) &&
+                  shape(find("blk.%d.ssm_conv1d.weight", il), c.ssm_conv_kernel, conv_dim, true) &&
+                  shape(find("blk.%d.ssm_beta.weight", il), E, nv, true) &&
+                  shape(find("blk.%d.ssm_alpha.weight", il), E, nv, true) &&
+                  shape(find("blk.%d.ssm_out.weight", il), d_inner, E, true) &&
+                  shape(find("blk.%d.ssm_dt.bias", il), nv, 0, false) &&
+                  shape(find("blk.%d.ssm_a", il), nv, 0, false) &&
+                  shape(find("blk.%d.ssm_norm.weight", il), dv, 0, false)))
+                return -1;
+        } else if (!attn((int)il)) {
+            return -1;
+        }
+    }
+    const int im = (int)n_layer;   // the MTP block
+    if (!common(im) || !attn(im) || !shape(find("blk.%d.nextn.eh_proj.weight", im), 2 * E, E, true) ||
+        !shape(find("blk.%d.nextn.enorm.weight", im), E, 0, false) ||
+        !shape(find("blk.%d.nextn.hnorm.weight", im), E, 0, false) ||
+        !shape(find("blk.%d.nextn.shared_head_norm.weight", im), E, 0, false))
+        return -1;
+    return 0;
 }
 
 // ------------------------------ engine ----------------------------------------
@@ -504,9 +628,11 @@ int build_gu(Engine& e, LayerW& l) {
 }
 
 int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
+    // host-side parse and checks first: a malformed file fails without device work
+    if (gguf_load(e.g, path) || validate_model(e.g)) return -1;
+    if (n_ctx == 0) { set_err(-1, "model_init: n_ctx must be > 0"); return -1; }
     CK(cudaGetDevice(&e.dev));
     CK(cudaStreamCreateWithFlags(&e.st, cudaStreamNonBlocking));
-    if (gguf_load(e.g, path)) return -1;
     e.cfg = e.g.cfg;
     qwen_config_t& c = e.cfg;
     qwen_dims_t& d = e.d;

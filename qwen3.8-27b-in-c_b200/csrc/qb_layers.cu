@@ -628,9 +628,18 @@ __global__ void __launch_bounds__(128) silu_mul_xprep_kernel(const float* __rest
 
 // ------------------------------- argmax --------------------------------------
 // key = ordered(value) << 32 | ~index: the max key is the largest value with
-// the lowest index among equals (first maximum wins, src/model.c:746-756).
+// the lowest index among equals.  This reproduces the reference's scan
+// `if (logits[i] > max) ...` seeded with logits[0] (src/model.c:746-756) for
+// every input, including the ones a plain ordering gets wrong:
+//  - -0 and +0 compare equal there, so both map to the key of +0 and the
+//    lower index wins;
+//  - a NaN never wins a comparison, so a NaN after index 0 gets the lowest
+//    key (it is chosen only if every entry is NaN, and then index 0 wins);
+//  - a NaN at index 0 makes every later comparison false, so the scan returns
+//    0: that entry gets the highest key.
 __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t i) {
-    uint32_t u = __float_as_uint(v);
+    if (v != v) return i == 0 ? ~0ull : (unsigned long long)(0xFFFFFFFFu - i);
+    uint32_t u = v == 0.f ? 0u : __float_as_uint(v);
     u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
     return ((unsigned long long)u << 32) | (0xFFFFFFFFu - i);
 }
@@ -641,6 +650,8 @@ __global__ void argmax_reset_kernel(unsigned long long* keys, int B) {
     if (threadIdx.x < B) keys[threadIdx.x] = 0ull;
 }
 
+// n < 2^31 entries per row; the loop index is 64-bit so that the last
+// stride cannot wrap for n near 2^31.
 __global__ void argmax_kernel(const float* __restrict__ x, long long ldx, int n,
                               unsigned long long* __restrict__ keys, int i0) {
     pdl_wait();
@@ -648,7 +659,8 @@ __global__ void argmax_kernel(const float* __restrict__ x, long long ldx, int n,
     const int b = blockIdx.y;
     const float* xr = x + (size_t)b * ldx;
     unsigned long long best = 0ull;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const long long step = (long long)gridDim.x * blockDim.x;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += step) {
         const unsigned long long k = argmax_key(xr[i], (uint32_t)(i0 + i));
         best = k > best ? k : best;
     }
@@ -926,16 +938,15 @@ cudaError_t qb_gdn_out_xprep(const float* o, const float* z, long long ld, const
 }
 
 cudaError_t qb_argmax_reset(unsigned long long* keys, int B, cudaStream_t st) {
-    qb_launch(argmax_reset_kernel, dim3(1), dim3(32), 0, st, keys, B);
-    return cudaGetLastError();
+    return qb_launch(argmax_reset_kernel, dim3(1), dim3(32), 0, st, keys, B);
 }
 
 cudaError_t qb_argmax(const float* x, long long ldx, int n, int B, unsigned long long* keys, cudaStream_t st,
                       int i0) {
-    const int blocks = (n + 1023) / 1024 < 148 ? (n + 1023) / 1024 : 148;
     if (n < 1) return cudaSuccess;   // no rows here: the keys keep their reset value
-    qb_launch(argmax_kernel, dim3(blocks, B), dim3(256), 0, st, x, ldx, n, keys, i0);
-    return cudaGetLastError();
+    const long long want = ((long long)n + 1023) / 1024;
+    const int blocks = want < 148 ? (int)want : 148;
+    return qb_launch(argmax_kernel, dim3(blocks, B), dim3(256), 0, st, x, ldx, n, keys, i0);
 }
 
 cudaError_t qb_tp_argmax(const unsigned long long* keys, int B, uint32_t* out, const QbArgX& x, cudaStream_t st) {
@@ -963,8 +974,7 @@ cudaError_t qb_tp_pull_rows(float* dst, const float* const* src, const int* r0, 
 }
 
 cudaError_t qb_argmax_to_u32(const unsigned long long* keys, int B, uint32_t* out, cudaStream_t st) {
-    qb_launch(argmax_to_u32_kernel, dim3(1), dim3(32), 0, st, keys, B, out);
-    return cudaGetLastError();
+    return qb_launch(argmax_to_u32_kernel, dim3(1), dim3(32), 0, st, keys, B, out);
 }
 
 cudaError_t qb_op_rmsnorm(float* out, const float* x, const float* w, long long n, float eps, cudaStream_t st) {

@@ -22,6 +22,13 @@ qb = _load("qwen_b200", os.path.join(PKG_DIR, "qwen_b200.py"))
 oracle = _load("qb_oracle", os.path.join(ROOT, "oracle", "ref.py"))
 
 
+def reference_dir():
+    """The reference checkout ($QB_REFERENCE_DIR, else "reference" beside this
+    repository), or None where its sources are absent (e.g. the GPU box)."""
+    ref = os.environ.get("QB_REFERENCE_DIR") or os.path.join(os.path.dirname(ROOT), "reference")
+    return ref if os.path.isfile(os.path.join(ref, "src", "model.c")) else None
+
+
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200)")
 
@@ -73,3 +80,20 @@ def small_gguf(workdir):
 @pytest.fixture(scope="session")
 def wide_gguf(workdir):
     return _gguf(workdir, "wide4", qb.WIDE4, seed=4)
+
+
+def full_gguf_path():
+    """The FULL benchmark model (seed 0), shared with bench.py: one 15.3 GB file
+    in /dev/shm, written once per box."""
+    d = "/dev/shm" if os.path.isdir("/dev/shm") else "/tmp"
+    return os.path.join(d, "qb_bench_full_seed0.gguf")
+
+
+@pytest.fixture(scope="session")
+def full_gguf():
+    path = full_gguf_path()
+    if not os.path.exists(path):
+        tmp = path + f".tmp{os.getpid()}"
+        qb.write_synth_gguf(tmp, qb.FULL, seed=0)
+        os.replace(tmp, path)
+    return path

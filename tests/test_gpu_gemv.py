@@ -119,6 +119,14 @@ def test_sample_greedy_first_max_wins():
     assert qb.sample_greedy(y) == oracle.port_argmax(y)
 
 
+def test_sample_greedy_nan_and_signed_zero():
+    """The device argmax returns what the reference's `>` scan returns
+    (src/model.c:746-756), NaN entries and -0 / +0 ties included."""
+    from test_oracle import _argmax_edge_rows
+    for x in _argmax_edge_rows(248320):
+        assert qb.sample_greedy(x) == oracle.port_argmax(x)
+
+
 @pytest.mark.parametrize("name", ["silu", "sigmoid", "softplus", "softmax", "rmsnorm", "l2norm"])
 @pytest.mark.parametrize("n", [8, 13, 5120])
 def test_ops_against_reference(name, n):

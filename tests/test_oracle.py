@@ -133,3 +133,25 @@ def test_golden_fixtures_reproduce(tiny_gguf):
     np.testing.assert_array_equal(toks, g["tokens"])
     np.testing.assert_array_equal(js, g["accept"])
     m.close()
+
+
+def _argmax_edge_rows(n=4099):
+    """Rows where an ordering by float bits would differ from the reference's
+    `>` scan: signed zeros, NaN after the maximum, NaN at entry 0, all NaN."""
+    rows = []
+    x = np.full(n, -1.0, np.float32); x[5] = -0.0; x[9] = 0.0; rows.append(x)          # -0 first: 5 wins
+    x = np.full(n, -1.0, np.float32); x[5] = 0.0; x[9] = -0.0; rows.append(x)
+    x = np.random.default_rng(3).standard_normal(n).astype(np.float32); x[17] = np.nan; rows.append(x)
+    x = np.random.default_rng(4).standard_normal(n).astype(np.float32); x[0] = np.nan; rows.append(x)
+    x = np.full(n, np.nan, np.float32); rows.append(x)
+    x = np.full(n, np.nan, np.float32); x[n - 1] = -np.inf; rows.append(x)
+    x = np.full(n, -np.inf, np.float32); rows.append(x)
+    return rows
+
+
+@pytest.mark.skipif(not oracle.available(), reason="oracle/_ref not built")
+def test_port_argmax_matches_reference_edge_cases():
+    L = oracle.ref()
+    for x in _argmax_edge_rows():
+        want = L.ref_argmax(x.ctypes.data_as(oracle.C.POINTER(oracle.C.c_float)), x.size)
+        assert oracle.port_argmax(x) == want
