@@ -2019,6 +2019,7 @@ struct Scratch {
     QbQmvWork work{};
 };
 std::mutex g_mu;
+constexpr int QB_GEMV_MULTI_MAX = 8;   // src/kernels.c:657 (GEMV_MULTI_MAX)
 // host GEMV API: IQ4_XS at n <= 4 on tcgen05 (QB_TC=1); default: int8 mma.sync
 bool host_tc() {
     static const bool on = [] {
@@ -2137,53 +2138,91 @@ int wcache_get(const gguf_tensor_info_t* W, const DevMat*& out) {
     return 0;
 }
 
-// out[t][r] for rows [r0, r1), t < n, from host x/out
-int gemv_host(const gguf_tensor_info_t* W, const float* x, uint64_t ldx, int n, float* out, uint64_t ldo, uint64_t r0,
-              uint64_t r1) {
-    if (!W || !x || !out || n < 1) { set_err(-1, "gemv: bad arguments"); return -1; }
+// out_i[t][r] = W_i x[t] for the n_mat matrices (all reading the same x), rows
+// [r0, r1) of each (r1 clamped to its rows), t < n, host x / outs.  One
+// dispatch: per chunk of up to QB_MAX_TOK vectors, one host-to-device copy of
+// x, one activation prep covering every format and width, one GEMV launch per
+// matrix queued back to back (each the launch a single-matrix call makes, so
+// the results are bit-identical to separate calls, as src/kernels.c:650-655
+// promises for the CPU), the device-to-host copies, one synchronisation.
+int gemv_multi_host(const gguf_tensor_info_t* const* Ws, int n_mat, const float* x, uint64_t ldx, int n,
+                    float* const* outs, const uint64_t* ldos, uint64_t r0, uint64_t r1) {
+    if (!Ws || !x || !outs || !ldos || n < 1 || n_mat < 1 || n_mat > QB_GEMV_MULTI_MAX) {
+        set_err(-1, "gemv: bad arguments (n %d, n_mat %d, at most %d matrices)", n, n_mat, QB_GEMV_MULTI_MAX);
+        return -1;
+    }
     std::lock_guard<std::mutex> lk(g_mu);
-    const DevMat* M = nullptr;
-    if (wcache_get(W, M)) return -1;
-    const int K = M->K;
-    if (r1 > (uint64_t)M->rows) r1 = M->rows;
-    if (r0 >= r1) return 0;
+    const DevMat* M[QB_GEMV_MULTI_MAX];
+    uint64_t lo[QB_GEMV_MULTI_MAX], hi[QB_GEMV_MULTI_MAX];
+    int Kmax = 0;
+    size_t out_floats = 0;
+    int need = 0;
+    for (int i = 0; i < n_mat; ++i) {
+        if (!Ws[i] || !outs[i]) { set_err(-1, "gemv: null matrix or output %d", i); return -1; }
+        if (wcache_get(Ws[i], M[i])) return -1;
+        Kmax = std::max(Kmax, M[i]->K);
+        hi[i] = std::min<uint64_t>(r1, (uint64_t)M[i]->rows);
+        lo[i] = std::min(r0, hi[i]);
+        out_floats += (size_t)std::min(n, QB_MAX_TOK) * M[i]->rows;
+    }
+    if (ldx < (uint64_t)Kmax) { set_err(-1, "gemv: ldx %llu < ne0 %d", (unsigned long long)ldx, Kmax); return -1; }
     Scratch* s = nullptr;
     for (int t0 = 0; t0 < n; t0 += QB_MAX_TOK) {
         const int nn = std::min(QB_MAX_TOK, n - t0);
-        if (scratch_get(s, (size_t)nn * K, (size_t)nn * M->rows, K)) return -1;
-        CK(cudaMemcpy2DAsync(s->x, (size_t)K * 4, x + (size_t)t0 * ldx, ldx * 4, (size_t)K * 4, nn, cudaMemcpyHostToDevice, s->st));
-        const int t_lo = (int)(r0 / (2 * QB_TILE)) * 2;   // start on a tile pair
-        if (M->type == QB_F32) {
-            CK(qb_qmv_f32((const float*)M->w, M->rows, K, s->x, K, nn, s->out, M->rows, 0, (int)r0, (int)r1, s->st));
-        } else {
-            if (scratch_work(s, M->rows)) return -1;
-            QbXIn in{s->x, K, nullptr, K};
-            const bool tc = M->w_tc && nn <= 4 && host_tc();
-            CK(qb_xprep(&in, 1, nn, 1e-6f, s->xb, qb_xprep_needs(M->type, nn, tc ? 1 : 0), s->st));
-            if (tc) {
-                const int T0 = (int)(r0 / 128);   // start on a 128-row tile
-                QbQSeg seg;
-                seg.w = (const uint8_t*)M->w_tc + (size_t)T0 * (K / 256) * qb_repacked_bytes_tc(128, 256);
-                seg.out = s->out + (size_t)T0 * 128;
-                seg.ldo = M->rows;
-                seg.rows = (int)(r1 - (uint64_t)T0 * 128);
-                CK(qb_qmv_tc(&seg, 1, K, nn, s->xb, 0, (int)(r0 - (uint64_t)T0 * 128), (int)(r1 - (uint64_t)T0 * 128),
-                             s->work, s->st));
-            } else {
-            QbQSeg seg;
-            seg.w = (const uint8_t*)M->w + (size_t)t_lo * (K / qb_unit_cols(M->type)) * qb_unit_bytes(M->type);
-            seg.out = s->out + (size_t)t_lo * QB_TILE;
-            seg.ldo = M->rows;
-            seg.rows = (int)(r1 - (uint64_t)t_lo * QB_TILE);
-            CK(qb_qmv(M->type, &seg, 1, K, nn, s->xb, 0, (int)(r0 - (uint64_t)t_lo * QB_TILE),
-                      (int)(r1 - (uint64_t)t_lo * QB_TILE), s->work, s->st));
-            }
+        if (scratch_get(s, (size_t)nn * Kmax, out_floats, Kmax)) return -1;
+        CK(cudaMemcpy2DAsync(s->x, (size_t)Kmax * 4, x + (size_t)t0 * ldx, ldx * 4, (size_t)Kmax * 4, nn,
+                             cudaMemcpyHostToDevice, s->st));
+        need = 0;
+        for (int i = 0; i < n_mat; ++i) {
+            if (M[i]->type == QB_F32) continue;
+            const bool tc = M[i]->w_tc && nn <= 4 && host_tc();
+            need |= qb_xprep_needs(M[i]->type, nn, tc ? 1 : 0);
+            if (scratch_work(s, M[i]->rows)) return -1;
         }
-        CK(cudaMemcpy2DAsync(out + (size_t)t0 * ldo + r0, ldo * 4, s->out + r0, (size_t)M->rows * 4, (size_t)(r1 - r0) * 4, nn,
-                             cudaMemcpyDeviceToHost, s->st));
+        if (need) {
+            QbXIn in{s->x, Kmax, nullptr, Kmax};
+            CK(qb_xprep(&in, 1, nn, 1e-6f, s->xb, need, s->st));
+        }
+        float* o = s->out;
+        for (int i = 0; i < n_mat; ++i) {
+            const DevMat* W = M[i];
+            const int K = W->K;
+            const uint64_t a = lo[i], b = hi[i];
+            if (a < b) {
+                const int t_lo = (int)(a / (2 * QB_TILE)) * 2;   // start on a tile pair
+                if (W->type == QB_F32) {
+                    CK(qb_qmv_f32((const float*)W->w, W->rows, K, s->x, Kmax, nn, o, W->rows, 0, (int)a, (int)b, s->st));
+                } else if (W->w_tc && nn <= 4 && host_tc()) {
+                    const int T0 = (int)(a / 128);   // start on a 128-row tile
+                    QbQSeg seg;
+                    seg.w = (const uint8_t*)W->w_tc + (size_t)T0 * (K / 256) * qb_repacked_bytes_tc(128, 256);
+                    seg.out = o + (size_t)T0 * 128;
+                    seg.ldo = W->rows;
+                    seg.rows = (int)(b - (uint64_t)T0 * 128);
+                    CK(qb_qmv_tc(&seg, 1, K, nn, s->xb, 0, (int)(a - (uint64_t)T0 * 128), (int)(b - (uint64_t)T0 * 128),
+                                 s->work, s->st));
+                } else {
+                    QbQSeg seg;
+                    seg.w = (const uint8_t*)W->w + (size_t)t_lo * (K / qb_unit_cols(W->type)) * qb_unit_bytes(W->type);
+                    seg.out = o + (size_t)t_lo * QB_TILE;
+                    seg.ldo = W->rows;
+                    seg.rows = (int)(b - (uint64_t)t_lo * QB_TILE);
+                    CK(qb_qmv(W->type, &seg, 1, K, nn, s->xb, 0, (int)(a - (uint64_t)t_lo * QB_TILE),
+                              (int)(b - (uint64_t)t_lo * QB_TILE), s->work, s->st));
+                }
+                CK(cudaMemcpy2DAsync(outs[i] + (size_t)t0 * ldos[i] + a, ldos[i] * 4, o + a, (size_t)W->rows * 4,
+                                     (size_t)(b - a) * 4, nn, cudaMemcpyDeviceToHost, s->st));
+            }
+            o += (size_t)nn * W->rows;
+        }
         CK(cudaStreamSynchronize(s->st));
     }
     return 0;
+}
+
+int gemv_host(const gguf_tensor_info_t* W, const float* x, uint64_t ldx, int n, float* out, uint64_t ldo, uint64_t r0,
+              uint64_t r1) {
+    return gemv_multi_host(&W, 1, x, ldx, n, &out, &ldo, r0, r1);
 }
 
 int op_host(int which, float* out, const float* x, const float* w, uint64_t n, float eps) {
@@ -2225,11 +2264,21 @@ extern "C" void gemv_batch(pool_t*, const gguf_tensor_info_t* W, const float* x,
     gemv_host(W, x, ldx, n, out, ldo, 0, W ? W->ne[1] : 0);
 }
 extern "C" void gemv_multi(pool_t*, const gguf_tensor_info_t* const* Ws, const float* x, float* const* outs, int n_mat) {
-    for (int i = 0; i < n_mat; ++i) gemv_host(Ws[i], x, Ws[i]->ne[0], 1, outs[i], Ws[i]->ne[1], 0, Ws[i]->ne[1]);
+    if (!Ws || n_mat < 1 || n_mat > QB_GEMV_MULTI_MAX || !Ws[0]) {
+        set_err(-1, "gemv_multi: bad arguments (n_mat %d, at most %d)", n_mat, QB_GEMV_MULTI_MAX);
+        return;
+    }
+    uint64_t ldos[QB_GEMV_MULTI_MAX];
+    uint64_t K = 0;
+    for (int i = 0; i < n_mat; ++i) {
+        ldos[i] = Ws[i] ? Ws[i]->ne[1] : 0;
+        K = std::max<uint64_t>(K, Ws[i] ? Ws[i]->ne[0] : 0);
+    }
+    gemv_multi_host(Ws, n_mat, x, K, 1, outs, ldos, 0, ~0ull);
 }
 extern "C" void gemv_multi_batch(pool_t*, const gguf_tensor_info_t* const* Ws, const float* x, uint64_t ldx, int n,
                                  float* const* outs, const uint64_t* ldos, int n_mat) {
-    for (int i = 0; i < n_mat; ++i) gemv_host(Ws[i], x, ldx, n, outs[i], ldos[i], 0, Ws[i]->ne[1]);
+    gemv_multi_host(Ws, n_mat, x, ldx, n, outs, ldos, 0, ~0ull);
 }
 extern "C" void rmsnorm(float* out, const float* x, const float* weight, uint64_t n, float eps) {
     op_host(0, out, x, weight, n, eps);

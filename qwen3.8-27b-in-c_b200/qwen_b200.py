@@ -100,6 +100,7 @@ def lib():
                                       C.c_uint64, C.c_uint64]
         L.gemv_multi_batch.argtypes = [vp, P(P(TensorInfo)), P(f32), C.c_uint64, i32, P(P(f32)),
                                        P(C.c_uint64), i32]
+        L.gemv_multi.argtypes = [vp, P(P(TensorInfo)), P(f32), P(P(f32)), i32]
         for n in ("rmsnorm",):
             getattr(L, n).argtypes = [P(f32), P(f32), P(f32), C.c_uint64, f32]
         L.l2norm.argtypes = [P(f32), P(f32), C.c_uint64, f32]
@@ -176,6 +177,31 @@ def gemv_batch(t, x, n=None, out=None):
     lib().gemv_batch(None, C.byref(t), _fp(x), x.shape[1], n, _fp(out), out.shape[1])
     check()
     return out
+
+
+def gemv_multi_batch(ts, x, n=None):
+    """outs[i][n][rows_i] = W_i x (include/kernels.h:32-34): every matrix reads the
+    same x, in one dispatch."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    n = x.shape[0] if n is None else n
+    outs = [np.zeros((n, t.ne[1]), np.float32) for t in ts]
+    W = (C.POINTER(TensorInfo) * len(ts))(*[C.pointer(t) for t in ts])
+    O = (C.POINTER(C.c_float) * len(ts))(*[_fp(o) for o in outs])
+    ld = (C.c_uint64 * len(ts))(*[o.shape[1] for o in outs])
+    lib().gemv_multi_batch(None, W, _fp(x), x.shape[1], n, O, ld, len(ts))
+    check()
+    return outs
+
+
+def gemv_multi(ts, x):
+    """The single-vector form (include/kernels.h:28-29)."""
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    outs = [np.zeros(t.ne[1], np.float32) for t in ts]
+    W = (C.POINTER(TensorInfo) * len(ts))(*[C.pointer(t) for t in ts])
+    O = (C.POINTER(C.c_float) * len(ts))(*[_fp(o) for o in outs])
+    lib().gemv_multi(None, W, _fp(x), O, len(ts))
+    check()
+    return outs
 
 
 def gemv_rows_batch(t, x, r0, r1):

@@ -139,3 +139,32 @@ def test_ops_against_reference(name, n):
         np.testing.assert_array_equal(got, ref)   # polynomial exp restated exactly
     else:
         np.testing.assert_allclose(got, ref, rtol=2e-6, atol=1e-7)
+
+
+@pytest.mark.parametrize("n", [1, 3, 8, 11])
+def test_gemv_multi_batch_one_dispatch(n):
+    """gemv_multi_batch (include/kernels.h:32-34): every matrix reads the same x,
+    the formats differ, n above QB_MAX_TOK runs in chunks.  Each output is
+    bit-identical to a separate gemv_batch call (the reference's invariant,
+    src/kernels.c:650-655) and matches the compiled reference."""
+    K = 1024
+    spec = [(qb.GGML_IQ4_XS, 300), (qb.GGML_Q6_K, 520), (qb.GGML_Q8_0, 64), (qb.GGML_IQ4_XS, 48)]
+    raws = [qb.synth_matrix(g, r, K, seed=40 + i, d_sigma=0.01) for i, (g, r) in enumerate(spec)]
+    ts = [qb.tensor(raw, g, K, r) for raw, (g, r) in zip(raws, spec)]
+    x = qb.synth_normal(n * K, seed=77 + n).reshape(n, K)
+    outs = qb.gemv_multi_batch(ts, x)
+    for raw, (g, r), t, o in zip(raws, spec, ts, outs):
+        np.testing.assert_array_equal(o, qb.gemv_batch(t, x))
+        ref = oracle.ref_gemv_batch(raw, g, K, r, x)
+        assert rel(o, ref) < RTOL
+
+
+def test_gemv_multi_single_vector_and_limits():
+    K = 512
+    raws = [qb.synth_matrix(qb.GGML_IQ4_XS, 64 + 32 * i, K, seed=i, d_sigma=0.01) for i in range(3)]
+    ts = [qb.tensor(raw, qb.GGML_IQ4_XS, K, 64 + 32 * i) for i, raw in enumerate(raws)]
+    x = qb.synth_normal(K, seed=5)
+    for o, t in zip(qb.gemv_multi(ts, x), ts):
+        np.testing.assert_array_equal(o, qb.gemv_batch(t, x[None])[0])
+    with pytest.raises(RuntimeError, match="at most 8"):
+        qb.gemv_multi(ts * 3, x)
