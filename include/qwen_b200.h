@@ -187,6 +187,27 @@ void sigmoid_inplace(float *x, uint64_t n);
 void softplus_inplace(float *x, uint64_t n);
 void softmax_inplace(float *x, uint64_t n);
 
+/* ---- include/sampler.h (non-greedy sampling, src/sampler.c:49-162) ----
+ * Same struct, names and behaviour; the draw runs on the GPU.  sampler_sample
+ * takes HOST logits as the reference does, penalises them in place (the same
+ * float operations, copied back) and advances s->rng_state.  A seeded stream
+ * gives the reference's tokens: each term's exp is the correctly rounded one
+ * (the reference uses glibc's expf, one ulp away on about 0.06 % of inputs),
+ * and exact ties inside the top-k list are taken in index order. */
+#ifndef SAMPLER_H
+typedef struct {
+    float temp;
+    float top_p;
+    uint32_t top_k;
+    float repeat_penalty;
+    uint32_t repeat_last_n;
+    uint64_t rng_state;
+} sampler_t;
+#endif
+sampler_t *sampler_init(float temp, float top_p, uint32_t top_k, float repeat_penalty, uint64_t seed);
+void sampler_free(sampler_t *s);
+uint32_t sampler_sample(sampler_t *s, float *logits, uint32_t vocab_size, const uint32_t *tokens, size_t n_tokens);
+
 /* include/model.h:151-152: per-section timers of the CPU engine's
  * model_forward.  Exported so reference callers (src/main.c:256-263) link; the
  * device engine leaves them at zero and qwen_prof_calls at 0, so the CLI skips
@@ -222,6 +243,16 @@ int qb_spec_generate(qwen_model_t *m, uint32_t n_predict, uint32_t n_spec, const
  * n_predict-1 single-token forwards, each fed its own device argmax.
  * Returns the number of tokens, or -1. */
 int qb_greedy_generate(qwen_model_t *m, uint32_t n_predict, uint32_t *out_tokens);
+
+/* src/main.c:232-248 with a sampler (temperature / top-k / top-p / repetition
+ * penalty): token 0 is drawn from m->logits, then n_predict-1 forwards, each
+ * followed by a draw on the device, with no host round trip per token.
+ * tokens[0..n_tokens) is the history the repetition penalty sees (the prompt
+ * and earlier output); s->rng_state advances as sampler_sample's would, and
+ * m->logits holds the last forward's logits as the last draw left them.
+ * Returns the number of tokens, or -1. */
+int qb_sample_generate(qwen_model_t *m, sampler_t *s, uint32_t n_predict, const uint32_t *tokens,
+                       size_t n_tokens, uint32_t *out_tokens);
 
 /* Device argmax of the last model_forward_batch row b (no host scan). */
 uint32_t qb_last_argmax(qwen_model_t *m, uint32_t b);

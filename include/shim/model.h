@@ -7,5 +7,6 @@
 #define QWEN_B200_SHIM_MODEL_H
 #include "gguf.h"
 #include "threadpool.h"
+#include "sampler.h"
 #include "qwen_b200.h"
 #endif

@@ -13,6 +13,8 @@
  *                           PREFILL_MAX_B, + mtp_forward_batch when spec on)
  *   ref_spec_generate    <- src/main.c:158-225 (greedy MTP speculation), plus
  *                           an optional forced accept length per cycle
+ *   ref_sample_generate  <- src/main.c:232-248 with a sampler (sampler_sample
+ *                           after each model_forward; EOS omitted)
  *   ref_greedy_generate  <- src/main.c:232-248 with temperature 0 (the
  *                           sampler's greedy branch is an argmax, identical to
  *                           model_sample_greedy, src/model.c:746-756)
@@ -21,6 +23,7 @@
 #define _POSIX_C_SOURCE 200809L
 #include "model.h"
 #include "kernels.h"
+#include "sampler.h"
 #include "quant.h"
 #include <stdio.h>
 #include <stdlib.h>
@@ -226,4 +229,23 @@ double ref_now(void) {
     struct timespec ts;
     clock_gettime(CLOCK_MONOTONIC, &ts);
     return (double)ts.tv_sec + (double)ts.tv_nsec * 1e-9;
+}
+
+uint32_t ref_sample_generate(ref_t *r, sampler_t *smp, uint32_t n_predict, uint32_t *all_tokens, uint32_t n_all,
+                             uint32_t *out_tokens) {
+    qwen_model_t *m = &r->m;
+    const uint32_t V = m->cfg.vocab_size;
+    if (n_predict == 0) return 0;
+    uint32_t cur = sampler_sample(smp, m->logits, V, all_tokens, n_all);
+    all_tokens[n_all++] = cur;
+    out_tokens[0] = cur;
+    uint32_t generated = 1;
+    for (uint32_t i = 1; i < n_predict; i++) {
+        if (m->pos >= m->n_ctx) break;
+        model_forward(m, r->pool, cur, m->pos);
+        cur = sampler_sample(smp, m->logits, V, all_tokens, n_all);
+        all_tokens[n_all++] = cur;
+        out_tokens[generated++] = cur;
+    }
+    return generated;
 }

@@ -78,6 +78,13 @@ def ref():
         L.dequant_row.argtypes = [i32, vp, C.c_uint64, P(f32)]
         L.dequant_row.restype = i32
         L.ref_spec_max_b.restype = i32
+        L.sampler_init.argtypes = [f32, f32, u32, f32, C.c_uint64]
+        L.sampler_init.restype = vp
+        L.sampler_free.argtypes = [vp]
+        L.sampler_sample.argtypes = [vp, P(f32), u32, P(u32), C.c_size_t]
+        L.sampler_sample.restype = u32
+        L.ref_sample_generate.argtypes = [vp, vp, u32, P(u32), u32, P(u32)]
+        L.ref_sample_generate.restype = u32
         for n in ("rmsnorm",):
             getattr(L, n).argtypes = [P(f32), P(f32), P(f32), C.c_uint64, f32]
         L.l2norm.argtypes = [P(f32), P(f32), C.c_uint64, f32]
@@ -180,10 +187,39 @@ class RefModel:
                                     _up(js), max_cycles, C.byref(nc))
         return out[:n].copy(), js[:nc.value].copy()
 
+    def sample_generate(self, sampler, n_predict, history):
+        """src/main.c:232-248 with the reference sampler (RefSampler)."""
+        h = np.zeros(len(history) + n_predict + 1, np.uint32)
+        h[:len(history)] = history
+        out = np.zeros(n_predict + 1, np.uint32)
+        n = ref().ref_sample_generate(self.h, sampler.s, n_predict, _up(h), len(history), _up(out))
+        return out[:n].copy()
+
     def greedy_generate(self, n_predict):
         out = np.zeros(n_predict + 1, np.uint32)
         n = ref().ref_greedy_generate(self.h, n_predict, _up(out))
         return out[:n].copy()
+
+
+class RefSampler:
+    """The reference sampler (src/sampler.c) itself, from oracle/_ref."""
+
+    def __init__(self, temp, top_p, top_k, repeat_penalty, seed):
+        self.s = ref().sampler_init(temp, top_p, top_k, repeat_penalty, seed)
+
+    @property
+    def rng_state(self):
+        # sampler_t: float, float, u32, float, u32, (pad), u64
+        return C.c_uint64.from_address(self.s + 24).value
+
+    def sample(self, logits, tokens):
+        t = np.ascontiguousarray(tokens, np.uint32)
+        return ref().sampler_sample(self.s, _fp(logits), logits.size, _up(t) if t.size else None, t.size)
+
+    def close(self):
+        if self.s:
+            ref().sampler_free(self.s)
+            self.s = None
 
 
 def ref_gemv_batch(data, gtype, ne0, ne1, x, n_threads=0):

@@ -18,7 +18,7 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 
-CU_SOURCES = ["qb_quant.cu", "qb_qmv_tc.cu", "qb_layers.cu", "qb_engine.cu"]
+CU_SOURCES = ["qb_quant.cu", "qb_qmv_tc.cu", "qb_layers.cu", "qb_sample.cu", "qb_engine.cu"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",

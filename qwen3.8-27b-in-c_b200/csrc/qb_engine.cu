@@ -468,6 +468,11 @@ struct Engine {
     int g_cycle_k = -1;
     size_t cycle_kernels = 0;
     cudaGraphExec_t g_greedy = nullptr;
+    cudaGraphExec_t g_sample = nullptr;   // forward + sampling step (qb_sample_generate)
+    QbSampDev* samp = nullptr;            // sampler parameters, history and generator on the device
+    unsigned long long* samp_cand = nullptr;
+    unsigned long long* samp_keys = nullptr;
+    uint32_t* samp_am = nullptr;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     float last_ms = 0.f;
     bool any_q45 = false;
@@ -498,6 +503,7 @@ Engine::~Engine() {
         }
     if (g_cycle) cudaGraphExecDestroy(g_cycle);
     if (g_greedy) cudaGraphExecDestroy(g_greedy);
+    if (g_sample) cudaGraphExecDestroy(g_sample);
     if (ev0) cudaEventDestroy(ev0);
     if (ev1) cudaEventDestroy(ev1);
     for (void* p : allocs) cudaFree(p);
@@ -1361,6 +1367,26 @@ int capture(Engine& e, cudaGraphExec_t* out, int (*rec)(Engine&, int), int arg) 
     return 0;
 }
 
+// sampling decode step: the token just sampled goes out and feeds the next forward
+__global__ void sample_step_kernel(QbCtrl* c, const QbSampDev* sd, uint32_t* out_tok, int advance) {
+    pdl_wait();
+    pdl_trigger();
+    const uint32_t t = sd->token;
+    if (c->greedy_n < c->cap_out) out_tok[c->greedy_n] = t;
+    c->greedy_n += 1;
+    c->fwd_tok[0] = t;
+    if (advance) c->fwd_pos += 1;
+}
+
+// one step of src/main.c:241-242: forward of the previous token, then sample
+int record_sample(Engine& e, int) {
+    if (fwd_backbone(e, 1, 0, false)) return -1;   // every rank holds the whole logit row
+    CK(qb_sample(e.logits, e.V, e.samp, e.samp_cand, e.samp_keys, e.samp_am, e.st));
+    CK(qb_launch(sample_step_kernel, dim3(1), dim3(1), 0, e.st, e.ctrl, (const QbSampDev*)e.samp, e.d_out_tok, 1));
+    CK(cudaGetLastError());
+    return 0;
+}
+
 int record_greedy(Engine& e, int) {
     if (fwd_backbone(e, 1, 0, true)) return -1;
     CK(qb_launch(greedy_step_kernel, dim3(1), dim3(1), 0, e.st, e.ctrl, e.d_out_tok));
@@ -1395,6 +1421,7 @@ int ensure_out_buffers(Engine& e, uint32_t n_out, uint32_t n_j, uint32_t n_force
         // buffers captured in graphs: re-capture after reallocation
         if (e.g_cycle) { cudaGraphExecDestroy(e.g_cycle); e.g_cycle = nullptr; }
         if (e.g_greedy) { cudaGraphExecDestroy(e.g_greedy); e.g_greedy = nullptr; }
+        if (e.g_sample) { cudaGraphExecDestroy(e.g_sample); e.g_sample = nullptr; }
         const uint32_t co = std::max(n_out, std::max(e.cap_out, 4096u));
         const uint32_t cj = std::max(n_j, std::max(e.cap_j, 4096u));
         const uint32_t cf = std::max(n_forced, std::max(e.cap_forced, 1024u));
@@ -2307,6 +2334,136 @@ extern "C" uint32_t model_sample_greedy(const float* logits, uint32_t vocab_size
         return 0;
     }
     return r;
+}
+
+// ------------------------------ sampling ------------------------------------
+// sampler_* keep the names, fields and behaviour of include/sampler.h /
+// src/sampler.c; the draw itself runs on the device (qb_sample.cu).
+
+namespace {
+// device sampler state from the host sampler and the token history (its last
+// QB_SAMP_HIST tokens land at their ring positions)
+QbSampDev samp_state(const sampler_t* s, const uint32_t* tokens, size_t n_tokens) {
+    QbSampDev h{};
+    h.temp = s->temp;
+    h.top_p = s->top_p;
+    h.top_k = s->top_k;
+    h.repeat_penalty = s->repeat_penalty;
+    h.repeat_last_n = s->repeat_last_n;
+    h.rng = s->rng_state;
+    h.n_hist = tokens ? (uint32_t)n_tokens : 0u;
+    const size_t m = h.n_hist < QB_SAMP_HIST ? h.n_hist : QB_SAMP_HIST;
+    for (size_t i = h.n_hist - m; i < h.n_hist; ++i) h.hist[i % QB_SAMP_HIST] = tokens[i];
+    return h;
+}
+
+int samp_alloc(QbSampDev*& sd, unsigned long long*& cand, unsigned long long*& keys, uint32_t*& am, int V) {
+    if (sd) return 0;
+    CK(cudaMalloc(&sd, sizeof(QbSampDev)));
+    CK(cudaMalloc(&cand, (size_t)qb_sample_lists(V) * 256 * sizeof(unsigned long long)));
+    CK(cudaMalloc(&keys, 2 * sizeof(unsigned long long)));
+    CK(cudaMalloc(&am, 2 * sizeof(uint32_t)));
+    return 0;
+}
+struct HostSamp {
+    QbSampDev* sd = nullptr;
+    unsigned long long *cand = nullptr, *keys = nullptr;
+    uint32_t* am = nullptr;
+    int V = 0;
+};
+std::unordered_map<int, HostSamp> g_hsamp;   // per device, for sampler_sample
+}  // namespace
+
+extern "C" sampler_t* sampler_init(float temp, float top_p, uint32_t top_k, float repeat_penalty, uint64_t seed) {
+    sampler_t* s = (sampler_t*)calloc(1, sizeof(sampler_t));
+    if (!s) return nullptr;
+    s->temp = temp;
+    s->top_p = top_p;
+    s->top_k = top_k == 0 ? 40 : top_k;
+    s->repeat_penalty = repeat_penalty <= 0.0f ? 1.0f : repeat_penalty;
+    s->repeat_last_n = 64;
+    s->rng_state = seed == 0 ? 0x123456789abcdefULL : seed;
+    return s;
+}
+
+extern "C" void sampler_free(sampler_t* s) { free(s); }
+
+// Host logits, as the reference: they are penalised in place (the same float
+// operations, done on the device and copied back) and s->rng_state advances.
+extern "C" uint32_t sampler_sample(sampler_t* s, float* logits, uint32_t vocab_size, const uint32_t* tokens,
+                                   size_t n_tokens) {
+    if (!s || !logits || vocab_size == 0) return 0;
+    std::lock_guard<std::mutex> lk(g_mu);
+    Scratch* sc = nullptr;
+    if (scratch_get(sc, vocab_size, 1, 0)) return 0;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) { set_err(-2, "sampler_sample: no device"); return 0; }
+    HostSamp& hs = g_hsamp[dev];
+    if (hs.sd && hs.V < (int)vocab_size) {   // the candidate lists grow with the vocabulary
+        cudaFree(hs.sd); cudaFree(hs.cand); cudaFree(hs.keys); cudaFree(hs.am);
+        hs = HostSamp();
+    }
+    if (samp_alloc(hs.sd, hs.cand, hs.keys, hs.am, (int)vocab_size)) return 0;
+    hs.V = std::max(hs.V, (int)vocab_size);
+    const QbSampDev h = samp_state(s, tokens, n_tokens);
+    const bool penal = s->repeat_penalty != 1.0f && tokens && n_tokens > 0;
+    QbSampDev out;
+    if (cudaMemcpyAsync(sc->x, logits, (size_t)vocab_size * 4, cudaMemcpyHostToDevice, sc->st) != cudaSuccess ||
+        cudaMemcpyAsync(hs.sd, &h, sizeof h, cudaMemcpyHostToDevice, sc->st) != cudaSuccess ||
+        qb_sample(sc->x, (int)vocab_size, hs.sd, hs.cand, hs.keys, hs.am, sc->st) != cudaSuccess ||
+        cudaMemcpyAsync(&out, hs.sd, sizeof out, cudaMemcpyDeviceToHost, sc->st) != cudaSuccess ||
+        (penal && cudaMemcpyAsync(logits, sc->x, (size_t)vocab_size * 4, cudaMemcpyDeviceToHost, sc->st) != cudaSuccess) ||
+        cudaStreamSynchronize(sc->st) != cudaSuccess) {
+        set_err(-2, "sampler_sample: CUDA failure");
+        return 0;
+    }
+    s->rng_state = out.rng;
+    return out.token;
+}
+
+// src/main.c:232-248 with a sampler: token 0 = sample(m->logits), then
+// n_predict - 1 steps of forward + sample, all on the device.  tokens /
+// n_tokens: the history the repetition penalty sees (prompt and anything
+// generated before); the new tokens extend it.
+extern "C" int qb_sample_generate(qwen_model_t* m, sampler_t* s, uint32_t n_predict, const uint32_t* tokens,
+                                  size_t n_tokens, uint32_t* out_tokens) {
+    Engine* e = E_(m);
+    if (!e || !s || !out_tokens || m->pos == 0) { set_err(-1, "qb_sample_generate: bad arguments"); return -1; }
+    if (n_predict == 0) return 0;
+    CK(cudaSetDevice(e->dev));
+    if (ensure_out_buffers(*e, n_predict + 1, 1, 1)) return -1;
+    if (samp_alloc(e->samp, e->samp_cand, e->samp_keys, e->samp_am, e->V)) return -1;
+    if (!e->g_sample && capture(*e, &e->g_sample, record_sample, 0)) return -1;
+    const QbSampDev h = samp_state(s, tokens, n_tokens);
+    QbCtrl hc;
+    CK(cudaMemcpyAsync(&hc, e->ctrl, sizeof hc, cudaMemcpyDeviceToHost, e->st));
+    if (dev_sync(*e)) return -1;
+    hc.fwd_pos = m->pos;
+    hc.greedy_n = 0;
+    hc.cap_out = e->cap_out;
+    CK(cudaMemcpyAsync(e->ctrl, &hc, sizeof hc, cudaMemcpyHostToDevice, e->st));
+    CK(cudaMemcpyAsync(e->samp, &h, sizeof h, cudaMemcpyHostToDevice, e->st));
+    // the logits the caller holds (the last forward's, possibly edited) are the first draw's
+    CK(cudaMemcpyAsync(e->logits, m->logits, (size_t)e->V * 4, cudaMemcpyHostToDevice, e->st));
+    CK(qb_sample(e->logits, e->V, e->samp, e->samp_cand, e->samp_keys, e->samp_am, e->st));
+    CK(qb_launch(sample_step_kernel, dim3(1), dim3(1), 0, e->st, e->ctrl, (const QbSampDev*)e->samp, e->d_out_tok, 0));
+    uint32_t steps = n_predict - 1;
+    if (m->pos + steps > (uint32_t)e->n_ctx) steps = (uint32_t)e->n_ctx - m->pos;
+    CK(cudaEventRecord(e->ev0, e->st));
+    for (uint32_t i = 0; i < steps; ++i) CK(cudaGraphLaunch(e->g_sample, e->st));
+    CK(cudaEventRecord(e->ev1, e->st));
+    CK(cudaEventSynchronize(e->ev1));
+    cudaEventElapsedTime(&e->last_ms, e->ev0, e->ev1);
+    const uint32_t n = steps + 1;
+    QbSampDev out;
+    CK(cudaMemcpyAsync(out_tokens, e->d_out_tok, (size_t)n * 4, cudaMemcpyDeviceToHost, e->st));
+    CK(cudaMemcpyAsync(&out, e->samp, sizeof out, cudaMemcpyDeviceToHost, e->st));
+    // the logits the reference leaves: the last forward's, penalised by the last draw
+    CK(cudaMemcpyAsync(m->logits, e->logits, (size_t)e->V * 4, cudaMemcpyDeviceToHost, e->st));
+    if (dev_sync(*e)) return -1;
+    s->rng_state = out.rng;
+    m->pos += steps;
+    return (int)n;
 }
 
 // ---------------------- allocation-free greedy argmax -------------------------

@@ -198,3 +198,23 @@ cudaError_t qb_op_rmsnorm(float* out, const float* x, const float* w, long long 
 cudaError_t qb_op_l2norm(float* out, const float* x, long long n, float eps, cudaStream_t st);
 cudaError_t qb_op_act(int which, float* x, long long n, cudaStream_t st);   // 0 silu 1 sigmoid 2 softplus
 cudaError_t qb_op_softmax(float* x, long long n, cudaStream_t st);
+
+// ---- non-greedy sampling (qb_sample.cu; src/sampler.c:61-162) ----
+#define QB_SAMP_HIST 64   // history ring: the reference penalises at most the last 64 tokens
+struct QbSampDev {
+    float temp, top_p;
+    uint32_t top_k;
+    float repeat_penalty;
+    uint32_t repeat_last_n;
+    uint32_t n_hist;                 // tokens appended so far (the ring holds the last QB_SAMP_HIST)
+    unsigned long long rng;          // xorshift64 state
+    uint32_t hist[QB_SAMP_HIST];
+    uint32_t token;                  // the last sampled token
+};
+// blocks of the top-K pass over a vocabulary of V (candidate lists of 256 keys each)
+int qb_sample_lists(int V);
+// Samples from logits[0..V) (penalised in place) with the parameters, history
+// and generator in sd; the token lands in sd->token and the history.  cand:
+// qb_sample_lists(V) x 256 keys; keys / am: one argmax key and index.
+cudaError_t qb_sample(float* logits, int V, QbSampDev* sd, unsigned long long* cand, unsigned long long* keys,
+                      uint32_t* am, cudaStream_t st);

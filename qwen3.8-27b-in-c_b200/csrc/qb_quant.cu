@@ -598,6 +598,22 @@ __device__ __forceinline__ void pair_final(const QmvK& p, int pair, float (&v)[2
                 if (tok < p.N) p.epi_h[(size_t)tok * p.epi_ldh + j] = __fmul_rn(silu_ref(v[0][i]), v[1][i]);
             }
     } else if (active) {
+        // residual launches: every old value is loaded before the first store, so the
+        // eight loads overlap instead of each waiting behind the previous store (the
+        // stores may alias them, so the compiler keeps the order it is given)
+        float prev[2][4];
+        if (p.accumulate && !(TP && !p.tp.gather)) {
+#pragma unroll
+            for (int t = 0; t < 2; ++t)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int rr = lp * 32 + t * 16 + g + ((i & 2) ? 8 : 0);
+                    const int tok = (i & 1) ? t1 : t0;
+                    prev[t][i] = (tok < p.N && rr < S.rows && rr >= p.row_lo && rr < p.row_hi)
+                                     ? __ldcg(S.out + (size_t)tok * S.ldo + rr)
+                                     : 0.f;
+                }
+        }
 #pragma unroll
         for (int t = 0; t < 2; ++t)
 #pragma unroll
@@ -614,7 +630,7 @@ __device__ __forceinline__ void pair_final(const QmvK& p, int pair, float (&v)[2
                         *w = make_uint2(__float_as_uint(v[t][i]), sq + 1u);
                         continue;
                     }
-                    const float y = p.accumulate ? (__ldcg(dst) + v[t][i]) : v[t][i];
+                    const float y = p.accumulate ? prev[t][i] + v[t][i] : v[t][i];
                     *dst = y;
                     if (TP && p.tp.gather)
                         for (int q = 0; q < p.tp.np; ++q)

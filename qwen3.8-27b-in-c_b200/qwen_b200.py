@@ -30,7 +30,7 @@ EXPORTED = [
     "qb_last_error", "qb_last_error_str", "qb_clear_error", "qb_prefill", "qb_spec_generate",
     "qb_greedy_generate", "qb_last_argmax", "qb_last_loop_ms", "qb_read_state", "qb_read_buffer",
     "qb_reset", "qb_bench", "qb_model_init_tp", "qb_tp_handle", "qb_tp_connect", "qb_tp_rows",
-    "qb_argmax_rows_noalloc",
+    "qb_argmax_rows_noalloc", "sampler_init", "sampler_free", "sampler_sample", "qb_sample_generate",
 ]
 
 
@@ -67,6 +67,12 @@ class QwenModel(C.Structure):
                 ("x", C.POINTER(C.c_float)), ("logits", C.POINTER(C.c_float)),
                 ("logits_b", C.POINTER(C.c_float)), ("h_save", C.POINTER(C.c_float)),
                 ("n_ctx", C.c_uint32), ("pos", C.c_uint32), ("eng", C.c_void_p)]
+
+
+class SamplerT(C.Structure):
+    """sampler_t (reference include/sampler.h:7-14)."""
+    _fields_ = [("temp", C.c_float), ("top_p", C.c_float), ("top_k", C.c_uint32), ("repeat_penalty", C.c_float),
+                ("repeat_last_n", C.c_uint32), ("rng_state", C.c_uint64)]
 
 
 _lib = None
@@ -136,6 +142,13 @@ def lib():
         L.qb_tp_rows.restype = None
         L.qb_argmax_rows_noalloc.argtypes = [vp, C.c_int64, u32, u32, vp, vp]
         L.qb_argmax_rows_noalloc.restype = i32
+        L.sampler_init.argtypes = [f32, f32, u32, f32, C.c_uint64]
+        L.sampler_init.restype = P(SamplerT)
+        L.sampler_free.argtypes = [P(SamplerT)]
+        L.sampler_sample.argtypes = [P(SamplerT), P(f32), u32, P(u32), C.c_size_t]
+        L.sampler_sample.restype = u32
+        L.qb_sample_generate.argtypes = [P(QwenModel), P(SamplerT), u32, P(u32), C.c_size_t, P(u32)]
+        L.qb_sample_generate.restype = i32
         _lib = L
     return _lib
 
@@ -225,6 +238,37 @@ def argmax_rows_noalloc(logits_ptr, ld, n, rows, out_ptr, stream_ptr=None):
     if rc:
         check()
     return rc
+
+
+class Sampler:
+    """sampler_init / sampler_sample / sampler_free (include/sampler.h) on the GPU."""
+
+    def __init__(self, temp, top_p, top_k, repeat_penalty, seed):
+        self.s = lib().sampler_init(temp, top_p, top_k, repeat_penalty, seed)
+        if not self.s:
+            raise RuntimeError("sampler_init failed")
+
+    @property
+    def rng_state(self):
+        return self.s.contents.rng_state
+
+    def sample(self, logits, tokens):
+        """Returns the token; logits (float32 numpy) are penalised in place."""
+        t = np.ascontiguousarray(tokens, np.uint32)
+        r = lib().sampler_sample(self.s, _fp(logits), logits.size, _up(t) if t.size else None, t.size)
+        check()
+        return r
+
+    def close(self):
+        if self.s:
+            lib().sampler_free(self.s)
+            self.s = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def op(name, x, w=None, eps=1e-6):
@@ -371,6 +415,18 @@ class Model:
         if n < 0:
             check()
             raise RuntimeError("qb_greedy_generate failed")
+        return out[:n].copy()
+
+    def sample_generate(self, sampler, n_predict, history):
+        """qb_sample_generate: n_predict tokens drawn on the device (history: the
+        tokens the repetition penalty sees)."""
+        out = np.zeros(n_predict + 1, np.uint32)
+        h = np.ascontiguousarray(history, np.uint32)
+        n = lib().qb_sample_generate(C.byref(self.m), sampler.s, n_predict, _up(h) if h.size else None, h.size,
+                                     _up(out))
+        if n < 0:
+            check()
+            raise RuntimeError("qb_sample_generate failed")
         return out[:n].copy()
 
     def reset(self):
