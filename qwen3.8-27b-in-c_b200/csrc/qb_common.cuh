@@ -82,6 +82,27 @@ __device__ __forceinline__ float small_u2f(uint32_t v) {
     return __int_as_float(0x4B000000u | v) - 8388608.0f;
 }
 
+// ---- waits on other ranks ----
+// A wait on a peer gives up after kPeerWaitNs of wall-clock time (%globaltimer),
+// or at once when the error word already records a failed wait, so that a
+// rank that stopped taking part costs one bound, not one per exchange.
+constexpr unsigned long long kPeerWaitNs = 2000000000ull;
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// true: stop waiting (the error word is set, to code when this wait ran out)
+__device__ __forceinline__ bool peer_wait_over(uint32_t it, unsigned long long t0, unsigned* err, unsigned code) {
+    if (it & 63u) return false;
+    if (*(volatile unsigned*)err) return true;
+    if (global_ns() - t0 > kPeerWaitNs) {
+        atomicExch(err, code);
+        return true;
+    }
+    return false;
+}
+
 // ---- programmatic dependent launch (PDL) ----
 // Every kernel calls pdl_wait() before it touches data written by (or read
 // by) the kernel before it on the stream, and pdl_trigger() once it no longer

@@ -704,12 +704,12 @@ __global__ void tp_argmax_kernel(const unsigned long long* __restrict__ keys, in
         for (int r = 0; r < x.world && ok; ++r) {
             const unsigned long long* src = x.xk + 2 * (((size_t)(s & 1u) * QB_TP_MAX + r) * QB_MAX_TOK + b);
             unsigned long long v0, v1;
+            const unsigned long long t0 = global_ns();
             for (uint32_t it = 0;; ++it) {
                 asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v0) : "l"(src) : "memory");
                 asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v1) : "l"(src + 1) : "memory");
                 if ((unsigned)v0 == s && (unsigned)v1 == s) break;
-                if (it >= (1u << 24)) {
-                    atomicExch(x.err, 4u);
+                if (peer_wait_over(it, t0, x.err, 4u)) {
                     ok = false;
                     break;
                 }

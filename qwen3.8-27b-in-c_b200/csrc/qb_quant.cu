@@ -810,14 +810,12 @@ __device__ __noinline__ void tp_arrive(TpK t, uint32_t s_arrive, int lane) {
     for (int q = 0; q < t.np; ++q) {
         const int peer = q < t.rank ? q : q + 1;
         const unsigned* f = t.flags + peer;
+        const unsigned long long t0 = global_ns();
         for (uint32_t it = 0;; ++it) {
             unsigned v;
             asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
             if ((int)(v - seq) >= 0) break;
-            if (it >= (1u << 24)) {
-                atomicExch(t.err, 4u);
-                return;
-            }
+            if (peer_wait_over(it, t0, t.err, 4u)) return;
             __nanosleep(64);
         }
     }
@@ -1037,14 +1035,12 @@ __global__ void __launch_bounds__(256) tp_reduce_kernel(float* __restrict__ x, l
     for (int q = 0; q < r.world; ++q) {
         const uint4* src = reinterpret_cast<const uint4*>(r.part[q] + pe);
         uint4 v;
+        const unsigned long long t0 = global_ns();
         for (uint32_t it = 0;; ++it) {
             asm volatile("ld.volatile.global.v4.u32 {%0,%1,%2,%3}, [%4];"
                          : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(src) : "memory");
             if (v.y == sq && v.w == sq) break;
-            if (it >= (1u << 22)) {
-                atomicExch(r.err, 4u);
-                return;
-            }
+            if (peer_wait_over(it, t0, r.err, 4u)) return;
             __nanosleep(32);
         }
         if (q == 0) {

@@ -142,3 +142,82 @@ def test_two_rank_tensor_parallel(tmp_path):
     bad = [(r, out[-2000:], err[-3000:]) for r, (pr, (out, err)) in enumerate(zip(procs, outs))
            if pr.returncode != 0 or f"tp ok {r}" not in out]
     assert not bad, bad
+
+
+LEAVE = r"""
+import os, sys, time, datetime
+import numpy as np
+sys.path.insert(0, {root!r})
+sys.path.insert(0, os.path.join({root!r}, "tests"))
+import torch, torch.distributed as dist
+from conftest import qb, oracle
+rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+torch.cuda.set_device(rank)
+dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=300))
+path = qb.write_synth_gguf(os.path.join({tmp!r}, f"small_{{rank}}.gguf"), qb.SMALL, seed=3)
+m = qb.Model(path, 128, rank, world)
+hs = [None] * world
+dist.all_gather_object(hs, m.tp_handle())
+m.tp_connect(hs)
+dist.barrier()
+p = np.random.default_rng(7).integers(0, qb.SMALL["vocab"], 12).astype(np.uint32)
+m.prefill(p, 0)
+first = m.greedy_generate(4)          # both ranks: a normal step
+dist.barrier()                        # no kernel of either rank in flight from here
+if rank == 1:
+    dist.barrier()                    # rank 1 leaves: it takes no further step (and keeps its memory)
+else:
+    t0 = time.time()
+    try:
+        m.greedy_generate(4)
+        raise SystemExit("rank 0: the step without its peer did not fail")
+    except RuntimeError as e:
+        msg = str(e)
+    waited = time.time() - t0
+    assert "tensor-parallel peer" in msg and "code 4" in msg, msg
+    assert waited < 60, waited        # bounded: about one 2 s wait, not one per exchange
+    # the context is still usable: device work through the C ABI and torch
+    K, rows = 1024, 96
+    raw = qb.synth_matrix(qb.GGML_IQ4_XS, rows, K, seed=1, d_sigma=0.01)
+    x = qb.synth_normal(2 * K, seed=2).reshape(2, K)
+    got = qb.gemv_batch(qb.tensor(raw, qb.GGML_IQ4_XS, K, rows), x)
+    want = oracle.port_gemv(raw, qb.GGML_IQ4_XS, K, x)
+    assert np.linalg.norm(got - want) / np.linalg.norm(want) < 1e-5
+    assert float(torch.arange(10, device="cuda", dtype=torch.float32).sum()) == 45.0
+    torch.cuda.synchronize()
+    print("waited", round(waited, 2), "first", first.tolist(), flush=True)
+    dist.barrier()
+m.close()                             # each rank frees its own memory after the other is done with it
+dist.destroy_process_group()
+print("leave ok", rank)
+"""
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
+def test_rank_leaves_between_steps(tmp_path):
+    """A rank that stops taking part between steps: the survivor's next
+    exchange gives up after its bounded wait, the call returns the error
+    (qb_last_error, code 4), and the device stays usable.  No GPU faults:
+    the leaving rank stays alive and keeps its memory mapped; only host
+    barriers (gloo) coordinate the ranks; no NVLink multicast is involved."""
+    code = LEAVE.format(root=ROOT, tmp=str(tmp_path))
+    port = str(_free_port())
+    procs = []
+    for r in range(2):
+        env = dict(os.environ, RANK=str(r), WORLD_SIZE="2", MASTER_ADDR="127.0.0.1", MASTER_PORT=port,
+                   NCCL_NVLS_ENABLE="0")
+        env.pop("QB_TC", None)
+        procs.append(subprocess.Popen([sys.executable, "-c", code], env=env, stdout=subprocess.PIPE,
+                                      stderr=subprocess.PIPE, text=True))
+    outs = []
+    for pr in procs:
+        try:
+            outs.append(pr.communicate(timeout=600))
+        except subprocess.TimeoutExpired:
+            for q in procs:
+                q.kill()
+            raise
+    bad = [(r, out[-2000:], err[-3000:]) for r, (pr, (out, err)) in enumerate(zip(procs, outs))
+           if pr.returncode != 0 or f"leave ok {r}" not in out]
+    assert not bad, bad
