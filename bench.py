@@ -210,9 +210,40 @@ def cpu_reference_run(path, n_threads, warmup, steps, time_budget=None):
         if time_budget and time.perf_counter() - t0 > time_budget:
             break
     dt = time.perf_counter() - t0
+    # C2's rate: plain greedy decode from where the cycles left off (one forward per token)
+    tg = time.perf_counter()
+    g = m.greedy_generate(4)
+    greedy_tps = (len(g) - 1) / (time.perf_counter() - tg)
     m.close()
-    stream = {"tokens": np.concatenate(all_t), "accept": np.concatenate(all_j), "prefill_logits": prefill_logits}
+    stream = {"tokens": np.concatenate(all_t), "accept": np.concatenate(all_j), "prefill_logits": prefill_logits,
+              "greedy_tok_s": greedy_tps}
     return toks / dt, f"{cycles} cycles ({toks} tokens) after {warmup} warm-up cycles, prompt {PROMPT_LEN}", stream
+
+
+def cpu_micro_c1(n_threads, reps=3):
+    """C1 on the reference's own gemv_batch (host cores): the 17408 x 5120
+    IQ4_XS matrix of the seeded generator, N = 1, 2, 4, GB/s of weight bytes
+    (page-cache warm: one untimed call first)."""
+    orc = _load("qb_oracle", os.path.join(ROOT, "oracle", "ref.py"))
+    if not orc.available():
+        return None
+    rows, K = 17408, 5120
+    raw = qb.synth_matrix(qb.GGML_IQ4_XS, rows, K, seed=0, d_sigma=0.02)
+    out = {}
+    for n in (1, 2, 4):
+        x = np.random.default_rng(n).standard_normal((n, K)).astype(np.float32)
+        orc.ref_gemv_batch(raw, qb.GGML_IQ4_XS, K, rows, x, n_threads)
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            orc.ref_gemv_batch(raw, qb.GGML_IQ4_XS, K, rows, x, n_threads)
+        t = (time.perf_counter() - t0) / reps
+        out[f"n{n}"] = {"ms": t * 1e3, "GB/s": raw.nbytes / t / 1e9}
+    return out
+
+
+def shards_of(world, tp):
+    """GPUs the weights are split over (each streams 1/shards of them)."""
+    return world if tp else 1
 
 
 def aggregate(ms, n_tok, tp, dist=None, device="cpu"):
@@ -341,6 +372,24 @@ def run_ours(args, rank, world, local_rank):
     ms_head, b_head = model.bench(3, 4, 20)
     ms_draft, b_draft = model.bench(2, 1, 10)
     ms_ver, b_ver = model.bench(0, 4, 10)        # verify step (64 layers + head, B=4)
+    ms_tok, b_tok = model.bench(0, 1, 10)        # one-token forward (64 layers + head): C2's bytes per token
+    c1 = {}
+    for n in (1, 2, 4):                          # C1: one 17408 x 5120 IQ4_XS matrix, rotated over 64 copies
+        ms_c1, b_c1 = model.bench(8, n, 5)
+        gbs = b_c1 / shards_of(world, tp) / (ms_c1 / 1e3) / 1e9
+        c1[f"n{n}"] = {"us": ms_c1 * 1e3, "GB/s": gbs, "frac": gbs / peaks()[0]}
+    # C2: 128-token prompt (plain prefill), then 256 greedy tokens on the device
+    gold = golden_full()
+    model.reset()
+    model.prefill(prompt_tokens(seq_rank), 0)
+    g_toks = model.greedy_generate(256)
+    ms_g = model.last_loop_ms()
+    c2_tps = (len(g_toks) - 1) / (ms_g / 1e3)
+    c2_gbs = b_tok / shards_of(world, tp) * c2_tps / 1e9
+    c2 = {"tok/s": c2_tps, "ms_per_token": ms_g / max(len(g_toks) - 1, 1), "GB/s": c2_gbs,
+          "frac": c2_gbs / peaks()[0], "bytes_per_token": b_tok,
+          "tokens_equal_golden": bool(gold is not None and seq_rank == 0 and
+                                      np.array_equal(g_toks[:len(gold["greedy"])], gold["greedy"]))}
     log(f"components gemv {ms_gemv:.4f} head {ms_head:.4f} draft {ms_draft:.3f} verify {ms_ver:.3f} ms")
     shards = world if tp else 1   # each GPU streams 1/shards of the weights
     gemv_gbs = b_gemv / shards / (ms_gemv / 1e3) / 1e9
@@ -355,6 +404,9 @@ def run_ours(args, rank, world, local_rank):
             if ref is not None:   # the reference's own stream on the same box, same inputs
                 parity["reference_live"] = stream_parity(stream_t, stream_j, ref["tokens"], ref["accept"])
                 parity["reference_live"]["prefill_logits_rel_l2"] = rel_l2(prefill_logits, ref["prefill_logits"])
+                c2["reference_cpu_tok/s"] = ref["greedy_tok_s"]
+            log("cpu reference C1 micro")
+            c1["reference_cpu"] = cpu_micro_c1(os.cpu_count())
         checks = [v for v in parity.values() if isinstance(v, dict)]
         parity["tokens_equal"] = bool(checks) and all(c["tokens_equal"] for c in checks) and \
             parity.get("ranks_agree", True)
@@ -379,6 +431,8 @@ def run_ours(args, rank, world, local_rank):
                          "peak_kind": peak_kind},
             "verify_step": {"ms": ms_ver, "bytes": b_ver, "bytes_per_gpu": b_ver / shards, "GB/s": ver_gbs,
                             "frac": ver_gbs / hbm},
+            "configs": {"C1 IQ4_XS 17408x5120 GEMV (64 rotated copies)": c1,
+                        "C2 greedy decode, prompt 128 + 256 tokens": c2},
             "draft_ms": ms_draft, "head_ms": ms_head,
             "head_GB/s": b_head / shards / (ms_head / 1e3) / 1e9,
             "clocks": clk.summary(),

@@ -1892,7 +1892,7 @@ extern "C" float qb_bench(qwen_model_t* m, int what, uint32_t arg, uint32_t iter
             b = mat_bytes(e->eh_proj) + mat_bytes(l.q) + mat_bytes(l.k) + mat_bytes(l.v) + mat_bytes(l.o) +
                 mat_bytes(l.ffn_gate) + mat_bytes(l.ffn_up) + mat_bytes(l.ffn_down) + mat_bytes(e->output);
         }
-    } else if (what == 1 || what == 3 || (what >= 5 && what <= 7)) {
+    } else if (what == 1 || what == 3 || (what >= 5 && what <= 8)) {
         if (arg < 1 || arg > QB_MAX_TOK) return -1.f;
         // one graph of the launches (all layers except for the head), replayed: no host launch gaps
         const int nl = what != 3 ? (int)e->L.size() : 1;
@@ -1923,6 +1923,13 @@ extern "C" float qb_bench(qwen_model_t* m, int what, uint32_t arg, uint32_t iter
                                                       2LL * en.d.n_kv_head * en.d.head_dim};
                             if (gemv_group(en, m3, o3, ld3, 3, en.E, a, 0)) return -1;
                         }
+                    } else if (wh == 8) {
+                        // one FFN up matrix alone (the 17408 x 5120 IQ4_XS micro)
+                        fresh_input(en);
+                        const DevMat* m1[1] = {&ly.ffn_up};
+                        float* o1[1] = {en.up};
+                        const long long ld1[1] = {en.F};
+                        if (!ly.ffn_up.w || gemv_group(en, m1, o1, ld1, 1, en.E, a, 0)) return -1;
                     } else if (wh == 1) {
                         // the FFN gate / up launch as the forward runs it
                         const LayerW& l = en.L[li];
@@ -1959,9 +1966,11 @@ extern "C" float qb_bench(qwen_model_t* m, int what, uint32_t arg, uint32_t iter
         cudaGraphExecDestroy(ge);
         iters *= (uint32_t)nl;
         const LayerW& l0 = e->L[0];
-        if (what == 1 || what == 3) {
-            b = what == 1 ? (double)(mat_bytes(l0.ffn_gate) + mat_bytes(l0.ffn_up)) : (double)mat_bytes(e->output);
-            b += (double)arg * e->E * 4 + (double)arg * (what == 1 ? 2.0 * e->F : e->V) * 4;
+        if (what == 1 || what == 3 || what == 8) {
+            b = what == 1   ? (double)(mat_bytes(l0.ffn_gate) + mat_bytes(l0.ffn_up))
+                : what == 8 ? (double)mat_bytes(l0.ffn_up)
+                            : (double)mat_bytes(e->output);
+            b += (double)arg * e->E * 4 + (double)arg * (what == 1 ? 2.0 * e->F : what == 8 ? e->F : e->V) * 4;
         } else {
             for (const LayerW& l : e->L) {   // the average launch over the layers
                 if (what == 5) b += mat_bytes(l.ffn_down);
