@@ -2091,6 +2091,7 @@ int scratch_get(Scratch*& s, size_t x_floats, size_t out_floats, int K) {
         if (s->xb.xq) cudaFree(s->xb.xq);
         if (s->xb.xqscale) cudaFree(s->xb.xqscale);
         if (s->xb.xtc) cudaFree(s->xb.xtc);
+        if (s->xb.xtc16) cudaFree(s->xb.xtc16);
         s->k_cap = std::max<size_t>((size_t)K, 4096);
         const int kc = (int)((s->k_cap + 255) / 256 * 256);
         CK(cudaMalloc(&s->xb.xfrag, qb_xfrag_bytes(kc)));
@@ -2098,7 +2099,9 @@ int scratch_get(Scratch*& s, size_t x_floats, size_t out_floats, int K) {
         CK(cudaMalloc(&s->xb.xq, qb_xq_bytes(kc)));
         CK(cudaMemset(s->xb.xq, 0, qb_xq_bytes(kc)));
         CK(cudaMalloc(&s->xb.xscale, QB_MAX_TOK * (kc / 256) * 4));
-        CK(cudaMalloc(&s->xb.xqscale, QB_MAX_TOK * (kc / 256) * 4));
+        CK(cudaMalloc(&s->xb.xqscale, QB_TC16_TOK * (kc / 256) * 4));   // the 16-token path's rows too
+        CK(cudaMalloc(&s->xb.xtc16, qb_xtc16_bytes(kc)));
+        CK(cudaMemset(s->xb.xtc16, 0, qb_xtc16_bytes(kc)));
         CK(cudaMalloc(&s->xb.xtc, qb_xtc_bytes(kc)));
         CK(cudaMemset(s->xb.xtc, 0, qb_xtc_bytes(kc)));
         CK(cudaMalloc(&s->xb.xsum, QB_MAX_TOK * (kc / 32) * 4));
@@ -2174,13 +2177,31 @@ int wcache_get(const gguf_tensor_info_t* W, const DevMat*& out) {
     return 0;
 }
 
+// the tcgen05 tile layout of an IQ4_XS matrix of the host API, repacked from
+// the caller's blocks on first use (the 16-token path reads it)
+int wcache_tc(const gguf_tensor_info_t* W, const DevMat* M) {
+    if (M->w_tc) return 0;
+    const size_t src_bytes = gguf_row_bytes((int)W->type, W->ne[0]) * W->ne[1];
+    void* tmp = nullptr;
+    void* dst = nullptr;
+    CK(cudaMalloc(&tmp, src_bytes));
+    CK(cudaMemcpy(tmp, W->data, src_bytes, cudaMemcpyHostToDevice));
+    CK(cudaMalloc(&dst, qb_repacked_bytes_tc(M->rows, M->K)));
+    CK(qb_repack_tc(tmp, M->rows, M->K, dst, 0));
+    CK(cudaDeviceSynchronize());
+    cudaFree(tmp);
+    const_cast<DevMat*>(M)->w_tc = dst;
+    return 0;
+}
+
 // out_i[t][r] = W_i x[t] for the n_mat matrices (all reading the same x), rows
 // [r0, r1) of each (r1 clamped to its rows), t < n, host x / outs.  One
-// dispatch: per chunk of up to QB_MAX_TOK vectors, one host-to-device copy of
-// x, one activation prep covering every format and width, one GEMV launch per
-// matrix queued back to back (each the launch a single-matrix call makes, so
-// the results are bit-identical to separate calls, as src/kernels.c:650-655
-// promises for the CPU), the device-to-host copies, one synchronisation.
+// dispatch: per chunk of vectors (QB_MAX_TOK, or QB_TC16_TOK for IQ4_XS above
+// QB_MAX_TOK vectors), one host-to-device copy of x, one activation prep
+// covering every format and width, one GEMV launch per matrix queued back to
+// back (each the launch a single-matrix call makes, so the results are
+// bit-identical to separate calls, as src/kernels.c:650-655 promises for the
+// CPU), the device-to-host copies, one synchronisation.
 int gemv_multi_host(const gguf_tensor_info_t* const* Ws, int n_mat, const float* x, uint64_t ldx, int n,
                     float* const* outs, const uint64_t* ldos, uint64_t r0, uint64_t r1) {
     if (!Ws || !x || !outs || !ldos || n < 1 || n_mat < 1 || n_mat > QB_GEMV_MULTI_MAX) {
@@ -2191,7 +2212,6 @@ int gemv_multi_host(const gguf_tensor_info_t* const* Ws, int n_mat, const float*
     const DevMat* M[QB_GEMV_MULTI_MAX];
     uint64_t lo[QB_GEMV_MULTI_MAX], hi[QB_GEMV_MULTI_MAX];
     int Kmax = 0;
-    size_t out_floats = 0;
     int need = 0;
     for (int i = 0; i < n_mat; ++i) {
         if (!Ws[i] || !outs[i]) { set_err(-1, "gemv: null matrix or output %d", i); return -1; }
@@ -2199,59 +2219,85 @@ int gemv_multi_host(const gguf_tensor_info_t* const* Ws, int n_mat, const float*
         Kmax = std::max(Kmax, M[i]->K);
         hi[i] = std::min<uint64_t>(r1, (uint64_t)M[i]->rows);
         lo[i] = std::min(r0, hi[i]);
-        out_floats += (size_t)std::min(n, QB_MAX_TOK) * M[i]->rows;
     }
     if (ldx < (uint64_t)Kmax) { set_err(-1, "gemv: ldx %llu < ne0 %d", (unsigned long long)ldx, Kmax); return -1; }
+    // more vectors than one mma.sync sweep takes: IQ4_XS matrices run 16 per sweep on
+    // tcgen05, the others 8 per sweep.  The path is a property of the matrix and n
+    // alone, so a matrix gives the same bits here as in its own gemv_batch call.
+    bool wide_of[QB_GEMV_MULTI_MAX];
+    for (int i = 0; i < n_mat; ++i) {
+        wide_of[i] = n > QB_MAX_TOK && M[i]->type == QB_IQ4_XS;
+        if (wide_of[i] && wcache_tc(Ws[i], M[i])) return -1;
+    }
     Scratch* s = nullptr;
-    for (int t0 = 0; t0 < n; t0 += QB_MAX_TOK) {
-        const int nn = std::min(QB_MAX_TOK, n - t0);
-        if (scratch_get(s, (size_t)nn * Kmax, out_floats, Kmax)) return -1;
-        CK(cudaMemcpy2DAsync(s->x, (size_t)Kmax * 4, x + (size_t)t0 * ldx, ldx * 4, (size_t)Kmax * 4, nn,
-                             cudaMemcpyHostToDevice, s->st));
-        need = 0;
-        for (int i = 0; i < n_mat; ++i) {
-            if (M[i]->type == QB_F32) continue;
-            const bool tc = M[i]->w_tc && nn <= 4 && host_tc();
-            need |= qb_xprep_needs(M[i]->type, nn, tc ? 1 : 0);
-            if (scratch_work(s, M[i]->rows)) return -1;
-        }
-        if (need) {
-            QbXIn in{s->x, Kmax, nullptr, Kmax};
-            CK(qb_xprep(&in, 1, nn, 1e-6f, s->xb, need, s->st));
-        }
-        float* o = s->out;
-        for (int i = 0; i < n_mat; ++i) {
-            const DevMat* W = M[i];
-            const int K = W->K;
-            const uint64_t a = lo[i], b = hi[i];
-            if (a < b) {
-                const int t_lo = (int)(a / (2 * QB_TILE)) * 2;   // start on a tile pair
-                if (W->type == QB_F32) {
-                    CK(qb_qmv_f32((const float*)W->w, W->rows, K, s->x, Kmax, nn, o, W->rows, 0, (int)a, (int)b, s->st));
-                } else if (W->w_tc && nn <= 4 && host_tc()) {
-                    const int T0 = (int)(a / 128);   // start on a 128-row tile
-                    QbQSeg seg;
-                    seg.w = (const uint8_t*)W->w_tc + (size_t)T0 * (K / 256) * qb_repacked_bytes_tc(128, 256);
-                    seg.out = o + (size_t)T0 * 128;
-                    seg.ldo = W->rows;
-                    seg.rows = (int)(b - (uint64_t)T0 * 128);
-                    CK(qb_qmv_tc(&seg, 1, K, nn, s->xb, 0, (int)(a - (uint64_t)T0 * 128), (int)(b - (uint64_t)T0 * 128),
-                                 s->work, s->st));
-                } else {
-                    QbQSeg seg;
-                    seg.w = (const uint8_t*)W->w + (size_t)t_lo * (K / qb_unit_cols(W->type)) * qb_unit_bytes(W->type);
-                    seg.out = o + (size_t)t_lo * QB_TILE;
-                    seg.ldo = W->rows;
-                    seg.rows = (int)(b - (uint64_t)t_lo * QB_TILE);
-                    CK(qb_qmv(W->type, &seg, 1, K, nn, s->xb, 0, (int)(a - (uint64_t)t_lo * QB_TILE),
-                              (int)(b - (uint64_t)t_lo * QB_TILE), s->work, s->st));
-                }
-                CK(cudaMemcpy2DAsync(outs[i] + (size_t)t0 * ldos[i] + a, ldos[i] * 4, o + a, (size_t)W->rows * 4,
-                                     (size_t)(b - a) * 4, nn, cudaMemcpyDeviceToHost, s->st));
+    for (int pass = 0; pass < 2; ++pass) {   // pass 0: 8-vector chunks, pass 1: 16-vector chunks
+        const bool wide = pass == 1;
+        bool any = false;
+        size_t of = 0;
+        for (int i = 0; i < n_mat; ++i)
+            if (wide_of[i] == wide) {
+                any = true;
+                of += (size_t)std::min(n, wide ? QB_TC16_TOK : QB_MAX_TOK) * M[i]->rows;
             }
-            o += (size_t)nn * W->rows;
+        if (!any) continue;
+        const int chunk = wide ? QB_TC16_TOK : QB_MAX_TOK;
+        for (int t0 = 0; t0 < n; t0 += chunk) {
+            const int nn = std::min(chunk, n - t0);
+            if (scratch_get(s, (size_t)nn * Kmax, of, Kmax)) return -1;
+            CK(cudaMemcpy2DAsync(s->x, (size_t)Kmax * 4, x + (size_t)t0 * ldx, ldx * 4, (size_t)Kmax * 4, nn,
+                                 cudaMemcpyHostToDevice, s->st));
+            need = 0;
+            for (int i = 0; i < n_mat; ++i) {
+                if (wide_of[i] != wide || M[i]->type == QB_F32) continue;
+                const bool tc = M[i]->w_tc && nn <= 4 && host_tc();
+                need |= wide ? QB_XP_TC16 : qb_xprep_needs(M[i]->type, nn, tc ? 1 : 0);
+                if (scratch_work(s, M[i]->rows)) return -1;
+            }
+            if (need) {
+                QbXIn in{s->x, Kmax, nullptr, Kmax};
+                CK(qb_xprep(&in, 1, nn, 1e-6f, s->xb, need, s->st));
+            }
+            float* o = s->out;
+            for (int i = 0; i < n_mat; ++i) {
+                if (wide_of[i] != wide) continue;
+                const DevMat* W = M[i];
+                const int K = W->K;
+                const uint64_t a = lo[i], b = hi[i];
+                if (a < b) {
+                    const int t_lo = (int)(a / (2 * QB_TILE)) * 2;   // start on a tile pair
+                    if (W->type == QB_F32) {
+                        CK(qb_qmv_f32((const float*)W->w, W->rows, K, s->x, Kmax, nn, o, W->rows, 0, (int)a, (int)b,
+                                      s->st));
+                    } else if (wide || (W->w_tc && nn <= 4 && host_tc())) {
+                        const int T0 = (int)(a / 128);   // start on a 128-row tile
+                        QbQSeg seg;
+                        seg.w = (const uint8_t*)W->w_tc + (size_t)T0 * (K / 256) * qb_repacked_bytes_tc(128, 256);
+                        seg.out = o + (size_t)T0 * 128;
+                        seg.ldo = W->rows;
+                        seg.rows = (int)(b - (uint64_t)T0 * 128);
+                        if (wide)
+                            CK(qb_qmv_tc16(&seg, 1, K, nn, s->xb, 0, (int)(a - (uint64_t)T0 * 128),
+                                           (int)(b - (uint64_t)T0 * 128), s->work, s->st));
+                        else
+                            CK(qb_qmv_tc(&seg, 1, K, nn, s->xb, 0, (int)(a - (uint64_t)T0 * 128),
+                                         (int)(b - (uint64_t)T0 * 128), s->work, s->st));
+                    } else {
+                        QbQSeg seg;
+                        seg.w = (const uint8_t*)W->w + (size_t)t_lo * (K / qb_unit_cols(W->type)) * qb_unit_bytes(W->type);
+                        seg.out = o + (size_t)t_lo * QB_TILE;
+                        seg.ldo = W->rows;
+                        seg.rows = (int)(b - (uint64_t)t_lo * QB_TILE);
+                        CK(qb_qmv(W->type, &seg, 1, K, nn, s->xb, 0, (int)(a - (uint64_t)t_lo * QB_TILE),
+                                  (int)(b - (uint64_t)t_lo * QB_TILE), s->work, s->st));
+                    }
+                    CK(cudaMemcpy2DAsync(outs[i] + (size_t)t0 * ldos[i] + a, ldos[i] * 4, o + a, (size_t)W->rows * 4,
+                                         (size_t)(b - a) * 4, nn, cudaMemcpyDeviceToHost, s->st));
+                }
+                o += (size_t)nn * W->rows;
+            }
+            // the staging buffers are reused by the next chunk: its copies must have left
+            CK(cudaStreamSynchronize(s->st));
         }
-        CK(cudaStreamSynchronize(s->st));
     }
     return 0;
 }

@@ -43,8 +43,10 @@ struct QbXBuf {
     uint2* xq;               // int8 digit mma B fragments (IQ4_XS), qb_xbuf_bytes
     float* xqscale;          // [QB_MAX_TOK][K/256] power-of-two scale of xq and xtc
     uint8_t* xtc;            // int8 digits as tcgen05 B tiles, 4 KB per 256 columns (N <= 4)
+    uint8_t* xtc16;          // the same for up to 16 tokens, 12 KB per 256 columns (qb_qmv_tc16)
 };
-enum { QB_XP_F16 = 1, QB_XP_SUM = 2, QB_XP_I8 = 4, QB_XP_TC = 8 };   // qb_xprep outputs
+enum { QB_XP_F16 = 1, QB_XP_SUM = 2, QB_XP_I8 = 4, QB_XP_TC = 8, QB_XP_TC16 = 16 };   // qb_xprep outputs
+#define QB_TC16_TOK 16       // input vectors of one qb_qmv_tc16 launch; xqscale rows it needs
 
 // ---- quantised GEMV (qb_quant.cu) ----
 size_t qb_repacked_bytes(int type, int rows, int K);
@@ -53,6 +55,7 @@ cudaError_t qb_repack(int type, const void* src_dev, int rows, int K, void* dst_
 size_t qb_xfrag_bytes(int K);
 size_t qb_xq_bytes(int K);
 size_t qb_xtc_bytes(int K);
+size_t qb_xtc16_bytes(int K);
 // which qb_xprep outputs a matrix of this type reads at N input vectors
 // (IQ4_XS: the tcgen05 tiles when N <= 4 and tc != 0, else the mma.sync fragments)
 int qb_xprep_needs(int type, int N = QB_MAX_TOK, int tc = 0);
@@ -130,6 +133,11 @@ size_t qb_repacked_bytes_tc(int rows, int K);
 cudaError_t qb_repack_tc(const void* src_dev, int rows, int K, void* dst_dev, cudaStream_t st);
 int qb_qmv_tc_max_ctas();
 size_t qb_qmv_tc_partial_floats(int max_ctas);
+// 9..16 input vectors (QB_TC16_TOK): the same weight layout, activation digits
+// from xb.xtc16 (qb_xprep QB_XP_TC16), scales from xb.xqscale
+// [QB_TC16_TOK][K/256]; one CTA per SM
+cudaError_t qb_qmv_tc16(const QbQSeg* segs, int nseg, int K, int N, const QbXBuf& xb, int accumulate, int row_lo,
+                        int row_hi, const QbQmvWork& work, cudaStream_t st);
 // segs[i].w are qb_repack_tc layouts
 cudaError_t qb_qmv_tc(const QbQSeg* segs, int nseg, int K, int N, const QbXBuf& xb, int accumulate, int row_lo,
                       int row_hi, const QbQmvWork& work, cudaStream_t st);

@@ -1322,6 +1322,7 @@ size_t qb_xfrag_bytes(int K) { return (size_t)(K + 255) / 256 * 256 / 16 * 2 * 3
 size_t qb_xq_bytes(int K) { return (size_t)(K + 255) / 256 * 256 / 32 * 3 * 32 * sizeof(uint2); }
 
 size_t qb_xtc_bytes(int K) { return (size_t)(K + 255) / 256 * 4096; }
+size_t qb_xtc16_bytes(int K) { return (size_t)(K + 255) / 256 * 12288; }
 
 int qb_xprep_needs(int type, int N, int tc) {
     switch (type) {
@@ -1337,7 +1338,9 @@ int qb_xprep_needs(int type, int N, int tc) {
 cudaError_t qb_xprep(const QbXIn* in, int nseg, int N, float eps, const QbXBuf& xb, int what, cudaStream_t st) {
     XSeg s[2] = {};
     int K = 0;
-    if (nseg < 1 || nseg > 2 || N < 1 || N > QB_MAX_TOK) return cudaErrorInvalidValue;
+    // up to QB_MAX_TOK tokens, or QB_TC16_TOK for the 16-token tcgen05 tiles alone
+    if (nseg < 1 || nseg > 2 || N < 1 || N > ((what == QB_XP_TC16) ? QB_TC16_TOK : QB_MAX_TOK))
+        return cudaErrorInvalidValue;
     for (int i = 0; i < nseg; ++i) {
         s[i].x = in[i].x;
         s[i].ldx = in[i].ldx;
@@ -1347,7 +1350,8 @@ cudaError_t qb_xprep(const QbXIn* in, int nseg, int N, float eps, const QbXBuf& 
         K += in[i].len;
     }
     if (((what & QB_XP_F16) && (!xb.xfrag || !xb.xscale)) || ((what & QB_XP_SUM) && !xb.xsum) ||
-        ((what & QB_XP_I8) && (!xb.xq || !xb.xqscale)) || ((what & QB_XP_TC) && (!xb.xtc || !xb.xqscale || N > 4)))
+        ((what & QB_XP_I8) && (!xb.xq || !xb.xqscale)) || ((what & QB_XP_TC) && (!xb.xtc || !xb.xqscale || N > 4)) ||
+        ((what & QB_XP_TC16) && (!xb.xtc16 || !xb.xqscale)))
         return cudaErrorInvalidValue;
     const int nb = K / 256;
     return qb_launch(xprep_kernel, dim3((nb + 7) / 8, N), dim3(256), 0, st, s[0], s[1], nseg, N, eps, xb, what);

@@ -85,7 +85,7 @@ __device__ __forceinline__ void xprep_emit_g(const float (&v)[G][8], int t0, int
                 for (int k = 0; k < G; ++k) xb.xsum[(t0 + k) * (K >> 5) + sb] = ps[k];
         }
     }
-    if (what & (QB_XP_I8 | QB_XP_TC)) {
+    if (what & (QB_XP_I8 | QB_XP_TC | QB_XP_TC16)) {
         // X = rint(x * 2^e) with |X| <= 2^22, as balanced int8 digits X = 65536 d0 + 256 d1 + d2
         // (|d0| <= 64).  Lane 8j + c (c < 4) holds elements 4c..4c+3 of sub-block j and
         // lane 8j + c + 4 elements 16+4c..16+4c+3: together one mma B register pair.
@@ -143,7 +143,15 @@ __device__ __forceinline__ void xprep_emit_g(const float (&v)[G][8], int t0, int
                         uint2 bv;
                         bv.x = prmt(dg[k][dgi], other[k][dgi], 0x5140u);   // (4c, 4c+16, 4c+1, 4c+17)
                         bv.y = prmt(dg[k][dgi], other[k][dgi], 0x7362u);   // (4c+2, 4c+18, 4c+3, 4c+19)
-                        if (what & QB_XP_I8) xb.xq[((size_t)kb * NTI + dnt[dgi]) * 32 + dcol[dgi] * 4 + c] = bv;
+                        if ((what & QB_XP_I8) && t < QB_MAX_TOK)
+                            xb.xq[((size_t)kb * NTI + dnt[dgi]) * 32 + dcol[dgi] * 4 + c] = bv;
+                        if (what & QB_XP_TC16) {
+                            // 48-row tcgen05 B tile of the sub-block, digit-major: row n = 16 digit + t
+                            // (one 16-column accumulator group per digit); same core-matrix layout
+                            const int nrow = 16 * dgi + t;
+                            *reinterpret_cast<uint2*>(xb.xtc16 + (size_t)kb * 1536 + (c >> 1) * 128 +
+                                                      (nrow >> 3) * 256 + (nrow & 7) * 16 + (c & 1) * 8) = bv;
+                        }
                         if ((what & QB_XP_TC) && t < 4) {
                             // tcgen05 B tile of the sub-block: row n = 3t + digit, 32 k bytes in the
                             // order above; K-major core matrices of 8 rows x 16 B, K chunks 128 B apart,

@@ -168,3 +168,45 @@ def test_gemv_multi_single_vector_and_limits():
         np.testing.assert_array_equal(o, qb.gemv_batch(t, x[None])[0])
     with pytest.raises(RuntimeError, match="at most 8"):
         qb.gemv_multi(ts * 3, x)
+
+
+@pytest.mark.parametrize("n", [9, 12, 16, 17, 32, 64])
+def test_gemv_batch_iq4_wide_tcgen05(n):
+    """More than 8 vectors: IQ4_XS runs 16 per weight sweep on the tcgen05
+    kernel (qb_qmv_tc16).  The reference's gemv_batch runs them 8 at a time,
+    each chunk bit-identical to a single-vector sweep (src/test_batch.c:44-57),
+    so the bar is the same as for the mma.sync path."""
+    K, rows = 2048, 333        # rows not a multiple of the 128-row tile
+    raw = qb.synth_matrix(qb.GGML_IQ4_XS, rows, K, seed=200 + n, d_sigma=0.01)
+    x = qb.synth_normal(n * K, seed=300 + n).reshape(n, K)
+    t = qb.tensor(raw, qb.GGML_IQ4_XS, K, rows)
+    got = qb.gemv_batch(t, x)
+    ref = oracle.ref_gemv_batch(raw, qb.GGML_IQ4_XS, K, rows, x)
+    for i in range(n):
+        assert rel(got[i], ref[i]) < RTOL, (i, rel(got[i], ref[i]))
+
+
+@pytest.mark.parametrize("n", [16, 32])
+def test_gemv_batch_iq4_wide_micro_shape(n):
+    """The C1 micro matrix (17408 x 5120) at the prefill / multi-stream widths."""
+    K, rows = 5120, 17408
+    raw = qb.synth_matrix(qb.GGML_IQ4_XS, rows, K, seed=0, d_sigma=0.02)
+    x = qb.synth_normal(n * K, seed=n).reshape(n, K)
+    got = qb.gemv_batch(qb.tensor(raw, qb.GGML_IQ4_XS, K, rows), x)
+    ref = oracle.ref_gemv_batch(raw, qb.GGML_IQ4_XS, K, rows, x)
+    for i in range(n):
+        assert rel(got[i], ref[i]) < RTOL, (i, rel(got[i], ref[i]))
+
+
+def test_gemv_multi_batch_iq4_wide():
+    """gemv_multi_batch with 20 vectors over IQ4_XS matrices: the 16-token
+    kernel per chunk, each matrix bit-identical to its own gemv_batch."""
+    K, n = 1024, 20
+    specs = [(300, 1), (520, 2), (64, 3)]
+    raws = [qb.synth_matrix(qb.GGML_IQ4_XS, r, K, seed=s, d_sigma=0.01) for r, s in specs]
+    ts = [qb.tensor(raw, qb.GGML_IQ4_XS, K, r) for raw, (r, _) in zip(raws, specs)]
+    x = qb.synth_normal(n * K, seed=9).reshape(n, K)
+    outs = qb.gemv_multi_batch(ts, x)
+    for raw, (r, _), t, o in zip(raws, specs, ts, outs):
+        np.testing.assert_array_equal(o, qb.gemv_batch(t, x))
+        assert rel(o, oracle.ref_gemv_batch(raw, qb.GGML_IQ4_XS, K, r, x)) < RTOL
