@@ -378,6 +378,12 @@ def run_ours(args, rank, world, local_rank):
         ms_c1, b_c1 = model.bench(8, n, 5)
         gbs = b_c1 / shards_of(world, tp) / (ms_c1 / 1e3) / 1e9
         c1[f"n{n}"] = {"us": ms_c1 * 1e3, "GB/s": gbs, "frac": gbs / peaks()[0]}
+    if not tp:   # the prefill / multi-stream width: 16 vectors per sweep on tcgen05, beside 2 x 8 on mma.sync
+        ms_w, b_w = model.bench(9, 16, 5)
+        ms_8, _ = model.bench(8, 8, 5)
+        c1["n16_tcgen05"] = {"us": ms_w * 1e3, "GB/s": b_w / (ms_w / 1e3) / 1e9,
+                             "frac": b_w / (ms_w / 1e3) / 1e9 / peaks()[0],
+                             "us_as_2x8_mma_sync": 2 * ms_8 * 1e3}
     # C2: 128-token prompt (plain prefill), then 256 greedy tokens on the device
     gold = golden_full()
     model.reset()

@@ -428,6 +428,7 @@ struct Engine {
     float *logits, *mtp_x, *mtp_h, *mtp_logits, *emb;
     QbXBuf xb{};                          // prepared GEMV activations (what the next GEMV reads)
     QbXBuf xb_alt{};                      // where a fused GEMV epilogue prepares the input after that
+    QbXBuf xb16{};                        // 16-vector tcgen05 activation tiles (qb_bench what = 9)
     const float* xss = nullptr;           // xb holds x * norm_w: per-block sums of squares of x (QbInNorm)
     bool xready = false;                  // xb already holds the next normed input (fused epilogue)
     bool fuse = false;                    // fused GEMV epilogues (QB_FUSE=1; mma.sync path only)
@@ -1980,6 +1981,61 @@ extern "C" float qb_bench(qwen_model_t* m, int what, uint32_t arg, uint32_t iter
             }
             b /= (double)nl;
         }
+    } else if (what == 9) {
+        // one FFN up matrix at N = arg (9..16) on the 16-vector tcgen05 kernel, rotated over
+        // all layers; the tcgen05 tile copies of those matrices are made on first use
+        if (arg < 1 || arg > QB_TC16_TOK || e->tp_world > 1) return -1.f;
+        const int nl = (int)e->L.size();
+        for (int li = 0; li < nl; ++li) {
+            DevMat& up = e->L[li].ffn_up;
+            if (up.w_tc || up.type != QB_IQ4_XS) continue;
+            char nm[64];
+            snprintf(nm, sizeof nm, "blk.%d.ffn_up.weight", li);
+            const GTensor* t = e->g.find(nm);
+            if (!t) return -1.f;
+            const size_t src = gguf_row_bytes(t->type, t->ne[0]) * t->ne[1];
+            void* tmp = nullptr;
+            if (cudaMalloc(&tmp, src) != cudaSuccess) return -1.f;
+            up.w_tc = e->dalloc(qb_repacked_bytes_tc(up.rows, up.K));
+            if (!up.w_tc || cudaMemcpy(tmp, t->data, src, cudaMemcpyHostToDevice) != cudaSuccess ||
+                qb_repack_tc(tmp, up.rows, up.K, up.w_tc, e->st) != cudaSuccess ||
+                cudaStreamSynchronize(e->st) != cudaSuccess) {
+                cudaFree(tmp);
+                return -1.f;
+            }
+            cudaFree(tmp);
+        }
+        if (!e->xb16.xtc16) {
+            e->xb16.xtc16 = (uint8_t*)e->dalloc(qb_xtc16_bytes(e->E));
+            e->xb16.xqscale = (float*)e->dalloc((size_t)QB_TC16_TOK * (e->E / 256) * 4);
+            if (!e->xb16.xtc16 || !e->xb16.xqscale) return -1.f;
+        }
+        // input: arg rows of the FFN activation buffer (any finite values), prepared once
+        const QbXIn in{e->act, e->E, nullptr, e->E};
+        if (qb_xprep(&in, 1, (int)arg, e->eps, e->xb16, QB_XP_TC16, e->st) != cudaSuccess) return -1.f;
+        struct Rec9 {
+            static int go(Engine& en, int a) {
+                for (const LayerW& ly : en.L) {
+                    QbQSeg seg;
+                    seg.w = ly.ffn_up.w_tc;
+                    seg.out = en.logits;   // [a][F] rows of the logits buffer
+                    seg.ldo = en.F;
+                    seg.rows = ly.ffn_up.rows;
+                    CK(qb_qmv_tc16(&seg, 1, en.E, a, en.xb16, 0, 0, 1 << 30, en.work, en.st));
+                }
+                return 0;
+            }
+        };
+        if (capture(*e, &ge, Rec9::go, (int)arg)) return -1.f;
+        cudaGraphLaunch(ge, e->st);
+        cudaEventRecord(e->ev0, e->st);
+        for (uint32_t i = 0; i < iters; ++i) cudaGraphLaunch(ge, e->st);
+        cudaEventRecord(e->ev1, e->st);
+        cudaEventSynchronize(e->ev1);
+        cudaEventElapsedTime(&ms, e->ev0, e->ev1);
+        cudaGraphExecDestroy(ge);
+        iters *= (uint32_t)nl;
+        b = (double)mat_bytes(e->L[0].ffn_up) + (double)arg * e->E * 4 + (double)arg * e->F * 4;
     } else if (what == 4) {
         // kernels launched per speculative cycle (nodes of the captured cycle graph)
         if (bytes) *bytes = 0;
