@@ -296,8 +296,11 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_tc_kernel(TcK p) {
 // tokens, then d1, then d2), so the MMA is M 128 N 48 K 32 and each digit's
 // sums are one 16-column group of accumulators.  Tensor memory: A in 2 x 64
 // columns as above, D in 8 sub-blocks x 48 columns: all 512 columns, one CTA
-// per SM.  The epilogue applies the sub-block scales per digit in int32 and
-// combines the digits in fp32 in the order of the other paths
+// per SM.  Eight decode / epilogue warps, two per tensor-memory lane quarter:
+// warp w (half h = w / 4) decodes sub-blocks 4h..4h+3 of its 32 rows and runs
+// the epilogue of tokens 8h..8h+7, so two warps per SM sub-partition hide each
+// other's latency.  The epilogue applies the sub-block scales per digit in
+// int32 and combines the digits in fp32 in the order of the other paths
 // (65536 d0 + (256 d1 + d2)), so a (tile, block) gives the same value here as
 // in the mma.sync GEMV; only the order of the per-block sums across split
 // tiles differs.
@@ -307,21 +310,24 @@ constexpr int kRing16 = 4;
 constexpr uint32_t kCols16 = 512;
 constexpr uint32_t kDCol16 = 128;
 constexpr uint32_t kIdesc16 = idesc_i8(128, 48);
+constexpr int kWarps16 = 8;                   // decode / epilogue warps
+constexpr int kThreads16 = kWarps16 * 32 + 32;   // + producer warp
 
-// row m of tile T complete for 16 tokens (finish_row with 16 token columns;
-// partial rows of 16 floats)
-__device__ void finish_row16(const TcK& p, int T, int cta, int s0, int s1, int m, const float (&tot)[16]) {
+// row m of tile T complete for tokens 8h..8h+7: store them, or combine the split
+// tile's per-CTA partials of this half (last arriving CTA, CTA order)
+__device__ void finish_row16(const TcK& p, int T, int cta, int s0, int s1, int m, int h, const float (&tot)[8]) {
     const int sg = seg_of_tile(p, T);
     const int row = (T - p.tile0[sg]) * kRows + m;
-    auto store = [&](const float (&v)[16]) {
+    const int tb = 8 * h;
+    auto store = [&](const float (&v)[8]) {
         if (row >= p.rows[sg] || row < p.row_lo || row >= p.row_hi) return;
-        float prev[16];
+        float prev[8];
 #pragma unroll
-        for (int t = 0; t < 16; ++t)
-            prev[t] = (t < p.N && p.accumulate) ? p.out[sg][(size_t)t * p.ldo[sg] + row] : 0.f;
+        for (int t = 0; t < 8; ++t)
+            prev[t] = (tb + t < p.N && p.accumulate) ? p.out[sg][(size_t)(tb + t) * p.ldo[sg] + row] : 0.f;
 #pragma unroll
-        for (int t = 0; t < 16; ++t)
-            if (t < p.N) p.out[sg][(size_t)t * p.ldo[sg] + row] = p.accumulate ? prev[t] + v[t] : v[t];
+        for (int t = 0; t < 8; ++t)
+            if (tb + t < p.N) p.out[sg][(size_t)(tb + t) * p.ldo[sg] + row] = p.accumulate ? prev[t] + v[t] : v[t];
     };
     const int P0 = T * p.nb, P1 = P0 + p.nb;
     if (s0 <= P0 && s1 >= P1) {
@@ -329,27 +335,27 @@ __device__ void finish_row16(const TcK& p, int T, int cta, int s0, int s1, int m
         return;
     }
     const int piece = s0 > P0 ? 0 : 1;
-    float4* dst = reinterpret_cast<float4*>(p.partial + (((size_t)cta * 2 + piece) * kRows + m) * 16);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) dst[q] = make_float4(tot[4 * q], tot[4 * q + 1], tot[4 * q + 2], tot[4 * q + 3]);
+    float4* dst = reinterpret_cast<float4*>(p.partial + (((size_t)cta * 2 + piece) * kRows + m) * 16 + tb);
+    dst[0] = make_float4(tot[0], tot[1], tot[2], tot[3]);
+    dst[1] = make_float4(tot[4], tot[5], tot[6], tot[7]);
     const int c_first = stage_cta(p.S, p.G, P0), c_last = stage_cta(p.S, p.G, P1 - 1);
-    unsigned* ctr = p.counters + (size_t)T * kRows + m;
+    unsigned* ctr = p.counters + ((size_t)T * kRows + m) * 2 + h;
     const unsigned old = atom_add_acq_rel_gpu(ctr, 1u);
     if ((int)old != c_last - c_first) return;
-    float sum[16];
+    float sum[8];
 #pragma unroll
-    for (int t = 0; t < 16; ++t) sum[t] = 0.f;
+    for (int t = 0; t < 8; ++t) sum[t] = 0.f;
     for (int c = c_first; c <= c_last; ++c) {
         const int pc = cta_s0(p.S, p.G, c) > P0 ? 0 : 1;
-        const volatile float* v = p.partial + (((size_t)c * 2 + pc) * kRows + m) * 16;
+        const volatile float* v = p.partial + (((size_t)c * 2 + pc) * kRows + m) * 16 + tb;
 #pragma unroll
-        for (int t = 0; t < 16; ++t) sum[t] += v[t];
+        for (int t = 0; t < 8; ++t) sum[t] += v[t];
     }
     store(sum);
     *ctr = 0u;
 }
 
-__global__ void __launch_bounds__(kThreads, 1) qmv_tc16_kernel(TcK p) {
+__global__ void __launch_bounds__(kThreads16, 1) qmv_tc16_kernel(TcK p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + kRing16;
@@ -380,7 +386,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_tc16_kernel(TcK p) {
     const uint32_t tmem = *tmem_holder;
     pdl_trigger();
 
-    if (warp == kDecodeWarps) {
+    if (warp == kWarps16) {
         // ------------------------------ producer ------------------------------
         if (lane == 0 && n > 0) {
             auto weights_of = [&](int s) -> const uint8_t* {
@@ -415,11 +421,12 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_tc16_kernel(TcK p) {
     } else if (n > 0) {
         // --------------------------- decode / epilogue ---------------------------
         pdl_wait();
-        const int m = threadIdx.x;
-        const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-        float tot[16];
+        const int q = warp & 3, h = warp >> 2;         // lane quarter, half
+        const int m = q * 32 + lane;                   // weight row of this thread
+        const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+        float tot[8];
 #pragma unroll
-        for (int t = 0; t < 16; ++t) tot[t] = 0.f;
+        for (int t = 0; t < 8; ++t) tot[t] = 0.f;
         int sc_prev[8] = {0, 0, 0, 0, 0, 0, 0, 0};
         float d_prev = 0.f;
         int last_mma = -1;
@@ -441,50 +448,56 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_tc16_kernel(TcK p) {
                     }
                     const uint32_t abuf = tmem + lane_base + (uint32_t)((r & 1) * 64);
 #pragma unroll
-                    for (int sb = 0; sb < 8; ++sb) {
-                        const uint4 q = lds128(u + sb * (kRows * 16) + m * 16);
+                    for (int k = 0; k < 4; ++k) {
+                        const int sb = 4 * h + k;
+                        const uint4 qq = lds128(u + sb * (kRows * 16) + m * 16);
                         uint32_t a[8];
-                        iq4_i8(q.x, a[0], a[1]);
-                        iq4_i8(q.y, a[2], a[3]);
-                        iq4_i8(q.z, a[4], a[5]);
-                        iq4_i8(q.w, a[6], a[7]);
+                        iq4_i8(qq.x, a[0], a[1]);
+                        iq4_i8(qq.y, a[2], a[3]);
+                        iq4_i8(qq.z, a[4], a[5]);
+                        iq4_i8(qq.w, a[6], a[7]);
                         tmem_st8(abuf + (uint32_t)(sb * 8), a);
                     }
                     tmem_wait_st();
                 }
             }
-            // epilogue of stage r-1: per digit (d2, d1, d0) the sub-block-scaled int32 sums
+            // epilogue of stage r-1, tokens 8h..8h+7: per digit (d2, d1, d0) the
+            // sub-block-scaled int32 sums
             if (r >= 1 && !*dec_abort) {
                 const int rp = r - 1;
                 if (!mbar_wait_sleep(mma_done, (uint32_t)rp & 1u, kSleepNs)) {
                     *dec_abort = 1;
                 } else {
                     tc_fence_after();
-                    const uint32_t dbase = tmem + lane_base + kDCol16;
+                    const uint32_t dbase = tmem + lane_base + kDCol16 + (uint32_t)(8 * h);
                     const int b_prev = (s0 + rp) % p.nb;
-                    float f[16];
+                    float f[8];
 #pragma unroll
                     for (int g = 2; g >= 0; --g) {
-                        int acc[16];
+                        int acc[8];
 #pragma unroll
-                        for (int t = 0; t < 16; ++t) acc[t] = 0;
+                        for (int t = 0; t < 8; ++t) acc[t] = 0;
 #pragma unroll
-                        for (int sb = 0; sb < 8; sb += 2) {
-                            uint32_t v0[16], v1[16];
-                            tmem_ld16(dbase + (uint32_t)(sb * 48 + g * 16), v0);
-                            tmem_ld16(dbase + (uint32_t)((sb + 1) * 48 + g * 16), v1);
+                        for (int sb = 0; sb < 8; sb += 4) {
+                            uint32_t v0[8], v1[8], v2[8], v3[8];
+                            tmem_ld8(dbase + (uint32_t)(sb * 48 + g * 16), v0);
+                            tmem_ld8(dbase + (uint32_t)((sb + 1) * 48 + g * 16), v1);
+                            tmem_ld8(dbase + (uint32_t)((sb + 2) * 48 + g * 16), v2);
+                            tmem_ld8(dbase + (uint32_t)((sb + 3) * 48 + g * 16), v3);
                             tmem_wait_ld();
 #pragma unroll
-                            for (int t = 0; t < 16; ++t)
-                                acc[t] += sc_prev[sb] * (int)v0[t] + sc_prev[sb + 1] * (int)v1[t];
+                            for (int t = 0; t < 8; ++t)
+                                acc[t] += sc_prev[sb] * (int)v0[t] + sc_prev[sb + 1] * (int)v1[t] +
+                                          sc_prev[sb + 2] * (int)v2[t] + sc_prev[sb + 3] * (int)v3[t];
                         }
 #pragma unroll
-                        for (int t = 0; t < 16; ++t) {
+                        for (int t = 0; t < 8; ++t) {
                             if (g == 2) f[t] = (float)acc[t];
                             else if (g == 1) f[t] = fmaf((float)acc[t], 256.f, f[t]);
                             else {
+                                const int tok = 8 * h + t;
                                 const float v = fmaf((float)acc[t], 65536.f, f[t]) * d_prev;
-                                const float xs = t < p.N ? __ldg(p.xqscale + t * p.nb + b_prev) : 0.f;
+                                const float xs = tok < p.N ? __ldg(p.xqscale + tok * p.nb + b_prev) : 0.f;
                                 tot[t] = fmaf(xs, v, tot[t]);
                             }
                         }
@@ -492,14 +505,14 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_tc16_kernel(TcK p) {
                     if (threadIdx.x == 0) mbar_arrive(empty + rp % kRing16);
                     const int s = s0 + rp;
                     if ((s + 1) % p.nb == 0 || rp == n - 1) {
-                        finish_row16(p, s / p.nb, cta, s0, s1, m, tot);
+                        finish_row16(p, s / p.nb, cta, s0, s1, m, h, tot);
 #pragma unroll
-                        for (int t = 0; t < 16; ++t) tot[t] = 0.f;
+                        for (int t = 0; t < 8; ++t) tot[t] = 0.f;
                     }
                 }
             }
             tc_fence_before();
-            named_bar_sync(1, kDecodeThreads);
+            named_bar_sync(1, kWarps16 * 32);
             if (*dec_abort) break;
             if (r < n && threadIdx.x == 0) {
                 tc_fence_after();
@@ -681,5 +694,5 @@ cudaError_t qb_qmv_tc16(const QbQSeg* segs, int nseg, int K, int N, const QbXBuf
         if (e != cudaSuccess) return e;
         attr_set = true;
     }
-    return qb_launch(qmv_tc16_kernel, dim3(G), dim3(kThreads), smem, st, p);
+    return qb_launch(qmv_tc16_kernel, dim3(G), dim3(kThreads16), smem, st, p);
 }
