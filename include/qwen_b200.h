@@ -99,6 +99,14 @@ typedef struct {
  *   mtp_h     [n_embd]           read by mtp_forward (caller may write it,
  *                                src/main.c:220), written back after it
  *   pos                          next position, as in the reference */
+/* One backbone layer as the layer functions below take it (include/model.h:33-57
+ * names the reference's fields; its weights live on the device here, so a
+ * caller only reads which layer it is and whether it is recurrent). */
+typedef struct qwen_layer {
+    uint32_t index;
+    bool is_recurrent;
+} qwen_layer_t;
+
 typedef struct qwen_model {
     qwen_config_t cfg;
     qwen_dims_t dims;
@@ -109,6 +117,7 @@ typedef struct qwen_model {
     float *h_save;
     uint32_t n_ctx;
     uint32_t pos;
+    qwen_layer_t *layers;  /* [dims.n_layer], as m->layers in the reference */
     void *eng;             /* device engine (opaque) */
 #ifdef GGUF_H
     /* Only when the reference gguf.h was included first (a relinked reference
@@ -136,6 +145,13 @@ void pool_run(pool_t *p, pool_fn_t fn, void *arg);
 /* ---- include/model.h:117-148 ---- */
 int model_init(qwen_model_t *m, const char *path, uint32_t n_ctx);
 void model_free(qwen_model_t *m);
+/* include/model.h:121-122: one layer of one token on the hidden state m->x
+ * (host mirror, read and written): the gated-attention block at position pos,
+ * or the Gated DeltaNet block on the current recurrent state, each with its
+ * SwiGLU FFN and both residuals (src/model.c:418-485, 617-695).  Runs on the
+ * device; L is &m->layers[il]. */
+void attention_layer(qwen_model_t *m, qwen_layer_t *L, pool_t *pool, uint32_t pos);
+void gdn_layer(qwen_model_t *m, qwen_layer_t *L, pool_t *pool);
 void model_forward(qwen_model_t *m, pool_t *pool, uint32_t token, uint32_t pos);
 void model_forward_batch(qwen_model_t *m, pool_t *pool, const uint32_t *tokens, uint32_t pos,
                          uint32_t B, int ckpt);

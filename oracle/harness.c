@@ -89,6 +89,12 @@ void ref_forward_batch(ref_t *r, const uint32_t *toks, uint32_t pos, uint32_t B,
     model_forward_batch(&r->m, r->pool, toks, pos, B, ckpt);
 }
 void ref_rollback_to(ref_t *r, uint32_t b) { model_rollback_to(&r->m, b); }
+/* one layer on m->x: attention_layer / gdn_layer (include/model.h:121-122) */
+void ref_layer(ref_t *r, uint32_t il, uint32_t pos) {
+    qwen_layer_t *L = &r->m.layers[il];
+    if (L->is_recurrent) gdn_layer(&r->m, L, r->pool);
+    else attention_layer(&r->m, L, r->pool, pos);
+}
 void ref_mtp_forward(ref_t *r, uint32_t tok, uint32_t pos, int want_logits) {
     mtp_forward(&r->m, r->pool, tok, pos, want_logits);
 }

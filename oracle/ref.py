@@ -61,6 +61,7 @@ def ref():
         L.ref_forward.argtypes = [vp, u32, u32]
         L.ref_forward_batch.argtypes = [vp, P(u32), u32, u32, i32]
         L.ref_rollback_to.argtypes = [vp, u32]
+        L.ref_layer.argtypes = [vp, u32, u32]
         L.ref_mtp_forward.argtypes = [vp, u32, u32, i32]
         L.ref_mtp_forward_batch.argtypes = [vp, P(u32), u32, u32, i32]
         L.ref_argmax.argtypes = [P(f32), u32]
@@ -156,6 +157,12 @@ class RefModel:
     def state(self, il, which, n):
         p = ref().ref_layer_state(self.h, il, which)
         return np.ctypeslib.as_array(p, (n,)).copy()
+
+    def set_x(self, v):
+        np.ctypeslib.as_array(ref().ref_x(self.h), (self.E,))[:] = v
+
+    def layer(self, il, pos):
+        ref().ref_layer(self.h, il, pos)
 
     def forward(self, tok, pos):
         ref().ref_forward(self.h, tok, pos)

@@ -1510,6 +1510,16 @@ extern "C" int qb_model_init_tp(qwen_model_t* m, const char* path, uint32_t n_ct
         return -1;
     }
     memset(m->mtp_h, 0, (size_t)e->E * 4);
+    m->layers = (qwen_layer_t*)calloc(e->L.size() ? e->L.size() : 1, sizeof(qwen_layer_t));
+    if (!m->layers) {
+        set_err(-2, "layer table");
+        model_free(m);
+        return -1;
+    }
+    for (size_t il = 0; il < e->L.size(); ++il) {
+        m->layers[il].index = (uint32_t)il;
+        m->layers[il].is_recurrent = e->L[il].rec;
+    }
     return 0;
 }
 
@@ -1567,6 +1577,7 @@ extern "C" void model_free(qwen_model_t* m) {
     if (m->h_save) cudaFreeHost(m->h_save);
     if (m->mtp_h) cudaFreeHost(m->mtp_h);
     if (m->x) cudaFreeHost(m->x);
+    free(m->layers);
     memset(m, 0, sizeof *m);
 }
 
@@ -1583,6 +1594,45 @@ static int do_forward_batch(qwen_model_t* m, const uint32_t* tokens, uint32_t po
     if (sync_host_mirrors_after_batch(m, *e, (int)B)) return -1;
     m->pos = pos + B;
     return 0;
+}
+
+// one layer of one token on m->x (attention_layer / gdn_layer)
+static void one_layer(qwen_model_t* m, const qwen_layer_t* L, uint32_t pos, bool want_rec, const char* who) {
+    Engine* e = E_(m);
+    if (!e || !L || L->index >= e->L.size() || e->L[L->index].rec != want_rec) {
+        set_err(-1, "%s: bad model or layer", who);
+        return;
+    }
+    if (cudaSetDevice(e->dev) != cudaSuccess) { set_err(-2, "%s: device", who); return; }
+    const LayerW& l = e->L[L->index];
+    auto fail = [&]() { set_err(-2, "%s: CUDA failure", who); };
+    if (cudaMemcpyAsync(e->bx, m->x, (size_t)e->E * 4, cudaMemcpyHostToDevice, e->st) != cudaSuccess ||
+        cudaMemcpyAsync(&e->ctrl->fwd_pos, &pos, 4, cudaMemcpyHostToDevice, e->st) != cudaSuccess)
+        return fail();
+    fresh_input(*e);
+    e->xready = false;
+    const NextIn next = layer_in(*e, l, 1);
+    int r;
+    if (l.rec) {
+        r = gdn_block(*e, l, 1, 0, next);
+    } else {
+        float* kc = e->kv_k + (size_t)l.aidx * e->kv_layer;
+        float* vc = e->kv_v + (size_t)l.aidx * e->kv_layer;
+        r = attn_block(*e, l, e->bx, 1, &e->ctrl->fwd_pos, kc, vc, next);
+    }
+    fresh_input(*e);
+    e->xready = false;
+    if (r) return;
+    if (cudaMemcpyAsync(m->x, e->bx, (size_t)e->E * 4, cudaMemcpyDeviceToHost, e->st) != cudaSuccess) return fail();
+    dev_sync(*e);
+}
+
+extern "C" void attention_layer(qwen_model_t* m, qwen_layer_t* L, pool_t*, uint32_t pos) {
+    one_layer(m, L, pos, false, "attention_layer");
+}
+
+extern "C" void gdn_layer(qwen_model_t* m, qwen_layer_t* L, pool_t*) {
+    one_layer(m, L, 0, true, "gdn_layer");
 }
 
 extern "C" void model_forward(qwen_model_t* m, pool_t*, uint32_t token, uint32_t pos) {

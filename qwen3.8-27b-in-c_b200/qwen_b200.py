@@ -22,7 +22,8 @@ BLOCK = {GGML_F32: (1, 4), GGML_Q8_0: (32, 34), GGML_Q4_K: (256, 144), GGML_Q5_K
 # symbols declared in include/qwen_b200.h (checked by the CPU test suite)
 EXPORTED = [
     "pool_create", "pool_destroy", "pool_run",
-    "model_init", "model_free", "model_forward", "model_forward_batch", "model_snapshot_states",
+    "model_init", "model_free", "attention_layer", "gdn_layer", "model_forward", "model_forward_batch",
+    "model_snapshot_states",
     "model_rollback_states", "model_rollback_to", "mtp_forward", "mtp_forward_batch",
     "model_sample_greedy",
     "gemv_rows", "gemv", "gemv_rows_batch", "gemv_batch", "gemv_multi", "gemv_multi_batch",
@@ -62,11 +63,16 @@ class QwenDims(C.Structure):
                                   "conv_dim", "d_conv", "d_state")]
 
 
+class QwenLayer(C.Structure):
+    _fields_ = [("index", C.c_uint32), ("is_recurrent", C.c_bool)]
+
+
 class QwenModel(C.Structure):
     _fields_ = [("cfg", QwenConfig), ("dims", QwenDims), ("mtp_h", C.POINTER(C.c_float)),
                 ("x", C.POINTER(C.c_float)), ("logits", C.POINTER(C.c_float)),
                 ("logits_b", C.POINTER(C.c_float)), ("h_save", C.POINTER(C.c_float)),
-                ("n_ctx", C.c_uint32), ("pos", C.c_uint32), ("eng", C.c_void_p)]
+                ("n_ctx", C.c_uint32), ("pos", C.c_uint32), ("layers", C.POINTER(QwenLayer)),
+                ("eng", C.c_void_p)]
 
 
 class SamplerT(C.Structure):
@@ -91,6 +97,8 @@ def lib():
         L.model_init.restype = i32
         L.model_free.argtypes = [P(QwenModel)]
         L.model_forward.argtypes = [P(QwenModel), vp, u32, u32]
+        L.attention_layer.argtypes = [P(QwenModel), P(QwenLayer), vp, u32]
+        L.gdn_layer.argtypes = [P(QwenModel), P(QwenLayer), vp]
         L.model_forward_batch.argtypes = [P(QwenModel), vp, P(u32), u32, u32, i32]
         L.model_rollback_to.argtypes = [P(QwenModel), u32]
         L.mtp_forward.argtypes = [P(QwenModel), vp, u32, u32, i32]
@@ -368,6 +376,18 @@ class Model:
         return np.ctypeslib.as_array(self.m.x, (self.E,)).copy()
 
     # -------- model.h API --------
+    def set_x(self, v):
+        np.ctypeslib.as_array(self.m.x, (self.E,))[:] = v
+
+    def layer(self, il, pos):
+        """attention_layer / gdn_layer on m->x (the layer kind decides which)."""
+        L = C.pointer(self.m.layers[il])
+        if self.m.layers[il].is_recurrent:
+            lib().gdn_layer(C.byref(self.m), L, None)
+        else:
+            lib().attention_layer(C.byref(self.m), L, None, pos)
+        check()
+
     def forward(self, tok, pos):
         lib().model_forward(C.byref(self.m), None, tok, pos)
         check()

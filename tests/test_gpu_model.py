@@ -136,3 +136,23 @@ def test_wide_model_spec(wide_gguf):
     np.testing.assert_array_equal(gj, rj)
     assert rel(g.logits(), r.logits()) < RTOL
     g.close(); r.close()
+
+
+def test_single_layers_against_reference(gguf):
+    """attention_layer / gdn_layer (include/model.h:121-122) one token at a time on
+    m->x, layer by layer, against the reference's own layer functions: the hidden
+    state after every layer and the recurrent state after the DeltaNet layers."""
+    g, r = qb.Model(gguf, 64), oracle.RefModel(gguf, 64, 4)
+    rng = np.random.default_rng(8)
+    for pos in range(3):
+        x = rng.standard_normal(g.E).astype(np.float32)
+        g.set_x(x)
+        r.set_x(x)
+        for il in range(r.n_layer):
+            g.layer(il, pos)
+            r.layer(il, pos)
+            assert rel(g.x(), r.x()) < RTOL, (pos, il, rel(g.x(), r.x()))
+            if r.is_recurrent(il):
+                n_ssm = qb.TINY["ssm_v_heads"] * 128 * 128
+                assert rel(g.read_state(il, 1, n_ssm), r.state(il, 1, n_ssm)) < RTOL
+    g.close(); r.close()
