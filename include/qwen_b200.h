@@ -8,6 +8,7 @@
  * header (through include/shim) with no source edit; src/main.c does:
  *
  *   model_init / model_free            include/model.h:117-118
+ *   attention_layer / gdn_layer        include/model.h:121-122
  *   model_forward                      include/model.h:125
  *   model_forward_batch                include/model.h:130-131
  *   model_rollback_to                  include/model.h:136
@@ -19,6 +20,7 @@
  *   rmsnorm / l2norm / silu_inplace / sigmoid_inplace / softplus_inplace /
  *   softmax_inplace                    include/kernels.h:36-44
  *   pool_create / pool_destroy / pool_run   include/threadpool.h:9-15
+ *   sampler_init / sampler_free / sampler_sample   include/sampler.h:16-19
  *
  * All pointers in these calls are HOST pointers, as in the reference; the
  * library owns the CUDA device memory (weights, KV caches, recurrent states
@@ -310,11 +312,13 @@ int64_t qb_read_buffer(qwen_model_t *m, int id, float *dst, int64_t max_floats);
  *
  * One process per GPU.  Every rank loads the same GGUF with
  * qb_model_init_tp(m, path, n_ctx, rank, world) (world <= 8; model_init is
- * world = 1) and keeps rows [r0, r1) of every quantised matrix
- * (qb_tp_rows; the output head splits over the vocabulary).  Everything else
- * is replicated.  Each GEMV stores its rows into every rank's copy of the
- * output over NVLink and ends with a bounded cross-rank barrier, so all
- * ranks hold identical activations, logits and tokens.
+ * world = 1) and keeps its share of the heads: its DeltaNet k-heads with their
+ * v-heads, its attention q-heads with their kv-heads, its FFN columns (whole
+ * 256-column blocks) and its rows of the output head.  The mixers and the
+ * SwiGLU run on local data; the out-projections and the down projection write
+ * partial sums that every rank adds in rank order (NVLink loads of the peers'
+ * tagged words), so all ranks hold identical activations, logits and tokens.
+ * Waits on other ranks give up after 2 s (the call then returns its error).
  *
  * Set-up: qb_tp_handle() writes this rank's 64-byte IPC handle of its
  * activation arena; the caller exchanges the handles of all ranks (any host
