@@ -95,6 +95,13 @@ def golden_full():
         return None
 
 
+def golden_long():
+    """The compiled reference's output on C4 (2048-token prompt, then MTP
+    speculation): tests/golden/full_long.npz, or None when absent."""
+    f = os.path.join(ROOT, "tests", "golden", "full_long.npz")
+    return np.load(f) if os.path.exists(f) else None
+
+
 def rel_l2(a, b):
     a, b = np.float64(a), np.float64(b)
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
@@ -188,7 +195,9 @@ def cpu_reference_run(path, n_threads, warmup, steps, time_budget=None):
     n_ctx = PROMPT_LEN + 4 * (warmup + steps) + 64
     m = orc.RefModel(path, n_ctx, n_threads)
     log("reference model_init")
+    tp0 = time.perf_counter()
     m.prefill(prompt_tokens(0), 1)
+    prefill_tps = PROMPT_LEN / (time.perf_counter() - tp0)
     prefill_logits = m.logits()
     log("reference prefill")
     forced = forced_schedule()
@@ -216,7 +225,7 @@ def cpu_reference_run(path, n_threads, warmup, steps, time_budget=None):
     greedy_tps = (len(g) - 1) / (time.perf_counter() - tg)
     m.close()
     stream = {"tokens": np.concatenate(all_t), "accept": np.concatenate(all_j), "prefill_logits": prefill_logits,
-              "greedy_tok_s": greedy_tps}
+              "greedy_tok_s": greedy_tps, "prefill_tok_s": prefill_tps}
     return toks / dt, f"{cycles} cycles ({toks} tokens) after {warmup} warm-up cycles, prompt {PROMPT_LEN}", stream
 
 
@@ -239,6 +248,49 @@ def cpu_micro_c1(n_threads, reps=3):
         t = (time.perf_counter() - t0) / reps
         out[f"n{n}"] = {"ms": t * 1e3, "GB/s": raw.nbytes / t / 1e9}
     return out
+
+
+C4_PROMPT, C4_DECODE = 2048, 1024
+
+
+def run_c4(args, model, open_model, close_model, seq_rank, ms_ver_short):
+    """C4: a 2048-token prompt (256 prefill chunks of 8, device-timed), then MTP
+    speculation (k = 3, forced schedule) for 1024 tokens at that context, then
+    the verify step re-timed at the context reached (about 3072), against the
+    verify step at the short context of C3.  The model is re-opened with a
+    context of 3200 positions; the new model is returned under "_model"."""
+    close_model(model)
+    model = open_model(C4_PROMPT + C4_DECODE + 128)
+    prompt = np.random.default_rng(2000 + seq_rank).integers(0, qb.FULL["vocab"], C4_PROMPT).astype(np.uint32)
+    forced = forced_schedule()
+    model.prefill(prompt, 1)   # warm: captures the chunk graph
+    model.reset()
+    model.prefill(prompt, 1)
+    ms_pf = model.last_loop_ms()
+    lg = model.logits()
+    log(f"C4 prefill {ms_pf:.1f} ms")
+    toks, js = model.spec_generate(C4_DECODE, 3, forced=forced, max_cycles=4096)
+    ms_dec = model.last_loop_ms()
+    log(f"C4 decode {len(toks)} tokens {ms_dec:.1f} ms")
+    ms_v, b_v = model.bench(0, 4, 10)
+    c4 = {"prefill_tok/s": C4_PROMPT / (ms_pf / 1e3), "prefill_ms": ms_pf,
+          "prefill_chunks": C4_PROMPT // 8,
+          "decode_tok/s": len(toks) / (ms_dec / 1e3), "decode_tokens": int(len(toks)),
+          "decode_context": [C4_PROMPT, int(model.pos)],
+          "verify_ms_at_context": ms_v, "verify_context": int(model.pos), "verify_bytes": b_v,
+          "verify_ms_short_context": ms_ver_short,
+          "attention_share_of_verify": (ms_v - ms_ver_short) / ms_v,
+          "kv_bytes_per_verify": 16 * model.pos * 2 * 1024 * 4}
+    gold = golden_long()
+    if gold is not None and seq_rank == 0:
+        n = min(len(toks), len(gold["tokens"]))
+        c4["parity_golden"] = {
+            "prefill_logits_rel_l2": rel_l2(lg[:: int(gold["sub_stride"])], gold["prefill_sub"]),
+            "tokens_equal": bool(np.array_equal(toks[:n], gold["tokens"][:n])),
+            "accept_equal": bool(np.array_equal(js[:len(gold["accept"])], gold["accept"])),
+            "n_tokens": int(n)}
+    c4["_model"] = model
+    return c4
 
 
 def shards_of(world, tp):
@@ -302,16 +354,29 @@ def run_ours(args, rank, world, local_rank):
     seq_rank = 0 if tp else rank   # tensor parallelism: one sequence for all ranks
     path = gguf_path(rank, world)
     n_ctx = max(1024, PROMPT_LEN + 4 * (args.warmup + args.steps) + 64)
-    t0 = time.time()
-    if tp:
-        model = qb.Model(path, n_ctx, rank, world)
-        handles = [None] * world
-        dist.all_gather_object(handles, model.tp_handle())
-        model.tp_connect(handles)
-        dist.barrier()
-    else:
-        model = qb.Model(path, n_ctx)
-    print(f"[bench r{rank}] model_init {time.time() - t0:.1f}s", file=sys.stderr, flush=True)
+
+    def open_model(n_ctx):
+        t0 = time.time()
+        if tp:
+            m = qb.Model(path, n_ctx, rank, world)
+            handles = [None] * world
+            dist.all_gather_object(handles, m.tp_handle())
+            m.tp_connect(handles)
+            dist.barrier()
+        else:
+            m = qb.Model(path, n_ctx)
+        print(f"[bench r{rank}] model_init {time.time() - t0:.1f}s", file=sys.stderr, flush=True)
+        return m
+
+    def close_model(m):
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()   # tensor parallelism: no rank still writes into a peer's buffers
+        m.close()
+        if dist:
+            dist.barrier()
+
+    model = open_model(n_ctx)
     forced = forced_schedule()
 
     # ---- device-timed value: K speculative cycles ----
@@ -396,6 +461,9 @@ def run_ours(args, rank, world, local_rank):
           "frac": c2_gbs / peaks()[0], "bytes_per_token": b_tok,
           "tokens_equal_golden": bool(gold is not None and seq_rank == 0 and
                                       np.array_equal(g_toks[:len(gold["greedy"])], gold["greedy"]))}
+    c4 = run_c4(args, model, open_model, close_model, seq_rank, ms_ver) if not args.no_c4 else None
+    if c4 is not None:
+        model = c4.pop("_model")
     log(f"components gemv {ms_gemv:.4f} head {ms_head:.4f} draft {ms_draft:.3f} verify {ms_ver:.3f} ms")
     shards = world if tp else 1   # each GPU streams 1/shards of the weights
     gemv_gbs = b_gemv / shards / (ms_gemv / 1e3) / 1e9
@@ -411,6 +479,8 @@ def run_ours(args, rank, world, local_rank):
                 parity["reference_live"] = stream_parity(stream_t, stream_j, ref["tokens"], ref["accept"])
                 parity["reference_live"]["prefill_logits_rel_l2"] = rel_l2(prefill_logits, ref["prefill_logits"])
                 c2["reference_cpu_tok/s"] = ref["greedy_tok_s"]
+                if c4 is not None:   # prefill rate of the reference on the 128-token prompt (8-token chunks)
+                    c4["reference_cpu_prefill_tok/s"] = ref["prefill_tok_s"]
             log("cpu reference C1 micro")
             c1["reference_cpu"] = cpu_micro_c1(os.cpu_count())
         checks = [v for v in parity.values() if isinstance(v, dict)]
@@ -438,7 +508,8 @@ def run_ours(args, rank, world, local_rank):
             "verify_step": {"ms": ms_ver, "bytes": b_ver, "bytes_per_gpu": b_ver / shards, "GB/s": ver_gbs,
                             "frac": ver_gbs / hbm},
             "configs": {"C1 IQ4_XS 17408x5120 GEMV (64 rotated copies)": c1,
-                        "C2 greedy decode, prompt 128 + 256 tokens": c2},
+                        "C2 greedy decode, prompt 128 + 256 tokens": c2,
+                        "C4 long context, prompt 2048 + 1024 speculative tokens": c4},
             "draft_ms": ms_draft, "head_ms": ms_head,
             "head_GB/s": b_head / shards / (ms_head / 1e3) / 1e9,
             "clocks": clk.summary(),
@@ -446,12 +517,7 @@ def run_ours(args, rank, world, local_rank):
         if cpu_v is not None:
             line["cpu_baseline"] = {"value": cpu_v, "unit": "tok/s", "cores": os.cpu_count(), "kind": "reference",
                                     "sample": cpu_sample}
-    torch.cuda.synchronize()
-    if dist:
-        dist.barrier()   # tensor parallelism: no rank still writes into a peer's buffers
-    model.close()
-    if dist:
-        dist.barrier()
+    close_model(model)
     if line:
         print(json.dumps(line))
 
@@ -492,6 +558,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-c4", action="store_true", help="skip the long-context configuration C4")
     ap.add_argument("--mode", default="bench", choices=["bench", "components"])
     ap.add_argument("--shape", default="wide4", choices=["wide4", "full"])
     ap.add_argument("--iters", type=int, default=3)

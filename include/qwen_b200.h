@@ -243,7 +243,9 @@ void qb_clear_error(void);
 
 /* src/main.c:132-152: batched prefill in chunks of PREFILL_MAX_B, plus the
  * MTP cache fill when spec != 0; afterwards m->logits holds the logits of
- * the last prompt token.  Returns 0 or -1. */
+ * the last prompt token.  The prompt is copied to the device once and the
+ * chunks run back to back (one graph replay per full chunk, no host wait in
+ * between); qb_last_loop_ms then gives their device time.  Returns 0 or -1. */
 int qb_prefill(qwen_model_t *m, const uint32_t *tokens, uint32_t n, int spec);
 
 /* src/main.c:158-225: greedy MTP speculation with n_spec drafts.  Drafts,
@@ -275,7 +277,8 @@ int qb_sample_generate(qwen_model_t *m, sampler_t *s, uint32_t n_predict, const 
 /* Device argmax of the last model_forward_batch row b (no host scan). */
 uint32_t qb_last_argmax(qwen_model_t *m, uint32_t b);
 
-/* Timing helper for benchmarks: CUDA-event time of the last qb_* loop, ms. */
+/* Timing helper for benchmarks: CUDA-event time of the last qb_* loop
+ * (qb_prefill, qb_spec_generate, qb_greedy_generate, qb_sample_generate), ms. */
 float qb_last_loop_ms(qwen_model_t *m);
 
 /* Copy the recurrent state of backbone layer il (0 conv, 1 ssm) or the KV

@@ -470,6 +470,8 @@ struct Engine {
     size_t cycle_kernels = 0;
     cudaGraphExec_t g_greedy = nullptr;
     cudaGraphExec_t g_sample = nullptr;   // forward + sampling step (qb_sample_generate)
+    cudaGraphExec_t g_prefill[2] = {};    // one full prefill chunk, without / with the MTP fill
+    uint32_t* d_prompt = nullptr;         // [n_ctx] prompt tokens staged for the prefill graphs
     QbSampDev* samp = nullptr;            // sampler parameters, history and generator on the device
     unsigned long long* samp_cand = nullptr;
     unsigned long long* samp_keys = nullptr;
@@ -505,6 +507,8 @@ Engine::~Engine() {
     if (g_cycle) cudaGraphExecDestroy(g_cycle);
     if (g_greedy) cudaGraphExecDestroy(g_greedy);
     if (g_sample) cudaGraphExecDestroy(g_sample);
+    for (cudaGraphExec_t& gp : g_prefill)
+        if (gp) cudaGraphExecDestroy(gp);
     if (ev0) cudaEventDestroy(ev0);
     if (ev1) cudaEventDestroy(ev1);
     for (void* p : allocs) cudaFree(p);
@@ -941,7 +945,8 @@ int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
     e.gates = (float2*)e.dalloc((size_t)T8 * 256 * sizeof(float2));
     e.keys = (unsigned long long*)e.dalloc(2 * T8 * sizeof(unsigned long long));
     e.ctrl = (QbCtrl*)e.dalloc(sizeof(QbCtrl));
-    if (!e.bx || !e.logits || !e.xb.xfrag || !e.xb.xq || !e.ctrl || !e.emb || !e.keys) {
+    e.d_prompt = (uint32_t*)e.dalloc((size_t)e.n_ctx * 4);
+    if (!e.bx || !e.logits || !e.xb.xfrag || !e.xb.xq || !e.ctrl || !e.emb || !e.keys || !e.d_prompt) {
         set_err(-2, "activation alloc");
         return -1;
     }
@@ -1340,6 +1345,36 @@ int record_cycle(Engine& e, int k) {
     return 0;
 }
 
+// prefill chunk start (src/main.c:137-146): the next B prompt tokens from the
+// staged prompt at fwd_pos feed the backbone and, at the same positions, the MTP fill
+__global__ void prefill_chunk_kernel(QbCtrl* c, const uint32_t* prompt, int B) {
+    pdl_wait();
+    pdl_trigger();
+    const uint32_t p = c->fwd_pos;
+    for (int i = 0; i < B; ++i) {
+        c->fwd_tok[i] = prompt[p + i];
+        c->mtp_tok[i] = prompt[p + i];
+    }
+    c->mtp_pos = p;
+}
+__global__ void prefill_advance_kernel(QbCtrl* c, int B) {
+    pdl_wait();
+    pdl_trigger();
+    c->fwd_pos += (uint32_t)B;
+}
+
+// one full prefill chunk before the last: states, KV cache and h_save advance,
+// no output head; with spec the MTP KV cache fills from h_save (src/model.c:1069-1103)
+int record_prefill(Engine& e, int spec) {
+    CK(qb_launch(prefill_chunk_kernel, dim3(1), dim3(1), 0, e.st, e.ctrl, (const uint32_t*)e.d_prompt,
+                 (int)PREFILL_MAX_B));
+    if (fwd_backbone(e, PREFILL_MAX_B, 0, false, false)) return -1;
+    if (spec && fwd_mtp(e, PREFILL_MAX_B, e.h_save, 0)) return -1;
+    CK(qb_launch(prefill_advance_kernel, dim3(1), dim3(1), 0, e.st, e.ctrl, (int)PREFILL_MAX_B));
+    CK(cudaGetLastError());
+    return 0;
+}
+
 size_t g_last_graph_kernels = 0;
 
 int capture(Engine& e, cudaGraphExec_t* out, int (*rec)(Engine&, int), int arg) {
@@ -1717,23 +1752,28 @@ extern "C" float qb_last_loop_ms(qwen_model_t* m) {
 
 extern "C" int qb_prefill(qwen_model_t* m, const uint32_t* tokens, uint32_t n, int spec) {
     Engine* e = E_(m);
-    if (!e || n == 0 || n > (uint32_t)e->n_ctx) { set_err(-1, "qb_prefill: bad arguments"); return -1; }
+    if (!e || !tokens || n == 0 || n > (uint32_t)e->n_ctx) { set_err(-1, "qb_prefill: bad arguments"); return -1; }
     CK(cudaSetDevice(e->dev));
-    uint32_t pos = 0, lastB = 0;
-    while (pos < n) {
-        const uint32_t B = std::min<uint32_t>(n - pos, PREFILL_MAX_B);
-        CK(cudaMemcpyAsync(e->ctrl->fwd_tok, tokens + pos, B * 4, cudaMemcpyHostToDevice, e->st));
-        CK(cudaMemcpyAsync(&e->ctrl->fwd_pos, &pos, 4, cudaMemcpyHostToDevice, e->st));
-        if (fwd_backbone(*e, (int)B, 0, false, pos + B >= n)) return -1;   // logits of the last chunk only
-        if (spec) {
-            CK(cudaMemcpyAsync(e->ctrl->mtp_tok, tokens + pos, B * 4, cudaMemcpyHostToDevice, e->st));
-            CK(cudaMemcpyAsync(&e->ctrl->mtp_pos, &pos, 4, cudaMemcpyHostToDevice, e->st));
-            if (fwd_mtp(*e, (int)B, e->h_save, 0)) return -1;
-        }
-        if (dev_sync(*e)) return -1;   // host token/pos sources must outlive the copies
-        pos += B;
-        lastB = B;
+    spec = spec ? 1 : 0;
+    // the whole prompt goes to the device once; every full chunk before the last is
+    // one replay of the chunk graph, which takes its tokens from there at fwd_pos
+    CK(cudaMemcpyAsync(e->d_prompt, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, e->st));
+    const uint32_t n_full = (n - 1) / PREFILL_MAX_B;   // chunks before the last one
+    if (n_full && !e->g_prefill[spec] && capture(*e, &e->g_prefill[spec], record_prefill, spec)) return -1;
+    CK(cudaEventRecord(e->ev0, e->st));
+    CK(qb_launch(set_u32_kernel, dim3(1), dim3(1), 0, e->st, &e->ctrl->fwd_pos, 0u));
+    for (uint32_t c = 0; c < n_full; ++c) CK(cudaGraphLaunch(e->g_prefill[spec], e->st));
+    // the last chunk (1..8 tokens) with the output head: logits and argmax of its rows
+    const uint32_t pos = n_full * PREFILL_MAX_B, lastB = n - pos;
+    CK(cudaMemcpyAsync(e->ctrl->fwd_tok, e->d_prompt + pos, lastB * 4, cudaMemcpyDeviceToDevice, e->st));
+    CK(qb_launch(set_u32_kernel, dim3(1), dim3(1), 0, e->st, &e->ctrl->fwd_pos, pos));
+    if (fwd_backbone(*e, (int)lastB, 0, false, true)) return -1;
+    if (spec) {
+        CK(cudaMemcpyAsync(e->ctrl->mtp_tok, e->d_prompt + pos, lastB * 4, cudaMemcpyDeviceToDevice, e->st));
+        CK(qb_launch(set_u32_kernel, dim3(1), dim3(1), 0, e->st, &e->ctrl->mtp_pos, pos));
+        if (fwd_mtp(*e, (int)lastB, e->h_save, 0)) return -1;
     }
+    CK(cudaEventRecord(e->ev1, e->st));
     // next cand0 = argmax of the last prompt token's logits
     CK(cudaMemcpyAsync(&e->ctrl->next_cand0, &e->ctrl->argmax[lastB - 1], 4, cudaMemcpyDeviceToDevice, e->st));
     CK(cudaMemcpyAsync(m->logits, e->logits + (size_t)(lastB - 1) * e->V, (size_t)e->V * 4, cudaMemcpyDeviceToHost,
@@ -1741,6 +1781,7 @@ extern "C" int qb_prefill(qwen_model_t* m, const uint32_t* tokens, uint32_t n, i
     CK(cudaMemcpyAsync(m->h_save, e->h_save, (size_t)lastB * e->E * 4, cudaMemcpyDeviceToHost, e->st));
     CK(cudaMemcpyAsync(m->mtp_h, e->mtp_h, (size_t)e->E * 4, cudaMemcpyDeviceToHost, e->st));
     if (dev_sync(*e)) return -1;
+    CK(cudaEventElapsedTime(&e->last_ms, e->ev0, e->ev1));
     m->pos = n;
     return 0;
 }
