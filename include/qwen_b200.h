@@ -290,6 +290,28 @@ int64_t qb_read_state(qwen_model_t *m, uint32_t il, int which, float *dst, int64
  * zero, rollback slot 0, pos = 0.  Returns 0 or -1. */
 int qb_reset(qwen_model_t *m);
 
+/* Multi-sequence speculative decode (no counterpart in the reference, which
+ * decodes one sequence per process).  qb_seq_init gives the model n_seq
+ * (1..8) sequences on the same weights, each with its own recurrent slots, KV
+ * caches (n_ctx positions), control block and MTP hidden row, all zero.
+ * qb_seq_prefill runs qb_prefill(spec = 1) on sequence `seq`.  qb_seq_generate
+ * then runs n_cycles cycles of src/main.c:158-225 on all sequences at once:
+ * the MTP drafts at n_seq rows, the verify at n_seq * (n_spec + 1) rows (at
+ * most 32), acceptance and rollback per sequence, one CUDA graph per cycle;
+ * forced accept lengths (as in qb_spec_generate) apply to every sequence.
+ * Sequence s's tokens go to out_tokens[s * cap ..] (out_counts[s] of them,
+ * at most cap), its accept lengths to out_j[s * n_cycles ..] (may be NULL).
+ * Each sequence emits the tokens it would emit alone.  One GPU, default GEMV
+ * paths (no QB_TC / QB_FUSE).  After qb_seq_init the single-sequence calls act
+ * on the sequence last named by qb_seq_prefill (0 at first).  Return 0 / -1,
+ * or (qb_seq_generate) the cycles run, which is fewer than n_cycles only when
+ * a sequence would pass n_ctx. */
+int qb_seq_init(qwen_model_t *m, uint32_t n_seq);
+int qb_seq_prefill(qwen_model_t *m, uint32_t seq, const uint32_t *tokens, uint32_t n);
+int qb_seq_generate(qwen_model_t *m, uint32_t n_cycles, uint32_t n_spec, const uint32_t *forced,
+                    uint32_t n_forced, uint32_t *out_tokens, uint32_t cap, uint32_t *out_counts,
+                    uint32_t *out_j);
+
 /* Device time (ms, CUDA events on the model's stream, mean of `iters`) of one
  * component: what = 0 verify forward of `arg` tokens with checkpoints, 1 the
  * fused FFN gate+up GEMV at N = arg rotated over all layers, 2 one MTP draft

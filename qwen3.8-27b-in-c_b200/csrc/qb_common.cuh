@@ -6,6 +6,8 @@
 
 #define QB_TILE 16          // rows per tensor-core tile (m16n8k16 M dimension)
 #define QB_MAX_TOK 8        // verify / prefill width handled by one GEMV launch
+#define QB_WIDE 32          // rows of one multi-sequence forward (QB_MAX_TOK-row chunks per GEMV launch)
+#define QB_MAX_SEQ 8        // sequences of one multi-sequence forward
 #define QB_MAX_SEG 4        // matrices fused into one GEMV launch (shared input)
 
 // ggml type ids, identical to the GGUF numbering (reference include/gguf.h:40-64)

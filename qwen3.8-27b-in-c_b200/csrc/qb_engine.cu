@@ -423,7 +423,7 @@ struct Engine {
     size_t kv_layer = 0;
     float *rope_cos = nullptr, *rope_sin = nullptr;
 
-    // activations (QB_MAX_TOK rows each)
+    // activations (QB_WIDE rows each)
     float *bx, *h_save, *qkv, *qkvc, *z, *beta, *alpha, *o, *y, *qbuf, *kvbuf, *attn_o, *gate, *up, *act;
     float *logits, *mtp_x, *mtp_h, *mtp_logits, *emb;
     QbXBuf xb{};                          // prepared GEMV activations (what the next GEMV reads)
@@ -455,7 +455,7 @@ struct Engine {
     float* attn_po = nullptr;             // attention chunk partials (qb_attn_decode)
     float2* gates = nullptr;              // DeltaNet (beta, decay) per (token, v-head)
     float2* attn_pml = nullptr;
-    unsigned long long* keys = nullptr;   // [2][QB_MAX_TOK]: backbone, mtp
+    unsigned long long* keys = nullptr;   // [2][QB_WIDE]: backbone, mtp
     QbQmvWork work{};
     QbCtrl* ctrl = nullptr;
     uint32_t* d_forced = nullptr;
@@ -463,6 +463,21 @@ struct Engine {
     uint32_t* d_out_j = nullptr;
     uint32_t cap_forced = 0, cap_out = 0, cap_j = 0;
     int ld_qkv = 0;
+
+    // multi-sequence decode (qb_seq_*): n_seq sequences, each with its own recurrent
+    // slots, KV caches, control block and MTP hidden row, at these strides (floats) from
+    // sequence 0's; the single-sequence paths run on sequence cur_seq
+    int n_seq = 1, cur_seq = 0;
+    int ms_S = 1;                         // sequences of the forward being recorded (1: single sequence)
+    long long seq_conv = 0, seq_ssm = 0, seq_kv = 0, seq_mtpkv = 0;
+    float *conv_base = nullptr, *ssm_base = nullptr, *kv_k_base = nullptr, *kv_v_base = nullptr;
+    float *mtp_k_base = nullptr, *mtp_v_base = nullptr, *mtp_h_base = nullptr;
+    QbCtrl* ctrl_base = nullptr;
+    uint32_t* wam = nullptr;              // [2][QB_WIDE] argmax of the verify / MTP rows (multi-sequence)
+    std::vector<uint32_t> seq_pos;        // tokens consumed per sequence (host)
+    cudaGraphExec_t g_mcycle = nullptr;   // one multi-sequence cycle
+    int g_mcycle_k = -1;
+    size_t mcycle_kernels = 0;
 
     // graphs
     cudaGraphExec_t g_cycle = nullptr;
@@ -505,6 +520,7 @@ Engine::~Engine() {
             p = nullptr;
         }
     if (g_cycle) cudaGraphExecDestroy(g_cycle);
+    if (g_mcycle) cudaGraphExecDestroy(g_mcycle);
     if (g_greedy) cudaGraphExecDestroy(g_greedy);
     if (g_sample) cudaGraphExecDestroy(g_sample);
     for (cudaGraphExec_t& gp : g_prefill)
@@ -873,16 +889,17 @@ int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
         CK(cudaStreamSynchronize(e.st));
     }
 
-    // ---- activations ----
-    const int T8 = QB_MAX_TOK;
+    // ---- activations: QB_WIDE rows (multi-sequence forwards), QB_MAX_TOK for the
+    // tensor-parallel partial sums and the input preparation chunks ----
+    const int T8 = QB_MAX_TOK, TW = QB_WIDE;
     e.ld_qkv = std::max<int>({(int)d.conv_dim, 2 * (int)d.n_head * (int)d.head_dim, e.F, 2 * e.E});
     auto A = [&](size_t n) { return (float*)e.dalloc(n * 4); };
     {   // every buffer a GEMV writes, plus the TP flags, in one arena (peers map it)
-        const size_t sz[12] = {(size_t)T8 * e.E,      (size_t)T8 * e.ld_qkv,   (size_t)T8 * d.d_inner,
-                               (size_t)T8 * 256,      (size_t)T8 * 256,        (size_t)T8 * 2 * d.n_head * d.head_dim,
-                               (size_t)T8 * 2 * d.n_kv_head * d.head_dim,      (size_t)T8 * e.F,
-                               (size_t)T8 * e.F,      (size_t)T8 * e.V,        (size_t)T8 * e.E,
-                               (size_t)T8 * e.V};
+        const size_t sz[12] = {(size_t)TW * e.E,      (size_t)TW * e.ld_qkv,   (size_t)TW * d.d_inner,
+                               (size_t)TW * 256,      (size_t)TW * 256,        (size_t)TW * 2 * d.n_head * d.head_dim,
+                               (size_t)TW * 2 * d.n_kv_head * d.head_dim,      (size_t)TW * e.F,
+                               (size_t)TW * e.F,      (size_t)TW * e.V,        (size_t)TW * e.E,
+                               (size_t)TW * e.V};
         float** dst[12] = {&e.bx, &e.qkv, &e.z, &e.beta, &e.alpha, &e.qbuf, &e.kvbuf, &e.gate, &e.up, &e.logits,
                            &e.mtp_x, &e.mtp_logits};
         size_t off[12], total = 0;
@@ -905,20 +922,28 @@ int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
         e.tp.part = e.part;
         e.tp.part_slot = (long long)T8 * e.E;
     }
-    e.h_save = A((size_t)T8 * e.E);
-    e.qkvc = A((size_t)T8 * e.ld_qkv);
-    e.o = A((size_t)T8 * d.d_inner);
-    e.y = A((size_t)T8 * d.d_inner);
-    e.attn_o = A((size_t)T8 * d.n_head * d.head_dim);
-    e.act = A((size_t)T8 * e.F);
+    e.h_save = A((size_t)TW * e.E);
+    e.qkvc = A((size_t)TW * e.ld_qkv);
+    e.o = A((size_t)TW * d.d_inner);
+    e.y = A((size_t)TW * d.d_inner);
+    e.attn_o = A((size_t)TW * d.n_head * d.head_dim);
+    e.act = A((size_t)TW * e.F);
     e.mtp_h = A((size_t)e.E);
-    e.emb = A((size_t)T8 * e.E);
+    e.emb = A((size_t)TW * e.E);
+    e.wam = (uint32_t*)e.dalloc(2 * (size_t)TW * 4);
     const int Kmax = std::max<int>({2 * e.E, e.F, (int)d.d_inner, (int)(d.n_head * d.head_dim)});
-    e.xb.xfrag = (uint2*)e.dalloc(qb_xfrag_bytes(Kmax));
-    e.xb.xscale = A((size_t)T8 * (Kmax / 256));
-    e.xb.xsum = A((size_t)T8 * (Kmax / 32));
-    e.xb.xq = (uint2*)e.dalloc(qb_xq_bytes(Kmax));
-    e.xb.xqscale = A((size_t)T8 * (Kmax / 256));
+    // the GEMV input: QB_WIDE / QB_MAX_TOK chunks of QB_MAX_TOK rows (QbXBuf chunk strides)
+    const int NC = TW / T8;
+    e.xb.cs_frag = (long long)(qb_xfrag_bytes(Kmax) / sizeof(uint2));
+    e.xb.cs_scale = (long long)T8 * (Kmax / 256);
+    e.xb.cs_sum = (long long)T8 * (Kmax / 32);
+    e.xb.cs_q = (long long)(qb_xq_bytes(Kmax) / sizeof(uint2));
+    e.xb.cs_qscale = (long long)T8 * (Kmax / 256);
+    e.xb.xfrag = (uint2*)e.dalloc(NC * qb_xfrag_bytes(Kmax));
+    e.xb.xscale = A((size_t)NC * T8 * (Kmax / 256));
+    e.xb.xsum = A((size_t)NC * T8 * (Kmax / 32));
+    e.xb.xq = (uint2*)e.dalloc(NC * qb_xq_bytes(Kmax));
+    e.xb.xqscale = A((size_t)NC * T8 * (Kmax / 256));
     e.xb.xtc = (uint8_t*)e.dalloc(qb_xtc_bytes(Kmax));
     if (!e.xb.xtc) { set_err(-2, "activation alloc"); return -1; }
     if (e.fuse) {
@@ -942,19 +967,20 @@ int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
         e.attn_pml = (float2*)e.dalloc(q_rows * sizeof(float2));
         if (!e.attn_po || !e.attn_pml) { set_err(-2, "attention scratch alloc"); return -1; }
     }
-    e.gates = (float2*)e.dalloc((size_t)T8 * 256 * sizeof(float2));
-    e.keys = (unsigned long long*)e.dalloc(2 * T8 * sizeof(unsigned long long));
+    e.gates = (float2*)e.dalloc((size_t)TW * 256 * sizeof(float2));
+    e.keys = (unsigned long long*)e.dalloc(2 * TW * sizeof(unsigned long long));
     e.ctrl = (QbCtrl*)e.dalloc(sizeof(QbCtrl));
     e.d_prompt = (uint32_t*)e.dalloc((size_t)e.n_ctx * 4);
-    if (!e.bx || !e.logits || !e.xb.xfrag || !e.xb.xq || !e.ctrl || !e.emb || !e.keys || !e.d_prompt) {
+    if (!e.bx || !e.logits || !e.xb.xfrag || !e.xb.xq || !e.ctrl || !e.emb || !e.keys || !e.d_prompt || !e.wam) {
         set_err(-2, "activation alloc");
         return -1;
     }
-    CK(cudaMemset(e.xb.xfrag, 0, qb_xfrag_bytes(Kmax)));
-    CK(cudaMemset(e.xb.xscale, 0, (size_t)T8 * (Kmax / 256) * 4));
-    CK(cudaMemset(e.xb.xsum, 0, (size_t)T8 * (Kmax / 32) * 4));
-    CK(cudaMemset(e.xb.xq, 0, qb_xq_bytes(Kmax)));
-    CK(cudaMemset(e.xb.xqscale, 0, (size_t)T8 * (Kmax / 256) * 4));
+    CK(cudaMemset(e.xb.xfrag, 0, NC * qb_xfrag_bytes(Kmax)));
+    CK(cudaMemset(e.xb.xscale, 0, (size_t)NC * T8 * (Kmax / 256) * 4));
+    CK(cudaMemset(e.xb.xsum, 0, (size_t)NC * T8 * (Kmax / 32) * 4));
+    CK(cudaMemset(e.xb.xq, 0, NC * qb_xq_bytes(Kmax)));
+    CK(cudaMemset(e.xb.xqscale, 0, (size_t)NC * T8 * (Kmax / 256) * 4));
+    CK(cudaMemset(e.wam, 0, 2 * (size_t)TW * 4));
     CK(cudaMemset(e.ctrl, 0, sizeof(QbCtrl)));
     CK(cudaMemset(e.mtp_h, 0, (size_t)e.E * 4));
     {   // GEMV scratch: arrival counters for the largest launch (head or fused FFN / mixer)
@@ -964,6 +990,15 @@ int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
     CK(cudaEventCreate(&e.ev0));
     CK(cudaEventCreate(&e.ev1));
     CK(cudaDeviceSynchronize());
+    e.conv_base = e.conv_slots;
+    e.ssm_base = e.ssm_slots;
+    e.kv_k_base = e.kv_k;
+    e.kv_v_base = e.kv_v;
+    e.mtp_k_base = e.mtp_k;
+    e.mtp_v_base = e.mtp_v;
+    e.mtp_h_base = e.mtp_h;
+    e.ctrl_base = e.ctrl;
+    e.seq_pos.assign(1, 0u);
     return 0;
 }
 
@@ -981,6 +1016,23 @@ enum TpMode {
 int gemv_group(Engine& e, const DevMat* const* mats, float* const* outs, const long long* ldos, int nm, int K,
                int N, int accumulate, const QbEpi* epi = nullptr, int tp_mode = TP_LOCAL) {
     if (epi && nm != 1) { set_err(-1, "fused epilogue on a multi-matrix GEMV"); return -1; }
+    if (N > QB_MAX_TOK) {   // wide input (multi-sequence forward): one weight sweep per chunk of QB_MAX_TOK rows
+        if (N > QB_WIDE || nm > QB_MAX_SEG * 4 || epi || e.xss || e.use_tc || e.tp_world > 1) {
+            set_err(-1, "wide GEMV: at most %d rows, no fused epilogue, one GPU", QB_WIDE);
+            return -1;
+        }
+        const QbXBuf xb0 = e.xb;
+        for (int c = 0; c * QB_MAX_TOK < N; ++c) {
+            float* oc[QB_MAX_SEG * 4];
+            for (int i = 0; i < nm; ++i) oc[i] = outs[i] + (size_t)c * QB_MAX_TOK * ldos[i];
+            e.xb = qb_xb_chunk(xb0, c);
+            const int r = gemv_group(e, mats, oc, ldos, nm, K, std::min(QB_MAX_TOK, N - c * QB_MAX_TOK), accumulate,
+                                     nullptr, tp_mode);
+            e.xb = xb0;
+            if (r) return -1;
+        }
+        return 0;
+    }
     const QbInNorm in_norm{e.xss, e.eps};
     // fuse matrices of the same type; different types run as separate launches
     int i = 0;
@@ -1025,6 +1077,16 @@ int gemv_group(Engine& e, const DevMat* const* mats, float* const* outs, const l
     }
     return 0;
 }
+
+// The sequences of the forward being recorded: e.ms_S sequences of B / e.ms_S rows,
+// control blocks sizeof(QbCtrl) apart, states `state` floats apart.
+QbSeqs seqs(const Engine& e, int B, long long state) {
+    return QbSeqs{e.ms_S, B / e.ms_S, (long long)(sizeof(QbCtrl) / 4), state};
+}
+// where the verify / MTP heads leave their argmax: the control block of a single
+// sequence, the flat per-row arrays of a multi-sequence forward
+uint32_t* am_verify(Engine& e) { return e.ms_S > 1 ? e.wam : e.ctrl->argmax; }
+uint32_t* am_mtp(Engine& e) { return e.ms_S > 1 ? e.wam + QB_WIDE : e.ctrl->mtp_argmax; }
 
 // a kernel other than a GEMV epilogue is about to write e.xb
 void fresh_input(Engine& e) {
@@ -1118,7 +1180,8 @@ NextIn ffn_in(const Engine& e, const LayerW& l, int B) {
 
 // gated attention block on residual x, positions *pos .. *pos+B-1
 int attn_block(Engine& e, const LayerW& l, float* x, int B, const uint32_t* pos, float* kc, float* vc,
-               const NextIn& next) {
+               long long kv_seq, const NextIn& next) {
+    const QbSeqs sq = seqs(e, B, kv_seq);
     // this rank's q-heads and kv-heads (all of them on one GPU)
     const qwen_dims_t& d = e.d;
     const int qw = 2 * d.n_head * d.head_dim, kvw = d.n_kv_head * d.head_dim, kvw_loc = e.nkv_loc * d.head_dim;
@@ -1128,10 +1191,10 @@ int attn_block(Engine& e, const LayerW& l, float* x, int B, const uint32_t* pos,
     const long long ld3[3] = {qw, 2 * kvw, 2 * kvw};
     if (gemv_group(e, m3, o3, ld3, 3, e.E, B, 0)) return -1;
     CK(qb_attn_prep(e.qbuf, qw, e.kvbuf, 2 * kvw, l.q_norm, l.k_norm, e.nh_loc, e.nkv_loc, d.head_dim,
-                    e.rope_half, e.rope_cos, e.rope_sin, pos, B, e.eps, kc, vc, e.st));
+                    e.rope_half, e.rope_cos, e.rope_sin, pos, B, e.eps, kc, vc, e.st, &sq));
     fresh_input(e);
     CK(qb_attn_decode(e.qbuf, qw, kc, vc, e.nh_loc, e.nkv_loc, d.head_dim, pos, B, e.n_ctx, e.attn_o,
-                      e.nh_loc * d.head_dim, e.attn_po, e.attn_pml, e.xb, xp_needs(e, {&l.o}, B), e.st));
+                      e.nh_loc * d.head_dim, e.attn_po, e.attn_pml, e.xb, xp_needs(e, {&l.o}, B), e.st, &sq));
     QbEpi eb;
     if (residual_gemv(e, &l.o, x, e.nh_loc * d.head_dim, B, residual_epi(e, ffn_in(e, l, B), eb))) return -1;
     return ffn_block(e, l, x, B, next);
@@ -1149,10 +1212,11 @@ int gdn_block(Engine& e, const LayerW& l, int B, int ckpt, const NextIn& next) {
     if (gemv_group(e, m4, o4, ld4, 4, e.E, B, 0)) return -1;
     float* conv = e.conv_slots + (size_t)l.ridx * e.conv_layer;
     float* ssm = e.ssm_slots + (size_t)l.ridx * e.ssm_layer;
+    const QbSeqs sq_conv = seqs(e, B, e.seq_conv), sq_ssm = seqs(e, B, e.seq_ssm);
     CK(qb_gdn_conv(e.qkv, e.ld_qkv, conv_loc, B, l.conv_w, conv, e.conv_slot_stride, &e.ctrl->cur_slot, ckpt,
-                   e.qkvc, e.ld_qkv, e.beta, e.alpha, 256, l.dt_bias, l.ssm_a, e.nv_loc, e.gates, e.st));
+                   e.qkvc, e.ld_qkv, e.beta, e.alpha, 256, l.dt_bias, l.ssm_a, e.nv_loc, e.gates, e.st, &sq_conv));
     CK(qb_gdn_recur(e.qkvc, e.ld_qkv, e.gates, e.nk_loc, e.nv_loc, d.head_k_dim, B, e.eps, ssm,
-                    e.ssm_slot_stride, &e.ctrl->cur_slot, ckpt, e.o, d.d_inner, e.st));
+                    e.ssm_slot_stride, &e.ctrl->cur_slot, ckpt, e.o, d.d_inner, e.st, &sq_ssm));
     fresh_input(e);
     if (d.head_v_dim == 128 && e.nv_loc % 2 == 0) {
         CK(qb_gdn_out_xprep(e.o, e.z, d.d_inner, l.ssm_norm, e.nv_loc, d.head_v_dim, B, e.eps, e.y, e.xb,
@@ -1173,6 +1237,12 @@ __global__ void set_u32_kernel(uint32_t* p, uint32_t v) {
     pdl_wait();
     pdl_trigger();
     *p = v;
+}
+// cur_slot of the control blocks of all sequences (one block each)
+__global__ void set_slot_kernel(QbCtrl* c, uint32_t v) {
+    pdl_wait();
+    pdl_trigger();
+    if (threadIdx.x == 0) c[blockIdx.x].cur_slot = v;
 }
 __global__ void copy_f32_kernel(float* __restrict__ dst, const float* __restrict__ src, int n) {
     pdl_wait();
@@ -1213,7 +1283,8 @@ int head(Engine& e, float* out, int B, unsigned long long* keys, uint32_t* am, b
 // Without with_head (prefill chunks before the last) the output head and the
 // argmax are skipped: only the states, the KV cache and h_save advance.
 int fwd_backbone(Engine& e, int B, int ckpt, bool local_rows = false, bool with_head = true) {
-    CK(qb_embed(e.embd_type, e.tok_embd, e.E, e.ctrl->fwd_tok, B, e.bx, e.E, e.st));
+    const QbSeqs sq_tok = seqs(e, B, 0);
+    CK(qb_embed(e.embd_type, e.tok_embd, e.E, e.ctrl->fwd_tok, B, e.bx, e.E, e.st, &sq_tok));
     fresh_input(e);
     for (size_t il = 0; il < e.L.size(); ++il) {
         const LayerW& l = e.L[il];
@@ -1224,16 +1295,16 @@ int fwd_backbone(Engine& e, int B, int ckpt, bool local_rows = false, bool with_
         } else {
             float* kc = e.kv_k + (size_t)l.aidx * e.kv_layer;
             float* vc = e.kv_v + (size_t)l.aidx * e.kv_layer;
-            if (attn_block(e, l, e.bx, B, &e.ctrl->fwd_pos, kc, vc, next)) return -1;
+            if (attn_block(e, l, e.bx, B, &e.ctrl->fwd_pos, kc, vc, e.seq_kv, next)) return -1;
         }
     }
     CK(copy_f32(e.h_save, e.bx, B * e.E, e.st));
     if (with_head) {
         if (norm_input(e, e.bx, e.out_norm, B, xp_needs(e, {&e.output}, B))) return -1;
-        if (head(e, e.logits, B, e.keys, e.ctrl->argmax, local_rows)) return -1;
+        if (head(e, e.logits, B, e.keys, am_verify(e), local_rows)) return -1;
     }
-    if (ckpt) CK(qb_launch(set_u32_kernel, dim3(1), dim3(1), 0, e.st, &e.ctrl->cur_slot,
-                           (uint32_t)std::min(B - 1, kNSlot - 1)));
+    if (ckpt) CK(qb_launch(set_slot_kernel, dim3(e.ms_S), dim3(1), 0, e.st, e.ctrl,
+                           (uint32_t)std::min(B / e.ms_S - 1, kNSlot - 1)));
     CK(cudaGetLastError());
     return 0;
 }
@@ -1242,7 +1313,9 @@ int fwd_backbone(Engine& e, int B, int ckpt, bool local_rows = false, bool with_
 // ctrl->mtp_pos + b, hidden input = hsrc rows (mtp_h for the single-token
 // chain, h_save for the batch fill).  mtp_h <- output of the last token.
 int fwd_mtp(Engine& e, int B, const float* hsrc, int want_logits, bool local_rows = false) {
-    CK(qb_embed(e.embd_type, e.tok_embd, e.E, e.ctrl->mtp_tok, B, e.emb, e.E, e.st));
+    if (e.ms_S > 1 && B != e.ms_S) { set_err(-1, "multi-sequence MTP step: one row per sequence"); return -1; }
+    const QbSeqs sq_tok = seqs(e, B, 0);
+    CK(qb_embed(e.embd_type, e.tok_embd, e.E, e.ctrl->mtp_tok, B, e.emb, e.E, e.st, &sq_tok));
     QbXIn in[2] = {{e.emb, e.E, e.enorm, e.E}, {hsrc, e.E, e.hnorm, e.E}};
     fresh_input(e);
     CK(qb_xprep(in, 2, B, e.eps, e.xb, xp_needs(e, {&e.eh_proj}, B), e.st));
@@ -1251,51 +1324,72 @@ int fwd_mtp(Engine& e, int B, const float* hsrc, int want_logits, bool local_row
     const long long ld1[1] = {e.E};
     if (gemv_group(e, m1, o1, ld1, 1, 2 * e.E, B, 0)) return -1;
     const NextIn next = want_logits ? NextIn{e.shnorm, xp_needs(e, {&e.output}, B)} : NextIn{};
-    if (attn_block(e, e.mtp, e.mtp_x, B, &e.ctrl->mtp_pos, e.mtp_k, e.mtp_v, next)) return -1;
-    CK(copy_f32(e.mtp_h, e.mtp_x + (size_t)(B - 1) * e.E, e.E, e.st));
+    if (attn_block(e, e.mtp, e.mtp_x, B, &e.ctrl->mtp_pos, e.mtp_k, e.mtp_v, e.seq_mtpkv, next)) return -1;
+    if (e.ms_S > 1)   // every sequence's row: each sequence's MTP hidden
+        CK(copy_f32(e.mtp_h, e.mtp_x, B * e.E, e.st));
+    else
+        CK(copy_f32(e.mtp_h, e.mtp_x + (size_t)(B - 1) * e.E, e.E, e.st));
     if (want_logits) {
         if (norm_input(e, e.mtp_x, e.shnorm, B, xp_needs(e, {&e.output}, B))) return -1;
-        if (head(e, e.mtp_logits, B, e.keys + QB_MAX_TOK, e.ctrl->mtp_argmax, local_rows)) return -1;
+        if (head(e, e.mtp_logits, B, e.keys + QB_WIDE, am_mtp(e), local_rows)) return -1;
     }
     return 0;
 }
 
 // ------------------------- speculative cycle kernels ----------------------------
 
+// The cycle kernels run one block per sequence (blockIdx.x; one block for a single
+// sequence): control block c + blockIdx.x.
+//
 // cycle start: cand[0] = next_cand0; first draft input = (cand[0], P+1)
 __global__ void spec_start_kernel(QbCtrl* c) {
     pdl_wait();
     pdl_trigger();
+    c += blockIdx.x;
     c->cand[0] = c->next_cand0;
     c->mtp_tok[0] = c->cand[0];
     c->mtp_pos = c->P + 1;
 }
-// after draft s: cand[s] = argmax; next draft input = (cand[s], P+s+1)
-__global__ void spec_draft_kernel(QbCtrl* c, int s) {
+// after draft s: cand[s] = the draft's argmax (am[sequence]); next draft input = (cand[s], P+s+1)
+__global__ void spec_draft_kernel(QbCtrl* c, int s, const uint32_t* am) {
     pdl_wait();
     pdl_trigger();
-    c->cand[s] = c->mtp_argmax[0];
+    const uint32_t a = am[blockIdx.x];
+    c += blockIdx.x;
+    c->cand[s] = a;
     c->mtp_tok[0] = c->cand[s];
     c->mtp_pos = c->P + s + 1;
 }
 __global__ void spec_verify_setup_kernel(QbCtrl* c, int k) {
     pdl_wait();
     pdl_trigger();
+    c += blockIdx.x;
     for (int i = 0; i <= k; ++i) c->fwd_tok[i] = c->cand[i];
     c->fwd_pos = c->P + 1;
 }
 // acceptance (src/main.c:191-223): j = first i < k with argmax(logits_b[i])
 // != cand[i+1], or the forced length; emit cand[0..j]; live slot = j; MTP
 // anchor on (cand[j], h_save[j]) at P+j+1; next cand0 = argmax(logits_b[j]).
+// Sequence q reads the verify argmax am[q (k+1) + i] and h_save rows q (k+1) + i,
+// writes its tokens at out_tok + q * out_stride, its accept lengths at out_j + q *
+// j_stride and its MTP hidden row mtp_h + q E.
 __global__ void spec_accept_kernel(QbCtrl* c, int k, const uint32_t* forced, uint32_t* out_tok,
-                                   uint32_t* out_j, const float* h_save, float* mtp_h, int E) {
+                                   uint32_t* out_j, const float* h_save, float* mtp_h, int E, const uint32_t* am,
+                                   long long out_stride, long long j_stride) {
     pdl_wait();
     pdl_trigger();
+    const int q = blockIdx.x;
+    c += q;
+    am += (size_t)q * (k + 1);
+    out_tok += (size_t)q * out_stride;
+    out_j += (size_t)q * j_stride;
+    h_save += (size_t)q * (k + 1) * E;
+    mtp_h += (size_t)q * E;
     __shared__ uint32_t sj;
     if (threadIdx.x == 0) {
         uint32_t j = (uint32_t)k;
         for (int i = 0; i < k; ++i)
-            if (c->argmax[i] != c->cand[i + 1]) { j = (uint32_t)i; break; }
+            if (am[i] != c->cand[i + 1]) { j = (uint32_t)i; break; }
         if (c->n_forced) {
             j = forced[c->cycle % c->n_forced];
             if (j > (uint32_t)k) j = (uint32_t)k;
@@ -1310,7 +1404,7 @@ __global__ void spec_accept_kernel(QbCtrl* c, int k, const uint32_t* forced, uin
         const uint32_t P_new = c->P + j + 1;
         c->mtp_tok[0] = c->cand[j];
         c->mtp_pos = P_new;              // anchor position P + j + 1
-        c->next_cand0 = c->argmax[j];
+        c->next_cand0 = am[j];
         c->P = P_new;
         sj = j;
     }
@@ -1331,16 +1425,18 @@ __global__ void greedy_step_kernel(QbCtrl* c, uint32_t* out_tok) {
 }
 
 int record_cycle(Engine& e, int k) {
-    CK(qb_launch(spec_start_kernel, dim3(1), dim3(1), 0, e.st, e.ctrl));
+    const int S = e.ms_S;
+    CK(qb_launch(spec_start_kernel, dim3(S), dim3(1), 0, e.st, e.ctrl));
     for (int s = 1; s <= k; ++s) {
-        if (fwd_mtp(e, 1, e.mtp_h, 1, true)) return -1;
-        CK(qb_launch(spec_draft_kernel, dim3(1), dim3(1), 0, e.st, e.ctrl, s));
+        if (fwd_mtp(e, S, e.mtp_h, 1, true)) return -1;
+        CK(qb_launch(spec_draft_kernel, dim3(S), dim3(1), 0, e.st, e.ctrl, s, (const uint32_t*)am_mtp(e)));
     }
-    CK(qb_launch(spec_verify_setup_kernel, dim3(1), dim3(1), 0, e.st, e.ctrl, k));
-    if (fwd_backbone(e, k + 1, 1, true)) return -1;
-    CK(qb_launch(spec_accept_kernel, dim3(1), dim3(256), 0, e.st, e.ctrl, k, (const uint32_t*)e.d_forced, e.d_out_tok,
-                 e.d_out_j, (const float*)e.h_save, e.mtp_h, e.E));
-    if (fwd_mtp(e, 1, e.mtp_h, 0)) return -1;
+    CK(qb_launch(spec_verify_setup_kernel, dim3(S), dim3(1), 0, e.st, e.ctrl, k));
+    if (fwd_backbone(e, S * (k + 1), 1, true)) return -1;
+    CK(qb_launch(spec_accept_kernel, dim3(S), dim3(256), 0, e.st, e.ctrl, k, (const uint32_t*)e.d_forced, e.d_out_tok,
+                 e.d_out_j, (const float*)e.h_save, e.mtp_h, e.E, (const uint32_t*)am_verify(e),
+                 (long long)e.cap_out, (long long)e.cap_j));
+    if (fwd_mtp(e, S, e.mtp_h, 0)) return -1;
     CK(cudaGetLastError());
     return 0;
 }
@@ -1456,14 +1552,16 @@ int ensure_out_buffers(Engine& e, uint32_t n_out, uint32_t n_j, uint32_t n_force
     if (n_out > e.cap_out || n_j > e.cap_j || n_forced > e.cap_forced) {
         // buffers captured in graphs: re-capture after reallocation
         if (e.g_cycle) { cudaGraphExecDestroy(e.g_cycle); e.g_cycle = nullptr; }
+        if (e.g_mcycle) { cudaGraphExecDestroy(e.g_mcycle); e.g_mcycle = nullptr; }
         if (e.g_greedy) { cudaGraphExecDestroy(e.g_greedy); e.g_greedy = nullptr; }
         if (e.g_sample) { cudaGraphExecDestroy(e.g_sample); e.g_sample = nullptr; }
         const uint32_t co = std::max(n_out, std::max(e.cap_out, 4096u));
         const uint32_t cj = std::max(n_j, std::max(e.cap_j, 4096u));
         const uint32_t cf = std::max(n_forced, std::max(e.cap_forced, 1024u));
         uint32_t *a = nullptr, *b = nullptr, *f = nullptr;
-        CK(cudaMalloc(&a, (size_t)co * 4));
-        CK(cudaMalloc(&b, (size_t)cj * 4));
+        // per sequence: cap_out tokens and cap_j accept lengths
+        CK(cudaMalloc(&a, (size_t)co * e.n_seq * 4));
+        CK(cudaMalloc(&b, (size_t)cj * e.n_seq * 4));
         CK(cudaMalloc(&f, (size_t)cf * 4));
         if (e.d_out_tok) cudaFree(e.d_out_tok);
         if (e.d_out_j) cudaFree(e.d_out_j);
@@ -1492,6 +1590,33 @@ int dev_sync(Engine& e) {
         return -1;
     }
     return 0;
+}
+
+// Graphs record the state pointers of the sequence they were captured for.
+void drop_graphs(Engine& e) {
+    cudaGraphExec_t* gs[] = {&e.g_cycle, &e.g_mcycle, &e.g_greedy, &e.g_sample, &e.g_prefill[0], &e.g_prefill[1]};
+    for (cudaGraphExec_t* g : gs)
+        if (*g) {
+            cudaGraphExecDestroy(*g);
+            *g = nullptr;
+        }
+    e.g_cycle_k = e.g_mcycle_k = -1;
+}
+
+// Sequence s's recurrent slots, KV caches, control block and MTP hidden row become
+// the ones the single-sequence paths use.
+void select_seq(Engine& e, int s) {
+    if (s == e.cur_seq) return;
+    drop_graphs(e);
+    e.conv_slots = e.conv_base + (size_t)s * e.seq_conv;
+    e.ssm_slots = e.ssm_base + (size_t)s * e.seq_ssm;
+    e.kv_k = e.kv_k_base + (size_t)s * e.seq_kv;
+    e.kv_v = e.kv_v_base + (size_t)s * e.seq_kv;
+    e.mtp_k = e.mtp_k_base + (size_t)s * e.seq_mtpkv;
+    e.mtp_v = e.mtp_v_base + (size_t)s * e.seq_mtpkv;
+    e.mtp_h = e.mtp_h_base + (size_t)s * e.E;
+    e.ctrl = e.ctrl_base + s;
+    e.cur_seq = s;
 }
 
 int sync_host_mirrors_after_batch(qwen_model_t* m, Engine& e, int B) {
@@ -1653,7 +1778,7 @@ static void one_layer(qwen_model_t* m, const qwen_layer_t* L, uint32_t pos, bool
     } else {
         float* kc = e->kv_k + (size_t)l.aidx * e->kv_layer;
         float* vc = e->kv_v + (size_t)l.aidx * e->kv_layer;
-        r = attn_block(*e, l, e->bx, 1, &e->ctrl->fwd_pos, kc, vc, next);
+        r = attn_block(*e, l, e->bx, 1, &e->ctrl->fwd_pos, kc, vc, 0, next);
     }
     fresh_input(*e);
     e->xready = false;
@@ -1932,6 +2057,151 @@ extern "C" int qb_reset(qwen_model_t* m) {
     memset(m->mtp_h, 0, (size_t)e->E * 4);
     m->pos = 0;
     return 0;
+}
+
+// ------------------------- multi-sequence decode ---------------------------------
+// n_seq sequences share the weights; each gets its own recurrent slots, KV caches,
+// control block and MTP hidden row (all zero), and one qb_seq_generate cycle runs
+// drafts, verify and acceptance of all of them with one weight sweep per step:
+// the MTP drafts at n_seq rows, the verify at n_seq (k + 1) rows, in QB_MAX_TOK-row
+// GEMV chunks.
+extern "C" int qb_seq_init(qwen_model_t* m, uint32_t n_seq) {
+    Engine* e = E_(m);
+    if (!e || n_seq < 1 || n_seq > QB_MAX_SEQ) { set_err(-1, "qb_seq_init: 1..%d sequences", QB_MAX_SEQ); return -1; }
+    if (e->tp_world > 1 || e->fuse || e->use_tc) {
+        set_err(-1, "qb_seq_init: multi-sequence decode runs on one GPU with the default GEMV paths");
+        return -1;
+    }
+    CK(cudaSetDevice(e->dev));
+    CK(cudaStreamSynchronize(e->st));
+    select_seq(*e, 0);
+    drop_graphs(*e);
+    int na = 0;
+    for (const LayerW& l : e->L) na += l.rec ? 0 : 1;
+    const size_t conv1 = std::max<size_t>(1, e->conv_slot_stride * kNSlot), ssm1 = std::max<size_t>(1, e->ssm_slot_stride * kNSlot);
+    const size_t kv1 = std::max<size_t>(1, e->kv_layer * (size_t)na), mtp1 = e->kv_layer, h1 = (size_t)e->E;
+    const size_t q_rows = (size_t)e->d.n_head * QB_MAX_TOK * qb_attn_max_chunks(e->n_ctx);
+    void* olds[] = {e->conv_base, e->ssm_base, e->kv_k_base, e->kv_v_base, e->mtp_k_base, e->mtp_v_base,
+                    e->mtp_h_base, e->ctrl_base, e->attn_po, e->attn_pml};
+    for (void* p : olds) e->dfree(p);
+    const size_t S = n_seq;
+    e->conv_base = (float*)e->dalloc(S * conv1 * 4);
+    e->ssm_base = (float*)e->dalloc(S * ssm1 * 4);
+    e->kv_k_base = (float*)e->dalloc(S * kv1 * 4);
+    e->kv_v_base = (float*)e->dalloc(S * kv1 * 4);
+    e->mtp_k_base = (float*)e->dalloc(S * mtp1 * 4);
+    e->mtp_v_base = (float*)e->dalloc(S * mtp1 * 4);
+    e->mtp_h_base = (float*)e->dalloc(S * h1 * 4);
+    e->ctrl_base = (QbCtrl*)e->dalloc(S * sizeof(QbCtrl));
+    e->attn_po = (float*)e->dalloc(S * q_rows * e->d.head_dim * 4);
+    e->attn_pml = (float2*)e->dalloc(S * q_rows * sizeof(float2));
+    if (!e->conv_base || !e->ssm_base || !e->kv_k_base || !e->kv_v_base || !e->mtp_k_base || !e->mtp_v_base ||
+        !e->mtp_h_base || !e->ctrl_base || !e->attn_po || !e->attn_pml) {
+        set_err(-2, "qb_seq_init: state alloc for %u sequences", n_seq);
+        return -1;   // the model is unusable now; model_free releases what was allocated
+    }
+    CK(cudaMemsetAsync(e->conv_base, 0, S * conv1 * 4, e->st));
+    CK(cudaMemsetAsync(e->ssm_base, 0, S * ssm1 * 4, e->st));
+    CK(cudaMemsetAsync(e->mtp_h_base, 0, S * h1 * 4, e->st));
+    CK(cudaMemsetAsync(e->ctrl_base, 0, S * sizeof(QbCtrl), e->st));
+    e->seq_conv = (long long)conv1;
+    e->seq_ssm = (long long)ssm1;
+    e->seq_kv = (long long)kv1;
+    e->seq_mtpkv = (long long)mtp1;
+    e->n_seq = (int)n_seq;
+    e->cur_seq = -1;
+    select_seq(*e, 0);
+    e->seq_pos.assign(n_seq, 0u);
+    // per-sequence output buffers are sized on the next call
+    if (e->d_out_tok) cudaFree(e->d_out_tok);
+    if (e->d_out_j) cudaFree(e->d_out_j);
+    e->d_out_tok = e->d_out_j = nullptr;
+    e->cap_out = e->cap_j = 0;
+    if (dev_sync(*e)) return -1;
+    memset(m->mtp_h, 0, (size_t)e->E * 4);
+    m->pos = 0;
+    return 0;
+}
+
+extern "C" int qb_seq_prefill(qwen_model_t* m, uint32_t seq, const uint32_t* tokens, uint32_t n) {
+    Engine* e = E_(m);
+    if (!e || seq >= (uint32_t)e->n_seq) { set_err(-1, "qb_seq_prefill: no sequence %u", seq); return -1; }
+    CK(cudaSetDevice(e->dev));
+    select_seq(*e, (int)seq);
+    if (qb_prefill(m, tokens, n, 1)) return -1;
+    e->seq_pos[seq] = n;
+    return 0;
+}
+
+extern "C" int qb_seq_generate(qwen_model_t* m, uint32_t n_cycles, uint32_t n_spec, const uint32_t* forced,
+                               uint32_t n_forced, uint32_t* out_tokens, uint32_t cap, uint32_t* out_counts,
+                               uint32_t* out_j) {
+    Engine* e = E_(m);
+    if (!e || !out_tokens || !out_counts || cap == 0) { set_err(-1, "qb_seq_generate: bad arguments"); return -1; }
+    CK(cudaSetDevice(e->dev));
+    const int S = e->n_seq;
+    const int k = (int)std::min<uint32_t>(n_spec, SPEC_MAX_B - 1);
+    if (k < 1 || S * (k + 1) > QB_WIDE) {
+        set_err(-1, "qb_seq_generate: n_spec must be >= 1 and n_seq (n_spec + 1) <= %d", QB_WIDE);
+        return -1;
+    }
+    for (int s = 0; s < S; ++s)
+        if (e->seq_pos[s] == 0) { set_err(-1, "qb_seq_generate: sequence %d has no prefill", s); return -1; }
+    if (ensure_out_buffers(*e, cap + (uint32_t)k + 1, n_cycles, n_forced)) return -1;
+    select_seq(*e, 0);
+    if (!e->g_mcycle || e->g_mcycle_k != k) {
+        if (e->g_mcycle) { cudaGraphExecDestroy(e->g_mcycle); e->g_mcycle = nullptr; }
+        e->ms_S = S;
+        const int r = capture(*e, &e->g_mcycle, record_cycle, k);
+        e->ms_S = 1;
+        if (r) return -1;
+        e->g_mcycle_k = k;
+        e->mcycle_kernels = g_last_graph_kernels;
+    }
+    // loop state of every sequence: P = tokens consumed - 1, counters reset
+    std::vector<QbCtrl> hc((size_t)S);
+    CK(cudaMemcpyAsync(hc.data(), e->ctrl_base, S * sizeof(QbCtrl), cudaMemcpyDeviceToHost, e->st));
+    if (dev_sync(*e)) return -1;
+    for (int s = 0; s < S; ++s) {
+        hc[s].P = e->seq_pos[s] - 1;
+        hc[s].k = (uint32_t)k;
+        hc[s].cycle = 0;
+        hc[s].n_out = 0;
+        hc[s].n_forced = n_forced;
+        hc[s].cap_out = std::min(cap, e->cap_out);
+        hc[s].cap_j = std::min(n_cycles, e->cap_j);
+    }
+    CK(cudaMemcpyAsync(e->ctrl_base, hc.data(), S * sizeof(QbCtrl), cudaMemcpyHostToDevice, e->st));
+    if (n_forced) CK(cudaMemcpyAsync(e->d_forced, forced, n_forced * 4, cudaMemcpyHostToDevice, e->st));
+    uint32_t cycles = 0;
+    CK(cudaEventRecord(e->ev0, e->st));
+    while (cycles < n_cycles) {
+        // every cycle moves a sequence by at most k + 1 positions; verify writes P+1..P+k+1
+        uint32_t Pmax = 0;
+        for (int s = 0; s < S; ++s) Pmax = std::max(Pmax, hc[s].P);
+        const uint32_t room = (uint32_t)e->n_ctx > Pmax + (uint32_t)k + 2 ? ((uint32_t)e->n_ctx - Pmax - k - 2) / (k + 1) : 0;
+        const uint32_t batch = std::min(std::min(n_cycles - cycles, 32u), room);
+        if (batch == 0) break;
+        for (uint32_t i = 0; i < batch; ++i) CK(cudaGraphLaunch(e->g_mcycle, e->st));
+        cycles += batch;
+        CK(cudaMemcpyAsync(hc.data(), e->ctrl_base, S * sizeof(QbCtrl), cudaMemcpyDeviceToHost, e->st));
+        if (dev_sync(*e)) return -1;
+    }
+    CK(cudaEventRecord(e->ev1, e->st));
+    CK(cudaEventSynchronize(e->ev1));
+    cudaEventElapsedTime(&e->last_ms, e->ev0, e->ev1);
+    for (int s = 0; s < S; ++s) {
+        out_counts[s] = std::min(hc[s].n_out, cap);
+        CK(cudaMemcpyAsync(out_tokens + (size_t)s * cap, e->d_out_tok + (size_t)s * e->cap_out, (size_t)out_counts[s] * 4,
+                           cudaMemcpyDeviceToHost, e->st));
+        if (out_j)
+            CK(cudaMemcpyAsync(out_j + (size_t)s * n_cycles, e->d_out_j + (size_t)s * e->cap_j,
+                               (size_t)std::min(cycles, hc[s].cap_j) * 4, cudaMemcpyDeviceToHost, e->st));
+        e->seq_pos[s] = hc[s].P + 1;
+    }
+    if (dev_sync(*e)) return -1;
+    m->pos = e->seq_pos[0];
+    return (int)cycles;
 }
 
 namespace {

@@ -44,6 +44,29 @@ struct QbXBuf {
     float* xqscale;          // [QB_MAX_TOK][K/256] power-of-two scale of xq and xtc
     uint8_t* xtc;            // int8 digits as tcgen05 B tiles, 4 KB per 256 columns (N <= 4)
     uint8_t* xtc16;          // the same for up to 16 tokens, 12 KB per 256 columns (qb_qmv_tc16)
+    // Wide inputs (N > QB_MAX_TOK, up to QB_WIDE rows): row r is row r % 8 of chunk
+    // r / 8, and chunk c is an input of its own (min(8, N - 8c) rows, the N <= 8
+    // layouts above) at these element offsets times c (qb_xb_chunk).  xtc / xtc16
+    // are not chunked.
+    long long cs_frag, cs_scale, cs_sum, cs_q, cs_qscale;
+};
+// chunk c of a wide input (qb_kernels.h QbXBuf)
+__host__ __device__ inline QbXBuf qb_xb_chunk(const QbXBuf& xb, int c) {
+    QbXBuf r = xb;
+    r.xfrag = xb.xfrag ? xb.xfrag + c * xb.cs_frag : nullptr;
+    r.xscale = xb.xscale ? xb.xscale + c * xb.cs_scale : nullptr;
+    r.xsum = xb.xsum ? xb.xsum + c * xb.cs_sum : nullptr;
+    r.xq = xb.xq ? xb.xq + c * xb.cs_q : nullptr;
+    r.xqscale = xb.xqscale ? xb.xqscale + c * xb.cs_qscale : nullptr;
+    return r;
+}
+// Independent sequences in one launch of a stateful layer kernel (multi-sequence
+// decode): sequence s covers input rows [s * T, s * T + T); its position and
+// recurrent-slot words lie `ctrl` 32-bit words after sequence 0's, its state
+// (recurrent slots, KV cache) `state` floats after.  One sequence: {B, 0, 0}.
+struct QbSeqs {
+    int S, T;
+    long long ctrl, state;
 };
 enum { QB_XP_F16 = 1, QB_XP_SUM = 2, QB_XP_I8 = 4, QB_XP_TC = 8, QB_XP_TC16 = 16 };   // qb_xprep outputs
 #define QB_TC16_TOK 16       // input vectors of one qb_qmv_tc16 launch; xqscale rows it needs
@@ -148,29 +171,33 @@ cudaError_t qb_qmv_f32(const float* W, int rows, int K, const float* x, long lon
 // ---- layer kernels (qb_layers.cu) ----
 struct QbCtrl;   // device control block (qb_engine.h)
 
+// The stateful kernels take the sequences of a multi-sequence forward (sq: S
+// sequences of T rows, S * T == B; nullptr: one sequence of B rows).  qb_embed:
+// row b's token is tokens[(b / T) * sq->ctrl + b % T].
 cudaError_t qb_embed(int type, const void* tok_embd, int n_embd, const uint32_t* tokens, int B, float* out,
-                     long long ldo, cudaStream_t st);
+                     long long ldo, cudaStream_t st, const QbSeqs* sq = nullptr);
 // conv1d + SiLU of all channels, plus the recurrence gates (beta, decay) per (token, v-head)
 cudaError_t qb_gdn_conv(const float* qkv, long long ld_qkv, int conv_dim, int B, const float* conv_w,
                         float* state_slots, size_t slot_stride, const uint32_t* cur_slot, int ckpt,
                         float* out, long long ld_out, const float* beta, const float* alpha, long long ld_ba,
-                        const float* dt_bias, const float* ssm_a, int n_v, float2* gates, cudaStream_t st);
+                        const float* dt_bias, const float* ssm_a, int n_v, float2* gates, cudaStream_t st,
+                        const QbSeqs* sq = nullptr);
 cudaError_t qb_gdn_recur(const float* qkvc, long long ld_qkvc, const float2* gates, int n_k, int n_v, int dk, int B,
                          float eps, float* state_slots, size_t slot_stride, const uint32_t* cur_slot, int ckpt,
-                         float* out, long long ld_out, cudaStream_t st);
+                         float* out, long long ld_out, cudaStream_t st, const QbSeqs* sq = nullptr);
 cudaError_t qb_gdn_out(const float* o, const float* z, long long ld, const float* norm_w, int n_v, int dv,
                        int B, float eps, float* y, cudaStream_t st);
 cudaError_t qb_attn_prep(float* q, long long ldq, const float* kv, long long ldkv, const float* q_norm,
                          const float* k_norm, int n_head, int n_kv, int hd, int rope_half,
                          const float* rope_cos, const float* rope_sin, const uint32_t* pos, int B, float eps,
-                         float* k_cache, float* v_cache, cudaStream_t st);
-// attention scratch: part_o [n_head][QB_MAX_TOK][qb_attn_max_chunks(n_ctx)][256] floats,
-// part_ml [n_head][QB_MAX_TOK][qb_attn_max_chunks(n_ctx)] float2
+                         float* k_cache, float* v_cache, cudaStream_t st, const QbSeqs* sq = nullptr);
+// attention scratch: part_o [S][n_head][QB_MAX_TOK][qb_attn_max_chunks(n_ctx)][256] floats,
+// part_ml [S][n_head][QB_MAX_TOK][qb_attn_max_chunks(n_ctx)] float2 (S sequences)
 int qb_attn_max_chunks(int n_ctx);
 cudaError_t qb_attn_decode(const float* q, long long ldq, const float* k_cache, const float* v_cache,
                            int n_head, int n_kv, int hd, const uint32_t* pos, int B, int n_ctx, float* out,
                            long long ldo, float* part_o, float2* part_ml, const QbXBuf& xb, int what,
-                           cudaStream_t st);   // also emits the o-projection GEMV input (what: QB_XP_*)
+                           cudaStream_t st, const QbSeqs* sq = nullptr);   // also emits the o-projection GEMV input
 // SwiGLU / gated RMSNorm fused with the GEMV activation prep of their output
 cudaError_t qb_silu_mul_xprep(const float* gate, const float* up, long long ld, int n, int B, float* out,
                               const QbXBuf& xb, int what, cudaStream_t st);

@@ -106,12 +106,14 @@ __host__ __device__ inline size_t row_bytes_of(int type, int n) {
     }
 }
 
+// row b's token: tok[(b / T) * tstride + b % T] (T rows per sequence, each
+// sequence's tokens tstride words apart)
 __global__ void embed_kernel(int type, const uint8_t* __restrict__ E, int n, const uint32_t* __restrict__ tok,
-                             float* __restrict__ out, long long ldo) {
+                             int T, long long tstride, float* __restrict__ out, long long ldo) {
     pdl_wait();
     pdl_trigger();
     const int b = blockIdx.y;
-    const uint8_t* row = E + (size_t)tok[b] * row_bytes_of(type, n);
+    const uint8_t* row = E + (size_t)tok[(size_t)(b / T) * tstride + b % T] * row_bytes_of(type, n);
     for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < n; e += gridDim.x * blockDim.x)
         out[(size_t)b * ldo + e] = dequant_elem(type, row, e);
 }
@@ -124,9 +126,20 @@ __global__ void gdn_conv_kernel(const float* __restrict__ qkv, long long ld_qkv,
                                 const uint32_t* __restrict__ cur_slot, int ckpt, float* __restrict__ out,
                                 long long ld_out, const float* __restrict__ beta, const float* __restrict__ alpha,
                                 long long ld_ba, const float* __restrict__ dt_bias, const float* __restrict__ ssm_a,
-                                int n_v, float2* __restrict__ gates) {
+                                int n_v, float2* __restrict__ gates, QbSeqs sq) {
     pdl_wait();
     pdl_trigger();
+    {   // sequence blockIdx.y: its B rows, its slots and slot index
+        const int sidx = blockIdx.y;
+        const size_t r0 = (size_t)sidx * B;
+        qkv += r0 * ld_qkv;
+        out += r0 * ld_out;
+        beta += r0 * ld_ba;
+        alpha += r0 * ld_ba;
+        gates += r0 * n_v;
+        slots += (size_t)sidx * sq.state;
+        cur_slot += (size_t)sidx * sq.ctrl;
+    }
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c < n_v * B) {
         // per (token, v-head) gates of the recurrence (src/model.c:494-500):
@@ -175,9 +188,18 @@ __global__ void __launch_bounds__(128) gdn_recur_kernel(
     const float* __restrict__ qkvc, long long ld_qkvc, const float2* __restrict__ gates, int n_k, int n_v, int B,
     float eps, float* __restrict__ slots,
     size_t slot_stride, const uint32_t* __restrict__ cur_slot, int ckpt, float* __restrict__ out,
-    long long ld_out) {
+    long long ld_out, QbSeqs sq) {
     pdl_wait();
     pdl_trigger();
+    {   // sequence blockIdx.z: its B rows, its slots and slot index
+        const int sidx = blockIdx.z;
+        const size_t r0 = (size_t)sidx * B;
+        qkvc += r0 * ld_qkvc;
+        gates += r0 * n_v;
+        out += r0 * ld_out;
+        slots += (size_t)sidx * sq.state;
+        cur_slot += (size_t)sidx * sq.ctrl;
+    }
     __shared__ float qn[QB_MAX_TOK][kDK], kn[QB_MAX_TOK][kDK];
     __shared__ float kq_s[QB_MAX_TOK], beta_s[QB_MAX_TOK], decay_s[QB_MAX_TOK];
     const int h = blockIdx.x, kh = h % n_k;
@@ -350,14 +372,17 @@ __global__ void attn_prep_kernel(float* __restrict__ q, long long ldq, const flo
                                  long long ldkv, const float* __restrict__ qw, const float* __restrict__ kw,
                                  int n_head, int n_kv, int hd, int half, const float* __restrict__ rc,
                                  const float* __restrict__ rs, const uint32_t* __restrict__ pos0, float eps,
-                                 float* __restrict__ kc, float* __restrict__ vc) {
+                                 float* __restrict__ kc, float* __restrict__ vc, QbSeqs sq) {
     pdl_wait();
     pdl_trigger();
-    const int b = blockIdx.y;
+    const int b = blockIdx.y;   // input row; sequence b / T, its token b % T
+    const int sidx = b / sq.T;
     const int unit = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     const int nj = hd / 32;   // 8 for hd = 256
-    const uint32_t pos = *pos0 + b;
+    const uint32_t pos = pos0[(size_t)sidx * sq.ctrl] + (uint32_t)(b - sidx * sq.T);
+    kc += (size_t)sidx * sq.state;
+    vc += (size_t)sidx * sq.state;
     const int kvrow = n_kv * hd;
     if (unit >= n_head + 2 * n_kv) return;
     float v[8];
@@ -427,11 +452,21 @@ __global__ void __launch_bounds__(256) attn_part_kernel(const float* __restrict_
                                                         const float* __restrict__ kc, const float* __restrict__ vc,
                                                         int n_head, int n_kv, const uint32_t* __restrict__ pos0p,
                                                         int B, float* __restrict__ part_o,
-                                                        float2* __restrict__ part_ml, int max_chunks) {
+                                                        float2* __restrict__ part_ml, int max_chunks, QbSeqs sq) {
     pdl_wait();
     pdl_trigger();
     constexpr int HD = kAttnHD, C = kAttnC, KS = HD + 4;   // padded rows: conflict-free 16-byte loads
     const int kh = blockIdx.x, c = blockIdx.y;
+    {   // sequence blockIdx.z: its B query rows, KV cache, position and chunk partials
+        const int sidx = blockIdx.z;
+        q += (size_t)sidx * B * ldq;
+        kc += (size_t)sidx * sq.state;
+        vc += (size_t)sidx * sq.state;
+        pos0p += (size_t)sidx * sq.ctrl;
+        const size_t pq = (size_t)sidx * n_head * QB_MAX_TOK * max_chunks;
+        part_ml += pq;
+        part_o += pq * HD;
+    }
     const int pos0 = (int)*pos0p;
     const int t0 = c * C;
     if (t0 >= pos0 + B) return;
@@ -541,17 +576,18 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const float* __restri
                                                            const float* __restrict__ part_o,
                                                            const float2* __restrict__ part_ml, int max_chunks,
                                                            int n_head, int N, float* __restrict__ out,
-                                                           long long ldo, QbXBuf xb, int what) {
+                                                           long long ldo, QbXBuf xb, int what, QbSeqs sq) {
     // a GEMV follows: release it before waiting, so that its CTAs take their places and
     // start streaming weights while this short kernel runs
     pdl_trigger();
     pdl_wait();
     constexpr int HD = kAttnHD;
-    const int b = blockIdx.y, lane = threadIdx.x & 31;
+    const int b = blockIdx.y, lane = threadIdx.x & 31;   // input row b: sequence b / T, its token b % T
     const int h = blockIdx.x * 4 + (threadIdx.x >> 5);
     if (h >= n_head) return;
-    const int nch = ((int)*pos0p + b) / kAttnC + 1;   // chunks holding positions 0 .. pos + b
-    const size_t qrow = (size_t)h * QB_MAX_TOK + b;
+    const int sidx = b / sq.T, tb = b - sidx * sq.T;
+    const int nch = ((int)pos0p[(size_t)sidx * sq.ctrl] + tb) / kAttnC + 1;   // chunks holding positions 0 .. pos + tb
+    const size_t qrow = ((size_t)sidx * n_head + h) * QB_MAX_TOK + tb;
     const float2* ml = part_ml + qrow * max_chunks;
     float M = -INFINITY;
     for (int cc = 0; cc < nch; ++cc) M = fmaxf(M, ml[cc].x);
@@ -834,30 +870,41 @@ __global__ void op_softmax_kernel(float* x, long long n) {
 
 // ================================ launchers ====================================
 
+// the sequences of a multi-sequence launch (sq, S * T == B rows), or one sequence of B rows
+static bool seqs_of(const QbSeqs* sq, int B, QbSeqs& out) {
+    out = sq ? *sq : QbSeqs{1, B, 0, 0};
+    return out.S >= 1 && out.S <= QB_MAX_SEQ && out.T >= 1 && out.S * out.T == B;
+}
+
 cudaError_t qb_embed(int type, const void* tok_embd, int n_embd, const uint32_t* tokens, int B, float* out,
-                     long long ldo, cudaStream_t st) {
-    qb_launch(embed_kernel, dim3((n_embd + 255) / 256, B), dim3(256), 0, st, type, (const uint8_t*)tok_embd, n_embd, tokens,
-                                                                out, ldo);
-    return cudaGetLastError();
+                     long long ldo, cudaStream_t st, const QbSeqs* sq) {
+    QbSeqs q;
+    if (!seqs_of(sq, B, q)) return cudaErrorInvalidValue;
+    return qb_launch(embed_kernel, dim3((n_embd + 255) / 256, B), dim3(256), 0, st, type, (const uint8_t*)tok_embd,
+                     n_embd, tokens, q.T, q.ctrl, out, ldo);
 }
 
 cudaError_t qb_gdn_conv(const float* qkv, long long ld_qkv, int conv_dim, int B, const float* conv_w,
                         float* state_slots, size_t slot_stride, const uint32_t* cur_slot, int ckpt,
                         float* out, long long ld_out, const float* beta, const float* alpha, long long ld_ba,
-                        const float* dt_bias, const float* ssm_a, int n_v, float2* gates, cudaStream_t st) {
-    const int threads = conv_dim > n_v * B ? conv_dim : n_v * B;
-    qb_launch(gdn_conv_kernel, dim3((threads + 127) / 128), dim3(128), 0, st, qkv, ld_qkv, conv_dim, B, conv_w,
-              state_slots, slot_stride, cur_slot, ckpt, out, ld_out, beta, alpha, ld_ba, dt_bias, ssm_a, n_v, gates);
-    return cudaGetLastError();
+                        const float* dt_bias, const float* ssm_a, int n_v, float2* gates, cudaStream_t st,
+                        const QbSeqs* sq) {
+    QbSeqs q;
+    if (!seqs_of(sq, B, q)) return cudaErrorInvalidValue;
+    const int T = q.T;
+    const int threads = conv_dim > n_v * T ? conv_dim : n_v * T;
+    return qb_launch(gdn_conv_kernel, dim3((threads + 127) / 128, q.S), dim3(128), 0, st, qkv, ld_qkv, conv_dim, T,
+                     conv_w, state_slots, slot_stride, cur_slot, ckpt, out, ld_out, beta, alpha, ld_ba, dt_bias, ssm_a,
+                     n_v, gates, q);
 }
 
 cudaError_t qb_gdn_recur(const float* qkvc, long long ld_qkvc, const float2* gates, int n_k, int n_v, int dk, int B,
                          float eps, float* state_slots, size_t slot_stride, const uint32_t* cur_slot, int ckpt,
-                         float* out, long long ld_out, cudaStream_t st) {
-    if (dk != kDK || B > QB_MAX_TOK) return cudaErrorInvalidValue;
-    qb_launch(gdn_recur_kernel, dim3(n_v, kDK / 16), dim3(128), 0, st, qkvc, ld_qkvc, gates, n_k, n_v, B, eps,
-              state_slots, slot_stride, cur_slot, ckpt, out, ld_out);
-    return cudaGetLastError();
+                         float* out, long long ld_out, cudaStream_t st, const QbSeqs* sq) {
+    QbSeqs q;
+    if (dk != kDK || !seqs_of(sq, B, q) || q.T > QB_MAX_TOK) return cudaErrorInvalidValue;
+    return qb_launch(gdn_recur_kernel, dim3(n_v, kDK / 16, q.S), dim3(128), 0, st, qkvc, ld_qkvc, gates, n_k, n_v, q.T,
+                     eps, state_slots, slot_stride, cur_slot, ckpt, out, ld_out, q);
 }
 
 cudaError_t qb_gdn_out(const float* o, const float* z, long long ld, const float* norm_w, int n_v, int dv,
@@ -869,13 +916,12 @@ cudaError_t qb_gdn_out(const float* o, const float* z, long long ld, const float
 cudaError_t qb_attn_prep(float* q, long long ldq, const float* kv, long long ldkv, const float* q_norm,
                          const float* k_norm, int n_head, int n_kv, int hd, int rope_half,
                          const float* rope_cos, const float* rope_sin, const uint32_t* pos, int B, float eps,
-                         float* k_cache, float* v_cache, cudaStream_t st) {
-    if (hd != 256 || rope_half % 32 != 0 || rope_half * 2 > hd) return cudaErrorInvalidValue;
+                         float* k_cache, float* v_cache, cudaStream_t st, const QbSeqs* sq) {
+    QbSeqs sqv;
+    if (hd != 256 || rope_half % 32 != 0 || rope_half * 2 > hd || !seqs_of(sq, B, sqv)) return cudaErrorInvalidValue;
     const int units = n_head + 2 * n_kv;
-    qb_launch(attn_prep_kernel, dim3((units + 3) / 4, B), dim3(128), 0, st, q, ldq, kv, ldkv, q_norm, k_norm, n_head, n_kv,
-                                                               hd, rope_half, rope_cos, rope_sin, pos, eps,
-                                                               k_cache, v_cache);
-    return cudaGetLastError();
+    return qb_launch(attn_prep_kernel, dim3((units + 3) / 4, B), dim3(128), 0, st, q, ldq, kv, ldkv, q_norm, k_norm,
+                     n_head, n_kv, hd, rope_half, rope_cos, rope_sin, pos, eps, k_cache, v_cache, sqv);
 }
 
 int qb_attn_max_chunks(int n_ctx) { return (n_ctx + kAttnC - 1) / kAttnC; }
@@ -883,8 +929,13 @@ int qb_attn_max_chunks(int n_ctx) { return (n_ctx + kAttnC - 1) / kAttnC; }
 cudaError_t qb_attn_decode(const float* q, long long ldq, const float* k_cache, const float* v_cache,
                            int n_head, int n_kv, int hd, const uint32_t* pos, int B, int n_ctx, float* out,
                            long long ldo, float* part_o, float2* part_ml, const QbXBuf& xb, int what,
-                           cudaStream_t st) {
-    if (hd != kAttnHD || n_kv < 1 || n_head % n_kv || B < 1 || B > QB_MAX_TOK) return cudaErrorInvalidValue;
+                           cudaStream_t st, const QbSeqs* sq) {
+    QbSeqs sqv;
+    if (hd != kAttnHD || n_kv < 1 || n_head % n_kv || B < 1 || B > QB_WIDE || !seqs_of(sq, B, sqv) ||
+        sqv.T > QB_MAX_TOK)
+        return cudaErrorInvalidValue;
+    const int N = B;   // rows of all sequences; B from here on: rows per sequence
+    B = sqv.T;
     const int G = n_head / n_kv, NQ = G * B;
     if ((NQ + 7) / 8 > kAttnMaxQPT) return cudaErrorInvalidValue;
     const int max_chunks = qb_attn_max_chunks(n_ctx);
@@ -902,8 +953,8 @@ cudaError_t qb_attn_decode(const float* q, long long ldq, const float* k_cache, 
                 return e;                                                                                       \
             configured_for = smem;                                                                              \
         }                                                                                                       \
-        qb_launch(attn_part_kernel<Q>, dim3(n_kv, max_chunks), dim3(256), smem, st, q, ldq, k_cache, v_cache,  \
-                  n_head, n_kv, pos, B, part_o, part_ml, max_chunks);                                           \
+        qb_launch(attn_part_kernel<Q>, dim3(n_kv, max_chunks, sqv.S), dim3(256), smem, st, q, ldq, k_cache,     \
+                  v_cache, n_head, n_kv, pos, B, part_o, part_ml, max_chunks, sqv);                             \
         break;                                                                                                  \
     }
     switch (qpt) {
@@ -911,9 +962,8 @@ cudaError_t qb_attn_decode(const float* q, long long ldq, const float* k_cache, 
     default: return cudaErrorInvalidValue;
     }
 #undef QB_ATTN_CASE
-    qb_launch(attn_combine_kernel, dim3((n_head + 3) / 4, B), dim3(128), 0, st, q, ldq, pos, (const float*)part_o,
-              (const float2*)part_ml, max_chunks, n_head, B, out, ldo, xb, what);
-    return cudaGetLastError();
+    return qb_launch(attn_combine_kernel, dim3((n_head + 3) / 4, N), dim3(128), 0, st, q, ldq, pos,
+                     (const float*)part_o, (const float2*)part_ml, max_chunks, n_head, N, out, ldo, xb, what, sqv);
 }
 
 cudaError_t qb_silu_mul(const float* gate, const float* up, long long ld, int n, int B, float* out,
@@ -924,14 +974,14 @@ cudaError_t qb_silu_mul(const float* gate, const float* up, long long ld, int n,
 
 cudaError_t qb_silu_mul_xprep(const float* gate, const float* up, long long ld, int n, int B, float* out,
                               const QbXBuf& xb, int what, cudaStream_t st) {
-    if (n % 256 || B < 1 || B > QB_MAX_TOK) return cudaErrorInvalidValue;
+    if (n % 256 || B < 1 || B > QB_WIDE) return cudaErrorInvalidValue;
     qb_launch(silu_mul_xprep_kernel, dim3((n / 256 + 3) / 4, B), dim3(128), 0, st, gate, up, ld, n, B, out, xb, what);
     return cudaGetLastError();
 }
 
 cudaError_t qb_gdn_out_xprep(const float* o, const float* z, long long ld, const float* norm_w, int n_v, int dv,
                              int B, float eps, float* y, const QbXBuf& xb, int what, cudaStream_t st) {
-    if (dv != 128 || n_v % 2 || B < 1 || B > QB_MAX_TOK) return cudaErrorInvalidValue;
+    if (dv != 128 || n_v % 2 || B < 1 || B > QB_WIDE) return cudaErrorInvalidValue;
     qb_launch(gdn_out_xprep_kernel, dim3((n_v / 2 + 3) / 4, B), dim3(128), 0, st, o, z, ld, norm_w, n_v, eps, y, B, xb,
               what);
     return cudaGetLastError();

@@ -1338,8 +1338,13 @@ int qb_xprep_needs(int type, int N, int tc) {
 cudaError_t qb_xprep(const QbXIn* in, int nseg, int N, float eps, const QbXBuf& xb, int what, cudaStream_t st) {
     XSeg s[2] = {};
     int K = 0;
-    // up to QB_MAX_TOK tokens, or QB_TC16_TOK for the 16-token tcgen05 tiles alone
-    if (nseg < 1 || nseg > 2 || N < 1 || N > ((what == QB_XP_TC16) ? QB_TC16_TOK : QB_MAX_TOK))
+    // up to QB_MAX_TOK tokens, QB_TC16_TOK for the 16-token tcgen05 tiles alone, or
+    // QB_WIDE in chunks of QB_MAX_TOK (QbXBuf chunk strides set for every output asked for)
+    const bool wide = N > QB_MAX_TOK && what != QB_XP_TC16;
+    if (nseg < 1 || nseg > 2 || N < 1 || N > (what == QB_XP_TC16 ? QB_TC16_TOK : QB_WIDE))
+        return cudaErrorInvalidValue;
+    if (wide && ((what & (QB_XP_TC | QB_XP_TC16)) || ((what & QB_XP_F16) && (!xb.cs_frag || !xb.cs_scale)) ||
+                 ((what & QB_XP_SUM) && !xb.cs_sum) || ((what & QB_XP_I8) && (!xb.cs_q || !xb.cs_qscale))))
         return cudaErrorInvalidValue;
     for (int i = 0; i < nseg; ++i) {
         s[i].x = in[i].x;

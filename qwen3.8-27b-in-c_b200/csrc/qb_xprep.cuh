@@ -168,7 +168,15 @@ __device__ __forceinline__ void xprep_emit_g(const float (&v)[G][8], int t0, int
 }
 
 // one token: v[0..3] = elements 4*lane .. 4*lane+3 of block b of token t, v[4..7] = 128 + 4*lane ..
+// A wide input (N > QB_MAX_TOK, no 16-token tcgen05 tiles) goes to the chunk of 8 rows
+// that holds t.
 __device__ __forceinline__ void xprep_emit(const float (&v)[8], int t, int b, int N, int nb, int K,
                                            const QbXBuf& xb, int what, int lane) {
+    if (N > QB_MAX_TOK && !(what & QB_XP_TC16)) {
+        const int c = t >> 3;
+        xprep_emit_g<1>(reinterpret_cast<const float (&)[1][8]>(v), t & 7, b, min(QB_MAX_TOK, N - 8 * c), nb, K,
+                        qb_xb_chunk(xb, c), what & ~(QB_XP_TC | QB_XP_TC16), lane);
+        return;
+    }
     xprep_emit_g<1>(reinterpret_cast<const float (&)[1][8]>(v), t, b, N, nb, K, xb, what, lane);
 }

@@ -32,6 +32,7 @@ EXPORTED = [
     "qb_greedy_generate", "qb_last_argmax", "qb_last_loop_ms", "qb_read_state", "qb_read_buffer",
     "qb_reset", "qb_bench", "qb_model_init_tp", "qb_tp_handle", "qb_tp_connect", "qb_tp_rows",
     "qb_argmax_rows_noalloc", "sampler_init", "sampler_free", "sampler_sample", "qb_sample_generate",
+    "qb_seq_init", "qb_seq_prefill", "qb_seq_generate",
 ]
 
 
@@ -138,6 +139,12 @@ def lib():
         L.qb_read_buffer.restype = C.c_int64
         L.qb_reset.argtypes = [P(QwenModel)]
         L.qb_reset.restype = i32
+        L.qb_seq_init.argtypes = [P(QwenModel), u32]
+        L.qb_seq_init.restype = i32
+        L.qb_seq_prefill.argtypes = [P(QwenModel), u32, P(u32), u32]
+        L.qb_seq_prefill.restype = i32
+        L.qb_seq_generate.argtypes = [P(QwenModel), u32, u32, P(u32), u32, P(u32), u32, P(u32), P(u32)]
+        L.qb_seq_generate.restype = i32
         L.qb_bench.argtypes = [P(QwenModel), i32, u32, u32, P(C.c_double)]
         L.qb_bench.restype = f32
         L.qb_model_init_tp.argtypes = [P(QwenModel), C.c_char_p, u32, i32, i32]
@@ -448,6 +455,35 @@ class Model:
             check()
             raise RuntimeError("qb_sample_generate failed")
         return out[:n].copy()
+
+    # ---- multi-sequence decode (qb_seq_*) ----
+    def seq_init(self, n_seq):
+        if lib().qb_seq_init(C.byref(self.m), n_seq) != 0:
+            check()
+            raise RuntimeError("qb_seq_init failed")
+        self.n_seq = n_seq
+
+    def seq_prefill(self, seq, toks):
+        t = np.ascontiguousarray(toks, np.uint32)
+        if lib().qb_seq_prefill(C.byref(self.m), seq, _up(t), t.size) != 0:
+            check()
+            raise RuntimeError("qb_seq_prefill failed")
+
+    def seq_generate(self, n_cycles, n_spec=3, forced=None, cap=None):
+        """n_cycles speculative cycles of every sequence: ([tokens of sequence s],
+        [accept lengths of sequence s])."""
+        S = self.n_seq
+        cap = cap or n_cycles * (n_spec + 1) + 8
+        out = np.zeros((S, cap), np.uint32)
+        cnt = np.zeros(S, np.uint32)
+        js = np.zeros((S, n_cycles), np.uint32)
+        f = np.ascontiguousarray(forced if forced is not None else [], np.uint32)
+        n = lib().qb_seq_generate(C.byref(self.m), n_cycles, n_spec, _up(f) if f.size else None, f.size,
+                                  _up(out), cap, _up(cnt), _up(js))
+        if n < 0:
+            check()
+            raise RuntimeError("qb_seq_generate failed")
+        return [out[s, :cnt[s]].copy() for s in range(S)], [js[s, :n].copy() for s in range(S)]
 
     def reset(self):
         if lib().qb_reset(C.byref(self.m)) != 0:
