@@ -293,6 +293,44 @@ def run_c4(args, model, open_model, close_model, seq_rank, ms_ver_short):
     return c4
 
 
+C5_SEQ, C5_CTX = 8, (256, 4096)
+
+
+def run_c5(args, model, open_model, close_model):
+    """C5: 8 sequences at seeded contexts U{256..4096} (each prefilled alone),
+    then MTP speculation (k = 3, forced schedule) of all of them at once: the
+    verify runs 8 x 4 = 32 rows per weight sweep (8-row GEMV chunks), the drafts
+    8 rows.  Device-timed over the timed cycles; sequence 0 is then re-run alone
+    from the same prompt and must emit the same tokens.  Returns (dict, model)."""
+    close_model(model)
+    model = open_model(C5_CTX[1] + 4 * (args.warmup + args.c5_steps) + 64)
+    rng = np.random.default_rng(5000)
+    lens = rng.integers(C5_CTX[0], C5_CTX[1] + 1, C5_SEQ)
+    prompts = [rng.integers(0, qb.FULL["vocab"], int(n)).astype(np.uint32) for n in lens]
+    forced = forced_schedule()
+    model.seq_init(C5_SEQ)
+    t0 = time.time()
+    for s, p in enumerate(prompts):
+        model.seq_prefill(s, p)
+    log(f"C5 prefill of {int(lens.sum())} tokens {time.time() - t0:.1f}s")
+    w_t, w_j = model.seq_generate(args.warmup, 3, forced=forced)
+    toks, js = model.seq_generate(args.c5_steps, 3, forced=np.roll(forced, -args.warmup))
+    ms = model.last_loop_ms()
+    n_tok = int(sum(len(t) for t in toks))
+    log(f"C5 {args.c5_steps} cycles, {n_tok} tokens, {ms:.1f} ms")
+    seq0 = np.concatenate([w_t[0], toks[0]])
+    model.seq_init(1)   # sequence 0 alone, same prompt and schedule
+    model.prefill(prompts[0], 1)
+    alone, _ = model.spec_generate(10 ** 6, 3, forced=forced, max_cycles=args.warmup + args.c5_steps)
+    c5 = {"tok/s": n_tok / (ms / 1e3), "ms_per_cycle": ms / args.c5_steps, "sequences": C5_SEQ,
+          "contexts": [int(n) for n in lens], "cycles_timed": args.c5_steps, "tokens_timed": n_tok,
+          "verify_rows": C5_SEQ * 4, "draft_rows": C5_SEQ,
+          "gemv_path": "IQ4_XS: all 32 rows in one sweep on tcgen05 (qb_qmv_tcw); Q6_K head / Q8_0 in 8-row "
+                       "mma.sync chunks",
+          "seq0_tokens_equal_single": bool(np.array_equal(seq0, alone))}
+    return c5, model
+
+
 def shards_of(world, tp):
     """GPUs the weights are split over (each streams 1/shards of them)."""
     return world if tp else 1
@@ -444,11 +482,12 @@ def run_ours(args, rank, world, local_rank):
         gbs = b_c1 / shards_of(world, tp) / (ms_c1 / 1e3) / 1e9
         c1[f"n{n}"] = {"us": ms_c1 * 1e3, "GB/s": gbs, "frac": gbs / peaks()[0]}
     if not tp:   # the prefill / multi-stream width: 16 vectors per sweep on tcgen05, beside 2 x 8 on mma.sync
-        ms_w, b_w = model.bench(9, 16, 5)
         ms_8, _ = model.bench(8, 8, 5)
-        c1["n16_tcgen05"] = {"us": ms_w * 1e3, "GB/s": b_w / (ms_w / 1e3) / 1e9,
-                             "frac": b_w / (ms_w / 1e3) / 1e9 / peaks()[0],
-                             "us_as_2x8_mma_sync": 2 * ms_8 * 1e3}
+        for nw in (16, 32):   # one sweep on the scale-folded tcgen05 GEMM
+            ms_w, b_w = model.bench(10, nw, 5)
+            c1[f"n{nw}_tcgen05"] = {"us": ms_w * 1e3, "GB/s": b_w / (ms_w / 1e3) / 1e9,
+                                   "frac": b_w / (ms_w / 1e3) / 1e9 / peaks()[0],
+                                   f"us_as_{nw // 8}x8_mma_sync": nw // 8 * ms_8 * 1e3}
     # C2: 128-token prompt (plain prefill), then 256 greedy tokens on the device
     gold = golden_full()
     model.reset()
@@ -464,6 +503,9 @@ def run_ours(args, rank, world, local_rank):
     c4 = run_c4(args, model, open_model, close_model, seq_rank, ms_ver) if not args.no_c4 else None
     if c4 is not None:
         model = c4.pop("_model")
+    c5 = None
+    if not tp and not args.no_c5:   # multi-sequence decode runs on one GPU (replicas: one set per GPU)
+        c5, model = run_c5(args, model, open_model, close_model)
     log(f"components gemv {ms_gemv:.4f} head {ms_head:.4f} draft {ms_draft:.3f} verify {ms_ver:.3f} ms")
     shards = world if tp else 1   # each GPU streams 1/shards of the weights
     gemv_gbs = b_gemv / shards / (ms_gemv / 1e3) / 1e9
@@ -509,7 +551,8 @@ def run_ours(args, rank, world, local_rank):
                             "frac": ver_gbs / hbm},
             "configs": {"C1 IQ4_XS 17408x5120 GEMV (64 rotated copies)": c1,
                         "C2 greedy decode, prompt 128 + 256 tokens": c2,
-                        "C4 long context, prompt 2048 + 1024 speculative tokens": c4},
+                        "C4 long context, prompt 2048 + 1024 speculative tokens": c4,
+                        "C5 multi-sequence, 8 sequences x (k=3 -> 4) = 32 verify rows": c5},
             "draft_ms": ms_draft, "head_ms": ms_head,
             "head_GB/s": b_head / shards / (ms_head / 1e3) / 1e9,
             "clocks": clk.summary(),
@@ -559,6 +602,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-c4", action="store_true", help="skip the long-context configuration C4")
+    ap.add_argument("--no-c5", action="store_true", help="skip the multi-sequence configuration C5")
+    ap.add_argument("--c5-steps", type=int, default=40, help="timed multi-sequence cycles (C5)")
     ap.add_argument("--mode", default="bench", choices=["bench", "components"])
     ap.add_argument("--shape", default="wide4", choices=["wide4", "full"])
     ap.add_argument("--iters", type=int, default=3)

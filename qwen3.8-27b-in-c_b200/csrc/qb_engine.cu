@@ -367,7 +367,8 @@ struct DevMat {
     int row0 = 0, rows_all = 0;   // tensor parallelism: output rows land at row0 + i; rows_all = the tensor's rows
     size_t bytes_all = 0;         // GGUF bytes of the whole tensor (algorithmic traffic of the job)
     void* w = nullptr;      // repacked into 16-row mma.sync tiles (quant) or plain row-major (F32)
-    void* w_tc = nullptr;   // IQ4_XS also in 128-row tcgen05 tiles (qb_qmv_tc, N <= 4)
+    void* w_tc = nullptr;   // IQ4_XS also in 128-row tcgen05 tiles (qb_qmv_tc, N <= 4; qb_qmv_tcw, N > 8)
+    const GTensor* src = nullptr;   // the GGUF tensor it came from (whole matrix on one GPU)
     uint64_t fingerprint = 0;   // host-API weight cache only
 };
 
@@ -494,6 +495,7 @@ struct Engine {
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     float last_ms = 0.f;
     bool any_q45 = false;
+    bool tcw = false;                     // IQ4_XS above QB_MAX_TOK rows on qb_qmv_tcw (w_tc of every IQ4_XS matrix)
 
     ~Engine();
     void* dalloc(size_t bytes) {
@@ -588,6 +590,7 @@ int upload_mat(Engine& e, const GTensor* t, DevMat& m, void* tmp, size_t tmp_byt
                int row0 = 0) {
     if (!t) { set_err(-1, "missing tensor"); return -1; }
     m.type = t->type;
+    m.src = t;
     m.rows_all = (int)t->ne[1];
     m.row0 = row0;
     m.bytes_all = gguf_row_bytes(t->type, t->ne[0]) * t->ne[1];
@@ -935,16 +938,16 @@ int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
     // the GEMV input: QB_WIDE / QB_MAX_TOK chunks of QB_MAX_TOK rows (QbXBuf chunk strides)
     const int NC = TW / T8;
     e.xb.cs_frag = (long long)(qb_xfrag_bytes(Kmax) / sizeof(uint2));
-    e.xb.cs_scale = (long long)T8 * (Kmax / 256);
-    e.xb.cs_sum = (long long)T8 * (Kmax / 32);
     e.xb.cs_q = (long long)(qb_xq_bytes(Kmax) / sizeof(uint2));
-    e.xb.cs_qscale = (long long)T8 * (Kmax / 256);
     e.xb.xfrag = (uint2*)e.dalloc(NC * qb_xfrag_bytes(Kmax));
     e.xb.xscale = A((size_t)NC * T8 * (Kmax / 256));
     e.xb.xsum = A((size_t)NC * T8 * (Kmax / 32));
     e.xb.xq = (uint2*)e.dalloc(NC * qb_xq_bytes(Kmax));
     e.xb.xqscale = A((size_t)NC * T8 * (Kmax / 256));
     e.xb.xtc = (uint8_t*)e.dalloc(qb_xtc_bytes(Kmax));
+    e.xb.xtc16 = (uint8_t*)e.dalloc(qb_xtc16_bytes(Kmax));   // wide inputs on qb_qmv_tcw
+    e.xb.xtc32 = (uint8_t*)e.dalloc(qb_xtc32_bytes(Kmax));
+    if (!e.xb.xtc16 || !e.xb.xtc32) { set_err(-2, "activation alloc"); return -1; }
     if (!e.xb.xtc) { set_err(-2, "activation alloc"); return -1; }
     if (e.fuse) {
         e.xb_alt.xfrag = (uint2*)e.dalloc(qb_xfrag_bytes(Kmax));
@@ -961,6 +964,8 @@ int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
         CK(cudaMemset(e.xb_alt.xsum, 0, (size_t)T8 * (Kmax / 32) * 4));
     }
     CK(cudaMemset(e.xb.xtc, 0, qb_xtc_bytes(Kmax)));
+    CK(cudaMemset(e.xb.xtc16, 0, qb_xtc16_bytes(Kmax)));
+    CK(cudaMemset(e.xb.xtc32, 0, qb_xtc32_bytes(Kmax)));
     {
         const size_t q_rows = (size_t)d.n_head * T8 * qb_attn_max_chunks((int)e.n_ctx);
         e.attn_po = A(q_rows * d.head_dim);
@@ -1021,11 +1026,47 @@ int gemv_group(Engine& e, const DevMat* const* mats, float* const* outs, const l
             set_err(-1, "wide GEMV: at most %d rows, no fused epilogue, one GPU", QB_WIDE);
             return -1;
         }
+        // IQ4_XS with tcgen05 tiles: all rows in one sweep on the tensor cores; the
+        // other matrices in 8-row chunks (xp_needs prepared both input formats)
+        const DevMat* rest[QB_MAX_SEG * 4];
+        float* rest_out[QB_MAX_SEG * 4];
+        long long rest_ld[QB_MAX_SEG * 4];
+        int nr = 0;
+        QbQSeg segs[QB_MAX_SEG];
+        int ns = 0;
+        auto flush = [&]() -> int {
+            if (ns) CK(qb_qmv_tcw(segs, ns, K, N, e.xb, accumulate, 0, 1 << 30, e.work, e.st));
+            ns = 0;
+            return 0;
+        };
+        for (int i = 0; i < nm; ++i) {
+            if (e.tcw && mats[i]->type == QB_IQ4_XS && mats[i]->w_tc) {
+                if (mats[i]->rows == 0) continue;
+                if (ns == QB_MAX_SEG && flush()) return -1;
+                segs[ns].w = mats[i]->w_tc;
+                segs[ns].out = outs[i] + mats[i]->row0;
+                segs[ns].ldo = ldos[i];
+                segs[ns].rows = mats[i]->rows;
+                ++ns;
+            } else {
+                rest[nr] = mats[i];
+                rest_out[nr] = outs[i];
+                rest_ld[nr] = ldos[i];
+                ++nr;
+            }
+        }
+        if (flush()) return -1;
+        e.xready = false;
+        if (nr == 0) return 0;
+        mats = rest;
+        outs = rest_out;
+        ldos = rest_ld;
+        nm = nr;
         const QbXBuf xb0 = e.xb;
         for (int c = 0; c * QB_MAX_TOK < N; ++c) {
             float* oc[QB_MAX_SEG * 4];
             for (int i = 0; i < nm; ++i) oc[i] = outs[i] + (size_t)c * QB_MAX_TOK * ldos[i];
-            e.xb = qb_xb_chunk(xb0, c);
+            e.xb = qb_xb_chunk(xb0, c, K / 256);
             const int r = gemv_group(e, mats, oc, ldos, nm, K, std::min(QB_MAX_TOK, N - c * QB_MAX_TOK), accumulate,
                                      nullptr, tp_mode);
             e.xb = xb0;
@@ -1110,7 +1151,12 @@ int residual_gemv(Engine& e, const DevMat* m, float* x, int K, int N, const QbEp
 // the qb_xprep outputs that the matrices consuming an input of N tokens read
 int xp_needs(const Engine& e, std::initializer_list<const DevMat*> ms, int N) {
     int w = 0;
-    for (const DevMat* m : ms) w |= qb_xprep_needs(m->type, N, e.use_tc ? 1 : 0);
+    for (const DevMat* m : ms) {
+        if (e.tcw && N > QB_MAX_TOK && m->type == QB_IQ4_XS && m->w_tc)
+            w |= N <= QB_TC16_TOK ? QB_XP_TC16 : QB_XP_TC32;   // qb_qmv_tcw, one sweep for all rows
+        else
+            w |= qb_xprep_needs(m->type, N, e.use_tc ? 1 : 0);
+    }
     return w;
 }
 
@@ -1545,6 +1591,25 @@ int tp_fill_logits_row(Engine& e, int row) {
     }
     CK(qb_tp_pull_rows(dst, src, r0, r1, e.tp_world, e.tp_rank, e.st));
     CK(qb_qmv_ex(e.output.type, nullptr, 0, e.E, 1, e.xb, 0, nullptr, nullptr, &bar, e.work, e.st));
+    return 0;
+}
+
+// The tcgen05 tile copy of an IQ4_XS matrix (qb_repack_tc of its GGUF rows), made on first use.
+int ensure_w_tc(Engine& e, DevMat& m) {
+    if (m.w_tc || m.type != QB_IQ4_XS || m.rows == 0) return 0;
+    if (!m.src || m.rows != m.rows_all) { set_err(-1, "tcgen05 tiles need the whole matrix"); return -1; }
+    const size_t src = gguf_row_bytes(m.src->type, m.src->ne[0]) * m.src->ne[1];
+    void* tmp = nullptr;
+    CK(cudaMalloc(&tmp, src));
+    m.w_tc = e.dalloc(qb_repacked_bytes_tc(m.rows, m.K));
+    // stream-ordered copy: a pageable cudaMemcpy may return before its DMA lands, and the
+    // model's stream does not wait for the legacy stream
+    cudaError_t ce = m.w_tc ? cudaMemcpyAsync(tmp, m.src->data, src, cudaMemcpyHostToDevice, e.st)
+                            : cudaErrorMemoryAllocation;
+    if (ce == cudaSuccess) ce = qb_repack_tc(tmp, m.rows, m.K, m.w_tc, e.st);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(e.st);
+    cudaFree(tmp);
+    CK(ce);
     return 0;
 }
 
@@ -2104,6 +2169,21 @@ extern "C" int qb_seq_init(qwen_model_t* m, uint32_t n_seq) {
     CK(cudaMemsetAsync(e->ssm_base, 0, S * ssm1 * 4, e->st));
     CK(cudaMemsetAsync(e->mtp_h_base, 0, S * h1 * 4, e->st));
     CK(cudaMemsetAsync(e->ctrl_base, 0, S * sizeof(QbCtrl), e->st));
+    const char* tcw_env = getenv("QB_TCW");   // QB_TCW=0: wide verifies in 8-row mma.sync chunks only
+    if (n_seq * SPEC_MAX_B > QB_MAX_TOK && !e->tcw && !(tcw_env && tcw_env[0] == '0')) {
+        // verify widths above 8 rows: every IQ4_XS matrix also in tcgen05 tiles (qb_qmv_tcw)
+        auto each = [&](LayerW& l) {
+            DevMat* ms[] = {&l.ffn_gate, &l.ffn_up, &l.ffn_down, &l.wqkv, &l.wgate, &l.wbeta, &l.walpha, &l.ssm_out,
+                            &l.q, &l.k, &l.v, &l.o};
+            for (DevMat* d : ms)
+                if (d->w && ensure_w_tc(*e, *d)) return -1;
+            return 0;
+        };
+        for (LayerW& l : e->L)
+            if (each(l)) return -1;
+        if (each(e->mtp)) return -1;
+        e->tcw = true;
+    }
     e->seq_conv = (long long)conv1;
     e->seq_ssm = (long long)ssm1;
     e->seq_kv = (long long)kv1;
@@ -2342,52 +2422,40 @@ extern "C" float qb_bench(qwen_model_t* m, int what, uint32_t arg, uint32_t iter
             }
             b /= (double)nl;
         }
-    } else if (what == 9) {
-        // one FFN up matrix at N = arg (9..16) on the 16-vector tcgen05 kernel, rotated over
-        // all layers; the tcgen05 tile copies of those matrices are made on first use
-        if (arg < 1 || arg > QB_TC16_TOK || e->tp_world > 1) return -1.f;
+    } else if (what == 9 || what == 10) {
+        // one FFN up matrix at N = arg, rotated over all layers: what 9 on the 16-vector
+        // tcgen05 kernel (9..16), what 10 on the scale-folded one (9..32); the tcgen05
+        // tile copies of those matrices are made on first use
+        if (arg < 1 || arg > (what == 9 ? QB_TC16_TOK : QB_TCW_TOK) || e->tp_world > 1) return -1.f;
         const int nl = (int)e->L.size();
-        for (int li = 0; li < nl; ++li) {
-            DevMat& up = e->L[li].ffn_up;
-            if (up.w_tc || up.type != QB_IQ4_XS) continue;
-            char nm[64];
-            snprintf(nm, sizeof nm, "blk.%d.ffn_up.weight", li);
-            const GTensor* t = e->g.find(nm);
-            if (!t) return -1.f;
-            const size_t src = gguf_row_bytes(t->type, t->ne[0]) * t->ne[1];
-            void* tmp = nullptr;
-            if (cudaMalloc(&tmp, src) != cudaSuccess) return -1.f;
-            up.w_tc = e->dalloc(qb_repacked_bytes_tc(up.rows, up.K));
-            if (!up.w_tc || cudaMemcpy(tmp, t->data, src, cudaMemcpyHostToDevice) != cudaSuccess ||
-                qb_repack_tc(tmp, up.rows, up.K, up.w_tc, e->st) != cudaSuccess ||
-                cudaStreamSynchronize(e->st) != cudaSuccess) {
-                cudaFree(tmp);
-                return -1.f;
-            }
-            cudaFree(tmp);
-        }
+        for (int li = 0; li < nl; ++li)
+            if (ensure_w_tc(*e, e->L[li].ffn_up)) return -1.f;
         if (!e->xb16.xtc16) {
             e->xb16.xtc16 = (uint8_t*)e->dalloc(qb_xtc16_bytes(e->E));
-            e->xb16.xqscale = (float*)e->dalloc((size_t)QB_TC16_TOK * (e->E / 256) * 4);
-            if (!e->xb16.xtc16 || !e->xb16.xqscale) return -1.f;
+            e->xb16.xtc32 = (uint8_t*)e->dalloc(qb_xtc32_bytes(e->E));
+            e->xb16.xqscale = (float*)e->dalloc((size_t)QB_TCW_TOK * (e->E / 256) * 4);
+            if (!e->xb16.xtc16 || !e->xb16.xtc32 || !e->xb16.xqscale) return -1.f;
         }
         // input: arg rows of the FFN activation buffer (any finite values), prepared once
         const QbXIn in{e->act, e->E, nullptr, e->E};
-        if (qb_xprep(&in, 1, (int)arg, e->eps, e->xb16, QB_XP_TC16, e->st) != cudaSuccess) return -1.f;
+        const int xw = (what == 9 || arg <= QB_TC16_TOK) ? QB_XP_TC16 : QB_XP_TC32;
+        if (qb_xprep(&in, 1, (int)arg, e->eps, e->xb16, xw, e->st) != cudaSuccess) return -1.f;
         struct Rec9 {
-            static int go(Engine& en, int a) {
+            static int go(Engine& en, int packed) {
+                const int a = packed & 0xFF, wh = packed >> 8;
                 for (const LayerW& ly : en.L) {
                     QbQSeg seg;
                     seg.w = ly.ffn_up.w_tc;
                     seg.out = en.logits;   // [a][F] rows of the logits buffer
                     seg.ldo = en.F;
                     seg.rows = ly.ffn_up.rows;
-                    CK(qb_qmv_tc16(&seg, 1, en.E, a, en.xb16, 0, 0, 1 << 30, en.work, en.st));
+                    if (wh == 9) CK(qb_qmv_tc16(&seg, 1, en.E, a, en.xb16, 0, 0, 1 << 30, en.work, en.st));
+                    else CK(qb_qmv_tcw(&seg, 1, en.E, a, en.xb16, 0, 0, 1 << 30, en.work, en.st));
                 }
                 return 0;
             }
         };
-        if (capture(*e, &ge, Rec9::go, (int)arg)) return -1.f;
+        if (capture(*e, &ge, Rec9::go, (int)arg | (what << 8))) return -1.f;
         cudaGraphLaunch(ge, e->st);
         cudaEventRecord(e->ev0, e->st);
         for (uint32_t i = 0; i < iters; ++i) cudaGraphLaunch(ge, e->st);
@@ -2509,6 +2577,7 @@ int scratch_get(Scratch*& s, size_t x_floats, size_t out_floats, int K) {
         if (s->xb.xqscale) cudaFree(s->xb.xqscale);
         if (s->xb.xtc) cudaFree(s->xb.xtc);
         if (s->xb.xtc16) cudaFree(s->xb.xtc16);
+        if (s->xb.xtc32) cudaFree(s->xb.xtc32);
         s->k_cap = std::max<size_t>((size_t)K, 4096);
         const int kc = (int)((s->k_cap + 255) / 256 * 256);
         CK(cudaMalloc(&s->xb.xfrag, qb_xfrag_bytes(kc)));
@@ -2516,9 +2585,11 @@ int scratch_get(Scratch*& s, size_t x_floats, size_t out_floats, int K) {
         CK(cudaMalloc(&s->xb.xq, qb_xq_bytes(kc)));
         CK(cudaMemset(s->xb.xq, 0, qb_xq_bytes(kc)));
         CK(cudaMalloc(&s->xb.xscale, QB_MAX_TOK * (kc / 256) * 4));
-        CK(cudaMalloc(&s->xb.xqscale, QB_TC16_TOK * (kc / 256) * 4));   // the 16-token path's rows too
+        CK(cudaMalloc(&s->xb.xqscale, QB_TCW_TOK * (kc / 256) * 4));   // the 32-token path's rows too
         CK(cudaMalloc(&s->xb.xtc16, qb_xtc16_bytes(kc)));
         CK(cudaMemset(s->xb.xtc16, 0, qb_xtc16_bytes(kc)));
+        CK(cudaMalloc(&s->xb.xtc32, qb_xtc32_bytes(kc)));
+        CK(cudaMemset(s->xb.xtc32, 0, qb_xtc32_bytes(kc)));
         CK(cudaMalloc(&s->xb.xtc, qb_xtc_bytes(kc)));
         CK(cudaMemset(s->xb.xtc, 0, qb_xtc_bytes(kc)));
         CK(cudaMalloc(&s->xb.xsum, QB_MAX_TOK * (kc / 32) * 4));
@@ -2595,7 +2666,7 @@ int wcache_get(const gguf_tensor_info_t* W, const DevMat*& out) {
 }
 
 // the tcgen05 tile layout of an IQ4_XS matrix of the host API, repacked from
-// the caller's blocks on first use (the 16-token path reads it)
+// the caller's blocks on first use (the wide tcgen05 path reads it)
 int wcache_tc(const gguf_tensor_info_t* W, const DevMat* M) {
     if (M->w_tc) return 0;
     const size_t src_bytes = gguf_row_bytes((int)W->type, W->ne[0]) * W->ne[1];
@@ -2613,7 +2684,7 @@ int wcache_tc(const gguf_tensor_info_t* W, const DevMat* M) {
 
 // out_i[t][r] = W_i x[t] for the n_mat matrices (all reading the same x), rows
 // [r0, r1) of each (r1 clamped to its rows), t < n, host x / outs.  One
-// dispatch: per chunk of vectors (QB_MAX_TOK, or QB_TC16_TOK for IQ4_XS above
+// dispatch: per chunk of vectors (QB_MAX_TOK, or QB_TCW_TOK for IQ4_XS above
 // QB_MAX_TOK vectors), one host-to-device copy of x, one activation prep
 // covering every format and width, one GEMV launch per matrix queued back to
 // back (each the launch a single-matrix call makes, so the results are
@@ -2638,26 +2709,27 @@ int gemv_multi_host(const gguf_tensor_info_t* const* Ws, int n_mat, const float*
         lo[i] = std::min(r0, hi[i]);
     }
     if (ldx < (uint64_t)Kmax) { set_err(-1, "gemv: ldx %llu < ne0 %d", (unsigned long long)ldx, Kmax); return -1; }
-    // more vectors than one mma.sync sweep takes: IQ4_XS matrices run 16 per sweep on
-    // tcgen05, the others 8 per sweep.  The path is a property of the matrix and n
-    // alone, so a matrix gives the same bits here as in its own gemv_batch call.
+    // more vectors than one mma.sync sweep takes: IQ4_XS matrices run 32 per sweep on
+    // tcgen05 (qb_qmv_tcw), the others 8 per sweep.  The path is a property of the
+    // matrix and n alone, so a matrix gives the same bits here as in its own
+    // gemv_batch call.
     bool wide_of[QB_GEMV_MULTI_MAX];
     for (int i = 0; i < n_mat; ++i) {
         wide_of[i] = n > QB_MAX_TOK && M[i]->type == QB_IQ4_XS;
         if (wide_of[i] && wcache_tc(Ws[i], M[i])) return -1;
     }
     Scratch* s = nullptr;
-    for (int pass = 0; pass < 2; ++pass) {   // pass 0: 8-vector chunks, pass 1: 16-vector chunks
+    for (int pass = 0; pass < 2; ++pass) {   // pass 0: 8-vector chunks, pass 1: 32-vector chunks
         const bool wide = pass == 1;
         bool any = false;
         size_t of = 0;
         for (int i = 0; i < n_mat; ++i)
             if (wide_of[i] == wide) {
                 any = true;
-                of += (size_t)std::min(n, wide ? QB_TC16_TOK : QB_MAX_TOK) * M[i]->rows;
+                of += (size_t)std::min(n, wide ? QB_TCW_TOK : QB_MAX_TOK) * M[i]->rows;
             }
         if (!any) continue;
-        const int chunk = wide ? QB_TC16_TOK : QB_MAX_TOK;
+        const int chunk = wide ? QB_TCW_TOK : QB_MAX_TOK;
         for (int t0 = 0; t0 < n; t0 += chunk) {
             const int nn = std::min(chunk, n - t0);
             if (scratch_get(s, (size_t)nn * Kmax, of, Kmax)) return -1;
@@ -2667,7 +2739,7 @@ int gemv_multi_host(const gguf_tensor_info_t* const* Ws, int n_mat, const float*
             for (int i = 0; i < n_mat; ++i) {
                 if (wide_of[i] != wide || M[i]->type == QB_F32) continue;
                 const bool tc = M[i]->w_tc && nn <= 4 && host_tc();
-                need |= wide ? QB_XP_TC16 : qb_xprep_needs(M[i]->type, nn, tc ? 1 : 0);
+                need |= wide ? (nn <= QB_TC16_TOK ? QB_XP_TC16 : QB_XP_TC32) : qb_xprep_needs(M[i]->type, nn, tc ? 1 : 0);
                 if (scratch_work(s, M[i]->rows)) return -1;
             }
             if (need) {
@@ -2693,8 +2765,8 @@ int gemv_multi_host(const gguf_tensor_info_t* const* Ws, int n_mat, const float*
                         seg.ldo = W->rows;
                         seg.rows = (int)(b - (uint64_t)T0 * 128);
                         if (wide)
-                            CK(qb_qmv_tc16(&seg, 1, K, nn, s->xb, 0, (int)(a - (uint64_t)T0 * 128),
-                                           (int)(b - (uint64_t)T0 * 128), s->work, s->st));
+                            CK(qb_qmv_tcw(&seg, 1, K, nn, s->xb, 0, (int)(a - (uint64_t)T0 * 128),
+                                          (int)(b - (uint64_t)T0 * 128), s->work, s->st));
                         else
                             CK(qb_qmv_tc(&seg, 1, K, nn, s->xb, 0, (int)(a - (uint64_t)T0 * 128),
                                          (int)(b - (uint64_t)T0 * 128), s->work, s->st));

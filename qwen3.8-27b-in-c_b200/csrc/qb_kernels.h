@@ -43,21 +43,24 @@ struct QbXBuf {
     uint2* xq;               // int8 digit mma B fragments (IQ4_XS), qb_xbuf_bytes
     float* xqscale;          // [QB_MAX_TOK][K/256] power-of-two scale of xq and xtc
     uint8_t* xtc;            // int8 digits as tcgen05 B tiles, 4 KB per 256 columns (N <= 4)
-    uint8_t* xtc16;          // the same for up to 16 tokens, 12 KB per 256 columns (qb_qmv_tc16)
-    // Wide inputs (N > QB_MAX_TOK, up to QB_WIDE rows): row r is row r % 8 of chunk
-    // r / 8, and chunk c is an input of its own (min(8, N - 8c) rows, the N <= 8
-    // layouts above) at these element offsets times c (qb_xb_chunk).  xtc / xtc16
-    // are not chunked.
-    long long cs_frag, cs_scale, cs_sum, cs_q, cs_qscale;
+    uint8_t* xtc16;          // the same for up to 16 tokens, 12 KB per 256 columns (qb_qmv_tcw, 16 tokens)
+    uint8_t* xtc32;          // the same for up to 32 tokens, 24 KB per 256 columns (qb_qmv_tcw, 32 tokens)
+    // Wide inputs (N > QB_MAX_TOK, up to QB_WIDE rows) for the 8-row formats (xfrag,
+    // xscale, xsum, xq): row r is row r % 8 of chunk r / 8, and chunk c is an input of
+    // its own (min(8, N - 8c) rows, the N <= 8 layouts above; qb_xb_chunk).  The
+    // fragment arrays of chunk c start c * cs_frag / cs_q elements in; the per-row
+    // arrays (xscale, xsum, xqscale) keep row r at row r, so the 16- and 32-token
+    // tiles share xqscale with the chunks.
+    long long cs_frag, cs_q;
 };
-// chunk c of a wide input (qb_kernels.h QbXBuf)
-__host__ __device__ inline QbXBuf qb_xb_chunk(const QbXBuf& xb, int c) {
+// chunk c (rows 8c..8c+7) of a wide input of nb = K / 256 blocks
+__host__ __device__ inline QbXBuf qb_xb_chunk(const QbXBuf& xb, int c, int nb) {
     QbXBuf r = xb;
     r.xfrag = xb.xfrag ? xb.xfrag + c * xb.cs_frag : nullptr;
-    r.xscale = xb.xscale ? xb.xscale + c * xb.cs_scale : nullptr;
-    r.xsum = xb.xsum ? xb.xsum + c * xb.cs_sum : nullptr;
+    r.xscale = xb.xscale ? xb.xscale + (long long)c * 8 * nb : nullptr;
+    r.xsum = xb.xsum ? xb.xsum + (long long)c * 64 * nb : nullptr;
     r.xq = xb.xq ? xb.xq + c * xb.cs_q : nullptr;
-    r.xqscale = xb.xqscale ? xb.xqscale + c * xb.cs_qscale : nullptr;
+    r.xqscale = xb.xqscale ? xb.xqscale + (long long)c * 8 * nb : nullptr;
     return r;
 }
 // Independent sequences in one launch of a stateful layer kernel (multi-sequence
@@ -68,8 +71,9 @@ struct QbSeqs {
     int S, T;
     long long ctrl, state;
 };
-enum { QB_XP_F16 = 1, QB_XP_SUM = 2, QB_XP_I8 = 4, QB_XP_TC = 8, QB_XP_TC16 = 16 };   // qb_xprep outputs
+enum { QB_XP_F16 = 1, QB_XP_SUM = 2, QB_XP_I8 = 4, QB_XP_TC = 8, QB_XP_TC16 = 16, QB_XP_TC32 = 32 };   // qb_xprep outputs
 #define QB_TC16_TOK 16       // input vectors of one qb_qmv_tc16 launch; xqscale rows it needs
+#define QB_TCW_TOK 32        // input vectors of one qb_qmv_tcw launch
 
 // ---- quantised GEMV (qb_quant.cu) ----
 size_t qb_repacked_bytes(int type, int rows, int K);
@@ -79,6 +83,7 @@ size_t qb_xfrag_bytes(int K);
 size_t qb_xq_bytes(int K);
 size_t qb_xtc_bytes(int K);
 size_t qb_xtc16_bytes(int K);
+size_t qb_xtc32_bytes(int K);
 // which qb_xprep outputs a matrix of this type reads at N input vectors
 // (IQ4_XS: the tcgen05 tiles when N <= 4 and tc != 0, else the mma.sync fragments)
 int qb_xprep_needs(int type, int N = QB_MAX_TOK, int tc = 0);
@@ -161,6 +166,12 @@ size_t qb_qmv_tc_partial_floats(int max_ctas);
 // [QB_TC16_TOK][K/256]; one CTA per SM
 cudaError_t qb_qmv_tc16(const QbQSeg* segs, int nseg, int K, int N, const QbXBuf& xb, int accumulate, int row_lo,
                         int row_hi, const QbQmvWork& work, cudaStream_t st);
+// 9..32 input vectors in one weight sweep, sub-block scales folded into the
+// weights (two int8 planes per code): activation tiles from xb.xtc16 (N <= 16)
+// or xb.xtc32, scales from xb.xqscale [N][K/256]; one CTA per SM; the same
+// value per (tile, block) as qb_qmv_tc16 and the mma.sync GEMV
+cudaError_t qb_qmv_tcw(const QbQSeg* segs, int nseg, int K, int N, const QbXBuf& xb, int accumulate, int row_lo,
+                       int row_hi, const QbQmvWork& work, cudaStream_t st);
 // segs[i].w are qb_repack_tc layouts
 cudaError_t qb_qmv_tc(const QbQSeg* segs, int nseg, int K, int N, const QbXBuf& xb, int accumulate, int row_lo,
                       int row_hi, const QbQmvWork& work, cudaStream_t st);

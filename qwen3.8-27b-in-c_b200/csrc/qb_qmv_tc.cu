@@ -542,6 +542,290 @@ __global__ void __launch_bounds__(kThreads16, 1) qmv_tc16_kernel(TcK p) {
     if (warp == 0) tmem_dealloc(tmem, kCols16);
 }
 
+// ------------------------ wide GEMM, scales folded ---------------------------
+// Up to NT = 16 or 32 input vectors per weight sweep.  The sub-block scale s
+// (ls - 32, 6 bits signed) is folded into the weights: each code c of a
+// sub-block becomes A = s * kvalues[c] (|A| <= 4064), written to tensor memory
+// as two int8 planes A = 64 H + L (L in [-32, 31], H in [-63, 64]) by a
+// byte-permute lookup in a shared table indexed by s.  Per (tile, block) stage
+// one thread issues 16 MMAs (M 128, N 3 NT, K 32): the 8 sub-blocks of each
+// plane accumulate into one D region, so the sums arrive already scaled, and
+// per (row, token, digit) the epilogue forms 64 SH + SL.  That integer is the
+// one the other paths build from per-sub-block sums (sum over k of s kv_k D_k),
+// and the digits and the fp16 block scale are combined in fp32 in the same
+// order (65536 d0 + (256 d1 + d2)), so a (tile, block) gives the same value
+// here, on qb_qmv_tc16 and on the mma.sync GEMV.
+//
+// Tensor memory: A = 2 buffers x (H, L) x 8 sub-blocks x 8 columns (256), then
+// D = (H, L) x 3 NT columns (192 for 32 tokens); one CTA per SM.  The decode
+// of stage r (8 warps, two per lane quarter, each half of the sub-blocks of
+// its 32 rows) overlaps the MMAs of stage r-1; the epilogue of stage r-1 (each
+// warp half of the tokens) runs before the MMAs of stage r are issued.
+template <int NT>
+struct Tcw {
+    static constexpr int kB = 8 * 3 * NT * 32;          // B tiles of one block
+    static constexpr int kStage = kUnit + kB;
+    static constexpr int kRing = 4;
+    static constexpr uint32_t kDCol = 256;
+    static constexpr uint32_t kIdesc = idesc_i8(128, 3 * NT);
+    static constexpr int kTok = NT / 2;                 // tokens of one epilogue warp
+};
+constexpr int kWarpsW = 8;
+constexpr int kThreadsW = kWarpsW * 32 + 32;            // + producer warp
+constexpr int kLutBytes = 64 * 2 * 16;                  // [s + 32][H, L][code]
+constexpr int kHdrW = 256 + kLutBytes;
+
+// 8 codes (the nibbles of w, element order of iq4_i8) -> bytes of the two planes
+__device__ __forceinline__ void lut16x2(uint32_t w, const uint4& TH, const uint4& TL, uint32_t& h0, uint32_t& h1,
+                                        uint32_t& l0, uint32_t& l1) {
+    const uint32_t idx = w & 0x77777777u;
+    const uint32_t sel = ((w >> 1) & 0x44444444u) | 0x32103210u;
+    const uint32_t idxh = idx >> 16, selh = sel >> 16;
+    h0 = prmt(prmt(TH.x, TH.y, idx), prmt(TH.z, TH.w, idx), sel);
+    h1 = prmt(prmt(TH.x, TH.y, idxh), prmt(TH.z, TH.w, idxh), selh);
+    l0 = prmt(prmt(TL.x, TL.y, idx), prmt(TL.z, TL.w, idx), sel);
+    l1 = prmt(prmt(TL.x, TL.y, idxh), prmt(TL.z, TL.w, idxh), selh);
+}
+
+template <int NT>
+__device__ void finish_row_w(const TcK& p, int T, int cta, int s0, int s1, int m, int h,
+                             const float (&tot)[Tcw<NT>::kTok]) {
+    constexpr int KT = Tcw<NT>::kTok;
+    const int sg = seg_of_tile(p, T);
+    const int row = (T - p.tile0[sg]) * kRows + m;
+    const int tb = KT * h;
+    auto store = [&](const float (&v)[KT]) {
+        if (row >= p.rows[sg] || row < p.row_lo || row >= p.row_hi) return;
+        float prev[KT];
+#pragma unroll
+        for (int t = 0; t < KT; ++t)
+            prev[t] = (tb + t < p.N && p.accumulate) ? p.out[sg][(size_t)(tb + t) * p.ldo[sg] + row] : 0.f;
+#pragma unroll
+        for (int t = 0; t < KT; ++t)
+            if (tb + t < p.N) p.out[sg][(size_t)(tb + t) * p.ldo[sg] + row] = p.accumulate ? prev[t] + v[t] : v[t];
+    };
+    const int P0 = T * p.nb, P1 = P0 + p.nb;
+    if (s0 <= P0 && s1 >= P1) {
+        store(tot);
+        return;
+    }
+    const int piece = s0 > P0 ? 0 : 1;
+    float4* dst = reinterpret_cast<float4*>(p.partial + (((size_t)cta * 2 + piece) * kRows + m) * NT + tb);
+#pragma unroll
+    for (int i = 0; i < KT / 4; ++i) dst[i] = make_float4(tot[4 * i], tot[4 * i + 1], tot[4 * i + 2], tot[4 * i + 3]);
+    const int c_first = stage_cta(p.S, p.G, P0), c_last = stage_cta(p.S, p.G, P1 - 1);
+    unsigned* ctr = p.counters + ((size_t)T * kRows + m) * 2 + h;
+    const unsigned old = atom_add_acq_rel_gpu(ctr, 1u);
+    if ((int)old != c_last - c_first) return;
+    float sum[KT];
+#pragma unroll
+    for (int t = 0; t < KT; ++t) sum[t] = 0.f;
+    for (int c = c_first; c <= c_last; ++c) {
+        const int pc = cta_s0(p.S, p.G, c) > P0 ? 0 : 1;
+        const volatile float* v = p.partial + (((size_t)c * 2 + pc) * kRows + m) * NT + tb;
+#pragma unroll
+        for (int t = 0; t < KT; ++t) sum[t] += v[t];
+    }
+    store(sum);
+    *ctr = 0u;
+}
+
+// KT consecutive accumulator columns of this thread's lane
+template <int KT>
+__device__ __forceinline__ void tmem_ldk(uint32_t taddr, uint32_t (&v)[KT]) {
+    if constexpr (KT == 16) {
+        tmem_ld16(taddr, v);
+    } else {
+        tmem_ld8(taddr, v);
+    }
+}
+
+template <int NT>
+__global__ void __launch_bounds__(kThreadsW, 1) qmv_tcw_kernel(TcK p) {
+    using C = Tcw<NT>;
+    constexpr int KT = C::kTok;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + C::kRing;
+    uint64_t* mma_done = empty + C::kRing;
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mma_done + 1);
+    volatile int* dec_abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
+    uint8_t* lut = smem + 256;
+    uint8_t* ring = smem + kHdrW;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int cta = blockIdx.x;
+    const int s0 = cta_s0(p.S, p.G, cta), s1 = cta_s0(p.S, p.G, cta + 1);
+    const int n = s1 - s0;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < C::kRing; ++i) {
+            mbar_init(full + i, 1);
+            mbar_init(empty + i, 1);
+        }
+        mbar_init(mma_done, 1);
+        *dec_abort = 0;
+        mbar_fence_init();
+    }
+    // planes of s * kvalues[c] for every s: L = ((A + 32) mod 64) - 32, H = (A - L) / 64
+    for (int i = threadIdx.x; i < 64 * 16; i += blockDim.x) {
+        const int sv = (i >> 4) - 32, c = i & 15;
+        const uint32_t kw = c < 4 ? kIq4I8T0 : c < 8 ? kIq4I8T1 : c < 12 ? kIq4I8T2 : kIq4I8T3;   // kvalues
+        const int a = sv * (int)(int8_t)(kw >> (8 * (c & 3)));
+        const int l = ((a + 32) & 63) - 32;
+        lut[(i >> 4) * 32 + c] = (uint8_t)(int8_t)((a - l) >> 6);
+        lut[(i >> 4) * 32 + 16 + c] = (uint8_t)(int8_t)l;
+    }
+    if (warp == 0) {
+        tmem_alloc(tmem_holder, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_holder;
+    pdl_trigger();
+
+    if (warp == kWarpsW) {
+        // ------------------------------ producer ------------------------------
+        if (lane == 0 && n > 0) {
+            auto weights_of = [&](int s) -> const uint8_t* {
+                const int T = s / p.nb, b = s - T * p.nb;
+                const int sg = seg_of_tile(p, T);
+                return p.w[sg] + ((size_t)(T - p.tile0[sg]) * p.nb + b) * kUnit;
+            };
+            const int pre = n < C::kRing ? n : C::kRing;
+            for (int r = 0; r < pre; ++r) {
+                mbar_expect_tx(full + r, C::kStage);
+                bulk_g2s(ring + r * C::kStage, weights_of(s0 + r), kUnit, full + r);
+            }
+            pdl_wait();   // the activation digits are written by the previous kernel
+            for (int r = 0; r < pre; ++r)
+                bulk_g2s(ring + r * C::kStage + kUnit, p.xb + (size_t)((s0 + r) % p.nb) * C::kB, C::kB, full + r);
+            int issued = pre;
+            for (int r = C::kRing; r < n; ++r) {
+                const int slot = r % C::kRing;
+                if (!mbar_wait_sleep(empty + slot, (uint32_t)((r / C::kRing) - 1) & 1u, kSleepNs)) {
+                    atomicExch(p.err, 3u);
+                    break;
+                }
+                const int s = s0 + r;
+                mbar_expect_tx(full + slot, C::kStage);
+                bulk_g2s(ring + slot * C::kStage, weights_of(s), kUnit, full + slot);
+                bulk_g2s(ring + slot * C::kStage + kUnit, p.xb + (size_t)(s % p.nb) * C::kB, C::kB, full + slot);
+                issued = r + 1;
+            }
+            for (int r = issued - C::kRing > 0 ? issued - C::kRing : 0; r < issued; ++r)
+                mbar_wait(full + r % C::kRing, (uint32_t)(r / C::kRing) & 1u, 1u << 20);
+        }
+    } else if (n > 0) {
+        // --------------------------- decode / epilogue ---------------------------
+        pdl_wait();
+        const int q = warp & 3, h = warp >> 2;         // lane quarter, half
+        const int m = q * 32 + lane;                   // weight row of this thread
+        const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+        float tot[KT];
+#pragma unroll
+        for (int t = 0; t < KT; ++t) tot[t] = 0.f;
+        float d_prev = 0.f;
+        int last_mma = -1;
+        for (int r = 0; r <= n; ++r) {
+            float d = 0.f;
+            if (r < n) {
+                const int slot = r % C::kRing;
+                if (!mbar_wait_sleep(full + slot, (uint32_t)(r / C::kRing) & 1u, kSleepNs)) {
+                    *dec_abort = 1;
+                } else {
+                    const uint8_t* u = ring + slot * C::kStage;
+                    uint32_t L0, L1;
+                    iq4_scale_bytes(lds64(u + kQsBytes + m * 8), L0, L1, d);
+                    const uint32_t abuf = tmem + lane_base + (uint32_t)((r & 1) * 128);
+                    const uint32_t Lh = h ? L1 : L0;           // ls of sub-blocks 4h..4h+3
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const int sb = 4 * h + k;
+                        const uint4 qq = lds128(u + sb * (kRows * 16) + m * 16);
+                        const uint8_t* tl = lut + ubyte(Lh, k) * 32;   // (ls - 32) + 32
+                        const uint4 TH = lds128(tl), TL = lds128(tl + 16);
+                        uint32_t aH[8], aL[8];
+                        lut16x2(qq.x, TH, TL, aH[0], aH[1], aL[0], aL[1]);
+                        lut16x2(qq.y, TH, TL, aH[2], aH[3], aL[2], aL[3]);
+                        lut16x2(qq.z, TH, TL, aH[4], aH[5], aL[4], aL[5]);
+                        lut16x2(qq.w, TH, TL, aH[6], aH[7], aL[6], aL[7]);
+                        tmem_st8(abuf + (uint32_t)(sb * 8), aH);
+                        tmem_st8(abuf + 64u + (uint32_t)(sb * 8), aL);
+                    }
+                    tmem_wait_st();
+                }
+            }
+            // epilogue of stage r-1, tokens KT h .. KT h + KT - 1: per digit 64 SH + SL
+            if (r >= 1 && !*dec_abort) {
+                const int rp = r - 1;
+                if (!mbar_wait_sleep(mma_done, (uint32_t)rp & 1u, kSleepNs)) {
+                    *dec_abort = 1;
+                } else {
+                    tc_fence_after();
+                    const uint32_t dbase = tmem + lane_base + C::kDCol + (uint32_t)(KT * h);
+                    const int b_prev = (s0 + rp) % p.nb;
+                    float f[KT];
+#pragma unroll
+                    for (int g = 2; g >= 0; --g) {
+                        uint32_t vh[KT], vl[KT];
+                        tmem_ldk<KT>(dbase + (uint32_t)(g * NT), vh);
+                        tmem_ldk<KT>(dbase + (uint32_t)(3 * NT + g * NT), vl);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int t = 0; t < KT; ++t) {
+                            const int c = 64 * (int)vh[t] + (int)vl[t];
+                            if (g == 2) f[t] = (float)c;
+                            else if (g == 1) f[t] = fmaf((float)c, 256.f, f[t]);
+                            else {
+                                const int tok = KT * h + t;
+                                const float v = fmaf((float)c, 65536.f, f[t]) * d_prev;
+                                const float xs = tok < p.N ? __ldg(p.xqscale + tok * p.nb + b_prev) : 0.f;
+                                tot[t] = fmaf(xs, v, tot[t]);
+                            }
+                        }
+                    }
+                    if (threadIdx.x == 0) mbar_arrive(empty + rp % C::kRing);
+                    const int s = s0 + rp;
+                    if ((s + 1) % p.nb == 0 || rp == n - 1) {
+                        finish_row_w<NT>(p, s / p.nb, cta, s0, s1, m, h, tot);
+#pragma unroll
+                        for (int t = 0; t < KT; ++t) tot[t] = 0.f;
+                    }
+                }
+            }
+            tc_fence_before();
+            named_bar_sync(1, kWarpsW * 32);
+            if (*dec_abort) break;
+            if (r < n && threadIdx.x == 0) {
+                tc_fence_after();
+                const uint32_t a0 = tmem + (uint32_t)((r & 1) * 128);
+                const uint32_t bsm = smem_u32(ring + (r % C::kRing) * C::kStage + kUnit);
+#pragma unroll
+                for (int sb = 0; sb < 8; ++sb) {
+                    const uint64_t bd = smem_desc_kmajor(bsm + (uint32_t)(sb * 3 * NT * 32), 128u, 256u);
+                    tc_mma_i8(tmem + C::kDCol, a0 + (uint32_t)(sb * 8), bd, C::kIdesc, sb > 0 ? 1u : 0u);
+                    tc_mma_i8(tmem + C::kDCol + 3u * NT, a0 + 64u + (uint32_t)(sb * 8), bd, C::kIdesc,
+                              sb > 0 ? 1u : 0u);
+                }
+                tc_commit(mma_done);
+                last_mma = r;
+            }
+            d_prev = d;
+        }
+        if (*dec_abort) {
+            if (threadIdx.x == 0) {
+                atomicExch(p.err, 4u);
+                if (last_mma >= 0) mbar_wait(mma_done, (uint32_t)last_mma & 1u, 1u << 20);
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
 // ------------------------------- repack ---------------------------------------
 // GGUF block_iq4_xs rows -> per (128-row tile, 256-column block): qs as
 // [8 sub-blocks][128 rows][16 B], then [128 rows][8 B] scales in the
@@ -604,7 +888,7 @@ int qb_qmv_tc_max_ctas() {
 }
 
 // partial rows of both kernels: 16 token columns (the N <= 4 kernel uses 4 of them per row slot)
-size_t qb_qmv_tc_partial_floats(int max_ctas) { return (size_t)max_ctas * 2 * kRows * 16; }
+size_t qb_qmv_tc_partial_floats(int max_ctas) { return (size_t)max_ctas * 2 * kRows * QB_TCW_TOK; }
 
 cudaError_t qb_qmv_tc(const QbQSeg* segs, int nseg, int K, int N, const QbXBuf& xb, int accumulate, int row_lo,
                       int row_hi, const QbQmvWork& work, cudaStream_t st) {
@@ -695,4 +979,64 @@ cudaError_t qb_qmv_tc16(const QbQSeg* segs, int nseg, int K, int N, const QbXBuf
         attr_set = true;
     }
     return qb_launch(qmv_tc16_kernel, dim3(G), dim3(kThreads16), smem, st, p);
+}
+
+cudaError_t qb_qmv_tcw(const QbQSeg* segs, int nseg, int K, int N, const QbXBuf& xb, int accumulate, int row_lo,
+                       int row_hi, const QbQmvWork& work, cudaStream_t st) {
+    const bool n16 = N <= QB_TC16_TOK;
+    if (nseg < 1 || nseg > QB_MAX_SEG || N < 1 || N > QB_TCW_TOK || K % 256 || !xb.xqscale ||
+        (n16 ? !xb.xtc16 : !xb.xtc32))
+        return cudaErrorInvalidValue;
+    TcK p = {};
+    int tiles = 0;
+    for (int i = 0; i < nseg; ++i) {
+        p.w[i] = (const uint8_t*)segs[i].w;
+        p.out[i] = segs[i].out;
+        p.ldo[i] = segs[i].ldo;
+        p.rows[i] = segs[i].rows;
+        p.tile0[i] = tiles;
+        tiles += (segs[i].rows + kRows - 1) / kRows;
+    }
+    p.tile0[nseg] = tiles;
+    if ((long long)tiles * kRows > work.max_tc_rows) return cudaErrorInvalidValue;
+    p.nseg = nseg;
+    p.nb = K / 256;
+    p.N = N;
+    const long long S = (long long)tiles * p.nb;
+    if (S >= (1ll << 30)) return cudaErrorInvalidValue;
+    p.S = (int)S;
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    int G = sms;   // one CTA per SM: each holds all 512 tensor-memory columns
+    if (G > work.max_tc_ctas) G = work.max_tc_ctas;
+    if (G > p.S) G = p.S;
+    p.G = G;
+    p.xb = n16 ? xb.xtc16 : xb.xtc32;
+    p.xqscale = xb.xqscale;
+    p.accumulate = accumulate;
+    p.row_lo = row_lo;
+    p.row_hi = row_hi;
+    p.partial = work.tc_partial;
+    p.counters = work.tc_counters;
+    p.err = work.err;
+    if (n16) {
+        const size_t smem = kHdrW + (size_t)Tcw<16>::kRing * Tcw<16>::kStage;
+        static bool attr16 = false;
+        if (!attr16) {
+            cudaError_t e = cudaFuncSetAttribute(qmv_tcw_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)smem);
+            if (e != cudaSuccess) return e;
+            attr16 = true;
+        }
+        return qb_launch(qmv_tcw_kernel<16>, dim3(G), dim3(kThreadsW), smem, st, p);
+    }
+    const size_t smem = kHdrW + (size_t)Tcw<32>::kRing * Tcw<32>::kStage;
+    static bool attr32 = false;
+    if (!attr32) {
+        cudaError_t e = cudaFuncSetAttribute(qmv_tcw_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        attr32 = true;
+    }
+    return qb_launch(qmv_tcw_kernel<32>, dim3(G), dim3(kThreadsW), smem, st, p);
 }

@@ -1323,6 +1323,7 @@ size_t qb_xq_bytes(int K) { return (size_t)(K + 255) / 256 * 256 / 32 * 3 * 32 *
 
 size_t qb_xtc_bytes(int K) { return (size_t)(K + 255) / 256 * 4096; }
 size_t qb_xtc16_bytes(int K) { return (size_t)(K + 255) / 256 * 12288; }
+size_t qb_xtc32_bytes(int K) { return (size_t)(K + 255) / 256 * 24576; }
 
 int qb_xprep_needs(int type, int N, int tc) {
     switch (type) {
@@ -1338,13 +1339,11 @@ int qb_xprep_needs(int type, int N, int tc) {
 cudaError_t qb_xprep(const QbXIn* in, int nseg, int N, float eps, const QbXBuf& xb, int what, cudaStream_t st) {
     XSeg s[2] = {};
     int K = 0;
-    // up to QB_MAX_TOK tokens, QB_TC16_TOK for the 16-token tcgen05 tiles alone, or
-    // QB_WIDE in chunks of QB_MAX_TOK (QbXBuf chunk strides set for every output asked for)
-    const bool wide = N > QB_MAX_TOK && what != QB_XP_TC16;
-    if (nseg < 1 || nseg > 2 || N < 1 || N > (what == QB_XP_TC16 ? QB_TC16_TOK : QB_WIDE))
-        return cudaErrorInvalidValue;
-    if (wide && ((what & (QB_XP_TC | QB_XP_TC16)) || ((what & QB_XP_F16) && (!xb.cs_frag || !xb.cs_scale)) ||
-                 ((what & QB_XP_SUM) && !xb.cs_sum) || ((what & QB_XP_I8) && (!xb.cs_q || !xb.cs_qscale))))
+    // up to QB_MAX_TOK tokens; or up to QB_WIDE, the 8-row formats in chunks of
+    // QB_MAX_TOK rows (QbXBuf chunk strides set), the 16-token tiles up to 16 rows
+    if (nseg < 1 || nseg > 2 || N < 1 || N > QB_WIDE) return cudaErrorInvalidValue;
+    if (N > QB_MAX_TOK && ((what & QB_XP_TC) || ((what & QB_XP_TC16) && N > QB_TC16_TOK) ||
+                           ((what & QB_XP_F16) && !xb.cs_frag) || ((what & QB_XP_I8) && !xb.cs_q)))
         return cudaErrorInvalidValue;
     for (int i = 0; i < nseg; ++i) {
         s[i].x = in[i].x;
@@ -1356,7 +1355,7 @@ cudaError_t qb_xprep(const QbXIn* in, int nseg, int N, float eps, const QbXBuf& 
     }
     if (((what & QB_XP_F16) && (!xb.xfrag || !xb.xscale)) || ((what & QB_XP_SUM) && !xb.xsum) ||
         ((what & QB_XP_I8) && (!xb.xq || !xb.xqscale)) || ((what & QB_XP_TC) && (!xb.xtc || !xb.xqscale || N > 4)) ||
-        ((what & QB_XP_TC16) && (!xb.xtc16 || !xb.xqscale)))
+        ((what & QB_XP_TC16) && (!xb.xtc16 || !xb.xqscale)) || ((what & QB_XP_TC32) && (!xb.xtc32 || !xb.xqscale)))
         return cudaErrorInvalidValue;
     const int nb = K / 256;
     return qb_launch(xprep_kernel, dim3((nb + 7) / 8, N), dim3(256), 0, st, s[0], s[1], nseg, N, eps, xb, what);

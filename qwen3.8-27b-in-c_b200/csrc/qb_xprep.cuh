@@ -85,7 +85,7 @@ __device__ __forceinline__ void xprep_emit_g(const float (&v)[G][8], int t0, int
                 for (int k = 0; k < G; ++k) xb.xsum[(t0 + k) * (K >> 5) + sb] = ps[k];
         }
     }
-    if (what & (QB_XP_I8 | QB_XP_TC | QB_XP_TC16)) {
+    if (what & (QB_XP_I8 | QB_XP_TC | QB_XP_TC16 | QB_XP_TC32)) {
         // X = rint(x * 2^e) with |X| <= 2^22, as balanced int8 digits X = 65536 d0 + 256 d1 + d2
         // (|d0| <= 64).  Lane 8j + c (c < 4) holds elements 4c..4c+3 of sub-block j and
         // lane 8j + c + 4 elements 16+4c..16+4c+3: together one mma B register pair.
@@ -145,11 +145,16 @@ __device__ __forceinline__ void xprep_emit_g(const float (&v)[G][8], int t0, int
                         bv.y = prmt(dg[k][dgi], other[k][dgi], 0x7362u);   // (4c+2, 4c+18, 4c+3, 4c+19)
                         if ((what & QB_XP_I8) && t < QB_MAX_TOK)
                             xb.xq[((size_t)kb * NTI + dnt[dgi]) * 32 + dcol[dgi] * 4 + c] = bv;
-                        if (what & QB_XP_TC16) {
+                        if ((what & QB_XP_TC16) && t < 16) {
                             // 48-row tcgen05 B tile of the sub-block, digit-major: row n = 16 digit + t
                             // (one 16-column accumulator group per digit); same core-matrix layout
                             const int nrow = 16 * dgi + t;
                             *reinterpret_cast<uint2*>(xb.xtc16 + (size_t)kb * 1536 + (c >> 1) * 128 +
+                                                      (nrow >> 3) * 256 + (nrow & 7) * 16 + (c & 1) * 8) = bv;
+                        }
+                        if (what & QB_XP_TC32) {   // the same with 32 tokens: row n = 32 digit + t
+                            const int nrow = 32 * dgi + t;
+                            *reinterpret_cast<uint2*>(xb.xtc32 + (size_t)kb * 3072 + (c >> 1) * 128 +
                                                       (nrow >> 3) * 256 + (nrow & 7) * 16 + (c & 1) * 8) = bv;
                         }
                         if ((what & QB_XP_TC) && t < 4) {
@@ -168,15 +173,20 @@ __device__ __forceinline__ void xprep_emit_g(const float (&v)[G][8], int t0, int
 }
 
 // one token: v[0..3] = elements 4*lane .. 4*lane+3 of block b of token t, v[4..7] = 128 + 4*lane ..
-// A wide input (N > QB_MAX_TOK, no 16-token tcgen05 tiles) goes to the chunk of 8 rows
-// that holds t.
+// A wide input (N > QB_MAX_TOK): the 8-row formats go to the chunk of 8 rows that
+// holds t, the 16- / 32-token tcgen05 tiles take row t itself.
 __device__ __forceinline__ void xprep_emit(const float (&v)[8], int t, int b, int N, int nb, int K,
                                            const QbXBuf& xb, int what, int lane) {
-    if (N > QB_MAX_TOK && !(what & QB_XP_TC16)) {
-        const int c = t >> 3;
-        xprep_emit_g<1>(reinterpret_cast<const float (&)[1][8]>(v), t & 7, b, min(QB_MAX_TOK, N - 8 * c), nb, K,
-                        qb_xb_chunk(xb, c), what & ~(QB_XP_TC | QB_XP_TC16), lane);
+    const float (&v1)[1][8] = reinterpret_cast<const float (&)[1][8]>(v);
+    if (N > QB_MAX_TOK) {
+        const int tcw = what & (QB_XP_TC16 | QB_XP_TC32);
+        const int rest = what & (QB_XP_F16 | QB_XP_SUM | QB_XP_I8);
+        if (rest) {
+            const int c = t >> 3;
+            xprep_emit_g<1>(v1, t & 7, b, min(QB_MAX_TOK, N - 8 * c), nb, K, qb_xb_chunk(xb, c, nb), rest, lane);
+        }
+        if (tcw) xprep_emit_g<1>(v1, t, b, N, nb, K, xb, tcw, lane);
         return;
     }
-    xprep_emit_g<1>(reinterpret_cast<const float (&)[1][8]>(v), t, b, N, nb, K, xb, what, lane);
+    xprep_emit_g<1>(v1, t, b, N, nb, K, xb, what, lane);
 }

@@ -170,10 +170,11 @@ def test_gemv_multi_single_vector_and_limits():
         qb.gemv_multi(ts * 3, x)
 
 
-@pytest.mark.parametrize("n", [9, 12, 16, 17, 32, 64])
+@pytest.mark.parametrize("n", [9, 12, 16, 17, 32, 33, 64])
 def test_gemv_batch_iq4_wide_tcgen05(n):
-    """More than 8 vectors: IQ4_XS runs 16 per weight sweep on the tcgen05
-    kernel (qb_qmv_tc16).  The reference's gemv_batch runs them 8 at a time,
+    """More than 8 vectors: IQ4_XS runs up to 32 per weight sweep on the tcgen05
+    kernel (qb_qmv_tcw: sub-block scales folded into two int8 weight planes, one
+    accumulator per plane and digit).  The reference's gemv_batch runs them 8 at a time,
     each chunk bit-identical to a single-vector sweep (src/test_batch.c:44-57),
     so the bar is the same as for the mma.sync path."""
     K, rows = 2048, 333        # rows not a multiple of the 128-row tile
@@ -198,9 +199,22 @@ def test_gemv_batch_iq4_wide_micro_shape(n):
         assert rel(got[i], ref[i]) < RTOL, (i, rel(got[i], ref[i]))
 
 
+def test_gemv_iq4_wide_rows_do_not_depend_on_width():
+    """The 32-token and the 16-token instantiation of qb_qmv_tcw give every
+    vector the same bits (the per-(tile, block) integer sums are exact and the
+    tile split over CTAs depends on the matrix only), at any width 9..32."""
+    K, rows = 2048, 333
+    raw = qb.synth_matrix(qb.GGML_IQ4_XS, rows, K, seed=41, d_sigma=0.01)
+    t = qb.tensor(raw, qb.GGML_IQ4_XS, K, rows)
+    x = qb.synth_normal(32 * K, seed=42).reshape(32, K)
+    full = qb.gemv_batch(t, x)                  # one 32-token sweep
+    for n in (9, 16, 17, 24):
+        np.testing.assert_array_equal(qb.gemv_batch(t, x[:n]), full[:n], err_msg=f"n = {n}")
+
+
 def test_gemv_multi_batch_iq4_wide():
-    """gemv_multi_batch with 20 vectors over IQ4_XS matrices: the 16-token
-    kernel per chunk, each matrix bit-identical to its own gemv_batch."""
+    """gemv_multi_batch with 20 vectors over IQ4_XS matrices: the 32-token
+    kernel, each matrix bit-identical to its own gemv_batch."""
     K, n = 1024, 20
     specs = [(300, 1), (520, 2), (64, 3)]
     raws = [qb.synth_matrix(qb.GGML_IQ4_XS, r, K, seed=s, d_sigma=0.01) for r, s in specs]
