@@ -30,7 +30,7 @@ struct QbQmvWork {
     int max_pairs;
     // tcgen05 IQ4_XS path (qb_qmv_tc)
     float* tc_partial;       // [max_tc_ctas][2][128][4]
-    unsigned* tc_counters;   // [max_tc_rows][2] (per row; per row and token half for 16 vectors), zero-initialised
+    unsigned* tc_counters;   // [max_tc_rows][4] (per row, or per row and token group of 8), zero-initialised
     int max_tc_ctas;
     long long max_tc_rows;   // rows of all fused matrices, rounded up to 128-row tiles
 };

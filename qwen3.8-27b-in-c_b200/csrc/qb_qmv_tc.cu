@@ -548,19 +548,33 @@ __global__ void __launch_bounds__(kThreads16, 1) qmv_tc16_kernel(TcK p) {
 // sub-block becomes A = s * kvalues[c] (|A| <= 4064), written to tensor memory
 // as two int8 planes A = 64 H + L (L in [-32, 31], H in [-63, 64]) by a
 // byte-permute lookup in a shared table indexed by s.  Per (tile, block) stage
-// one thread issues 16 MMAs (M 128, N 3 NT, K 32): the 8 sub-blocks of each
-// plane accumulate into one D region, so the sums arrive already scaled, and
-// per (row, token, digit) the epilogue forms 64 SH + SL.  That integer is the
-// one the other paths build from per-sub-block sums (sum over k of s kv_k D_k),
-// and the digits and the fp16 block scale are combined in fp32 in the same
-// order (65536 d0 + (256 d1 + d2)), so a (tile, block) gives the same value
-// here, on qb_qmv_tc16 and on the mma.sync GEMV.
+// 16 MMAs (M 128, N 3 NT, K 32): the 8 sub-blocks of each plane accumulate into
+// one D region, so the sums arrive already scaled, and per (row, token, digit)
+// the epilogue forms 64 SH + SL.  That integer is the one the other paths build
+// from per-sub-block sums (sum over k of s kv_k D_k), and the digits and the
+// fp16 block scale are combined in fp32 in the same order (65536 d0 + (256 d1 +
+// d2)), so a (tile, block) gives the same value here, on qb_qmv_tc16 and on the
+// mma.sync GEMV.
 //
-// Tensor memory: A = 2 buffers x (H, L) x 8 sub-blocks x 8 columns (256), then
-// D = (H, L) x 3 NT columns (192 for 32 tokens); one CTA per SM.  The decode
-// of stage r (8 warps, two per lane quarter, each half of the sub-blocks of
-// its 32 rows) overlaps the MMAs of stage r-1; the epilogue of stage r-1 (each
-// warp half of the tokens) runs before the MMAs of stage r are issued.
+// Warp roles, each stage handed on by mbarriers so that neighbouring stages
+// overlap:
+//   warp 0       producer: bulk copies of the stage's weights and activation
+//                tiles into a 4-slot ring (slot freed by the MMAs' commit);
+//   warp 1       allocates the tensor memory; lane 0 issues the 16 MMAs of a
+//                stage once its A buffer is full and the epilogue has read D;
+//   warps 2-9    decode: two per lane quarter, each half of the sub-blocks of
+//                its 32 rows, into one of two A buffers (2 planes x 8 sub-blocks
+//                x 8 columns); the rows' block scales go to a 4-deep stage array;
+//   warps 10-    epilogue: NT / 8 per lane quarter, 8 tokens each; D is read
+//                into registers and released before the arithmetic.
+// Tensor memory: A 2 x 128 columns, D (H, L) x 3 NT columns; one CTA per SM.
+//
+// What bounds it (CUDA-event and per-stage timestamps, 17408 x 5120, 148 CTAs):
+// the tensor pipe.  The 16 MMAs of a 32-token stage (6.3 M int8 MACs) issue in
+// about 1.1 us, some 2000 MACs per SM clock, and the epilogue's read-out of D
+// and the hand-back add about 0.7 us before the next stage's MMAs; the decode
+// of the next stage (1.3 us) overlaps.  Exact sums need the 6 products per
+// weight and token (2 planes x 3 digits).
 template <int NT>
 struct Tcw {
     static constexpr int kB = 8 * 3 * NT * 32;          // B tiles of one block
@@ -568,12 +582,16 @@ struct Tcw {
     static constexpr int kRing = 4;
     static constexpr uint32_t kDCol = 256;
     static constexpr uint32_t kIdesc = idesc_i8(128, 3 * NT);
-    static constexpr int kTok = NT / 2;                 // tokens of one epilogue warp
+    static constexpr int kEpiWarps = NT / 2;            // 4 lane quarters x NT / 8 token groups
+    static constexpr int kWarps = 10 + kEpiWarps;
+    static constexpr int kThreads = kWarps * 32;
 };
-constexpr int kWarpsW = 8;
-constexpr int kThreadsW = kWarpsW * 32 + 32;            // + producer warp
-constexpr int kLutBytes = 64 * 2 * 16;                  // [s + 32][H, L][code]
-constexpr int kHdrW = 256 + kLutBytes;
+constexpr int kLutBytes = 64 * 2 * 16;                  // [H, L][s + 32][code]: 16-byte rows, 8 bank groups
+constexpr int kDStage = 4;                              // block scales of the last 4 stages
+constexpr int kXsMax = QB_TCW_TOK * 80;                 // activation scales [N][K / 256] (K <= 20480)
+constexpr int kHdrW = 256 + kLutBytes + kDStage * kRows * 4 + kXsMax * 4;
+constexpr int kTokW = 8;                                // tokens of one epilogue warp
+constexpr uint32_t kSpinW = 1u << 24;                   // try_wait rounds of the MMA / epilogue hand-offs (bounded)
 
 // 8 codes (the nibbles of w, element order of iq4_i8) -> bytes of the two planes
 __device__ __forceinline__ void lut16x2(uint32_t w, const uint4& TH, const uint4& TL, uint32_t& h0, uint32_t& h1,
@@ -587,21 +605,21 @@ __device__ __forceinline__ void lut16x2(uint32_t w, const uint4& TH, const uint4
     l1 = prmt(prmt(TL.x, TL.y, idxh), prmt(TL.z, TL.w, idxh), selh);
 }
 
+// row m of tile T complete for tokens tb..tb+7 (token group tg): store them, or
+// combine the split tile's per-CTA partials of this group (last arriving CTA, CTA order)
 template <int NT>
-__device__ void finish_row_w(const TcK& p, int T, int cta, int s0, int s1, int m, int h,
-                             const float (&tot)[Tcw<NT>::kTok]) {
-    constexpr int KT = Tcw<NT>::kTok;
+__device__ void finish_row_w(const TcK& p, int T, int cta, int s0, int s1, int m, int tg, const float (&tot)[kTokW]) {
     const int sg = seg_of_tile(p, T);
     const int row = (T - p.tile0[sg]) * kRows + m;
-    const int tb = KT * h;
-    auto store = [&](const float (&v)[KT]) {
+    const int tb = kTokW * tg;
+    auto store = [&](const float (&v)[kTokW]) {
         if (row >= p.rows[sg] || row < p.row_lo || row >= p.row_hi) return;
-        float prev[KT];
+        float prev[kTokW];
 #pragma unroll
-        for (int t = 0; t < KT; ++t)
-            prev[t] = (tb + t < p.N && p.accumulate) ? p.out[sg][(size_t)(tb + t) * p.ldo[sg] + row] : 0.f;
+        for (int t = 0; t < kTokW; ++t)   // L2 loads: this SM's L1 may hold an older copy of the output
+            prev[t] = (tb + t < p.N && p.accumulate) ? __ldcg(p.out[sg] + (size_t)(tb + t) * p.ldo[sg] + row) : 0.f;
 #pragma unroll
-        for (int t = 0; t < KT; ++t)
+        for (int t = 0; t < kTokW; ++t)
             if (tb + t < p.N) p.out[sg][(size_t)(tb + t) * p.ldo[sg] + row] = p.accumulate ? prev[t] + v[t] : v[t];
     };
     const int P0 = T * p.nb, P1 = P0 + p.nb;
@@ -611,46 +629,40 @@ __device__ void finish_row_w(const TcK& p, int T, int cta, int s0, int s1, int m
     }
     const int piece = s0 > P0 ? 0 : 1;
     float4* dst = reinterpret_cast<float4*>(p.partial + (((size_t)cta * 2 + piece) * kRows + m) * NT + tb);
-#pragma unroll
-    for (int i = 0; i < KT / 4; ++i) dst[i] = make_float4(tot[4 * i], tot[4 * i + 1], tot[4 * i + 2], tot[4 * i + 3]);
+    dst[0] = make_float4(tot[0], tot[1], tot[2], tot[3]);
+    dst[1] = make_float4(tot[4], tot[5], tot[6], tot[7]);
     const int c_first = stage_cta(p.S, p.G, P0), c_last = stage_cta(p.S, p.G, P1 - 1);
-    unsigned* ctr = p.counters + ((size_t)T * kRows + m) * 2 + h;
+    unsigned* ctr = p.counters + ((size_t)T * kRows + m) * 4 + tg;
     const unsigned old = atom_add_acq_rel_gpu(ctr, 1u);
     if ((int)old != c_last - c_first) return;
-    float sum[KT];
+    float sum[kTokW];
 #pragma unroll
-    for (int t = 0; t < KT; ++t) sum[t] = 0.f;
+    for (int t = 0; t < kTokW; ++t) sum[t] = 0.f;
     for (int c = c_first; c <= c_last; ++c) {
         const int pc = cta_s0(p.S, p.G, c) > P0 ? 0 : 1;
         const volatile float* v = p.partial + (((size_t)c * 2 + pc) * kRows + m) * NT + tb;
 #pragma unroll
-        for (int t = 0; t < KT; ++t) sum[t] += v[t];
+        for (int t = 0; t < kTokW; ++t) sum[t] += v[t];
     }
     store(sum);
     *ctr = 0u;
 }
 
-// KT consecutive accumulator columns of this thread's lane
-template <int KT>
-__device__ __forceinline__ void tmem_ldk(uint32_t taddr, uint32_t (&v)[KT]) {
-    if constexpr (KT == 16) {
-        tmem_ld16(taddr, v);
-    } else {
-        tmem_ld8(taddr, v);
-    }
-}
-
 template <int NT>
-__global__ void __launch_bounds__(kThreadsW, 1) qmv_tcw_kernel(TcK p) {
+__global__ void __launch_bounds__(Tcw<NT>::kThreads, 1) qmv_tcw_kernel(TcK p) {
     using C = Tcw<NT>;
-    constexpr int KT = C::kTok;
     extern __shared__ __align__(1024) uint8_t smem[];
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-    uint64_t* empty = full + C::kRing;
-    uint64_t* mma_done = empty + C::kRing;
-    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mma_done + 1);
-    volatile int* dec_abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);   // [kRing] producer -> decode / MMA
+    uint64_t* empty = full + C::kRing;                    // [kRing] MMA commit -> producer
+    uint64_t* a_full = empty + C::kRing;                  // [2] decode -> MMA
+    uint64_t* a_free = a_full + 2;                        // [2] MMA commit -> decode
+    uint64_t* d_full = a_free + 2;                        // MMA commit -> epilogue
+    uint64_t* d_free = d_full + 1;                        // epilogue -> MMA
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(d_free + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
     uint8_t* lut = smem + 256;
+    float* dstage = reinterpret_cast<float*>(smem + 256 + kLutBytes);   // [kDStage][kRows]
+    float* xs_s = dstage + kDStage * kRows;                               // [N][nb] activation scales
     uint8_t* ring = smem + kHdrW;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int cta = blockIdx.x;
@@ -661,8 +673,13 @@ __global__ void __launch_bounds__(kThreadsW, 1) qmv_tcw_kernel(TcK p) {
             mbar_init(full + i, 1);
             mbar_init(empty + i, 1);
         }
-        mbar_init(mma_done, 1);
-        *dec_abort = 0;
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(a_full + i, 8);   // the 8 decode warps
+            mbar_init(a_free + i, 1);
+        }
+        mbar_init(d_full, 1);
+        mbar_init(d_free, C::kEpiWarps);
+        *abort_flag = 0;
         mbar_fence_init();
     }
     // planes of s * kvalues[c] for every s: L = ((A + 32) mod 64) - 32, H = (A - L) / 64
@@ -671,10 +688,10 @@ __global__ void __launch_bounds__(kThreadsW, 1) qmv_tcw_kernel(TcK p) {
         const uint32_t kw = c < 4 ? kIq4I8T0 : c < 8 ? kIq4I8T1 : c < 12 ? kIq4I8T2 : kIq4I8T3;   // kvalues
         const int a = sv * (int)(int8_t)(kw >> (8 * (c & 3)));
         const int l = ((a + 32) & 63) - 32;
-        lut[(i >> 4) * 32 + c] = (uint8_t)(int8_t)((a - l) >> 6);
-        lut[(i >> 4) * 32 + 16 + c] = (uint8_t)(int8_t)l;
+        lut[(i >> 4) * 16 + c] = (uint8_t)(int8_t)((a - l) >> 6);
+        lut[1024 + (i >> 4) * 16 + c] = (uint8_t)(int8_t)l;
     }
-    if (warp == 0) {
+    if (warp == 1) {
         tmem_alloc(tmem_holder, 512);
         tmem_relinquish();
     }
@@ -684,7 +701,7 @@ __global__ void __launch_bounds__(kThreadsW, 1) qmv_tcw_kernel(TcK p) {
     const uint32_t tmem = *tmem_holder;
     pdl_trigger();
 
-    if (warp == kWarpsW) {
+    if (warp == 0) {
         // ------------------------------ producer ------------------------------
         if (lane == 0 && n > 0) {
             auto weights_of = [&](int s) -> const uint8_t* {
@@ -697,14 +714,15 @@ __global__ void __launch_bounds__(kThreadsW, 1) qmv_tcw_kernel(TcK p) {
                 mbar_expect_tx(full + r, C::kStage);
                 bulk_g2s(ring + r * C::kStage, weights_of(s0 + r), kUnit, full + r);
             }
-            pdl_wait();   // the activation digits are written by the previous kernel
+            pdl_wait();   // the activation tiles are written by the previous kernel
             for (int r = 0; r < pre; ++r)
                 bulk_g2s(ring + r * C::kStage + kUnit, p.xb + (size_t)((s0 + r) % p.nb) * C::kB, C::kB, full + r);
             int issued = pre;
-            for (int r = C::kRing; r < n; ++r) {
+            for (int r = C::kRing; r < n && !*abort_flag; ++r) {
                 const int slot = r % C::kRing;
                 if (!mbar_wait_sleep(empty + slot, (uint32_t)((r / C::kRing) - 1) & 1u, kSleepNs)) {
                     atomicExch(p.err, 3u);
+                    *abort_flag = 1;
                     break;
                 }
                 const int s = s0 + r;
@@ -713,91 +731,25 @@ __global__ void __launch_bounds__(kThreadsW, 1) qmv_tcw_kernel(TcK p) {
                 bulk_g2s(ring + slot * C::kStage + kUnit, p.xb + (size_t)(s % p.nb) * C::kB, C::kB, full + slot);
                 issued = r + 1;
             }
+            // no copy may still land in shared memory when the CTA exits
             for (int r = issued - C::kRing > 0 ? issued - C::kRing : 0; r < issued; ++r)
                 mbar_wait(full + r % C::kRing, (uint32_t)(r / C::kRing) & 1u, 1u << 20);
         }
-    } else if (n > 0) {
-        // --------------------------- decode / epilogue ---------------------------
-        pdl_wait();
-        const int q = warp & 3, h = warp >> 2;         // lane quarter, half
-        const int m = q * 32 + lane;                   // weight row of this thread
-        const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-        float tot[KT];
-#pragma unroll
-        for (int t = 0; t < KT; ++t) tot[t] = 0.f;
-        float d_prev = 0.f;
-        int last_mma = -1;
-        for (int r = 0; r <= n; ++r) {
-            float d = 0.f;
-            if (r < n) {
-                const int slot = r % C::kRing;
-                if (!mbar_wait_sleep(full + slot, (uint32_t)(r / C::kRing) & 1u, kSleepNs)) {
-                    *dec_abort = 1;
-                } else {
-                    const uint8_t* u = ring + slot * C::kStage;
-                    uint32_t L0, L1;
-                    iq4_scale_bytes(lds64(u + kQsBytes + m * 8), L0, L1, d);
-                    const uint32_t abuf = tmem + lane_base + (uint32_t)((r & 1) * 128);
-                    const uint32_t Lh = h ? L1 : L0;           // ls of sub-blocks 4h..4h+3
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        const int sb = 4 * h + k;
-                        const uint4 qq = lds128(u + sb * (kRows * 16) + m * 16);
-                        const uint8_t* tl = lut + ubyte(Lh, k) * 32;   // (ls - 32) + 32
-                        const uint4 TH = lds128(tl), TL = lds128(tl + 16);
-                        uint32_t aH[8], aL[8];
-                        lut16x2(qq.x, TH, TL, aH[0], aH[1], aL[0], aL[1]);
-                        lut16x2(qq.y, TH, TL, aH[2], aH[3], aL[2], aL[3]);
-                        lut16x2(qq.z, TH, TL, aH[4], aH[5], aL[4], aL[5]);
-                        lut16x2(qq.w, TH, TL, aH[6], aH[7], aL[6], aL[7]);
-                        tmem_st8(abuf + (uint32_t)(sb * 8), aH);
-                        tmem_st8(abuf + 64u + (uint32_t)(sb * 8), aL);
-                    }
-                    tmem_wait_st();
+    } else if (warp == 1) {
+        // -------------------------------- MMA ---------------------------------
+        if (lane == 0 && n > 0) {
+            int last = -1;
+            for (int r = 0; r < n; ++r) {
+                // the stage's activation tiles (already landed: the decode warps saw them), its A
+                // buffer, and D read out by the epilogue of the stage before.  (No suspend hint on
+                // these hand-offs: a waiter resumed late leaves the tensor pipe idle.)
+                if (!mbar_wait(full + r % C::kRing, (uint32_t)(r / C::kRing) & 1u, kSpinW) ||
+                    !mbar_wait(a_full + (r & 1), (uint32_t)(r >> 1) & 1u, kSpinW) ||
+                    (r >= 1 && !mbar_wait(d_free, (uint32_t)(r - 1) & 1u, kSpinW)) || *abort_flag) {
+                    atomicExch(p.err, 4u);
+                    *abort_flag = 1;
+                    break;
                 }
-            }
-            // epilogue of stage r-1, tokens KT h .. KT h + KT - 1: per digit 64 SH + SL
-            if (r >= 1 && !*dec_abort) {
-                const int rp = r - 1;
-                if (!mbar_wait_sleep(mma_done, (uint32_t)rp & 1u, kSleepNs)) {
-                    *dec_abort = 1;
-                } else {
-                    tc_fence_after();
-                    const uint32_t dbase = tmem + lane_base + C::kDCol + (uint32_t)(KT * h);
-                    const int b_prev = (s0 + rp) % p.nb;
-                    float f[KT];
-#pragma unroll
-                    for (int g = 2; g >= 0; --g) {
-                        uint32_t vh[KT], vl[KT];
-                        tmem_ldk<KT>(dbase + (uint32_t)(g * NT), vh);
-                        tmem_ldk<KT>(dbase + (uint32_t)(3 * NT + g * NT), vl);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int t = 0; t < KT; ++t) {
-                            const int c = 64 * (int)vh[t] + (int)vl[t];
-                            if (g == 2) f[t] = (float)c;
-                            else if (g == 1) f[t] = fmaf((float)c, 256.f, f[t]);
-                            else {
-                                const int tok = KT * h + t;
-                                const float v = fmaf((float)c, 65536.f, f[t]) * d_prev;
-                                const float xs = tok < p.N ? __ldg(p.xqscale + tok * p.nb + b_prev) : 0.f;
-                                tot[t] = fmaf(xs, v, tot[t]);
-                            }
-                        }
-                    }
-                    if (threadIdx.x == 0) mbar_arrive(empty + rp % C::kRing);
-                    const int s = s0 + rp;
-                    if ((s + 1) % p.nb == 0 || rp == n - 1) {
-                        finish_row_w<NT>(p, s / p.nb, cta, s0, s1, m, h, tot);
-#pragma unroll
-                        for (int t = 0; t < KT; ++t) tot[t] = 0.f;
-                    }
-                }
-            }
-            tc_fence_before();
-            named_bar_sync(1, kWarpsW * 32);
-            if (*dec_abort) break;
-            if (r < n && threadIdx.x == 0) {
                 tc_fence_after();
                 const uint32_t a0 = tmem + (uint32_t)((r & 1) * 128);
                 const uint32_t bsm = smem_u32(ring + (r % C::kRing) * C::kStage + kUnit);
@@ -808,22 +760,111 @@ __global__ void __launch_bounds__(kThreadsW, 1) qmv_tcw_kernel(TcK p) {
                     tc_mma_i8(tmem + C::kDCol + 3u * NT, a0 + 64u + (uint32_t)(sb * 8), bd, C::kIdesc,
                               sb > 0 ? 1u : 0u);
                 }
-                tc_commit(mma_done);
-                last_mma = r;
+                tc_commit(d_full);
+                tc_commit(a_free + (r & 1));
+                tc_commit(empty + r % C::kRing);
+                last = r;
             }
-            d_prev = d;
+            // the tensor memory is freed below: the last MMAs must have completed
+            if (last >= 0) mbar_wait(a_free + (last & 1), (uint32_t)(last >> 1) & 1u, 1u << 20);
         }
-        if (*dec_abort) {
-            if (threadIdx.x == 0) {
-                atomicExch(p.err, 4u);
-                if (last_mma >= 0) mbar_wait(mma_done, (uint32_t)last_mma & 1u, 1u << 20);
+    } else if (warp < 10) {
+        // ------------------------------- decode -------------------------------
+        if (n > 0) {
+            const int q = warp & 3, h = (warp - 2) >> 2;   // lane quarter (warp % 4), sub-block half
+            const int m = q * 32 + lane;
+            const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+            for (int r = 0; r < n; ++r) {
+                const int slot = r % C::kRing;
+                if (!mbar_wait_sleep(full + slot, (uint32_t)(r / C::kRing) & 1u, kSleepNs) ||
+                    (r >= 2 && !mbar_wait_sleep(a_free + (r & 1), (uint32_t)((r - 2) >> 1) & 1u, kSleepNs)) ||
+                    *abort_flag) {
+                    atomicExch(p.err, 4u);
+                    *abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint8_t* u = ring + slot * C::kStage;
+                uint32_t L0, L1;
+                float d;
+                iq4_scale_bytes(lds64(u + kQsBytes + m * 8), L0, L1, d);
+                if (h == 0) dstage[(r % kDStage) * kRows + m] = d;
+                const uint32_t abuf = tmem + lane_base + (uint32_t)((r & 1) * 128);
+                const uint32_t Lh = h ? L1 : L0;           // ls of sub-blocks 4h..4h+3
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int sb = 4 * h + k;
+                    const uint4 qq = lds128(u + sb * (kRows * 16) + m * 16);
+                    const uint8_t* tl = lut + ubyte(Lh, k) * 16;   // (ls - 32) + 32
+                    const uint4 TH = lds128(tl), TL = lds128(tl + 1024);
+                    uint32_t aH[8], aL[8];
+                    lut16x2(qq.x, TH, TL, aH[0], aH[1], aL[0], aL[1]);
+                    lut16x2(qq.y, TH, TL, aH[2], aH[3], aL[2], aL[3]);
+                    lut16x2(qq.z, TH, TL, aH[4], aH[5], aL[4], aL[5]);
+                    lut16x2(qq.w, TH, TL, aH[6], aH[7], aL[6], aL[7]);
+                    tmem_st8(abuf + (uint32_t)(sb * 8), aH);
+                    tmem_st8(abuf + 64u + (uint32_t)(sb * 8), aL);
+                }
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(a_full + (r & 1));
+            }
+        }
+    } else {
+        // ------------------------------ epilogue ------------------------------
+        if (n > 0) {
+            pdl_wait();   // the output rows (accumulate) and the scales are the previous kernels'
+            // this launch's activation scales into shared memory (L2 loads: an older copy may be in L1)
+            for (int i = threadIdx.x - 320; i < p.N * p.nb; i += C::kEpiWarps * 32) xs_s[i] = __ldcg(p.xqscale + i);
+            named_bar_sync(2, C::kEpiWarps * 32);
+            const int q = warp & 3, tg = (warp - 10) >> 2;   // lane quarter (warp % 4), token group
+            const int m = q * 32 + lane;
+            const uint32_t dbase = tmem + ((uint32_t)(q * 32) << 16) + C::kDCol + (uint32_t)(kTokW * tg);
+            float tot[kTokW];
+#pragma unroll
+            for (int t = 0; t < kTokW; ++t) tot[t] = 0.f;
+            for (int r = 0; r < n; ++r) {
+                if (!mbar_wait(d_full, (uint32_t)r & 1u, kSpinW) || *abort_flag) {
+                    atomicExch(p.err, 4u);
+                    *abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
+                const float d = dstage[(r % kDStage) * kRows + m];
+                uint32_t v[6][kTokW];   // (H, L) x digit 0..2
+#pragma unroll
+                for (int g = 0; g < 3; ++g) {
+                    tmem_ld8(dbase + (uint32_t)(g * NT), v[2 * g]);
+                    tmem_ld8(dbase + (uint32_t)(3 * NT + g * NT), v[2 * g + 1]);
+                }
+                tmem_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(d_free);   // D may take the next stage's sums
+                const int b = (s0 + r) % p.nb;
+#pragma unroll
+                for (int t = 0; t < kTokW; ++t) {
+                    const int tok = kTokW * tg + t;
+                    float f = (float)(64 * (int)v[4][t] + (int)v[5][t]);
+                    f = fmaf((float)(64 * (int)v[2][t] + (int)v[3][t]), 256.f, f);
+                    const float val = fmaf((float)(64 * (int)v[0][t] + (int)v[1][t]), 65536.f, f) * d;
+                    const float xs = tok < p.N ? xs_s[tok * p.nb + b] : 0.f;
+                    tot[t] = fmaf(xs, val, tot[t]);
+                }
+                const int s = s0 + r;
+                if ((s + 1) % p.nb == 0 || r == n - 1) {
+                    finish_row_w<NT>(p, s / p.nb, cta, s0, s1, m, tg, tot);
+#pragma unroll
+                    for (int t = 0; t < kTokW; ++t) tot[t] = 0.f;
+                }
             }
         }
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 0) tmem_dealloc(tmem, 512);
+    if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
 // ------------------------------- repack ---------------------------------------
@@ -984,7 +1025,7 @@ cudaError_t qb_qmv_tc16(const QbQSeg* segs, int nseg, int K, int N, const QbXBuf
 cudaError_t qb_qmv_tcw(const QbQSeg* segs, int nseg, int K, int N, const QbXBuf& xb, int accumulate, int row_lo,
                        int row_hi, const QbQmvWork& work, cudaStream_t st) {
     const bool n16 = N <= QB_TC16_TOK;
-    if (nseg < 1 || nseg > QB_MAX_SEG || N < 1 || N > QB_TCW_TOK || K % 256 || !xb.xqscale ||
+    if (nseg < 1 || nseg > QB_MAX_SEG || N < 1 || N > QB_TCW_TOK || K % 256 || N * (K / 256) > kXsMax || !xb.xqscale ||
         (n16 ? !xb.xtc16 : !xb.xtc32))
         return cudaErrorInvalidValue;
     TcK p = {};
@@ -1029,7 +1070,7 @@ cudaError_t qb_qmv_tcw(const QbQSeg* segs, int nseg, int K, int N, const QbXBuf&
             if (e != cudaSuccess) return e;
             attr16 = true;
         }
-        return qb_launch(qmv_tcw_kernel<16>, dim3(G), dim3(kThreadsW), smem, st, p);
+        return qb_launch(qmv_tcw_kernel<16>, dim3(G), dim3(Tcw<16>::kThreads), smem, st, p);
     }
     const size_t smem = kHdrW + (size_t)Tcw<32>::kRing * Tcw<32>::kStage;
     static bool attr32 = false;
@@ -1038,5 +1079,5 @@ cudaError_t qb_qmv_tcw(const QbQSeg* segs, int nseg, int K, int N, const QbXBuf&
         if (e != cudaSuccess) return e;
         attr32 = true;
     }
-    return qb_launch(qmv_tcw_kernel<32>, dim3(G), dim3(kThreadsW), smem, st, p);
+    return qb_launch(qmv_tcw_kernel<32>, dim3(G), dim3(Tcw<32>::kThreads), smem, st, p);
 }
