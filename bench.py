@@ -584,7 +584,9 @@ def run_components(args):
                                    ("draft", 2, 1, args.iters), ("verify_b4", 0, 4, args.iters),
                                    # these run on stale activations (timing only): after the others
                                    ("ffn_down_n4", 5, 4, args.iters), ("out_proj_n4", 6, 4, args.iters),
-                                   ("in_proj_n4", 7, 4, args.iters)]:
+                                   ("in_proj_n4", 7, 4, args.iters),
+                                   # FFN up on the wide tcgen05 GEMM (multi-sequence verify / 32 rows)
+                                   ("tcw_ffn_up_n32", 10, 32, args.iters), ("tcw_ffn_up_n16", 10, 16, args.iters)]:
         if args.only and name not in args.only.split(","):
             continue
         ms, b = model.bench(what, arg, iters)
