@@ -316,9 +316,9 @@ int qb_seq_generate(qwen_model_t *m, uint32_t n_cycles, uint32_t n_spec, const u
  * component: what = 0 verify forward of `arg` tokens with checkpoints, 1 the
  * fused FFN gate+up GEMV at N = arg rotated over all layers, 2 one MTP draft
  * with logits, 3 the output-head GEMV at N = arg, 5 / 6 / 7 the down, out- and
- * in-projection GEMVs at N = arg, 8 one FFN up matrix alone at N = arg, 9 the
- * same on the 16-vector tcgen05 kernel at N = arg <= 16 (every one of these
- * rotated over all layers); what = 4 returns instead
+ * in-projection GEMVs at N = arg, 8 one FFN up matrix alone at N = arg, 10 the
+ * same on the wide tcgen05 GEMM at N = arg <= 32 (every one of these rotated
+ * over all layers); what = 4 returns instead
  * the number of kernels one speculative cycle launches (after a
  * qb_spec_generate call).  *bytes receives the algorithmic bytes of one
  * run.  Overwrites KV / recurrent state.  -1 on error. */

@@ -2422,11 +2422,10 @@ extern "C" float qb_bench(qwen_model_t* m, int what, uint32_t arg, uint32_t iter
             }
             b /= (double)nl;
         }
-    } else if (what == 9 || what == 10) {
-        // one FFN up matrix at N = arg, rotated over all layers: what 9 on the 16-vector
-        // tcgen05 kernel (9..16), what 10 on the scale-folded one (9..32); the tcgen05
-        // tile copies of those matrices are made on first use
-        if (arg < 1 || arg > (what == 9 ? QB_TC16_TOK : QB_TCW_TOK) || e->tp_world > 1) return -1.f;
+    } else if (what == 10) {
+        // one FFN up matrix at N = arg (1..32), rotated over all layers, on the wide tcgen05
+        // GEMM; the tcgen05 tile copies of those matrices are made on first use
+        if (arg < 1 || arg > QB_TCW_TOK || e->tp_world > 1) return -1.f;
         const int nl = (int)e->L.size();
         for (int li = 0; li < nl; ++li)
             if (ensure_w_tc(*e, e->L[li].ffn_up)) return -1.f;
@@ -2438,24 +2437,22 @@ extern "C" float qb_bench(qwen_model_t* m, int what, uint32_t arg, uint32_t iter
         }
         // input: arg rows of the FFN activation buffer (any finite values), prepared once
         const QbXIn in{e->act, e->E, nullptr, e->E};
-        const int xw = (what == 9 || arg <= QB_TC16_TOK) ? QB_XP_TC16 : QB_XP_TC32;
+        const int xw = arg <= QB_TC16_TOK ? QB_XP_TC16 : QB_XP_TC32;
         if (qb_xprep(&in, 1, (int)arg, e->eps, e->xb16, xw, e->st) != cudaSuccess) return -1.f;
         struct Rec9 {
-            static int go(Engine& en, int packed) {
-                const int a = packed & 0xFF, wh = packed >> 8;
+            static int go(Engine& en, int a) {
                 for (const LayerW& ly : en.L) {
                     QbQSeg seg;
                     seg.w = ly.ffn_up.w_tc;
                     seg.out = en.logits;   // [a][F] rows of the logits buffer
                     seg.ldo = en.F;
                     seg.rows = ly.ffn_up.rows;
-                    if (wh == 9) CK(qb_qmv_tc16(&seg, 1, en.E, a, en.xb16, 0, 0, 1 << 30, en.work, en.st));
-                    else CK(qb_qmv_tcw(&seg, 1, en.E, a, en.xb16, 0, 0, 1 << 30, en.work, en.st));
+                    CK(qb_qmv_tcw(&seg, 1, en.E, a, en.xb16, 0, 0, 1 << 30, en.work, en.st));
                 }
                 return 0;
             }
         };
-        if (capture(*e, &ge, Rec9::go, (int)arg | (what << 8))) return -1.f;
+        if (capture(*e, &ge, Rec9::go, (int)arg)) return -1.f;
         cudaGraphLaunch(ge, e->st);
         cudaEventRecord(e->ev0, e->st);
         for (uint32_t i = 0; i < iters; ++i) cudaGraphLaunch(ge, e->st);

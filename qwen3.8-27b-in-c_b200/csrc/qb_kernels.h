@@ -161,15 +161,10 @@ size_t qb_repacked_bytes_tc(int rows, int K);
 cudaError_t qb_repack_tc(const void* src_dev, int rows, int K, void* dst_dev, cudaStream_t st);
 int qb_qmv_tc_max_ctas();
 size_t qb_qmv_tc_partial_floats(int max_ctas);
-// 9..16 input vectors (QB_TC16_TOK): the same weight layout, activation digits
-// from xb.xtc16 (qb_xprep QB_XP_TC16), scales from xb.xqscale
-// [QB_TC16_TOK][K/256]; one CTA per SM
-cudaError_t qb_qmv_tc16(const QbQSeg* segs, int nseg, int K, int N, const QbXBuf& xb, int accumulate, int row_lo,
-                        int row_hi, const QbQmvWork& work, cudaStream_t st);
 // 9..32 input vectors in one weight sweep, sub-block scales folded into the
 // weights (two int8 planes per code): activation tiles from xb.xtc16 (N <= 16)
 // or xb.xtc32, scales from xb.xqscale [N][K/256]; one CTA per SM; the same
-// value per (tile, block) as qb_qmv_tc16 and the mma.sync GEMV
+// value per (tile, block) as the mma.sync GEMV
 cudaError_t qb_qmv_tcw(const QbQSeg* segs, int nseg, int K, int N, const QbXBuf& xb, int accumulate, int row_lo,
                        int row_hi, const QbQmvWork& work, cudaStream_t st);
 // segs[i].w are qb_repack_tc layouts

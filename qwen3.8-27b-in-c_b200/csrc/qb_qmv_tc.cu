@@ -290,258 +290,6 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qmv_tc_kernel(TcK p) {
     if (warp == 0) tmem_dealloc(tmem, kCols);
 }
 
-// ----------------------- 16 input vectors (N 9..16) -------------------------
-// The same tiles and decode for up to 16 tokens: the activation digits of a
-// sub-block are a 48-row B tile, digit-major (row 16 d + t: d0 of the 16
-// tokens, then d1, then d2), so the MMA is M 128 N 48 K 32 and each digit's
-// sums are one 16-column group of accumulators.  Tensor memory: A in 2 x 64
-// columns as above, D in 8 sub-blocks x 48 columns: all 512 columns, one CTA
-// per SM.  Eight decode / epilogue warps, two per tensor-memory lane quarter:
-// warp w (half h = w / 4) decodes sub-blocks 4h..4h+3 of its 32 rows and runs
-// the epilogue of tokens 8h..8h+7, so two warps per SM sub-partition hide each
-// other's latency.  The epilogue applies the sub-block scales per digit in
-// int32 and combines the digits in fp32 in the order of the other paths
-// (65536 d0 + (256 d1 + d2)), so a (tile, block) gives the same value here as
-// in the mma.sync GEMV; only the order of the per-block sums across split
-// tiles differs.
-constexpr int kB16 = 8 * 48 * 32;             // B tiles of one block: 12288
-constexpr int kStage16 = kUnit + kB16;        // 29696
-constexpr int kRing16 = 4;
-constexpr uint32_t kCols16 = 512;
-constexpr uint32_t kDCol16 = 128;
-constexpr uint32_t kIdesc16 = idesc_i8(128, 48);
-constexpr int kWarps16 = 8;                   // decode / epilogue warps
-constexpr int kThreads16 = kWarps16 * 32 + 32;   // + producer warp
-
-// row m of tile T complete for tokens 8h..8h+7: store them, or combine the split
-// tile's per-CTA partials of this half (last arriving CTA, CTA order)
-__device__ void finish_row16(const TcK& p, int T, int cta, int s0, int s1, int m, int h, const float (&tot)[8]) {
-    const int sg = seg_of_tile(p, T);
-    const int row = (T - p.tile0[sg]) * kRows + m;
-    const int tb = 8 * h;
-    auto store = [&](const float (&v)[8]) {
-        if (row >= p.rows[sg] || row < p.row_lo || row >= p.row_hi) return;
-        float prev[8];
-#pragma unroll
-        for (int t = 0; t < 8; ++t)
-            prev[t] = (tb + t < p.N && p.accumulate) ? p.out[sg][(size_t)(tb + t) * p.ldo[sg] + row] : 0.f;
-#pragma unroll
-        for (int t = 0; t < 8; ++t)
-            if (tb + t < p.N) p.out[sg][(size_t)(tb + t) * p.ldo[sg] + row] = p.accumulate ? prev[t] + v[t] : v[t];
-    };
-    const int P0 = T * p.nb, P1 = P0 + p.nb;
-    if (s0 <= P0 && s1 >= P1) {
-        store(tot);
-        return;
-    }
-    const int piece = s0 > P0 ? 0 : 1;
-    float4* dst = reinterpret_cast<float4*>(p.partial + (((size_t)cta * 2 + piece) * kRows + m) * 16 + tb);
-    dst[0] = make_float4(tot[0], tot[1], tot[2], tot[3]);
-    dst[1] = make_float4(tot[4], tot[5], tot[6], tot[7]);
-    const int c_first = stage_cta(p.S, p.G, P0), c_last = stage_cta(p.S, p.G, P1 - 1);
-    unsigned* ctr = p.counters + ((size_t)T * kRows + m) * 2 + h;
-    const unsigned old = atom_add_acq_rel_gpu(ctr, 1u);
-    if ((int)old != c_last - c_first) return;
-    float sum[8];
-#pragma unroll
-    for (int t = 0; t < 8; ++t) sum[t] = 0.f;
-    for (int c = c_first; c <= c_last; ++c) {
-        const int pc = cta_s0(p.S, p.G, c) > P0 ? 0 : 1;
-        const volatile float* v = p.partial + (((size_t)c * 2 + pc) * kRows + m) * 16 + tb;
-#pragma unroll
-        for (int t = 0; t < 8; ++t) sum[t] += v[t];
-    }
-    store(sum);
-    *ctr = 0u;
-}
-
-__global__ void __launch_bounds__(kThreads16, 1) qmv_tc16_kernel(TcK p) {
-    extern __shared__ __align__(1024) uint8_t smem[];
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-    uint64_t* empty = full + kRing16;
-    uint64_t* mma_done = empty + kRing16;
-    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mma_done + 1);
-    volatile int* dec_abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
-    uint8_t* ring = smem + kHdr;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int cta = blockIdx.x;
-    const int s0 = cta_s0(p.S, p.G, cta), s1 = cta_s0(p.S, p.G, cta + 1);
-    const int n = s1 - s0;
-    if (threadIdx.x == 0) {
-        for (int i = 0; i < kRing16; ++i) {
-            mbar_init(full + i, 1);
-            mbar_init(empty + i, 1);
-        }
-        mbar_init(mma_done, 1);
-        *dec_abort = 0;
-        mbar_fence_init();
-    }
-    if (warp == 0) {
-        tmem_alloc(tmem_holder, kCols16);
-        tmem_relinquish();
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = *tmem_holder;
-    pdl_trigger();
-
-    if (warp == kWarps16) {
-        // ------------------------------ producer ------------------------------
-        if (lane == 0 && n > 0) {
-            auto weights_of = [&](int s) -> const uint8_t* {
-                const int T = s / p.nb, b = s - T * p.nb;
-                const int sg = seg_of_tile(p, T);
-                return p.w[sg] + ((size_t)(T - p.tile0[sg]) * p.nb + b) * kUnit;
-            };
-            const int pre = n < kRing16 ? n : kRing16;
-            for (int r = 0; r < pre; ++r) {
-                mbar_expect_tx(full + r, kStage16);
-                bulk_g2s(ring + r * kStage16, weights_of(s0 + r), kUnit, full + r);
-            }
-            pdl_wait();   // the activation digits are written by the previous kernel
-            for (int r = 0; r < pre; ++r)
-                bulk_g2s(ring + r * kStage16 + kUnit, p.xb + (size_t)((s0 + r) % p.nb) * kB16, kB16, full + r);
-            int issued = pre;
-            for (int r = kRing16; r < n; ++r) {
-                const int slot = r % kRing16;
-                if (!mbar_wait_sleep(empty + slot, (uint32_t)((r / kRing16) - 1) & 1u, kSleepNs)) {
-                    atomicExch(p.err, 3u);
-                    break;
-                }
-                const int s = s0 + r;
-                mbar_expect_tx(full + slot, kStage16);
-                bulk_g2s(ring + slot * kStage16, weights_of(s), kUnit, full + slot);
-                bulk_g2s(ring + slot * kStage16 + kUnit, p.xb + (size_t)(s % p.nb) * kB16, kB16, full + slot);
-                issued = r + 1;
-            }
-            for (int r = issued - kRing16 > 0 ? issued - kRing16 : 0; r < issued; ++r)
-                mbar_wait(full + r % kRing16, (uint32_t)(r / kRing16) & 1u, 1u << 20);
-        }
-    } else if (n > 0) {
-        // --------------------------- decode / epilogue ---------------------------
-        pdl_wait();
-        const int q = warp & 3, h = warp >> 2;         // lane quarter, half
-        const int m = q * 32 + lane;                   // weight row of this thread
-        const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-        float tot[8];
-#pragma unroll
-        for (int t = 0; t < 8; ++t) tot[t] = 0.f;
-        int sc_prev[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        float d_prev = 0.f;
-        int last_mma = -1;
-        for (int r = 0; r <= n; ++r) {
-            int sc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-            float d = 0.f;
-            if (r < n) {
-                const int slot = r % kRing16;
-                if (!mbar_wait_sleep(full + slot, (uint32_t)(r / kRing16) & 1u, kSleepNs)) {
-                    *dec_abort = 1;
-                } else {
-                    const uint8_t* u = ring + slot * kStage16;
-                    uint32_t L0, L1;
-                    iq4_scale_bytes(lds64(u + kQsBytes + m * 8), L0, L1, d);
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        sc[i] = ubyte(L0, i) - 32;
-                        sc[4 + i] = ubyte(L1, i) - 32;
-                    }
-                    const uint32_t abuf = tmem + lane_base + (uint32_t)((r & 1) * 64);
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        const int sb = 4 * h + k;
-                        const uint4 qq = lds128(u + sb * (kRows * 16) + m * 16);
-                        uint32_t a[8];
-                        iq4_i8(qq.x, a[0], a[1]);
-                        iq4_i8(qq.y, a[2], a[3]);
-                        iq4_i8(qq.z, a[4], a[5]);
-                        iq4_i8(qq.w, a[6], a[7]);
-                        tmem_st8(abuf + (uint32_t)(sb * 8), a);
-                    }
-                    tmem_wait_st();
-                }
-            }
-            // epilogue of stage r-1, tokens 8h..8h+7: per digit (d2, d1, d0) the
-            // sub-block-scaled int32 sums
-            if (r >= 1 && !*dec_abort) {
-                const int rp = r - 1;
-                if (!mbar_wait_sleep(mma_done, (uint32_t)rp & 1u, kSleepNs)) {
-                    *dec_abort = 1;
-                } else {
-                    tc_fence_after();
-                    const uint32_t dbase = tmem + lane_base + kDCol16 + (uint32_t)(8 * h);
-                    const int b_prev = (s0 + rp) % p.nb;
-                    float f[8];
-#pragma unroll
-                    for (int g = 2; g >= 0; --g) {
-                        int acc[8];
-#pragma unroll
-                        for (int t = 0; t < 8; ++t) acc[t] = 0;
-#pragma unroll
-                        for (int sb = 0; sb < 8; sb += 4) {
-                            uint32_t v0[8], v1[8], v2[8], v3[8];
-                            tmem_ld8(dbase + (uint32_t)(sb * 48 + g * 16), v0);
-                            tmem_ld8(dbase + (uint32_t)((sb + 1) * 48 + g * 16), v1);
-                            tmem_ld8(dbase + (uint32_t)((sb + 2) * 48 + g * 16), v2);
-                            tmem_ld8(dbase + (uint32_t)((sb + 3) * 48 + g * 16), v3);
-                            tmem_wait_ld();
-#pragma unroll
-                            for (int t = 0; t < 8; ++t)
-                                acc[t] += sc_prev[sb] * (int)v0[t] + sc_prev[sb + 1] * (int)v1[t] +
-                                          sc_prev[sb + 2] * (int)v2[t] + sc_prev[sb + 3] * (int)v3[t];
-                        }
-#pragma unroll
-                        for (int t = 0; t < 8; ++t) {
-                            if (g == 2) f[t] = (float)acc[t];
-                            else if (g == 1) f[t] = fmaf((float)acc[t], 256.f, f[t]);
-                            else {
-                                const int tok = 8 * h + t;
-                                const float v = fmaf((float)acc[t], 65536.f, f[t]) * d_prev;
-                                const float xs = tok < p.N ? __ldg(p.xqscale + tok * p.nb + b_prev) : 0.f;
-                                tot[t] = fmaf(xs, v, tot[t]);
-                            }
-                        }
-                    }
-                    if (threadIdx.x == 0) mbar_arrive(empty + rp % kRing16);
-                    const int s = s0 + rp;
-                    if ((s + 1) % p.nb == 0 || rp == n - 1) {
-                        finish_row16(p, s / p.nb, cta, s0, s1, m, h, tot);
-#pragma unroll
-                        for (int t = 0; t < 8; ++t) tot[t] = 0.f;
-                    }
-                }
-            }
-            tc_fence_before();
-            named_bar_sync(1, kWarps16 * 32);
-            if (*dec_abort) break;
-            if (r < n && threadIdx.x == 0) {
-                tc_fence_after();
-                const uint32_t a0 = tmem + (uint32_t)((r & 1) * 64);
-                const uint32_t bsm = smem_u32(ring + (r % kRing16) * kStage16 + kUnit);
-#pragma unroll
-                for (int sb = 0; sb < 8; ++sb)
-                    tc_mma_i8(tmem + kDCol16 + (uint32_t)(sb * 48), a0 + (uint32_t)(sb * 8),
-                              smem_desc_kmajor(bsm + (uint32_t)(sb * 1536), 128u, 256u), kIdesc16, 0u);
-                tc_commit(mma_done);
-                last_mma = r;
-            }
-#pragma unroll
-            for (int i = 0; i < 8; ++i) sc_prev[i] = sc[i];
-            d_prev = d;
-        }
-        if (*dec_abort) {
-            if (threadIdx.x == 0) {
-                atomicExch(p.err, 4u);
-                if (last_mma >= 0) mbar_wait(mma_done, (uint32_t)last_mma & 1u, 1u << 20);
-            }
-        }
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    if (warp == 0) tmem_dealloc(tmem, kCols16);
-}
-
 // ------------------------ wide GEMM, scales folded ---------------------------
 // Up to NT = 16 or 32 input vectors per weight sweep.  The sub-block scale s
 // (ls - 32, 6 bits signed) is folded into the weights: each code c of a
@@ -553,8 +301,7 @@ __global__ void __launch_bounds__(kThreads16, 1) qmv_tc16_kernel(TcK p) {
 // the epilogue forms 64 SH + SL.  That integer is the one the other paths build
 // from per-sub-block sums (sum over k of s kv_k D_k), and the digits and the
 // fp16 block scale are combined in fp32 in the same order (65536 d0 + (256 d1 +
-// d2)), so a (tile, block) gives the same value here, on qb_qmv_tc16 and on the
-// mma.sync GEMV.
+// d2)), so a (tile, block) gives the same value here and on the mma.sync GEMV.
 //
 // Warp roles, each stage handed on by mbarriers so that neighbouring stages
 // overlap:
@@ -975,52 +722,6 @@ cudaError_t qb_qmv_tc(const QbQSeg* segs, int nseg, int K, int N, const QbXBuf& 
     return qb_launch(qmv_tc_kernel, dim3(G), dim3(kThreads), smem, st, p);
 }
 
-cudaError_t qb_qmv_tc16(const QbQSeg* segs, int nseg, int K, int N, const QbXBuf& xb, int accumulate, int row_lo,
-                        int row_hi, const QbQmvWork& work, cudaStream_t st) {
-    if (nseg < 1 || nseg > QB_MAX_SEG || N < 1 || N > QB_TC16_TOK || K % 256 || !xb.xtc16 || !xb.xqscale)
-        return cudaErrorInvalidValue;
-    TcK p = {};
-    int tiles = 0;
-    for (int i = 0; i < nseg; ++i) {
-        p.w[i] = (const uint8_t*)segs[i].w;
-        p.out[i] = segs[i].out;
-        p.ldo[i] = segs[i].ldo;
-        p.rows[i] = segs[i].rows;
-        p.tile0[i] = tiles;
-        tiles += (segs[i].rows + kRows - 1) / kRows;
-    }
-    p.tile0[nseg] = tiles;
-    if ((long long)tiles * kRows > work.max_tc_rows) return cudaErrorInvalidValue;
-    p.nseg = nseg;
-    p.nb = K / 256;
-    p.N = N;
-    const long long S = (long long)tiles * p.nb;
-    if (S >= (1ll << 30)) return cudaErrorInvalidValue;
-    p.S = (int)S;
-    int dev = 0, sms = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    int G = sms;   // one CTA per SM: each holds all 512 tensor-memory columns
-    if (G > work.max_tc_ctas) G = work.max_tc_ctas;
-    if (G > p.S) G = p.S;
-    p.G = G;
-    p.xb = xb.xtc16;
-    p.xqscale = xb.xqscale;
-    p.accumulate = accumulate;
-    p.row_lo = row_lo;
-    p.row_hi = row_hi;
-    p.partial = work.tc_partial;
-    p.counters = work.tc_counters;
-    p.err = work.err;
-    const size_t smem = kHdr + (size_t)kRing16 * kStage16;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(qmv_tc16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        attr_set = true;
-    }
-    return qb_launch(qmv_tc16_kernel, dim3(G), dim3(kThreads16), smem, st, p);
-}
 
 cudaError_t qb_qmv_tcw(const QbQSeg* segs, int nseg, int K, int N, const QbXBuf& xb, int accumulate, int row_lo,
                        int row_hi, const QbQmvWork& work, cudaStream_t st) {

@@ -1565,8 +1565,7 @@ cudaError_t qb_qmv_work_alloc(QbQmvWork& w, int max_pairs) {
     w.max_tc_rows = (long long)max_pairs * 32 + 128 * QB_MAX_SEG;   // every fused matrix rounds up to a tile
     if ((e = cudaMalloc(&w.tc_partial, qb_qmv_tc_partial_floats(w.max_tc_ctas) * sizeof(float))) != cudaSuccess)
         return e;
-    // per row, or per row and token half (qb_qmv_tc16)
-    // per row and token group: 2 groups of 8 (qb_qmv_tc16), 4 (qb_qmv_tcw)
+    // per row (qb_qmv_tc), or per row and token group of 8 (qb_qmv_tcw)
     if ((e = cudaMalloc(&w.tc_counters, (size_t)w.max_tc_rows * 4 * sizeof(unsigned))) != cudaSuccess) return e;
     if ((e = cudaMemset(w.tc_counters, 0, (size_t)w.max_tc_rows * 4 * sizeof(unsigned))) != cudaSuccess) return e;
     if ((e = cudaMemset(w.err, 0, sizeof(unsigned))) != cudaSuccess) return e;
