@@ -254,13 +254,15 @@ C4_PROMPT, C4_DECODE = 2048, 1024
 
 
 def run_c4(args, model, open_model, close_model, seq_rank, ms_ver_short):
-    """C4: a 2048-token prompt (256 prefill chunks of 8, device-timed), then MTP
+    """C4: a 2048-token prompt (63 prefill chunks of 32 and 4 of 8, device-timed), then MTP
     speculation (k = 3, forced schedule) for 1024 tokens at that context, then
     the verify step re-timed at the context reached (about 3072), against the
     verify step at the short context of C3.  The model is re-opened with a
     context of 3200 positions; the new model is returned under "_model"."""
     close_model(model)
     model = open_model(C4_PROMPT + C4_DECODE + 128)
+    if not args.parallel == "tp" or int(os.environ.get("WORLD_SIZE", "1")) == 1:
+        model.enable_wide()   # 32-token prefill chunks: IQ4_XS on the wide tcgen05 GEMM
     prompt = np.random.default_rng(2000 + seq_rank).integers(0, qb.FULL["vocab"], C4_PROMPT).astype(np.uint32)
     forced = forced_schedule()
     model.prefill(prompt, 1)   # warm: captures the chunk graph
@@ -274,7 +276,7 @@ def run_c4(args, model, open_model, close_model, seq_rank, ms_ver_short):
     log(f"C4 decode {len(toks)} tokens {ms_dec:.1f} ms")
     ms_v, b_v = model.bench(0, 4, 10)
     c4 = {"prefill_tok/s": C4_PROMPT / (ms_pf / 1e3), "prefill_ms": ms_pf,
-          "prefill_chunks": C4_PROMPT // 8,
+          "prefill_chunks": "63 x 32 + 4 x 8 tokens (32-token chunks: IQ4_XS on the wide tcgen05 GEMM)",
           "decode_tok/s": len(toks) / (ms_dec / 1e3), "decode_tokens": int(len(toks)),
           "decode_context": [C4_PROMPT, int(model.pos)],
           "verify_ms_at_context": ms_v, "verify_context": int(model.pos), "verify_bytes": b_v,

@@ -241,11 +241,13 @@ int qb_last_error(void);
 const char *qb_last_error_str(void);
 void qb_clear_error(void);
 
-/* src/main.c:132-152: batched prefill in chunks of PREFILL_MAX_B, plus the
- * MTP cache fill when spec != 0; afterwards m->logits holds the logits of
- * the last prompt token.  The prompt is copied to the device once and the
- * chunks run back to back (one graph replay per full chunk, no host wait in
- * between); qb_last_loop_ms then gives their device time.  Returns 0 or -1. */
+/* src/main.c:132-152: batched prefill, plus the MTP cache fill when spec != 0;
+ * afterwards m->logits holds the logits of the last prompt token.  The prompt
+ * is copied to the device once and the chunks run back to back (one graph
+ * replay per full chunk, no host wait in between): chunks of 32 tokens while
+ * more than 32 remain (one GPU), then of PREFILL_MAX_B, the last one with the
+ * output head; qb_last_loop_ms then gives their device time.  Each token's
+ * arithmetic does not depend on the chunk it is in.  Returns 0 or -1. */
 int qb_prefill(qwen_model_t *m, const uint32_t *tokens, uint32_t n, int spec);
 
 /* src/main.c:158-225: greedy MTP speculation with n_spec drafts.  Drafts,
@@ -307,6 +309,11 @@ int qb_reset(qwen_model_t *m);
  * or (qb_seq_generate) the cycles run, which is fewer than n_cycles only when
  * a sequence would pass n_ctx. */
 int qb_seq_init(qwen_model_t *m, uint32_t n_seq);
+/* Keep a tcgen05 tile copy of every IQ4_XS matrix (13 GB more for the 64-layer
+ * model), so that GEMV inputs of more than 8 rows run IQ4_XS 32 rows per weight
+ * sweep: qb_prefill's 32-token chunks and the multi-sequence verify
+ * (qb_seq_init does this itself from 3 sequences on).  One GPU.  0 / -1. */
+int qb_enable_wide(qwen_model_t *m);
 int qb_seq_prefill(qwen_model_t *m, uint32_t seq, const uint32_t *tokens, uint32_t n);
 int qb_seq_generate(qwen_model_t *m, uint32_t n_cycles, uint32_t n_spec, const uint32_t *forced,
                     uint32_t n_forced, uint32_t *out_tokens, uint32_t cap, uint32_t *out_counts,

@@ -360,6 +360,8 @@ int validate_model(const Gguf& g) {
 // ------------------------------ engine ----------------------------------------
 
 constexpr int kNSlot = 4;
+constexpr int kPrefillW = QB_WIDE;                 // tokens of a wide prefill chunk
+constexpr int kAttnGroups = kPrefillW / QB_MAX_TOK;   // its attention query groups
 
 struct DevMat {
     int type = -1;
@@ -388,10 +390,10 @@ struct LayerW {
 
 struct QbCtrl {
     uint32_t fwd_pos;
-    uint32_t fwd_tok[QB_MAX_TOK];
+    uint32_t fwd_tok[QB_WIDE];   // up to a 32-token prefill chunk
     uint32_t cur_slot;
     uint32_t mtp_pos;
-    uint32_t mtp_tok[QB_MAX_TOK];
+    uint32_t mtp_tok[QB_WIDE];
     uint32_t argmax[QB_MAX_TOK];
     uint32_t mtp_argmax[QB_MAX_TOK];
     // speculative loop
@@ -470,6 +472,7 @@ struct Engine {
     // sequence 0's; the single-sequence paths run on sequence cur_seq
     int n_seq = 1, cur_seq = 0;
     int ms_S = 1;                         // sequences of the forward being recorded (1: single sequence)
+    int attn_groups = 1;                  // a 32-token prefill chunk's attention as 4 groups of 8 queries
     long long seq_conv = 0, seq_ssm = 0, seq_kv = 0, seq_mtpkv = 0;
     float *conv_base = nullptr, *ssm_base = nullptr, *kv_k_base = nullptr, *kv_v_base = nullptr;
     float *mtp_k_base = nullptr, *mtp_v_base = nullptr, *mtp_h_base = nullptr;
@@ -487,6 +490,7 @@ struct Engine {
     cudaGraphExec_t g_greedy = nullptr;
     cudaGraphExec_t g_sample = nullptr;   // forward + sampling step (qb_sample_generate)
     cudaGraphExec_t g_prefill[2] = {};    // one full prefill chunk, without / with the MTP fill
+    cudaGraphExec_t g_prefill_w[2] = {};  // the same for a 32-token chunk
     uint32_t* d_prompt = nullptr;         // [n_ctx] prompt tokens staged for the prefill graphs
     QbSampDev* samp = nullptr;            // sampler parameters, history and generator on the device
     unsigned long long* samp_cand = nullptr;
@@ -526,6 +530,8 @@ Engine::~Engine() {
     if (g_greedy) cudaGraphExecDestroy(g_greedy);
     if (g_sample) cudaGraphExecDestroy(g_sample);
     for (cudaGraphExec_t& gp : g_prefill)
+        if (gp) cudaGraphExecDestroy(gp);
+    for (cudaGraphExec_t& gp : g_prefill_w)
         if (gp) cudaGraphExecDestroy(gp);
     if (ev0) cudaEventDestroy(ev0);
     if (ev1) cudaEventDestroy(ev1);
@@ -967,7 +973,8 @@ int engine_init(Engine& e, const char* path, uint32_t n_ctx) {
     CK(cudaMemset(e.xb.xtc16, 0, qb_xtc16_bytes(Kmax)));
     CK(cudaMemset(e.xb.xtc32, 0, qb_xtc32_bytes(Kmax)));
     {
-        const size_t q_rows = (size_t)d.n_head * T8 * qb_attn_max_chunks((int)e.n_ctx);
+        // chunk partials of up to kAttnGroups query groups (a 32-token prefill chunk)
+        const size_t q_rows = (size_t)kAttnGroups * d.n_head * T8 * qb_attn_max_chunks((int)e.n_ctx);
         e.attn_po = A(q_rows * d.head_dim);
         e.attn_pml = (float2*)e.dalloc(q_rows * sizeof(float2));
         if (!e.attn_po || !e.attn_pml) { set_err(-2, "attention scratch alloc"); return -1; }
@@ -1122,7 +1129,7 @@ int gemv_group(Engine& e, const DevMat* const* mats, float* const* outs, const l
 // The sequences of the forward being recorded: e.ms_S sequences of B / e.ms_S rows,
 // control blocks sizeof(QbCtrl) apart, states `state` floats apart.
 QbSeqs seqs(const Engine& e, int B, long long state) {
-    return QbSeqs{e.ms_S, B / e.ms_S, (long long)(sizeof(QbCtrl) / 4), state};
+    return QbSeqs{e.ms_S, B / e.ms_S, (long long)(sizeof(QbCtrl) / 4), state, 0};
 }
 // where the verify / MTP heads leave their argmax: the control block of a single
 // sequence, the flat per-row arrays of a multi-sequence forward
@@ -1227,7 +1234,9 @@ NextIn ffn_in(const Engine& e, const LayerW& l, int B) {
 // gated attention block on residual x, positions *pos .. *pos+B-1
 int attn_block(Engine& e, const LayerW& l, float* x, int B, const uint32_t* pos, float* kc, float* vc,
                long long kv_seq, const NextIn& next) {
-    const QbSeqs sq = seqs(e, B, kv_seq);
+    // a long prefill chunk: its queries in attn_groups groups over the one cache
+    const QbSeqs sq = e.attn_groups > 1 ? QbSeqs{e.attn_groups, B / e.attn_groups, 0, 0, B / e.attn_groups}
+                                        : seqs(e, B, kv_seq);
     // this rank's q-heads and kv-heads (all of them on one GPU)
     const qwen_dims_t& d = e.d;
     const int qw = 2 * d.n_head * d.head_dim, kvw = d.n_kv_head * d.head_dim, kvw_loc = e.nkv_loc * d.head_dim;
@@ -1507,12 +1516,17 @@ __global__ void prefill_advance_kernel(QbCtrl* c, int B) {
 
 // one full prefill chunk before the last: states, KV cache and h_save advance,
 // no output head; with spec the MTP KV cache fills from h_save (src/model.c:1069-1103)
-int record_prefill(Engine& e, int spec) {
-    CK(qb_launch(prefill_chunk_kernel, dim3(1), dim3(1), 0, e.st, e.ctrl, (const uint32_t*)e.d_prompt,
-                 (int)PREFILL_MAX_B));
-    if (fwd_backbone(e, PREFILL_MAX_B, 0, false, false)) return -1;
-    if (spec && fwd_mtp(e, PREFILL_MAX_B, e.h_save, 0)) return -1;
-    CK(qb_launch(prefill_advance_kernel, dim3(1), dim3(1), 0, e.st, e.ctrl, (int)PREFILL_MAX_B));
+// arg: bit 0 spec, bit 1 a wide chunk (kPrefillW tokens: attention in kAttnGroups query
+// groups, GEMVs of all rows at once)
+int record_prefill(Engine& e, int arg) {
+    const int spec = arg & 1, B = (arg & 2) ? kPrefillW : PREFILL_MAX_B;
+    CK(qb_launch(prefill_chunk_kernel, dim3(1), dim3(1), 0, e.st, e.ctrl, (const uint32_t*)e.d_prompt, B));
+    e.attn_groups = B / QB_MAX_TOK;
+    int r = fwd_backbone(e, B, 0, false, false);
+    if (!r && spec) r = fwd_mtp(e, B, e.h_save, 0);
+    e.attn_groups = 1;
+    if (r) return -1;
+    CK(qb_launch(prefill_advance_kernel, dim3(1), dim3(1), 0, e.st, e.ctrl, B));
     CK(cudaGetLastError());
     return 0;
 }
@@ -1613,6 +1627,33 @@ int ensure_w_tc(Engine& e, DevMat& m) {
     return 0;
 }
 
+// tcgen05 tile copies of every IQ4_XS matrix: GEMV inputs of more than QB_MAX_TOK rows
+// (prefill chunks, multi-sequence verifies) then run IQ4_XS on qb_qmv_tcw
+int enable_tcw(Engine& e) {
+    if (e.tcw) return 0;
+    if (e.tp_world > 1 || e.fuse || e.use_tc) { set_err(-1, "wide tcgen05 GEMM: one GPU, default GEMV paths"); return -1; }
+    auto each = [&](LayerW& l) {
+        DevMat* ms[] = {&l.ffn_gate, &l.ffn_up, &l.ffn_down, &l.wqkv, &l.wgate, &l.wbeta, &l.walpha, &l.ssm_out,
+                        &l.q, &l.k, &l.v, &l.o};
+        for (DevMat* d : ms)
+            if (d->w && ensure_w_tc(e, *d)) return -1;
+        return 0;
+    };
+    for (LayerW& l : e.L)
+        if (each(l)) return -1;
+    if (each(e.mtp)) return -1;
+    e.tcw = true;
+    // graphs recorded before route wide inputs through the 8-row chunks
+    cudaGraphExec_t* gs[] = {&e.g_mcycle, &e.g_prefill_w[0], &e.g_prefill_w[1]};
+    for (cudaGraphExec_t* g : gs)
+        if (*g) {
+            cudaGraphExecDestroy(*g);
+            *g = nullptr;
+        }
+    e.g_mcycle_k = -1;
+    return 0;
+}
+
 int ensure_out_buffers(Engine& e, uint32_t n_out, uint32_t n_j, uint32_t n_forced) {
     if (n_out > e.cap_out || n_j > e.cap_j || n_forced > e.cap_forced) {
         // buffers captured in graphs: re-capture after reallocation
@@ -1659,7 +1700,8 @@ int dev_sync(Engine& e) {
 
 // Graphs record the state pointers of the sequence they were captured for.
 void drop_graphs(Engine& e) {
-    cudaGraphExec_t* gs[] = {&e.g_cycle, &e.g_mcycle, &e.g_greedy, &e.g_sample, &e.g_prefill[0], &e.g_prefill[1]};
+    cudaGraphExec_t* gs[] = {&e.g_cycle,      &e.g_mcycle,      &e.g_greedy,       &e.g_sample,
+                             &e.g_prefill[0], &e.g_prefill[1], &e.g_prefill_w[0], &e.g_prefill_w[1]};
     for (cudaGraphExec_t* g : gs)
         if (*g) {
             cudaGraphExecDestroy(*g);
@@ -1945,16 +1987,21 @@ extern "C" int qb_prefill(qwen_model_t* m, const uint32_t* tokens, uint32_t n, i
     if (!e || !tokens || n == 0 || n > (uint32_t)e->n_ctx) { set_err(-1, "qb_prefill: bad arguments"); return -1; }
     CK(cudaSetDevice(e->dev));
     spec = spec ? 1 : 0;
-    // the whole prompt goes to the device once; every full chunk before the last is
-    // one replay of the chunk graph, which takes its tokens from there at fwd_pos
+    // the whole prompt goes to the device once; every full chunk before the last is one
+    // replay of a chunk graph, which takes its tokens from there at fwd_pos: chunks of
+    // kPrefillW tokens while more than kPrefillW remain (one GPU), then of PREFILL_MAX_B
     CK(cudaMemcpyAsync(e->d_prompt, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, e->st));
-    const uint32_t n_full = (n - 1) / PREFILL_MAX_B;   // chunks before the last one
+    const uint32_t n_wide = e->tp_world == 1 && !e->fuse && !e->use_tc && n > (uint32_t)kPrefillW
+                                ? (n - 1) / kPrefillW : 0;
+    const uint32_t n_full = (n - n_wide * kPrefillW - 1) / PREFILL_MAX_B;   // 8-token chunks before the last
+    if (n_wide && !e->g_prefill_w[spec] && capture(*e, &e->g_prefill_w[spec], record_prefill, spec | 2)) return -1;
     if (n_full && !e->g_prefill[spec] && capture(*e, &e->g_prefill[spec], record_prefill, spec)) return -1;
     CK(cudaEventRecord(e->ev0, e->st));
     CK(qb_launch(set_u32_kernel, dim3(1), dim3(1), 0, e->st, &e->ctrl->fwd_pos, 0u));
+    for (uint32_t c = 0; c < n_wide; ++c) CK(cudaGraphLaunch(e->g_prefill_w[spec], e->st));
     for (uint32_t c = 0; c < n_full; ++c) CK(cudaGraphLaunch(e->g_prefill[spec], e->st));
     // the last chunk (1..8 tokens) with the output head: logits and argmax of its rows
-    const uint32_t pos = n_full * PREFILL_MAX_B, lastB = n - pos;
+    const uint32_t pos = n_wide * kPrefillW + n_full * PREFILL_MAX_B, lastB = n - pos;
     CK(cudaMemcpyAsync(e->ctrl->fwd_tok, e->d_prompt + pos, lastB * 4, cudaMemcpyDeviceToDevice, e->st));
     CK(qb_launch(set_u32_kernel, dim3(1), dim3(1), 0, e->st, &e->ctrl->fwd_pos, pos));
     if (fwd_backbone(*e, (int)lastB, 0, false, true)) return -1;
@@ -2146,6 +2193,7 @@ extern "C" int qb_seq_init(qwen_model_t* m, uint32_t n_seq) {
     const size_t conv1 = std::max<size_t>(1, e->conv_slot_stride * kNSlot), ssm1 = std::max<size_t>(1, e->ssm_slot_stride * kNSlot);
     const size_t kv1 = std::max<size_t>(1, e->kv_layer * (size_t)na), mtp1 = e->kv_layer, h1 = (size_t)e->E;
     const size_t q_rows = (size_t)e->d.n_head * QB_MAX_TOK * qb_attn_max_chunks(e->n_ctx);
+    const size_t n_part = std::max<size_t>(n_seq, kAttnGroups);   // sequences, or prefill query groups
     void* olds[] = {e->conv_base, e->ssm_base, e->kv_k_base, e->kv_v_base, e->mtp_k_base, e->mtp_v_base,
                     e->mtp_h_base, e->ctrl_base, e->attn_po, e->attn_pml};
     for (void* p : olds) e->dfree(p);
@@ -2158,8 +2206,8 @@ extern "C" int qb_seq_init(qwen_model_t* m, uint32_t n_seq) {
     e->mtp_v_base = (float*)e->dalloc(S * mtp1 * 4);
     e->mtp_h_base = (float*)e->dalloc(S * h1 * 4);
     e->ctrl_base = (QbCtrl*)e->dalloc(S * sizeof(QbCtrl));
-    e->attn_po = (float*)e->dalloc(S * q_rows * e->d.head_dim * 4);
-    e->attn_pml = (float2*)e->dalloc(S * q_rows * sizeof(float2));
+    e->attn_po = (float*)e->dalloc(n_part * q_rows * e->d.head_dim * 4);
+    e->attn_pml = (float2*)e->dalloc(n_part * q_rows * sizeof(float2));
     if (!e->conv_base || !e->ssm_base || !e->kv_k_base || !e->kv_v_base || !e->mtp_k_base || !e->mtp_v_base ||
         !e->mtp_h_base || !e->ctrl_base || !e->attn_po || !e->attn_pml) {
         set_err(-2, "qb_seq_init: state alloc for %u sequences", n_seq);
@@ -2170,20 +2218,7 @@ extern "C" int qb_seq_init(qwen_model_t* m, uint32_t n_seq) {
     CK(cudaMemsetAsync(e->mtp_h_base, 0, S * h1 * 4, e->st));
     CK(cudaMemsetAsync(e->ctrl_base, 0, S * sizeof(QbCtrl), e->st));
     const char* tcw_env = getenv("QB_TCW");   // QB_TCW=0: wide verifies in 8-row mma.sync chunks only
-    if (n_seq * SPEC_MAX_B > QB_MAX_TOK && !e->tcw && !(tcw_env && tcw_env[0] == '0')) {
-        // verify widths above 8 rows: every IQ4_XS matrix also in tcgen05 tiles (qb_qmv_tcw)
-        auto each = [&](LayerW& l) {
-            DevMat* ms[] = {&l.ffn_gate, &l.ffn_up, &l.ffn_down, &l.wqkv, &l.wgate, &l.wbeta, &l.walpha, &l.ssm_out,
-                            &l.q, &l.k, &l.v, &l.o};
-            for (DevMat* d : ms)
-                if (d->w && ensure_w_tc(*e, *d)) return -1;
-            return 0;
-        };
-        for (LayerW& l : e->L)
-            if (each(l)) return -1;
-        if (each(e->mtp)) return -1;
-        e->tcw = true;
-    }
+    if (n_seq * SPEC_MAX_B > QB_MAX_TOK && !(tcw_env && tcw_env[0] == '0') && enable_tcw(*e)) return -1;
     e->seq_conv = (long long)conv1;
     e->seq_ssm = (long long)ssm1;
     e->seq_kv = (long long)kv1;
@@ -2201,6 +2236,13 @@ extern "C" int qb_seq_init(qwen_model_t* m, uint32_t n_seq) {
     memset(m->mtp_h, 0, (size_t)e->E * 4);
     m->pos = 0;
     return 0;
+}
+
+extern "C" int qb_enable_wide(qwen_model_t* m) {
+    Engine* e = E_(m);
+    if (!e) { set_err(-1, "qb_enable_wide: no model"); return -1; }
+    CK(cudaSetDevice(e->dev));
+    return enable_tcw(*e);
 }
 
 extern "C" int qb_seq_prefill(qwen_model_t* m, uint32_t seq, const uint32_t* tokens, uint32_t n) {

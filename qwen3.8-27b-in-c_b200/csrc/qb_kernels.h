@@ -66,10 +66,14 @@ __host__ __device__ inline QbXBuf qb_xb_chunk(const QbXBuf& xb, int c, int nb) {
 // Independent sequences in one launch of a stateful layer kernel (multi-sequence
 // decode): sequence s covers input rows [s * T, s * T + T); its position and
 // recurrent-slot words lie `ctrl` 32-bit words after sequence 0's, its state
-// (recurrent slots, KV cache) `state` floats after.  One sequence: {B, 0, 0}.
+// (recurrent slots, KV cache) `state` floats after, and its first position is its
+// position word plus s * pos_step.  One sequence: {1, B, 0, 0, 0}.  The attention
+// kernels also take one long prefill chunk as S groups of T queries over the same
+// cache: {S, T, 0, 0, T}.
 struct QbSeqs {
     int S, T;
     long long ctrl, state;
+    int pos_step;
 };
 enum { QB_XP_F16 = 1, QB_XP_SUM = 2, QB_XP_I8 = 4, QB_XP_TC = 8, QB_XP_TC16 = 16, QB_XP_TC32 = 32 };   // qb_xprep outputs
 #define QB_TC16_TOK 16       // input vectors of one qb_qmv_tc16 launch; xqscale rows it needs

@@ -205,8 +205,6 @@ __global__ void __launch_bounds__(128) gdn_recur_kernel(
     const int h = blockIdx.x, kh = h % n_k;
     const int tid = threadIdx.x, lane = tid & 31, l8 = lane & 7;
     const int grp = tid >> 3;   // 16 groups of 8 lanes
-    // this group's state row and its tokens' v values: loads issued first, so that
-    // their latency overlaps the q / k norms below
     const int row = blockIdx.y * 16 + grp;
     const int cur = (int)*cur_slot;
     const size_t head_off = (size_t)h * kDK * kDK + (size_t)row * kDK;
@@ -216,80 +214,89 @@ __global__ void __launch_bounds__(128) gdn_recur_kernel(
 #pragma unroll
         for (int m = 0; m < 16; ++m) S[m] = src[l8 + 8 * m];
     }
-    float vrow[QB_MAX_TOK];
-#pragma unroll
-    for (int b = 0; b < QB_MAX_TOK; ++b)
-        vrow[b] = b < B ? qkvc[(size_t)b * ld_qkvc + (size_t)2 * n_k * kDK + (size_t)h * kDK + row] : 0.f;
-
-    // L2 norms: group (b, which) for b < B, which in {q, k}.  Every lane of a
-    // warp runs the shuffles; inactive groups work on zeros and store nothing.
-    for (int base = 0; base < 2 * B; base += 16) {
-        const int gi = base + grp;
-        const bool act = gi < 2 * B;
-        const int b = act ? gi >> 1 : 0, which = gi & 1;
-        const float* src = qkvc + (size_t)b * ld_qkvc + (size_t)which * n_k * kDK + (size_t)kh * kDK;
-        float acc = 0.f;
-#pragma unroll
-        for (int m = 0; m < 16; ++m) {
-            const float v = act ? src[l8 + 8 * m] : 0.f;
-            acc = fmaf(v, v, acc);
-        }
-        const float ss = hsum8(acc);
-        const float nrm = sqrtf(ss);
-        const float scale = __fdiv_rn(1.0f, nrm > eps ? nrm : eps);
-        if (act) {
-            float* dst = which ? kn[b] : qn[b];
-#pragma unroll
-            for (int m = 0; m < 16; ++m) dst[l8 + 8 * m] = __fmul_rn(src[l8 + 8 * m], scale);
-        }
-    }
-    __syncthreads();
-    for (int base = 0; base < B; base += 16) {
-        const int b = base + grp;
-        const bool act = b < B;
-        float acc = 0.f;
-#pragma unroll
-        for (int m = 0; m < 16; ++m)
-            acc = act ? fmaf(kn[b][l8 + 8 * m], qn[b][l8 + 8 * m], acc) : 0.f;
-        const float kq = hsum8(acc);
-        if (act && l8 == 0) {
-            kq_s[b] = kq;
-            const float2 gt = gates[(size_t)b * n_v + h];   // gdn_conv_kernel
-            beta_s[b] = gt.x;
-            decay_s[b] = gt.y;
-        }
-    }
-    __syncthreads();
-
     const float q_scale = __fdiv_rn(1.0f, sqrtf((float)kDK));
+    // tokens in groups of QB_MAX_TOK (prefill chunks of up to 32 tokens); the state row
+    // stays in registers from one group to the next
+    for (int g0 = 0; g0 < B; g0 += QB_MAX_TOK) {
+        const int G = min(QB_MAX_TOK, B - g0);
+        // this group's state row and its tokens' v values: loads issued first, so that
+        // their latency overlaps the q / k norms below
+        float vrow[QB_MAX_TOK];
 #pragma unroll
-    for (int b = 0; b < QB_MAX_TOK; ++b) {
-        if (b >= B) break;
-        float ak = 0.f, aq = 0.f;
+        for (int b = 0; b < QB_MAX_TOK; ++b)
+            vrow[b] = b < G ? qkvc[(size_t)(g0 + b) * ld_qkvc + (size_t)2 * n_k * kDK + (size_t)h * kDK + row] : 0.f;
+        if (g0 > 0) __syncthreads();   // the previous group's qn / kn / gates are consumed
+
+        // L2 norms: group (b, which) for b < G, which in {q, k}.  Every lane of a
+        // warp runs the shuffles; inactive groups work on zeros and store nothing.
+        for (int base = 0; base < 2 * G; base += 16) {
+            const int gi = base + grp;
+            const bool act = gi < 2 * G;
+            const int b = act ? gi >> 1 : 0, which = gi & 1;
+            const float* src = qkvc + (size_t)(g0 + b) * ld_qkvc + (size_t)which * n_k * kDK + (size_t)kh * kDK;
+            float acc = 0.f;
 #pragma unroll
-        for (int m = 0; m < 16; ++m) {
-            ak = fmaf(S[m], kn[b][l8 + 8 * m], ak);
-            aq = fmaf(S[m], qn[b][l8 + 8 * m], aq);
+            for (int m = 0; m < 16; ++m) {
+                const float v = act ? src[l8 + 8 * m] : 0.f;
+                acc = fmaf(v, v, acc);
+            }
+            const float ss = hsum8(acc);
+            const float nrm = sqrtf(ss);
+            const float scale = __fdiv_rn(1.0f, nrm > eps ? nrm : eps);
+            if (act) {
+                float* dst = which ? kn[b] : qn[b];
+#pragma unroll
+                for (int m = 0; m < 16; ++m) dst[l8 + 8 * m] = __fmul_rn(src[l8 + 8 * m], scale);
+            }
         }
-        const float sk = hsum8(ak), sq = hsum8(aq);
-        const float decay = decay_s[b];
-        const float v = vrow[b];
-        const float delta = __fmul_rn(decay, sk);
-        const float dj = __fmul_rn(__fsub_rn(v, delta), beta_s[b]);
-        const float o = __fmul_rn(__fadd_rn(__fmul_rn(decay, sq), __fmul_rn(dj, kq_s[b])), q_scale);
+        __syncthreads();
+        for (int base = 0; base < G; base += 16) {
+            const int b = base + grp;
+            const bool act = b < G;
+            float acc = 0.f;
 #pragma unroll
-        for (int m = 0; m < 16; ++m) S[m] = fmaf(dj, kn[b][l8 + 8 * m], __fmul_rn(decay, S[m]));
-        if (l8 == 0) out[(size_t)b * ld_out + (size_t)h * kDK + row] = o;
-        int slot = -1;
-        if (ckpt) {
-            if (b < kNSlot - 1 || b == B - 1) slot = b < kNSlot - 1 ? b : kNSlot - 1;
-        } else if (b == B - 1) {
-            slot = cur;
+            for (int m = 0; m < 16; ++m)
+                acc = act ? fmaf(kn[b][l8 + 8 * m], qn[b][l8 + 8 * m], acc) : 0.f;
+            const float kq = hsum8(acc);
+            if (act && l8 == 0) {
+                kq_s[b] = kq;
+                const float2 gt = gates[(size_t)(g0 + b) * n_v + h];   // gdn_conv_kernel
+                beta_s[b] = gt.x;
+                decay_s[b] = gt.y;
+            }
         }
-        if (slot >= 0) {
-            float* dst = slots + (size_t)slot * slot_stride + head_off;
+        __syncthreads();
+
 #pragma unroll
-            for (int m = 0; m < 16; ++m) dst[l8 + 8 * m] = S[m];
+        for (int b = 0; b < QB_MAX_TOK; ++b) {
+            if (b >= G) break;
+            float ak = 0.f, aq = 0.f;
+#pragma unroll
+            for (int m = 0; m < 16; ++m) {
+                ak = fmaf(S[m], kn[b][l8 + 8 * m], ak);
+                aq = fmaf(S[m], qn[b][l8 + 8 * m], aq);
+            }
+            const float sk = hsum8(ak), sq = hsum8(aq);
+            const float decay = decay_s[b];
+            const float v = vrow[b];
+            const float delta = __fmul_rn(decay, sk);
+            const float dj = __fmul_rn(__fsub_rn(v, delta), beta_s[b]);
+            const float o = __fmul_rn(__fadd_rn(__fmul_rn(decay, sq), __fmul_rn(dj, kq_s[b])), q_scale);
+#pragma unroll
+            for (int m = 0; m < 16; ++m) S[m] = fmaf(dj, kn[b][l8 + 8 * m], __fmul_rn(decay, S[m]));
+            const int bt = g0 + b;   // token index in the launch
+            if (l8 == 0) out[(size_t)bt * ld_out + (size_t)h * kDK + row] = o;
+            int slot = -1;
+            if (ckpt) {
+                if (bt < kNSlot - 1 || bt == B - 1) slot = bt < kNSlot - 1 ? bt : kNSlot - 1;
+            } else if (bt == B - 1) {
+                slot = cur;
+            }
+            if (slot >= 0) {
+                float* dst = slots + (size_t)slot * slot_stride + head_off;
+#pragma unroll
+                for (int m = 0; m < 16; ++m) dst[l8 + 8 * m] = S[m];
+            }
         }
     }
 }
@@ -380,7 +387,7 @@ __global__ void attn_prep_kernel(float* __restrict__ q, long long ldq, const flo
     const int unit = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     const int nj = hd / 32;   // 8 for hd = 256
-    const uint32_t pos = pos0[(size_t)sidx * sq.ctrl] + (uint32_t)(b - sidx * sq.T);
+    const uint32_t pos = pos0[(size_t)sidx * sq.ctrl] + (uint32_t)(sidx * sq.pos_step) + (uint32_t)(b - sidx * sq.T);
     kc += (size_t)sidx * sq.state;
     vc += (size_t)sidx * sq.state;
     const int kvrow = n_kv * hd;
@@ -467,7 +474,7 @@ __global__ void __launch_bounds__(256) attn_part_kernel(const float* __restrict_
         part_ml += pq;
         part_o += pq * HD;
     }
-    const int pos0 = (int)*pos0p;
+    const int pos0 = (int)*pos0p + (int)blockIdx.z * sq.pos_step;
     const int t0 = c * C;
     if (t0 >= pos0 + B) return;
     const int G = n_head / n_kv, NQ = G * B;
@@ -586,7 +593,7 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const float* __restri
     const int h = blockIdx.x * 4 + (threadIdx.x >> 5);
     if (h >= n_head) return;
     const int sidx = b / sq.T, tb = b - sidx * sq.T;
-    const int nch = ((int)pos0p[(size_t)sidx * sq.ctrl] + tb) / kAttnC + 1;   // chunks holding positions 0 .. pos + tb
+    const int nch = ((int)pos0p[(size_t)sidx * sq.ctrl] + sidx * sq.pos_step + tb) / kAttnC + 1;   // chunks up to pos + tb
     const size_t qrow = ((size_t)sidx * n_head + h) * QB_MAX_TOK + tb;
     const float2* ml = part_ml + qrow * max_chunks;
     float M = -INFINITY;
@@ -872,7 +879,7 @@ __global__ void op_softmax_kernel(float* x, long long n) {
 
 // the sequences of a multi-sequence launch (sq, S * T == B rows), or one sequence of B rows
 static bool seqs_of(const QbSeqs* sq, int B, QbSeqs& out) {
-    out = sq ? *sq : QbSeqs{1, B, 0, 0};
+    out = sq ? *sq : QbSeqs{1, B, 0, 0, 0};
     return out.S >= 1 && out.S <= QB_MAX_SEQ && out.T >= 1 && out.S * out.T == B;
 }
 
@@ -902,7 +909,8 @@ cudaError_t qb_gdn_recur(const float* qkvc, long long ld_qkvc, const float2* gat
                          float eps, float* state_slots, size_t slot_stride, const uint32_t* cur_slot, int ckpt,
                          float* out, long long ld_out, cudaStream_t st, const QbSeqs* sq) {
     QbSeqs q;
-    if (dk != kDK || !seqs_of(sq, B, q) || q.T > QB_MAX_TOK) return cudaErrorInvalidValue;
+    // more than QB_MAX_TOK tokens per sequence only without checkpoints (prefill chunks)
+    if (dk != kDK || !seqs_of(sq, B, q) || (ckpt && q.T > QB_MAX_TOK)) return cudaErrorInvalidValue;
     return qb_launch(gdn_recur_kernel, dim3(n_v, kDK / 16, q.S), dim3(128), 0, st, qkvc, ld_qkvc, gates, n_k, n_v, q.T,
                      eps, state_slots, slot_stride, cur_slot, ckpt, out, ld_out, q);
 }

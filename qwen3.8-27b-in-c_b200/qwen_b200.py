@@ -32,7 +32,7 @@ EXPORTED = [
     "qb_greedy_generate", "qb_last_argmax", "qb_last_loop_ms", "qb_read_state", "qb_read_buffer",
     "qb_reset", "qb_bench", "qb_model_init_tp", "qb_tp_handle", "qb_tp_connect", "qb_tp_rows",
     "qb_argmax_rows_noalloc", "sampler_init", "sampler_free", "sampler_sample", "qb_sample_generate",
-    "qb_seq_init", "qb_seq_prefill", "qb_seq_generate",
+    "qb_seq_init", "qb_seq_prefill", "qb_seq_generate", "qb_enable_wide",
 ]
 
 
@@ -141,6 +141,8 @@ def lib():
         L.qb_reset.restype = i32
         L.qb_seq_init.argtypes = [P(QwenModel), u32]
         L.qb_seq_init.restype = i32
+        L.qb_enable_wide.argtypes = [P(QwenModel)]
+        L.qb_enable_wide.restype = i32
         L.qb_seq_prefill.argtypes = [P(QwenModel), u32, P(u32), u32]
         L.qb_seq_prefill.restype = i32
         L.qb_seq_generate.argtypes = [P(QwenModel), u32, u32, P(u32), u32, P(u32), u32, P(u32), P(u32)]
@@ -455,6 +457,11 @@ class Model:
             check()
             raise RuntimeError("qb_sample_generate failed")
         return out[:n].copy()
+
+    def enable_wide(self):
+        if lib().qb_enable_wide(C.byref(self.m)) != 0:
+            check()
+            raise RuntimeError("qb_enable_wide failed")
 
     # ---- multi-sequence decode (qb_seq_*) ----
     def seq_init(self, n_seq):

@@ -1,7 +1,10 @@
 """Long context (config C4): a 2048-token prompt through the chunked prefill
-(256 chunks of 8, one graph replay each, no host wait in between), then MTP
-speculation at that context, where the attention reads 2048+ cached
-positions in 64 chunks per head.
+(chunks of 32 tokens while more than 32 remain, then of 8; one graph replay
+each, no host wait in between), then MTP speculation at that context, where
+the attention reads 2048+ cached positions in 64 chunks per head.  A 32-token
+chunk runs its attention as 4 groups of 8 queries and its IQ4_XS GEMVs in one
+sweep on the wide tcgen05 GEMM once qb_enable_wide made its tiles (else in
+8-row chunks).
 
   - WIDE4 (4 layers at full width) against the compiled reference engine run
     live: prefill logits relative L2 <= 1e-4, then tokens and accept lengths
@@ -55,11 +58,36 @@ def test_long_prompt_wide4_matches_reference(wide_gguf):
     r.close()
 
 
+@pytest.mark.skipif(not oracle.available(), reason="oracle/_ref not built")
+@pytest.mark.parametrize("wide", [False, True])
+def test_prefill_chunking_matches_reference(tiny_gguf, wide):
+    """Prompt lengths around the 32- and 8-token chunk boundaries, with and without
+    the wide tcgen05 GEMM: prefill logits, MTP hidden state and the speculative
+    stream after it equal the reference's."""
+    for n in (31, 32, 33, 40, 41, 64, 65, 100, 129):
+        prompt = np.random.default_rng(n).integers(0, 2048, n).astype(np.uint32)
+        g = qb.Model(tiny_gguf, 256)
+        if wide:
+            g.enable_wide()
+        g.prefill(prompt, 1)
+        r = oracle.RefModel(tiny_gguf, 256, 0)
+        r.prefill(prompt, 1)
+        assert rel(g.logits(), r.logits()) < RTOL, n
+        assert rel(g.mtp_h(), r.mtp_h()) < RTOL, n
+        gt, gj = g.spec_generate(24, 3, forced=forced_schedule())
+        rt, rj = r.spec_generate(24, 3, forced=forced_schedule())
+        np.testing.assert_array_equal(gt, rt, err_msg=f"n = {n}")
+        np.testing.assert_array_equal(gj, rj, err_msg=f"n = {n}")
+        g.close()
+        r.close()
+
+
 def test_long_prompt_full_matches_golden(full_gguf):
     gold = np.load(os.path.join(ROOT, "tests", "golden", "full_long.npz"))
     n = int(gold["prompt_len"])
     prompt = np.random.default_rng(int(gold["prompt_seed"])).integers(0, qb.FULL["vocab"], n).astype(np.uint32)
     m = qb.Model(full_gguf, n + 256)
+    m.enable_wide()   # the benchmark's C4 path: 32-token chunks on the wide tcgen05 GEMM
     m.prefill(prompt, 1)
     lg = m.logits()
     assert rel(lg[:: int(gold["sub_stride"])], gold["prefill_sub"]) < RTOL
