@@ -417,6 +417,8 @@ def run_ours(args, rank, world, local_rank):
             dist.barrier()
 
     model = open_model(n_ctx)
+    if not tp:
+        model.enable_wide()   # prompts in 32-token chunks, IQ4_XS on the wide tcgen05 GEMM
     forced = forced_schedule()
 
     # ---- device-timed value: K speculative cycles ----
