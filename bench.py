@@ -58,6 +58,15 @@ PROMPT_LEN = 128
 SEED = 0
 
 
+_RESULT_FD = None
+
+
+def emit(obj):
+    """The one JSON line of the run, on the process's real standard output; everything
+    else a library prints (NCCL's banner, warnings) goes to standard error."""
+    os.write(_RESULT_FD if _RESULT_FD is not None else 1, (json.dumps(obj) + "\n").encode())
+
+
 def log(msg):
     try:
         rss = int(open("/proc/self/statm").read().split()[1]) * os.sysconf("SC_PAGE_SIZE") / 1e9
@@ -371,7 +380,7 @@ def run_reference(args, rank, world):
     n_threads = os.cpu_count()
     v, sample, _ = cpu_reference_run(path, n_threads, args.warmup, args.steps)
     if v is None:
-        print(json.dumps({"impl": "reference", "unavailable": sample}))
+        emit({"impl": "reference", "unavailable": sample})
         return
     cfg = bench_config(args, world, world > 1 and args.parallel == "tp")
     line = {"impl": "reference", "platform": "host CPU, reference AVX2 engine", "metric": METRIC, "value": v,
@@ -381,7 +390,7 @@ def run_reference(args, rank, world):
             "config": cfg,
             "cpu_baseline": {"value": v, "unit": "tok/s", "cores": n_threads, "kind": "reference", "sample": sample},
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line))
+    emit(line)
 
 
 def run_ours(args, rank, world, local_rank):
@@ -566,7 +575,7 @@ def run_ours(args, rank, world, local_rank):
                                     "sample": cpu_sample}
     close_model(model)
     if line:
-        print(json.dumps(line))
+        emit(line)
 
 
 def run_components(args):
@@ -596,10 +605,14 @@ def run_components(args):
         ms, b = model.bench(what, arg, iters)
         out[name] = {"ms": ms, "bytes": b, "GB/s": b / ms / 1e6}
     model.close()
-    print(json.dumps(out))
+    emit(out)
 
 
 def main():
+    global _RESULT_FD
+    sys.stdout.flush()
+    _RESULT_FD = os.dup(1)   # the JSON line goes here; stray prints of any library to stderr
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
