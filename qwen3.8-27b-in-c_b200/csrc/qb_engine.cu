@@ -2194,25 +2194,31 @@ extern "C" int qb_seq_init(qwen_model_t* m, uint32_t n_seq) {
     const size_t kv1 = std::max<size_t>(1, e->kv_layer * (size_t)na), mtp1 = e->kv_layer, h1 = (size_t)e->E;
     const size_t q_rows = (size_t)e->d.n_head * QB_MAX_TOK * qb_attn_max_chunks(e->n_ctx);
     const size_t n_part = std::max<size_t>(n_seq, kAttnGroups);   // sequences, or prefill query groups
+    // the new arrays first: if one does not fit, the model keeps its current sequences
+    const size_t S = n_seq;
+    const size_t sizes[10] = {S * conv1 * 4, S * ssm1 * 4,   S * kv1 * 4,  S * kv1 * 4,
+                              S * mtp1 * 4,  S * mtp1 * 4,   S * h1 * 4,   S * sizeof(QbCtrl),
+                              n_part * q_rows * e->d.head_dim * 4, n_part * q_rows * sizeof(float2)};
+    void* fresh[10] = {};
+    for (int i = 0; i < 10; ++i)
+        if (!(fresh[i] = e->dalloc(sizes[i]))) {
+            for (int j = 0; j < i; ++j) e->dfree(fresh[j]);
+            set_err(-2, "qb_seq_init: state for %u sequences does not fit (%zu bytes more)", n_seq, sizes[i]);
+            return -1;
+        }
     void* olds[] = {e->conv_base, e->ssm_base, e->kv_k_base, e->kv_v_base, e->mtp_k_base, e->mtp_v_base,
                     e->mtp_h_base, e->ctrl_base, e->attn_po, e->attn_pml};
     for (void* p : olds) e->dfree(p);
-    const size_t S = n_seq;
-    e->conv_base = (float*)e->dalloc(S * conv1 * 4);
-    e->ssm_base = (float*)e->dalloc(S * ssm1 * 4);
-    e->kv_k_base = (float*)e->dalloc(S * kv1 * 4);
-    e->kv_v_base = (float*)e->dalloc(S * kv1 * 4);
-    e->mtp_k_base = (float*)e->dalloc(S * mtp1 * 4);
-    e->mtp_v_base = (float*)e->dalloc(S * mtp1 * 4);
-    e->mtp_h_base = (float*)e->dalloc(S * h1 * 4);
-    e->ctrl_base = (QbCtrl*)e->dalloc(S * sizeof(QbCtrl));
-    e->attn_po = (float*)e->dalloc(n_part * q_rows * e->d.head_dim * 4);
-    e->attn_pml = (float2*)e->dalloc(n_part * q_rows * sizeof(float2));
-    if (!e->conv_base || !e->ssm_base || !e->kv_k_base || !e->kv_v_base || !e->mtp_k_base || !e->mtp_v_base ||
-        !e->mtp_h_base || !e->ctrl_base || !e->attn_po || !e->attn_pml) {
-        set_err(-2, "qb_seq_init: state alloc for %u sequences", n_seq);
-        return -1;   // the model is unusable now; model_free releases what was allocated
-    }
+    e->conv_base = (float*)fresh[0];
+    e->ssm_base = (float*)fresh[1];
+    e->kv_k_base = (float*)fresh[2];
+    e->kv_v_base = (float*)fresh[3];
+    e->mtp_k_base = (float*)fresh[4];
+    e->mtp_v_base = (float*)fresh[5];
+    e->mtp_h_base = (float*)fresh[6];
+    e->ctrl_base = (QbCtrl*)fresh[7];
+    e->attn_po = (float*)fresh[8];
+    e->attn_pml = (float2*)fresh[9];
     CK(cudaMemsetAsync(e->conv_base, 0, S * conv1 * 4, e->st));
     CK(cudaMemsetAsync(e->ssm_base, 0, S * ssm1 * 4, e->st));
     CK(cudaMemsetAsync(e->mtp_h_base, 0, S * h1 * 4, e->st));
