@@ -84,19 +84,23 @@ def reference_dir():
     return ref if os.path.isfile(os.path.join(ref, "src", "model.c")) else None
 
 
-def build_oracle(verbose=False):
-    """The checker: compiled only where the reference sources exist."""
+def build_oracle(verbose=False, clis=False):
+    """The checker: compiled only where the reference sources exist.  With clis, also
+    the reference CLI on the reference engine and relinked against libqwenb200 (the
+    end-to-end CLI test; the library must be built first)."""
     ref = reference_dir()
     if ref is None:
         return None
-    _run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), f"REF={ref}"], verbose)
+    targets = ["all", "reference-cli", "relink-cli"] if clis else ["all"]
+    _run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), f"REF={ref}", *targets], verbose)
     return os.path.join(ROOT, "oracle", "_ref", "libqwenref.so")
 
 
 def build_all(verbose=False, force=False):
     build_synth(verbose, force)
-    build_oracle(verbose)
-    return build_engine(verbose, force)
+    out = build_engine(verbose, force)
+    build_oracle(verbose, clis=True)
+    return out
 
 
 if __name__ == "__main__":

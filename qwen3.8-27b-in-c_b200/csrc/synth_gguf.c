@@ -404,6 +404,7 @@ static int cfg_check(const qb_synth_cfg_t *c) {
     if (c->d_conv != 4 || c->full_attn_interval == 0) return -1;
     if (c->ssm_v_heads % c->ssm_groups) return -1;
     if (c->rope_dim > c->head_dim || c->rope_dim % 2) return -1;
+    if (c->tokenizer && c->vocab < 266) return -1;   /* 256 bytes, 6 merged, 3 specials, one more */
     return 0;
 }
 
@@ -449,6 +450,43 @@ int qb_synth_write(const char *path, const qb_synth_cfg_t *c) {
     kv_u32(&h, arch, ".nextn_predict_layers", 1);
     bput_str(&h, "qb.synth.seed"); bput_u32(&h, G_U64); bput_u64(&h, c->seed);
     n_kv = 21;   /* 2 general.* + 18 <arch>.* + qb.synth.seed */
+    if (c->tokenizer) {
+        /* Byte-level vocabulary: token b < 256 is byte b in the GPT-2 byte-to-unicode
+         * form (printable bytes as themselves, the others from U+0100 on, in byte
+         * order), then six merged pairs, <tN> fillers, and the chat specials at the
+         * end (<|im_end|> the last id: the end-of-sequence token). */
+        bput_str(&h, "tokenizer.ggml.tokens"); bput_u32(&h, G_ARR); bput_u32(&h, G_STR);
+        bput_u64(&h, c->vocab);
+        /* a few BPE merges (the reference tokenizer needs a merge table), their
+         * results right after the bytes; U+0120 is the space byte */
+        static const char* const merged[6] = {"th", "he", "in", "er", "an", "\xc4\xa0t"};
+        static const char* const merges[6] = {"t h", "h e", "i n", "e r", "a n", "\xc4\xa0 t"};
+        int extra = 0;
+        for (uint32_t id = 0; id < c->vocab; id++) {
+            char t[32];
+            if (id >= 256 && id < 262) {
+                snprintf(t, sizeof t, "%s", merged[id - 256]);
+            } else if (id < 256) {
+                const uint32_t b = id;
+                const int printable = (b >= '!' && b <= '~') || (b >= 0xA1 && b <= 0xAC) || (b >= 0xAE && b <= 0xFF);
+                const uint32_t cp = printable ? b : 256 + (uint32_t)extra++;
+                if (cp < 0x80) { t[0] = (char)cp; t[1] = 0; }
+                else { t[0] = (char)(0xC0 | (cp >> 6)); t[1] = (char)(0x80 | (cp & 0x3F)); t[2] = 0; }
+            } else if (id == c->vocab - 3) {
+                snprintf(t, sizeof t, "<|endoftext|>");
+            } else if (id == c->vocab - 2) {
+                snprintf(t, sizeof t, "<|im_start|>");
+            } else if (id == c->vocab - 1) {
+                snprintf(t, sizeof t, "<|im_end|>");
+            } else {
+                snprintf(t, sizeof t, "<t%u>", id);
+            }
+            bput_str(&h, t);
+        }
+        bput_str(&h, "tokenizer.ggml.merges"); bput_u32(&h, G_ARR); bput_u32(&h, G_STR); bput_u64(&h, 6);
+        for (int i = 0; i < 6; i++) bput_str(&h, merges[i]);
+        n_kv += 2;
+    }
     memcpy(h.p + kv_count_at, &n_kv, 8);
 
     uint64_t off = 0;

@@ -22,6 +22,8 @@ typedef struct {
                              QB_SYNTH_MIXED: also Q4_K / Q5_K / Q6_K / Q8_0 projections */
     float gain;           /* target RMS of a projection output for unit-RMS input */
     uint32_t n_threads;   /* 0 = all online CPUs */
+    uint32_t tokenizer;   /* 1: a byte-level tokenizer vocabulary (tokenizer.ggml.tokens), so the
+                             reference CLI can encode prompts and print tokens */
 } qb_synth_cfg_t;
 
 int qb_synth_write(const char *path, const qb_synth_cfg_t *cfg);

@@ -531,7 +531,7 @@ class SynthCfg(C.Structure):
                                            "head_dim", "rope_dim", "full_attn_interval", "ssm_state",
                                            "ssm_groups", "ssm_v_heads", "d_conv", "n_ctx_train")] + [
         ("rope_theta", C.c_float), ("rms_eps", C.c_float), ("seed", C.c_uint64), ("profile", C.c_uint32),
-        ("gain", C.c_float), ("n_threads", C.c_uint32)]
+        ("gain", C.c_float), ("n_threads", C.c_uint32), ("tokenizer", C.c_uint32)]
 
 
 # Model shapes.  FULL is the benchmark model; the
@@ -565,8 +565,9 @@ def synth_lib():
     return _synth
 
 
-def synth_cfg(shape, seed=0, profile=0, gain=1.0, rope_theta=1e7, rms_eps=1e-6, n_threads=0):
+def synth_cfg(shape, seed=0, profile=0, gain=1.0, rope_theta=1e7, rms_eps=1e-6, n_threads=0, tokenizer=0):
     c = SynthCfg(**shape)
+    c.tokenizer = tokenizer
     c.n_ctx_train = 262144
     c.rope_theta = rope_theta
     c.rms_eps = rms_eps
