@@ -605,6 +605,20 @@ def run_components(args):
         ms, b = model.bench(what, arg, iters)
         out[name] = {"ms": ms, "bytes": b, "GB/s": b / ms / 1e6}
     model.close()
+    if not args.only or "prefill32" in args.only.split(","):
+        # one 32-token prefill chunk (the C4 chunk: IQ4_XS on the wide tcgen05 GEMM, the
+        # recurrence over all 32 tokens, attention as 4 groups of 8), device-timed: a
+        # 65-token prompt (two such chunks and a last token with the head) less a 33-token one
+        model = qb.Model(path, 1024)
+        model.enable_wide()
+        best = {}
+        for n in (33, 65) * (max(args.iters, 1) + 1):
+            model.reset()
+            model.prefill(prompt_tokens(0)[:n], 1)
+            best[n] = min(best.get(n, 1e30), model.last_loop_ms())
+        model.close()
+        ms = best[65] - best[33]
+        out["prefill32"] = {"ms": ms, "tok/s": 32 / ms * 1e3, "ms_33": best[33], "ms_65": best[65]}
     emit(out)
 
 
