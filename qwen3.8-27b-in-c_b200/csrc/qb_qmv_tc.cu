@@ -571,6 +571,9 @@ __global__ void __launch_bounds__(Tcw<NT>::kThreads, 1) qmv_tcw_kernel(TcK p) {
             float tot[kTokW];
 #pragma unroll
             for (int t = 0; t < kTokW; ++t) tot[t] = 0.f;
+            // column block b and row tile T of stage s0 + r, stepped instead of divided
+            int b = s0 % p.nb, T = s0 / p.nb;
+            const float* xs_t = xs_s + (size_t)(kTokW * tg) * p.nb;   // this warp's tokens
             for (int r = 0; r < n; ++r) {
                 if (!mbar_wait(d_full, (uint32_t)r & 1u, kSpinW) || *abort_flag) {
                     atomicExch(p.err, 4u);
@@ -589,21 +592,23 @@ __global__ void __launch_bounds__(Tcw<NT>::kThreads, 1) qmv_tcw_kernel(TcK p) {
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(d_free);   // D may take the next stage's sums
-                const int b = (s0 + r) % p.nb;
 #pragma unroll
                 for (int t = 0; t < kTokW; ++t) {
                     const int tok = kTokW * tg + t;
                     float f = (float)(64 * (int)v[4][t] + (int)v[5][t]);
                     f = fmaf((float)(64 * (int)v[2][t] + (int)v[3][t]), 256.f, f);
                     const float val = fmaf((float)(64 * (int)v[0][t] + (int)v[1][t]), 65536.f, f) * d;
-                    const float xs = tok < p.N ? xs_s[tok * p.nb + b] : 0.f;
+                    const float xs = tok < p.N ? xs_t[t * p.nb + b] : 0.f;
                     tot[t] = fmaf(xs, val, tot[t]);
                 }
-                const int s = s0 + r;
-                if ((s + 1) % p.nb == 0 || r == n - 1) {
-                    finish_row_w<NT>(p, s / p.nb, cta, s0, s1, m, tg, tot);
+                if (b + 1 == p.nb || r == n - 1) {
+                    finish_row_w<NT>(p, T, cta, s0, s1, m, tg, tot);
 #pragma unroll
                     for (int t = 0; t < kTokW; ++t) tot[t] = 0.f;
+                }
+                if (++b == p.nb) {
+                    b = 0;
+                    ++T;
                 }
             }
         }
